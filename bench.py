@@ -1,0 +1,471 @@
+"""Benchmark of the paged-KV hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload llama70b-shard|llama8b]
+
+One step = one pass of the hot path over one batch: gather every block of a
+GPU's paged KV cache, for every layer and K/V, through a seeded random block
+table into contiguous 256-token chunks (LMCache KV_2LTD order: K/V x layer x
+tokens x row), then scatter the chunks back through the same table.  Both
+moves are single launches of the row-mover kernel.
+
+Default workload (the per-GPU shard of the Llama-3-70B-shaped cache split by
+KV head): 80 layers x K/V, 1 KV head per GPU, head_dim 128, block 16 tokens,
+bf16, 16 sequences x 32k tokens = 32,768 blocks per GPU, 21.47 GB of cache
+per GPU.  With N GPUs each rank owns its own head shard and block table
+(weak scaling, no collective in the data path; NCCL only aggregates timings).
+
+Also reported: the device-resident clock stream on the clock-stress workload
+(1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations, one Zipf(1.1)
+re-access per allocation) in evictions/s.
+
+--impl reference times the reference's CPU implementation of the same moves
+(torch index_select / index_copy_ per plane, the oracle restatement) on a
+bounded sample of the workload with all host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+WORKLOADS = {
+    "llama70b-shard": dict(layers=80, heads=1, head_dim=128, block_size=16, dtype=torch.bfloat16,
+                           seqs=16, seq_tokens=32768, chunk_tokens=256,
+                           label="Llama-3-70B KV-head shard: 80 layers x K/V, 1 KV head/GPU, head_dim 128, "
+                                 "block 16, bf16, 16 x 32k-token sequences (32,768 blocks/GPU), 256-token chunks"),
+    "llama8b": dict(layers=32, heads=8, head_dim=128, block_size=16, dtype=torch.float16,
+                    seqs=64, seq_tokens=256, chunk_tokens=256,
+                    label="Llama-3-8B cache: 32 layers x K/V, 8 KV heads, head_dim 128, block 16, fp16, "
+                          "1024 blocks/layer, 64 requests x 256 tokens"),
+}
+
+CPU_SAMPLE_BLOCKS = 2048  # blocks per plane in the bounded CPU sample
+
+
+def _peaks() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _traffic_per_launch(workload: str) -> float | None:
+    """DRAM bytes per mover launch from the committed ncu summary, if any."""
+    path = REPO / "profiles" / "mover_traffic.json"
+    try:
+        rec = json.loads(path.read_text())[workload]
+        return float(rec["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """NVML sampling of SM clock and throttle reasons during a timed region."""
+
+    def __init__(self, device_index: int, period_s: float = 0.05):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+        self.period_s = period_s
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                mhz = self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM)
+                reasons = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            self._stop.wait(self.period_s)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        n = self._nvml
+        names = {
+            "gpu_idle": getattr(n, "nvmlClocksEventReasonGpuIdle", 0x1),
+            "applications_clocks_setting": getattr(n, "nvmlClocksEventReasonApplicationsClocksSetting", 0x2),
+            "sw_power_cap": getattr(n, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(n, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sync_boost": getattr(n, "nvmlClocksEventReasonSyncBoost", 0x10),
+            "sw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "hw_power_brake_slowdown": getattr(n, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        reasons = [k for k, bit in names.items() if seen & bit and k != "gpu_idle"]
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# workload construction
+# ---------------------------------------------------------------------------
+
+
+def build_cache(w: dict, device, seed: int, num_blocks: int | None = None):
+    """Planes ordered K of every layer, then V of every layer (KV_2LTD chunks),
+    as views of one (layers, 2, num_blocks, block, heads, head_dim) tensor."""
+    nb = num_blocks or (w["seqs"] * w["seq_tokens"] // w["block_size"])
+    kv = torch.empty((w["layers"], 2, nb, w["block_size"], w["heads"], w["head_dim"]),
+                     dtype=w["dtype"], device=device)
+    if device.type == "cuda":
+        gen = torch.Generator(device=device).manual_seed(seed)
+        kv.normal_(generator=gen)
+    else:
+        gen = torch.Generator().manual_seed(seed)
+        kv.normal_(generator=gen)
+    planes = [kv[l, 0] for l in range(w["layers"])] + [kv[l, 1] for l in range(w["layers"])]
+    table = torch.randperm(nb, generator=torch.Generator().manual_seed(seed))
+    return kv, planes, table, nb
+
+
+def block_bytes(w: dict) -> int:
+    return w["block_size"] * w["heads"] * w["head_dim"] * torch.tensor([], dtype=w["dtype"]).element_size()
+
+
+# ---------------------------------------------------------------------------
+# CPU leg (the reference's torch CPU indexing, restated in oracle/moves.py)
+# ---------------------------------------------------------------------------
+
+
+def cpu_moves(w: dict, steps: int, warmup: int) -> dict:
+    from oracle import moves
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    cb = w["chunk_tokens"] // w["block_size"]
+    nb = min(CPU_SAMPLE_BLOCKS, w["seqs"] * w["seq_tokens"] // w["block_size"])
+    _, planes, table, nb = build_cache(w, torch.device("cpu"), 1234, num_blocks=nb)
+    payload = len(planes) * nb * block_bytes(w)
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        chunks = moves.gather_layers(planes, table, blocks_per_chunk=cb)
+        moves.scatter_layers(planes, table, chunks, blocks_per_chunk=cb)
+        t1 = time.perf_counter()
+        if i >= warmup:
+            times.append(t1 - t0)
+    gbs = 4 * payload * len(times) / sum(times) / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(planes)} planes x {nb} blocks ({payload / 1e9:.2f} GB of the cache) per step, "
+                      f"{len(times)} steps: per-plane index_select + index_copy_ on CPU tensors"}
+
+
+def cpu_clock(k: int) -> dict:
+    import oracle
+    from kv_cache_adapter_b200 import adapter as adapter_mod
+    from kv_cache_adapter_b200 import workloads
+
+    steps = 200_000 // k
+    p = workloads.clock_params(1 << 20, steps, k, k, seed=1234)
+    meta = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta)
+    reacc = workloads.zipf_reaccess(p)
+    ss = torch.zeros(1, dtype=torch.int64)
+    t0 = time.perf_counter()
+    _, done, rc = oracle.clock_stream(meta, ss, steps, k, reacc, k)
+    dt = time.perf_counter() - t0
+    return {"value": round(done * k / dt, 1), "unit": "evictions/s", "cores": 1, "kind": "port",
+            "sample": f"the full clock stress ({done * k} allocations), sequential C restatement"}
+
+
+# ---------------------------------------------------------------------------
+# GPU legs
+# ---------------------------------------------------------------------------
+
+
+def gpu_clock(device, k: int, reps: int = 3) -> dict:
+    from kv_cache_adapter_b200 import adapter as adapter_mod
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+    from kv_cache_adapter_b200 import workloads
+
+    steps = 200_000 // k
+    p = workloads.clock_params(1 << 20, steps, k, k, seed=1234)
+    meta0 = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta).to(device)
+    reacc = workloads.zipf_reaccess(p).to(device)
+    meta = meta0.clone()
+    ss = torch.zeros(1, dtype=torch.int64, device=device)
+    victims = torch.empty(steps * k, dtype=torch.int64, device=device)
+    ms = []
+    for r in range(reps + 1):
+        meta.copy_(meta0)
+        ss.zero_()
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.clock_stream(meta, ss, steps, k, reacc, k, victims=victims, check=False)
+        e1.record()
+        torch.cuda.synchronize(device)
+        if r:
+            ms.append(e0.elapsed_time(e1))
+    ops.check_status(device)
+    best = min(ms)
+    return {"alloc_per_step": k, "steps": steps, "ms": round(best, 3),
+            "evictions_per_s": round(steps * k / (best / 1e3), 1), "launches": 1}
+
+
+def run_ours(args, w: dict, world: int, rank: int, device) -> None:
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+
+    seed = 1234 + rank
+    kv, planes, table_h, nb = build_cache(w, device, seed)
+    cb = w["chunk_tokens"] // w["block_size"]
+    P = len(planes)
+    bbytes = block_bytes(w)
+    payload = P * nb * bbytes  # bytes of cache moved by one gather (and by one scatter)
+    chunks = torch.empty((nb // cb, P, cb, w["block_size"], w["heads"], w["head_dim"]), dtype=w["dtype"],
+                         device=device)
+    table = table_h.to(device)
+    ptab = ops.PlaneTable(planes, 1)
+
+    def step():
+        ops.gather_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
+        ops.scatter_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+
+    # correctness guard on the bench data: chunk 0 holds the first cb blocks
+    # of the table for plane 0 and the last plane
+    for p in (0, P - 1):
+        assert torch.equal(chunks[0, p].view(torch.int16), planes[p][table[:cb]].view(torch.int16))
+
+    # ---- device-timed region ------------------------------------------------
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+               torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device.index) as clocks:
+        start.record()
+        for g0, g1, s1 in events:
+            g0.record()
+            ops.gather_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
+            g1.record()
+            ops.scatter_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
+            s1.record()
+        end.record()
+        torch.cuda.synchronize(device)
+    _barrier(world)
+    ops.check_status(device)
+    total_ms = _max_over_ranks(start.elapsed_time(end), world, device)
+    launch_ms = [g0.elapsed_time(g1) for g0, g1, _ in events] + [g1.elapsed_time(s1) for _, g1, s1 in events]
+    avg_launch_ms = _max_over_ranks(sum(launch_ms) / len(launch_ms), world, device)
+
+    # ---- end-to-end through the public API with host buffers ------------------
+    table_pinned = table_h.clone().pin_memory()
+    table_dev = torch.empty_like(table)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        table_dev.copy_(table_pinned, non_blocking=True)
+        ops.gather_layers(ptab, table_dev, chunks, blocks_per_chunk=cb, check=False)
+        ops.scatter_layers(ptab, table_dev, chunks, blocks_per_chunk=cb, check=False)
+        ops.check_status(device)  # device -> host read of the step's status word
+    torch.cuda.synchronize(device)
+    e2e_s = _max_over_ranks(time.perf_counter() - t0, world, device)
+    _barrier(world)
+
+    # ---- clock stream (replicated pool per GPU) -------------------------------
+    clock = None if args.no_clock else [gpu_clock(device, 1), gpu_clock(device, 256)]
+    if clock is not None:
+        for c in clock:
+            c["evictions_per_s"] = _max_over_ranks(-c["evictions_per_s"], world, device) * -1  # slowest rank
+
+    if rank != 0:
+        return
+    algo_per_step = 4 * payload  # gather r+w + scatter r+w
+    value = world * algo_per_step * args.steps / (total_ms / 1e3) / 1e9
+    peak, peak_kind = _peaks()
+    achieved = 2 * payload / (avg_launch_ms / 1e3) / 1e9
+    traffic = _traffic_per_launch(args.workload)
+    line = {
+        "metric": "paged-KV gather+scatter GB/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if w["dtype"] == torch.bfloat16 else "fp16",
+        "data": "synthetic (seeded N(0,1) cache, seeded random block tables)",
+        "config": {
+            "workload": w["label"],
+            "planes": P,
+            "blocks_per_gpu": nb,
+            "block_bytes_per_plane": bbytes,
+            "cache_bytes_per_gpu": payload,
+            "chunk_layout": "KV_2LTD per 256-token chunk",
+            "l2": "inputs larger than L2 (cache and chunks are each > 126 MB)",
+            "parallelism": f"kv-head shard x{world}, no data-path collective",
+        },
+        "per_gpu_gbs": round(value / world, 2),
+        "hbm_frac_per_gpu": round(value / world / peak, 4),
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+            "traffic": traffic,
+            "kernel": "move_rows_kernel (gather and scatter launches)",
+            "algorithmic_bytes_per_launch": 2 * payload,
+            "avg_launch_ms": round(avg_launch_ms, 4),
+        },
+        "e2e": {
+            "value": round(world * algo_per_step * args.steps / e2e_s / 1e9, 2),
+            "unit": "GB/s",
+            "h2d_bytes_per_step": table_h.numel() * 8,
+            "d2h_bytes_per_step": 16,
+            "api": "kv_cache_adapter_cuda.gather_layers / scatter_layers (ctypes -> C ABI)",
+        },
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if clock is not None:
+        line["clock_eviction"] = {
+            "metric": "clock evictions/s",
+            "workload": "1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations, "
+                        "1 Zipf(1.1) re-access per allocation, device-resident stream (1 launch)",
+            "runs": clock,
+            "aggregate_evictions_per_s": {str(c["alloc_per_step"]): round(world * c["evictions_per_s"], 1)
+                                          for c in clock},
+        }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_moves(w, steps=2, warmup=1)
+        if clock is not None:
+            line["cpu_baseline_clock"] = [cpu_clock(1), cpu_clock(256)]
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args, w: dict, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    cpu = cpu_moves(w, steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference",
+        "metric": "paged-KV gather+scatter GB/s",
+        "value": cpu["value"],
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if w["dtype"] == torch.bfloat16 else "fp16",
+        "data": "synthetic (seeded N(0,1) cache, seeded random block tables)",
+        "config": {"workload": w["label"], "sample": cpu["sample"]},
+        "cpu_baseline": cpu,
+        "e2e": {"value": cpu["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama70b-shard")
+    ap.add_argument("--no-clock", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    w = WORKLOADS[args.workload]
+    world, rank, local = _dist()
+
+    if args.impl == "reference":
+        run_reference(args, w, world, rank)
+        return
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=device)
+    try:
+        run_ours(args, w, world, rank, device)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

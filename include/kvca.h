@@ -1,0 +1,246 @@
+/*
+ * kvca.h - C ABI of the B200 (sm_100a) paged-KV adapter hot path.
+ *
+ * Two families of entry points live behind this header:
+ *
+ *   1. Slot metadata and the clock sweep over a packed slot_meta array.
+ *      Each slot has one unsigned word holding a pin count (low half) and a
+ *      usage count (high half): uint8 words carry 4+4 bits, uint16 words 8+8
+ *      bits (adapter.py:17-36, adapter.py:1419-1432 of the reference).
+ *      These replace the six torch-extension ops that adapter.py calls on
+ *      its packed-metadata branch (csrc/ascend/adapter_meta_kernels.h:6-47,
+ *      call sites adapter.py:316-330, :397-415, :437-454, :477-491,
+ *      :557-593, :615-645).
+ *
+ *   2. Row movers between a block-paged cache and contiguous chunks.
+ *      These replace actual_blocks.index_select / index_copy_
+ *      (adapter.py:543, adapter.py:653-656, adapter.py:779-787) and the
+ *      slot_mapping-driven single-layer KV transfer (adapter.py:1200-1243,
+ *      adapter.py:1275-1285).
+ *
+ * Conventions
+ *   - Every pointer named d_* is a device pointer on the current device.
+ *   - Every entry point enqueues work on `stream` and returns without
+ *     synchronising.  The return value reports host-side argument errors and
+ *     launch failures only.  Errors found on the device (an id outside its
+ *     table, too few reusable slots) are written to d_status, a caller-owned
+ *     array of two int64 words: d_status[0] = first error code (0 = none),
+ *     d_status[1] = the offending value.  The first error wins; the caller
+ *     clears the words.
+ *   - meta_bits selects the slot_meta word: 8 (uint8) or 16 (uint16).
+ *   - No entry point allocates device memory.
+ */
+#ifndef KVCA_H_
+#define KVCA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kvca_stream_t; /* same type as cudaStream_t */
+
+/* Status codes (host return values and d_status[0]). */
+#define KVCA_OK 0
+#define KVCA_ERR_INSUFFICIENT_CAPACITY 1 /* reference: InsufficientCapacityError, adapter.py:525 */
+#define KVCA_ERR_BAD_INDEX 2             /* reference: IndexError from index_select / index_fill_ */
+#define KVCA_ERR_BAD_ARGUMENT 3          /* reference: TORCH_CHECK, kv_adapter_cuda.cu:43-51 */
+#define KVCA_ERR_CUDA 4                  /* launch or runtime failure */
+
+/* Clock-sweep victim order (see kvca_pop_reusable_slots). */
+#define KVCA_POP_ORDER_GROUPED 0
+#define KVCA_POP_ORDER_PREFIX 1
+
+/* Row-mover flags. */
+#define KVCA_FLAG_SKIP_NEGATIVE 1 /* index < 0 marks a padding row: skip it, no error */
+
+/* Upper bound on planes per row-mover call. */
+#define KVCA_MAX_PLANES 256
+
+/* ABI version of this header. */
+int kvca_abi_version(void);
+
+/* Number of SMs of the current device (0 when no device is usable). */
+int kvca_device_sm_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* Slot metadata                                                             */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Replaces inspect_load_requests (csrc/ascend/adapter_meta_kernels.h:6-9;
+ * strict semantics adapter.py:417-431).  For each request i:
+ *   cur[i] = l2p[ids[i]];  resident[i] = cur[i] >= 0;
+ *   resident: pin_out[i] = pin(slot_meta[cur[i]]) + 1 (not wrapped),
+ *             usage_out[i] = min(usage + 1, USAGE_MAX);
+ *   else pin_out[i] = 0, usage_out[i] = 0.
+ * usage_out has the slot_meta word type.
+ */
+int kvca_inspect_load_requests(int meta_bits, const int64_t* d_l2p, int64_t num_logical,
+                               const void* d_slot_meta, int64_t num_slots,
+                               const int64_t* d_ids, int64_t count, int64_t* d_cur_out,
+                               uint8_t* d_resident_out, int64_t* d_pin_out, void* d_usage_out,
+                               int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * Replaces inspect_save_requests (csrc/ascend/adapter_meta_kernels.h:11-14;
+ * strict semantics adapter.py:456-470).  existing[i] = cur[i] >= 0;
+ * usage_out[i] = existing ? min(usage + 1, USAGE_MAX) : 1.
+ */
+int kvca_inspect_save_requests(int meta_bits, const int64_t* d_l2p, int64_t num_logical,
+                               const void* d_slot_meta, int64_t num_slots,
+                               const int64_t* d_ids, int64_t count, int64_t* d_cur_out,
+                               uint8_t* d_existing_out, void* d_usage_out, int64_t* d_status,
+                               kvca_stream_t stream);
+
+/*
+ * Replaces pop_reusable_slots (csrc/ascend/adapter_meta_kernels.h:16-20;
+ * grouped order = the strict path adapter.py:472-525; prefix order = the
+ * reference CUDA kernel's selection, csrc/kv_adapter_cuda.cu:101-231).
+ *
+ * A slot is available when its pin count is 0 and it is not listed in
+ * d_blocked.  Scan order starts at *d_search_start and wraps.  T is the
+ * smallest usage value such that at least `count` available slots have
+ * usage <= T.
+ *   GROUPED: all available slots with usage 0 in scan order, then usage 1,
+ *            ..., then the first ones with usage T, until `count`.
+ *   PREFIX:  the first `count` available slots in scan order with usage <= T.
+ * If T > 0 every slot's usage becomes max(usage - T, 0).  Then
+ * *d_search_start = (d_out[count - 1] + 1) % num_slots.
+ * Too few available slots: d_status gets KVCA_ERR_INSUFFICIENT_CAPACITY and
+ * neither slot_meta nor search_start changes.
+ *
+ * d_scratch_bitmap: ceil(num_slots / 32) uint32 words, all zero on entry;
+ * the call marks the blocked slots in it and clears them again before it
+ * returns, so it is zero on exit.  kvca_pop_scratch_bytes gives its size.
+ * Calls sharing one bitmap must be ordered on one stream.
+ */
+size_t kvca_pop_scratch_bytes(int64_t num_slots);
+int kvca_pop_reusable_slots(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                            int64_t* d_search_start, const int64_t* d_blocked,
+                            int64_t num_blocked, int64_t count, int64_t* d_out,
+                            uint32_t* d_scratch_bitmap, int64_t* d_status,
+                            kvca_stream_t stream);
+
+/* Replaces choose_pop_launch_warps (csrc/binding.cpp:74-78): warps per CTA
+ * of the pop kernel for a table of num_slots slots. */
+int64_t kvca_choose_pop_launch_warps(int64_t num_slots);
+
+/*
+ * Replaces commit_load_metadata (csrc/ascend/adapter_meta_kernels.h:22-32;
+ * strict semantics adapter.py:595-604), in this order:
+ *   l2p[evicted] = -1;
+ *   l2p[miss_ids] = miss_slots; p2l[miss_slots] = miss_ids;
+ *   slot_meta[hit_slots] = pack(hit_pins, hit_usage);
+ *   slot_meta[miss_slots] = pack(1, miss_usage).
+ * hit_usage / miss_usage have the slot_meta word type.
+ */
+int kvca_commit_load_metadata(int meta_bits, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                              void* d_slot_meta, int64_t num_slots, const int64_t* d_evicted,
+                              int64_t num_evicted, const int64_t* d_miss_ids,
+                              const int64_t* d_miss_slots, int64_t num_miss,
+                              const int64_t* d_hit_slots, const int64_t* d_hit_pins,
+                              const void* d_hit_usage, int64_t num_hit, const void* d_miss_usage,
+                              int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * Replaces commit_save_metadata (csrc/ascend/adapter_meta_kernels.h:34-42;
+ * strict semantics adapter.py:647-651):
+ *   l2p[evicted] = -1; l2p[ids] = slots; p2l[slots] = ids;
+ *   slot_meta[slots] = pack(final_pins, final_usage).
+ * final_pins / final_usage have the slot_meta word type.
+ */
+int kvca_commit_save_metadata(int meta_bits, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                              void* d_slot_meta, int64_t num_slots, const int64_t* d_evicted,
+                              int64_t num_evicted, const int64_t* d_ids, const int64_t* d_slots,
+                              const void* d_final_pins, const void* d_final_usage, int64_t count,
+                              int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * Replaces release_metadata (csrc/ascend/adapter_meta_kernels.h:44-47;
+ * strict semantics adapter.py:332-336): for slot = l2p[ids[i]],
+ * pin = (pin - 1) mod 2^(meta_bits/2); usage unchanged.  A released pin of 0
+ * therefore wraps to the field maximum, as in the strict path.
+ */
+int kvca_release_metadata(int meta_bits, const int64_t* d_l2p, int64_t num_logical,
+                          void* d_slot_meta, int64_t num_slots, const int64_t* d_ids,
+                          int64_t count, int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * Device-resident clock stream: for step s in [0, num_steps):
+ *   v = pop(alloc_per_step, no blocked slots)           -> d_victims[s*alloc_per_step ...]
+ *   slot_meta[v] = pack(pin(slot_meta[v]), 1)           (victim refilled, as a save miss)
+ *   r = d_reaccess[s*reaccess_per_step ...]
+ *   slot_meta[r] = pack(pin, min(usage + 1, USAGE_MAX)) (hits; values read before any write)
+ * One launch runs every step.  On too few available slots it stops, sets
+ * d_status and writes the number of completed steps to *d_steps_done.
+ * reaccess_per_step <= 8192.  No reference counterpart as one call: it is the
+ * strict-path sequence pop (adapter.py:472-525), commit (adapter.py:647-651)
+ * and usage bump (adapter.py:1414-1416) run back to back.
+ */
+int kvca_clock_stream(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                      int64_t* d_search_start, int64_t num_steps, int64_t alloc_per_step,
+                      const int64_t* d_reaccess, int64_t reaccess_per_step, int64_t* d_victims,
+                      int64_t* d_steps_done, int64_t* d_status, kvca_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Row movers                                                                */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * A paged side: num_planes planes (one per layer and K/V), each an array of
+ * num_blocks blocks of block_size rows.  Row r of the call lives at
+ *   plane_ptrs[p] + (idx / block_size) * block_stride + (idx % block_size) * row_stride
+ * with idx = index[r] (index == NULL means idx = r).  block_size = 1 makes
+ * whole blocks the rows (block-granular moves); block_size > 1 with a token
+ * slot_mapping makes tokens the rows (adapter.py:1275-1285).
+ * plane_ptrs is a HOST array of num_planes device addresses.
+ */
+typedef struct kvca_paged_desc {
+  const uint64_t* plane_ptrs;
+  int64_t num_blocks;
+  int64_t block_size;
+  int64_t block_stride;
+  int64_t row_stride;
+  const int64_t* index;
+} kvca_paged_desc;
+
+/*
+ * A contiguous side: row r of plane p lives at
+ *   base + (r / rows_per_chunk) * chunk_stride + (r % rows_per_chunk) * row_stride
+ *        + p * plane_stride
+ * e.g. an LMCache-style chunk [K/V x layer][rows_per_chunk][row] per chunk has
+ * plane_stride = rows_per_chunk * row_bytes and
+ * chunk_stride = num_planes * plane_stride.
+ */
+typedef struct kvca_chunk_desc {
+  uint64_t base;
+  int64_t rows_per_chunk;
+  int64_t chunk_stride;
+  int64_t row_stride;
+  int64_t plane_stride;
+} kvca_chunk_desc;
+
+/* Paged -> contiguous: per plane, index_select of rows (adapter.py:543). */
+int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,
+                int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
+                kvca_stream_t stream);
+
+/* Contiguous -> paged: per plane, index_copy_ of rows (adapter.py:653-656). */
+int kvca_scatter(const kvca_chunk_desc* src, const kvca_paged_desc* dst, int64_t num_planes,
+                 int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
+                 kvca_stream_t stream);
+
+/* Paged -> paged in one pass: dst[dst.index[r]] = src[src.index[r]]
+ * (the index_select + index_copy_ pair of adapter.py:779-787). */
+int kvca_copy_paged(const kvca_paged_desc* src, const kvca_paged_desc* dst, int64_t num_planes,
+                    int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
+                    kvca_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVCA_H_ */

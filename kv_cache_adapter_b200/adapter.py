@@ -1,0 +1,699 @@
+"""KVCacheAdapter on B200: the reference's operator API with every metadata
+update, clock sweep and KV byte move running in the sm_100a kernels.
+
+Public surface and behaviour follow the reference's adapter.py:
+``KVCacheAdapter`` (adapter.py:126-677), ``InMemoryBlockStoreBackend``
+(adapter.py:679-833), ``_MergedKVBlockLayout`` (adapter.py:81-123), the
+packed slot-meta codec (adapter.py:17-36, :1414-1432) and the error types
+(adapter.py:50-59).
+
+Differences, all on purpose:
+  * CUDA ``actual_blocks`` go through the packed-slot-meta op set, so pin
+    and usage updates persist (the reference's CUDA branch hands its kernels
+    derived temporaries and loses them; its NPU branch does what is done
+    here).
+  * Gathers and scatters of KV blocks run in the row-mover kernels instead of
+    ``index_select`` / ``index_copy_``.
+  * There is no pure-torch path: a CUDA adapter without the native library
+    raises, and CPU tensors need an explicitly supplied op set (``native_ext``),
+    which the test suite uses to check this orchestration against the
+    reference on CPU.
+"""
+from __future__ import annotations
+
+import functools
+import importlib
+import os
+import time
+from dataclasses import dataclass
+from typing import Any, Protocol
+
+import torch
+
+from .errors import BlockNotFoundError, InsufficientCapacityError, KVCacheAdapterError
+
+ID_DTYPE = torch.int64
+_SLOT_META_BITS = int(os.getenv("KVCA_SLOT_META_BITS", "8"))
+if _SLOT_META_BITS == 8:
+    SLOT_META_DTYPE = torch.uint8
+    PIN_COUNT_BITS = 4
+    USAGE_COUNT_BITS = 4
+elif _SLOT_META_BITS == 16:
+    SLOT_META_DTYPE = torch.uint16
+    PIN_COUNT_BITS = 8
+    USAGE_COUNT_BITS = 8
+else:
+    raise ValueError("KVCA_SLOT_META_BITS must be 8 or 16")
+
+USAGE_DTYPE = SLOT_META_DTYPE
+PIN_COUNT_DTYPE = SLOT_META_DTYPE
+PIN_COUNT_MAX = (1 << PIN_COUNT_BITS) - 1
+USAGE_COUNT_MAX = (1 << USAGE_COUNT_BITS) - 1
+_PIN_COUNT_MASK = PIN_COUNT_MAX
+_USAGE_COUNT_MASK = USAGE_COUNT_MAX
+_USAGE_COUNT_SHIFT = PIN_COUNT_BITS
+
+STATE_FREE = 0
+STATE_RESERVED = 1
+STATE_LOADING = 2
+STATE_RESIDENT = 3
+STATE_NAMES = {
+    STATE_FREE: "free",
+    STATE_RESERVED: "reserved",
+    STATE_LOADING: "loading",
+    STATE_RESIDENT: "resident",
+}
+
+__all__ = [
+    "KVCacheAdapter",
+    "InMemoryBlockStoreBackend",
+    "BlockStoreBackend",
+    "KVCacheAdapterError",
+    "BlockNotFoundError",
+    "InsufficientCapacityError",
+]
+
+
+class BlockStoreBackend(Protocol):
+    def save_blocks(self, logical_block_ids: torch.Tensor, block_data: torch.Tensor) -> None:
+        ...
+
+    def load_blocks(
+        self,
+        logical_block_ids: torch.Tensor,
+        actual_blocks: torch.Tensor,
+        physical_slot_ids: torch.Tensor,
+    ) -> None:
+        ...
+
+
+@dataclass(frozen=True)
+class _EvictionPlan:
+    logical_block_ids: torch.Tensor
+    payloads: torch.Tensor
+
+
+@dataclass(frozen=True)
+class _MergedKVBlockLayout:
+    """Merged K/V block shape ``(bs, 2, *hidden)`` (token-major) or
+    ``(2, bs, *hidden)`` (adapter.py:81-123)."""
+
+    block_shape: torch.Size
+    block_size: int
+    hidden_dim: int
+    token_major: bool
+
+    @classmethod
+    def detect(cls, block_shape) -> "_MergedKVBlockLayout | None":
+        shape = torch.Size(block_shape)
+        if len(shape) != 4:
+            return None
+        if shape[1] == 2:
+            block_size, token_major = int(shape[0]), True
+        elif shape[0] == 2:
+            block_size, token_major = int(shape[1]), False
+        else:
+            return None
+        hidden = int(shape[2]) * int(shape[3])
+        return cls(block_shape=shape, block_size=block_size, hidden_dim=hidden, token_major=token_major)
+
+    @property
+    def transfer_shape(self) -> torch.Size:
+        if self.token_major:
+            return torch.Size((self.block_size, 2, self.hidden_dim))
+        return torch.Size((2, self.block_size, self.hidden_dim))
+
+    def flatten_block_batch(self, block_batch: torch.Tensor) -> torch.Tensor:
+        return block_batch.contiguous().view((block_batch.shape[0],) + tuple(self.transfer_shape))
+
+    def restore_block_tensor(self, stored_tensor: torch.Tensor) -> torch.Tensor:
+        return stored_tensor.view(self.block_shape)
+
+    def token_planes(self, actual_blocks: torch.Tensor) -> list[torch.Tensor]:
+        """The K and V planes of a merged cache ``(m, *block_shape)`` as
+        ``(m, block_size, hidden_dim)`` views for token-granular moves."""
+        m = actual_blocks.shape[0]
+        flat = actual_blocks.view(m, *self.transfer_shape)
+        if self.token_major:
+            return [flat[:, :, 0], flat[:, :, 1]]
+        return [flat[:, 0], flat[:, 1]]
+
+    def physical_slot_mapping(self, physical_slot_ids: torch.Tensor) -> torch.Tensor:
+        """slot_mapping[i * bs + t] = slot[i] * bs + t (adapter.py:1275-1285)."""
+        offsets = torch.arange(self.block_size, dtype=ID_DTYPE, device=physical_slot_ids.device)
+        return (physical_slot_ids.reshape(-1, 1) * self.block_size + offsets.reshape(1, -1)).reshape(-1)
+
+    def dense_slot_mapping(self, num_blocks: int, *, device: torch.device) -> torch.Tensor:
+        """adapter.py:1266-1273."""
+        return torch.arange(num_blocks * self.block_size, dtype=ID_DTYPE, device=device)
+
+    def chunk_offsets(self, num_blocks: int) -> list[int]:
+        """adapter.py:1287-1290."""
+        return [i * self.block_size for i in range(num_blocks)]
+
+    def chunk_sizes(self, num_blocks: int) -> list[int]:
+        """adapter.py:1292-1295."""
+        return [self.block_size] * num_blocks
+
+
+class KVCacheAdapter:
+    """Maps n logical ids onto m resident physical slots in ``actual_blocks``.
+
+    Contract (adapter.py:127-134):
+    - ``actual_blocks`` is the real ``(m, ...)`` resident tensor
+    - ``logical_block_ids`` must be ``torch.int64`` on the same device as ``actual_blocks``
+    - ``block_data`` must be on the same device/dtype/shape layout as ``actual_blocks``
+    - callers serialize access; this adapter is not thread-safe
+    """
+
+    def __init__(
+        self,
+        num_actual_blocks: int,
+        num_logical_blocks: int,
+        actual_blocks: torch.Tensor,
+        backend: BlockStoreBackend,
+        *,
+        prefer_native_extension: bool = True,
+        prefer_cuda_extension: bool | None = None,
+        native_ext: Any | None = None,
+        pop_order: str | None = None,
+    ) -> None:
+        if prefer_cuda_extension is not None:
+            prefer_native_extension = prefer_cuda_extension
+        if not isinstance(actual_blocks, torch.Tensor):
+            raise TypeError("actual_blocks must be torch.Tensor")
+        if actual_blocks.ndim < 1:
+            raise ValueError("actual_blocks must have a leading block dimension")
+        if num_actual_blocks <= 0:
+            raise ValueError("num_actual_blocks must be positive")
+        if num_logical_blocks <= 0:
+            raise ValueError("num_logical_blocks must be positive")
+        if num_actual_blocks > num_logical_blocks:
+            raise ValueError("num_actual_blocks must be <= num_logical_blocks")
+        if actual_blocks.shape[0] != num_actual_blocks:
+            raise ValueError("actual_blocks leading dimension must equal num_actual_blocks")
+
+        self.num_actual_blocks = int(num_actual_blocks)
+        self.num_logical_blocks = int(num_logical_blocks)
+        self.actual_blocks = actual_blocks
+        self.backend = backend
+        self.pop_order = pop_order or os.getenv("KVCA_POP_ORDER", "grouped")
+
+        device = actual_blocks.device
+        self._platform = device.type
+        self._logical_to_physical = torch.full((num_logical_blocks,), -1, dtype=ID_DTYPE, device=device)
+        self._physical_to_logical = torch.full((num_actual_blocks,), -1, dtype=ID_DTYPE, device=device)
+        self._slot_meta = torch.zeros((num_actual_blocks,), dtype=SLOT_META_DTYPE, device=device)
+        self._search_start = torch.zeros((1,), dtype=ID_DTYPE, device=device)
+        self._native_ext, self.runtime_path = self._detect_native_extension(
+            prefer_native_extension=prefer_native_extension, native_ext=native_ext)
+
+    # -- derived views (adapter.py:185-203) --------------------------------
+
+    @property
+    def _pin_count(self) -> torch.Tensor:
+        return _slot_meta_pin_counts(self._slot_meta)
+
+    @property
+    def _usage_count(self) -> torch.Tensor:
+        return _slot_meta_usage_counts(self._slot_meta)
+
+    @property
+    def _reusable_mask(self) -> torch.Tensor:
+        return self._pin_count == 0
+
+    @property
+    def _slot_state(self) -> torch.Tensor:
+        return torch.where(
+            self._physical_to_logical >= 0,
+            torch.full_like(self._physical_to_logical, STATE_RESIDENT),
+            torch.full_like(self._physical_to_logical, STATE_FREE),
+        )
+
+    # -- public API ---------------------------------------------------------
+
+    def save(self, logical_block_ids: torch.Tensor, block_data: torch.Tensor) -> None:
+        """adapter.py:205-255."""
+        _require_id_tensor(logical_block_ids, name="logical_block_ids")
+        _require_same_device(logical_block_ids, expected_device=self.actual_blocks.device, name="logical_block_ids")
+        self._validate_logical_block_ids(logical_block_ids)
+        _require_block_data_tensor(block_data, expected_blocks=logical_block_ids.shape[0], name="block_data")
+        _require_same_device(block_data, expected_device=self.actual_blocks.device, name="block_data")
+        _require_same_dtype(block_data, reference=self.actual_blocks, name="block_data")
+        _require_trailing_shape(block_data, self.actual_blocks, name="block_data")
+        if logical_block_ids.numel() == 0:
+            return
+        logical_block_ids = logical_block_ids.contiguous()
+
+        current_physical, existing_mask, inspected_usage = self._inspect_save_requests(logical_block_ids)
+        existing_positions = _selected_positions(existing_mask)
+        missing_positions = _unselected_positions(existing_mask)
+        existing_physical = current_physical.index_select(0, existing_positions)
+        missing_ids = logical_block_ids.index_select(0, missing_positions)
+        allocated_physical = self._pop_reusable_slots(missing_ids.shape[0], blocked_slot_ids=existing_physical)
+
+        selected_physical = current_physical.clone()
+        if missing_ids.numel() > 0:
+            selected_physical.index_copy_(0, missing_positions, allocated_physical)
+
+        # pins and usage are read after the sweep, which may have aged usage
+        final_pin_counts = _slot_meta_pin_counts(self._slot_meta.index_select(0, selected_physical))
+        final_usage_counts = inspected_usage
+        if missing_ids.numel() > 0 and existing_physical.numel() > 0:
+            final_usage_counts = torch.ones_like(logical_block_ids, dtype=USAGE_DTYPE)
+            final_usage_counts.index_copy_(
+                0,
+                existing_positions,
+                _saturating_increment_usage(_slot_meta_usage_counts(self._slot_meta.index_select(0, existing_physical))),
+            )
+        eviction_plan = self._build_eviction_plan(logical_block_ids, selected_physical)
+        if eviction_plan.logical_block_ids.numel() > 0:
+            self.backend.save_blocks(eviction_plan.logical_block_ids, eviction_plan.payloads)
+
+        self._copy_into_actual_blocks(selected_physical, block_data)
+        self._commit_save_metadata(
+            evicted_logical_block_ids=eviction_plan.logical_block_ids,
+            logical_block_ids=logical_block_ids,
+            physical_slot_ids=selected_physical,
+            final_pin_counts=final_pin_counts,
+            final_usage_counts=final_usage_counts,
+        )
+
+    def load(self, logical_block_ids: torch.Tensor) -> torch.Tensor:
+        """adapter.py:257-307."""
+        _require_id_tensor(logical_block_ids, name="logical_block_ids")
+        _require_same_device(logical_block_ids, expected_device=self.actual_blocks.device, name="logical_block_ids")
+        self._validate_logical_block_ids(logical_block_ids)
+        if logical_block_ids.numel() == 0:
+            return torch.empty_like(logical_block_ids)
+        logical_block_ids = logical_block_ids.contiguous()
+
+        current_physical, resident_mask, updated_pins, updated_usage = self._inspect_load_requests(logical_block_ids)
+        resident_positions = _selected_positions(resident_mask)
+        miss_positions = _unselected_positions(resident_mask)
+        hit_slot_ids = current_physical.index_select(0, resident_positions)
+        miss_logical_ids = logical_block_ids.index_select(0, miss_positions)
+        miss_slot_ids = self._pop_reusable_slots(miss_logical_ids.shape[0], blocked_slot_ids=hit_slot_ids)
+        eviction_plan = self._build_eviction_plan(miss_logical_ids, miss_slot_ids)
+
+        if eviction_plan.logical_block_ids.numel() > 0:
+            self.backend.save_blocks(eviction_plan.logical_block_ids, eviction_plan.payloads)
+        if miss_logical_ids.numel() > 0:
+            self.backend.load_blocks(miss_logical_ids, self.actual_blocks, miss_slot_ids)
+
+        if miss_logical_ids.numel() > 0 and hit_slot_ids.numel() > 0:
+            hit_usage = _saturating_increment_usage(_slot_meta_usage_counts(self._slot_meta.index_select(0, hit_slot_ids)))
+        else:
+            hit_usage = updated_usage.index_select(0, resident_positions)
+        miss_usage = torch.ones((miss_slot_ids.shape[0],), dtype=USAGE_DTYPE, device=self.actual_blocks.device)
+        result_physical = current_physical
+        if miss_positions.numel() > 0:
+            result_physical = current_physical.clone()
+            result_physical.index_copy_(0, miss_positions, miss_slot_ids)
+        self._commit_load_metadata(
+            evicted_logical_block_ids=eviction_plan.logical_block_ids,
+            miss_logical_block_ids=miss_logical_ids,
+            miss_physical_slot_ids=miss_slot_ids,
+            hit_slot_ids=hit_slot_ids,
+            hit_pin_counts=updated_pins.index_select(0, resident_positions),
+            hit_usage_counts=hit_usage,
+            miss_usage_counts=miss_usage,
+        )
+        return result_physical
+
+    def release(self, logical_block_ids: torch.Tensor) -> None:
+        """adapter.py:309-336: pin - 1 per id (a pin of 0 wraps to the field max)."""
+        _require_id_tensor(logical_block_ids, name="logical_block_ids")
+        _require_same_device(logical_block_ids, expected_device=self.actual_blocks.device, name="logical_block_ids")
+        self._validate_logical_block_ids(logical_block_ids)
+        if logical_block_ids.numel() == 0:
+            return
+        self._native_ext.release_metadata(
+            self._logical_to_physical, self._slot_meta, logical_block_ids.contiguous(), check=True)
+
+    def get_actual_block(self, physical_slot_id: int) -> torch.Tensor:
+        self._validate_physical_slot_id(physical_slot_id)
+        return self.actual_blocks[physical_slot_id]
+
+    def debug_snapshot(self) -> dict[str, object]:
+        """adapter.py:342-357."""
+        reusable_slots = self._ordered_reusable_slots()
+        logical_to_physical = self._logical_to_physical.detach().to(device="cpu")
+        slot_state = self._slot_state.detach().to(device="cpu")
+        return {
+            "runtime_path": self.runtime_path,
+            "logical_to_physical": {
+                logical_block_id: int(physical_slot_id)
+                for logical_block_id, physical_slot_id in enumerate(logical_to_physical.tolist())
+                if physical_slot_id >= 0
+            },
+            "lru_unpinned": reusable_slots.detach().to(device="cpu").tolist(),
+            "slot_state": [STATE_NAMES[int(state)] for state in slot_state.tolist()],
+            "pin_count": self._pin_count.detach().cpu().clone(),
+            "actual_blocks": self.actual_blocks.detach().cpu().clone(),
+        }
+
+    def shutdown(self) -> None:
+        backend_shutdown = getattr(self.backend, "shutdown", None)
+        if callable(backend_shutdown):
+            backend_shutdown()
+            return
+        backend_close = getattr(self.backend, "close", None)
+        if callable(backend_close):
+            backend_close()
+
+    # -- internals ------------------------------------------------------------
+
+    def _detect_native_extension(self, *, prefer_native_extension: bool, native_ext: Any | None) -> tuple[Any, str]:
+        """adapter.py:369-391, CUDA only."""
+        if native_ext is not None:
+            return native_ext, f"{self._platform}_ext_meta"
+        if self._platform == "cuda":
+            if not prefer_native_extension:
+                raise RuntimeError("CUDA actual_blocks require kv_cache_adapter_cuda; strict CUDA path is disabled")
+            ext = _load_cuda_extension_module()
+            if ext is None:
+                raise RuntimeError("CUDA actual_blocks require kv_cache_adapter_cuda, but the extension is unavailable")
+            return ext, "cuda_ext_meta"
+        raise RuntimeError(
+            f"kv_cache_adapter_b200 serves CUDA actual_blocks; got device {self._platform!r} "
+            "(pass native_ext= to supply an op set for other devices)")
+
+    def _inspect_load_requests(self, ids: torch.Tensor):
+        try:
+            return tuple(self._native_ext.inspect_load_requests(
+                self._logical_to_physical, self._slot_meta, ids, check=True))
+        except IndexError as exc:
+            raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
+
+    def _inspect_save_requests(self, ids: torch.Tensor):
+        try:
+            return tuple(self._native_ext.inspect_save_requests(
+                self._logical_to_physical, self._slot_meta, ids, check=True))
+        except IndexError as exc:
+            raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
+
+    def _pop_reusable_slots(self, count: int, *, blocked_slot_ids: torch.Tensor) -> torch.Tensor:
+        """adapter.py:472-525 through the native clock sweep."""
+        if count == 0:
+            return self._logical_to_physical[:0]
+        return self._native_ext.pop_reusable_slots(
+            self._slot_meta, self._search_start, blocked_slot_ids.contiguous(), count, order=self.pop_order)
+
+    def _build_eviction_plan(self, logical_block_ids: torch.Tensor, physical_slot_ids: torch.Tensor) -> _EvictionPlan:
+        """adapter.py:527-544; the payload gather runs in the row mover."""
+        if physical_slot_ids.numel() == 0:
+            return _EvictionPlan(logical_block_ids[:0], self.actual_blocks[:0])
+        previous_logical_ids = self._physical_to_logical.index_select(0, physical_slot_ids)
+        eviction_mask = (previous_logical_ids >= 0) & (previous_logical_ids != logical_block_ids)
+        eviction_positions = _selected_positions(eviction_mask)
+        eviction_logical_ids = previous_logical_ids.index_select(0, eviction_positions)
+        eviction_slot_ids = physical_slot_ids.index_select(0, eviction_positions)
+        payloads = self._native_ext.gather_blocks(self.actual_blocks, eviction_slot_ids)
+        return _EvictionPlan(eviction_logical_ids, payloads)
+
+    def _commit_load_metadata(self, *, evicted_logical_block_ids, miss_logical_block_ids, miss_physical_slot_ids,
+                              hit_slot_ids, hit_pin_counts, hit_usage_counts, miss_usage_counts) -> None:
+        self._native_ext.commit_load_metadata(
+            self._logical_to_physical, self._physical_to_logical, self._slot_meta,
+            evicted_logical_block_ids.contiguous(), miss_logical_block_ids.contiguous(),
+            miss_physical_slot_ids.contiguous(), hit_slot_ids.contiguous(), hit_pin_counts.contiguous(),
+            hit_usage_counts.contiguous(), miss_usage_counts.contiguous(), check=True)
+
+    def _commit_save_metadata(self, *, evicted_logical_block_ids, logical_block_ids, physical_slot_ids,
+                              final_pin_counts, final_usage_counts) -> None:
+        self._native_ext.commit_save_metadata(
+            self._logical_to_physical, self._physical_to_logical, self._slot_meta,
+            evicted_logical_block_ids.contiguous(), logical_block_ids.contiguous(), physical_slot_ids.contiguous(),
+            final_pin_counts.contiguous(), final_usage_counts.contiguous(), check=True)
+
+    def _copy_into_actual_blocks(self, physical_slot_ids: torch.Tensor, block_data: torch.Tensor) -> None:
+        """adapter.py:653-656 through the row mover."""
+        if physical_slot_ids.numel() == 0:
+            return
+        self._native_ext.scatter_blocks(self.actual_blocks, physical_slot_ids.contiguous(), block_data.contiguous())
+
+    def _ordered_reusable_slots(self) -> torch.Tensor:
+        scan_order = (self._search_start[0] + torch.arange(
+            self.num_actual_blocks, device=self.actual_blocks.device, dtype=ID_DTYPE)) % self.num_actual_blocks
+        return scan_order[self._reusable_mask.index_select(0, scan_order)]
+
+    def _validate_logical_block_ids(self, logical_block_ids: torch.Tensor) -> None:
+        """adapter.py:666-672; device ids are checked by the inspect kernels."""
+        if logical_block_ids.numel() == 0 or logical_block_ids.device.type != "cpu":
+            return
+        if torch.any(logical_block_ids < 0) or torch.any(logical_block_ids >= self.num_logical_blocks):
+            raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})")
+
+    def _validate_physical_slot_id(self, physical_slot_id: int) -> None:
+        if physical_slot_id < 0 or physical_slot_id >= self.num_actual_blocks:
+            raise ValueError(f"physical slot id {physical_slot_id} is outside [0, {self.num_actual_blocks})")
+
+
+class InMemoryBlockStoreBackend:
+    """Dense logical-id-indexed block store (adapter.py:679-833).
+
+    CUDA storage moves bytes with the row-mover kernels (``copy_blocks``
+    fuses the reference's index_select + index_copy_ of load_blocks).  A
+    store on the host stays a host store: it uses torch host indexing and
+    one host<->device copy per call.
+    """
+
+    def __init__(
+        self,
+        initial_data: dict[int, torch.Tensor] | torch.Tensor | None = None,
+        *,
+        num_logical_blocks: int | None = None,
+        present_mask: torch.Tensor | None = None,
+        save_delay_s: float = 0.0,
+        load_delay_s: float = 0.0,
+        record_device_ops: bool = False,
+        ops: Any | None = None,
+    ) -> None:
+        self._storage: torch.Tensor | None = None
+        self._present_mask: torch.Tensor | None = None
+        self._ops = ops
+        self._record_device_ops = record_device_ops
+        if isinstance(initial_data, torch.Tensor):
+            if initial_data.ndim < 1:
+                raise ValueError("initial_data tensor must have a leading block dimension")
+            self._storage = initial_data.detach().clone()
+            inferred = int(self._storage.shape[0])
+            if num_logical_blocks is None:
+                num_logical_blocks = inferred
+            elif num_logical_blocks != inferred:
+                raise ValueError("num_logical_blocks must match initial_data.shape[0]")
+            self._present_mask = (
+                present_mask.detach().clone().to(device=self._storage.device)
+                if present_mask is not None
+                else torch.ones((num_logical_blocks,), dtype=torch.bool, device=self._storage.device)
+            )
+        else:
+            if num_logical_blocks is None:
+                if initial_data:
+                    num_logical_blocks = max(initial_data) + 1
+                else:
+                    raise ValueError("num_logical_blocks is required when initial_data is empty")
+            self._present_mask = present_mask.detach().clone() if present_mask is not None else None
+            if initial_data:
+                first = next(iter(initial_data.values()))
+                self._storage = first.new_zeros((num_logical_blocks, *first.shape))
+                if self._present_mask is None:
+                    self._present_mask = torch.zeros((num_logical_blocks,), dtype=torch.bool, device=first.device)
+                else:
+                    self._present_mask = self._present_mask.to(device=first.device)
+                ids = torch.tensor(list(initial_data.keys()), dtype=ID_DTYPE, device=first.device)
+                payloads = torch.stack([initial_data[key] for key in initial_data.keys()], dim=0)
+                self._storage.index_copy_(0, ids, payloads)
+                self._present_mask.index_fill_(0, ids, True)
+
+        self.num_logical_blocks = int(num_logical_blocks)
+        self._save_delay_s = save_delay_s
+        self._load_delay_s = load_delay_s
+        self.save_calls: list[int] = []
+        self.load_calls: list[int] = []
+        self.operation_log: list[tuple[str, int]] = []
+        self.max_concurrent_saves = 0
+        self.max_concurrent_loads = 0
+        self._concurrent_saves = 0
+        self._concurrent_loads = 0
+
+    def _device_ops(self):
+        return self._ops if self._ops is not None else _load_cuda_extension_module()
+
+    def save_blocks(self, logical_block_ids: torch.Tensor, block_data: torch.Tensor) -> None:
+        """adapter.py:735-756."""
+        _require_id_tensor(logical_block_ids, name="logical_block_ids")
+        _require_block_data_tensor(block_data, expected_blocks=logical_block_ids.shape[0], name="block_data")
+        self._enter_save()
+        try:
+            if self._save_delay_s > 0:
+                time.sleep(self._save_delay_s)
+            if self._storage is None:
+                self._storage = block_data.new_zeros((self.num_logical_blocks, *block_data.shape[1:]))
+            else:
+                _require_trailing_shape(block_data, self._storage, name="block_data")
+                _require_same_dtype(block_data, reference=self._storage, name="block_data")
+            self._ensure_present_mask(device=self._storage.device)
+            ids = logical_block_ids.to(device=self._storage.device).contiguous()
+            data = block_data.to(device=self._storage.device, dtype=self._storage.dtype).contiguous()
+            if self._storage.device.type == "cpu" and self._ops is None:
+                self._storage.index_copy_(0, ids, data)
+            else:
+                self._device_ops().scatter_blocks(self._storage, ids, data)
+            self._present_mask.index_fill_(0, ids, True)
+            self._record_ids("save", logical_block_ids)
+        finally:
+            self._leave_save()
+
+    def load_blocks(self, logical_block_ids: torch.Tensor, actual_blocks: torch.Tensor,
+                    physical_slot_ids: torch.Tensor) -> None:
+        """adapter.py:758-790."""
+        _require_id_tensor(logical_block_ids, name="logical_block_ids")
+        _require_id_tensor(physical_slot_ids, name="physical_slot_ids")
+        if logical_block_ids.shape[0] != physical_slot_ids.shape[0]:
+            raise ValueError("physical_slot_ids leading dimension must match logical_block_ids")
+        self._enter_load()
+        try:
+            if self._load_delay_s > 0:
+                time.sleep(self._load_delay_s)
+            if self._storage is None:
+                raise BlockNotFoundError("backend storage is empty")
+            self._ensure_present_mask(device=self._storage.device)
+            ids = logical_block_ids.to(device=self._storage.device).contiguous()
+            hit_mask = self._present_mask.index_select(0, ids)
+            if not torch.all(hit_mask).item():
+                raise BlockNotFoundError("some logical blocks are not in backend")
+            _require_trailing_shape(actual_blocks, self._storage, name="actual_blocks")
+            slots = physical_slot_ids.to(device=actual_blocks.device).contiguous()
+            same_device = self._storage.device == actual_blocks.device
+            if same_device and self._storage.dtype == actual_blocks.dtype and (
+                    self._storage.device.type != "cpu" or self._ops is not None):
+                self._device_ops().copy_blocks(self._storage, ids, actual_blocks, slots)
+            else:
+                payloads = self._storage.index_select(0, ids).to(device=actual_blocks.device, dtype=actual_blocks.dtype)
+                if actual_blocks.device.type == "cpu" and self._ops is None:
+                    actual_blocks.index_copy_(0, slots, payloads)
+                else:
+                    self._device_ops().scatter_blocks(actual_blocks, slots, payloads.contiguous())
+            self._record_ids("load", logical_block_ids)
+        finally:
+            self._leave_load()
+
+    def snapshot(self) -> dict[int, torch.Tensor]:
+        if self._storage is None:
+            return {}
+        present_ids = torch.nonzero(self._present_mask, as_tuple=False).reshape(-1)
+        present_payloads = self._storage.index_select(0, present_ids.to(device=self._storage.device))
+        return {
+            logical_block_id: payload.detach().clone().cpu()
+            for logical_block_id, payload in zip(present_ids.tolist(), present_payloads.unbind(0))
+        }
+
+    def _enter_save(self) -> None:
+        self._concurrent_saves += 1
+        self.max_concurrent_saves = max(self.max_concurrent_saves, self._concurrent_saves)
+
+    def _leave_save(self) -> None:
+        self._concurrent_saves -= 1
+
+    def _enter_load(self) -> None:
+        self._concurrent_loads += 1
+        self.max_concurrent_loads = max(self.max_concurrent_loads, self._concurrent_loads)
+
+    def _leave_load(self) -> None:
+        self._concurrent_loads -= 1
+
+    def shutdown(self) -> None:
+        return None
+
+    def _ensure_present_mask(self, *, device: torch.device) -> None:
+        if self._present_mask is None:
+            self._present_mask = torch.zeros((self.num_logical_blocks,), dtype=torch.bool, device=device)
+        elif self._present_mask.device != device:
+            self._present_mask = self._present_mask.to(device=device)
+
+    def _record_ids(self, operation: str, logical_block_ids: torch.Tensor) -> None:
+        """adapter.py:825-833; device ids are recorded only when asked for
+        (``record_device_ops=True``), since reading them synchronises."""
+        if logical_block_ids.device.type != "cpu" and not self._record_device_ops:
+            return
+        ids = logical_block_ids.detach().tolist()
+        if operation == "save":
+            self.save_calls.extend(ids)
+        else:
+            self.load_calls.extend(ids)
+        self.operation_log.extend((operation, i) for i in ids)
+
+
+@functools.lru_cache(maxsize=1)
+def _load_cuda_extension_module() -> Any | None:
+    """adapter.py:1347-1367: the op set lives next to this file."""
+    try:
+        return importlib.import_module(f"{__package__}.kv_cache_adapter_cuda")
+    except ImportError:
+        return None
+
+
+def _saturating_increment_usage(values: torch.Tensor) -> torch.Tensor:
+    """adapter.py:1414-1416."""
+    incremented = values.to(dtype=torch.int32) + 1
+    return torch.clamp(incremented, max=USAGE_COUNT_MAX).to(dtype=USAGE_DTYPE)
+
+
+def _slot_meta_pin_counts(slot_meta: torch.Tensor, *, dtype: torch.dtype = PIN_COUNT_DTYPE) -> torch.Tensor:
+    """adapter.py:1419-1420."""
+    return (slot_meta.to(dtype=torch.int32) & _PIN_COUNT_MASK).to(dtype=dtype)
+
+
+def _slot_meta_usage_counts(slot_meta: torch.Tensor) -> torch.Tensor:
+    """adapter.py:1423-1424."""
+    return ((slot_meta.to(dtype=torch.int32) >> _USAGE_COUNT_SHIFT) & _USAGE_COUNT_MASK).to(dtype=USAGE_DTYPE)
+
+
+def _pack_slot_meta(pin_counts: torch.Tensor, usage_counts: torch.Tensor) -> torch.Tensor:
+    """adapter.py:1427-1432."""
+    packed = (pin_counts.to(dtype=torch.int32) & _PIN_COUNT_MASK) | (
+        (usage_counts.to(dtype=torch.int32) & _USAGE_COUNT_MASK) << _USAGE_COUNT_SHIFT)
+    return packed.to(dtype=SLOT_META_DTYPE)
+
+
+def _selected_positions(mask: torch.Tensor) -> torch.Tensor:
+    return torch.nonzero(mask.to(dtype=torch.int32), as_tuple=False).flatten()
+
+
+def _unselected_positions(mask: torch.Tensor) -> torch.Tensor:
+    return torch.nonzero(mask.to(dtype=torch.int32) == 0, as_tuple=False).flatten()
+
+
+def _require_id_tensor(values: torch.Tensor, *, name: str) -> None:
+    if not isinstance(values, torch.Tensor):
+        raise TypeError(f"{name} must be torch.Tensor")
+    if values.dtype != ID_DTYPE:
+        raise TypeError(f"{name} must have dtype torch.int64")
+    if values.ndim != 1:
+        raise ValueError(f"{name} must have shape (k,)")
+
+
+def _require_same_device(values: torch.Tensor, *, expected_device: torch.device, name: str) -> None:
+    if values.device != expected_device:
+        raise ValueError(f"{name} must be on device {expected_device}, got {values.device}")
+
+
+def _require_same_dtype(block_data: torch.Tensor, *, reference: torch.Tensor, name: str) -> None:
+    if block_data.dtype != reference.dtype:
+        raise TypeError(f"{name} must have dtype {reference.dtype}")
+
+
+def _require_block_data_tensor(block_data: torch.Tensor, *, expected_blocks: int, name: str) -> None:
+    if not isinstance(block_data, torch.Tensor):
+        raise TypeError(f"{name} must be torch.Tensor")
+    if block_data.ndim < 1:
+        raise ValueError(f"{name} must have a leading block dimension")
+    if block_data.shape[0] != expected_blocks:
+        raise ValueError(f"{name} leading dimension must match logical_block_ids length")
+
+
+def _require_trailing_shape(block_data: torch.Tensor, reference: torch.Tensor, *, name: str) -> None:
+    if block_data.ndim != reference.ndim or block_data.shape[1:] != reference.shape[1:]:
+        raise ValueError(f"{name} must have trailing shape {tuple(reference.shape[1:])}")

@@ -1,0 +1,277 @@
+// C ABI of the adapter hot path (declared in include/kvca.h).
+//
+// This layer checks host-visible arguments (sizes, null pointers, word
+// widths, plane counts), picks the widest vector access that every address
+// and stride allows, and hands off to the sm_100a launchers.  It allocates
+// nothing and never synchronises the stream.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "kvca.h"
+#include "kvca_launch.h"
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+
+int status_of(cudaError_t e) { return e == cudaSuccess ? KVCA_OK : KVCA_ERR_CUDA; }
+
+bool valid_meta_bits(int bits) { return bits == 8 || bits == 16; }
+
+// Largest power-of-two access width (<= 16) dividing x.
+int align_of(uint64_t x) {
+  if (x % 16 == 0) return 16;
+  if (x % 8 == 0) return 8;
+  if (x % 4 == 0) return 4;
+  if (x % 2 == 0) return 2;
+  return 1;
+}
+
+int min_align(int a, uint64_t x) {
+  const int b = align_of(x);
+  return a < b ? a : b;
+}
+
+bool check_paged(const kvca_paged_desc* d, int64_t num_planes, int64_t row_bytes, int* vec) {
+  if (d == nullptr || d->plane_ptrs == nullptr) return false;
+  if (d->num_blocks < 0 || d->block_size < 1 || d->block_stride < 0 || d->row_stride < 0)
+    return false;
+  if (d->block_size > 1 && d->row_stride < row_bytes) return false;
+  for (int64_t p = 0; p < num_planes; ++p) {
+    if (d->plane_ptrs[p] == 0) return false;
+    *vec = min_align(*vec, d->plane_ptrs[p]);
+  }
+  *vec = min_align(*vec, static_cast<uint64_t>(d->block_stride));
+  *vec = min_align(*vec, static_cast<uint64_t>(d->row_stride));
+  return true;
+}
+
+bool check_chunk(const kvca_chunk_desc* d, int* vec) {
+  if (d == nullptr || d->base == 0) return false;
+  if (d->rows_per_chunk < 1 || d->chunk_stride < 0 || d->row_stride < 0 || d->plane_stride < 0)
+    return false;
+  *vec = min_align(*vec, d->base);
+  *vec = min_align(*vec, static_cast<uint64_t>(d->chunk_stride));
+  *vec = min_align(*vec, static_cast<uint64_t>(d->row_stride));
+  *vec = min_align(*vec, static_cast<uint64_t>(d->plane_stride));
+  return true;
+}
+
+void to_side(const kvca_paged_desc* d, int64_t num_planes, kvca::PagedSide* s) {
+  memset(s, 0, sizeof(*s));
+  for (int64_t p = 0; p < num_planes; ++p) s->planes[p] = d->plane_ptrs[p];
+  s->index = d->index;
+  s->num_blocks = d->num_blocks;
+  s->block_size = d->block_size;
+  s->block_stride = d->block_stride;
+  s->row_stride = d->row_stride;
+}
+
+void to_side(const kvca_chunk_desc* d, kvca::ChunkSide* s) {
+  s->base = d->base;
+  s->rows_per_chunk = d->rows_per_chunk;
+  s->chunk_stride = d->chunk_stride;
+  s->row_stride = d->row_stride;
+  s->plane_stride = d->plane_stride;
+}
+
+bool common_move_args_ok(int64_t num_planes, int64_t num_rows, int64_t row_bytes) {
+  return num_planes >= 1 && num_planes <= KVCA_MAX_PLANES && num_rows >= 0 && row_bytes >= 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kvca_abi_version(void) { return kAbiVersion; }
+
+int kvca_device_sm_count(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+int kvca_inspect_load_requests(int meta_bits, const int64_t* d_l2p, int64_t num_logical,
+                               const void* d_slot_meta, int64_t num_slots,
+                               const int64_t* d_ids, int64_t count, int64_t* d_cur_out,
+                               uint8_t* d_resident_out, int64_t* d_pin_out, void* d_usage_out,
+                               int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) || count < 0 || num_logical < 0 || num_slots < 0)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (count == 0) return KVCA_OK;
+  if (!d_l2p || !d_slot_meta || !d_ids || !d_cur_out || !d_resident_out || !d_pin_out ||
+      !d_usage_out)
+    return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_inspect_load(meta_bits, d_l2p, num_logical, d_slot_meta,
+                                             num_slots, d_ids, count, d_cur_out, d_resident_out,
+                                             d_pin_out, d_usage_out, d_status, stream));
+}
+
+int kvca_inspect_save_requests(int meta_bits, const int64_t* d_l2p, int64_t num_logical,
+                               const void* d_slot_meta, int64_t num_slots,
+                               const int64_t* d_ids, int64_t count, int64_t* d_cur_out,
+                               uint8_t* d_existing_out, void* d_usage_out, int64_t* d_status,
+                               kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) || count < 0 || num_logical < 0 || num_slots < 0)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (count == 0) return KVCA_OK;
+  if (!d_l2p || !d_slot_meta || !d_ids || !d_cur_out || !d_existing_out || !d_usage_out)
+    return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_inspect_save(meta_bits, d_l2p, num_logical, d_slot_meta,
+                                             num_slots, d_ids, count, d_cur_out, d_existing_out,
+                                             d_usage_out, d_status, stream));
+}
+
+size_t kvca_pop_scratch_bytes(int64_t num_slots) {
+  if (num_slots <= 0) return 0;
+  return static_cast<size_t>((num_slots + 31) / 32) * sizeof(uint32_t);
+}
+
+int kvca_pop_reusable_slots(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                            int64_t* d_search_start, const int64_t* d_blocked,
+                            int64_t num_blocked, int64_t count, int64_t* d_out,
+                            uint32_t* d_scratch_bitmap, int64_t* d_status,
+                            kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits)) return KVCA_ERR_BAD_ARGUMENT;
+  if (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (num_slots <= 0 || count < 0 || num_blocked < 0) return KVCA_ERR_BAD_ARGUMENT;
+  if (count == 0) return KVCA_OK;
+  if (!d_slot_meta || !d_search_start || !d_out || !d_scratch_bitmap) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_blocked > 0 && !d_blocked) return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_pop(meta_bits, order, d_slot_meta, num_slots, d_search_start,
+                                    d_blocked, num_blocked, count, d_out, d_scratch_bitmap,
+                                    d_status, stream));
+}
+
+int64_t kvca_choose_pop_launch_warps(int64_t num_slots) {
+  if (num_slots <= 0) return 0;
+  return kvca::pop_threads_for(8, num_slots) / 32;
+}
+
+int kvca_commit_load_metadata(int meta_bits, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                              void* d_slot_meta, int64_t num_slots, const int64_t* d_evicted,
+                              int64_t num_evicted, const int64_t* d_miss_ids,
+                              const int64_t* d_miss_slots, int64_t num_miss,
+                              const int64_t* d_hit_slots, const int64_t* d_hit_pins,
+                              const void* d_hit_usage, int64_t num_hit, const void* d_miss_usage,
+                              int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) || num_evicted < 0 || num_miss < 0 || num_hit < 0 ||
+      num_logical < 0 || num_slots < 0)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (num_evicted == 0 && num_miss == 0 && num_hit == 0) return KVCA_OK;
+  if (!d_l2p || !d_p2l || !d_slot_meta) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_evicted > 0 && !d_evicted) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_miss > 0 && (!d_miss_ids || !d_miss_slots || !d_miss_usage)) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_hit > 0 && (!d_hit_slots || !d_hit_pins || !d_hit_usage)) return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_commit_load(
+      meta_bits, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_evicted, num_evicted,
+      d_miss_ids, d_miss_slots, num_miss, d_hit_slots, d_hit_pins, d_hit_usage, num_hit,
+      d_miss_usage, d_status, stream));
+}
+
+int kvca_commit_save_metadata(int meta_bits, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                              void* d_slot_meta, int64_t num_slots, const int64_t* d_evicted,
+                              int64_t num_evicted, const int64_t* d_ids, const int64_t* d_slots,
+                              const void* d_final_pins, const void* d_final_usage, int64_t count,
+                              int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) || num_evicted < 0 || count < 0 || num_logical < 0 ||
+      num_slots < 0)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (num_evicted == 0 && count == 0) return KVCA_OK;
+  if (!d_l2p || !d_p2l || !d_slot_meta) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_evicted > 0 && !d_evicted) return KVCA_ERR_BAD_ARGUMENT;
+  if (count > 0 && (!d_ids || !d_slots || !d_final_pins || !d_final_usage))
+    return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_commit_save(meta_bits, d_l2p, num_logical, d_p2l, d_slot_meta,
+                                            num_slots, d_evicted, num_evicted, d_ids, d_slots,
+                                            d_final_pins, d_final_usage, count, d_status,
+                                            stream));
+}
+
+int kvca_release_metadata(int meta_bits, const int64_t* d_l2p, int64_t num_logical,
+                          void* d_slot_meta, int64_t num_slots, const int64_t* d_ids,
+                          int64_t count, int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) || count < 0 || num_logical < 0 || num_slots < 0)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (count == 0) return KVCA_OK;
+  if (!d_l2p || !d_slot_meta || !d_ids) return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_release(meta_bits, d_l2p, num_logical, d_slot_meta, num_slots,
+                                        d_ids, count, d_status, stream));
+}
+
+int kvca_clock_stream(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                      int64_t* d_search_start, int64_t num_steps, int64_t alloc_per_step,
+                      const int64_t* d_reaccess, int64_t reaccess_per_step, int64_t* d_victims,
+                      int64_t* d_steps_done, int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits)) return KVCA_ERR_BAD_ARGUMENT;
+  if (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (num_slots <= 0 || num_steps < 0 || alloc_per_step < 1 || reaccess_per_step < 0 ||
+      reaccess_per_step > 8192)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (!d_slot_meta || !d_search_start || !d_victims || !d_steps_done) return KVCA_ERR_BAD_ARGUMENT;
+  if (reaccess_per_step > 0 && num_steps > 0 && !d_reaccess) return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_clock_stream(meta_bits, order, d_slot_meta, num_slots,
+                                             d_search_start, num_steps, alloc_per_step,
+                                             d_reaccess, reaccess_per_step, d_victims,
+                                             d_steps_done, d_status, stream));
+}
+
+int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,
+                int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
+                kvca_stream_t stream) {
+  if (!common_move_args_ok(num_planes, num_rows, row_bytes)) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_rows == 0) return KVCA_OK;
+  int vec = align_of(static_cast<uint64_t>(row_bytes));
+  if (!check_paged(src, num_planes, row_bytes, &vec) || !check_chunk(dst, &vec))
+    return KVCA_ERR_BAD_ARGUMENT;
+  kvca::PagedSide sp;
+  kvca::ChunkSide dc;
+  to_side(src, num_planes, &sp);
+  to_side(dst, &dc);
+  kvca::MoveArgs a{kvca::MoveKind::kGather, &sp, nullptr, nullptr, &dc, num_planes, num_rows,
+                   row_bytes, vec, flags, d_status};
+  return status_of(kvca::launch_move(a, stream));
+}
+
+int kvca_scatter(const kvca_chunk_desc* src, const kvca_paged_desc* dst, int64_t num_planes,
+                 int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
+                 kvca_stream_t stream) {
+  if (!common_move_args_ok(num_planes, num_rows, row_bytes)) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_rows == 0) return KVCA_OK;
+  int vec = align_of(static_cast<uint64_t>(row_bytes));
+  if (!check_chunk(src, &vec) || !check_paged(dst, num_planes, row_bytes, &vec))
+    return KVCA_ERR_BAD_ARGUMENT;
+  kvca::ChunkSide sc;
+  kvca::PagedSide dp;
+  to_side(src, &sc);
+  to_side(dst, num_planes, &dp);
+  kvca::MoveArgs a{kvca::MoveKind::kScatter, nullptr, &sc, &dp, nullptr, num_planes, num_rows,
+                   row_bytes, vec, flags, d_status};
+  return status_of(kvca::launch_move(a, stream));
+}
+
+int kvca_copy_paged(const kvca_paged_desc* src, const kvca_paged_desc* dst, int64_t num_planes,
+                    int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
+                    kvca_stream_t stream) {
+  if (!common_move_args_ok(num_planes, num_rows, row_bytes)) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_rows == 0) return KVCA_OK;
+  int vec = align_of(static_cast<uint64_t>(row_bytes));
+  if (!check_paged(src, num_planes, row_bytes, &vec) ||
+      !check_paged(dst, num_planes, row_bytes, &vec))
+    return KVCA_ERR_BAD_ARGUMENT;
+  kvca::PagedSide sp;
+  kvca::PagedSide dp;
+  to_side(src, num_planes, &sp);
+  to_side(dst, num_planes, &dp);
+  kvca::MoveArgs a{kvca::MoveKind::kCopyPaged, &sp, nullptr, &dp, nullptr, num_planes, num_rows,
+                   row_bytes, vec, flags, d_status};
+  return status_of(kvca::launch_move(a, stream));
+}
+
+}  // extern "C"

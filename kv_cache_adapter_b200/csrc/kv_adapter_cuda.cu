@@ -1,0 +1,991 @@
+// sm_100a kernels for the paged-KV adapter hot path.
+//
+//  * Slot metadata ops over a packed slot_meta array (pin count in the low
+//    half of each word, usage count in the high half; adapter.py:17-36,
+//    adapter.py:1419-1432 of the reference).
+//  * The clock sweep (pop_reusable_slots) as one CTA that scans the table in
+//    16-byte vectors, ranks candidates with warp ballots / block scans and
+//    stops at the first tile that completes the request when no aging is
+//    needed.
+//  * A device-resident clock stream that runs pop, refill and usage bumps
+//    for many steps inside one launch.
+//  * The row mover: 16-byte vectorised, coalesced copies of whole blocks or
+//    single token rows between paged planes and contiguous chunks, all
+//    planes (layers x K/V) of a call in one launch.
+//
+// Device-side errors never trap: they are written to a caller-owned status
+// pair (code, value) with first-error-wins semantics, and the offending row
+// or request is skipped.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "kvca_launch.h"
+
+namespace kvca {
+namespace {
+
+// ---------------------------------------------------------------------------
+// Status reporting
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void report(int64_t* status, int64_t code, int64_t value) {
+  if (status == nullptr) return;
+  const unsigned long long prev = atomicCAS(reinterpret_cast<unsigned long long*>(status), 0ull,
+                                            static_cast<unsigned long long>(code));
+  if (prev == 0ull) status[1] = value;
+}
+
+// ---------------------------------------------------------------------------
+// Packed slot metadata: pin count in the low half of the word, usage count in
+// the high half (adapter.py:1419-1432).
+// ---------------------------------------------------------------------------
+
+template <typename MetaT>
+struct Meta {
+  static constexpr int kFieldBits = static_cast<int>(sizeof(MetaT)) * 4;
+  static constexpr unsigned kFieldMask = (1u << kFieldBits) - 1u;
+  static constexpr int kUsageMax = static_cast<int>(kFieldMask);
+  static constexpr int kSlotsPerVec = 16 / static_cast<int>(sizeof(MetaT));
+
+  __device__ __forceinline__ static unsigned pin(unsigned w) { return w & kFieldMask; }
+  __device__ __forceinline__ static unsigned usage(unsigned w) {
+    return (w >> kFieldBits) & kFieldMask;
+  }
+  // Masks both fields exactly like _pack_slot_meta: pins above the field
+  // maximum and negative pins wrap.
+  __device__ __forceinline__ static MetaT pack(int64_t pin_count, int64_t usage_count) {
+    const uint64_t p = static_cast<uint64_t>(pin_count) & kFieldMask;
+    const uint64_t u = static_cast<uint64_t>(usage_count) & kFieldMask;
+    return static_cast<MetaT>(p | (u << kFieldBits));
+  }
+  __device__ __forceinline__ static unsigned sat_inc(unsigned usage_count) {
+    return usage_count + 1u > kFieldMask ? kFieldMask : usage_count + 1u;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Block-wide exclusive scan (blockDim.x a multiple of 32, at most 1024).
+// `sm` holds 33 ints.  Contains three __syncthreads.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int block_excl_scan(int x, int* total, int* sm) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int incl = x;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) sm[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nwarps = static_cast<int>(blockDim.x >> 5);
+    const int w = lane < nwarps ? sm[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, d);
+      if (lane >= d) wi += y;
+    }
+    if (lane < nwarps) sm[lane] = wi - w;
+    if (lane == 31) sm[32] = wi;
+  }
+  __syncthreads();
+  const int result = sm[warp] + incl - x;
+  *total = sm[32];
+  __syncthreads();
+  return result;
+}
+
+// ---------------------------------------------------------------------------
+// Metadata vector access: 16 bytes per thread when the table is 16-byte
+// aligned, element-wise at the ragged tail.
+// ---------------------------------------------------------------------------
+
+template <typename MetaT>
+union MetaVec {
+  uint4 raw;
+  MetaT s[Meta<MetaT>::kSlotsPerVec];
+};
+
+template <typename MetaT>
+__device__ __forceinline__ void load_meta_vec(const MetaT* meta, int64_t num_slots, int64_t v,
+                                              bool aligned, MetaVec<MetaT>& out) {
+  constexpr int kSpv = Meta<MetaT>::kSlotsPerVec;
+  const int64_t first = v * kSpv;
+  if (aligned && first + kSpv <= num_slots) {
+    out.raw = *reinterpret_cast<const uint4*>(meta + first);
+  } else {
+#pragma unroll
+    for (int j = 0; j < kSpv; ++j) out.s[j] = first + j < num_slots ? meta[first + j] : MetaT(0);
+  }
+}
+
+template <typename MetaT>
+__device__ __forceinline__ void store_meta_vec(MetaT* meta, int64_t num_slots, int64_t v,
+                                               bool aligned, const MetaVec<MetaT>& in) {
+  constexpr int kSpv = Meta<MetaT>::kSlotsPerVec;
+  const int64_t first = v * kSpv;
+  if (aligned && first + kSpv <= num_slots) {
+    *reinterpret_cast<uint4*>(meta + first) = in.raw;
+  } else {
+#pragma unroll
+    for (int j = 0; j < kSpv; ++j)
+      if (first + j < num_slots) meta[first + j] = in.s[j];
+  }
+}
+
+// Blocked-slot bits for the kSlotsPerVec slots starting at `first` (a
+// multiple of kSlotsPerVec, so they share one 32-bit bitmap word).  The
+// bitmap is written with atomics earlier in the same CTA; read it through L2.
+template <typename MetaT>
+__device__ __forceinline__ unsigned blocked_bits(const uint32_t* bitmap, int64_t first) {
+  constexpr int kSpv = Meta<MetaT>::kSlotsPerVec;
+  if (bitmap == nullptr) return 0u;
+  const unsigned word = __ldcg(bitmap + (first >> 5));
+  return (word >> (first & 31)) & ((1u << kSpv) - 1u);
+}
+
+// ---------------------------------------------------------------------------
+// Clock sweep
+// ---------------------------------------------------------------------------
+
+template <typename MetaT>
+struct PopShared {
+  int scan[33];
+  int hist[Meta<MetaT>::kUsageMax + 1];
+  long long cls_base[Meta<MetaT>::kUsageMax + 1];
+  long long run[Meta<MetaT>::kUsageMax + 1];
+  long long start;
+  long long last_slot;
+  long long need;
+  int threshold;
+};
+
+// One CTA selects `count` victims (see kvca_pop_reusable_slots for the
+// semantics).  Returns KVCA_OK or KVCA_ERR_INSUFFICIENT_CAPACITY, uniformly
+// across the CTA.  On insufficient capacity nothing but `out` is written.
+//
+// Scan order from start s is split into two segments of the slot space,
+// [s, N) then [0, s), each walked in aligned vectors so that loads stay
+// 16-byte wide.  The vector holding s is visited by both segments, each time
+// handling only its own slots.
+//
+// Pass 1 ranks available usage-0 slots in scan order and stops at the tile
+// that completes `count`: then T = 0 and nothing ages.  Otherwise a full
+// histogram fixes T, and pass 2 walks every tile once more, ranking classes
+// 1..T (grouped order) or all usage <= T (prefix order) and writing the aged
+// usage of every slot.
+template <typename MetaT>
+__device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
+                       const uint32_t* bitmap, int64_t count, int64_t* out, int order,
+                       bool aligned, PopShared<MetaT>& sh) {
+  using M = Meta<MetaT>;
+  constexpr int kSpv = M::kSlotsPerVec;
+  const int64_t n = num_slots;
+
+  if (threadIdx.x == 0) {
+    long long s = static_cast<long long>(*search_start % n);
+    if (s < 0) s += n;
+    sh.start = s;
+    sh.last_slot = s;
+  }
+  __syncthreads();
+  const int64_t s = sh.start;
+
+  // ---- Pass 1: usage-0 candidates with early exit -------------------------
+  int64_t found = 0;
+  bool done = false;
+  for (int seg = 0; seg < 2 && !done; ++seg) {
+    const int64_t lo = seg == 0 ? s : 0;
+    const int64_t hi = seg == 0 ? n : s;
+    if (lo >= hi) continue;
+    const int64_t v_begin = lo / kSpv;
+    const int64_t v_end = (hi + kSpv - 1) / kSpv;
+    for (int64_t tile = v_begin; tile < v_end; tile += blockDim.x) {
+      const int64_t v = tile + threadIdx.x;
+      unsigned mask = 0u;
+      if (v < v_end) {
+        MetaVec<MetaT> m;
+        load_meta_vec(meta, n, v, aligned, m);
+        const unsigned blk = blocked_bits<MetaT>(bitmap, v * kSpv);
+#pragma unroll
+        for (int j = 0; j < kSpv; ++j) {
+          const int64_t slot = v * kSpv + j;
+          const unsigned w = m.s[j];
+          const bool hit = slot >= lo && slot < hi && M::pin(w) == 0u && ((blk >> j) & 1u) == 0u &&
+                           M::usage(w) == 0u;
+          mask |= (hit ? 1u : 0u) << j;
+        }
+      }
+      int total;
+      const int base = block_excl_scan(__popc(mask), &total, sh.scan);
+      int64_t rank = found + base;
+      while (mask != 0u) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        if (rank < count) {
+          out[rank] = v * kSpv + j;
+          if (rank == count - 1) sh.last_slot = v * kSpv + j;
+        }
+        ++rank;
+      }
+      found += total;
+      if (found >= count) {
+        done = true;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (done) {
+    if (threadIdx.x == 0) *search_start = (sh.last_slot + 1) % n;
+    __syncthreads();
+    return KVCA_OK;
+  }
+
+  // ---- Histogram of available slots by usage ------------------------------
+  for (int i = threadIdx.x; i <= M::kUsageMax; i += blockDim.x) sh.hist[i] = 0;
+  __syncthreads();
+  {
+    const int64_t nvec = (n + kSpv - 1) / kSpv;
+    const int lane = threadIdx.x & 31;
+    for (int64_t tile = 0; tile < nvec; tile += blockDim.x) {
+      const int64_t v = tile + threadIdx.x;
+      MetaVec<MetaT> m;
+      unsigned blk = 0u;
+      if (v < nvec) {
+        load_meta_vec(meta, n, v, aligned, m);
+        blk = blocked_bits<MetaT>(bitmap, v * kSpv);
+      }
+#pragma unroll
+      for (int j = 0; j < kSpv; ++j) {
+        int key = -1;
+        if (v < nvec && v * kSpv + j < n) {
+          const unsigned w = m.s[j];
+          if (M::pin(w) == 0u && ((blk >> j) & 1u) == 0u) key = static_cast<int>(M::usage(w));
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        if (key >= 0 && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[key], __popc(peers));
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long cum = 0;
+    int threshold = -1;
+    for (int t = 0; t <= M::kUsageMax; ++t) {
+      sh.cls_base[t] = cum;
+      sh.run[t] = 0;
+      cum += sh.hist[t];
+      if (cum >= count) {
+        threshold = t;
+        break;
+      }
+    }
+    sh.threshold = threshold;
+    if (threshold >= 0) sh.need = count - sh.cls_base[threshold];
+  }
+  __syncthreads();
+  const int threshold = sh.threshold;
+  if (threshold < 0) return KVCA_ERR_INSUFFICIENT_CAPACITY;
+
+  // ---- Pass 2: ranked selection of classes <= T and aging -----------------
+  const int64_t need = sh.need;
+  int64_t run_prefix = 0;
+  for (int seg = 0; seg < 2; ++seg) {
+    const int64_t lo = seg == 0 ? s : 0;
+    const int64_t hi = seg == 0 ? n : s;
+    if (lo >= hi) continue;
+    const int64_t v_begin = lo / kSpv;
+    const int64_t v_end = (hi + kSpv - 1) / kSpv;
+    for (int64_t tile = v_begin; tile < v_end; tile += blockDim.x) {
+      const int64_t v = tile + threadIdx.x;
+      const bool active = v < v_end;
+      MetaVec<MetaT> m;
+      unsigned avail_mask = 0u;  // in segment, unpinned, not blocked
+      if (active) {
+        load_meta_vec(meta, n, v, aligned, m);
+        const unsigned blk = blocked_bits<MetaT>(bitmap, v * kSpv);
+        MetaVec<MetaT> aged;
+#pragma unroll
+        for (int j = 0; j < kSpv; ++j) {
+          const int64_t slot = v * kSpv + j;
+          const unsigned w = m.s[j];
+          const bool in_seg = slot >= lo && slot < hi;
+          if (in_seg && M::pin(w) == 0u && ((blk >> j) & 1u) == 0u) avail_mask |= 1u << j;
+          const unsigned u = M::usage(w);
+          const unsigned u_aged = u > static_cast<unsigned>(threshold) ? u - threshold : 0u;
+          aged.s[j] = in_seg ? M::pack(M::pin(w), u_aged) : m.s[j];
+        }
+        store_meta_vec(meta, n, v, aligned, aged);
+      }
+      if (order == KVCA_POP_ORDER_GROUPED) {
+        for (int c = 1; c <= threshold; ++c) {
+          if (sh.hist[c] == 0) continue;
+          unsigned mask = 0u;
+          if (active) {
+#pragma unroll
+            for (int j = 0; j < kSpv; ++j)
+              if (((avail_mask >> j) & 1u) && M::usage(m.s[j]) == static_cast<unsigned>(c))
+                mask |= 1u << j;
+          }
+          const long long run_c = sh.run[c];
+          int total;
+          const int base = block_excl_scan(__popc(mask), &total, sh.scan);
+          const int64_t limit = c < threshold ? static_cast<int64_t>(sh.hist[c]) : need;
+          int64_t rank = run_c + base;
+          while (mask != 0u) {
+            const int j = __ffs(mask) - 1;
+            mask &= mask - 1u;
+            if (rank < limit) {
+              out[sh.cls_base[c] + rank] = v * kSpv + j;
+              if (c == threshold && rank == need - 1) sh.last_slot = v * kSpv + j;
+            }
+            ++rank;
+          }
+          if (threadIdx.x == 0) sh.run[c] = run_c + total;
+        }
+      } else {
+        unsigned mask = 0u;
+        if (active) {
+#pragma unroll
+          for (int j = 0; j < kSpv; ++j)
+            if (((avail_mask >> j) & 1u) && M::usage(m.s[j]) <= static_cast<unsigned>(threshold))
+              mask |= 1u << j;
+        }
+        int total;
+        const int base = block_excl_scan(__popc(mask), &total, sh.scan);
+        int64_t rank = run_prefix + base;
+        while (mask != 0u) {
+          const int j = __ffs(mask) - 1;
+          mask &= mask - 1u;
+          if (rank < count) {
+            out[rank] = v * kSpv + j;
+            if (rank == count - 1) sh.last_slot = v * kSpv + j;
+          }
+          ++rank;
+        }
+        run_prefix += total;
+      }
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *search_start = (sh.last_slot + 1) % n;
+  __syncthreads();
+  return KVCA_OK;
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    pop_kernel(MetaT* meta, int64_t num_slots, int64_t* search_start, const int64_t* blocked,
+               int64_t num_blocked, int64_t count, int64_t* out, uint32_t* bitmap, int order,
+               bool aligned, int64_t* status) {
+  __shared__ PopShared<MetaT> sh;
+  __shared__ int bad_blocked;
+  if (threadIdx.x == 0) bad_blocked = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < num_blocked; i += blockDim.x) {
+    const int64_t b = blocked[i];
+    if (b < 0 || b >= num_slots) {
+      bad_blocked = 1;
+      report(status, KVCA_ERR_BAD_INDEX, b);
+    } else {
+      atomicOr(bitmap + (b >> 5), 1u << (b & 31));
+    }
+  }
+  __syncthreads();
+  if (bad_blocked == 0) {
+    const int rc = pop_cta<MetaT>(meta, num_slots, search_start, bitmap, count, out, order,
+                                  aligned, sh);
+    if (rc != KVCA_OK && threadIdx.x == 0) report(status, rc, count);
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < num_blocked; i += blockDim.x) {
+    const int64_t b = blocked[i];
+    if (b >= 0 && b < num_slots) atomicAnd(bitmap + (b >> 5), ~(1u << (b & 31)));
+  }
+}
+
+constexpr int kStreamMaxReaccessPerThread = 8;
+
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    clock_stream_kernel(MetaT* meta, int64_t num_slots, int64_t* search_start, int64_t num_steps,
+                        int64_t alloc_per_step, const int64_t* reaccess,
+                        int64_t reaccess_per_step, int64_t* victims, int64_t* steps_done,
+                        int order, bool aligned, int64_t* status) {
+  using M = Meta<MetaT>;
+  __shared__ PopShared<MetaT> sh;
+  int64_t step = 0;
+  for (; step < num_steps; ++step) {
+    int64_t* out = victims + step * alloc_per_step;
+    const int rc = pop_cta<MetaT>(meta, num_slots, search_start, nullptr, alloc_per_step, out,
+                                  order, aligned, sh);
+    if (rc != KVCA_OK) {
+      if (threadIdx.x == 0) report(status, rc, step);
+      break;
+    }
+    // Victims are refilled: pin kept (it is 0), usage 1 (adapter.py:233-242
+    // gives new saves usage 1; commit at adapter.py:651).
+    for (int64_t i = threadIdx.x; i < alloc_per_step; i += blockDim.x) {
+      const int64_t v = out[i];
+      meta[v] = M::pack(M::pin(meta[v]), 1);
+    }
+    __syncthreads();
+    // Usage bump of re-accessed slots: every value is read before any write,
+    // so duplicates in one batch bump once, as index_put_ does.
+    const int64_t* ids = reaccess + step * reaccess_per_step;
+    int64_t slot_ids[kStreamMaxReaccessPerThread];
+    MetaT values[kStreamMaxReaccessPerThread];
+#pragma unroll
+    for (int u = 0; u < kStreamMaxReaccessPerThread; ++u) {
+      const int64_t i = threadIdx.x + static_cast<int64_t>(u) * blockDim.x;
+      slot_ids[u] = -1;
+      values[u] = MetaT(0);
+      if (i < reaccess_per_step) {
+        const int64_t id = ids[i];
+        if (id < 0 || id >= num_slots) {
+          report(status, KVCA_ERR_BAD_INDEX, id);
+        } else {
+          const unsigned w = meta[id];
+          values[u] = M::pack(M::pin(w), M::sat_inc(M::usage(w)));
+          slot_ids[u] = id;
+        }
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kStreamMaxReaccessPerThread; ++u)
+      if (slot_ids[u] >= 0) meta[slot_ids[u]] = values[u];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *steps_done = step;
+}
+
+// ---------------------------------------------------------------------------
+// Inspect / commit / release
+// ---------------------------------------------------------------------------
+
+template <typename MetaT>
+__global__ void inspect_load_kernel(const int64_t* l2p, int64_t num_logical, const MetaT* meta,
+                                    int64_t num_slots, const int64_t* ids, int64_t count,
+                                    int64_t* cur_out, uint8_t* resident_out, int64_t* pin_out,
+                                    MetaT* usage_out, int64_t* status) {
+  using M = Meta<MetaT>;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t id = ids[i];
+    int64_t cur = -1;
+    if (id < 0 || id >= num_logical) {
+      report(status, KVCA_ERR_BAD_INDEX, id);
+    } else {
+      cur = l2p[id];
+    }
+    bool resident = false;
+    int64_t pin = 0;
+    unsigned usage = 0u;
+    if (cur >= num_slots) {
+      report(status, KVCA_ERR_BAD_INDEX, cur);
+    } else if (cur >= 0) {
+      const unsigned w = meta[cur];
+      resident = true;
+      pin = static_cast<int64_t>(M::pin(w)) + 1;
+      usage = M::sat_inc(M::usage(w));
+    }
+    cur_out[i] = cur;
+    resident_out[i] = resident ? 1 : 0;
+    pin_out[i] = pin;
+    usage_out[i] = static_cast<MetaT>(usage);
+  }
+}
+
+template <typename MetaT>
+__global__ void inspect_save_kernel(const int64_t* l2p, int64_t num_logical, const MetaT* meta,
+                                    int64_t num_slots, const int64_t* ids, int64_t count,
+                                    int64_t* cur_out, uint8_t* existing_out, MetaT* usage_out,
+                                    int64_t* status) {
+  using M = Meta<MetaT>;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t id = ids[i];
+    int64_t cur = -1;
+    if (id < 0 || id >= num_logical) {
+      report(status, KVCA_ERR_BAD_INDEX, id);
+    } else {
+      cur = l2p[id];
+    }
+    bool existing = false;
+    unsigned usage = 1u;
+    if (cur >= num_slots) {
+      report(status, KVCA_ERR_BAD_INDEX, cur);
+    } else if (cur >= 0) {
+      existing = true;
+      usage = M::sat_inc(M::usage(meta[cur]));
+    }
+    cur_out[i] = cur;
+    existing_out[i] = existing ? 1 : 0;
+    usage_out[i] = static_cast<MetaT>(usage);
+  }
+}
+
+__device__ __forceinline__ bool in_range(int64_t x, int64_t n) { return x >= 0 && x < n; }
+
+// Every id of the call must be inside its table before anything is written,
+// as in the reference, whose torch indexing raises before mutating.  Returns
+// true (uniformly) when all ids are valid; otherwise reports the first one.
+__device__ bool all_in_range(const int64_t* ids, int64_t count, int64_t limit, int64_t* status,
+                             int* flag) {
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
+    const int64_t v = ids[i];
+    if (!in_range(v, limit)) {
+      *flag = 1;
+      report(status, KVCA_ERR_BAD_INDEX, v);
+    }
+  }
+  __syncthreads();
+  return *flag == 0;
+}
+
+// One CTA, phases separated by barriers so each phase sees the previous one.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    commit_load_kernel(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
+                       int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
+                       const int64_t* miss_ids, const int64_t* miss_slots, int64_t num_miss,
+                       const int64_t* hit_slots, const int64_t* hit_pins, const MetaT* hit_usage,
+                       int64_t num_hit, const MetaT* miss_usage, int64_t* status) {
+  using M = Meta<MetaT>;
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  if (!all_in_range(evicted, num_evicted, num_logical, status, &bad)) return;
+  if (!all_in_range(miss_ids, num_miss, num_logical, status, &bad)) return;
+  if (!all_in_range(miss_slots, num_miss, num_slots, status, &bad)) return;
+  if (!all_in_range(hit_slots, num_hit, num_slots, status, &bad)) return;
+  for (int64_t i = threadIdx.x; i < num_evicted; i += blockDim.x) l2p[evicted[i]] = -1;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < num_miss; i += blockDim.x) {
+    l2p[miss_ids[i]] = miss_slots[i];
+    p2l[miss_slots[i]] = miss_ids[i];
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < num_hit; i += blockDim.x)
+    meta[hit_slots[i]] = M::pack(hit_pins[i], hit_usage[i]);
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < num_miss; i += blockDim.x)
+    meta[miss_slots[i]] = M::pack(1, miss_usage[i]);
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    commit_save_kernel(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
+                       int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
+                       const int64_t* ids, const int64_t* slots, const MetaT* final_pins,
+                       const MetaT* final_usage, int64_t count, int64_t* status) {
+  using M = Meta<MetaT>;
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  if (!all_in_range(evicted, num_evicted, num_logical, status, &bad)) return;
+  if (!all_in_range(ids, count, num_logical, status, &bad)) return;
+  if (!all_in_range(slots, count, num_slots, status, &bad)) return;
+  for (int64_t i = threadIdx.x; i < num_evicted; i += blockDim.x) l2p[evicted[i]] = -1;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
+    l2p[ids[i]] = slots[i];
+    p2l[slots[i]] = ids[i];
+    meta[slots[i]] = M::pack(final_pins[i], final_usage[i]);
+  }
+}
+
+constexpr int kReleasePerThread = 8;
+
+// One CTA.  All ids are checked first; then every new word is computed from
+// the words as they were on entry and only then written, so an id listed
+// twice releases one pin, as the reference's index_select + index_put_ does.
+// Batches above 1024 * kReleasePerThread ids run in rounds of that size.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    release_kernel(const int64_t* l2p, int64_t num_logical, MetaT* meta, int64_t num_slots,
+                   const int64_t* ids, int64_t count, int64_t* status) {
+  using M = Meta<MetaT>;
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  if (!all_in_range(ids, count, num_logical, status, &bad)) return;
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
+    const int64_t slot = l2p[ids[i]];
+    if (!in_range(slot, num_slots)) {
+      bad = 1;
+      report(status, KVCA_ERR_BAD_INDEX, slot);
+    }
+  }
+  __syncthreads();
+  if (bad) return;
+  const int64_t round = static_cast<int64_t>(blockDim.x) * kReleasePerThread;
+  for (int64_t base = 0; base < count; base += round) {
+    int64_t slot[kReleasePerThread];
+    MetaT next[kReleasePerThread];
+#pragma unroll
+    for (int u = 0; u < kReleasePerThread; ++u) {
+      const int64_t i = base + threadIdx.x + static_cast<int64_t>(u) * blockDim.x;
+      slot[u] = -1;
+      next[u] = MetaT(0);
+      if (i < count) {
+        slot[u] = l2p[ids[i]];
+        const unsigned w = meta[slot[u]];
+        next[u] = M::pack(static_cast<int64_t>(M::pin(w)) - 1, M::usage(w));
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kReleasePerThread; ++u)
+      if (slot[u] >= 0) meta[slot[u]] = next[u];
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row mover
+// ---------------------------------------------------------------------------
+
+struct MoveParams {
+  PagedSide src_paged;
+  PagedSide dst_paged;
+  ChunkSide src_chunk;
+  ChunkSide dst_chunk;
+  int64_t num_planes;
+  int64_t num_rows;
+  int64_t row_vecs;
+  int tpr_log2;  // threads per row = 1 << tpr_log2 (a power of two <= 32)
+  int32_t flags;
+  int64_t* status;
+};
+
+template <typename V>
+__device__ __forceinline__ V ld_stream(const V* p) {
+  return __ldcs(p);
+}
+template <>
+__device__ __forceinline__ uint4 ld_stream<uint4>(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+template <typename V>
+__device__ __forceinline__ void st_stream(V* p, const V& v) {
+  __stcs(p, v);
+}
+
+// Offset of row r (without the plane term) on a paged side, or -1 when the
+// row is skipped.  Reports ids outside the table.
+__device__ __forceinline__ int64_t paged_row_offset(const PagedSide& side, int64_t r,
+                                                    int32_t flags, int64_t* status, bool lead) {
+  const int64_t idx = side.index != nullptr ? side.index[r] : r;
+  if (idx < 0) {
+    if (!(flags & KVCA_FLAG_SKIP_NEGATIVE) && lead) report(status, KVCA_ERR_BAD_INDEX, idx);
+    return -1;
+  }
+  int64_t blk = idx;
+  int64_t off = 0;
+  if (side.block_size != 1) {
+    blk = idx / side.block_size;
+    off = idx - blk * side.block_size;
+  }
+  if (blk >= side.num_blocks) {
+    if (lead) report(status, KVCA_ERR_BAD_INDEX, idx);
+    return -1;
+  }
+  return blk * side.block_stride + off * side.row_stride;
+}
+
+__device__ __forceinline__ int64_t chunk_row_offset(const ChunkSide& side, int64_t r) {
+  const int64_t c = r / side.rows_per_chunk;
+  return c * side.chunk_stride + (r - c * side.rows_per_chunk) * side.row_stride;
+}
+
+constexpr int kMoverThreads = 256;
+constexpr int kMoverUnroll = 8;
+
+// Work item g = r * num_planes + p.  Each group of 2^tpr_log2 lanes takes one
+// contiguous range of items, so consecutive items share a row: the row's
+// index is loaded and its offset computed once per row, not once per plane.
+// Each lane keeps kMoverUnroll 16-byte vectors in flight.
+template <bool kSrcPaged, bool kDstPaged, typename V>
+__global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_constant__ MoveParams p) {
+  const int tpr = 1 << p.tpr_log2;
+  const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int lane = static_cast<int>(gtid & (tpr - 1));
+  const int64_t group = gtid >> p.tpr_log2;
+  const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
+  const int64_t planes = p.num_planes;
+  const int64_t items = planes * p.num_rows;
+  const int64_t per = items / num_groups;
+  const int64_t rem = items - per * num_groups;
+  const int64_t begin = group * per + (group < rem ? group : rem);
+  const int64_t end = begin + per + (group < rem ? 1 : 0);
+  if (begin >= end) return;
+
+  int64_t r = begin / planes;
+  int64_t pl = begin - r * planes;
+  int64_t src_row = 0;
+  int64_t dst_row = 0;
+  bool row_ready = false;
+  const bool lead = lane == 0;
+  const int64_t row_vecs = p.row_vecs;
+
+  for (int64_t g = begin; g < end; ++g) {
+    if (!row_ready) {
+      row_ready = true;
+      src_row = kSrcPaged ? paged_row_offset(p.src_paged, r, p.flags, p.status, lead)
+                          : chunk_row_offset(p.src_chunk, r);
+      dst_row = kDstPaged ? paged_row_offset(p.dst_paged, r, p.flags, p.status, lead)
+                          : chunk_row_offset(p.dst_chunk, r);
+    }
+    if (src_row >= 0 && dst_row >= 0) {
+      const V* src = reinterpret_cast<const V*>(
+          kSrcPaged ? p.src_paged.planes[pl] + src_row
+                    : p.src_chunk.base + src_row + pl * p.src_chunk.plane_stride);
+      V* dst = reinterpret_cast<V*>(kDstPaged
+                                        ? p.dst_paged.planes[pl] + dst_row
+                                        : p.dst_chunk.base + dst_row + pl * p.dst_chunk.plane_stride);
+      for (int64_t b = lane; b < row_vecs; b += static_cast<int64_t>(tpr) * kMoverUnroll) {
+        V buf[kMoverUnroll];
+#pragma unroll
+        for (int u = 0; u < kMoverUnroll; ++u) {
+          const int64_t i = b + static_cast<int64_t>(u) * tpr;
+          if (i < row_vecs) buf[u] = ld_stream(src + i);
+        }
+#pragma unroll
+        for (int u = 0; u < kMoverUnroll; ++u) {
+          const int64_t i = b + static_cast<int64_t>(u) * tpr;
+          if (i < row_vecs) st_stream(dst + i, buf[u]);
+        }
+      }
+    }
+    if (++pl == planes) {
+      pl = 0;
+      ++r;
+      row_ready = false;
+    }
+  }
+}
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+template <bool kSrcPaged, bool kDstPaged, typename V>
+cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
+  auto kernel = move_rows_kernel<kSrcPaged, kDstPaged, V>;
+  static int blocks_per_sm = 0;
+  if (blocks_per_sm == 0) {
+    int b = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kMoverThreads, 0);
+    if (e != cudaSuccess) return e;
+    blocks_per_sm = b > 0 ? b : 1;
+  }
+  const int sms = device_sm_count();
+  const int64_t items = p.num_planes * p.num_rows;
+  const int64_t threads_needed = items << p.tpr_log2;
+  int64_t blocks = (threads_needed + kMoverThreads - 1) / kMoverThreads;
+  const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
+  if (blocks > resident) blocks = resident;
+  if (blocks < 1) blocks = 1;
+  kernel<<<static_cast<unsigned>(blocks), kMoverThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <bool kSrcPaged, bool kDstPaged>
+cudaError_t launch_move_vec(const MoveParams& p, int vec_bytes, cudaStream_t stream) {
+  switch (vec_bytes) {
+    case 16: return launch_move_typed<kSrcPaged, kDstPaged, uint4>(p, stream);
+    case 8: return launch_move_typed<kSrcPaged, kDstPaged, uint2>(p, stream);
+    case 4: return launch_move_typed<kSrcPaged, kDstPaged, unsigned int>(p, stream);
+    case 2: return launch_move_typed<kSrcPaged, kDstPaged, unsigned short>(p, stream);
+    default: return launch_move_typed<kSrcPaged, kDstPaged, unsigned char>(p, stream);
+  }
+}
+
+int ceil_log2(int64_t x) {
+  int l = 0;
+  while ((int64_t{1} << l) < x) ++l;
+  return l;
+}
+
+int grid_for(int64_t count, int threads) {
+  const int sms = device_sm_count();
+  int64_t blocks = (count + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 1) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+
+cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
+  MoveParams p;
+  memset(&p, 0, sizeof(p));
+  if (a.src_paged) p.src_paged = *a.src_paged;
+  if (a.dst_paged) p.dst_paged = *a.dst_paged;
+  if (a.src_chunk) p.src_chunk = *a.src_chunk;
+  if (a.dst_chunk) p.dst_chunk = *a.dst_chunk;
+  p.num_planes = a.num_planes;
+  p.num_rows = a.num_rows;
+  p.row_vecs = a.row_bytes / a.vec_bytes;
+  // A row of row_vecs vectors gets about four vectors per lane.
+  int64_t lanes = (p.row_vecs + 3) / 4;
+  if (lanes > 32) lanes = 32;
+  if (lanes < 1) lanes = 1;
+  p.tpr_log2 = ceil_log2(lanes);
+  p.flags = a.flags;
+  p.status = a.status;
+  switch (a.kind) {
+    case MoveKind::kGather: return launch_move_vec<true, false>(p, a.vec_bytes, stream);
+    case MoveKind::kScatter: return launch_move_vec<false, true>(p, a.vec_bytes, stream);
+    default: return launch_move_vec<true, true>(p, a.vec_bytes, stream);
+  }
+}
+
+#define KVCA_META_DISPATCH(bits, ...)           \
+  do {                                          \
+    if ((bits) == 16) {                         \
+      using MetaT = uint16_t;                   \
+      __VA_ARGS__;                              \
+    } else {                                    \
+      using MetaT = uint8_t;                    \
+      __VA_ARGS__;                              \
+    }                                           \
+  } while (0)
+
+cudaError_t launch_inspect_load(int meta_bits, const int64_t* l2p, int64_t num_logical,
+                                const void* meta, int64_t num_slots, const int64_t* ids,
+                                int64_t count, int64_t* cur_out, uint8_t* resident_out,
+                                int64_t* pin_out, void* usage_out, int64_t* status,
+                                cudaStream_t stream) {
+  const int threads = 256;
+  KVCA_META_DISPATCH(meta_bits, inspect_load_kernel<MetaT><<<grid_for(count, threads), threads, 0, stream>>>(
+                                    l2p, num_logical, static_cast<const MetaT*>(meta), num_slots,
+                                    ids, count, cur_out, resident_out, pin_out,
+                                    static_cast<MetaT*>(usage_out), status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_inspect_save(int meta_bits, const int64_t* l2p, int64_t num_logical,
+                                const void* meta, int64_t num_slots, const int64_t* ids,
+                                int64_t count, int64_t* cur_out, uint8_t* existing_out,
+                                void* usage_out, int64_t* status, cudaStream_t stream) {
+  const int threads = 256;
+  KVCA_META_DISPATCH(meta_bits, inspect_save_kernel<MetaT><<<grid_for(count, threads), threads, 0, stream>>>(
+                                    l2p, num_logical, static_cast<const MetaT*>(meta), num_slots,
+                                    ids, count, cur_out, existing_out,
+                                    static_cast<MetaT*>(usage_out), status));
+  return cudaGetLastError();
+}
+
+int pop_threads_for(int meta_bits, int64_t num_slots) {
+  const int64_t spv = meta_bits == 16 ? 8 : 16;
+  const int64_t vecs = (num_slots + spv - 1) / spv;
+  int64_t threads = ((vecs + 31) / 32) * 32;
+  if (threads < 32) threads = 32;
+  if (threads > 1024) threads = 1024;
+  return static_cast<int>(threads);
+}
+
+cudaError_t launch_pop(int meta_bits, int order, void* meta, int64_t num_slots,
+                       int64_t* search_start, const int64_t* blocked, int64_t num_blocked,
+                       int64_t count, int64_t* out, uint32_t* bitmap, int64_t* status,
+                       cudaStream_t stream) {
+  const int threads = pop_threads_for(meta_bits, num_slots);
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  KVCA_META_DISPATCH(meta_bits, pop_kernel<MetaT><<<1, threads, 0, stream>>>(
+                                    static_cast<MetaT*>(meta), num_slots, search_start, blocked,
+                                    num_blocked, count, out, bitmap, order, aligned, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_commit_load(int meta_bits, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                               void* meta, int64_t num_slots, const int64_t* evicted,
+                               int64_t num_evicted, const int64_t* miss_ids,
+                               const int64_t* miss_slots, int64_t num_miss,
+                               const int64_t* hit_slots, const int64_t* hit_pins,
+                               const void* hit_usage, int64_t num_hit, const void* miss_usage,
+                               int64_t* status, cudaStream_t stream) {
+  int64_t longest = num_evicted > num_miss ? num_evicted : num_miss;
+  if (num_hit > longest) longest = num_hit;
+  int threads = static_cast<int>(((longest + 31) / 32) * 32);
+  if (threads < 32) threads = 32;
+  if (threads > 1024) threads = 1024;
+  KVCA_META_DISPATCH(meta_bits, commit_load_kernel<MetaT><<<1, threads, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
+                                    evicted, num_evicted, miss_ids, miss_slots, num_miss,
+                                    hit_slots, hit_pins, static_cast<const MetaT*>(hit_usage),
+                                    num_hit, static_cast<const MetaT*>(miss_usage), status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_commit_save(int meta_bits, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                               void* meta, int64_t num_slots, const int64_t* evicted,
+                               int64_t num_evicted, const int64_t* ids, const int64_t* slots,
+                               const void* final_pins, const void* final_usage, int64_t count,
+                               int64_t* status, cudaStream_t stream) {
+  const int64_t longest = num_evicted > count ? num_evicted : count;
+  int threads = static_cast<int>(((longest + 31) / 32) * 32);
+  if (threads < 32) threads = 32;
+  if (threads > 1024) threads = 1024;
+  KVCA_META_DISPATCH(meta_bits, commit_save_kernel<MetaT><<<1, threads, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
+                                    evicted, num_evicted, ids, slots,
+                                    static_cast<const MetaT*>(final_pins),
+                                    static_cast<const MetaT*>(final_usage), count, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_release(int meta_bits, const int64_t* l2p, int64_t num_logical, void* meta,
+                           int64_t num_slots, const int64_t* ids, int64_t count, int64_t* status,
+                           cudaStream_t stream) {
+  int threads = static_cast<int>(((count + 31) / 32) * 32);
+  if (threads < 32) threads = 32;
+  if (threads > 1024) threads = 1024;
+  KVCA_META_DISPATCH(meta_bits, release_kernel<MetaT><<<1, threads, 0, stream>>>(
+                                    l2p, num_logical, static_cast<MetaT*>(meta), num_slots, ids,
+                                    count, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_clock_stream(int meta_bits, int order, void* meta, int64_t num_slots,
+                                int64_t* search_start, int64_t num_steps, int64_t alloc_per_step,
+                                const int64_t* reaccess, int64_t reaccess_per_step,
+                                int64_t* victims, int64_t* steps_done, int64_t* status,
+                                cudaStream_t stream) {
+  int threads = pop_threads_for(meta_bits, num_slots);
+  const int64_t bump_threads =
+      ((reaccess_per_step + kStreamMaxReaccessPerThread - 1) / kStreamMaxReaccessPerThread + 31) /
+      32 * 32;
+  if (bump_threads > threads) threads = static_cast<int>(bump_threads > 1024 ? 1024 : bump_threads);
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  KVCA_META_DISPATCH(meta_bits, clock_stream_kernel<MetaT><<<1, threads, 0, stream>>>(
+                                    static_cast<MetaT*>(meta), num_slots, search_start, num_steps,
+                                    alloc_per_step, reaccess, reaccess_per_step, victims,
+                                    steps_done, order, aligned, status));
+  return cudaGetLastError();
+}
+
+}  // namespace kvca

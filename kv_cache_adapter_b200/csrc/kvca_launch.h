@@ -1,0 +1,92 @@
+// Internal launch interface between the C ABI layer (binding.cpp) and the
+// sm_100a kernels (kv_adapter_cuda.cu).  Arguments are already validated by
+// the caller; every function enqueues on `stream` and returns the CUDA error
+// of the launch.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kvca.h"
+
+namespace kvca {
+
+// Row-mover side descriptors as the kernels see them (plane table by value).
+struct PagedSide {
+  uint64_t planes[KVCA_MAX_PLANES];
+  const int64_t* index;
+  int64_t num_blocks;
+  int64_t block_size;
+  int64_t block_stride;
+  int64_t row_stride;
+};
+
+struct ChunkSide {
+  uint64_t base;
+  int64_t rows_per_chunk;
+  int64_t chunk_stride;
+  int64_t row_stride;
+  int64_t plane_stride;
+};
+
+enum class MoveKind : int { kGather = 0, kScatter = 1, kCopyPaged = 2 };
+
+struct MoveArgs {
+  MoveKind kind;
+  const PagedSide* src_paged;  // gather / copy
+  const ChunkSide* src_chunk;  // scatter
+  const PagedSide* dst_paged;  // scatter / copy
+  const ChunkSide* dst_chunk;  // gather
+  int64_t num_planes;
+  int64_t num_rows;
+  int64_t row_bytes;
+  int vec_bytes;  // 16, 8, 4, 2 or 1: widest access every address allows
+  int32_t flags;
+  int64_t* status;
+};
+
+cudaError_t launch_move(const MoveArgs& args, cudaStream_t stream);
+
+cudaError_t launch_inspect_load(int meta_bits, const int64_t* l2p, int64_t num_logical,
+                                const void* meta, int64_t num_slots, const int64_t* ids,
+                                int64_t count, int64_t* cur_out, uint8_t* resident_out,
+                                int64_t* pin_out, void* usage_out, int64_t* status,
+                                cudaStream_t stream);
+
+cudaError_t launch_inspect_save(int meta_bits, const int64_t* l2p, int64_t num_logical,
+                                const void* meta, int64_t num_slots, const int64_t* ids,
+                                int64_t count, int64_t* cur_out, uint8_t* existing_out,
+                                void* usage_out, int64_t* status, cudaStream_t stream);
+
+int pop_threads_for(int meta_bits, int64_t num_slots);
+
+cudaError_t launch_pop(int meta_bits, int order, void* meta, int64_t num_slots,
+                       int64_t* search_start, const int64_t* blocked, int64_t num_blocked,
+                       int64_t count, int64_t* out, uint32_t* bitmap, int64_t* status,
+                       cudaStream_t stream);
+
+cudaError_t launch_commit_load(int meta_bits, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                               void* meta, int64_t num_slots, const int64_t* evicted,
+                               int64_t num_evicted, const int64_t* miss_ids,
+                               const int64_t* miss_slots, int64_t num_miss,
+                               const int64_t* hit_slots, const int64_t* hit_pins,
+                               const void* hit_usage, int64_t num_hit, const void* miss_usage,
+                               int64_t* status, cudaStream_t stream);
+
+cudaError_t launch_commit_save(int meta_bits, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                               void* meta, int64_t num_slots, const int64_t* evicted,
+                               int64_t num_evicted, const int64_t* ids, const int64_t* slots,
+                               const void* final_pins, const void* final_usage, int64_t count,
+                               int64_t* status, cudaStream_t stream);
+
+cudaError_t launch_release(int meta_bits, const int64_t* l2p, int64_t num_logical, void* meta,
+                           int64_t num_slots, const int64_t* ids, int64_t count, int64_t* status,
+                           cudaStream_t stream);
+
+cudaError_t launch_clock_stream(int meta_bits, int order, void* meta, int64_t num_slots,
+                                int64_t* search_start, int64_t num_steps, int64_t alloc_per_step,
+                                const int64_t* reaccess, int64_t reaccess_per_step,
+                                int64_t* victims, int64_t* steps_done, int64_t* status,
+                                cudaStream_t stream);
+
+}  // namespace kvca

@@ -1,0 +1,570 @@
+"""``kv_cache_adapter_cuda``: the torch-facing op set over the sm_100a C ABI.
+
+The metadata ops keep the names, argument order and in-place behaviour of the
+packed-slot-meta extension API that adapter.py calls on its native branch
+(csrc/ascend/adapter_meta_kernels.h:6-47 of the reference; call sites
+adapter.py:316-330, :397-415, :437-454, :477-491, :557-593, :615-645).  The
+row movers replace the torch indexing the reference uses to move KV bytes
+(adapter.py:543, :653-656, :779-787) and its slot_mapping transfer
+(adapter.py:1200-1243, :1275-1285).
+
+Every op launches on the current CUDA stream of its tensors' device.  Errors
+found on the device land in a per-device status word.  ``pop_reusable_slots``
+always reads it (its capacity error must surface before the caller moves
+data, as in the reference, whose pop synchronises at ``torch::nonzero``);
+the other ops read it when ``check`` is true (the default comes from
+KVCA_SYNC_CHECKS, on unless set to 0) and otherwise leave errors for the
+next check or ``check_status()``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from typing import Sequence
+
+import torch
+
+from . import _lib
+from .errors import InsufficientCapacityError
+
+__all__ = [
+    "pop_reusable_slots",
+    "choose_pop_launch_warps",
+    "inspect_load_requests",
+    "inspect_save_requests",
+    "commit_load_metadata",
+    "commit_save_metadata",
+    "release_metadata",
+    "clock_stream",
+    "gather_blocks",
+    "scatter_blocks",
+    "copy_blocks",
+    "gather_layers",
+    "scatter_layers",
+    "gather_tokens",
+    "scatter_tokens",
+    "check_status",
+    "library_path",
+    "PlaneTable",
+]
+
+_lib_handle = _lib.load()
+
+SYNC_CHECKS = os.getenv("KVCA_SYNC_CHECKS", "1") != "0"
+POP_ORDERS = {"grouped": _lib.KVCA_POP_ORDER_GROUPED, "prefix": _lib.KVCA_POP_ORDER_PREFIX}
+_DEFAULT_POP_ORDER = os.getenv("KVCA_POP_ORDER", "grouped")
+
+_status_words: dict[int, torch.Tensor] = {}
+_pop_bitmaps: dict[tuple[int, int, int], torch.Tensor] = {}
+
+
+def library_path() -> str:
+    return str(_lib.lib_path())
+
+
+# ---------------------------------------------------------------------------
+# plumbing
+# ---------------------------------------------------------------------------
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    if t is None or t.numel() == 0:
+        return ctypes.c_void_p(0)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _status(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _status_words.get(idx)
+    if st is None:
+        st = torch.zeros(2, dtype=torch.int64, device=torch.device("cuda", idx))
+        _status_words[idx] = st
+    return st
+
+
+def _raise_for(code: int, value: int, what: str) -> None:
+    if code == _lib.KVCA_ERR_INSUFFICIENT_CAPACITY:
+        raise InsufficientCapacityError(
+            "No reusable actual block is available; all resident blocks are pinned"
+        )
+    if code == _lib.KVCA_ERR_BAD_INDEX:
+        raise IndexError(f"{what}: index {value} is out of range")
+    if code == _lib.KVCA_ERR_BAD_ARGUMENT:
+        raise ValueError(f"{what}: invalid arguments")
+    raise RuntimeError(f"{what}: CUDA launch failed (code {code})")
+
+
+def _host_rc(rc: int, what: str) -> None:
+    if rc != _lib.KVCA_OK:
+        _raise_for(rc, 0, what)
+
+
+def check_status(device: torch.device | int | None = None, what: str = "kv_cache_adapter_cuda") -> None:
+    """Synchronise with the device's status word; raise (and clear) a latched error."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    st = _status(device)
+    code, value = st.tolist()
+    if code != 0:
+        st.zero_()
+        _raise_for(int(code), int(value), what)
+
+
+def _maybe_check(device: torch.device, check: bool | None, what: str) -> None:
+    if SYNC_CHECKS if check is None else check:
+        check_status(device, what)
+
+
+def _require(t: torch.Tensor, dtype: torch.dtype | tuple[torch.dtype, ...], name: str) -> None:
+    """1-D, contiguous, CUDA, exact dtype (kv_adapter_cuda.cu:43-51 of the reference)."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    dtypes = dtype if isinstance(dtype, tuple) else (dtype,)
+    if t.dtype not in dtypes:
+        raise TypeError(f"{name} has incorrect dtype {t.dtype}")
+    if t.dim() != 1:
+        raise ValueError(f"{name} must be 1D")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _meta_bits(slot_meta: torch.Tensor) -> int:
+    if slot_meta.dtype == torch.uint8:
+        return 8
+    if slot_meta.dtype == torch.uint16:
+        return 16
+    raise TypeError(f"slot_meta must be uint8 or uint16, got {slot_meta.dtype}")
+
+
+_META_DTYPES = (torch.uint8, torch.uint16)
+
+# ---------------------------------------------------------------------------
+# slot metadata (packed slot_meta ABI)
+# ---------------------------------------------------------------------------
+
+
+def inspect_load_requests(logical_to_physical: torch.Tensor, slot_meta: torch.Tensor,
+                          logical_block_ids: torch.Tensor, *, check: bool | None = None):
+    """-> [current_physical:int64, resident:bool, updated_pins:int64, updated_usage:meta]."""
+    _require(logical_to_physical, torch.int64, "logical_to_physical")
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    _require(logical_block_ids, torch.int64, "logical_block_ids")
+    dev = logical_block_ids.device
+    k = logical_block_ids.numel()
+    cur = torch.empty(k, dtype=torch.int64, device=dev)
+    resident = torch.empty(k, dtype=torch.bool, device=dev)
+    pins = torch.empty(k, dtype=torch.int64, device=dev)
+    usage = torch.empty(k, dtype=slot_meta.dtype, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_inspect_load_requests(
+            _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
+            _ptr(slot_meta), slot_meta.numel(), _ptr(logical_block_ids), k, _ptr(cur),
+            _ptr(resident), _ptr(pins), _ptr(usage), _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "inspect_load_requests")
+    _maybe_check(dev, check, "inspect_load_requests")
+    return [cur, resident, pins, usage]
+
+
+def inspect_save_requests(logical_to_physical: torch.Tensor, slot_meta: torch.Tensor,
+                          logical_block_ids: torch.Tensor, *, check: bool | None = None):
+    """-> [current_physical:int64, existing:bool, final_usage:meta]."""
+    _require(logical_to_physical, torch.int64, "logical_to_physical")
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    _require(logical_block_ids, torch.int64, "logical_block_ids")
+    dev = logical_block_ids.device
+    k = logical_block_ids.numel()
+    cur = torch.empty(k, dtype=torch.int64, device=dev)
+    existing = torch.empty(k, dtype=torch.bool, device=dev)
+    usage = torch.empty(k, dtype=slot_meta.dtype, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_inspect_save_requests(
+            _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
+            _ptr(slot_meta), slot_meta.numel(), _ptr(logical_block_ids), k, _ptr(cur),
+            _ptr(existing), _ptr(usage), _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "inspect_save_requests")
+    _maybe_check(dev, check, "inspect_save_requests")
+    return [cur, existing, usage]
+
+
+def _bitmap(dev: torch.device, num_slots: int) -> torch.Tensor:
+    words = (num_slots + 31) // 32
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(dev).cuda_stream, words)
+    bm = _pop_bitmaps.get(key)
+    if bm is None:
+        bm = torch.zeros(words, dtype=torch.int32, device=dev)
+        _pop_bitmaps[key] = bm
+    return bm
+
+
+def pop_reusable_slots(slot_meta: torch.Tensor, search_start: torch.Tensor,
+                       blocked_slot_ids: torch.Tensor, count: int, *,
+                       order: str | None = None) -> torch.Tensor:
+    """Clock sweep; ages ``slot_meta`` and advances ``search_start`` in place.
+
+    ``order="grouped"`` (default) follows the reference's strict path
+    (adapter.py:472-525); ``order="prefix"`` the reference CUDA kernel's
+    selection (kv_adapter_cuda.cu:101-231).  Raises InsufficientCapacityError
+    when fewer than ``count`` slots are reusable, before changing anything.
+    """
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    _require(search_start, torch.int64, "search_start")
+    _require(blocked_slot_ids, torch.int64, "blocked_slot_ids")
+    if search_start.numel() != 1:
+        raise ValueError("search_start must have shape (1,)")
+    count = int(count)
+    if count < 0:
+        raise ValueError("count must be non-negative")
+    dev = slot_meta.device
+    out = torch.empty(count, dtype=torch.int64, device=dev)
+    if count == 0:
+        return out
+    n = slot_meta.numel()
+    if n == 0:
+        raise InsufficientCapacityError(
+            "No reusable actual block is available; all resident blocks are pinned")
+    order_code = POP_ORDERS[order or _DEFAULT_POP_ORDER]
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_pop_reusable_slots(
+            _meta_bits(slot_meta), order_code, _ptr(slot_meta), n, _ptr(search_start),
+            _ptr(blocked_slot_ids), blocked_slot_ids.numel(), count, _ptr(out),
+            _ptr(_bitmap(dev, n)), _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "pop_reusable_slots")
+    check_status(dev, "pop_reusable_slots")
+    return out
+
+
+def choose_pop_launch_warps(num_slots: int) -> int:
+    """Warps per CTA the pop kernel uses for ``num_slots`` slots (binding.cpp:74-78)."""
+    if int(num_slots) <= 0:
+        raise ValueError("num_slots must be positive")
+    return int(_lib_handle.kvca_choose_pop_launch_warps(int(num_slots)))
+
+
+def commit_load_metadata(logical_to_physical, physical_to_logical, slot_meta,
+                         evicted_logical_block_ids, miss_logical_block_ids, miss_physical_slot_ids,
+                         hit_slot_ids, hit_pin_counts, hit_usage_counts, miss_usage_counts, *,
+                         check: bool | None = None) -> None:
+    _require(logical_to_physical, torch.int64, "logical_to_physical")
+    _require(physical_to_logical, torch.int64, "physical_to_logical")
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    for t, name in ((evicted_logical_block_ids, "evicted_logical_block_ids"),
+                    (miss_logical_block_ids, "miss_logical_block_ids"),
+                    (miss_physical_slot_ids, "miss_physical_slot_ids"),
+                    (hit_slot_ids, "hit_slot_ids")):
+        _require(t, torch.int64, name)
+    dev = slot_meta.device
+    hit_pin_counts = hit_pin_counts.to(device=dev, dtype=torch.int64).contiguous()
+    hit_usage_counts = hit_usage_counts.to(device=dev, dtype=slot_meta.dtype).contiguous()
+    miss_usage_counts = miss_usage_counts.to(device=dev, dtype=slot_meta.dtype).contiguous()
+    if miss_logical_block_ids.numel() != miss_physical_slot_ids.numel() or \
+            miss_usage_counts.numel() != miss_physical_slot_ids.numel():
+        raise ValueError("miss ids, slots and usage counts must have the same length")
+    if hit_pin_counts.numel() != hit_slot_ids.numel() or hit_usage_counts.numel() != hit_slot_ids.numel():
+        raise ValueError("hit slots, pins and usage counts must have the same length")
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_commit_load_metadata(
+            _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
+            _ptr(physical_to_logical), _ptr(slot_meta), slot_meta.numel(),
+            _ptr(evicted_logical_block_ids), evicted_logical_block_ids.numel(),
+            _ptr(miss_logical_block_ids), _ptr(miss_physical_slot_ids),
+            miss_logical_block_ids.numel(), _ptr(hit_slot_ids), _ptr(hit_pin_counts),
+            _ptr(hit_usage_counts), hit_slot_ids.numel(), _ptr(miss_usage_counts),
+            _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "commit_load_metadata")
+    _maybe_check(dev, check, "commit_load_metadata")
+
+
+def commit_save_metadata(logical_to_physical, physical_to_logical, slot_meta,
+                         evicted_logical_block_ids, logical_block_ids, physical_slot_ids,
+                         final_pin_counts, final_usage_counts, *, check: bool | None = None) -> None:
+    _require(logical_to_physical, torch.int64, "logical_to_physical")
+    _require(physical_to_logical, torch.int64, "physical_to_logical")
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    for t, name in ((evicted_logical_block_ids, "evicted_logical_block_ids"),
+                    (logical_block_ids, "logical_block_ids"),
+                    (physical_slot_ids, "physical_slot_ids")):
+        _require(t, torch.int64, name)
+    dev = slot_meta.device
+    final_pin_counts = final_pin_counts.to(device=dev, dtype=slot_meta.dtype).contiguous()
+    final_usage_counts = final_usage_counts.to(device=dev, dtype=slot_meta.dtype).contiguous()
+    k = logical_block_ids.numel()
+    if physical_slot_ids.numel() != k or final_pin_counts.numel() != k or final_usage_counts.numel() != k:
+        raise ValueError("ids, slots, pins and usage counts must have the same length")
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_commit_save_metadata(
+            _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
+            _ptr(physical_to_logical), _ptr(slot_meta), slot_meta.numel(),
+            _ptr(evicted_logical_block_ids), evicted_logical_block_ids.numel(),
+            _ptr(logical_block_ids), _ptr(physical_slot_ids), _ptr(final_pin_counts),
+            _ptr(final_usage_counts), k, _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "commit_save_metadata")
+    _maybe_check(dev, check, "commit_save_metadata")
+
+
+def release_metadata(logical_to_physical, slot_meta, logical_block_ids, *,
+                     check: bool | None = None) -> None:
+    _require(logical_to_physical, torch.int64, "logical_to_physical")
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    _require(logical_block_ids, torch.int64, "logical_block_ids")
+    dev = slot_meta.device
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_release_metadata(
+            _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
+            _ptr(slot_meta), slot_meta.numel(), _ptr(logical_block_ids), logical_block_ids.numel(),
+            _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "release_metadata")
+    _maybe_check(dev, check, "release_metadata")
+
+
+def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps: int,
+                 alloc_per_step: int, reaccess: torch.Tensor, reaccess_per_step: int, *,
+                 victims: torch.Tensor | None = None, order: str | None = None,
+                 check: bool | None = None):
+    """Run ``num_steps`` of (pop, refill victims with usage 1, bump re-accessed
+    slots) in one launch.  Returns (victims, steps_done tensor)."""
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    _require(search_start, torch.int64, "search_start")
+    _require(reaccess, torch.int64, "reaccess")
+    dev = slot_meta.device
+    num_steps, alloc_per_step, reaccess_per_step = int(num_steps), int(alloc_per_step), int(reaccess_per_step)
+    if reaccess.numel() < num_steps * reaccess_per_step:
+        raise ValueError("reaccess holds fewer than num_steps * reaccess_per_step ids")
+    if victims is None:
+        victims = torch.empty(num_steps * alloc_per_step, dtype=torch.int64, device=dev)
+    else:
+        _require(victims, torch.int64, "victims")
+        if victims.numel() < num_steps * alloc_per_step:
+            raise ValueError("victims is too small")
+    steps_done = torch.zeros(1, dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_clock_stream(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(slot_meta),
+            slot_meta.numel(), _ptr(search_start), num_steps, alloc_per_step, _ptr(reaccess),
+            reaccess_per_step, _ptr(victims), _ptr(steps_done), _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "clock_stream")
+    _maybe_check(dev, check, "clock_stream")
+    return victims, steps_done
+
+
+# ---------------------------------------------------------------------------
+# row movers
+# ---------------------------------------------------------------------------
+
+
+def _dense_suffix(t: torch.Tensor, start: int) -> bool:
+    """True when dims ``start:`` of ``t`` are laid out contiguously."""
+    expected = 1
+    for size, stride in zip(reversed(t.shape[start:]), reversed(t.stride()[start:])):
+        if size != 1 and stride != expected:
+            return False
+        expected *= size
+    return True
+
+
+class PlaneTable:
+    """Plane table of a paged cache side: one device address per plane (layer x
+    K/V), all planes sharing shape, dtype, strides and device.
+
+    Build it once with ``PlaneTable(planes, row_dim)`` and pass it wherever a
+    list of planes is accepted, to skip re-validating the planes on every call.
+    ``row_dim`` is 1 for block-granular moves (rows are whole blocks) and 2
+    for token-granular moves (planes are ``(num_blocks, block_size, *row)``).
+    """
+
+    def __init__(self, planes: Sequence[torch.Tensor], row_dim: int = 1, name: str = "caches"):
+        if isinstance(planes, torch.Tensor):
+            planes = [planes]
+        planes = list(planes)
+        if not planes:
+            raise ValueError(f"{name} must hold at least one plane")
+        if len(planes) > _lib.KVCA_MAX_PLANES:
+            raise ValueError(f"{name}: at most {_lib.KVCA_MAX_PLANES} planes per call")
+        first = planes[0]
+        if not first.is_cuda:
+            raise ValueError(f"{name} must be CUDA tensors")
+        if first.dim() < row_dim:
+            raise ValueError(f"{name} planes must have at least {row_dim} dims")
+        for p in planes[1:]:
+            if (p.shape != first.shape or p.dtype != first.dtype or p.stride() != first.stride()
+                    or p.device != first.device):
+                raise ValueError(f"{name} planes must share shape, dtype, strides and device")
+        if not _dense_suffix(first, row_dim):
+            raise ValueError(f"{name}: the row dims of each plane must be contiguous")
+        esz = first.element_size()
+        self.planes = planes
+        self.device = first.device
+        self.dtype = first.dtype
+        self.num_blocks = int(first.shape[0])
+        self.block_size = int(first.shape[1]) if row_dim == 2 else 1
+        self.row_shape = tuple(first.shape[row_dim:])
+        self.row_bytes = int(math.prod(self.row_shape)) * esz
+        self.block_stride = int(first.stride(0)) * esz
+        self.row_stride = int(first.stride(1)) * esz if row_dim == 2 else self.row_bytes
+        self.row_dim = row_dim
+        self._table = (ctypes.c_uint64 * len(planes))(*[p.data_ptr() for p in planes])
+
+    def desc(self, index: torch.Tensor | None) -> _lib.PagedDesc:
+        return _lib.PagedDesc(
+            ctypes.cast(self._table, ctypes.POINTER(ctypes.c_uint64)), self.num_blocks,
+            self.block_size, self.block_stride, self.row_stride,
+            ctypes.c_void_p(index.data_ptr()) if index is not None and index.numel() else None)
+
+
+def _planes(caches, row_dim: int, name: str) -> PlaneTable:
+    if isinstance(caches, PlaneTable):
+        if caches.row_dim != row_dim:
+            raise ValueError(f"{name}: plane table built for row_dim {caches.row_dim}, need {row_dim}")
+        return caches
+    return PlaneTable(caches, row_dim, name)
+
+
+def _chunk_desc(t: torch.Tensor, rows_per_chunk: int, num_planes: int, row_bytes: int) -> _lib.ChunkDesc:
+    plane_stride = rows_per_chunk * row_bytes
+    return _lib.ChunkDesc(t.data_ptr(), rows_per_chunk, num_planes * plane_stride, row_bytes,
+                          plane_stride)
+
+
+def _require_index(idx: torch.Tensor, device: torch.device, name: str) -> None:
+    _require(idx, torch.int64, name)
+    if idx.device != device:
+        raise ValueError(f"{name} must be on {device}")
+
+
+def _launch_move(fn_name: str, src, dst, num_planes: int, num_rows: int, row_bytes: int,
+                 flags: int, device: torch.device, check: bool | None) -> None:
+    if num_rows == 0:
+        return
+    with torch.cuda.device(device):
+        rc = getattr(_lib_handle, fn_name)(
+            ctypes.byref(src), ctypes.byref(dst), num_planes, num_rows, row_bytes, flags,
+            _ptr(_status(device)), _stream(device))
+    _host_rc(rc, fn_name)
+    _maybe_check(device, check, fn_name)
+
+
+def _chunk_tensor(out: torch.Tensor | None, shape: tuple[int, ...], dtype, device, name: str) -> torch.Tensor:
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    if tuple(out.shape) != tuple(shape) or out.dtype != dtype or out.device != device:
+        raise ValueError(f"{name} must be {tuple(shape)} {dtype} on {device}")
+    if not out.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return out
+
+
+def gather_blocks(actual_blocks: torch.Tensor, slot_ids: torch.Tensor,
+                  out: torch.Tensor | None = None, *, check: bool | None = None) -> torch.Tensor:
+    """``actual_blocks.index_select(0, slot_ids)`` (adapter.py:543)."""
+    pl = _planes([actual_blocks], 1, "actual_blocks")
+    _require_index(slot_ids, pl.device, "slot_ids")
+    k = slot_ids.numel()
+    out = _chunk_tensor(out, (k, *pl.row_shape), pl.dtype, pl.device, "out")
+    _launch_move("kvca_gather", pl.desc(slot_ids), _chunk_desc(out, max(k, 1), 1, pl.row_bytes),
+                 1, k, pl.row_bytes, 0, pl.device, check)
+    return out
+
+
+def scatter_blocks(actual_blocks: torch.Tensor, slot_ids: torch.Tensor, block_data: torch.Tensor,
+                   *, check: bool | None = None) -> None:
+    """``actual_blocks.index_copy_(0, slot_ids, block_data)`` (adapter.py:653-656)."""
+    pl = _planes([actual_blocks], 1, "actual_blocks")
+    _require_index(slot_ids, pl.device, "slot_ids")
+    k = slot_ids.numel()
+    _chunk_tensor(block_data, (k, *pl.row_shape), pl.dtype, pl.device, "block_data")
+    _launch_move("kvca_scatter", _chunk_desc(block_data, max(k, 1), 1, pl.row_bytes),
+                 pl.desc(slot_ids), 1, k, pl.row_bytes, 0, pl.device, check)
+
+
+def copy_blocks(src_blocks: torch.Tensor, src_ids: torch.Tensor, dst_blocks: torch.Tensor,
+                dst_ids: torch.Tensor, *, check: bool | None = None) -> None:
+    """``dst.index_copy_(0, dst_ids, src.index_select(0, src_ids))`` in one pass
+    (adapter.py:779-787).  ``src_blocks`` and ``dst_blocks`` must not overlap."""
+    s = _planes([src_blocks], 1, "src_blocks")
+    d = _planes([dst_blocks], 1, "dst_blocks")
+    if s.row_bytes != d.row_bytes or s.dtype != d.dtype or s.device != d.device:
+        raise ValueError("src_blocks and dst_blocks must share block shape, dtype and device")
+    _require_index(src_ids, s.device, "src_ids")
+    _require_index(dst_ids, s.device, "dst_ids")
+    if src_ids.numel() != dst_ids.numel():
+        raise ValueError("src_ids and dst_ids must have the same length")
+    _launch_move("kvca_copy_paged", s.desc(src_ids), d.desc(dst_ids), 1, src_ids.numel(),
+                 s.row_bytes, 0, s.device, check)
+
+
+def _chunks_of(k: int, per_chunk: int | None, what: str) -> tuple[int, int]:
+    per = k if per_chunk is None else int(per_chunk)
+    if per < 1 or (k and k % per):
+        raise ValueError(f"{what} ({k}) must be a positive multiple of the chunk length ({per})")
+    return (k // per if per else 0), per
+
+
+def gather_layers(caches: Sequence[torch.Tensor], slot_ids: torch.Tensor,
+                  out: torch.Tensor | None = None, *, blocks_per_chunk: int | None = None,
+                  check: bool | None = None) -> torch.Tensor:
+    """Gather blocks ``slot_ids`` of every plane (layer x K/V) in one launch into
+    chunks ``(num_chunks, num_planes, blocks_per_chunk, *block)``: per plane,
+    ``cache.index_select(0, slot_ids)`` (adapter.py:543)."""
+    pl = _planes(caches, 1, "caches")
+    _require_index(slot_ids, pl.device, "slot_ids")
+    k = slot_ids.numel()
+    nc, cb = _chunks_of(k, blocks_per_chunk, "len(slot_ids)") if k else (0, max(1, blocks_per_chunk or 1))
+    P = len(pl.planes)
+    out = _chunk_tensor(out, (nc, P, cb, *pl.row_shape), pl.dtype, pl.device, "out")
+    _launch_move("kvca_gather", pl.desc(slot_ids), _chunk_desc(out, cb, P, pl.row_bytes), P, k,
+                 pl.row_bytes, 0, pl.device, check)
+    return out
+
+
+def scatter_layers(caches: Sequence[torch.Tensor], slot_ids: torch.Tensor, chunks: torch.Tensor,
+                   *, blocks_per_chunk: int | None = None, check: bool | None = None) -> None:
+    """Inverse of gather_layers: per plane ``cache.index_copy_(0, slot_ids, ...)``."""
+    pl = _planes(caches, 1, "caches")
+    _require_index(slot_ids, pl.device, "slot_ids")
+    k = slot_ids.numel()
+    nc, cb = _chunks_of(k, blocks_per_chunk, "len(slot_ids)") if k else (0, max(1, blocks_per_chunk or 1))
+    P = len(pl.planes)
+    _chunk_tensor(chunks, (nc, P, cb, *pl.row_shape), pl.dtype, pl.device, "chunks")
+    _launch_move("kvca_scatter", _chunk_desc(chunks, cb, P, pl.row_bytes), pl.desc(slot_ids), P,
+                 k, pl.row_bytes, 0, pl.device, check)
+
+
+def gather_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor,
+                  out: torch.Tensor | None = None, *, tokens_per_chunk: int | None = None,
+                  check: bool | None = None) -> torch.Tensor:
+    """Token rows ``slot_mapping[t]`` (= block * block_size + offset,
+    adapter.py:1275-1285) of every plane ``(num_blocks, block_size, *row)`` into
+    chunks ``(num_chunks, num_planes, tokens_per_chunk, *row)``.  Negative
+    mappings are padding: their rows are left untouched in ``out``."""
+    pl = _planes(caches, 2, "caches")
+    _require_index(slot_mapping, pl.device, "slot_mapping")
+    t = slot_mapping.numel()
+    nc, tpc = _chunks_of(t, tokens_per_chunk, "len(slot_mapping)") if t else (0, max(1, tokens_per_chunk or 1))
+    P = len(pl.planes)
+    out = _chunk_tensor(out, (nc, P, tpc, *pl.row_shape), pl.dtype, pl.device, "out")
+    _launch_move("kvca_gather", pl.desc(slot_mapping), _chunk_desc(out, tpc, P, pl.row_bytes), P,
+                 t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE, pl.device, check)
+    return out
+
+
+def scatter_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor, chunks: torch.Tensor,
+                   *, tokens_per_chunk: int | None = None, check: bool | None = None) -> None:
+    """reshape-and-cache: token row t of every plane goes to ``slot_mapping[t]``;
+    negative mappings are skipped."""
+    pl = _planes(caches, 2, "caches")
+    _require_index(slot_mapping, pl.device, "slot_mapping")
+    t = slot_mapping.numel()
+    nc, tpc = _chunks_of(t, tokens_per_chunk, "len(slot_mapping)") if t else (0, max(1, tokens_per_chunk or 1))
+    P = len(pl.planes)
+    _chunk_tensor(chunks, (nc, P, tpc, *pl.row_shape), pl.dtype, pl.device, "chunks")
+    _launch_move("kvca_scatter", _chunk_desc(chunks, tpc, P, pl.row_bytes), pl.desc(slot_mapping),
+                 P, t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE, pl.device, check)

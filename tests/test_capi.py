@@ -1,0 +1,71 @@
+"""CPU: the C ABI library loads, exports every entry point declared in
+include/kvca.h, and rejects bad host-side arguments before touching a device."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+from conftest import REPO
+from kv_cache_adapter_b200 import _lib
+
+HEADER = REPO / "include" / "kvca.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kvca_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_expected_entry_points():
+    names = declared_functions()
+    assert names == sorted(_lib.SIGNATURES), "ctypes signatures and include/kvca.h disagree"
+    for name in ("kvca_pop_reusable_slots", "kvca_inspect_load_requests", "kvca_inspect_save_requests",
+                 "kvca_commit_load_metadata", "kvca_commit_save_metadata", "kvca_release_metadata",
+                 "kvca_gather", "kvca_scatter", "kvca_copy_paged", "kvca_clock_stream"):
+        assert name in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_scratch_sizes():
+    lib = _lib.load()
+    assert lib.kvca_abi_version() == 1
+    assert lib.kvca_pop_scratch_bytes(0) == 0
+    assert lib.kvca_pop_scratch_bytes(1) == 4
+    assert lib.kvca_pop_scratch_bytes(32) == 4
+    assert lib.kvca_pop_scratch_bytes(33) == 8
+    assert lib.kvca_pop_scratch_bytes(1 << 20) == (1 << 20) // 8
+    assert lib.kvca_choose_pop_launch_warps(1) == 1
+    assert lib.kvca_choose_pop_launch_warps(1 << 20) == 32
+
+
+def test_host_side_argument_checks_need_no_device():
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    bad = _lib.KVCA_ERR_BAD_ARGUMENT
+    # unsupported slot-meta width
+    assert lib.kvca_release_metadata(7, null, 1, null, 1, null, 1, null, null) == bad
+    # unknown pop order, empty table, negative count
+    assert lib.kvca_pop_reusable_slots(8, 9, null, 4, null, null, 0, 1, null, null, null, null) == bad
+    assert lib.kvca_pop_reusable_slots(8, 0, null, 0, null, null, 0, 1, null, null, null, null) == bad
+    assert lib.kvca_pop_reusable_slots(8, 0, null, 4, null, null, 0, -1, null, null, null, null) == bad
+    # count 0 is a no-op that succeeds without any pointer
+    assert lib.kvca_pop_reusable_slots(8, 0, null, 4, null, null, 0, 0, null, null, null, null) == 0
+    assert lib.kvca_inspect_load_requests(8, null, 1, null, 1, null, 0, null, null, null, null, null, null) == 0
+    # missing pointers with work to do
+    assert lib.kvca_inspect_save_requests(8, null, 1, null, 1, null, 3, null, null, null, null, null) == bad
+    # too many re-accesses per step for the stream kernel
+    assert lib.kvca_clock_stream(8, 0, null, 4, null, 1, 1, null, 9000, null, null, null, null) == bad
+    # row movers: plane count and row size limits, missing descriptors
+    src = _lib.PagedDesc()
+    dst = _lib.ChunkDesc()
+    assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), 0, 4, 16, 0, null, null) == bad
+    assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), _lib.KVCA_MAX_PLANES + 1, 4, 16, 0, null, null) == bad
+    assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), 1, 4, 0, 0, null, null) == bad
+    assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), 1, 4, 16, 0, null, null) == bad  # null planes
+    assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), 1, 0, 16, 0, null, null) == 0  # nothing to move

@@ -1,0 +1,103 @@
+"""GPU parity: the device-resident clock stream (pop -> refill -> Zipf re-access
+bumps) against recorded reference streams and the oracle, up to the full
+clock-stress size (1,048,576 slots, 200k allocations)."""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from kv_cache_adapter_b200 import adapter as adapter_mod
+from kv_cache_adapter_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as m
+
+    return m
+
+
+def _pack16(pins, usage):
+    return ((pins.to(torch.int32) & 255) | ((usage.to(torch.int32) & 255) << 8)).to(torch.uint16)
+
+
+def test_recorded_reference_streams(ops, golden_dir):
+    for rec in json.loads((golden_dir / "clock_stream.json").read_text()):
+        p = rec["params"]
+        meta = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta).to(DEV)
+        ss = torch.zeros(1, dtype=torch.int64, device=DEV)
+        victims, done = ops.clock_stream(meta, ss, p["num_steps"], p["alloc_per_step"],
+                                         workloads.zipf_reaccess(p).to(DEV), p["reaccess_per_step"])
+        assert int(done) == rec["steps_done"]
+        assert victims.tolist() == rec["victims"]
+        assert workloads.sha256_of(meta) == rec["final_slot_meta_sha256"]
+        assert int(ss[0]) == rec["final_search_start"]
+
+
+def _run_both(ops, p, *, order="grouped", bits=8):
+    pack = adapter_mod._pack_slot_meta if bits == 8 else _pack16
+    meta_h = workloads.clock_initial_meta(p, pack)
+    reacc = workloads.zipf_reaccess(p)
+    ss_h = torch.zeros(1, dtype=torch.int64)
+    want, done_h, rc = oracle.clock_stream(meta_h, ss_h, p["num_steps"], p["alloc_per_step"], reacc,
+                                           p["reaccess_per_step"], order=order)
+    meta_d = workloads.clock_initial_meta(p, pack).to(DEV)
+    ss_d = torch.zeros(1, dtype=torch.int64, device=DEV)
+    got, done_d = ops.clock_stream(meta_d, ss_d, p["num_steps"], p["alloc_per_step"], reacc.to(DEV),
+                                   p["reaccess_per_step"], order=order, check=False)
+    torch.cuda.synchronize()
+    return (want, done_h, rc, meta_h, ss_h), (got, int(done_d), meta_d, ss_d)
+
+
+@pytest.mark.parametrize("order", ["grouped", "prefix"])
+@pytest.mark.parametrize("bits", [8, 16])
+@pytest.mark.parametrize("k,m,usage_hi", [(1, 1, 3), (256, 256, 3), (5, 40, 15), (64, 8, 1)])
+def test_streams_match_oracle(ops, order, bits, k, m, usage_hi):
+    p = workloads.clock_params(65536 + 37, 3000 if k == 1 else 400, k, m, seed=4242 + k + m,
+                               usage_hi=usage_hi)
+    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p, order=order, bits=bits)
+    assert rc == 0 and done_h == done_d == p["num_steps"]
+    assert torch.equal(got.cpu(), want)
+    assert np.array_equal(meta_d.cpu().numpy(), meta_h.numpy())
+    assert int(ss_d[0]) == int(ss_h[0])
+    ops.check_status(DEV)
+
+
+@pytest.mark.parametrize("k", [1, 256])
+def test_full_size_clock_stress_matches_oracle(ops, k):
+    """1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations with one
+    Zipf(1.1) re-access per allocation: identical victim sequence and final
+    usage array."""
+    steps = 200_000 // k
+    p = workloads.clock_params(1 << 20, steps, k, k, seed=1234)
+    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p)
+    assert rc == 0 and done_h == done_d == steps
+    assert torch.equal(got.cpu(), want)
+    assert workloads.sha256_of(meta_d) == workloads.sha256_of(meta_h)
+    assert int(ss_d[0]) == int(ss_h[0])
+    ops.check_status(DEV)
+
+
+def test_stream_stops_on_insufficient_capacity(ops):
+    from kv_cache_adapter_b200.errors import InsufficientCapacityError
+
+    # 10 slots, 3 pinned: 7 reusable; victims are refilled unpinned, so the
+    # stream only fails when a single step asks for more than 7.
+    pins = torch.tensor([1, 0, 0, 1, 0, 0, 1, 0, 0, 0])
+    meta = adapter_mod._pack_slot_meta(pins, torch.zeros(10, dtype=torch.int64)).to(DEV)
+    ss = torch.zeros(1, dtype=torch.int64, device=DEV)
+    reacc = torch.zeros(0, dtype=torch.int64, device=DEV)
+    victims, done = ops.clock_stream(meta, ss, 3, 8, reacc, 0, check=False)
+    assert int(done) == 0
+    with pytest.raises(InsufficientCapacityError):
+        ops.check_status(DEV)
+    victims, done = ops.clock_stream(meta, ss, 3, 7, reacc, 0)
+    assert int(done) == 3
