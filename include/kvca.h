@@ -48,6 +48,7 @@ typedef struct CUstream_st* kvca_stream_t; /* same type as cudaStream_t */
 #define KVCA_ERR_BAD_INDEX 2             /* reference: IndexError from index_select / index_fill_ */
 #define KVCA_ERR_BAD_ARGUMENT 3          /* reference: TORCH_CHECK, kv_adapter_cuda.cu:43-51 */
 #define KVCA_ERR_CUDA 4                  /* launch or runtime failure */
+#define KVCA_ERR_SIZE_LIMIT 5            /* table larger than a fixed-capacity entry point takes */
 
 /* Clock-sweep victim order (see kvca_pop_reusable_slots). */
 #define KVCA_POP_ORDER_GROUPED 0
@@ -123,6 +124,33 @@ int kvca_pop_reusable_slots(int meta_bits, int order, void* d_slot_meta, int64_t
                             int64_t num_blocked, int64_t count, int64_t* d_out,
                             uint32_t* d_scratch_bitmap, int64_t* d_status,
                             kvca_stream_t stream);
+
+/*
+ * kvca_pop_reusable_slots for callers that cannot allocate device memory.
+ * No counterpart in the reference: it exists for callers that may not call
+ * cudaMalloc (a serving loop whose device memory is reserved up front and
+ * must not touch the allocator again, host runtimes that hold no device
+ * allocator, embeddings whose memory budget is fixed at start-up).  Same
+ * semantics and result as kvca_pop_reusable_slots, but the blocked-slot
+ * bitmap is a device array inside this library (128 KiB per GPU that loads
+ * the library, held until the process exits), so there is no scratch
+ * argument.
+ *   - num_slots above KVCA_NOALLOC_MAX_SLOTS is rejected with
+ *     KVCA_ERR_SIZE_LIMIT before anything is launched.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls on a device share the array: calls that may overlap on the
+ *     GPU (different streams without ordering between them) race and must
+ *     not be issued.
+ *   - Allocates nothing (no cudaMalloc, no cudaFree, no allocating library
+ *     routine).
+ */
+#define KVCA_NOALLOC_MAX_SLOTS 1048576
+int kvca_pop_reusable_slots_noalloc(int meta_bits, int order, void* d_slot_meta,
+                                    int64_t num_slots, int64_t* d_search_start,
+                                    const int64_t* d_blocked, int64_t num_blocked, int64_t count,
+                                    int64_t* d_out, int64_t* d_status, kvca_stream_t stream);
 
 /* Replaces choose_pop_launch_warps (csrc/binding.cpp:74-78): warps per CTA
  * of the pop kernel for a table of num_slots slots. */

@@ -17,6 +17,8 @@ KVCA_ERR_INSUFFICIENT_CAPACITY = 1
 KVCA_ERR_BAD_INDEX = 2
 KVCA_ERR_BAD_ARGUMENT = 3
 KVCA_ERR_CUDA = 4
+KVCA_ERR_SIZE_LIMIT = 5
+KVCA_NOALLOC_MAX_SLOTS = 1048576
 
 KVCA_POP_ORDER_GROUPED = 0
 KVCA_POP_ORDER_PREFIX = 1
@@ -70,6 +72,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvca_pop_reusable_slots": (
         c_int,
         [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
+    "kvca_pop_reusable_slots_noalloc": (
+        c_int, [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_i64, c_ptr, c_ptr, c_ptr],
     ),
     "kvca_choose_pop_launch_warps": (c_i64, [c_i64]),
     "kvca_commit_load_metadata": (

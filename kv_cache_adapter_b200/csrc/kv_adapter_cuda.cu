@@ -989,3 +989,111 @@ cudaError_t launch_clock_stream(int meta_bits, int order, void* meta, int64_t nu
 }
 
 }  // namespace kvca
+
+// ---------------------------------------------------------------------------
+// Clock sweep for callers that cannot allocate device memory
+// ---------------------------------------------------------------------------
+//
+// kvca_pop_reusable_slots needs a blocked-slot bitmap from its caller.  Some
+// callers cannot provide one: a serving loop whose device memory is reserved
+// up front and must not touch the allocator again, a host language runtime
+// that owns no device allocator, or an embedding whose memory budget is fixed
+// at start-up.  For them the bitmap lives in a
+// file-scope device array instead, sized for at most KVCA_NOALLOC_MAX_SLOTS
+// slots (128 KiB), which every GPU that loads this library holds until the
+// process exits.
+
+#include <mutex>
+
+namespace kvca {
+namespace {
+
+constexpr int64_t kNoAllocWords = KVCA_NOALLOC_MAX_SLOTS / 32;
+constexpr int kMaxDevices = 64;
+
+// Shared by every call on a device; it keeps whatever the last call left.
+static __device__ __align__(256) uint32_t g_pop_scratch_bitmap[kNoAllocWords];
+
+std::mutex g_scratch_mutex;
+uint32_t* g_scratch_address[kMaxDevices] = {};
+
+// Device address of g_pop_scratch_bitmap on the current device, looked up
+// once per device (host code only holds a stand-in for the symbol).
+cudaError_t scratch_bitmap_address(uint32_t** address) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_address[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_pop_scratch_bitmap);
+    if (e != cudaSuccess) return e;
+    g_scratch_address[dev] = static_cast<uint32_t*>(p);
+  }
+  *address = g_scratch_address[dev];
+  return cudaSuccess;
+}
+
+// pop_kernel with the bitmap in the shared device array: the words this call
+// reads are zeroed first, since the previous call's contents are not trusted.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    pop_noalloc_kernel(MetaT* meta, int64_t num_slots, int64_t* search_start,
+                       const int64_t* blocked, int64_t num_blocked, int64_t count, int64_t* out,
+                       uint32_t* bitmap, int order, bool aligned, int64_t* status) {
+  __shared__ PopShared<MetaT> sh;
+  __shared__ int bad_blocked;
+  const int64_t words = (num_slots + 31) / 32;
+  for (int64_t i = threadIdx.x; i < words; i += blockDim.x) bitmap[i] = 0u;
+  if (threadIdx.x == 0) bad_blocked = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < num_blocked; i += blockDim.x) {
+    const int64_t b = blocked[i];
+    if (b < 0 || b >= num_slots) {
+      bad_blocked = 1;
+      report(status, KVCA_ERR_BAD_INDEX, b);
+    } else {
+      atomicOr(bitmap + (b >> 5), 1u << (b & 31));
+    }
+  }
+  __syncthreads();
+  if (bad_blocked == 0) {
+    const int rc = pop_cta<MetaT>(meta, num_slots, search_start, bitmap, count, out, order,
+                                  aligned, sh);
+    if (rc != KVCA_OK && threadIdx.x == 0) report(status, rc, count);
+  }
+}
+
+}  // namespace
+}  // namespace kvca
+
+extern "C" int kvca_pop_reusable_slots_noalloc(int meta_bits, int order, void* d_slot_meta,
+                                               int64_t num_slots, int64_t* d_search_start,
+                                               const int64_t* d_blocked, int64_t num_blocked,
+                                               int64_t count, int64_t* d_out, int64_t* d_status,
+                                               kvca_stream_t stream) {
+  if (meta_bits != 8 && meta_bits != 16) return KVCA_ERR_BAD_ARGUMENT;
+  if (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (num_slots <= 0 || count < 0 || num_blocked < 0) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_slots > KVCA_NOALLOC_MAX_SLOTS) return KVCA_ERR_SIZE_LIMIT;
+  if (count == 0) return KVCA_OK;
+  if (!d_slot_meta || !d_search_start || !d_out) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_blocked > 0 && !d_blocked) return KVCA_ERR_BAD_ARGUMENT;
+  uint32_t* bitmap = nullptr;
+  if (kvca::scratch_bitmap_address(&bitmap) != cudaSuccess) return KVCA_ERR_CUDA;
+  const int threads = kvca::pop_threads_for(meta_bits, num_slots);
+  const bool aligned = (reinterpret_cast<uintptr_t>(d_slot_meta) & 15u) == 0u;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (meta_bits == 16) {
+    kvca::pop_noalloc_kernel<uint16_t><<<1, threads, 0, s>>>(
+        static_cast<uint16_t*>(d_slot_meta), num_slots, d_search_start, d_blocked, num_blocked,
+        count, d_out, bitmap, order, aligned, d_status);
+  } else {
+    kvca::pop_noalloc_kernel<uint8_t><<<1, threads, 0, s>>>(
+        static_cast<uint8_t*>(d_slot_meta), num_slots, d_search_start, d_blocked, num_blocked,
+        count, d_out, bitmap, order, aligned, d_status);
+  }
+  return cudaGetLastError() == cudaSuccess ? KVCA_OK : KVCA_ERR_CUDA;
+}
