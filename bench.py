@@ -71,6 +71,7 @@ def _traffic_per_launch(workload: str) -> float | None:
         return None
 
 
+
 class ClockSampler:
     """NVML sampling of SM clock and throttle reasons during a timed region."""
 
@@ -376,7 +377,7 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
             "frac": round(achieved / peak, 4),
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
             "traffic": traffic,
-            "kernel": "move_rows_kernel (gather and scatter launches)",
+            "kernel": "move_rows_bulk_kernel (gather and scatter launches; TMA bulk copies)",
             "algorithmic_bytes_per_launch": 2 * payload,
             "avg_launch_ms": round(avg_launch_ms, 4),
         },
@@ -437,12 +438,17 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama70b-shard")
+    ap.add_argument("--seqs", type=int, default=None,
+                    help="override the number of sequences (smaller cases for profiling)")
     ap.add_argument("--no-clock", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.seqs is not None:
+        w["seqs"] = args.seqs
+        w["label"] += f" [reduced to {args.seqs} sequences]"
     world, rank, local = _dist()
 
     if args.impl == "reference":

@@ -49,6 +49,7 @@ typedef struct CUstream_st* kvca_stream_t; /* same type as cudaStream_t */
 #define KVCA_ERR_BAD_ARGUMENT 3          /* reference: TORCH_CHECK, kv_adapter_cuda.cu:43-51 */
 #define KVCA_ERR_CUDA 4                  /* launch or runtime failure */
 #define KVCA_ERR_SIZE_LIMIT 5            /* table larger than a fixed-capacity entry point takes */
+#define KVCA_ERR_DEVICE_TIMEOUT 6        /* a bounded device-side wait gave up (value: CTA index) */
 
 /* Clock-sweep victim order (see kvca_pop_reusable_slots). */
 #define KVCA_POP_ORDER_GROUPED 0

@@ -18,6 +18,7 @@ KVCA_ERR_BAD_INDEX = 2
 KVCA_ERR_BAD_ARGUMENT = 3
 KVCA_ERR_CUDA = 4
 KVCA_ERR_SIZE_LIMIT = 5
+KVCA_ERR_DEVICE_TIMEOUT = 6
 KVCA_NOALLOC_MAX_SLOTS = 1048576
 
 KVCA_POP_ORDER_GROUPED = 0

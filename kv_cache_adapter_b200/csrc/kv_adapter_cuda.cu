@@ -9,9 +9,10 @@
 //    needed.
 //  * A device-resident clock stream that runs pop, refill and usage bumps
 //    for many steps inside one launch.
-//  * The row mover: 16-byte vectorised, coalesced copies of whole blocks or
-//    single token rows between paged planes and contiguous chunks, all
-//    planes (layers x K/V) of a call in one launch.
+//  * The row mover: whole blocks or single token rows between paged planes
+//    and contiguous chunks, all planes (layers x K/V) of a call in one launch:
+//    TMA bulk copies staged through shared memory for 16-byte aligned rows of
+//    1 KiB or more, 16-byte vectorised coalesced loads/stores otherwise.
 //
 // Device-side errors never trap: they are written to a caller-owned status
 // pair (code, value) with first-error-wins semantics, and the offending row
@@ -662,7 +663,9 @@ struct MoveParams {
   int64_t num_planes;
   int64_t num_rows;
   int64_t row_vecs;
-  int tpr_log2;  // threads per row = 1 << tpr_log2 (a power of two <= 32)
+  int64_t seg_vecs;      // vectors per work item: rows longer than this are split
+  int64_t segs_per_row;  // ceil(row_vecs / seg_vecs)
+  int tpr_log2;  // threads per work item = 1 << tpr_log2 (a power of two <= 32)
   int32_t flags;
   int64_t* status;
 };
@@ -712,13 +715,17 @@ __device__ __forceinline__ int64_t chunk_row_offset(const ChunkSide& side, int64
   return c * side.chunk_stride + (r - c * side.rows_per_chunk) * side.row_stride;
 }
 
-constexpr int kMoverThreads = 256;
+constexpr int kMoverThreads = 512;
 constexpr int kMoverUnroll = 8;
+constexpr int64_t kMoverSegmentBytes = 16384;
 
-// Work item g = r * num_planes + p.  Each group of 2^tpr_log2 lanes takes one
-// contiguous range of items, so consecutive items share a row: the row's
-// index is loaded and its offset computed once per row, not once per plane.
-// Each lane keeps kMoverUnroll 16-byte vectors in flight.
+// Work item g = (r * num_planes + p) * segs_per_row + segment: a row of one
+// plane, split into segments of at most seg_vecs vectors so that every group
+// of lanes gets the same number of bytes however long the rows are.  Each
+// group of 2^tpr_log2 lanes takes one contiguous range of items, so
+// consecutive items share a row: the row's index is loaded and its offset
+// computed once per row, not once per plane or segment.  Each lane keeps
+// kMoverUnroll vectors in flight.
 template <bool kSrcPaged, bool kDstPaged, typename V>
 __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_constant__ MoveParams p) {
   const int tpr = 1 << p.tpr_log2;
@@ -727,20 +734,24 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
   const int64_t group = gtid >> p.tpr_log2;
   const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
   const int64_t planes = p.num_planes;
-  const int64_t items = planes * p.num_rows;
+  const int64_t segs = p.segs_per_row;
+  const int64_t per_row = planes * segs;
+  const int64_t items = per_row * p.num_rows;
   const int64_t per = items / num_groups;
   const int64_t rem = items - per * num_groups;
   const int64_t begin = group * per + (group < rem ? group : rem);
   const int64_t end = begin + per + (group < rem ? 1 : 0);
   if (begin >= end) return;
 
-  int64_t r = begin / planes;
-  int64_t pl = begin - r * planes;
+  int64_t r = begin / per_row;
+  int64_t pl = (begin - r * per_row) / segs;
+  int64_t sg = begin - r * per_row - pl * segs;
   int64_t src_row = 0;
   int64_t dst_row = 0;
   bool row_ready = false;
   const bool lead = lane == 0;
   const int64_t row_vecs = p.row_vecs;
+  const int64_t seg_vecs = p.seg_vecs;
 
   for (int64_t g = begin; g < end; ++g) {
     if (!row_ready) {
@@ -757,24 +768,29 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
       V* dst = reinterpret_cast<V*>(kDstPaged
                                         ? p.dst_paged.planes[pl] + dst_row
                                         : p.dst_chunk.base + dst_row + pl * p.dst_chunk.plane_stride);
-      for (int64_t b = lane; b < row_vecs; b += static_cast<int64_t>(tpr) * kMoverUnroll) {
+      const int64_t v_begin = sg * seg_vecs;
+      const int64_t v_end = v_begin + seg_vecs < row_vecs ? v_begin + seg_vecs : row_vecs;
+      for (int64_t b = v_begin + lane; b < v_end; b += static_cast<int64_t>(tpr) * kMoverUnroll) {
         V buf[kMoverUnroll];
 #pragma unroll
         for (int u = 0; u < kMoverUnroll; ++u) {
           const int64_t i = b + static_cast<int64_t>(u) * tpr;
-          if (i < row_vecs) buf[u] = ld_stream(src + i);
+          if (i < v_end) buf[u] = ld_stream(src + i);
         }
 #pragma unroll
         for (int u = 0; u < kMoverUnroll; ++u) {
           const int64_t i = b + static_cast<int64_t>(u) * tpr;
-          if (i < row_vecs) st_stream(dst + i, buf[u]);
+          if (i < v_end) st_stream(dst + i, buf[u]);
         }
       }
     }
-    if (++pl == planes) {
-      pl = 0;
-      ++r;
-      row_ready = false;
+    if (++sg == segs) {
+      sg = 0;
+      if (++pl == planes) {
+        pl = 0;
+        ++r;
+        row_ready = false;
+      }
     }
   }
 }
@@ -798,7 +814,7 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
     blocks_per_sm = b > 0 ? b : 1;
   }
   const int sms = device_sm_count();
-  const int64_t items = p.num_planes * p.num_rows;
+  const int64_t items = p.num_planes * p.num_rows * p.segs_per_row;
   const int64_t threads_needed = items << p.tpr_log2;
   int64_t blocks = (threads_needed + kMoverThreads - 1) / kMoverThreads;
   const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
@@ -808,21 +824,208 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// Row mover on the TMA bulk-copy engine (16-byte aligned rows of >= 1 KiB)
+// ---------------------------------------------------------------------------
+//
+// One warp per CTA; lane 0 streams its range of work items through a ring of
+// shared-memory stages: cp.async.bulk global->shared completes on the stage's
+// mbarrier, then cp.async.bulk shared->global writes it out, and the stage is
+// reused once that store has read it (cp.async.bulk.wait_group.read).  No
+// cluster multicast.  Rows are cut into segments of at most kBulkSegmentBytes;
+// the stage count makes stages x segment = kBulkStageBytes, and the grid holds
+// kBulkCtasPerSm CTAs per SM, so about 48 KiB are in flight per SM, the
+// amount that measured fastest on B200 (more in flight per SM was slower).
+
+constexpr int kBulkMaxStages = 16;
+constexpr int64_t kBulkSegmentBytes = 4096;
+constexpr int64_t kBulkStageBytes = 16384;
+constexpr int kBulkCtasPerSm = 3;
+constexpr int64_t kBulkMinRowBytes = 4096;
+constexpr uint32_t kBulkSpinLimit = 1u << 24;  // bounded mbarrier waits
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Waits until at most n of this thread's most recent bulk store groups are
+// still reading shared memory (the immediate must be a constant).
+__device__ __forceinline__ void bulk_wait_read(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.bulk.wait_group.read 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.bulk.wait_group.read 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.bulk.wait_group.read 6;" ::: "memory"); break;
+    case 7: asm volatile("cp.async.bulk.wait_group.read 7;" ::: "memory"); break;
+    case 8: asm volatile("cp.async.bulk.wait_group.read 8;" ::: "memory"); break;
+    case 9: asm volatile("cp.async.bulk.wait_group.read 9;" ::: "memory"); break;
+    case 10: asm volatile("cp.async.bulk.wait_group.read 10;" ::: "memory"); break;
+    case 11: asm volatile("cp.async.bulk.wait_group.read 11;" ::: "memory"); break;
+    case 12: asm volatile("cp.async.bulk.wait_group.read 12;" ::: "memory"); break;
+    case 13: asm volatile("cp.async.bulk.wait_group.read 13;" ::: "memory"); break;
+    case 14: asm volatile("cp.async.bulk.wait_group.read 14;" ::: "memory"); break;
+    default: asm volatile("cp.async.bulk.wait_group.read 15;" ::: "memory"); break;
+  }
+}
+
+// Bounded wait for the completion of phase `parity` of an mbarrier.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done = 0;
+  for (uint32_t tries = 0; tries < kBulkSpinLimit && !done; ++tries) {
+    asm volatile(
+        "{ .reg .pred q; mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2; selp.u32 %0, 1, 0, q; }"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  }
+  return done != 0;
+}
+
+template <bool kSrcPaged, bool kDstPaged>
+__global__ void __launch_bounds__(32) move_rows_bulk_kernel(const __grid_constant__ MoveParams p,
+                                                            int stages) {
+  extern __shared__ __align__(128) unsigned char stage_buf[];
+  __shared__ __align__(8) uint64_t full[kBulkMaxStages];
+  if (threadIdx.x != 0) return;
+  const int64_t planes = p.num_planes;
+  const int64_t segs = p.segs_per_row;
+  const int64_t per_row = planes * segs;
+  const int64_t items = per_row * p.num_rows;
+  const int64_t groups = gridDim.x;
+  const int64_t per = items / groups;
+  const int64_t rem = items - per * groups;
+  const int64_t group = blockIdx.x;
+  const int64_t begin = group * per + (group < rem ? group : rem);
+  const int64_t end = begin + per + (group < rem ? 1 : 0);
+  if (begin >= end) return;
+  for (int s = 0; s < stages; ++s)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+  const int64_t seg_bytes = p.seg_vecs * 16;
+  const int64_t row_bytes = p.row_vecs * 16;
+  int64_t r = begin / per_row;
+  int64_t pl = (begin - r * per_row) / segs;
+  int64_t sg = begin - r * per_row - pl * segs;
+  int64_t g = begin;
+  int64_t src_row = 0;
+  int64_t dst_row = 0;
+  bool row_ready = false;
+  uint64_t dst_q[kBulkMaxStages];
+  uint32_t bytes_q[kBulkMaxStages];
+  int64_t loaded = 0;  // loads issued
+  int64_t stored = 0;  // stores issued; item k uses stage k % stages
+  bool timed_out = false;
+  while (true) {
+    while (loaded < stored + stages && g < end) {
+      if (!row_ready) {
+        row_ready = true;
+        src_row = kSrcPaged ? paged_row_offset(p.src_paged, r, p.flags, p.status, true)
+                            : chunk_row_offset(p.src_chunk, r);
+        dst_row = kDstPaged ? paged_row_offset(p.dst_paged, r, p.flags, p.status, true)
+                            : chunk_row_offset(p.dst_chunk, r);
+      }
+      const bool valid = src_row >= 0 && dst_row >= 0;
+      const int64_t off = sg * seg_bytes;
+      const int64_t bytes = off + seg_bytes < row_bytes ? seg_bytes : row_bytes - off;
+      const uint64_t src = (kSrcPaged ? p.src_paged.planes[pl] + src_row
+                                      : p.src_chunk.base + src_row + pl * p.src_chunk.plane_stride) +
+                           off;
+      const uint64_t dst = (kDstPaged ? p.dst_paged.planes[pl] + dst_row
+                                      : p.dst_chunk.base + dst_row + pl * p.dst_chunk.plane_stride) +
+                           off;
+      ++g;
+      if (++sg == segs) {
+        sg = 0;
+        if (++pl == planes) {
+          pl = 0;
+          ++r;
+          row_ready = false;
+        }
+      }
+      if (!valid) continue;
+      const int stage = static_cast<int>(loaded % stages);
+      // the store of item loaded - stages used this stage: let it finish reading
+      if (loaded >= stages) bulk_wait_read(static_cast<int>(stored - 1 - (loaded - stages)));
+      unsigned char* buf = stage_buf + stage * seg_bytes;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                       smem_u32(&full[stage])),
+                   "r"(static_cast<uint32_t>(bytes))
+                   : "memory");
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(buf)),
+          "l"(src), "r"(static_cast<uint32_t>(bytes)), "r"(smem_u32(&full[stage]))
+          : "memory");
+      dst_q[stage] = dst;
+      bytes_q[stage] = static_cast<uint32_t>(bytes);
+      ++loaded;
+    }
+    if (stored == loaded) break;
+    const int stage = static_cast<int>(stored % stages);
+    if (!mbar_wait(&full[stage], static_cast<uint32_t>((stored / stages) & 1))) {
+      timed_out = true;
+      break;
+    }
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_q[stage]),
+                 "r"(smem_u32(stage_buf + stage * seg_bytes)), "r"(bytes_q[stage])
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    ++stored;
+  }
+  if (timed_out) {
+    report(p.status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
+    // let the loads still in flight land before shared memory is released
+    for (int64_t k = stored; k < loaded; ++k)
+      mbar_wait(&full[k % stages], static_cast<uint32_t>((k / stages) & 1));
+  }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+template <bool kSrcPaged, bool kDstPaged>
+cudaError_t launch_move_bulk(const MoveParams& base, cudaStream_t stream) {
+  MoveParams p = base;
+  p.seg_vecs = kBulkSegmentBytes / 16;
+  if (p.seg_vecs >= p.row_vecs) p.seg_vecs = p.row_vecs;
+  p.segs_per_row = (p.row_vecs + p.seg_vecs - 1) / p.seg_vecs;
+  const int64_t seg_bytes = p.seg_vecs * 16;
+  int stages = static_cast<int>(kBulkStageBytes / seg_bytes);
+  if (stages > kBulkMaxStages) stages = kBulkMaxStages;
+  if (stages < 2) stages = 2;
+  const int smem = static_cast<int>(stages * seg_bytes);
+  auto kernel = move_rows_bulk_kernel<kSrcPaged, kDstPaged>;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kBulkMaxStages * kBulkSegmentBytes));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int sms = device_sm_count();
+  const int64_t items = p.num_planes * p.num_rows * p.segs_per_row;
+  int64_t blocks = static_cast<int64_t>(sms > 0 ? sms : 1) * kBulkCtasPerSm;
+  if (blocks > items) blocks = items;
+  if (blocks < 1) blocks = 1;
+  kernel<<<static_cast<unsigned>(blocks), 32, smem, stream>>>(p, stages);
+  return cudaGetLastError();
+}
+
 template <bool kSrcPaged, bool kDstPaged>
 cudaError_t launch_move_vec(const MoveParams& p, int vec_bytes, cudaStream_t stream) {
   switch (vec_bytes) {
-    case 16: return launch_move_typed<kSrcPaged, kDstPaged, uint4>(p, stream);
+    case 16:
+      if (p.row_vecs * 16 >= kBulkMinRowBytes) return launch_move_bulk<kSrcPaged, kDstPaged>(p, stream);
+      return launch_move_typed<kSrcPaged, kDstPaged, uint4>(p, stream);
     case 8: return launch_move_typed<kSrcPaged, kDstPaged, uint2>(p, stream);
     case 4: return launch_move_typed<kSrcPaged, kDstPaged, unsigned int>(p, stream);
     case 2: return launch_move_typed<kSrcPaged, kDstPaged, unsigned short>(p, stream);
     default: return launch_move_typed<kSrcPaged, kDstPaged, unsigned char>(p, stream);
   }
-}
-
-int ceil_log2(int64_t x) {
-  int l = 0;
-  while ((int64_t{1} << l) < x) ++l;
-  return l;
 }
 
 int grid_for(int64_t count, int threads) {
@@ -850,11 +1053,16 @@ cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
   p.num_planes = a.num_planes;
   p.num_rows = a.num_rows;
   p.row_vecs = a.row_bytes / a.vec_bytes;
-  // A row of row_vecs vectors gets about four vectors per lane.
-  int64_t lanes = (p.row_vecs + 3) / 4;
+  // Work items of at most kMoverSegmentBytes; each gets the largest power of
+  // two lanes (at most 32) that leaves every lane at least four vectors.
+  p.seg_vecs = kMoverSegmentBytes / a.vec_bytes;
+  if (p.seg_vecs < 1) p.seg_vecs = 1;
+  if (p.seg_vecs >= p.row_vecs) p.seg_vecs = p.row_vecs;
+  p.segs_per_row = (p.row_vecs + p.seg_vecs - 1) / p.seg_vecs;
+  int64_t lanes = p.seg_vecs / 4;
   if (lanes > 32) lanes = 32;
-  if (lanes < 1) lanes = 1;
-  p.tpr_log2 = ceil_log2(lanes);
+  p.tpr_log2 = 0;
+  while ((int64_t{2} << p.tpr_log2) <= lanes) ++p.tpr_log2;
   p.flags = a.flags;
   p.status = a.status;
   switch (a.kind) {

@@ -96,6 +96,8 @@ def _raise_for(code: int, value: int, what: str) -> None:
         raise IndexError(f"{what}: index {value} is out of range")
     if code == _lib.KVCA_ERR_BAD_ARGUMENT:
         raise ValueError(f"{what}: invalid arguments")
+    if code == _lib.KVCA_ERR_DEVICE_TIMEOUT:
+        raise RuntimeError(f"{what}: a bounded device-side wait gave up (CTA {value})")
     raise RuntimeError(f"{what}: CUDA launch failed (code {code})")
 
 
