@@ -158,6 +158,22 @@ def _barrier(world: int) -> None:
         dist.barrier()
 
 
+def _min_over_ranks(x: float, world: int, device) -> float:
+    return -_max_over_ranks(-x, world, device)
+
+
+def _same_on_all_ranks(digest: str, world: int) -> bool:
+    """True when every rank computed the same digest (replicated slot tables
+    must pick identical victims on every KV-head shard)."""
+    if world == 1:
+        return True
+    import torch.distributed as dist
+
+    digests: list[str | None] = [None] * world
+    dist.all_gather_object(digests, digest)
+    return all(d == digest for d in digests)
+
+
 # ---------------------------------------------------------------------------
 # workload construction
 # ---------------------------------------------------------------------------
@@ -262,7 +278,8 @@ def gpu_clock(device, k: int, reps: int = 3) -> dict:
     ops.check_status(device)
     best = min(ms)
     return {"alloc_per_step": k, "steps": steps, "ms": round(best, 3),
-            "evictions_per_s": round(steps * k / (best / 1e3), 1), "launches": 1}
+            "evictions_per_s": round(steps * k / (best / 1e3), 1), "launches": 1,
+            "victims_sha256": workloads.sha256_of(victims), "slot_meta_sha256": workloads.sha256_of(meta)}
 
 
 def run_ours(args, w: dict, world: int, rank: int, device) -> None:
@@ -335,7 +352,8 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     clock = None if args.no_clock else [gpu_clock(device, 1), gpu_clock(device, 256)]
     if clock is not None:
         for c in clock:
-            c["evictions_per_s"] = _max_over_ranks(-c["evictions_per_s"], world, device) * -1  # slowest rank
+            c["evictions_per_s"] = _min_over_ranks(c["evictions_per_s"], world, device)  # slowest rank
+            c["identical_on_all_ranks"] = _same_on_all_ranks(c["victims_sha256"] + c["slot_meta_sha256"], world)
 
     if rank != 0:
         return

@@ -832,8 +832,8 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
 // One warp per CTA; lane 0 streams its range of work items through a ring of
 // shared-memory stages: cp.async.bulk global->shared completes on the stage's
 // mbarrier, then cp.async.bulk shared->global writes it out, and the stage is
-// reused once that store has read it (cp.async.bulk.wait_group.read).  No
-// cluster multicast.  Rows are cut into segments of at most kBulkSegmentBytes;
+// reused once that store has read it (cp.async.bulk.wait_group.read).  Every
+// copy stays within this CTA and this GPU's memory.  Rows are cut into segments of at most kBulkSegmentBytes;
 // the stage count makes stages x segment = kBulkStageBytes, and the grid holds
 // kBulkCtasPerSm CTAs per SM, so about 48 KiB are in flight per SM, the
 // amount that measured fastest on B200 (more in flight per SM was slower).
