@@ -95,6 +95,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, c_int, c_ptr, c_i64, c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr],
     ),
+    "kvca_clock_stream_scratch_bytes": (ctypes.c_size_t, [c_i64]),
+    "kvca_clock_stream_batched": (
+        c_int,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+         c_ptr],
+    ),
     "kvca_gather": (
         c_int,
         [ctypes.POINTER(PagedDesc), ctypes.POINTER(ChunkDesc), c_i64, c_i64, c_i64, ctypes.c_int32,

@@ -222,6 +222,32 @@ int kvca_clock_stream(int meta_bits, int order, void* d_slot_meta, int64_t num_s
                                              d_steps_done, d_status, stream));
 }
 
+size_t kvca_clock_stream_scratch_bytes(int64_t num_slots) {
+  if (num_slots <= 0) return 0;
+  return static_cast<size_t>(num_slots) * 5 * sizeof(int32_t);
+}
+
+int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                              int64_t* d_search_start, int64_t num_steps, int64_t alloc_per_step,
+                              const int64_t* d_reaccess, int64_t reaccess_per_step,
+                              int64_t* d_victims, int64_t* d_steps_done, int32_t* d_scratch,
+                              int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits)) return KVCA_ERR_BAD_ARGUMENT;
+  if (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX)
+    return KVCA_ERR_BAD_ARGUMENT;
+  const int64_t limit = INT32_MAX - 2;
+  if (num_slots <= 0 || num_slots > limit || num_steps < 0 || num_steps > limit ||
+      alloc_per_step < 1 || alloc_per_step > limit || reaccess_per_step < 0 ||
+      reaccess_per_step > 8192 || num_steps * alloc_per_step > limit)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (!d_slot_meta || !d_search_start || !d_victims || !d_steps_done || !d_scratch)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (reaccess_per_step > 0 && num_steps > 0 && !d_reaccess) return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_clock_stream_batched(
+      meta_bits, order, d_slot_meta, num_slots, d_search_start, num_steps, alloc_per_step,
+      d_reaccess, reaccess_per_step, d_victims, d_steps_done, d_scratch, d_status, stream));
+}
+
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,
                 int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
                 kvca_stream_t stream) {

@@ -414,58 +414,440 @@ __global__ void __launch_bounds__(1024)
 
 constexpr int kStreamMaxReaccessPerThread = 8;
 
+// One step of the clock stream, run by the whole CTA: pop `alloc_per_step`
+// victims, refill them, bump the step's re-accessed slots.  Returns KVCA_OK
+// or the pop's error (uniform).
+template <typename MetaT>
+__device__ int stream_step(MetaT* meta, int64_t num_slots, int64_t* search_start, int64_t step,
+                           int64_t alloc_per_step, const int64_t* reaccess,
+                           int64_t reaccess_per_step, int64_t* victims, int order, bool aligned,
+                           int64_t* status, PopShared<MetaT>& sh) {
+  using M = Meta<MetaT>;
+  int64_t* out = victims + step * alloc_per_step;
+  const int rc = pop_cta<MetaT>(meta, num_slots, search_start, nullptr, alloc_per_step, out, order,
+                                aligned, sh);
+  if (rc != KVCA_OK) return rc;
+  // Victims are refilled: pin kept (it is 0), usage 1 (adapter.py:233-242
+  // gives new saves usage 1; commit at adapter.py:651).
+  for (int64_t i = threadIdx.x; i < alloc_per_step; i += blockDim.x) {
+    const int64_t v = out[i];
+    meta[v] = M::pack(M::pin(meta[v]), 1);
+  }
+  __syncthreads();
+  // Usage bump of re-accessed slots: every value is read before any write,
+  // so duplicates in one batch bump once, as index_put_ does.
+  const int64_t* ids = reaccess + step * reaccess_per_step;
+  int64_t slot_ids[kStreamMaxReaccessPerThread];
+  MetaT values[kStreamMaxReaccessPerThread];
+#pragma unroll
+  for (int u = 0; u < kStreamMaxReaccessPerThread; ++u) {
+    const int64_t i = threadIdx.x + static_cast<int64_t>(u) * blockDim.x;
+    slot_ids[u] = -1;
+    values[u] = MetaT(0);
+    if (i < reaccess_per_step) {
+      const int64_t id = ids[i];
+      if (id < 0 || id >= num_slots) {
+        report(status, KVCA_ERR_BAD_INDEX, id);
+      } else {
+        const unsigned w = meta[id];
+        values[u] = M::pack(M::pin(w), M::sat_inc(M::usage(w)));
+        slot_ids[u] = id;
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kStreamMaxReaccessPerThread; ++u)
+    if (slot_ids[u] >= 0) meta[slot_ids[u]] = values[u];
+  __syncthreads();
+  return KVCA_OK;
+}
+
 template <typename MetaT>
 __global__ void __launch_bounds__(1024)
     clock_stream_kernel(MetaT* meta, int64_t num_slots, int64_t* search_start, int64_t num_steps,
                         int64_t alloc_per_step, const int64_t* reaccess,
                         int64_t reaccess_per_step, int64_t* victims, int64_t* steps_done,
                         int order, bool aligned, int64_t* status) {
-  using M = Meta<MetaT>;
   __shared__ PopShared<MetaT> sh;
   int64_t step = 0;
   for (; step < num_steps; ++step) {
-    int64_t* out = victims + step * alloc_per_step;
-    const int rc = pop_cta<MetaT>(meta, num_slots, search_start, nullptr, alloc_per_step, out,
-                                  order, aligned, sh);
+    const int rc = stream_step<MetaT>(meta, num_slots, search_start, step, alloc_per_step, reaccess,
+                                      reaccess_per_step, victims, order, aligned, status, sh);
     if (rc != KVCA_OK) {
       if (threadIdx.x == 0) report(status, rc, step);
       break;
     }
-    // Victims are refilled: pin kept (it is 0), usage 1 (adapter.py:233-242
-    // gives new saves usage 1; commit at adapter.py:651).
-    for (int64_t i = threadIdx.x; i < alloc_per_step; i += blockDim.x) {
-      const int64_t v = out[i];
-      meta[v] = M::pack(M::pin(meta[v]), 1);
-    }
-    __syncthreads();
-    // Usage bump of re-accessed slots: every value is read before any write,
-    // so duplicates in one batch bump once, as index_put_ does.
-    const int64_t* ids = reaccess + step * reaccess_per_step;
-    int64_t slot_ids[kStreamMaxReaccessPerThread];
-    MetaT values[kStreamMaxReaccessPerThread];
-#pragma unroll
-    for (int u = 0; u < kStreamMaxReaccessPerThread; ++u) {
-      const int64_t i = threadIdx.x + static_cast<int64_t>(u) * blockDim.x;
-      slot_ids[u] = -1;
-      values[u] = MetaT(0);
-      if (i < reaccess_per_step) {
-        const int64_t id = ids[i];
-        if (id < 0 || id >= num_slots) {
-          report(status, KVCA_ERR_BAD_INDEX, id);
-        } else {
-          const unsigned w = meta[id];
-          values[u] = M::pack(M::pin(w), M::sat_inc(M::usage(w)));
-          slot_ids[u] = id;
-        }
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kStreamMaxReaccessPerThread; ++u)
-      if (slot_ids[u] >= 0) meta[slot_ids[u]] = values[u];
-    __syncthreads();
   }
   if (threadIdx.x == 0) *steps_done = step;
+}
+
+// ---------------------------------------------------------------------------
+// Clock stream, batched over runs of steps that need no aging
+// ---------------------------------------------------------------------------
+//
+// While every pop finds `alloc_per_step` available usage-0 slots (T = 0) no
+// usage ever decreases: refills set 1, bumps add 1.  So from a state S at
+// step s0 the victims of the following steps are the available usage-0
+// slots of S in scan order from search_start (the candidates), taken k per
+// step, except that a candidate whose first re-access comes at a step before
+// the one that would take it has usage 1 by then and is passed over.  An
+// "epoch" computes all of that at once:
+//   1. compact the candidates (one pass over slot_meta);
+//   2. first re-access step of every slot re-accessed in the window of steps
+//      the candidates can cover (atomicMax on an encoded step);
+//   3. one warp walks the candidates in order and takes candidate j unless
+//      its first re-access step is below the step its rank gives it, 32 at a
+//      time with a ballot fixed point;
+//   4. fold the epoch's refills and bumps into each touched slot:
+//      usage = min(base + distinct bumping steps, max), base = 1 for a victim
+//      (only bumps at or after its step count) and the old usage otherwise.
+// The first step that cannot take k candidates needs aging (T > 0): it runs
+// as one exact step (stream_step), then the next epoch starts.  After short
+// epochs the kernel runs a stretch of exact steps instead.  Results equal the
+// step-by-step stream bit for bit.
+//
+// Scratch: 5 x num_slots int32 (candidates, their first re-access steps, and
+// three per-slot words that are zero on entry and left zero on exit).
+
+constexpr int64_t kEpochMinSteps = 8;
+constexpr int64_t kExactStepsAfterShortEpoch = 64;
+constexpr int kFilterChunks = 8;  // 32-candidate chunks loaded ahead by the filter warp
+constexpr int kWarpDedupMin = 16;   // re-accesses per step deduplicated in registers
+constexpr int kWarpDedupMax = 256;
+
+template <typename MetaT>
+struct EpochShared {
+  PopShared<MetaT> pop;
+  int scan[33];
+  long long start;
+  long long s_end;
+  long long last_victim;
+};
+
+__device__ __forceinline__ bool slot_ok(int64_t x, int64_t n) { return x >= 0 && x < n; }
+
+template <typename MetaT>
+__device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, int64_t s0,
+                                int64_t steps, int64_t k, const int64_t* reaccess, int64_t m,
+                                int64_t* victims, int32_t* cand, int32_t* cand_bump,
+                                int32_t* first_bump, int32_t* victim_step, int32_t* bump_count,
+                                bool aligned, int64_t* status, EpochShared<MetaT>& sh) {
+  using M = Meta<MetaT>;
+  constexpr int kSpv = M::kSlotsPerVec;
+  if (threadIdx.x == 0) {
+    long long p0 = static_cast<long long>(*search_start % n);
+    if (p0 < 0) p0 += n;
+    sh.start = p0;
+    sh.s_end = s0;
+    sh.last_victim = -1;
+  }
+  __syncthreads();
+  const int64_t p0 = sh.start;
+
+  // 1. candidates: available usage-0 slots in scan order from p0
+  int64_t nc = 0;
+  for (int seg = 0; seg < 2; ++seg) {
+    const int64_t lo = seg == 0 ? p0 : 0;
+    const int64_t hi = seg == 0 ? n : p0;
+    if (lo >= hi) continue;
+    const int64_t v_begin = lo / kSpv;
+    const int64_t v_end = (hi + kSpv - 1) / kSpv;
+    for (int64_t tile = v_begin; tile < v_end; tile += blockDim.x) {
+      const int64_t v = tile + threadIdx.x;
+      unsigned mask = 0u;
+      if (v < v_end) {
+        MetaVec<MetaT> mv;
+        load_meta_vec(meta, n, v, aligned, mv);
+#pragma unroll
+        for (int j = 0; j < kSpv; ++j) {
+          const int64_t slot = v * kSpv + j;
+          const unsigned w = mv.s[j];
+          if (slot >= lo && slot < hi && M::pin(w) == 0u && M::usage(w) == 0u) mask |= 1u << j;
+        }
+      }
+      int total;
+      const int base = block_excl_scan(__popc(mask), &total, sh.scan);
+      int64_t rank = nc + base;
+      while (mask != 0u) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        cand[rank++] = static_cast<int32_t>(v * kSpv + j);
+      }
+      nc += total;
+    }
+  }
+  // steps these candidates can serve: at most nc / k, plus the step that fails
+  int64_t s_hi = s0 + nc / k + 1;
+  if (s_hi > steps) s_hi = steps;
+  const int64_t ev_lo = s0 * m;
+  const int64_t ev_hi = s_hi * m;
+
+  // 2. first re-access step in the window, encoded as INT_MAX - step (0 = none)
+  for (int64_t e = ev_lo + threadIdx.x; e < ev_hi; e += blockDim.x) {
+    const int64_t x = reaccess[e];
+    if (!slot_ok(x, n)) {
+      report(status, KVCA_ERR_BAD_INDEX, x);
+      continue;
+    }
+    atomicMax(first_bump + x, static_cast<int32_t>(INT32_MAX - e / m));
+  }
+  __syncthreads();
+  for (int64_t j = threadIdx.x; j < nc; j += blockDim.x) {
+    const int32_t enc = first_bump[cand[j]];
+    cand_bump[j] = enc == 0 ? INT32_MAX : INT32_MAX - enc;
+  }
+  __syncthreads();
+
+  // 3. the filter: candidate j is taken at step s0 + (taken before j) / k
+  //    unless its first re-access step is smaller than that step.  32-bit
+  //    counts (the launcher keeps num_steps * alloc_per_step below 2^31);
+  //    within a chunk the step offset of lane j is (r0 + prefix_j) / k with
+  //    r0 = taken % k and prefix_j < 32, so no division is needed per lane.
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const unsigned below = (1u << lane) - 1u;
+    const int32_t kk = static_cast<int32_t>(k);
+    const int32_t max_taken = static_cast<int32_t>((steps - s0) * k);
+    const int32_t ncand = static_cast<int32_t>(nc);
+    const int32_t step0 = static_cast<int32_t>(s0);
+    int32_t taken = 0;
+    int32_t fb[kFilterChunks];
+    int32_t cs[kFilterChunks];
+#pragma unroll
+    for (int q = 0; q < kFilterChunks; ++q) {
+      const int32_t idx = q * 32 + lane;
+      fb[q] = idx < ncand ? cand_bump[idx] : -1;
+      cs[q] = idx < ncand ? cand[idx] : -1;
+    }
+    for (int32_t j = 0; j < ncand && taken < max_taken; j += 32 * kFilterChunks) {
+      // prefetch the next 256 candidates while this batch is resolved
+      int32_t fb_next[kFilterChunks];
+      int32_t cs_next[kFilterChunks];
+#pragma unroll
+      for (int q = 0; q < kFilterChunks; ++q) {
+        const int32_t idx = j + 32 * kFilterChunks + q * 32 + lane;
+        fb_next[q] = idx < ncand ? cand_bump[idx] : -1;
+        cs_next[q] = idx < ncand ? cand[idx] : -1;
+      }
+#pragma unroll
+      for (int q = 0; q < kFilterChunks; ++q) {
+        const unsigned present = __ballot_sync(0xffffffffu, cs[q] >= 0);
+        // candidates never re-accessed in the window are taken whatever their
+        // step; a chunk holding only those needs no fixed point
+        const unsigned pending = __ballot_sync(0xffffffffu, cs[q] >= 0 && fb[q] != INT32_MAX);
+        const int32_t n_present = __popc(present);
+        if (pending == 0u && taken + n_present <= max_taken) {
+          if (cs[q] >= 0) {
+            const int32_t pos = taken + __popc(present & below);
+            const int32_t st = kk == 1 ? step0 + pos : step0 + pos / kk;
+            victims[s0 * k + pos] = cs[q];
+            victim_step[cs[q]] = st + 1;
+          }
+          taken += n_present;
+          continue;
+        }
+        const int32_t q0 = kk == 1 ? taken : taken / kk;
+        const int32_t r0 = taken - q0 * kk;
+        const int32_t base_step = step0 + q0;
+        unsigned cur = present;
+        for (int it = 0; it < 33; ++it) {  // converges in at most 32 rounds
+          const int32_t prefix = __popc(cur & below);
+          const int32_t x = r0 + prefix;
+          const int32_t d = kk == 1 ? x : (kk >= 32 ? (x >= kk ? 1 : 0) : x / kk);
+          const bool ok = cs[q] >= 0 && taken + prefix < max_taken && fb[q] >= base_step + d;
+          const unsigned ok_mask = __ballot_sync(0xffffffffu, ok);
+          const unsigned diff = (ok_mask ^ cur) & present;
+          if (diff == 0u) break;
+          const unsigned keep = (1u << (__ffs(diff) - 1)) - 1u;
+          cur = (cur & keep) | (ok_mask & ~keep);
+        }
+        if ((cur >> lane) & 1u) {
+          const int32_t prefix = __popc(cur & below);
+          const int32_t x = r0 + prefix;
+          const int32_t d = kk == 1 ? x : (kk >= 32 ? (x >= kk ? 1 : 0) : x / kk);
+          victims[s0 * k + taken + prefix] = cs[q];
+          victim_step[cs[q]] = base_step + d + 1;
+        }
+        taken += __popc(cur);
+      }
+#pragma unroll
+      for (int q = 0; q < kFilterChunks; ++q) {
+        fb[q] = fb_next[q];
+        cs[q] = cs_next[q];
+      }
+    }
+    __syncwarp();
+    const int64_t full = taken / k;
+    // a step left incomplete is not an epoch step: undo its victims
+    for (int64_t pos = full * k + lane; pos < taken; pos += 32)
+      victim_step[victims[s0 * k + pos]] = 0;
+    if (lane == 0) {
+      sh.s_end = s0 + full;
+      sh.last_victim = full > 0 ? victims[s0 * k + full * k - 1] : -1;
+    }
+  }
+  __syncthreads();
+  const int64_t s_end = sh.s_end;
+  const int64_t v_lo = s0 * k;
+  const int64_t v_hi = s_end * k;
+  const int64_t cnt_hi = s_end * m;
+
+  // 4a. distinct bumping steps per slot (only steps >= a victim's own step).
+  //     16 to 256 re-accesses per step: one warp per step compares each id
+  //     with the step's earlier ids through shuffles; otherwise each event
+  //     scans its step's earlier ids in memory.
+  if (m >= kWarpDedupMin && m <= kWarpDedupMax) {
+    const int lane = threadIdx.x & 31;
+    const int nwarps = static_cast<int>(blockDim.x >> 5);
+    for (int64_t t = s0 + (threadIdx.x >> 5); t < s_end; t += nwarps) {
+      int64_t ids[kWarpDedupMax / 32];
+      bool dup[kWarpDedupMax / 32];
+#pragma unroll
+      for (int w = 0; w < kWarpDedupMax / 32; ++w) {
+        const int64_t i = static_cast<int64_t>(w) * 32 + lane;
+        ids[w] = i < m ? reaccess[t * m + i] : -1;
+        dup[w] = false;
+      }
+#pragma unroll
+      for (int u = 0; u < kWarpDedupMax / 32; ++u) {
+        if (static_cast<int64_t>(u) * 32 >= m) break;
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+          const int64_t v = __shfl_sync(0xffffffffu, ids[u], l);
+          const int i = u * 32 + l;
+#pragma unroll
+          for (int w = 0; w < kWarpDedupMax / 32; ++w)
+            dup[w] |= (w * 32 + lane > i) && ids[w] == v;
+        }
+      }
+#pragma unroll
+      for (int w = 0; w < kWarpDedupMax / 32; ++w) {
+        const int64_t x = ids[w];
+        if (dup[w] || !slot_ok(x, n)) continue;
+        const int32_t vs = victim_step[x];
+        if (vs == 0 || vs - 1 <= t) atomicAdd(bump_count + x, 1);
+      }
+    }
+  } else {
+    for (int64_t e = ev_lo + threadIdx.x; e < cnt_hi; e += blockDim.x) {
+      const int64_t x = reaccess[e];
+      if (!slot_ok(x, n)) continue;
+      const int64_t t = e / m;
+      bool dup = false;
+#pragma unroll 8
+      for (int64_t i = t * m; i < e; ++i) dup |= reaccess[i] == x;
+      if (dup) continue;
+      const int32_t vs = victim_step[x];
+      if (vs == 0 || vs - 1 <= t) atomicAdd(bump_count + x, 1);
+    }
+  }
+  __syncthreads();
+  // 4b. final usage of every touched slot, computed from the epoch-start
+  //     words (idempotent, so duplicates may compute it twice)
+  const int64_t n_ev = ev_hi - ev_lo;
+  const int64_t touched = n_ev + (v_hi - v_lo);
+  constexpr int kU = 4;
+  auto touched_slot = [&](int64_t i) -> int64_t {
+    return i < n_ev ? reaccess[ev_lo + i] : victims[v_lo + (i - n_ev)];
+  };
+  for (int64_t i0 = threadIdx.x; i0 < touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
+    int64_t xs[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      xs[u] = i < touched ? touched_slot(i) : -1;
+    }
+    unsigned ws[kU];
+    int32_t vss[kU], cts[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const bool ok = slot_ok(xs[u], n);
+      ws[u] = ok ? static_cast<unsigned>(meta[xs[u]]) : 0u;
+      vss[u] = ok ? victim_step[xs[u]] : 0;
+      cts[u] = ok ? bump_count[xs[u]] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (!slot_ok(xs[u], n)) continue;
+      int64_t fin = (vss[u] != 0 ? 1 : static_cast<int64_t>(M::usage(ws[u]))) + cts[u];
+      if (fin > M::kUsageMax) fin = M::kUsageMax;
+      first_bump[xs[u]] = static_cast<int32_t>(fin + 1);
+    }
+  }
+  __syncthreads();
+  for (int64_t i0 = threadIdx.x; i0 < touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
+    int64_t xs[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      xs[u] = i < touched ? touched_slot(i) : -1;
+    }
+    unsigned ws[kU];
+    int32_t fins[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const bool ok = slot_ok(xs[u], n);
+      ws[u] = ok ? static_cast<unsigned>(meta[xs[u]]) : 0u;
+      fins[u] = ok ? first_bump[xs[u]] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (slot_ok(xs[u], n)) meta[xs[u]] = M::pack(M::pin(ws[u]), fins[u] - 1);
+  }
+  __syncthreads();
+  // 4c. leave the per-slot scratch words zero again
+  for (int64_t i0 = threadIdx.x; i0 < touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      if (i >= touched) continue;
+      const int64_t x = touched_slot(i);
+      if (!slot_ok(x, n)) continue;
+      first_bump[x] = 0;
+      victim_step[x] = 0;
+      bump_count[x] = 0;
+    }
+  }
+  if (threadIdx.x == 0 && s_end > s0) *search_start = (sh.last_victim + 1) % n;
+  __syncthreads();
+  return s_end;
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    clock_stream_batched_kernel(MetaT* meta, int64_t num_slots, int64_t* search_start,
+                                int64_t num_steps, int64_t alloc_per_step, const int64_t* reaccess,
+                                int64_t reaccess_per_step, int64_t* victims, int64_t* steps_done,
+                                int order, bool aligned, int32_t* scratch, int64_t* status) {
+  __shared__ EpochShared<MetaT> sh;
+  const int64_t n = num_slots;
+  int32_t* cand = scratch;
+  int32_t* cand_bump = scratch + n;
+  int32_t* first_bump = scratch + 2 * n;
+  int32_t* victim_step = scratch + 3 * n;
+  int32_t* bump_count = scratch + 4 * n;
+  int64_t s = 0;
+  int64_t exact_until = 0;
+  while (s < num_steps) {
+    if (s >= exact_until) {
+      const int64_t s_end = stream_epoch<MetaT>(meta, n, search_start, s, num_steps, alloc_per_step,
+                                                reaccess, reaccess_per_step, victims, cand,
+                                                cand_bump, first_bump, victim_step, bump_count,
+                                                aligned, status, sh);
+      if (s_end - s < kEpochMinSteps) exact_until = s_end + 1 + kExactStepsAfterShortEpoch;
+      s = s_end;
+      if (s >= num_steps) break;
+    }
+    const int rc = stream_step<MetaT>(meta, n, search_start, s, alloc_per_step, reaccess,
+                                      reaccess_per_step, victims, order, aligned, status, sh.pop);
+    if (rc != KVCA_OK) {
+      if (threadIdx.x == 0) report(status, rc, s);
+      break;
+    }
+    ++s;
+  }
+  if (threadIdx.x == 0) *steps_done = s;
 }
 
 // ---------------------------------------------------------------------------
@@ -1193,6 +1575,20 @@ cudaError_t launch_clock_stream(int meta_bits, int order, void* meta, int64_t nu
                                     static_cast<MetaT*>(meta), num_slots, search_start, num_steps,
                                     alloc_per_step, reaccess, reaccess_per_step, victims,
                                     steps_done, order, aligned, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_clock_stream_batched(int meta_bits, int order, void* meta, int64_t num_slots,
+                                        int64_t* search_start, int64_t num_steps,
+                                        int64_t alloc_per_step, const int64_t* reaccess,
+                                        int64_t reaccess_per_step, int64_t* victims,
+                                        int64_t* steps_done, int32_t* scratch, int64_t* status,
+                                        cudaStream_t stream) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  KVCA_META_DISPATCH(meta_bits, clock_stream_batched_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    static_cast<MetaT*>(meta), num_slots, search_start, num_steps,
+                                    alloc_per_step, reaccess, reaccess_per_step, victims,
+                                    steps_done, order, aligned, scratch, status));
   return cudaGetLastError();
 }
 

@@ -328,12 +328,30 @@ def release_metadata(logical_to_physical, slot_meta, logical_block_ids, *,
     _maybe_check(dev, check, "release_metadata")
 
 
+_stream_scratch: dict[tuple[int, int, int], torch.Tensor] = {}
+
+
+def _clock_scratch(dev: torch.device, num_slots: int) -> torch.Tensor:
+    words = int(_lib_handle.kvca_clock_stream_scratch_bytes(num_slots)) // 4
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(dev).cuda_stream, words)
+    buf = _stream_scratch.get(key)
+    if buf is None:
+        buf = torch.zeros(words, dtype=torch.int32, device=dev)
+        _stream_scratch[key] = buf
+    return buf
+
+
 def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps: int,
                  alloc_per_step: int, reaccess: torch.Tensor, reaccess_per_step: int, *,
                  victims: torch.Tensor | None = None, order: str | None = None,
-                 check: bool | None = None):
-    """Run ``num_steps`` of (pop, refill victims with usage 1, bump re-accessed
-    slots) in one launch.  Returns (victims, steps_done tensor)."""
+                 method: str = "batched", check: bool | None = None):
+    """Run ``num_steps`` of (pop ``alloc_per_step`` victims, refill them with
+    usage 1, bump the step's ``reaccess_per_step`` re-accessed slots) in one
+    launch.  Returns (victims, steps_done tensor).
+
+    ``method="batched"`` resolves runs of steps that need no aging at once
+    (same results); ``method="steps"`` runs the steps one after another."""
     _require(slot_meta, _META_DTYPES, "slot_meta")
     _require(search_start, torch.int64, "search_start")
     _require(reaccess, torch.int64, "reaccess")
@@ -348,11 +366,20 @@ def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps:
         if victims.numel() < num_steps * alloc_per_step:
             raise ValueError("victims is too small")
     steps_done = torch.zeros(1, dtype=torch.int64, device=dev)
+    order_code = POP_ORDERS[order or _DEFAULT_POP_ORDER]
     with torch.cuda.device(dev):
-        rc = _lib_handle.kvca_clock_stream(
-            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(slot_meta),
-            slot_meta.numel(), _ptr(search_start), num_steps, alloc_per_step, _ptr(reaccess),
-            reaccess_per_step, _ptr(victims), _ptr(steps_done), _ptr(_status(dev)), _stream(dev))
+        if method == "batched":
+            rc = _lib_handle.kvca_clock_stream_batched(
+                _meta_bits(slot_meta), order_code, _ptr(slot_meta), slot_meta.numel(), _ptr(search_start),
+                num_steps, alloc_per_step, _ptr(reaccess), reaccess_per_step, _ptr(victims), _ptr(steps_done),
+                _ptr(_clock_scratch(dev, slot_meta.numel())), _ptr(_status(dev)), _stream(dev))
+        elif method == "steps":
+            rc = _lib_handle.kvca_clock_stream(
+                _meta_bits(slot_meta), order_code, _ptr(slot_meta), slot_meta.numel(), _ptr(search_start),
+                num_steps, alloc_per_step, _ptr(reaccess), reaccess_per_step, _ptr(victims), _ptr(steps_done),
+                _ptr(_status(dev)), _stream(dev))
+        else:
+            raise ValueError(f"unknown clock stream method {method!r}")
     _host_rc(rc, "clock_stream")
     _maybe_check(dev, check, "clock_stream")
     return victims, steps_done

@@ -29,20 +29,22 @@ def _pack16(pins, usage):
     return ((pins.to(torch.int32) & 255) | ((usage.to(torch.int32) & 255) << 8)).to(torch.uint16)
 
 
-def test_recorded_reference_streams(ops, golden_dir):
+@pytest.mark.parametrize("method", ["batched", "steps"])
+def test_recorded_reference_streams(ops, golden_dir, method):
     for rec in json.loads((golden_dir / "clock_stream.json").read_text()):
         p = rec["params"]
         meta = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta).to(DEV)
         ss = torch.zeros(1, dtype=torch.int64, device=DEV)
         victims, done = ops.clock_stream(meta, ss, p["num_steps"], p["alloc_per_step"],
-                                         workloads.zipf_reaccess(p).to(DEV), p["reaccess_per_step"])
+                                         workloads.zipf_reaccess(p).to(DEV), p["reaccess_per_step"],
+                                         method=method)
         assert int(done) == rec["steps_done"]
         assert victims.tolist() == rec["victims"]
         assert workloads.sha256_of(meta) == rec["final_slot_meta_sha256"]
         assert int(ss[0]) == rec["final_search_start"]
 
 
-def _run_both(ops, p, *, order="grouped", bits=8):
+def _run_both(ops, p, *, order="grouped", bits=8, method="batched"):
     pack = adapter_mod._pack_slot_meta if bits == 8 else _pack16
     meta_h = workloads.clock_initial_meta(p, pack)
     reacc = workloads.zipf_reaccess(p)
@@ -52,18 +54,20 @@ def _run_both(ops, p, *, order="grouped", bits=8):
     meta_d = workloads.clock_initial_meta(p, pack).to(DEV)
     ss_d = torch.zeros(1, dtype=torch.int64, device=DEV)
     got, done_d = ops.clock_stream(meta_d, ss_d, p["num_steps"], p["alloc_per_step"], reacc.to(DEV),
-                                   p["reaccess_per_step"], order=order, check=False)
+                                   p["reaccess_per_step"], order=order, method=method, check=False)
     torch.cuda.synchronize()
     return (want, done_h, rc, meta_h, ss_h), (got, int(done_d), meta_d, ss_d)
 
 
+@pytest.mark.parametrize("method", ["batched", "steps"])
 @pytest.mark.parametrize("order", ["grouped", "prefix"])
 @pytest.mark.parametrize("bits", [8, 16])
 @pytest.mark.parametrize("k,m,usage_hi", [(1, 1, 3), (256, 256, 3), (5, 40, 15), (64, 8, 1)])
-def test_streams_match_oracle(ops, order, bits, k, m, usage_hi):
+def test_streams_match_oracle(ops, method, order, bits, k, m, usage_hi):
     p = workloads.clock_params(65536 + 37, 3000 if k == 1 else 400, k, m, seed=4242 + k + m,
                                usage_hi=usage_hi)
-    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p, order=order, bits=bits)
+    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p, order=order, bits=bits,
+                                                                              method=method)
     assert rc == 0 and done_h == done_d == p["num_steps"]
     assert torch.equal(got.cpu(), want)
     assert np.array_equal(meta_d.cpu().numpy(), meta_h.numpy())
@@ -71,14 +75,15 @@ def test_streams_match_oracle(ops, order, bits, k, m, usage_hi):
     ops.check_status(DEV)
 
 
+@pytest.mark.parametrize("method", ["batched", "steps"])
 @pytest.mark.parametrize("k", [1, 256])
-def test_full_size_clock_stress_matches_oracle(ops, k):
+def test_full_size_clock_stress_matches_oracle(ops, k, method):
     """1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations with one
     Zipf(1.1) re-access per allocation: identical victim sequence and final
     usage array."""
     steps = 200_000 // k
     p = workloads.clock_params(1 << 20, steps, k, k, seed=1234)
-    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p)
+    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p, method=method)
     assert rc == 0 and done_h == done_d == steps
     assert torch.equal(got.cpu(), want)
     assert workloads.sha256_of(meta_d) == workloads.sha256_of(meta_h)
@@ -86,7 +91,26 @@ def test_full_size_clock_stress_matches_oracle(ops, k):
     ops.check_status(DEV)
 
 
-def test_stream_stops_on_insufficient_capacity(ops):
+@pytest.mark.parametrize("k,m,n,steps,usage_hi,pinned", [
+    (1, 4, 4096, 20000, 3, 0.05),      # long stream: the sweep wraps, many aging events
+    (3, 64, 1000, 3000, 15, 0.3),      # short epochs: exact stretches between them
+    (17, 5, 2048, 2000, 1, 0.0),       # k not dividing the candidate runs
+    (1, 0, 777, 5000, 2, 0.5),         # no re-access at all
+    (128, 1024, 4096, 300, 7, 0.1),    # heavy re-access with duplicates in each batch
+])
+def test_batched_stream_with_frequent_aging_matches_oracle(ops, k, m, n, steps, usage_hi, pinned):
+    p = workloads.clock_params(n, steps, k, m, seed=99 + k + m + n, usage_hi=usage_hi, pinned_frac=pinned)
+    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p, method="batched")
+    assert done_d == done_h
+    assert torch.equal(got.cpu()[: done_h * k], want[: done_h * k])
+    assert np.array_equal(meta_d.cpu().numpy(), meta_h.numpy())
+    assert int(ss_d[0]) == int(ss_h[0])
+    if rc == 0:
+        ops.check_status(DEV)
+
+
+@pytest.mark.parametrize("method", ["batched", "steps"])
+def test_stream_stops_on_insufficient_capacity(ops, method):
     from kv_cache_adapter_b200.errors import InsufficientCapacityError
 
     # 10 slots, 3 pinned: 7 reusable; victims are refilled unpinned, so the
@@ -95,9 +119,9 @@ def test_stream_stops_on_insufficient_capacity(ops):
     meta = adapter_mod._pack_slot_meta(pins, torch.zeros(10, dtype=torch.int64)).to(DEV)
     ss = torch.zeros(1, dtype=torch.int64, device=DEV)
     reacc = torch.zeros(0, dtype=torch.int64, device=DEV)
-    victims, done = ops.clock_stream(meta, ss, 3, 8, reacc, 0, check=False)
+    victims, done = ops.clock_stream(meta, ss, 3, 8, reacc, 0, check=False, method=method)
     assert int(done) == 0
     with pytest.raises(InsufficientCapacityError):
         ops.check_status(DEV)
-    victims, done = ops.clock_stream(meta, ss, 3, 7, reacc, 0)
+    victims, done = ops.clock_stream(meta, ss, 3, 7, reacc, 0, method=method)
     assert int(done) == 3
