@@ -224,13 +224,13 @@ int kvca_clock_stream(int meta_bits, int order, void* d_slot_meta, int64_t num_s
 
 size_t kvca_clock_stream_scratch_bytes(int64_t num_slots) {
   if (num_slots <= 0) return 0;
-  return static_cast<size_t>(num_slots) * 5 * sizeof(int32_t);
+  return static_cast<size_t>(num_slots) * 32;
 }
 
 int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
                               int64_t* d_search_start, int64_t num_steps, int64_t alloc_per_step,
                               const int64_t* d_reaccess, int64_t reaccess_per_step,
-                              int64_t* d_victims, int64_t* d_steps_done, int32_t* d_scratch,
+                              int64_t* d_victims, int64_t* d_steps_done, void* d_scratch,
                               int64_t* d_status, kvca_stream_t stream) {
   if (!valid_meta_bits(meta_bits)) return KVCA_ERR_BAD_ARGUMENT;
   if (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX)
@@ -242,10 +242,12 @@ int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64
     return KVCA_ERR_BAD_ARGUMENT;
   if (!d_slot_meta || !d_search_start || !d_victims || !d_steps_done || !d_scratch)
     return KVCA_ERR_BAD_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(d_scratch) & 7u) != 0u) return KVCA_ERR_BAD_ARGUMENT;
   if (reaccess_per_step > 0 && num_steps > 0 && !d_reaccess) return KVCA_ERR_BAD_ARGUMENT;
   return status_of(kvca::launch_clock_stream_batched(
       meta_bits, order, d_slot_meta, num_slots, d_search_start, num_steps, alloc_per_step,
-      d_reaccess, reaccess_per_step, d_victims, d_steps_done, d_scratch, d_status, stream));
+      d_reaccess, reaccess_per_step, d_victims, d_steps_done,
+      reinterpret_cast<unsigned char*>(d_scratch), d_status, stream));
 }
 
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,

@@ -492,13 +492,18 @@ __global__ void __launch_bounds__(1024)
 // slots of S in scan order from search_start (the candidates), taken k per
 // step, except that a candidate whose first re-access comes at a step before
 // the one that would take it has usage 1 by then and is passed over.  An
-// "epoch" computes all of that at once:
+// "epoch" computes all of that at once, with the whole CTA:
 //   1. compact the candidates (one pass over slot_meta);
 //   2. first re-access step of every slot re-accessed in the window of steps
-//      the candidates can cover (atomicMax on an encoded step);
-//   3. one warp walks the candidates in order and takes candidate j unless
-//      its first re-access step is below the step its rank gives it, 32 at a
-//      time with a ballot fixed point;
+//      the candidates can cover (atomicMax on an encoded step; the thread
+//      that sets a slot first lists it, so touched slots are listed once);
+//   3. candidates with a re-access in the window ("pending") are listed in
+//      order; one warp resolves only those, 32 at a time with a ballot fixed
+//      point: pending candidate j is taken unless its first re-access step is
+//      below s0 + (taken before j) / k, where taken before j = (candidates
+//      before j that are not pending) + (pending ones taken before it);
+//      every other candidate is taken while that count stays below the
+//      request, so block-wide scans place all victims at once;
 //   4. fold the epoch's refills and bumps into each touched slot:
 //      usage = min(base + distinct bumping steps, max), base = 1 for a victim
 //      (only bumps at or after its step count) and the old usage otherwise.
@@ -506,13 +511,10 @@ __global__ void __launch_bounds__(1024)
 // as one exact step (stream_step), then the next epoch starts.  After short
 // epochs the kernel runs a stretch of exact steps instead.  Results equal the
 // step-by-step stream bit for bit.
-//
-// Scratch: 5 x num_slots int32 (candidates, their first re-access steps, and
-// three per-slot words that are zero on entry and left zero on exit).
 
 constexpr int64_t kEpochMinSteps = 8;
 constexpr int64_t kExactStepsAfterShortEpoch = 64;
-constexpr int kFilterChunks = 8;  // 32-candidate chunks loaded ahead by the filter warp
+constexpr int kCandPerThread = 16;  // candidates per thread per block-scan tile
 constexpr int kWarpDedupMin = 16;   // re-accesses per step deduplicated in registers
 constexpr int kWarpDedupMax = 256;
 
@@ -523,6 +525,23 @@ struct EpochShared {
   long long start;
   long long s_end;
   long long last_victim;
+  int tp_total;  // pending candidates taken
+  int nu;        // distinct slots re-accessed in the window
+};
+
+// Scratch of kvca_clock_stream_batched, carved from one buffer (byte
+// offsets for num_slots = n): pending int64[n] at 0, cand int32[n] at 8n,
+// cand_bump int32[n] at 12n, touched int32[n] at 16n, then the three arrays
+// that are zero on entry and left zero on exit: first_bump, victim_step,
+// bump_count (int32[n] each, from 20n to 32n).
+struct EpochScratch {
+  int64_t* pending;
+  int32_t* cand;
+  int32_t* cand_bump;
+  int32_t* touched;
+  int32_t* first_bump;
+  int32_t* victim_step;
+  int32_t* bump_count;
 };
 
 __device__ __forceinline__ bool slot_ok(int64_t x, int64_t n) { return x >= 0 && x < n; }
@@ -530,17 +549,18 @@ __device__ __forceinline__ bool slot_ok(int64_t x, int64_t n) { return x >= 0 &&
 template <typename MetaT>
 __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, int64_t s0,
                                 int64_t steps, int64_t k, const int64_t* reaccess, int64_t m,
-                                int64_t* victims, int32_t* cand, int32_t* cand_bump,
-                                int32_t* first_bump, int32_t* victim_step, int32_t* bump_count,
-                                bool aligned, int64_t* status, EpochShared<MetaT>& sh) {
+                                int64_t* victims, const EpochScratch& w, bool aligned,
+                                int64_t* status, EpochShared<MetaT>& sh) {
   using M = Meta<MetaT>;
   constexpr int kSpv = M::kSlotsPerVec;
+  constexpr int C = kCandPerThread;
   if (threadIdx.x == 0) {
     long long p0 = static_cast<long long>(*search_start % n);
     if (p0 < 0) p0 += n;
     sh.start = p0;
     sh.s_end = s0;
     sh.last_victim = -1;
+    sh.nu = 0;
   }
   __syncthreads();
   const int64_t p0 = sh.start;
@@ -562,8 +582,8 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
 #pragma unroll
         for (int j = 0; j < kSpv; ++j) {
           const int64_t slot = v * kSpv + j;
-          const unsigned w = mv.s[j];
-          if (slot >= lo && slot < hi && M::pin(w) == 0u && M::usage(w) == 0u) mask |= 1u << j;
+          const unsigned wd = mv.s[j];
+          if (slot >= lo && slot < hi && M::pin(wd) == 0u && M::usage(wd) == 0u) mask |= 1u << j;
         }
       }
       int total;
@@ -572,7 +592,7 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
       while (mask != 0u) {
         const int j = __ffs(mask) - 1;
         mask &= mask - 1u;
-        cand[rank++] = static_cast<int32_t>(v * kSpv + j);
+        w.cand[rank++] = static_cast<int32_t>(v * kSpv + j);
       }
       nc += total;
     }
@@ -590,105 +610,125 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
       report(status, KVCA_ERR_BAD_INDEX, x);
       continue;
     }
-    atomicMax(first_bump + x, static_cast<int32_t>(INT32_MAX - e / m));
+    const int32_t old = atomicMax(w.first_bump + x, static_cast<int32_t>(INT32_MAX - e / m));
+    if (old == 0) w.touched[atomicAdd(&sh.nu, 1)] = static_cast<int32_t>(x);
   }
   __syncthreads();
+  const int nu = sh.nu;
   for (int64_t j = threadIdx.x; j < nc; j += blockDim.x) {
-    const int32_t enc = first_bump[cand[j]];
-    cand_bump[j] = enc == 0 ? INT32_MAX : INT32_MAX - enc;
+    const int32_t enc = w.first_bump[w.cand[j]];
+    w.cand_bump[j] = enc == 0 ? INT32_MAX : INT32_MAX - enc;
   }
   __syncthreads();
 
-  // 3. the filter: candidate j is taken at step s0 + (taken before j) / k
-  //    unless its first re-access step is smaller than that step.  32-bit
-  //    counts (the launcher keeps num_steps * alloc_per_step below 2^31);
-  //    within a chunk the step offset of lane j is (r0 + prefix_j) / k with
-  //    r0 = taken % k and prefix_j < 32, so no division is needed per lane.
+  // 3a. list the pending candidates in order: (index << 32) | first re-access step
+  int64_t np = 0;
+  for (int64_t tile = 0; tile < nc; tile += static_cast<int64_t>(blockDim.x) * C) {
+    const int64_t jb = tile + static_cast<int64_t>(threadIdx.x) * C;
+    int32_t b[C];
+    int cnt = 0;
+#pragma unroll
+    for (int u = 0; u < C; ++u) {
+      b[u] = jb + u < nc ? w.cand_bump[jb + u] : INT32_MAX;
+      cnt += b[u] != INT32_MAX;
+    }
+    int total;
+    int64_t p = np + block_excl_scan(cnt, &total, sh.scan);
+#pragma unroll
+    for (int u = 0; u < C; ++u)
+      if (b[u] != INT32_MAX)
+        w.pending[p++] = (static_cast<int64_t>(jb + u) << 32) | static_cast<uint32_t>(b[u]);
+    np += total;
+  }
+  __syncthreads();
+
+  // 3b. one warp resolves the pending candidates; each entry becomes
+  //     (pending candidates taken before it << 1) | taken
+  const int32_t kk = static_cast<int32_t>(k);
+  const int32_t max_taken = static_cast<int32_t>((steps - s0) * k);
+  const int32_t step0 = static_cast<int32_t>(s0);
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     const unsigned below = (1u << lane) - 1u;
-    const int32_t kk = static_cast<int32_t>(k);
-    const int32_t max_taken = static_cast<int32_t>((steps - s0) * k);
-    const int32_t ncand = static_cast<int32_t>(nc);
-    const int32_t step0 = static_cast<int32_t>(s0);
-    int32_t taken = 0;
-    int32_t fb[kFilterChunks];
-    int32_t cs[kFilterChunks];
-#pragma unroll
-    for (int q = 0; q < kFilterChunks; ++q) {
-      const int32_t idx = q * 32 + lane;
-      fb[q] = idx < ncand ? cand_bump[idx] : -1;
-      cs[q] = idx < ncand ? cand[idx] : -1;
-    }
-    for (int32_t j = 0; j < ncand && taken < max_taken; j += 32 * kFilterChunks) {
-      // prefetch the next 256 candidates while this batch is resolved
-      int32_t fb_next[kFilterChunks];
-      int32_t cs_next[kFilterChunks];
-#pragma unroll
-      for (int q = 0; q < kFilterChunks; ++q) {
-        const int32_t idx = j + 32 * kFilterChunks + q * 32 + lane;
-        fb_next[q] = idx < ncand ? cand_bump[idx] : -1;
-        cs_next[q] = idx < ncand ? cand[idx] : -1;
+    int32_t tp = 0;
+    for (int64_t p0w = 0; p0w < np; p0w += 32) {
+      const int64_t p = p0w + lane;
+      const bool here = p < np;
+      const int64_t pr = here ? w.pending[p] : 0;
+      const int32_t jj = static_cast<int32_t>(pr >> 32);
+      const int32_t b = static_cast<int32_t>(pr & 0xffffffffll);
+      const int32_t nonpending_before = here ? jj - static_cast<int32_t>(p) : 0;
+      const unsigned present = __ballot_sync(0xffffffffu, here);
+      unsigned cur = present;
+      for (int it = 0; it < 33; ++it) {  // converges in at most 32 rounds
+        const int32_t tb = nonpending_before + tp + __popc(cur & below);
+        const int32_t st = kk == 1 ? step0 + tb : step0 + tb / kk;
+        const bool ok = here && tb < max_taken && b >= st;
+        const unsigned ok_mask = __ballot_sync(0xffffffffu, ok);
+        const unsigned diff = (ok_mask ^ cur) & present;
+        if (diff == 0u) break;
+        const unsigned keep = (1u << (__ffs(diff) - 1)) - 1u;
+        cur = (cur & keep) | (ok_mask & ~keep);
       }
+      if (here)
+        w.pending[p] = (static_cast<int64_t>(tp + __popc(cur & below)) << 1) |
+                       static_cast<int64_t>((cur >> lane) & 1u);
+      tp += __popc(cur);
+    }
+    if (lane == 0) sh.tp_total = tp;
+  }
+  __syncthreads();
+  const int32_t tp_total = sh.tp_total;
+  int64_t total_taken = (nc - np) + tp_total;
+  if (total_taken > max_taken) total_taken = max_taken;
+  const int64_t full = total_taken / k;  // complete steps of this epoch
+  const int64_t full_pos = full * k;
+  const int64_t s_end = s0 + full;
+
+  // 3c. place every victim of the complete steps:
+  //     taken before j = (j - pending before j) + pending taken before j
+  {
+    int64_t np_run = 0;
+    for (int64_t tile = 0; tile < nc; tile += static_cast<int64_t>(blockDim.x) * C) {
+      const int64_t jb = tile + static_cast<int64_t>(threadIdx.x) * C;
+      int32_t b[C];
+      int cnt = 0;
 #pragma unroll
-      for (int q = 0; q < kFilterChunks; ++q) {
-        const unsigned present = __ballot_sync(0xffffffffu, cs[q] >= 0);
-        // candidates never re-accessed in the window are taken whatever their
-        // step; a chunk holding only those needs no fixed point
-        const unsigned pending = __ballot_sync(0xffffffffu, cs[q] >= 0 && fb[q] != INT32_MAX);
-        const int32_t n_present = __popc(present);
-        if (pending == 0u && taken + n_present <= max_taken) {
-          if (cs[q] >= 0) {
-            const int32_t pos = taken + __popc(present & below);
-            const int32_t st = kk == 1 ? step0 + pos : step0 + pos / kk;
-            victims[s0 * k + pos] = cs[q];
-            victim_step[cs[q]] = st + 1;
+      for (int u = 0; u < C; ++u) {
+        b[u] = jb + u < nc ? w.cand_bump[jb + u] : INT32_MAX;
+        cnt += b[u] != INT32_MAX;
+      }
+      int total;
+      int64_t pp = np_run + block_excl_scan(cnt, &total, sh.scan);
+      int64_t cached_pp = -1;
+      int64_t entry = 0;
+#pragma unroll
+      for (int u = 0; u < C; ++u) {
+        const int64_t j = jb + u;
+        if (j >= nc) continue;
+        const bool is_pending = b[u] != INT32_MAX;
+        int64_t tpb = tp_total;
+        if (pp < np) {
+          if (pp != cached_pp) {
+            entry = w.pending[pp];
+            cached_pp = pp;
           }
-          taken += n_present;
-          continue;
+          tpb = entry >> 1;
         }
-        const int32_t q0 = kk == 1 ? taken : taken / kk;
-        const int32_t r0 = taken - q0 * kk;
-        const int32_t base_step = step0 + q0;
-        unsigned cur = present;
-        for (int it = 0; it < 33; ++it) {  // converges in at most 32 rounds
-          const int32_t prefix = __popc(cur & below);
-          const int32_t x = r0 + prefix;
-          const int32_t d = kk == 1 ? x : (kk >= 32 ? (x >= kk ? 1 : 0) : x / kk);
-          const bool ok = cs[q] >= 0 && taken + prefix < max_taken && fb[q] >= base_step + d;
-          const unsigned ok_mask = __ballot_sync(0xffffffffu, ok);
-          const unsigned diff = (ok_mask ^ cur) & present;
-          if (diff == 0u) break;
-          const unsigned keep = (1u << (__ffs(diff) - 1)) - 1u;
-          cur = (cur & keep) | (ok_mask & ~keep);
+        const int64_t tb = (j - pp) + tpb;
+        const bool ok = is_pending ? (entry & 1) != 0 : tb < max_taken;
+        if (ok && tb < full_pos) {
+          const int32_t x = w.cand[j];
+          victims[s0 * k + tb] = x;
+          w.victim_step[x] = static_cast<int32_t>(s0 + tb / k + 1);
+          if (tb == full_pos - 1) sh.last_victim = x;
         }
-        if ((cur >> lane) & 1u) {
-          const int32_t prefix = __popc(cur & below);
-          const int32_t x = r0 + prefix;
-          const int32_t d = kk == 1 ? x : (kk >= 32 ? (x >= kk ? 1 : 0) : x / kk);
-          victims[s0 * k + taken + prefix] = cs[q];
-          victim_step[cs[q]] = base_step + d + 1;
-        }
-        taken += __popc(cur);
+        if (is_pending) ++pp;
       }
-#pragma unroll
-      for (int q = 0; q < kFilterChunks; ++q) {
-        fb[q] = fb_next[q];
-        cs[q] = cs_next[q];
-      }
-    }
-    __syncwarp();
-    const int64_t full = taken / k;
-    // a step left incomplete is not an epoch step: undo its victims
-    for (int64_t pos = full * k + lane; pos < taken; pos += 32)
-      victim_step[victims[s0 * k + pos]] = 0;
-    if (lane == 0) {
-      sh.s_end = s0 + full;
-      sh.last_victim = full > 0 ? victims[s0 * k + full * k - 1] : -1;
+      np_run += total;
     }
   }
   __syncthreads();
-  const int64_t s_end = sh.s_end;
   const int64_t v_lo = s0 * k;
   const int64_t v_hi = s_end * k;
   const int64_t cnt_hi = s_end * m;
@@ -704,10 +744,10 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
       int64_t ids[kWarpDedupMax / 32];
       bool dup[kWarpDedupMax / 32];
 #pragma unroll
-      for (int w = 0; w < kWarpDedupMax / 32; ++w) {
-        const int64_t i = static_cast<int64_t>(w) * 32 + lane;
-        ids[w] = i < m ? reaccess[t * m + i] : -1;
-        dup[w] = false;
+      for (int q = 0; q < kWarpDedupMax / 32; ++q) {
+        const int64_t i = static_cast<int64_t>(q) * 32 + lane;
+        ids[q] = i < m ? reaccess[t * m + i] : -1;
+        dup[q] = false;
       }
 #pragma unroll
       for (int u = 0; u < kWarpDedupMax / 32; ++u) {
@@ -717,16 +757,15 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
           const int64_t v = __shfl_sync(0xffffffffu, ids[u], l);
           const int i = u * 32 + l;
 #pragma unroll
-          for (int w = 0; w < kWarpDedupMax / 32; ++w)
-            dup[w] |= (w * 32 + lane > i) && ids[w] == v;
+          for (int q = 0; q < kWarpDedupMax / 32; ++q) dup[q] |= (q * 32 + lane > i) && ids[q] == v;
         }
       }
 #pragma unroll
-      for (int w = 0; w < kWarpDedupMax / 32; ++w) {
-        const int64_t x = ids[w];
-        if (dup[w] || !slot_ok(x, n)) continue;
-        const int32_t vs = victim_step[x];
-        if (vs == 0 || vs - 1 <= t) atomicAdd(bump_count + x, 1);
+      for (int q = 0; q < kWarpDedupMax / 32; ++q) {
+        const int64_t x = ids[q];
+        if (dup[q] || !slot_ok(x, n)) continue;
+        const int32_t vs = w.victim_step[x];
+        if (vs == 0 || vs - 1 <= t) atomicAdd(w.bump_count + x, 1);
       }
     }
   } else {
@@ -738,25 +777,25 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
 #pragma unroll 8
       for (int64_t i = t * m; i < e; ++i) dup |= reaccess[i] == x;
       if (dup) continue;
-      const int32_t vs = victim_step[x];
-      if (vs == 0 || vs - 1 <= t) atomicAdd(bump_count + x, 1);
+      const int32_t vs = w.victim_step[x];
+      if (vs == 0 || vs - 1 <= t) atomicAdd(w.bump_count + x, 1);
     }
   }
   __syncthreads();
-  // 4b. final usage of every touched slot, computed from the epoch-start
-  //     words (idempotent, so duplicates may compute it twice)
-  const int64_t n_ev = ev_hi - ev_lo;
-  const int64_t touched = n_ev + (v_hi - v_lo);
-  constexpr int kU = 4;
+
+  // 4b. final usage of every touched slot (each listed re-accessed slot once,
+  //     plus the victims), computed from the epoch-start words
+  const int64_t n_touched = nu + (v_hi - v_lo);
   auto touched_slot = [&](int64_t i) -> int64_t {
-    return i < n_ev ? reaccess[ev_lo + i] : victims[v_lo + (i - n_ev)];
+    return i < nu ? static_cast<int64_t>(w.touched[i]) : victims[v_lo + (i - nu)];
   };
-  for (int64_t i0 = threadIdx.x; i0 < touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
+  constexpr int kU = 4;
+  for (int64_t i0 = threadIdx.x; i0 < n_touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
     int64_t xs[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
-      xs[u] = i < touched ? touched_slot(i) : -1;
+      xs[u] = i < n_touched ? touched_slot(i) : -1;
     }
     unsigned ws[kU];
     int32_t vss[kU], cts[kU];
@@ -764,24 +803,24 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
     for (int u = 0; u < kU; ++u) {
       const bool ok = slot_ok(xs[u], n);
       ws[u] = ok ? static_cast<unsigned>(meta[xs[u]]) : 0u;
-      vss[u] = ok ? victim_step[xs[u]] : 0;
-      cts[u] = ok ? bump_count[xs[u]] : 0;
+      vss[u] = ok ? w.victim_step[xs[u]] : 0;
+      cts[u] = ok ? w.bump_count[xs[u]] : 0;
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       if (!slot_ok(xs[u], n)) continue;
       int64_t fin = (vss[u] != 0 ? 1 : static_cast<int64_t>(M::usage(ws[u]))) + cts[u];
       if (fin > M::kUsageMax) fin = M::kUsageMax;
-      first_bump[xs[u]] = static_cast<int32_t>(fin + 1);
+      w.first_bump[xs[u]] = static_cast<int32_t>(fin + 1);
     }
   }
   __syncthreads();
-  for (int64_t i0 = threadIdx.x; i0 < touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
+  for (int64_t i0 = threadIdx.x; i0 < n_touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
     int64_t xs[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
-      xs[u] = i < touched ? touched_slot(i) : -1;
+      xs[u] = i < n_touched ? touched_slot(i) : -1;
     }
     unsigned ws[kU];
     int32_t fins[kU];
@@ -789,7 +828,7 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
     for (int u = 0; u < kU; ++u) {
       const bool ok = slot_ok(xs[u], n);
       ws[u] = ok ? static_cast<unsigned>(meta[xs[u]]) : 0u;
-      fins[u] = ok ? first_bump[xs[u]] : 0;
+      fins[u] = ok ? w.first_bump[xs[u]] : 0;
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u)
@@ -797,17 +836,12 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   }
   __syncthreads();
   // 4c. leave the per-slot scratch words zero again
-  for (int64_t i0 = threadIdx.x; i0 < touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
-      if (i >= touched) continue;
-      const int64_t x = touched_slot(i);
-      if (!slot_ok(x, n)) continue;
-      first_bump[x] = 0;
-      victim_step[x] = 0;
-      bump_count[x] = 0;
-    }
+  for (int64_t i = threadIdx.x; i < n_touched; i += blockDim.x) {
+    const int64_t x = touched_slot(i);
+    if (!slot_ok(x, n)) continue;
+    w.first_bump[x] = 0;
+    w.victim_step[x] = 0;
+    w.bump_count[x] = 0;
   }
   if (threadIdx.x == 0 && s_end > s0) *search_start = (sh.last_victim + 1) % n;
   __syncthreads();
@@ -819,22 +853,24 @@ __global__ void __launch_bounds__(1024)
     clock_stream_batched_kernel(MetaT* meta, int64_t num_slots, int64_t* search_start,
                                 int64_t num_steps, int64_t alloc_per_step, const int64_t* reaccess,
                                 int64_t reaccess_per_step, int64_t* victims, int64_t* steps_done,
-                                int order, bool aligned, int32_t* scratch, int64_t* status) {
+                                int order, bool aligned, unsigned char* scratch, int64_t* status) {
   __shared__ EpochShared<MetaT> sh;
   const int64_t n = num_slots;
-  int32_t* cand = scratch;
-  int32_t* cand_bump = scratch + n;
-  int32_t* first_bump = scratch + 2 * n;
-  int32_t* victim_step = scratch + 3 * n;
-  int32_t* bump_count = scratch + 4 * n;
+  EpochScratch w;
+  w.pending = reinterpret_cast<int64_t*>(scratch);
+  w.cand = reinterpret_cast<int32_t*>(scratch + 8 * n);
+  w.cand_bump = reinterpret_cast<int32_t*>(scratch + 12 * n);
+  w.touched = reinterpret_cast<int32_t*>(scratch + 16 * n);
+  w.first_bump = reinterpret_cast<int32_t*>(scratch + 20 * n);
+  w.victim_step = reinterpret_cast<int32_t*>(scratch + 24 * n);
+  w.bump_count = reinterpret_cast<int32_t*>(scratch + 28 * n);
   int64_t s = 0;
   int64_t exact_until = 0;
   while (s < num_steps) {
     if (s >= exact_until) {
       const int64_t s_end = stream_epoch<MetaT>(meta, n, search_start, s, num_steps, alloc_per_step,
-                                                reaccess, reaccess_per_step, victims, cand,
-                                                cand_bump, first_bump, victim_step, bump_count,
-                                                aligned, status, sh);
+                                                reaccess, reaccess_per_step, victims, w, aligned,
+                                                status, sh);
       if (s_end - s < kEpochMinSteps) exact_until = s_end + 1 + kExactStepsAfterShortEpoch;
       s = s_end;
       if (s >= num_steps) break;
@@ -1582,8 +1618,8 @@ cudaError_t launch_clock_stream_batched(int meta_bits, int order, void* meta, in
                                         int64_t* search_start, int64_t num_steps,
                                         int64_t alloc_per_step, const int64_t* reaccess,
                                         int64_t reaccess_per_step, int64_t* victims,
-                                        int64_t* steps_done, int32_t* scratch, int64_t* status,
-                                        cudaStream_t stream) {
+                                        int64_t* steps_done, unsigned char* scratch,
+                                        int64_t* status, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
   KVCA_META_DISPATCH(meta_bits, clock_stream_batched_kernel<MetaT><<<1, 1024, 0, stream>>>(
                                     static_cast<MetaT*>(meta), num_slots, search_start, num_steps,

@@ -93,7 +93,7 @@ cudaError_t launch_clock_stream_batched(int meta_bits, int order, void* meta, in
                                         int64_t* search_start, int64_t num_steps,
                                         int64_t alloc_per_step, const int64_t* reaccess,
                                         int64_t reaccess_per_step, int64_t* victims,
-                                        int64_t* steps_done, int32_t* scratch, int64_t* status,
-                                        cudaStream_t stream);
+                                        int64_t* steps_done, unsigned char* scratch,
+                                        int64_t* status, cudaStream_t stream);
 
 }  // namespace kvca
