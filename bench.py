@@ -40,14 +40,24 @@ sys.path.insert(0, str(REPO))
 import torch  # noqa: E402
 
 WORKLOADS = {
-    "llama70b-shard": dict(layers=80, heads=1, head_dim=128, block_size=16, dtype=torch.bfloat16,
+    "llama70b-shard": dict(layers=80, kv=2, heads=1, head_dim=128, block_size=16, dtype=torch.bfloat16,
                            seqs=16, seq_tokens=32768, chunk_tokens=256,
                            label="Llama-3-70B KV-head shard: 80 layers x K/V, 1 KV head/GPU, head_dim 128, "
                                  "block 16, bf16, 16 x 32k-token sequences (32,768 blocks/GPU), 256-token chunks"),
-    "llama8b": dict(layers=32, heads=8, head_dim=128, block_size=16, dtype=torch.float16,
+    "llama8b": dict(layers=32, kv=2, heads=8, head_dim=128, block_size=16, dtype=torch.float16,
                     seqs=64, seq_tokens=256, chunk_tokens=256,
                     label="Llama-3-8B cache: 32 layers x K/V, 8 KV heads, head_dim 128, block 16, fp16, "
                           "1024 blocks/layer, 64 requests x 256 tokens"),
+    "mla-layer-shard": dict(layers=8, kv=1, heads=1, head_dim=576, block_size=64, dtype=torch.bfloat16,
+                            seqs=1, seq_tokens=131072, chunk_tokens=256,
+                            label="MLA latent cache, one GPU's layer range (8 of 61 layers): one 576-wide "
+                                  "row (512 + 64 rope) per token, block 64, bf16, 128k-token context "
+                                  "(2,048 blocks), 256-token chunks"),
+    "mla-layer-shard-fp8": dict(layers=8, kv=1, heads=1, head_dim=576, block_size=64,
+                                dtype=torch.float8_e4m3fn, seqs=1, seq_tokens=131072, chunk_tokens=256,
+                                label="MLA latent cache, fp8-e4m3 byte view: one GPU's layer range (8 of 61 "
+                                      "layers), 576 bytes per token, block 64, 128k-token context, "
+                                      "256-token chunks"),
 }
 
 CPU_SAMPLE_BLOCKS = 2048  # blocks per plane in the bounded CPU sample
@@ -183,21 +193,27 @@ def build_cache(w: dict, device, seed: int, num_blocks: int | None = None):
     """Planes ordered K of every layer, then V of every layer (KV_2LTD chunks),
     as views of one (layers, 2, num_blocks, block, heads, head_dim) tensor."""
     nb = num_blocks or (w["seqs"] * w["seq_tokens"] // w["block_size"])
-    kv = torch.empty((w["layers"], 2, nb, w["block_size"], w["heads"], w["head_dim"]),
-                     dtype=w["dtype"], device=device)
-    if device.type == "cuda":
-        gen = torch.Generator(device=device).manual_seed(seed)
-        kv.normal_(generator=gen)
+    shape = (w["layers"], w["kv"], nb, w["block_size"], w["heads"], w["head_dim"])
+    gen = torch.Generator(device=device).manual_seed(seed) if device.type == "cuda" else \
+        torch.Generator().manual_seed(seed)
+    if w["dtype"] == torch.float8_e4m3fn:  # moved as raw bytes
+        kv = torch.empty(shape, dtype=torch.uint8, device=device)
+        kv.random_(0, 256, generator=gen)
+        kv = kv.view(torch.float8_e4m3fn)
     else:
-        gen = torch.Generator().manual_seed(seed)
+        kv = torch.empty(shape, dtype=w["dtype"], device=device)
         kv.normal_(generator=gen)
-    planes = [kv[l, 0] for l in range(w["layers"])] + [kv[l, 1] for l in range(w["layers"])]
+    planes = [kv[l, h] for h in range(w["kv"]) for l in range(w["layers"])]
     table = torch.randperm(nb, generator=torch.Generator().manual_seed(seed))
     return kv, planes, table, nb
 
 
+def _dtype_name(dt) -> str:
+    return {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float8_e4m3fn: "fp8-e4m3 (bytes)"}.get(dt, str(dt))
+
+
 def block_bytes(w: dict) -> int:
-    return w["block_size"] * w["heads"] * w["head_dim"] * torch.tensor([], dtype=w["dtype"]).element_size()
+    return w["block_size"] * w["heads"] * w["head_dim"] * torch.empty(0, dtype=w["dtype"]).element_size()
 
 
 # ---------------------------------------------------------------------------
@@ -213,6 +229,7 @@ def cpu_moves(w: dict, steps: int, warmup: int) -> dict:
     cb = w["chunk_tokens"] // w["block_size"]
     nb = min(CPU_SAMPLE_BLOCKS, w["seqs"] * w["seq_tokens"] // w["block_size"])
     _, planes, table, nb = build_cache(w, torch.device("cpu"), 1234, num_blocks=nb)
+    planes = [p.view(torch.uint8) if p.dtype == torch.float8_e4m3fn else p for p in planes]
     payload = len(planes) * nb * block_bytes(w)
     times = []
     for i in range(warmup + steps):
@@ -308,7 +325,7 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     # correctness guard on the bench data: chunk 0 holds the first cb blocks
     # of the table for plane 0 and the last plane
     for p in (0, P - 1):
-        assert torch.equal(chunks[0, p].view(torch.int16), planes[p][table[:cb]].view(torch.int16))
+        assert torch.equal(chunks[0, p].view(torch.uint8), planes[p][table[:cb]].view(torch.uint8))
 
     # ---- device-timed region ------------------------------------------------
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
@@ -374,7 +391,7 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16" if w["dtype"] == torch.bfloat16 else "fp16",
+        "dtype": _dtype_name(w["dtype"]),
         "data": "synthetic (seeded N(0,1) cache, seeded random block tables)",
         "config": {
             "workload": w["label"],
@@ -428,6 +445,77 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     print(json.dumps(line), flush=True)
 
 
+DECODE_STEPS_PER_BENCH_STEP = 50
+
+
+def run_decode_mix(args, world: int, rank: int, device) -> None:
+    """Decode append + gather mix: 256 sequences append one token per decode
+    step into a full 65,536-block pool (reshape-and-cache through a per-token
+    slot_mapping); sequences whose block fills up get a new one from the clock
+    sweep, whose victims are gathered to a spill chunk first.  One bench step
+    = 50 decode steps, so the default 20 timed bench steps are 1,000 decode
+    steps."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+    from kv_cache_adapter_b200.workloads import DecodeMix
+
+    per = DECODE_STEPS_PER_BENCH_STEP
+    heads = args.heads or 1
+    mix = DecodeMix(ops, device, layers=32, heads=heads, head_dim=128, block_size=16, num_blocks=65536,
+                    seqs=256, dtype=torch.float16, seed=1234 + rank,
+                    max_steps=(args.warmup + args.steps) * per + 32)
+    rows = torch.randn((1, mix.num_planes, mix.seqs, *mix.row_shape), dtype=torch.float16, device=device)
+    for _ in range(args.warmup * per):
+        mix.step(rows)
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    tok0, blk0 = mix.tokens, mix.gathered_blocks
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device.index) as clocks:
+        start.record()
+        for _ in range(args.steps * per):
+            mix.step(rows)
+        end.record()
+        torch.cuda.synchronize(device)
+    _barrier(world)
+    ops.check_status(device)
+    ms = _max_over_ranks(start.elapsed_time(end), world, device)
+    tokens, blocks = mix.tokens - tok0, mix.gathered_blocks - blk0
+    row_bytes = heads * 128 * 2
+    moved = 2 * mix.num_planes * (tokens * row_bytes + blocks * row_bytes * mix.block_size)
+    if rank != 0:
+        return
+    decode_steps = args.steps * per
+    line = {
+        "metric": "paged-KV decode append + eviction gather GB/s",
+        "value": round(world * moved / (ms / 1e3) / 1e9, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "ms_per_decode_step": round(ms / decode_steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) cache and token rows, seeded pool state)",
+        "config": {
+            "workload": f"decode append + gather mix: 32 layers x K/V, {heads} KV head(s)/GPU, head_dim 128, "
+                        f"block 16, fp16, full 65,536-block pool, 256 sequences x 1 token per decode step, "
+                        f"{per} decode steps per bench step, clock eviction + spill gather when a block fills",
+            "parallelism": f"kv-head shard x{world}, no data-path collective",
+        },
+        "tokens_per_s": round(world * tokens / (ms / 1e3), 1),
+        "evictions_per_s": round(world * blocks / (ms / 1e3), 1),
+        "gpu_launches_per_decode_step": "1 scatter; plus pop, gather, commit, release on steps that evict",
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, w: dict, world: int, rank: int) -> None:
     if rank != 0:
         return
@@ -443,7 +531,7 @@ def run_reference(args, w: dict, world: int, rank: int) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16" if w["dtype"] == torch.bfloat16 else "fp16",
+        "dtype": _dtype_name(w["dtype"]),
         "data": "synthetic (seeded N(0,1) cache, seeded random block tables)",
         "config": {"workload": w["label"], "sample": cpu["sample"]},
         "cpu_baseline": cpu,
@@ -458,7 +546,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama70b-shard")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix"], default="llama70b-shard")
+    ap.add_argument("--heads", type=int, default=None, help="KV heads per GPU for the decode mix (default 1)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="override the number of sequences (smaller cases for profiling)")
     ap.add_argument("--no-clock", action="store_true")
@@ -466,7 +555,7 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    w = dict(WORKLOADS[args.workload])
+    w = dict(WORKLOADS.get(args.workload, WORKLOADS["llama8b"]))
     if args.seqs is not None:
         w["seqs"] = args.seqs
         w["label"] += f" [reduced to {args.seqs} sequences]"
@@ -486,7 +575,10 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=device)
     try:
-        run_ours(args, w, world, rank, device)
+        if args.workload == "decode-mix":
+            run_decode_mix(args, world, rank, device)
+        else:
+            run_ours(args, w, world, rank, device)
     finally:
         if world > 1:
             import torch.distributed as dist

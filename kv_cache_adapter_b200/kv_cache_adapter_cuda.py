@@ -210,13 +210,15 @@ def _bitmap(dev: torch.device, num_slots: int) -> torch.Tensor:
 
 def pop_reusable_slots(slot_meta: torch.Tensor, search_start: torch.Tensor,
                        blocked_slot_ids: torch.Tensor, count: int, *,
-                       order: str | None = None) -> torch.Tensor:
+                       order: str | None = None, check: bool = True) -> torch.Tensor:
     """Clock sweep; ages ``slot_meta`` and advances ``search_start`` in place.
 
     ``order="grouped"`` (default) follows the reference's strict path
     (adapter.py:472-525); ``order="prefix"`` the reference CUDA kernel's
     selection (kv_adapter_cuda.cu:101-231).  Raises InsufficientCapacityError
     when fewer than ``count`` slots are reusable, before changing anything.
+    ``check=False`` skips the synchronising status read (a caller that knows
+    the pool has room, or checks later with ``check_status``).
     """
     _require(slot_meta, _META_DTYPES, "slot_meta")
     _require(search_start, torch.int64, "search_start")
@@ -241,7 +243,8 @@ def pop_reusable_slots(slot_meta: torch.Tensor, search_start: torch.Tensor,
             _ptr(blocked_slot_ids), blocked_slot_ids.numel(), count, _ptr(out),
             _ptr(_bitmap(dev, n)), _ptr(_status(dev)), _stream(dev))
     _host_rc(rc, "pop_reusable_slots")
-    check_status(dev, "pop_reusable_slots")
+    if check:
+        check_status(dev, "pop_reusable_slots")
     return out
 
 

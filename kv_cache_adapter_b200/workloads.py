@@ -170,3 +170,112 @@ def zipf_reaccess(params: dict) -> torch.Tensor:
 
 def sha256_of(t: torch.Tensor) -> str:
     return hashlib.sha256(t.detach().cpu().contiguous().numpy().tobytes()).hexdigest()
+
+
+# ---------------------------------------------------------------------------
+# Decode append + gather mix (reshape-and-cache with clock eviction)
+# ---------------------------------------------------------------------------
+
+
+class DecodeMix:
+    """A paged KV pool serving `seqs` decoding sequences, one token each per step.
+
+    The pool (``num_blocks`` blocks of ``block_size`` tokens, every block of
+    every plane = layer x K/V) starts full: every block holds a resident
+    logical block, unpinned, usage uniform in 0..3.  Each sequence owns one
+    pinned block it is filling (seeded random fill positions, so sequences
+    fill up on different steps).  One step:
+
+      1. every sequence whose block is full gets a new one: the clock sweep
+         pops that many victims (the pool is full, so each one evicts its
+         logical block), the victims' bytes of every plane are gathered into
+         a spill chunk (the copy an LMCache-style store would take), the new
+         blocks are committed as freshly saved and pinned (pin 1, usage 1)
+         and the full blocks are released (pin 1 -> 0);
+      2. one token per sequence is scattered into every plane through the
+         per-token slot_mapping = block * block_size + position.
+
+    ``ops`` supplies pop_reusable_slots, gather_layers, commit_save_metadata,
+    release_metadata and scatter_tokens (the CUDA module, or a CPU stand-in in
+    the tests).  Host-side control (which sequences need a block) never reads
+    device memory.
+    """
+
+    def __init__(self, ops, device, *, layers: int = 32, heads: int = 1, head_dim: int = 128,
+                 block_size: int = 16, num_blocks: int = 65536, seqs: int = 256,
+                 dtype=torch.float16, seed: int = 1234, max_steps: int = 1000):
+        self.ops = ops
+        self.device = device
+        self.layers, self.block_size, self.seqs = layers, block_size, seqs
+        self.num_blocks = num_blocks
+        gen_dev = torch.Generator(device=device).manual_seed(seed) if device.type == "cuda" else \
+            torch.Generator().manual_seed(seed)
+        self.kv = torch.empty((layers, 2, num_blocks, block_size, heads, head_dim), dtype=dtype, device=device)
+        self.kv.normal_(generator=gen_dev)
+        self.block_planes = [self.kv[l, 0] for l in range(layers)] + [self.kv[l, 1] for l in range(layers)]
+        self.token_planes = [p.reshape(num_blocks, block_size, heads * head_dim) for p in self.block_planes]
+        self.num_planes = len(self.block_planes)
+        self.row_shape = (heads * head_dim,)
+        rng = np.random.default_rng(seed)
+        # logical ids: the resident ones, then fresh ids for new blocks
+        self.num_logical = num_blocks + seqs * (max_steps // block_size + 2)
+        resident = rng.permutation(num_blocks).astype(np.int64)  # logical id of each slot
+        l2p = np.full(self.num_logical, -1, np.int64)
+        l2p[resident] = np.arange(num_blocks)
+        usage = rng.integers(0, 4, num_blocks)
+        pins = np.zeros(num_blocks, np.int64)
+        cur_block = rng.choice(num_blocks, seqs, replace=False).astype(np.int64)
+        pins[cur_block] = 1
+        self.cur_logical = resident[cur_block].copy()
+        self.pos = rng.integers(0, block_size, seqs).astype(np.int64)
+        meta = (pins & 15) | ((usage & 15) << 4)
+        self.slot_meta = torch.tensor(meta.astype(np.uint8), device=device)
+        self.l2p = torch.tensor(l2p, device=device)
+        self.p2l = torch.tensor(resident, device=device)
+        self.search_start = torch.zeros(1, dtype=torch.int64, device=device)
+        self.next_logical = num_blocks
+        # device copies (never aliases of the host arrays, also on the CPU)
+        self.cur_block_dev = torch.tensor(cur_block, device=device)
+        self.pos_dev = torch.tensor(self.pos, device=device)
+        self.spill = torch.empty((seqs, self.num_planes, 1, block_size, heads, head_dim), dtype=dtype,
+                                 device=device)
+        self.empty_ids = torch.empty(0, dtype=torch.int64, device=device)
+        self.evictions = 0
+        self.tokens = 0
+        self.gathered_blocks = 0
+
+    def need_new_blocks(self) -> np.ndarray:
+        return np.nonzero(self.pos == self.block_size)[0]
+
+    def step(self, token_rows: torch.Tensor, *, check: bool = False):
+        """token_rows: (1, num_planes, seqs, *row) chunk of this step's tokens.
+        Returns the spill chunk of the blocks evicted this step (a view)."""
+        need = self.need_new_blocks()
+        c = int(need.size)
+        spill = self.spill[:c]
+        if c:
+            ops = self.ops
+            need_dev = torch.tensor(need, device=self.device)
+            victims = ops.pop_reusable_slots(self.slot_meta, self.search_start, self.empty_ids, c, check=check)
+            evicted = self.p2l.index_select(0, victims)
+            ops.gather_layers(self.block_planes, victims, spill, blocks_per_chunk=1, check=check)
+            new_ids = torch.arange(self.next_logical, self.next_logical + c, dtype=torch.int64, device=self.device)
+            self.next_logical += c
+            ones = torch.ones(c, dtype=torch.uint8, device=self.device)
+            ops.commit_save_metadata(self.l2p, self.p2l, self.slot_meta, evicted, new_ids, victims, ones, ones,
+                                     check=check)
+            old_ids = torch.tensor(self.cur_logical[need], device=self.device)
+            ops.release_metadata(self.l2p, self.slot_meta, old_ids, check=check)
+            self.cur_block_dev.index_copy_(0, need_dev, victims)
+            self.cur_logical[need] = np.arange(self.next_logical - c, self.next_logical)
+            self.pos[need] = 0
+            self.pos_dev.index_fill_(0, need_dev, 0)
+            self.evictions += c
+            self.gathered_blocks += c
+        slot_mapping = self.cur_block_dev * self.block_size + self.pos_dev
+        self.ops.scatter_tokens(self.token_planes, slot_mapping, token_rows, tokens_per_chunk=self.seqs,
+                                check=check)
+        self.pos += 1
+        self.pos_dev += 1
+        self.tokens += self.seqs
+        return spill

@@ -37,7 +37,7 @@ class OracleOps:
         self.calls.append("inspect_save_requests")
         return list(_translate(oracle.inspect_save_requests, l2p, slot_meta, ids))
 
-    def pop_reusable_slots(self, slot_meta, search_start, blocked, count, order=None):
+    def pop_reusable_slots(self, slot_meta, search_start, blocked, count, order=None, check=True):
         self.calls.append("pop_reusable_slots")
         return _translate(oracle.pop_reusable_slots, slot_meta, search_start, blocked, count,
                           order=order or "grouped")
@@ -65,3 +65,27 @@ class OracleOps:
     def copy_blocks(self, src, src_ids, dst, dst_ids, check=None):
         self.calls.append("copy_blocks")
         moves.copy_blocks(src, src_ids, dst, dst_ids)
+
+    def gather_layers(self, caches, slot_ids, out=None, blocks_per_chunk=None, check=None):
+        self.calls.append("gather_layers")
+        got = moves.gather_layers(list(caches), slot_ids, blocks_per_chunk=blocks_per_chunk)
+        if out is None:
+            return got
+        out.copy_(got)
+        return out
+
+    def scatter_layers(self, caches, slot_ids, chunks, blocks_per_chunk=None, check=None):
+        self.calls.append("scatter_layers")
+        moves.scatter_layers(list(caches), slot_ids, chunks, blocks_per_chunk=blocks_per_chunk)
+
+    def gather_tokens(self, caches, slot_mapping, out=None, tokens_per_chunk=None, check=None):
+        self.calls.append("gather_tokens")
+        got = moves.gather_tokens(list(caches), slot_mapping, tokens_per_chunk=tokens_per_chunk)
+        if out is None:
+            return got
+        out.copy_(got)
+        return out
+
+    def scatter_tokens(self, caches, slot_mapping, chunks, tokens_per_chunk=None, check=None):
+        self.calls.append("scatter_tokens")
+        moves.scatter_tokens(list(caches), slot_mapping, chunks, tokens_per_chunk=tokens_per_chunk)

@@ -1,0 +1,62 @@
+"""The decode append + gather mix (reshape-and-cache with clock eviction).
+
+CPU: the driver's host logic through the oracle op set.
+GPU: the same driver on the CUDA op set against the oracle, step by step:
+spilled blocks, the whole cache, slot_meta, l2p / p2l and search_start must
+be identical bytes after every step.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from kv_cache_adapter_b200.workloads import DecodeMix
+from oracle_ops import OracleOps
+
+SMALL = dict(layers=2, heads=2, head_dim=32, block_size=16, num_blocks=256, seqs=48, max_steps=200)
+
+
+def _rows(step: int, mix: DecodeMix) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(10_000 + step)
+    return torch.randn((1, mix.num_planes, mix.seqs, *mix.row_shape), generator=gen).to(mix.kv.dtype)
+
+
+def test_decode_mix_host_logic_on_cpu():
+    ops = OracleOps()
+    mix = DecodeMix(ops, torch.device("cpu"), **SMALL)
+    pins0 = int(((mix.slot_meta & 15) != 0).sum())
+    assert pins0 == SMALL["seqs"]
+    total_new = 0
+    for step in range(120):
+        need = mix.need_new_blocks().size
+        spill = mix.step(_rows(step, mix))
+        assert spill.shape[0] == need
+        total_new += need
+        # one pinned block per sequence, all of them distinct
+        pinned = torch.nonzero((mix.slot_meta & 15) != 0).flatten().sort().values
+        assert torch.equal(pinned, mix.cur_block_dev.sort().values)
+        # l2p and p2l stay inverse on the resident blocks
+        assert torch.equal(mix.l2p[mix.p2l], torch.arange(mix.num_blocks))
+    assert total_new == mix.evictions > 0
+    assert mix.tokens == 120 * SMALL["seqs"]
+
+
+@pytest.mark.gpu
+def test_decode_mix_matches_oracle_step_by_step():
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as cuda_ops
+
+    dev = torch.device("cuda", 0)
+    gpu = DecodeMix(cuda_ops, dev, **SMALL)
+    cpu = DecodeMix(OracleOps(), torch.device("cpu"), **SMALL)
+    cpu.kv.copy_(gpu.kv.cpu())
+    for step in range(150):
+        rows = _rows(step, cpu)
+        spill_g = gpu.step(rows.to(dev), check=True)
+        spill_c = cpu.step(rows)
+        assert torch.equal(spill_g.cpu().view(torch.int16), spill_c.view(torch.int16)), step
+        assert torch.equal(gpu.slot_meta.cpu(), cpu.slot_meta), step
+        assert torch.equal(gpu.l2p.cpu(), cpu.l2p) and torch.equal(gpu.p2l.cpu(), cpu.p2l), step
+        assert int(gpu.search_start[0]) == int(cpu.search_start[0]), step
+    assert torch.equal(gpu.kv.cpu().view(torch.int16), cpu.kv.view(torch.int16))
+    assert gpu.evictions == cpu.evictions > 100
