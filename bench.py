@@ -460,34 +460,48 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
 
     per = DECODE_STEPS_PER_BENCH_STEP
     heads = args.heads or 1
+    cycles = -(-args.steps * per // 16)  # timed decode steps, rounded up to whole 16-step cycles
     mix = DecodeMix(ops, device, layers=32, heads=heads, head_dim=128, block_size=16, num_blocks=65536,
                     seqs=256, dtype=torch.float16, seed=1234 + rank,
-                    max_steps=(args.warmup + args.steps) * per + 32)
+                    max_steps=(args.warmup * per + 17) + 2 * cycles * 16 + 64)
     rows = torch.randn((1, mix.num_planes, mix.seqs, *mix.row_shape), dtype=torch.float16, device=device)
-    for _ in range(args.warmup * per):
+    # warm-up: eager steps (at least one full cycle), aligned to the start of a cycle
+    warm = max(args.warmup * per, 17)
+    warm += (1 - warm) % 16
+    for _ in range(warm):
         mix.step(rows)
     torch.cuda.synchronize(device)
     ops.check_status(device)
-    tok0, blk0 = mix.tokens, mix.gathered_blocks
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    _barrier(world)
-    torch.cuda.synchronize(device)
-    with ClockSampler(device.index) as clocks:
+
+    def timed(run) -> float:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        torch.cuda.synchronize(device)
         start.record()
-        for _ in range(args.steps * per):
-            mix.step(rows)
+        run()
         end.record()
         torch.cuda.synchronize(device)
-    _barrier(world)
-    ops.check_status(device)
-    ms = _max_over_ranks(start.elapsed_time(end), world, device)
-    tokens, blocks = mix.tokens - tok0, mix.gathered_blocks - blk0
+        _barrier(world)
+        ops.check_status(device)
+        return _max_over_ranks(start.elapsed_time(end), world, device)
+
+    # host-issued: one Python call per op
+    tok0, blk0 = mix.tokens, mix.gathered_blocks
+    eager_ms = timed(lambda: [mix.step(rows) for _ in range(cycles * 16)])
+    eager_tokens, eager_blocks = mix.tokens - tok0, mix.gathered_blocks - blk0
+    # graph-captured: one replay per 16-step cycle
+    graph, per_cycle = mix.capture_cycle(rows)
+    with ClockSampler(device.index) as clocks:
+        ms = timed(lambda: [graph.replay() for _ in range(cycles)])
+    tokens, blocks = cycles * 16 * mix.seqs, cycles * per_cycle
+    assert (tokens, blocks) == (eager_tokens, eager_blocks)
     row_bytes = heads * 128 * 2
     moved = 2 * mix.num_planes * (tokens * row_bytes + blocks * row_bytes * mix.block_size)
+    del graph
     if rank != 0:
         return
-    decode_steps = args.steps * per
+    decode_steps = cycles * 16
     line = {
         "metric": "paged-KV decode append + eviction gather GB/s",
         "value": round(world * moved / (ms / 1e3) / 1e9, 2),
@@ -497,6 +511,7 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 4),
         "ms_per_decode_step": round(ms / decode_steps, 5),
+        "decode_steps_timed": decode_steps,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -505,12 +520,16 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         "config": {
             "workload": f"decode append + gather mix: 32 layers x K/V, {heads} KV head(s)/GPU, head_dim 128, "
                         f"block 16, fp16, full 65,536-block pool, 256 sequences x 1 token per decode step, "
-                        f"{per} decode steps per bench step, clock eviction + spill gather when a block fills",
+                        f"{per} decode steps per bench step (timed in whole 16-step cycles), clock eviction + "
+                        f"spill gather when a block fills",
             "parallelism": f"kv-head shard x{world}, no data-path collective",
         },
         "tokens_per_s": round(world * tokens / (ms / 1e3), 1),
         "evictions_per_s": round(world * blocks / (ms / 1e3), 1),
         "gpu_launches_per_decode_step": "1 scatter; plus pop, gather, commit, release on steps that evict",
+        "issue": "CUDA graph, one replay per 16-step cycle",
+        "host_issued": {"value": round(world * moved / (eager_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                        "ms_per_decode_step": round(eager_ms / decode_steps, 5)},
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

@@ -197,8 +197,10 @@ class DecodeMix:
 
     ``ops`` supplies pop_reusable_slots, gather_layers, commit_save_metadata,
     release_metadata and scatter_tokens (the CUDA module, or a CPU stand-in in
-    the tests).  Host-side control (which sequences need a block) never reads
-    device memory.
+    the tests).  All per-step state lives on the device; the host only keeps
+    the fill positions, which decide which sequences need a block, so steps
+    issue no host<->device traffic and a whole cycle of ``block_size`` steps
+    can be captured in a CUDA graph (``capture_cycle``).
     """
 
     def __init__(self, ops, device, *, layers: int = 32, heads: int = 1, head_dim: int = 128,
@@ -214,6 +216,9 @@ class DecodeMix:
         self.kv.normal_(generator=gen_dev)
         self.block_planes = [self.kv[l, 0] for l in range(layers)] + [self.kv[l, 1] for l in range(layers)]
         self.token_planes = [p.reshape(num_blocks, block_size, heads * head_dim) for p in self.block_planes]
+        table = getattr(ops, "PlaneTable", None)
+        self.block_table = table(self.block_planes, 1) if table else self.block_planes
+        self.token_table = table(self.token_planes, 2) if table else self.token_planes
         self.num_planes = len(self.block_planes)
         self.row_shape = (heads * head_dim,)
         rng = np.random.default_rng(seed)
@@ -226,26 +231,37 @@ class DecodeMix:
         pins = np.zeros(num_blocks, np.int64)
         cur_block = rng.choice(num_blocks, seqs, replace=False).astype(np.int64)
         pins[cur_block] = 1
-        self.cur_logical = resident[cur_block].copy()
         self.pos = rng.integers(0, block_size, seqs).astype(np.int64)
         meta = (pins & 15) | ((usage & 15) << 4)
         self.slot_meta = torch.tensor(meta.astype(np.uint8), device=device)
         self.l2p = torch.tensor(l2p, device=device)
         self.p2l = torch.tensor(resident, device=device)
         self.search_start = torch.zeros(1, dtype=torch.int64, device=device)
-        self.next_logical = num_blocks
         # device copies (never aliases of the host arrays, also on the CPU)
         self.cur_block_dev = torch.tensor(cur_block, device=device)
+        self.cur_logical_dev = torch.tensor(resident[cur_block], device=device)
         self.pos_dev = torch.tensor(self.pos, device=device)
+        self.next_logical_dev = torch.tensor([num_blocks], dtype=torch.int64, device=device)
         self.spill = torch.empty((seqs, self.num_planes, 1, block_size, heads, head_dim), dtype=dtype,
                                  device=device)
         self.empty_ids = torch.empty(0, dtype=torch.int64, device=device)
+        self._need = {}  # need set (bytes) -> (index tensor, ones, arange) on the device
         self.evictions = 0
         self.tokens = 0
         self.gathered_blocks = 0
 
     def need_new_blocks(self) -> np.ndarray:
         return np.nonzero(self.pos == self.block_size)[0]
+
+    def _need_tensors(self, need: np.ndarray):
+        key = need.tobytes()
+        got = self._need.get(key)
+        if got is None:
+            c = int(need.size)
+            got = (torch.tensor(need, device=self.device), torch.ones(c, dtype=torch.uint8, device=self.device),
+                   torch.arange(c, dtype=torch.int64, device=self.device))
+            self._need[key] = got
+        return got
 
     def step(self, token_rows: torch.Tensor, *, check: bool = False):
         """token_rows: (1, num_planes, seqs, *row) chunk of this step's tokens.
@@ -255,27 +271,48 @@ class DecodeMix:
         spill = self.spill[:c]
         if c:
             ops = self.ops
-            need_dev = torch.tensor(need, device=self.device)
+            need_dev, ones, offsets = self._need_tensors(need)
             victims = ops.pop_reusable_slots(self.slot_meta, self.search_start, self.empty_ids, c, check=check)
             evicted = self.p2l.index_select(0, victims)
-            ops.gather_layers(self.block_planes, victims, spill, blocks_per_chunk=1, check=check)
-            new_ids = torch.arange(self.next_logical, self.next_logical + c, dtype=torch.int64, device=self.device)
-            self.next_logical += c
-            ones = torch.ones(c, dtype=torch.uint8, device=self.device)
+            ops.gather_layers(self.block_table, victims, spill, blocks_per_chunk=1, check=check)
+            new_ids = self.next_logical_dev + offsets
+            self.next_logical_dev += c
             ops.commit_save_metadata(self.l2p, self.p2l, self.slot_meta, evicted, new_ids, victims, ones, ones,
                                      check=check)
-            old_ids = torch.tensor(self.cur_logical[need], device=self.device)
-            ops.release_metadata(self.l2p, self.slot_meta, old_ids, check=check)
+            ops.release_metadata(self.l2p, self.slot_meta, self.cur_logical_dev.index_select(0, need_dev),
+                                 check=check)
             self.cur_block_dev.index_copy_(0, need_dev, victims)
-            self.cur_logical[need] = np.arange(self.next_logical - c, self.next_logical)
+            self.cur_logical_dev.index_copy_(0, need_dev, new_ids)
             self.pos[need] = 0
             self.pos_dev.index_fill_(0, need_dev, 0)
             self.evictions += c
             self.gathered_blocks += c
         slot_mapping = self.cur_block_dev * self.block_size + self.pos_dev
-        self.ops.scatter_tokens(self.token_planes, slot_mapping, token_rows, tokens_per_chunk=self.seqs,
+        self.ops.scatter_tokens(self.token_table, slot_mapping, token_rows, tokens_per_chunk=self.seqs,
                                 check=check)
         self.pos += 1
         self.pos_dev += 1
         self.tokens += self.seqs
         return spill
+
+    def capture_cycle(self, token_rows: torch.Tensor):
+        """Capture the next ``block_size`` steps (one full cycle of the fill
+        positions, after which the schedule repeats) into a CUDA graph and
+        return (graph, evictions per replay).  Every need set of the cycle
+        must have been seen in eager steps before (their index tensors are
+        made outside the capture), so run at least one cycle eagerly first;
+        replaying the graph then advances the device state by one cycle."""
+        counters = (self.evictions, self.tokens, self.gathered_blocks)
+        pos = self.pos.copy()
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(self.block_size):
+                    self.step(token_rows, check=False)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        per_replay = self.evictions - counters[0]
+        self.evictions, self.tokens, self.gathered_blocks = counters
+        assert np.array_equal(self.pos, pos)  # a full cycle: the schedule repeats
+        return graph, per_replay

@@ -60,3 +60,32 @@ def test_decode_mix_matches_oracle_step_by_step():
         assert int(gpu.search_start[0]) == int(cpu.search_start[0]), step
     assert torch.equal(gpu.kv.cpu().view(torch.int16), cpu.kv.view(torch.int16))
     assert gpu.evictions == cpu.evictions > 100
+
+
+@pytest.mark.gpu
+def test_decode_mix_graph_replay_matches_eager():
+    """A captured cycle of block_size steps, replayed, leaves exactly the state
+    that running the same steps eagerly leaves."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as cuda_ops
+
+    dev = torch.device("cuda", 0)
+    eager = DecodeMix(cuda_ops, dev, **SMALL)
+    graphed = DecodeMix(cuda_ops, dev, **SMALL)
+    rows = _rows(0, eager).to(dev)
+    for _ in range(SMALL["block_size"] + 1):  # one full cycle eagerly, then step 1 of the next
+        eager.step(rows)
+        graphed.step(rows)
+    graph, per_cycle = graphed.capture_cycle(rows)
+    assert per_cycle == SMALL["seqs"]
+    for _ in range(5):
+        for _ in range(SMALL["block_size"]):
+            eager.step(rows)
+        graph.replay()
+    torch.cuda.synchronize()
+    cuda_ops.check_status(dev)
+    assert torch.equal(eager.kv.view(torch.int16), graphed.kv.view(torch.int16))
+    assert torch.equal(eager.slot_meta, graphed.slot_meta)
+    assert torch.equal(eager.l2p, graphed.l2p) and torch.equal(eager.p2l, graphed.p2l)
+    assert torch.equal(eager.search_start, graphed.search_start)
+    assert torch.equal(eager.cur_block_dev, graphed.cur_block_dev)
+    assert torch.equal(eager.next_logical_dev, graphed.next_logical_dev)
