@@ -535,6 +535,114 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     print(json.dumps(line), flush=True)
 
 
+ADAPTER_CONFIG = dict(num_actual=256, num_logical=1024, batch=32, block=128, hit_rates=(0.0, 0.5, 1.0))
+
+
+def _adapter_case(device, ops=None, backend_ops=None):
+    from kv_cache_adapter_b200 import InMemoryBlockStoreBackend, KVCacheAdapter
+
+    c = ADAPTER_CONFIG
+    payloads = torch.arange(c["num_logical"] * c["block"], dtype=torch.float32, device=device)
+    backend = InMemoryBlockStoreBackend(payloads.reshape(c["num_logical"], c["block"]), ops=backend_ops)
+    actual = torch.zeros((c["num_actual"], c["block"]), dtype=torch.float32, device=device)
+    return KVCacheAdapter(c["num_actual"], c["num_logical"], actual, backend, native_ext=ops)
+
+
+def _sample_ids(ad, rng: "np.random.Generator", hit_rate: float) -> torch.Tensor:
+    """Seeded batch: `hit_rate` of it resident unpinned logical ids, the rest
+    non-resident ones, in random order (reads the adapter state on the host)."""
+    import numpy as np
+
+    c = ADAPTER_CONFIG
+    p2l = ad._physical_to_logical.cpu().numpy()
+    pins = (ad._slot_meta.cpu().numpy().astype(np.int64) & 15)
+    resident = p2l[(p2l >= 0) & (pins == 0)]
+    cold = np.setdiff1d(np.arange(c["num_logical"]), p2l[p2l >= 0])
+    hits = int(round(c["batch"] * hit_rate))
+    ids = np.concatenate([rng.permutation(resident)[:hits], rng.permutation(cold)[: c["batch"] - hits]])
+    return torch.tensor(rng.permutation(ids), dtype=torch.int64, device=ad.actual_blocks.device)
+
+
+def _time_adapter(ad, device, steps: int, warmup: int) -> list[dict]:
+    import numpy as np
+
+    def sync():
+        if device.type == "cuda":
+            torch.cuda.synchronize(device)
+
+    c = ADAPTER_CONFIG
+    rng = np.random.default_rng(1234)
+    initial = torch.arange(c["num_actual"], dtype=torch.int64, device=device)
+    ad.load(initial)
+    ad.release(initial)
+    out = []
+    for hr in c["hit_rates"]:
+        load_s = save_s = 0.0
+        for i in range(warmup + steps):
+            ids = _sample_ids(ad, rng, hr)
+            sync()
+            t0 = time.perf_counter()
+            ad.load(ids)
+            sync()
+            t1 = time.perf_counter()
+            ad.release(ids)
+            ids = _sample_ids(ad, rng, hr)
+            data = torch.tensor(rng.standard_normal((c["batch"], c["block"])), dtype=torch.float32, device=device)
+            sync()
+            t2 = time.perf_counter()
+            ad.save(ids, data)
+            sync()
+            t3 = time.perf_counter()
+            if i >= warmup:
+                load_s += t1 - t0
+                save_s += t3 - t2
+        out.append({"hit_rate": hr, "load_ms": round(load_s * 1e3 / steps, 4), "save_ms": round(save_s * 1e3 / steps, 4)})
+    return out
+
+
+def run_adapter(args, world: int, rank: int, device) -> None:
+    """KVCacheAdapter.load / save per call on the configuration of the
+    reference's runtime-path benchmark (256 physical / 1,024 logical blocks,
+    batch 32, 128-float blocks, in-memory backend on the device)."""
+    steps = max(args.steps, 20)
+    cuda = _time_adapter(_adapter_case(device), device, steps, args.warmup)
+    stepwise_ad = _adapter_case(device)
+    stepwise_ad._planned = False  # inspect, pop, commit as separate launches
+    stepwise = _time_adapter(stepwise_ad, device, steps, args.warmup)
+    if rank != 0:
+        return
+    calls = sum(2 for _ in cuda) * steps
+    total_ms = sum((r["load_ms"] + r["save_ms"]) * steps for r in cuda)
+    line = {
+        "metric": "KVCacheAdapter load+save calls/s",
+        "value": round(world * calls / (total_ms / 1e3), 1),
+        "unit": "calls/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic (seeded batches at fixed hit rates)",
+        "config": {"workload": "adapter load/save: 256 physical / 1,024 logical blocks, batch 32, "
+                               "128 x fp32 blocks, in-memory backend on the device, hit rates 0 / 0.5 / 1",
+                   "timing": "host clock around each call, synchronised before and after"},
+        "per_hit_rate": cuda,
+        "per_hit_rate_stepwise": stepwise,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "tests"))
+        from oracle_ops import OracleOps
+
+        ops = OracleOps()
+        cpu = _time_adapter(_adapter_case(torch.device("cpu"), ops, ops), torch.device("cpu"), steps, args.warmup)
+        line["cpu_baseline"] = {"kind": "port", "cores": torch.get_num_threads(), "per_hit_rate": cpu,
+                                "sample": "the same calls through the same adapter code on CPU tensors with "
+                                          "the oracle op set (restatement of the reference's strict path)"}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, w: dict, world: int, rank: int) -> None:
     if rank != 0:
         return
@@ -565,7 +673,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix"], default="llama70b-shard")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter"], default="llama70b-shard")
     ap.add_argument("--heads", type=int, default=None, help="KV heads per GPU for the decode mix (default 1)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="override the number of sequences (smaller cases for profiling)")
@@ -596,6 +704,8 @@ def main() -> None:
     try:
         if args.workload == "decode-mix":
             run_decode_mix(args, world, rank, device)
+        elif args.workload == "adapter":
+            run_adapter(args, world, rank, device)
         else:
             run_ours(args, w, world, rank, device)
     finally:

@@ -164,7 +164,9 @@ int64_t kvca_choose_pop_launch_warps(int64_t num_slots);
  *   l2p[miss_ids] = miss_slots; p2l[miss_slots] = miss_ids;
  *   slot_meta[hit_slots] = pack(hit_pins, hit_usage);
  *   slot_meta[miss_slots] = pack(1, miss_usage).
- * hit_usage / miss_usage have the slot_meta word type.
+ * hit_usage / miss_usage have the slot_meta word type.  A miss id listed
+ * more than once keeps the slot of its last occurrence, as index_put_
+ * applied in order leaves it.
  */
 int kvca_commit_load_metadata(int meta_bits, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
                               void* d_slot_meta, int64_t num_slots, const int64_t* d_evicted,
@@ -179,7 +181,8 @@ int kvca_commit_load_metadata(int meta_bits, int64_t* d_l2p, int64_t num_logical
  * strict semantics adapter.py:647-651):
  *   l2p[evicted] = -1; l2p[ids] = slots; p2l[slots] = ids;
  *   slot_meta[slots] = pack(final_pins, final_usage).
- * final_pins / final_usage have the slot_meta word type.
+ * final_pins / final_usage have the slot_meta word type.  An id listed more
+ * than once keeps the slot of its last occurrence (index_put_ in order).
  */
 int kvca_commit_save_metadata(int meta_bits, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
                               void* d_slot_meta, int64_t num_slots, const int64_t* d_evicted,
@@ -232,6 +235,51 @@ int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64
                               const int64_t* d_reaccess, int64_t reaccess_per_step,
                               int64_t* d_victims, int64_t* d_steps_done, void* d_scratch,
                               int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * One-call planning of KVCacheAdapter.load (adapter.py:257-307, the
+ * orchestration that otherwise takes inspect, two nonzero compactions, a pop
+ * and an eviction-plan compaction, each synchronising the host).  One CTA:
+ *   inspect, hits / misses compacted in request order (hit slots, their
+ *   pin + 1 and usage + 1; miss ids), pop(#miss) with the hit slots blocked
+ *   (victims), the eviction plan of the victims (evict_ids / evict_slots:
+ *   victims whose previous logical id differs from the miss id), the hits'
+ *   usage re-read after the pop's aging when there were misses, and the
+ *   returned slot per request (result).
+ * d_counts[5] = n_hit, n_miss, n_evict, error code, error value.  Output
+ * arrays hold `count` entries; only the first n_* are defined.  The caller
+ * then moves the evicted payloads, loads the misses and commits with
+ * kvca_commit_load_metadata (miss usage 1).  d_scratch_bitmap as for
+ * kvca_pop_reusable_slots.  No reference counterpart as one call.
+ */
+int kvca_plan_load(int meta_bits, int order, const int64_t* d_l2p, int64_t num_logical,
+                   const int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                   int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                   uint32_t* d_scratch_bitmap, int64_t* d_result, int64_t* d_hit_slots,
+                   int64_t* d_hit_pins, void* d_hit_usage, int64_t* d_miss_ids,
+                   int64_t* d_victims, int64_t* d_evict_ids, int64_t* d_evict_slots,
+                   int64_t* d_counts, int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * One-call planning of KVCacheAdapter.save (adapter.py:221-243): existing /
+ * missing ids, pop(#missing) with the existing slots blocked (allocated),
+ * the selected slot per request, final pins and usage read after the pop
+ * (missing: 1; existing: usage + 1 saturating), and the eviction plan over
+ * all selected slots in request order.  d_move_slots is d_selected with the
+ * earlier occurrences of a repeated existing slot set to -1, so a row
+ * scatter with KVCA_FLAG_SKIP_NEGATIVE leaves the last row, as the
+ * reference's index_copy_ (adapter.py:656) applied in order does.  d_counts
+ * as for kvca_plan_load with n_existing first.  The caller then spills the
+ * evicted payloads, scatters the new data and commits with
+ * kvca_commit_save_metadata.
+ */
+int kvca_plan_save(int meta_bits, int order, const int64_t* d_l2p, int64_t num_logical,
+                   const int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                   int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                   uint32_t* d_scratch_bitmap, int64_t* d_selected, int64_t* d_move_slots,
+                   void* d_final_pins, void* d_final_usage, int64_t* d_allocated,
+                   int64_t* d_evict_ids, int64_t* d_evict_slots, int64_t* d_counts,
+                   int64_t* d_status, kvca_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Row movers                                                                */

@@ -101,6 +101,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_int, c_int, c_ptr, c_i64, c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
          c_ptr],
     ),
+    "kvca_plan_load": (
+        c_int,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+         c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
+    "kvca_plan_save": (
+        c_int,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+         c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
     "kvca_gather": (
         c_int,
         [ctypes.POINTER(PagedDesc), ctypes.POINTER(ChunkDesc), c_i64, c_i64, c_i64, ctypes.c_int32,

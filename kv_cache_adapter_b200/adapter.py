@@ -207,6 +207,9 @@ class KVCacheAdapter:
         self._search_start = torch.zeros((1,), dtype=ID_DTYPE, device=device)
         self._native_ext, self.runtime_path = self._detect_native_extension(
             prefer_native_extension=prefer_native_extension, native_ext=native_ext)
+        # An op set with plan_load / plan_save runs the inspect -> split -> pop ->
+        # eviction-plan part of load / save as one launch with one host sync.
+        self._planned = all(callable(getattr(self._native_ext, n, None)) for n in ("plan_load", "plan_save"))
 
     # -- derived views (adapter.py:185-203) --------------------------------
 
@@ -244,6 +247,9 @@ class KVCacheAdapter:
         if logical_block_ids.numel() == 0:
             return
         logical_block_ids = logical_block_ids.contiguous()
+        if self._planned:
+            self._save_planned(logical_block_ids, block_data)
+            return
 
         current_physical, existing_mask, inspected_usage = self._inspect_save_requests(logical_block_ids)
         existing_positions = _selected_positions(existing_mask)
@@ -287,6 +293,8 @@ class KVCacheAdapter:
         if logical_block_ids.numel() == 0:
             return torch.empty_like(logical_block_ids)
         logical_block_ids = logical_block_ids.contiguous()
+        if self._planned:
+            return self._load_planned(logical_block_ids)
 
         current_physical, resident_mask, updated_pins, updated_usage = self._inspect_load_requests(logical_block_ids)
         resident_positions = _selected_positions(resident_mask)
@@ -379,6 +387,39 @@ class KVCacheAdapter:
             f"kv_cache_adapter_b200 serves CUDA actual_blocks; got device {self._platform!r} "
             "(pass native_ext= to supply an op set for other devices)")
 
+    def _plan(self, op: str, ids: torch.Tensor):
+        try:
+            return getattr(self._native_ext, op)(
+                self._logical_to_physical, self._physical_to_logical, self._slot_meta, self._search_start, ids,
+                order=self.pop_order)
+        except IndexError as exc:
+            raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
+
+    def _load_planned(self, ids: torch.Tensor) -> torch.Tensor:
+        """load (adapter.py:257-307) with the planning steps in one device call;
+        the backend calls, the row movers and the commit follow unchanged."""
+        plan = self._plan("plan_load", ids)
+        if plan.evict_ids.numel() > 0:
+            self.backend.save_blocks(plan.evict_ids, self._native_ext.gather_blocks(self.actual_blocks, plan.evict_slots))
+        if plan.miss_ids.numel() > 0:
+            self.backend.load_blocks(plan.miss_ids, self.actual_blocks, plan.victims)
+        miss_usage = torch.ones((plan.victims.shape[0],), dtype=USAGE_DTYPE, device=self.actual_blocks.device)
+        self._native_ext.commit_load_metadata(
+            self._logical_to_physical, self._physical_to_logical, self._slot_meta, plan.evict_ids, plan.miss_ids,
+            plan.victims, plan.hit_slots, plan.hit_pins, plan.hit_usage, miss_usage, check=False)
+        return plan.result
+
+    def _save_planned(self, ids: torch.Tensor, block_data: torch.Tensor) -> None:
+        """save (adapter.py:205-255) with the planning steps in one device call."""
+        plan = self._plan("plan_save", ids)
+        if plan.evict_ids.numel() > 0:
+            self.backend.save_blocks(plan.evict_ids, self._native_ext.gather_blocks(self.actual_blocks, plan.evict_slots))
+        self._native_ext.scatter_blocks(self.actual_blocks, plan.move_slots, block_data.contiguous(),
+                                        skip_negative=True)
+        self._native_ext.commit_save_metadata(
+            self._logical_to_physical, self._physical_to_logical, self._slot_meta, plan.evict_ids, ids,
+            plan.selected, plan.final_pins, plan.final_usage, check=False)
+
     def _inspect_load_requests(self, ids: torch.Tensor):
         try:
             return tuple(self._native_ext.inspect_load_requests(
@@ -428,10 +469,13 @@ class KVCacheAdapter:
             final_pin_counts.contiguous(), final_usage_counts.contiguous(), check=True)
 
     def _copy_into_actual_blocks(self, physical_slot_ids: torch.Tensor, block_data: torch.Tensor) -> None:
-        """adapter.py:653-656 through the row mover."""
+        """adapter.py:653-656 through the row mover.  index_copy_ applied in
+        order leaves the last row of a repeated slot, so earlier repeats are
+        dropped before the (unordered) scatter."""
         if physical_slot_ids.numel() == 0:
             return
-        self._native_ext.scatter_blocks(self.actual_blocks, physical_slot_ids.contiguous(), block_data.contiguous())
+        self._native_ext.scatter_blocks(self.actual_blocks, _last_occurrences(physical_slot_ids, self.num_actual_blocks),
+                                        block_data.contiguous(), skip_negative=True)
 
     def _ordered_reusable_slots(self) -> torch.Tensor:
         scan_order = (self._search_start[0] + torch.arange(
@@ -539,8 +583,9 @@ class InMemoryBlockStoreBackend:
             data = block_data.to(device=self._storage.device, dtype=self._storage.dtype).contiguous()
             if self._storage.device.type == "cpu" and self._ops is None:
                 self._storage.index_copy_(0, ids, data)
-            else:
-                self._device_ops().scatter_blocks(self._storage, ids, data)
+            else:  # a repeated id keeps its last row, as index_copy_ in order does
+                self._device_ops().scatter_blocks(self._storage, _last_occurrences(ids, self.num_logical_blocks),
+                                                  data, skip_negative=True)
             self._present_mask.index_fill_(0, ids, True)
             self._record_ids("save", logical_block_ids)
         finally:
@@ -639,6 +684,20 @@ def _saturating_increment_usage(values: torch.Tensor) -> torch.Tensor:
     """adapter.py:1414-1416."""
     incremented = values.to(dtype=torch.int32) + 1
     return torch.clamp(incremented, max=USAGE_COUNT_MAX).to(dtype=USAGE_DTYPE)
+
+
+def _last_occurrences(ids: torch.Tensor, size: int) -> torch.Tensor:
+    """``ids`` with every occurrence but the last of a repeated id set to -1,
+    so that an unordered scatter skipping negatives leaves what index_copy_
+    applied in order leaves.  Ids outside [0, size) become ``size``, which the
+    row mover rejects, instead of reaching a torch index op."""
+    positions = torch.arange(ids.numel(), dtype=ID_DTYPE, device=ids.device)
+    valid = (ids >= 0) & (ids < size)
+    safe = torch.where(valid, ids, 0)
+    last = torch.full((size,), -1, dtype=ID_DTYPE, device=ids.device)
+    last.scatter_reduce_(0, safe, torch.where(valid, positions, -1), reduce="amax")
+    keep = last.index_select(0, safe) == positions
+    return torch.where(valid, torch.where(keep, ids, -1), size).contiguous()
 
 
 def _slot_meta_pin_counts(slot_meta: torch.Tensor, *, dtype: torch.dtype = PIN_COUNT_DTYPE) -> torch.Tensor:

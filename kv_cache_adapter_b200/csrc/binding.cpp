@@ -250,6 +250,51 @@ int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64
       reinterpret_cast<unsigned char*>(d_scratch), d_status, stream));
 }
 
+static bool plan_args_ok(int meta_bits, int order, const int64_t* l2p, int64_t num_logical,
+                         const int64_t* p2l, const void* meta, int64_t num_slots,
+                         const int64_t* search_start, const int64_t* ids, int64_t count,
+                         const uint32_t* bitmap, const int64_t* counts) {
+  return valid_meta_bits(meta_bits) &&
+         (order == KVCA_POP_ORDER_GROUPED || order == KVCA_POP_ORDER_PREFIX) && num_logical > 0 &&
+         num_slots > 0 && count > 0 && l2p && p2l && meta && search_start && ids && bitmap && counts;
+}
+
+int kvca_plan_load(int meta_bits, int order, const int64_t* d_l2p, int64_t num_logical,
+                   const int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                   int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                   uint32_t* d_scratch_bitmap, int64_t* d_result, int64_t* d_hit_slots,
+                   int64_t* d_hit_pins, void* d_hit_usage, int64_t* d_miss_ids,
+                   int64_t* d_victims, int64_t* d_evict_ids, int64_t* d_evict_slots,
+                   int64_t* d_counts, int64_t* d_status, kvca_stream_t stream) {
+  if (!plan_args_ok(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
+                    d_search_start, d_ids, count, d_scratch_bitmap, d_counts) ||
+      !d_result || !d_hit_slots || !d_hit_pins || !d_hit_usage || !d_miss_ids || !d_victims ||
+      !d_evict_ids || !d_evict_slots)
+    return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_plan_load(
+      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
+      count, d_scratch_bitmap, d_result, d_hit_slots, d_hit_pins, d_hit_usage, d_miss_ids,
+      d_victims, d_evict_ids, d_evict_slots, d_counts, d_status, stream));
+}
+
+int kvca_plan_save(int meta_bits, int order, const int64_t* d_l2p, int64_t num_logical,
+                   const int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                   int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                   uint32_t* d_scratch_bitmap, int64_t* d_selected, int64_t* d_move_slots,
+                   void* d_final_pins, void* d_final_usage, int64_t* d_allocated,
+                   int64_t* d_evict_ids, int64_t* d_evict_slots, int64_t* d_counts,
+                   int64_t* d_status, kvca_stream_t stream) {
+  if (!plan_args_ok(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
+                    d_search_start, d_ids, count, d_scratch_bitmap, d_counts) ||
+      !d_selected || !d_move_slots || !d_final_pins || !d_final_usage || !d_allocated || !d_evict_ids ||
+      !d_evict_slots)
+    return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_plan_save(
+      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
+      count, d_scratch_bitmap, d_selected, d_move_slots, d_final_pins, d_final_usage, d_allocated,
+      d_evict_ids, d_evict_slots, d_counts, d_status, stream));
+}
+
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,
                 int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
                 kvca_stream_t stream) {

@@ -970,6 +970,25 @@ __device__ bool all_in_range(const int64_t* ids, int64_t count, int64_t limit, i
   return *flag == 0;
 }
 
+// l2p[ids[i]] = slots[i] for i in [0, count), a repeated id keeping the slot
+// of its last occurrence, as a sequential index_put_ leaves it.  Every
+// target is first set to a mark below any encoded position, the largest
+// position per id is then elected with atomicMax, and only the elected
+// thread stores its slot (the others read back either the winner's encoded
+// position or the stored slot, never their own).  Ends without a barrier.
+__device__ void scatter_last_wins(int64_t* l2p, const int64_t* ids, const int64_t* slots,
+                                  int64_t count) {
+  constexpr long long kMark = LLONG_MIN;
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) l2p[ids[i]] = kMark;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x)
+    atomicMax(reinterpret_cast<long long*>(l2p + ids[i]), kMark + 1 + i);
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x)
+    if (__ldcg(reinterpret_cast<const long long*>(l2p + ids[i])) == kMark + 1 + i)
+      l2p[ids[i]] = slots[i];
+}
+
 // One CTA, phases separated by barriers so each phase sees the previous one.
 template <typename MetaT>
 __global__ void __launch_bounds__(1024)
@@ -988,10 +1007,8 @@ __global__ void __launch_bounds__(1024)
   if (!all_in_range(hit_slots, num_hit, num_slots, status, &bad)) return;
   for (int64_t i = threadIdx.x; i < num_evicted; i += blockDim.x) l2p[evicted[i]] = -1;
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < num_miss; i += blockDim.x) {
-    l2p[miss_ids[i]] = miss_slots[i];
-    p2l[miss_slots[i]] = miss_ids[i];
-  }
+  scatter_last_wins(l2p, miss_ids, miss_slots, num_miss);
+  for (int64_t i = threadIdx.x; i < num_miss; i += blockDim.x) p2l[miss_slots[i]] = miss_ids[i];
   __syncthreads();
   for (int64_t i = threadIdx.x; i < num_hit; i += blockDim.x)
     meta[hit_slots[i]] = M::pack(hit_pins[i], hit_usage[i]);
@@ -1015,8 +1032,9 @@ __global__ void __launch_bounds__(1024)
   if (!all_in_range(slots, count, num_slots, status, &bad)) return;
   for (int64_t i = threadIdx.x; i < num_evicted; i += blockDim.x) l2p[evicted[i]] = -1;
   __syncthreads();
+  scatter_last_wins(l2p, ids, slots, count);
+  // a repeated slot is repeated with its id, pins and usage: any store wins
   for (int64_t i = threadIdx.x; i < count; i += blockDim.x) {
-    l2p[ids[i]] = slots[i];
     p2l[slots[i]] = ids[i];
     meta[slots[i]] = M::pack(final_pins[i], final_usage[i]);
   }
@@ -1066,6 +1084,257 @@ __global__ void __launch_bounds__(1024)
     for (int u = 0; u < kReleasePerThread; ++u)
       if (slot[u] >= 0) meta[slot[u]] = next[u];
     __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Load / save planning: everything of KVCacheAdapter.load / save that decides
+// slots, in one CTA, so the host synchronises once per call (to size the
+// backend calls) instead of at every step.
+// ---------------------------------------------------------------------------
+//
+// counts[0..4] = n_hit (load) or n_existing (save), n_miss, n_evict, error
+// code, error value.  On an error nothing but the outputs is written (a bad
+// id is found before anything changes; too few reusable slots leave the
+// table as the pop found it).
+
+constexpr int kPackShift = 16;  // hit/miss tile counts packed in one scan word
+
+template <typename MetaT>
+struct PlanShared {
+  PopShared<MetaT> pop;
+  int bad;
+  int repeated;
+  long long bad_value;
+  long long ids[1024];
+};
+
+__device__ __forceinline__ void plan_fail(int64_t* counts, int64_t* status, int code, int64_t value) {
+  counts[3] = code;
+  counts[4] = value;
+  report(status, code, value);
+}
+
+// Validates ids and their current slots; returns false (uniformly) on a bad id.
+template <typename MetaT>
+__device__ bool plan_validate(const int64_t* l2p, int64_t n_logical, int64_t n, const int64_t* ids,
+                              int64_t k, int64_t* counts, int64_t* status, PlanShared<MetaT>& sh) {
+  if (threadIdx.x == 0) sh.bad = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+    const int64_t id = ids[i];
+    bool bad = !in_range(id, n_logical);
+    int64_t v = id;
+    if (!bad) {
+      const int64_t cur = l2p[id];
+      if (cur >= n) {
+        bad = true;
+        v = cur;
+      }
+    }
+    if (bad && atomicCAS(&sh.bad, 0, 1) == 0) sh.bad_value = v;
+  }
+  __syncthreads();
+  if (sh.bad) {
+    if (threadIdx.x == 0) plan_fail(counts, status, KVCA_ERR_BAD_INDEX, sh.bad_value);
+    return false;
+  }
+  return true;
+}
+
+// KVCacheAdapter.load up to the backend calls (adapter.py:264-305):
+// inspect (hits: pin + 1, usage + 1 saturating), hit / miss compaction in
+// request order, pop(#miss) with the hit slots blocked, the eviction plan of
+// the popped slots, the hits' usage re-read after the pop's aging, and the
+// returned slots.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    plan_load_kernel(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
+                     int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
+                     int order, bool aligned, int64_t* result, int64_t* hit_slots, int64_t* hit_pins,
+                     MetaT* hit_usage, int64_t* miss_ids, int64_t* victims, int64_t* evict_ids,
+                     int64_t* evict_slots, int64_t* counts, int64_t* status) {
+  using M = Meta<MetaT>;
+  __shared__ PlanShared<MetaT> sh;
+  if (threadIdx.x == 0) counts[3] = counts[4] = 0;
+  if (!plan_validate<MetaT>(l2p, n_logical, n, ids, k, counts, status, sh)) return;
+  // hits and misses in request order; the hit slots are blocked for the pop
+  int64_t nh = 0, nm = 0;
+  for (int64_t tile = 0; tile < k; tile += blockDim.x) {
+    const int64_t i = tile + threadIdx.x;
+    const int64_t cur = i < k ? l2p[ids[i]] : -1;
+    const bool hit = i < k && cur >= 0;
+    const bool miss = i < k && cur < 0;
+    int total;
+    const int base = block_excl_scan((hit ? 1 : 0) | ((miss ? 1 : 0) << kPackShift), &total, sh.pop.scan);
+    if (hit) {
+      const int64_t r = nh + (base & ((1 << kPackShift) - 1));
+      const unsigned w = meta[cur];
+      hit_slots[r] = cur;
+      hit_pins[r] = static_cast<int64_t>(M::pin(w)) + 1;
+      hit_usage[r] = static_cast<MetaT>(M::sat_inc(M::usage(w)));
+      atomicOr(bitmap + (cur >> 5), 1u << (cur & 31));
+      result[i] = cur;
+    }
+    if (miss) miss_ids[nm + (base >> kPackShift)] = ids[i];
+    nh += total & ((1 << kPackShift) - 1);
+    nm += total >> kPackShift;
+  }
+  __syncthreads();
+  int rc = KVCA_OK;
+  if (nm > 0) rc = pop_cta<MetaT>(meta, n, search_start, bitmap, nm, victims, order, aligned, sh.pop);
+  __syncthreads();
+  for (int64_t j = threadIdx.x; j < nh; j += blockDim.x) {
+    const int64_t b = hit_slots[j];
+    atomicAnd(bitmap + (b >> 5), ~(1u << (b & 31)));
+  }
+  if (rc != KVCA_OK) {
+    if (threadIdx.x == 0) plan_fail(counts, status, rc, nm);
+    return;
+  }
+  // returned slots at the miss positions; the eviction plan of the victims
+  int64_t mi = 0, ne = 0;
+  for (int64_t tile = 0; tile < k; tile += blockDim.x) {
+    const int64_t i = tile + threadIdx.x;
+    const bool miss = i < k && l2p[ids[i]] < 0;
+    int total;
+    const int base = block_excl_scan(miss ? 1 : 0, &total, sh.pop.scan);
+    if (miss) result[i] = victims[mi + base];
+    mi += total;
+  }
+  for (int64_t tile = 0; tile < nm; tile += blockDim.x) {
+    const int64_t j = tile + threadIdx.x;
+    int64_t prev = -1;
+    if (j < nm) prev = p2l[victims[j]];
+    const bool ev = j < nm && prev >= 0 && prev != miss_ids[j];
+    int total;
+    const int base = block_excl_scan(ev ? 1 : 0, &total, sh.pop.scan);
+    if (ev) {
+      evict_ids[ne + base] = prev;
+      evict_slots[ne + base] = victims[j];
+    }
+    ne += total;
+  }
+  // with misses the pop may have aged usage: hits take usage + 1 of what is left
+  if (nm > 0)
+    for (int64_t j = threadIdx.x; j < nh; j += blockDim.x)
+      hit_usage[j] = static_cast<MetaT>(M::sat_inc(M::usage(meta[hit_slots[j]])));
+  if (threadIdx.x == 0) {
+    counts[0] = nh;
+    counts[1] = nm;
+    counts[2] = ne;
+  }
+}
+
+// KVCacheAdapter.save up to the backend call (adapter.py:221-243): existing /
+// missing compaction, pop(#missing) with the existing slots blocked, the
+// selected slots, final pins and usage read after the pop, and the eviction
+// plan over every selected slot in request order.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    plan_save_kernel(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
+                     int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
+                     int order, bool aligned, int64_t* selected, int64_t* move_slots,
+                     MetaT* final_pins, MetaT* final_usage, int64_t* allocated, int64_t* evict_ids,
+                     int64_t* evict_slots, int64_t* counts, int64_t* status) {
+  using M = Meta<MetaT>;
+  __shared__ PlanShared<MetaT> sh;
+  if (threadIdx.x == 0) {
+    counts[3] = counts[4] = 0;
+    sh.repeated = 0;
+  }
+  if (!plan_validate<MetaT>(l2p, n_logical, n, ids, k, counts, status, sh)) return;
+  int64_t nx = 0, nm = 0;
+  for (int64_t tile = 0; tile < k; tile += blockDim.x) {
+    const int64_t i = tile + threadIdx.x;
+    const int64_t cur = i < k ? l2p[ids[i]] : -1;
+    const bool ex = i < k && cur >= 0;
+    const bool miss = i < k && cur < 0;
+    int total;
+    block_excl_scan((ex ? 1 : 0) | ((miss ? 1 : 0) << kPackShift), &total, sh.pop.scan);
+    if (ex) {
+      const unsigned bit = 1u << (cur & 31);
+      if (atomicOr(bitmap + (cur >> 5), bit) & bit) sh.repeated = 1;  // an existing id asked twice
+      selected[i] = cur;
+    }
+    nx += total & ((1 << kPackShift) - 1);
+    nm += total >> kPackShift;
+  }
+  __syncthreads();
+  int rc = KVCA_OK;
+  if (nm > 0) rc = pop_cta<MetaT>(meta, n, search_start, bitmap, nm, allocated, order, aligned, sh.pop);
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+    const int64_t cur = l2p[ids[i]];
+    if (cur >= 0) atomicAnd(bitmap + (cur >> 5), ~(1u << (cur & 31)));
+  }
+  if (rc != KVCA_OK) {
+    if (threadIdx.x == 0) plan_fail(counts, status, rc, nm);
+    return;
+  }
+  int64_t mi = 0, ne = 0;
+  for (int64_t tile = 0; tile < k; tile += blockDim.x) {
+    const int64_t i = tile + threadIdx.x;
+    const int64_t cur = i < k ? l2p[ids[i]] : -1;
+    const bool miss = i < k && cur < 0;
+    int total;
+    const int base = block_excl_scan(miss ? 1 : 0, &total, sh.pop.scan);
+    int64_t slot = cur;
+    if (miss) {
+      slot = allocated[mi + base];
+      selected[i] = slot;
+    }
+    if (i < k) move_slots[i] = slot;
+    bool ev = false;
+    int64_t prev = -1;
+    if (i < k) {
+      const unsigned w = meta[slot];
+      final_pins[i] = static_cast<MetaT>(M::pin(w));
+      final_usage[i] = static_cast<MetaT>(miss ? 1u : M::sat_inc(M::usage(w)));
+      prev = p2l[slot];
+      ev = prev >= 0 && prev != ids[i];
+    }
+    mi += total;
+    __syncthreads();
+    int etotal;
+    const int ebase = block_excl_scan(ev ? 1 : 0, &etotal, sh.pop.scan);
+    if (ev) {
+      evict_ids[ne + ebase] = prev;
+      evict_slots[ne + ebase] = slot;
+    }
+    ne += etotal;
+  }
+  // Rows for the data scatter: an existing slot named more than once takes
+  // the row of its last occurrence (index_copy_ applied in order), so the
+  // earlier ones are dropped (-1).  Only when the first pass saw a repeat:
+  // every existing position compares its id with the later ones, staged
+  // through shared memory one 1024-id chunk at a time.
+  __syncthreads();
+  if (sh.repeated) {
+    for (int64_t tile = 0; tile < k; tile += blockDim.x) {
+      const int64_t i = tile + threadIdx.x;
+      const int64_t id = i < k ? ids[i] : -1;
+      const bool ex = i < k && l2p[id] >= 0;
+      bool later = false;
+      for (int64_t c = tile; c < k; c += blockDim.x) {
+        __syncthreads();
+        if (c + threadIdx.x < k) sh.ids[threadIdx.x] = ids[c + threadIdx.x];
+        __syncthreads();
+        const int64_t m = k - c < blockDim.x ? k - c : blockDim.x;
+        if (ex && !later)
+          for (int64_t j = 0; j < m; ++j)
+            if (c + j > i && sh.ids[j] == id) {
+              later = true;
+              break;
+            }
+      }
+      if (later) move_slots[i] = -1;
+    }
+  }
+  if (threadIdx.x == 0) {
+    counts[0] = nx;
+    counts[1] = nm;
+    counts[2] = ne;
   }
 }
 
@@ -1581,6 +1850,39 @@ cudaError_t launch_commit_save(int meta_bits, int64_t* l2p, int64_t num_logical,
                                     evicted, num_evicted, ids, slots,
                                     static_cast<const MetaT*>(final_pins),
                                     static_cast<const MetaT*>(final_usage), count, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_plan_load(int meta_bits, int order, const int64_t* l2p, int64_t num_logical,
+                             const int64_t* p2l, void* meta, int64_t num_slots,
+                             int64_t* search_start, const int64_t* ids, int64_t count,
+                             uint32_t* bitmap, int64_t* result, int64_t* hit_slots,
+                             int64_t* hit_pins, void* hit_usage, int64_t* miss_ids, int64_t* victims,
+                             int64_t* evict_ids, int64_t* evict_slots, int64_t* counts,
+                             int64_t* status, cudaStream_t stream) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  KVCA_META_DISPATCH(meta_bits, plan_load_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
+                                    search_start, ids, count, bitmap, order, aligned, result,
+                                    hit_slots, hit_pins, static_cast<MetaT*>(hit_usage), miss_ids,
+                                    victims, evict_ids, evict_slots, counts, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_plan_save(int meta_bits, int order, const int64_t* l2p, int64_t num_logical,
+                             const int64_t* p2l, void* meta, int64_t num_slots,
+                             int64_t* search_start, const int64_t* ids, int64_t count,
+                             uint32_t* bitmap, int64_t* selected, int64_t* move_slots,
+                             void* final_pins, void* final_usage, int64_t* allocated,
+                             int64_t* evict_ids, int64_t* evict_slots, int64_t* counts,
+                             int64_t* status, cudaStream_t stream) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  KVCA_META_DISPATCH(meta_bits, plan_save_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
+                                    search_start, ids, count, bitmap, order, aligned, selected,
+                                    move_slots, static_cast<MetaT*>(final_pins),
+                                    static_cast<MetaT*>(final_usage),
+                                    allocated, evict_ids, evict_slots, counts, status));
   return cudaGetLastError();
 }
 

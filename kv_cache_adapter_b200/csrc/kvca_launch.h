@@ -96,4 +96,20 @@ cudaError_t launch_clock_stream_batched(int meta_bits, int order, void* meta, in
                                         int64_t* steps_done, unsigned char* scratch,
                                         int64_t* status, cudaStream_t stream);
 
+cudaError_t launch_plan_load(int meta_bits, int order, const int64_t* l2p, int64_t num_logical,
+                             const int64_t* p2l, void* meta, int64_t num_slots,
+                             int64_t* search_start, const int64_t* ids, int64_t count,
+                             uint32_t* bitmap, int64_t* result, int64_t* hit_slots,
+                             int64_t* hit_pins, void* hit_usage, int64_t* miss_ids, int64_t* victims,
+                             int64_t* evict_ids, int64_t* evict_slots, int64_t* counts,
+                             int64_t* status, cudaStream_t stream);
+
+cudaError_t launch_plan_save(int meta_bits, int order, const int64_t* l2p, int64_t num_logical,
+                             const int64_t* p2l, void* meta, int64_t num_slots,
+                             int64_t* search_start, const int64_t* ids, int64_t count,
+                             uint32_t* bitmap, int64_t* selected, int64_t* move_slots,
+                             void* final_pins, void* final_usage, int64_t* allocated,
+                             int64_t* evict_ids, int64_t* evict_slots, int64_t* counts,
+                             int64_t* status, cudaStream_t stream);
+
 }  // namespace kvca

@@ -44,6 +44,8 @@ __all__ = [
     "scatter_layers",
     "gather_tokens",
     "scatter_tokens",
+    "plan_load",
+    "plan_save",
     "check_status",
     "library_path",
     "PlaneTable",
@@ -388,6 +390,93 @@ def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps:
     return victims, steps_done
 
 
+class LoadPlan:
+    """Result of ``plan_load``: views sized by the plan's counts."""
+
+    __slots__ = ("result", "hit_slots", "hit_pins", "hit_usage", "miss_ids", "victims", "evict_ids",
+                 "evict_slots")
+
+    def __init__(self, **kw):
+        for k, v in kw.items():
+            setattr(self, k, v)
+
+
+class SavePlan:
+    """Result of ``plan_save``: views sized by the plan's counts."""
+
+    __slots__ = ("selected", "move_slots", "final_pins", "final_usage", "allocated", "evict_ids", "evict_slots")
+
+    def __init__(self, **kw):
+        for k, v in kw.items():
+            setattr(self, k, v)
+
+
+def _plan_counts(counts: torch.Tensor, what: str) -> list[int]:
+    vals = counts.tolist()  # the call's only synchronisation
+    if vals[3] != 0:
+        _status(counts.device).zero_()
+        _raise_for(int(vals[3]), int(vals[4]), what)
+    return vals
+
+
+def plan_load(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor, slot_meta: torch.Tensor,
+              search_start: torch.Tensor, logical_block_ids: torch.Tensor, *,
+              order: str | None = None) -> LoadPlan:
+    """inspect + hit/miss split + pop + eviction plan of KVCacheAdapter.load
+    (adapter.py:264-305) in one launch and one synchronisation.  Mutates
+    slot_meta (aging) and search_start like pop_reusable_slots."""
+    for t, name in ((logical_to_physical, "logical_to_physical"), (physical_to_logical, "physical_to_logical"),
+                    (search_start, "search_start"), (logical_block_ids, "logical_block_ids")):
+        _require(t, torch.int64, name)
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    dev = slot_meta.device
+    k = logical_block_ids.numel()
+    buf = torch.empty((7, k), dtype=torch.int64, device=dev)
+    hit_usage = torch.empty(k, dtype=slot_meta.dtype, device=dev)
+    counts = torch.empty(5, dtype=torch.int64, device=dev)
+    n = slot_meta.numel()
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_plan_load(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
+            logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
+            _ptr(logical_block_ids), k, _ptr(_bitmap(dev, n)), _ptr(buf[0]), _ptr(buf[1]), _ptr(buf[2]),
+            _ptr(hit_usage), _ptr(buf[3]), _ptr(buf[4]), _ptr(buf[5]), _ptr(buf[6]), _ptr(counts),
+            _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "plan_load")
+    nh, nm, ne = _plan_counts(counts, "plan_load")[:3]
+    return LoadPlan(result=buf[0], hit_slots=buf[1, :nh], hit_pins=buf[2, :nh], hit_usage=hit_usage[:nh],
+                    miss_ids=buf[3, :nm], victims=buf[4, :nm], evict_ids=buf[5, :ne], evict_slots=buf[6, :ne])
+
+
+def plan_save(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor, slot_meta: torch.Tensor,
+              search_start: torch.Tensor, logical_block_ids: torch.Tensor, *,
+              order: str | None = None) -> SavePlan:
+    """inspect + existing/missing split + pop + final pins/usage + eviction
+    plan of KVCacheAdapter.save (adapter.py:221-243) in one launch and one
+    synchronisation."""
+    for t, name in ((logical_to_physical, "logical_to_physical"), (physical_to_logical, "physical_to_logical"),
+                    (search_start, "search_start"), (logical_block_ids, "logical_block_ids")):
+        _require(t, torch.int64, name)
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    dev = slot_meta.device
+    k = logical_block_ids.numel()
+    buf = torch.empty((5, k), dtype=torch.int64, device=dev)
+    small = torch.empty((2, k), dtype=slot_meta.dtype, device=dev)
+    counts = torch.empty(5, dtype=torch.int64, device=dev)
+    n = slot_meta.numel()
+    with torch.cuda.device(dev):
+        rc = _lib_handle.kvca_plan_save(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
+            logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
+            _ptr(logical_block_ids), k, _ptr(_bitmap(dev, n)), _ptr(buf[0]), _ptr(buf[4]), _ptr(small[0]),
+            _ptr(small[1]), _ptr(buf[1]), _ptr(buf[2]), _ptr(buf[3]), _ptr(counts), _ptr(_status(dev)),
+            _stream(dev))
+    _host_rc(rc, "plan_save")
+    nx, nm, ne = _plan_counts(counts, "plan_save")[:3]
+    return SavePlan(selected=buf[0], move_slots=buf[4], final_pins=small[0], final_usage=small[1],
+                    allocated=buf[1, :nm], evict_ids=buf[2, :ne], evict_slots=buf[3, :ne])
+
+
 # ---------------------------------------------------------------------------
 # row movers
 # ---------------------------------------------------------------------------
@@ -507,14 +596,17 @@ def gather_blocks(actual_blocks: torch.Tensor, slot_ids: torch.Tensor,
 
 
 def scatter_blocks(actual_blocks: torch.Tensor, slot_ids: torch.Tensor, block_data: torch.Tensor,
-                   *, check: bool | None = None) -> None:
-    """``actual_blocks.index_copy_(0, slot_ids, block_data)`` (adapter.py:653-656)."""
+                   *, skip_negative: bool = False, check: bool | None = None) -> None:
+    """``actual_blocks.index_copy_(0, slot_ids, block_data)`` (adapter.py:653-656).
+    Slots must be distinct (a repeated slot receives one of its rows); with
+    ``skip_negative`` rows whose slot is negative are not written."""
     pl = _planes([actual_blocks], 1, "actual_blocks")
     _require_index(slot_ids, pl.device, "slot_ids")
     k = slot_ids.numel()
     _chunk_tensor(block_data, (k, *pl.row_shape), pl.dtype, pl.device, "block_data")
     _launch_move("kvca_scatter", _chunk_desc(block_data, max(k, 1), 1, pl.row_bytes),
-                 pl.desc(slot_ids), 1, k, pl.row_bytes, 0, pl.device, check)
+                 pl.desc(slot_ids), 1, k, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE if skip_negative else 0,
+                 pl.device, check)
 
 
 def copy_blocks(src_blocks: torch.Tensor, src_ids: torch.Tensor, dst_blocks: torch.Tensor,

@@ -58,8 +58,11 @@ class OracleOps:
         self.calls.append("gather_blocks")
         return moves.gather_blocks(actual_blocks, slot_ids)
 
-    def scatter_blocks(self, actual_blocks, slot_ids, block_data, check=None):
+    def scatter_blocks(self, actual_blocks, slot_ids, block_data, skip_negative=False, check=None):
         self.calls.append("scatter_blocks")
+        if skip_negative:
+            keep = slot_ids >= 0
+            slot_ids, block_data = slot_ids[keep], block_data[keep]
         moves.scatter_blocks(actual_blocks, slot_ids, block_data)
 
     def copy_blocks(self, src, src_ids, dst, dst_ids, check=None):

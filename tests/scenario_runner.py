@@ -22,7 +22,8 @@ def _flat(t: torch.Tensor | None):
     return t.detach().cpu().reshape(t.shape[0], -1)
 
 
-def run_and_compare(case: dict, device: torch.device, *, native_ext=None, backend_ops=None) -> None:
+def run_and_compare(case: dict, device: torch.device, *, native_ext=None, backend_ops=None,
+                    planned: bool | None = None) -> None:
     spec = case["spec"]
     shape = tuple(spec["block_shape"])
     init = {int(k): torch.tensor(v, dtype=torch.float32, device=device).reshape(shape)
@@ -36,6 +37,9 @@ def run_and_compare(case: dict, device: torch.device, *, native_ext=None, backen
     ad = KVCacheAdapter(spec["num_actual"], spec["num_logical"],
                         torch.zeros((spec["num_actual"], *shape), dtype=torch.float32, device=device),
                         backend, native_ext=native_ext)
+    if planned is not None:  # force the one-launch planners on or off
+        assert ad._planned or not planned
+        ad._planned = planned
     for i, step in enumerate(case["steps"]):
         where = f"case {spec['case']} step {i} {step['op']} {step['ids']}"
         ids = torch.tensor(step["ids"], dtype=torch.int64, device=device)

@@ -43,10 +43,11 @@ def backend_with(api, rows: dict[int, list[float]], **kw):
     return api.InMemoryBlockStoreBackend({k: _payload(v) for k, v in rows.items()}, record_device_ops=True, **kw)
 
 
+@pytest.mark.parametrize("planned", [True, False])
 @pytest.mark.parametrize("case_index", range(60))
-def test_recorded_reference_scenarios(case_index):
+def test_recorded_reference_scenarios(case_index, planned):
     case = scenario_runner.load_scenarios()[case_index]
-    scenario_runner.run_and_compare(case, DEV)
+    scenario_runner.run_and_compare(case, DEV, planned=planned)
 
 
 def test_runtime_path_and_native_library_loaded(api):
