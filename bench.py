@@ -606,6 +606,9 @@ def run_adapter(args, world: int, rank: int, device) -> None:
     batch 32, 128-float blocks, in-memory backend on the device)."""
     steps = max(args.steps, 20)
     cuda = _time_adapter(_adapter_case(device), device, steps, args.warmup)
+    planned_ad = _adapter_case(device)
+    planned_ad._device_store = lambda: None  # one-launch plan, then the backend's own calls
+    planned = _time_adapter(planned_ad, device, steps, args.warmup)
     stepwise_ad = _adapter_case(device)
     stepwise_ad._planned = False  # inspect, pop, commit as separate launches
     stepwise = _time_adapter(stepwise_ad, device, steps, args.warmup)
@@ -629,6 +632,8 @@ def run_adapter(args, world: int, rank: int, device) -> None:
                                "128 x fp32 blocks, in-memory backend on the device, hit rates 0 / 0.5 / 1",
                    "timing": "host clock around each call, synchronised before and after"},
         "per_hit_rate": cuda,
+        "path": "device store: plan, spill, fill, commit enqueued with one host read per call",
+        "per_hit_rate_planned": planned,
         "per_hit_rate_stepwise": stepwise,
     }
     if world == 1 and not args.no_cpu_baseline:

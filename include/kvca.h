@@ -50,6 +50,7 @@ typedef struct CUstream_st* kvca_stream_t; /* same type as cudaStream_t */
 #define KVCA_ERR_CUDA 4                  /* launch or runtime failure */
 #define KVCA_ERR_SIZE_LIMIT 5            /* table larger than a fixed-capacity entry point takes */
 #define KVCA_ERR_DEVICE_TIMEOUT 6        /* a bounded device-side wait gave up (value: CTA index) */
+#define KVCA_ERR_BLOCK_NOT_FOUND 7       /* reference: BlockNotFoundError, adapter.py:805 (value: id) */
 
 /* Clock-sweep victim order (see kvca_pop_reusable_slots). */
 #define KVCA_POP_ORDER_GROUPED 0
@@ -246,7 +247,9 @@ int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64
  *   victims whose previous logical id differs from the miss id), the hits'
  *   usage re-read after the pop's aging when there were misses, and the
  *   returned slot per request (result).
- * d_counts[5] = n_hit, n_miss, n_evict, error code, error value.  Output
+ * d_counts[7] = n_hit, n_miss, n_evict, error code, error value, and the
+ * status word's code and value as the launch found them (an error latched
+ * by an earlier launch whose status was not read yet).  Output
  * arrays hold `count` entries; only the first n_* are defined.  The caller
  * then moves the evicted payloads, loads the misses and commits with
  * kvca_commit_load_metadata (miss usage 1).  d_scratch_bitmap as for
@@ -280,6 +283,58 @@ int kvca_plan_save(int meta_bits, int order, const int64_t* d_l2p, int64_t num_l
                    void* d_final_pins, void* d_final_usage, int64_t* d_allocated,
                    int64_t* d_evict_ids, int64_t* d_evict_slots, int64_t* d_counts,
                    int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * A block store resident on the same GPU: the in-memory backend
+ * (InMemoryBlockStoreBackend, adapter.py:679-833) with its storage tensor
+ * on the device.  Row l of the store holds logical block l at
+ * storage + l * storage_row_stride; present[l] != 0 once block l was saved.
+ * scratch holds one int32 per logical block, zero on entry and left zero.
+ */
+typedef struct kvca_device_store {
+  uint64_t storage;
+  int64_t storage_row_stride;
+  uint8_t* present;
+  int32_t* scratch;
+} kvca_device_store;
+
+/*
+ * KVCacheAdapter.load (adapter.py:257-307) against a device-resident store,
+ * enqueued as one sequence with no host synchronisation: kvca_plan_load,
+ * the spill of evicted payloads into the store (backend.save_blocks,
+ * adapter.py:735-756; a repeated evicted id keeps its last payload), the
+ * store's presence check of the misses (adapter.py:801-806), the fill of the
+ * victims from the store (adapter.py:779-787) and the commit (miss usage 1).
+ * actual_blocks: slot s at d_actual + s * actual_row_stride, row_bytes each.
+ * d_work: 7 * count int64, d_work_meta: count slot_meta words.  d_result:
+ * the returned slot per request.  d_counts[7] as for kvca_plan_load; a miss
+ * absent from the store gives code KVCA_ERR_BLOCK_NOT_FOUND after the spill
+ * and before any fill or commit, as the reference's backend raises.  No
+ * reference counterpart as one call.
+ */
+int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+                           int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                           int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                           uint32_t* d_scratch_bitmap, const kvca_device_store* store,
+                           uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
+                           int64_t* d_work, void* d_work_meta, int64_t* d_result,
+                           int64_t* d_counts, int64_t* d_status, kvca_stream_t stream);
+
+/*
+ * KVCacheAdapter.save (adapter.py:205-255) against a device-resident store,
+ * one sequence with no host synchronisation: kvca_plan_save, the spill of
+ * evicted payloads into the store, the commit and the scatter of
+ * d_block_data (count rows of row_bytes, contiguous) into the selected
+ * slots (a repeated slot keeps its last row).  d_work: 5 * count int64,
+ * d_work_meta: 2 * count slot_meta words.  d_counts as for kvca_plan_save.
+ */
+int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+                           int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                           int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                           uint32_t* d_scratch_bitmap, const kvca_device_store* store,
+                           uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
+                           uint64_t d_block_data, int64_t* d_work, void* d_work_meta,
+                           int64_t* d_counts, int64_t* d_status, kvca_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Row movers                                                                */

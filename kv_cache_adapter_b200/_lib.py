@@ -19,6 +19,7 @@ KVCA_ERR_BAD_ARGUMENT = 3
 KVCA_ERR_CUDA = 4
 KVCA_ERR_SIZE_LIMIT = 5
 KVCA_ERR_DEVICE_TIMEOUT = 6
+KVCA_ERR_BLOCK_NOT_FOUND = 7
 KVCA_NOALLOC_MAX_SLOTS = 1048576
 
 KVCA_POP_ORDER_GROUPED = 0
@@ -54,6 +55,17 @@ class ChunkDesc(ctypes.Structure):
         ("chunk_stride", c_i64),
         ("row_stride", c_i64),
         ("plane_stride", c_i64),
+    ]
+
+
+class DeviceStore(ctypes.Structure):
+    """kvca_device_store."""
+
+    _fields_ = [
+        ("storage", ctypes.c_uint64),
+        ("storage_row_stride", c_i64),
+        ("present", c_ptr),
+        ("scratch", c_ptr),
     ]
 
 
@@ -110,6 +122,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
          c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
+    "kvca_load_device_store": (
+        c_int,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr,
+         ctypes.POINTER(DeviceStore), ctypes.c_uint64, c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
+    "kvca_save_device_store": (
+        c_int,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr,
+         ctypes.POINTER(DeviceStore), ctypes.c_uint64, c_i64, c_i64, ctypes.c_uint64, c_ptr, c_ptr, c_ptr, c_ptr,
+         c_ptr],
     ),
     "kvca_gather": (
         c_int,

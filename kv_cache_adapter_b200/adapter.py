@@ -248,7 +248,11 @@ class KVCacheAdapter:
             return
         logical_block_ids = logical_block_ids.contiguous()
         if self._planned:
-            self._save_planned(logical_block_ids, block_data)
+            store = self._device_store()
+            if store is not None:
+                self._save_device_store(logical_block_ids, block_data, store)
+            else:
+                self._save_planned(logical_block_ids, block_data)
             return
 
         current_physical, existing_mask, inspected_usage = self._inspect_save_requests(logical_block_ids)
@@ -294,6 +298,9 @@ class KVCacheAdapter:
             return torch.empty_like(logical_block_ids)
         logical_block_ids = logical_block_ids.contiguous()
         if self._planned:
+            store = self._device_store()
+            if store is not None:
+                return self._load_device_store(logical_block_ids, store)
             return self._load_planned(logical_block_ids)
 
         current_physical, resident_mask, updated_pins, updated_usage = self._inspect_load_requests(logical_block_ids)
@@ -395,12 +402,52 @@ class KVCacheAdapter:
         except IndexError as exc:
             raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
 
+    def _device_store(self):
+        """The backend's device-resident store (storage, present, scratch) when
+        it offers one for these actual_blocks and the op set drives it."""
+        offer = getattr(self.backend, "device_store", None)
+        if not callable(offer) or not callable(getattr(self._native_ext, "load_device_store", None)):
+            return None
+        if not self.actual_blocks.is_contiguous():
+            return None
+        return offer(self.actual_blocks)
+
+    def _load_device_store(self, ids: torch.Tensor, store) -> torch.Tensor:
+        """load (adapter.py:257-307) with the backend's spill and fill on the
+        device: one enqueued sequence and one host read."""
+        storage, present, scratch = store
+        try:
+            result, counts = self._native_ext.load_device_store(
+                self._logical_to_physical, self._physical_to_logical, self._slot_meta, self._search_start, ids,
+                self.actual_blocks, storage, present, scratch, order=self.pop_order)
+        except IndexError as exc:
+            raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
+        except BlockNotFoundError as exc:
+            self.backend.note_device_ops(saved=exc.counts[2] > 0, loaded=True)
+            raise
+        self.backend.note_device_ops(saved=counts[2] > 0, loaded=counts[1] > 0)
+        return result
+
+    def _save_device_store(self, ids: torch.Tensor, block_data: torch.Tensor, store) -> None:
+        """save (adapter.py:205-255) with the backend's spill on the device."""
+        storage, present, scratch = store
+        try:
+            counts = self._native_ext.save_device_store(
+                self._logical_to_physical, self._physical_to_logical, self._slot_meta, self._search_start, ids,
+                block_data.contiguous(), self.actual_blocks, storage, present, scratch, order=self.pop_order)
+        except IndexError as exc:
+            raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
+        self.backend.note_device_ops(saved=counts[2] > 0, loaded=False)
+
     def _load_planned(self, ids: torch.Tensor) -> torch.Tensor:
         """load (adapter.py:257-307) with the planning steps in one device call;
         the backend calls, the row movers and the commit follow unchanged."""
         plan = self._plan("plan_load", ids)
+        # slots from the plan are in range by construction: the launches below
+        # leave their status to the next read (the backend's or the next plan's)
         if plan.evict_ids.numel() > 0:
-            self.backend.save_blocks(plan.evict_ids, self._native_ext.gather_blocks(self.actual_blocks, plan.evict_slots))
+            self.backend.save_blocks(
+                plan.evict_ids, self._native_ext.gather_blocks(self.actual_blocks, plan.evict_slots, check=False))
         if plan.miss_ids.numel() > 0:
             self.backend.load_blocks(plan.miss_ids, self.actual_blocks, plan.victims)
         miss_usage = torch.ones((plan.victims.shape[0],), dtype=USAGE_DTYPE, device=self.actual_blocks.device)
@@ -413,9 +460,10 @@ class KVCacheAdapter:
         """save (adapter.py:205-255) with the planning steps in one device call."""
         plan = self._plan("plan_save", ids)
         if plan.evict_ids.numel() > 0:
-            self.backend.save_blocks(plan.evict_ids, self._native_ext.gather_blocks(self.actual_blocks, plan.evict_slots))
+            self.backend.save_blocks(
+                plan.evict_ids, self._native_ext.gather_blocks(self.actual_blocks, plan.evict_slots, check=False))
         self._native_ext.scatter_blocks(self.actual_blocks, plan.move_slots, block_data.contiguous(),
-                                        skip_negative=True)
+                                        skip_negative=True, check=False)
         self._native_ext.commit_save_metadata(
             self._logical_to_physical, self._physical_to_logical, self._slot_meta, plan.evict_ids, ids,
             plan.selected, plan.final_pins, plan.final_usage, check=False)
@@ -557,10 +605,38 @@ class InMemoryBlockStoreBackend:
         self.save_calls: list[int] = []
         self.load_calls: list[int] = []
         self.operation_log: list[tuple[str, int]] = []
+        self._device_scratch: torch.Tensor | None = None
         self.max_concurrent_saves = 0
         self.max_concurrent_loads = 0
         self._concurrent_saves = 0
         self._concurrent_loads = 0
+
+    def device_store(self, actual_blocks: torch.Tensor):
+        """(storage, present mask, scratch) when loads and saves against this
+        store can run on the device without a host round trip: storage on
+        actual_blocks' GPU with its dtype and block shape, the default op set,
+        no recording of device ids and no delays.  None otherwise."""
+        st = self._storage
+        if (self._ops is not None or self._record_device_ops or self._save_delay_s > 0 or self._load_delay_s > 0
+                or st is None or actual_blocks.device.type != "cuda" or st.device != actual_blocks.device
+                or st.dtype != actual_blocks.dtype or st.shape[1:] != actual_blocks.shape[1:]
+                or not st.is_contiguous()):
+            return None
+        self._ensure_present_mask(device=st.device)
+        scratch = self._device_scratch
+        if scratch is None or scratch.device != st.device:
+            scratch = self._device_scratch = torch.zeros(st.shape[0], dtype=torch.int32, device=st.device)
+        return st, self._present_mask, scratch
+
+    def note_device_ops(self, *, saved: bool, loaded: bool) -> None:
+        """Bookkeeping of a save / load that ran on the device (device ids are
+        not recorded, as for ``record_device_ops=False``)."""
+        if saved:
+            self._enter_save()
+            self._leave_save()
+        if loaded:
+            self._enter_load()
+            self._leave_load()
 
     def _device_ops(self):
         return self._ops if self._ops is not None else _load_cuda_extension_module()

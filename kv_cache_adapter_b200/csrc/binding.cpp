@@ -295,6 +295,103 @@ int kvca_plan_save(int meta_bits, int order, const int64_t* d_l2p, int64_t num_l
       d_evict_ids, d_evict_slots, d_counts, d_status, stream));
 }
 
+// One-plane paged side: slot s at base + s * row_stride.
+static void one_plane(uint64_t base, int64_t rows, int64_t row_stride, const int64_t* index,
+                      kvca::PagedSide* out) {
+  out->planes[0] = base;
+  out->index = index;
+  out->num_blocks = rows;
+  out->block_size = 1;
+  out->block_stride = row_stride;
+  out->row_stride = row_stride;
+}
+
+static bool store_ok(const kvca_device_store* store, uint64_t actual, int64_t actual_row_stride,
+                     int64_t row_bytes) {
+  return store && store->storage && store->present && store->scratch && actual &&
+         row_bytes > 0 && actual_row_stride >= row_bytes && store->storage_row_stride >= row_bytes;
+}
+
+int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+                           int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                           int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                           uint32_t* d_scratch_bitmap, const kvca_device_store* store,
+                           uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
+                           int64_t* d_work, void* d_work_meta, int64_t* d_result,
+                           int64_t* d_counts, int64_t* d_status, kvca_stream_t stream) {
+  if (!plan_args_ok(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
+                    d_search_start, d_ids, count, d_scratch_bitmap, d_counts) ||
+      !store_ok(store, d_actual, actual_row_stride, row_bytes) || !d_work || !d_work_meta ||
+      !d_result)
+    return KVCA_ERR_BAD_ARGUMENT;
+  int rc = status_of(kvca::launch_store_load_meta(
+      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
+      count, d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_result,
+      d_counts, d_status, stream));
+  if (rc != KVCA_OK) return rc;
+  int vec = align_of(static_cast<uint64_t>(row_bytes));
+  vec = min_align(vec, d_actual);
+  vec = min_align(vec, static_cast<uint64_t>(actual_row_stride));
+  vec = min_align(vec, store->storage);
+  vec = min_align(vec, static_cast<uint64_t>(store->storage_row_stride));
+  const int64_t k = count;
+  kvca::PagedSide actual_evicted, store_evicted, store_missed, actual_filled;
+  one_plane(d_actual, num_slots, actual_row_stride, d_work + 5 * k, &actual_evicted);
+  one_plane(store->storage, num_logical, store->storage_row_stride, d_work + 4 * k, &store_evicted);
+  one_plane(store->storage, num_logical, store->storage_row_stride, d_work + 2 * k, &store_missed);
+  one_plane(d_actual, num_slots, actual_row_stride, d_work + 6 * k, &actual_filled);
+  kvca::MoveArgs spill{kvca::MoveKind::kCopyPaged, &actual_evicted, nullptr, &store_evicted,
+                       nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
+  rc = status_of(kvca::launch_move(spill, stream));
+  if (rc != KVCA_OK) return rc;
+  kvca::MoveArgs fill{kvca::MoveKind::kCopyPaged, &store_missed, nullptr, &actual_filled,
+                      nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
+  return status_of(kvca::launch_move(fill, stream));
+}
+
+int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+                           int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                           int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                           uint32_t* d_scratch_bitmap, const kvca_device_store* store,
+                           uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
+                           uint64_t d_block_data, int64_t* d_work, void* d_work_meta,
+                           int64_t* d_counts, int64_t* d_status, kvca_stream_t stream) {
+  if (!plan_args_ok(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
+                    d_search_start, d_ids, count, d_scratch_bitmap, d_counts) ||
+      !store_ok(store, d_actual, actual_row_stride, row_bytes) || !d_block_data || !d_work ||
+      !d_work_meta)
+    return KVCA_ERR_BAD_ARGUMENT;
+  int rc = status_of(kvca::launch_store_save_meta(
+      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
+      count, d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_counts,
+      d_status, stream));
+  if (rc != KVCA_OK) return rc;
+  int vec = align_of(static_cast<uint64_t>(row_bytes));
+  vec = min_align(vec, d_actual);
+  vec = min_align(vec, static_cast<uint64_t>(actual_row_stride));
+  vec = min_align(vec, store->storage);
+  vec = min_align(vec, static_cast<uint64_t>(store->storage_row_stride));
+  vec = min_align(vec, d_block_data);
+  const int64_t k = count;
+  kvca::PagedSide actual_evicted, store_evicted, actual_selected;
+  one_plane(d_actual, num_slots, actual_row_stride, d_work + 3 * k, &actual_evicted);
+  one_plane(store->storage, num_logical, store->storage_row_stride, d_work + 2 * k, &store_evicted);
+  one_plane(d_actual, num_slots, actual_row_stride, d_work + 4 * k, &actual_selected);
+  kvca::MoveArgs spill{kvca::MoveKind::kCopyPaged, &actual_evicted, nullptr, &store_evicted,
+                       nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
+  rc = status_of(kvca::launch_move(spill, stream));
+  if (rc != KVCA_OK) return rc;
+  kvca::ChunkSide data;
+  data.base = d_block_data;
+  data.rows_per_chunk = k;
+  data.chunk_stride = k * row_bytes;
+  data.row_stride = row_bytes;
+  data.plane_stride = k * row_bytes;
+  kvca::MoveArgs scatter{kvca::MoveKind::kScatter, nullptr, &data, &actual_selected, nullptr, 1,
+                         k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
+  return status_of(kvca::launch_move(scatter, stream));
+}
+
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,
                 int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
                 kvca_stream_t stream) {

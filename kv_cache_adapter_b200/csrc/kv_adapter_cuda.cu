@@ -989,22 +989,20 @@ __device__ void scatter_last_wins(int64_t* l2p, const int64_t* ids, const int64_
       l2p[ids[i]] = slots[i];
 }
 
-// One CTA, phases separated by barriers so each phase sees the previous one.
+// Commit bodies, run by one CTA, phases separated by barriers so each phase
+// sees the previous one.  `bad` is a zeroed shared flag.
 template <typename MetaT>
-__global__ void __launch_bounds__(1024)
-    commit_load_kernel(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
-                       int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
-                       const int64_t* miss_ids, const int64_t* miss_slots, int64_t num_miss,
-                       const int64_t* hit_slots, const int64_t* hit_pins, const MetaT* hit_usage,
-                       int64_t num_hit, const MetaT* miss_usage, int64_t* status) {
+__device__ void commit_load_body(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
+                                 int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
+                                 const int64_t* miss_ids, const int64_t* miss_slots,
+                                 int64_t num_miss, const int64_t* hit_slots,
+                                 const int64_t* hit_pins, const MetaT* hit_usage, int64_t num_hit,
+                                 const MetaT* miss_usage, int64_t* status, int* bad) {
   using M = Meta<MetaT>;
-  __shared__ int bad;
-  if (threadIdx.x == 0) bad = 0;
-  __syncthreads();
-  if (!all_in_range(evicted, num_evicted, num_logical, status, &bad)) return;
-  if (!all_in_range(miss_ids, num_miss, num_logical, status, &bad)) return;
-  if (!all_in_range(miss_slots, num_miss, num_slots, status, &bad)) return;
-  if (!all_in_range(hit_slots, num_hit, num_slots, status, &bad)) return;
+  if (!all_in_range(evicted, num_evicted, num_logical, status, bad)) return;
+  if (!all_in_range(miss_ids, num_miss, num_logical, status, bad)) return;
+  if (!all_in_range(miss_slots, num_miss, num_slots, status, bad)) return;
+  if (!all_in_range(hit_slots, num_hit, num_slots, status, bad)) return;
   for (int64_t i = threadIdx.x; i < num_evicted; i += blockDim.x) l2p[evicted[i]] = -1;
   __syncthreads();
   scatter_last_wins(l2p, miss_ids, miss_slots, num_miss);
@@ -1013,23 +1011,21 @@ __global__ void __launch_bounds__(1024)
   for (int64_t i = threadIdx.x; i < num_hit; i += blockDim.x)
     meta[hit_slots[i]] = M::pack(hit_pins[i], hit_usage[i]);
   __syncthreads();
+  // no miss_usage: every miss takes usage 1, as KVCacheAdapter.load passes it
   for (int64_t i = threadIdx.x; i < num_miss; i += blockDim.x)
-    meta[miss_slots[i]] = M::pack(1, miss_usage[i]);
+    meta[miss_slots[i]] = M::pack(1, miss_usage != nullptr ? miss_usage[i] : MetaT(1));
 }
 
 template <typename MetaT>
-__global__ void __launch_bounds__(1024)
-    commit_save_kernel(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
-                       int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
-                       const int64_t* ids, const int64_t* slots, const MetaT* final_pins,
-                       const MetaT* final_usage, int64_t count, int64_t* status) {
+__device__ void commit_save_body(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
+                                 int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
+                                 const int64_t* ids, const int64_t* slots, const MetaT* final_pins,
+                                 const MetaT* final_usage, int64_t count, int64_t* status,
+                                 int* bad) {
   using M = Meta<MetaT>;
-  __shared__ int bad;
-  if (threadIdx.x == 0) bad = 0;
-  __syncthreads();
-  if (!all_in_range(evicted, num_evicted, num_logical, status, &bad)) return;
-  if (!all_in_range(ids, count, num_logical, status, &bad)) return;
-  if (!all_in_range(slots, count, num_slots, status, &bad)) return;
+  if (!all_in_range(evicted, num_evicted, num_logical, status, bad)) return;
+  if (!all_in_range(ids, count, num_logical, status, bad)) return;
+  if (!all_in_range(slots, count, num_slots, status, bad)) return;
   for (int64_t i = threadIdx.x; i < num_evicted; i += blockDim.x) l2p[evicted[i]] = -1;
   __syncthreads();
   scatter_last_wins(l2p, ids, slots, count);
@@ -1038,6 +1034,34 @@ __global__ void __launch_bounds__(1024)
     p2l[slots[i]] = ids[i];
     meta[slots[i]] = M::pack(final_pins[i], final_usage[i]);
   }
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    commit_load_kernel(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
+                       int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
+                       const int64_t* miss_ids, const int64_t* miss_slots, int64_t num_miss,
+                       const int64_t* hit_slots, const int64_t* hit_pins, const MetaT* hit_usage,
+                       int64_t num_hit, const MetaT* miss_usage, int64_t* status) {
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  commit_load_body<MetaT>(l2p, num_logical, p2l, meta, num_slots, evicted, num_evicted, miss_ids,
+                          miss_slots, num_miss, hit_slots, hit_pins, hit_usage, num_hit,
+                          miss_usage, status, &bad);
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    commit_save_kernel(int64_t* l2p, int64_t num_logical, int64_t* p2l, MetaT* meta,
+                       int64_t num_slots, const int64_t* evicted, int64_t num_evicted,
+                       const int64_t* ids, const int64_t* slots, const MetaT* final_pins,
+                       const MetaT* final_usage, int64_t count, int64_t* status) {
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  commit_save_body<MetaT>(l2p, num_logical, p2l, meta, num_slots, evicted, num_evicted, ids,
+                          slots, final_pins, final_usage, count, status, &bad);
 }
 
 constexpr int kReleasePerThread = 8;
@@ -1115,6 +1139,14 @@ __device__ __forceinline__ void plan_fail(int64_t* counts, int64_t* status, int 
   report(status, code, value);
 }
 
+// counts[5..6] take the status word as the plan finds it, so that the one
+// read of counts also reports an error latched by an earlier unchecked launch.
+__device__ __forceinline__ void plan_begin(int64_t* counts, const int64_t* status) {
+  counts[3] = counts[4] = 0;
+  counts[5] = status[0];
+  counts[6] = status[1];
+}
+
 // Validates ids and their current slots; returns false (uniformly) on a bad id.
 template <typename MetaT>
 __device__ bool plan_validate(const int64_t* l2p, int64_t n_logical, int64_t n, const int64_t* ids,
@@ -1156,7 +1188,7 @@ __global__ void __launch_bounds__(1024)
                      int64_t* evict_slots, int64_t* counts, int64_t* status) {
   using M = Meta<MetaT>;
   __shared__ PlanShared<MetaT> sh;
-  if (threadIdx.x == 0) counts[3] = counts[4] = 0;
+  if (threadIdx.x == 0) plan_begin(counts, status);
   if (!plan_validate<MetaT>(l2p, n_logical, n, ids, k, counts, status, sh)) return;
   // hits and misses in request order; the hit slots are blocked for the pop
   int64_t nh = 0, nm = 0;
@@ -1240,7 +1272,7 @@ __global__ void __launch_bounds__(1024)
   using M = Meta<MetaT>;
   __shared__ PlanShared<MetaT> sh;
   if (threadIdx.x == 0) {
-    counts[3] = counts[4] = 0;
+    plan_begin(counts, status);
     sh.repeated = 0;
   }
   if (!plan_validate<MetaT>(l2p, n_logical, n, ids, k, counts, status, sh)) return;
@@ -1336,6 +1368,94 @@ __global__ void __launch_bounds__(1024)
     counts[1] = nm;
     counts[2] = ne;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Device-resident block store: the metadata half of a load / save after the
+// plan, with no host round trip in between
+// ---------------------------------------------------------------------------
+//
+// The store is the in-memory backend's (adapter.py:679-833) with its storage
+// on this GPU: row l of `storage` holds logical block l, present[l] != 0 once
+// it was saved.  A fused load runs plan_load, then store_load_finish, then
+// the spill copy (actual[evict_slots] -> storage[evict_ids]) and the fill
+// copy (storage[miss_ids] -> actual[load_slots]); a fused save runs
+// plan_save, store_save_finish, the spill copy and the data scatter.  The
+// finish kernels read the plan's counts from device memory.
+
+// Spill preparation: among repeated evicted ids only the last occurrence
+// keeps its slot (the others get -1, so the spill copy skips them and leaves
+// the payload index_copy_ applied in order leaves), and every evicted id is
+// marked present.  `scratch` (one int per logical id) is zero on entry and
+// left zero.  Ends with a barrier.
+__device__ void store_spill_prepare(const int64_t* evict_ids, int64_t* evict_slots, int64_t ne,
+                                    int32_t* scratch, uint8_t* present) {
+  for (int64_t j = threadIdx.x; j < ne; j += blockDim.x)
+    atomicMax(scratch + evict_ids[j], static_cast<int32_t>(j + 1));
+  __syncthreads();
+  for (int64_t j = threadIdx.x; j < ne; j += blockDim.x)
+    if (__ldcg(scratch + evict_ids[j]) != static_cast<int32_t>(j + 1)) evict_slots[j] = -1;
+  __syncthreads();
+  for (int64_t j = threadIdx.x; j < ne; j += blockDim.x) {
+    scratch[evict_ids[j]] = 0;
+    present[evict_ids[j]] = 1;
+  }
+  __syncthreads();
+}
+
+// After plan_load: spill preparation, then the backend's presence check of
+// the misses (adapter.py:801-806); when every miss is present, the slots to
+// fill (load_slots = victims) and the commit.  A missing block sets
+// counts[3..4] = KVCA_ERR_BLOCK_NOT_FOUND, id and leaves load_slots at -1:
+// the evictions stay spilled, nothing is filled or committed, as when the
+// backend raises.  Nothing runs when the plan failed.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    store_load_finish_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
+                             int64_t* counts, const int64_t* hit_slots, const int64_t* hit_pins,
+                             const MetaT* hit_usage, const int64_t* miss_ids,
+                             const int64_t* victims, const int64_t* evict_ids,
+                             int64_t* evict_slots, int32_t* scratch, uint8_t* present,
+                             int64_t* load_slots, int64_t* status) {
+  __shared__ int bad;
+  __shared__ int missing;
+  __shared__ long long missing_id;
+  if (counts[3] != 0) return;  // written by the plan launch: uniform
+  const int64_t nh = counts[0], nm = counts[1], ne = counts[2];
+  if (threadIdx.x == 0) bad = missing = 0;
+  store_spill_prepare(evict_ids, evict_slots, ne, scratch, present);
+  for (int64_t j = threadIdx.x; j < nm; j += blockDim.x)
+    if (present[miss_ids[j]] == 0 && atomicCAS(&missing, 0, 1) == 0) missing_id = miss_ids[j];
+  __syncthreads();
+  if (missing) {
+    if (threadIdx.x == 0) {
+      counts[3] = KVCA_ERR_BLOCK_NOT_FOUND;
+      counts[4] = missing_id;
+    }
+    return;
+  }
+  for (int64_t j = threadIdx.x; j < nm; j += blockDim.x) load_slots[j] = victims[j];
+  commit_load_body<MetaT>(l2p, n_logical, p2l, meta, n, evict_ids, ne, miss_ids, victims, nm,
+                          hit_slots, hit_pins, hit_usage, nh, nullptr, status, &bad);
+}
+
+// After plan_save: spill preparation and the commit.  Nothing runs when the
+// plan failed.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    store_save_finish_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
+                             int64_t* counts, const int64_t* ids, int64_t k,
+                             const int64_t* selected, const MetaT* final_pins,
+                             const MetaT* final_usage, const int64_t* evict_ids,
+                             int64_t* evict_slots, int32_t* scratch, uint8_t* present,
+                             int64_t* status) {
+  __shared__ int bad;
+  if (counts[3] != 0) return;
+  const int64_t ne = counts[2];
+  if (threadIdx.x == 0) bad = 0;
+  store_spill_prepare(evict_ids, evict_slots, ne, scratch, present);
+  commit_save_body<MetaT>(l2p, n_logical, p2l, meta, n, evict_ids, ne, ids, selected, final_pins,
+                          final_usage, k, status, &bad);
 }
 
 // ---------------------------------------------------------------------------
@@ -1883,6 +2003,67 @@ cudaError_t launch_plan_save(int meta_bits, int order, const int64_t* l2p, int64
                                     move_slots, static_cast<MetaT*>(final_pins),
                                     static_cast<MetaT*>(final_usage),
                                     allocated, evict_ids, evict_slots, counts, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_store_load_meta(int meta_bits, int order, int64_t* l2p, int64_t num_logical,
+                                   int64_t* p2l, void* meta, int64_t num_slots,
+                                   int64_t* search_start, const int64_t* ids, int64_t count,
+                                   uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                   int64_t* work, void* work_meta, int64_t* result,
+                                   int64_t* counts, int64_t* status, cudaStream_t stream) {
+  const int64_t k = count;
+  int64_t* hit_slots = work;
+  int64_t* hit_pins = work + k;
+  int64_t* miss_ids = work + 2 * k;
+  int64_t* victims = work + 3 * k;
+  int64_t* evict_ids = work + 4 * k;
+  int64_t* evict_slots = work + 5 * k;
+  int64_t* load_slots = work + 6 * k;
+  // miss_ids, evict_ids, evict_slots and load_slots index the copies: -1
+  // (skipped, no error) wherever the plan or the finish kernel writes nothing
+  cudaError_t e = cudaMemsetAsync(miss_ids, 0xFF, 5 * k * sizeof(int64_t), stream);
+  if (e != cudaSuccess) return e;
+  e = launch_plan_load(meta_bits, order, l2p, num_logical, p2l, meta, num_slots, search_start, ids,
+                       count, bitmap, result, hit_slots, hit_pins, work_meta, miss_ids, victims,
+                       evict_ids, evict_slots, counts, status, stream);
+  if (e != cudaSuccess) return e;
+  KVCA_META_DISPATCH(meta_bits, store_load_finish_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
+                                    counts, hit_slots, hit_pins,
+                                    static_cast<const MetaT*>(work_meta), miss_ids, victims,
+                                    evict_ids, evict_slots, scratch, present, load_slots, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_store_save_meta(int meta_bits, int order, int64_t* l2p, int64_t num_logical,
+                                   int64_t* p2l, void* meta, int64_t num_slots,
+                                   int64_t* search_start, const int64_t* ids, int64_t count,
+                                   uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                   int64_t* work, void* work_meta, int64_t* counts,
+                                   int64_t* status, cudaStream_t stream) {
+  const int64_t k = count;
+  int64_t* selected = work;
+  int64_t* allocated = work + k;
+  int64_t* evict_ids = work + 2 * k;
+  int64_t* evict_slots = work + 3 * k;
+  int64_t* move_slots = work + 4 * k;
+  const size_t wsz = meta_bits == 8 ? 1 : 2;
+  void* final_pins = work_meta;
+  void* final_usage = static_cast<char*>(work_meta) + k * wsz;
+  // evict_ids, evict_slots and move_slots index the copies: -1 where unwritten
+  cudaError_t e = cudaMemsetAsync(evict_ids, 0xFF, 3 * k * sizeof(int64_t), stream);
+  if (e != cudaSuccess) return e;
+  e = launch_plan_save(meta_bits, order, l2p, num_logical, p2l, meta, num_slots, search_start, ids,
+                       count, bitmap, selected, move_slots, final_pins, final_usage, allocated,
+                       evict_ids, evict_slots, counts, status, stream);
+  if (e != cudaSuccess) return e;
+  KVCA_META_DISPATCH(meta_bits, store_save_finish_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
+                                    counts, ids, count, selected,
+                                    static_cast<const MetaT*>(final_pins),
+                                    static_cast<const MetaT*>(final_usage), evict_ids,
+                                    evict_slots, scratch, present, status));
   return cudaGetLastError();
 }
 

@@ -112,4 +112,24 @@ cudaError_t launch_plan_save(int meta_bits, int order, const int64_t* l2p, int64
                              int64_t* evict_ids, int64_t* evict_slots, int64_t* counts,
                              int64_t* status, cudaStream_t stream);
 
+// Fused load / save with a device-resident block store: memset, plan, finish
+// (metadata); the caller then enqueues the two row copies.  Work layouts:
+// load  int64 [hit_slots, hit_pins, miss_ids, victims, evict_ids, evict_slots,
+//              load_slots] x count, meta [hit_usage] x count;
+// save  int64 [selected, allocated, evict_ids, evict_slots, move_slots] x count,
+//       meta [final_pins, final_usage] x count.
+cudaError_t launch_store_load_meta(int meta_bits, int order, int64_t* l2p, int64_t num_logical,
+                                   int64_t* p2l, void* meta, int64_t num_slots,
+                                   int64_t* search_start, const int64_t* ids, int64_t count,
+                                   uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                   int64_t* work, void* work_meta, int64_t* result,
+                                   int64_t* counts, int64_t* status, cudaStream_t stream);
+
+cudaError_t launch_store_save_meta(int meta_bits, int order, int64_t* l2p, int64_t num_logical,
+                                   int64_t* p2l, void* meta, int64_t num_slots,
+                                   int64_t* search_start, const int64_t* ids, int64_t count,
+                                   uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                   int64_t* work, void* work_meta, int64_t* counts,
+                                   int64_t* status, cudaStream_t stream);
+
 }  // namespace kvca

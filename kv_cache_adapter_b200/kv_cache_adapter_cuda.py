@@ -18,6 +18,7 @@ next check or ``check_status()``.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 import os
@@ -26,7 +27,7 @@ from typing import Sequence
 import torch
 
 from . import _lib
-from .errors import InsufficientCapacityError
+from .errors import BlockNotFoundError, InsufficientCapacityError
 
 __all__ = [
     "pop_reusable_slots",
@@ -46,6 +47,8 @@ __all__ = [
     "scatter_tokens",
     "plan_load",
     "plan_save",
+    "load_device_store",
+    "save_device_store",
     "check_status",
     "library_path",
     "PlaneTable",
@@ -76,8 +79,24 @@ def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr())
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
 def _stream(device: torch.device) -> ctypes.c_void_p:
+    if _raw_stream is not None:
+        return ctypes.c_void_p(_raw_stream(_index(device)))
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _on(device: torch.device):
+    """The device's context for a launch (no switch when it is current)."""
+    if _index(device) == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def _status(device: torch.device) -> torch.Tensor:
@@ -98,6 +117,8 @@ def _raise_for(code: int, value: int, what: str) -> None:
         raise IndexError(f"{what}: index {value} is out of range")
     if code == _lib.KVCA_ERR_BAD_ARGUMENT:
         raise ValueError(f"{what}: invalid arguments")
+    if code == _lib.KVCA_ERR_BLOCK_NOT_FOUND:
+        raise BlockNotFoundError("some logical blocks are not in backend")
     if code == _lib.KVCA_ERR_DEVICE_TIMEOUT:
         raise RuntimeError(f"{what}: a bounded device-side wait gave up (CTA {value})")
     raise RuntimeError(f"{what}: CUDA launch failed (code {code})")
@@ -168,7 +189,7 @@ def inspect_load_requests(logical_to_physical: torch.Tensor, slot_meta: torch.Te
     resident = torch.empty(k, dtype=torch.bool, device=dev)
     pins = torch.empty(k, dtype=torch.int64, device=dev)
     usage = torch.empty(k, dtype=slot_meta.dtype, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_inspect_load_requests(
             _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
             _ptr(slot_meta), slot_meta.numel(), _ptr(logical_block_ids), k, _ptr(cur),
@@ -189,7 +210,7 @@ def inspect_save_requests(logical_to_physical: torch.Tensor, slot_meta: torch.Te
     cur = torch.empty(k, dtype=torch.int64, device=dev)
     existing = torch.empty(k, dtype=torch.bool, device=dev)
     usage = torch.empty(k, dtype=slot_meta.dtype, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_inspect_save_requests(
             _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
             _ptr(slot_meta), slot_meta.numel(), _ptr(logical_block_ids), k, _ptr(cur),
@@ -239,7 +260,7 @@ def pop_reusable_slots(slot_meta: torch.Tensor, search_start: torch.Tensor,
         raise InsufficientCapacityError(
             "No reusable actual block is available; all resident blocks are pinned")
     order_code = POP_ORDERS[order or _DEFAULT_POP_ORDER]
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_pop_reusable_slots(
             _meta_bits(slot_meta), order_code, _ptr(slot_meta), n, _ptr(search_start),
             _ptr(blocked_slot_ids), blocked_slot_ids.numel(), count, _ptr(out),
@@ -278,7 +299,7 @@ def commit_load_metadata(logical_to_physical, physical_to_logical, slot_meta,
         raise ValueError("miss ids, slots and usage counts must have the same length")
     if hit_pin_counts.numel() != hit_slot_ids.numel() or hit_usage_counts.numel() != hit_slot_ids.numel():
         raise ValueError("hit slots, pins and usage counts must have the same length")
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_commit_load_metadata(
             _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
             _ptr(physical_to_logical), _ptr(slot_meta), slot_meta.numel(),
@@ -307,7 +328,7 @@ def commit_save_metadata(logical_to_physical, physical_to_logical, slot_meta,
     k = logical_block_ids.numel()
     if physical_slot_ids.numel() != k or final_pin_counts.numel() != k or final_usage_counts.numel() != k:
         raise ValueError("ids, slots, pins and usage counts must have the same length")
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_commit_save_metadata(
             _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
             _ptr(physical_to_logical), _ptr(slot_meta), slot_meta.numel(),
@@ -324,7 +345,7 @@ def release_metadata(logical_to_physical, slot_meta, logical_block_ids, *,
     _require(slot_meta, _META_DTYPES, "slot_meta")
     _require(logical_block_ids, torch.int64, "logical_block_ids")
     dev = slot_meta.device
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_release_metadata(
             _meta_bits(slot_meta), _ptr(logical_to_physical), logical_to_physical.numel(),
             _ptr(slot_meta), slot_meta.numel(), _ptr(logical_block_ids), logical_block_ids.numel(),
@@ -372,7 +393,7 @@ def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps:
             raise ValueError("victims is too small")
     steps_done = torch.zeros(1, dtype=torch.int64, device=dev)
     order_code = POP_ORDERS[order or _DEFAULT_POP_ORDER]
-    with torch.cuda.device(dev):
+    with _on(dev):
         if method == "batched":
             rc = _lib_handle.kvca_clock_stream_batched(
                 _meta_bits(slot_meta), order_code, _ptr(slot_meta), slot_meta.numel(), _ptr(search_start),
@@ -412,10 +433,18 @@ class SavePlan:
 
 
 def _plan_counts(counts: torch.Tensor, what: str) -> list[int]:
-    vals = counts.tolist()  # the call's only synchronisation
-    if vals[3] != 0:
+    """The call's only synchronisation: the plan's counts, its error, and an
+    error latched earlier by an unchecked launch (raised first)."""
+    vals = counts.tolist()
+    if vals[5] != 0 or vals[3] != 0:
         _status(counts.device).zero_()
-        _raise_for(int(vals[3]), int(vals[4]), what)
+        if vals[5] != 0:
+            _raise_for(int(vals[5]), int(vals[6]), "an earlier unchecked launch")
+        try:
+            _raise_for(int(vals[3]), int(vals[4]), what)
+        except BlockNotFoundError as exc:
+            exc.counts = vals  # the plan's counts: the spill has run
+            raise
     return vals
 
 
@@ -433,9 +462,9 @@ def plan_load(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tens
     k = logical_block_ids.numel()
     buf = torch.empty((7, k), dtype=torch.int64, device=dev)
     hit_usage = torch.empty(k, dtype=slot_meta.dtype, device=dev)
-    counts = torch.empty(5, dtype=torch.int64, device=dev)
+    counts = torch.empty(7, dtype=torch.int64, device=dev)
     n = slot_meta.numel()
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_plan_load(
             _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
             logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
@@ -462,9 +491,9 @@ def plan_save(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tens
     k = logical_block_ids.numel()
     buf = torch.empty((5, k), dtype=torch.int64, device=dev)
     small = torch.empty((2, k), dtype=slot_meta.dtype, device=dev)
-    counts = torch.empty(5, dtype=torch.int64, device=dev)
+    counts = torch.empty(7, dtype=torch.int64, device=dev)
     n = slot_meta.numel()
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = _lib_handle.kvca_plan_save(
             _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
             logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
@@ -475,6 +504,91 @@ def plan_save(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tens
     nx, nm, ne = _plan_counts(counts, "plan_save")[:3]
     return SavePlan(selected=buf[0], move_slots=buf[4], final_pins=small[0], final_usage=small[1],
                     allocated=buf[1, :nm], evict_ids=buf[2, :ne], evict_slots=buf[3, :ne])
+
+
+def _rows_of(t: torch.Tensor, name: str) -> tuple[int, int]:
+    """(row stride, row bytes) of a tensor whose dim 0 indexes dense rows."""
+    if not _dense_suffix(t, 1):
+        raise ValueError(f"{name}: each row must be contiguous")
+    esz = t.element_size()
+    return int(t.stride(0)) * esz, int(math.prod(t.shape[1:])) * esz
+
+
+def _store_desc(storage: torch.Tensor, present: torch.Tensor, scratch: torch.Tensor,
+                actual_blocks: torch.Tensor) -> tuple[_lib.DeviceStore, int, int]:
+    if storage.device != actual_blocks.device or storage.dtype != actual_blocks.dtype \
+            or storage.shape[1:] != actual_blocks.shape[1:]:
+        raise ValueError("storage and actual_blocks must share device, dtype and block shape")
+    _require(present, torch.bool, "present")
+    _require(scratch, torch.int32, "scratch")
+    n_logical = storage.shape[0]
+    if present.numel() != n_logical or scratch.numel() != n_logical:
+        raise ValueError("present and scratch need one entry per stored block")
+    s_stride, row_bytes = _rows_of(storage, "storage")
+    a_stride, _ = _rows_of(actual_blocks, "actual_blocks")
+    return _lib.DeviceStore(storage.data_ptr(), s_stride, present.data_ptr(), scratch.data_ptr()), a_stride, row_bytes
+
+
+def load_device_store(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor, slot_meta: torch.Tensor,
+                      search_start: torch.Tensor, logical_block_ids: torch.Tensor, actual_blocks: torch.Tensor,
+                      storage: torch.Tensor, present: torch.Tensor, scratch: torch.Tensor, *,
+                      order: str | None = None) -> tuple[torch.Tensor, list[int]]:
+    """KVCacheAdapter.load against a block store on the same GPU (storage row
+    l = logical block l): plan, spill, presence check, fill and commit as one
+    enqueued sequence, then one read of the counts.  Returns (slots, counts);
+    raises InsufficientCapacityError / BlockNotFoundError / IndexError with
+    the reference's state effects."""
+    for t, name in ((logical_to_physical, "logical_to_physical"), (physical_to_logical, "physical_to_logical"),
+                    (search_start, "search_start"), (logical_block_ids, "logical_block_ids")):
+        _require(t, torch.int64, name)
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    desc, a_stride, row_bytes = _store_desc(storage, present, scratch, actual_blocks)
+    dev = slot_meta.device
+    k = logical_block_ids.numel()
+    n = slot_meta.numel()
+    work = torch.empty(7 * k, dtype=torch.int64, device=dev)
+    work_meta = torch.empty(k, dtype=slot_meta.dtype, device=dev)
+    result = torch.empty(k, dtype=torch.int64, device=dev)
+    counts = torch.empty(7, dtype=torch.int64, device=dev)
+    with _on(dev):
+        rc = _lib_handle.kvca_load_device_store(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
+            logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
+            _ptr(logical_block_ids), k, _ptr(_bitmap(dev, n)), ctypes.byref(desc), actual_blocks.data_ptr(),
+            a_stride, row_bytes, _ptr(work), _ptr(work_meta), _ptr(result), _ptr(counts), _ptr(_status(dev)),
+            _stream(dev))
+    _host_rc(rc, "load_device_store")
+    return result, _plan_counts(counts, "load_device_store")
+
+
+def save_device_store(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor, slot_meta: torch.Tensor,
+                      search_start: torch.Tensor, logical_block_ids: torch.Tensor, block_data: torch.Tensor,
+                      actual_blocks: torch.Tensor, storage: torch.Tensor, present: torch.Tensor,
+                      scratch: torch.Tensor, *, order: str | None = None) -> list[int]:
+    """KVCacheAdapter.save against a block store on the same GPU: plan, spill,
+    commit and data scatter as one enqueued sequence, then one read of the
+    counts (returned)."""
+    for t, name in ((logical_to_physical, "logical_to_physical"), (physical_to_logical, "physical_to_logical"),
+                    (search_start, "search_start"), (logical_block_ids, "logical_block_ids")):
+        _require(t, torch.int64, name)
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    desc, a_stride, row_bytes = _store_desc(storage, present, scratch, actual_blocks)
+    dev = slot_meta.device
+    k = logical_block_ids.numel()
+    _chunk_tensor(block_data, (k, *actual_blocks.shape[1:]), actual_blocks.dtype, dev, "block_data")
+    n = slot_meta.numel()
+    work = torch.empty(5 * k, dtype=torch.int64, device=dev)
+    work_meta = torch.empty(2 * k, dtype=slot_meta.dtype, device=dev)
+    counts = torch.empty(7, dtype=torch.int64, device=dev)
+    with _on(dev):
+        rc = _lib_handle.kvca_save_device_store(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
+            logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
+            _ptr(logical_block_ids), k, _ptr(_bitmap(dev, n)), ctypes.byref(desc), actual_blocks.data_ptr(),
+            a_stride, row_bytes, block_data.data_ptr(), _ptr(work), _ptr(work_meta), _ptr(counts),
+            _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "save_device_store")
+    return _plan_counts(counts, "save_device_store")
 
 
 # ---------------------------------------------------------------------------
@@ -541,11 +655,27 @@ class PlaneTable:
             ctypes.c_void_p(index.data_ptr()) if index is not None and index.numel() else None)
 
 
+_single_plane_tables: dict[tuple, PlaneTable] = {}
+
+
 def _planes(caches, row_dim: int, name: str) -> PlaneTable:
     if isinstance(caches, PlaneTable):
         if caches.row_dim != row_dim:
             raise ValueError(f"{name}: plane table built for row_dim {caches.row_dim}, need {row_dim}")
         return caches
+    if isinstance(caches, (list, tuple)) and len(caches) == 1 and isinstance(caches[0], torch.Tensor):
+        # One-plane tables (actual_blocks, backend storage) are rebuilt on every
+        # call otherwise; the table depends only on address, layout and dtype.
+        t = caches[0]
+        key = (t.data_ptr(), tuple(t.shape), t.stride(), t.dtype, t.device, row_dim)
+        table = _single_plane_tables.get(key)
+        if table is None:
+            table = PlaneTable(caches, row_dim, name)
+            table.planes = [None]  # no reference kept: the cache must not hold memory alive
+            if len(_single_plane_tables) >= 64:
+                _single_plane_tables.clear()
+            _single_plane_tables[key] = table
+        return table
     return PlaneTable(caches, row_dim, name)
 
 
@@ -565,7 +695,7 @@ def _launch_move(fn_name: str, src, dst, num_planes: int, num_rows: int, row_byt
                  flags: int, device: torch.device, check: bool | None) -> None:
     if num_rows == 0:
         return
-    with torch.cuda.device(device):
+    with _on(device):
         rc = getattr(_lib_handle, fn_name)(
             ctypes.byref(src), ctypes.byref(dst), num_planes, num_rows, row_bytes, flags,
             _ptr(_status(device)), _stream(device))

@@ -43,11 +43,18 @@ def backend_with(api, rows: dict[int, list[float]], **kw):
     return api.InMemoryBlockStoreBackend({k: _payload(v) for k, v in rows.items()}, record_device_ops=True, **kw)
 
 
-@pytest.mark.parametrize("planned", [True, False])
+@pytest.mark.parametrize("path", ["device_store", "planned", "stepwise"])
 @pytest.mark.parametrize("case_index", range(60))
-def test_recorded_reference_scenarios(case_index, planned):
+def test_recorded_reference_scenarios(case_index, path):
+    """device_store: plan, spill, fill and commit enqueued with one host read
+    (the backend's storage lives on the GPU once it has any block); planned:
+    one-launch plan, then the backend calls; stepwise: inspect, pop, commit as
+    separate launches."""
     case = scenario_runner.load_scenarios()[case_index]
-    scenario_runner.run_and_compare(case, DEV, planned=planned)
+    scenario_runner.run_and_compare(case, DEV, planned=path != "stepwise", record=path != "device_store")
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda
+
+    kv_cache_adapter_cuda.check_status(DEV)  # nothing latched by the unchecked launches
 
 
 def test_runtime_path_and_native_library_loaded(api):

@@ -229,19 +229,22 @@ def test_save_with_repeated_ids_keeps_last_row(api_gpu):
         ad.release(torch.tensor([5, 6, 7], dtype=torch.int64, device=DEV))
 
 
+@pytest.mark.parametrize("path", ["device_store", "planned"])
 @pytest.mark.parametrize("seed,num_actual,num_logical,max_batch", [
     (1, 4, 16, 4),
     (2, 64, 256, 48),
     (3, 1000, 4000, 700),
     (4, 3000, 20000, 2500),
 ])
-def test_planned_adapter_matches_oracle_adapter(api_gpu, seed, num_actual, num_logical, max_batch):
-    """Random load / save / release programs with duplicates, pin pressure and
-    capacity errors: the planned CUDA adapter and the oracle-backed CPU
+def test_planned_adapter_matches_oracle_adapter(api_gpu, seed, num_actual, num_logical, max_batch, path):
+    """Random load / save / release programs with duplicates, pin pressure,
+    capacity errors and blocks missing from the store: the CUDA adapter (store
+    driven on the device, or plan + backend calls) and the oracle-backed CPU
     adapter agree on every result, error and the full state after each op."""
     rng = np.random.default_rng(seed)
     shape = (2, 3)
-    init = {i: torch.full(shape, float(i)) for i in range(num_logical)}
+    # a few logical blocks are in no store: loading them raises BlockNotFoundError
+    init = {i: torch.full(shape, float(i)) for i in range(num_logical) if i % 17 != 5}
     cpu_ops = OracleOps()
     ref = adapter_mod.KVCacheAdapter(
         num_actual, num_logical, torch.zeros((num_actual, *shape)),
@@ -250,8 +253,9 @@ def test_planned_adapter_matches_oracle_adapter(api_gpu, seed, num_actual, num_l
     gpu = adapter_mod.KVCacheAdapter(
         num_actual, num_logical, torch.zeros((num_actual, *shape), device=DEV),
         adapter_mod.InMemoryBlockStoreBackend({k: v.to(DEV) for k, v in init.items()},
-                                              num_logical_blocks=num_logical))
+                                              num_logical_blocks=num_logical, record_device_ops=path == "planned"))
     assert gpu._planned and not ref._planned
+    assert (gpu._device_store() is not None) == (path == "device_store")
     pinned: list[int] = []
     for step in range(60):
         op = rng.choice(["load", "save", "release"], p=[0.45, 0.3, 0.25])
@@ -282,6 +286,36 @@ def test_planned_adapter_matches_oracle_adapter(api_gpu, seed, num_actual, num_l
         for name in ("_logical_to_physical", "_physical_to_logical", "_slot_meta", "_search_start"):
             assert torch.equal(getattr(gpu, name).cpu(), getattr(ref, name)), (step, op, name)
         assert torch.equal(gpu.actual_blocks.cpu(), ref.actual_blocks), (step, op)
+        assert torch.equal(gpu.backend._storage.cpu(), ref.backend._storage), (step, op)
+        assert torch.equal(gpu.backend._present_mask.cpu(), ref.backend._present_mask), (step, op)
+    if path == "device_store":
+        assert int(gpu.backend._device_scratch.count_nonzero()) == 0
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda
+
+    kv_cache_adapter_cuda.check_status(DEV)
+
+
+def test_device_store_path_runs_one_sequence(api_gpu, monkeypatch):
+    """With a store on the GPU, load and save call the device-store entry
+    points and nothing else of the op set but release."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ext
+
+    backend = api_gpu.InMemoryBlockStoreBackend(
+        {i: torch.full((2, 4), float(i), device=DEV) for i in range(16)}, num_logical_blocks=16)
+    ad = api_gpu.KVCacheAdapter(4, 16, torch.zeros((4, 2, 4), device=DEV), backend)
+    called = []
+    for name in ("plan_load", "plan_save", "gather_blocks", "scatter_blocks", "copy_blocks",
+                 "commit_load_metadata", "commit_save_metadata", "pop_reusable_slots"):
+        monkeypatch.setattr(ext, name, lambda *a, _n=name, **k: called.append(_n))
+    assert ad.load(torch.tensor([3, 5], device=DEV)).tolist() == [0, 1]
+    ad.release(torch.tensor([3, 5], device=DEV))
+    ad.save(torch.tensor([7, 3], device=DEV), torch.ones((2, 2, 4), device=DEV))
+    assert ad.load(torch.tensor([1, 2, 9, 3], device=DEV)).tolist() == [3, 1, 2, 0]
+    assert called == []
+    assert torch.equal(ad.actual_blocks[0], torch.ones((2, 4), device=DEV))
+    assert torch.equal(backend._storage[5], torch.full((2, 4), 5.0, device=DEV))
+    assert backend.max_concurrent_saves == 1 and backend.max_concurrent_loads == 1
+    ext.check_status(DEV)
 
 
 @pytest.fixture(scope="module")
