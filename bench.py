@@ -648,6 +648,115 @@ def run_adapter(args, world: int, rank: int, device) -> None:
     print(json.dumps(line), flush=True)
 
 
+HOST_TIER_CONFIG = dict(num_actual=4096, num_logical=16384, moved=1024, block=(2, 16, 8, 128), dtype=torch.float16)
+
+
+def run_host_tier(args, world: int, rank: int, device) -> None:
+    """Spill + fill between device blocks and a pinned host tier: 1,024
+    random 64 KiB merged K/V blocks (Llama-3-8B layer, bs 16, fp16) out to
+    random rows of a 1 GiB pinned arena and 1,024 others back, per step.
+    Against the reference's CUDA host path (one cudaMemcpyAsync per block,
+    adapter.py:960-966, :1035-1037) and one contiguous copy of the same bytes
+    per direction (the copy engines' rate over the host link)."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ext
+
+    c = HOST_TIER_CONFIG
+    g = torch.Generator().manual_seed(1234)
+    actual = torch.randn((c["num_actual"], *c["block"]), generator=g).to(c["dtype"]).to(device)
+    arena = torch.zeros((c["num_logical"], *c["block"]), dtype=c["dtype"], pin_memory=True)
+    block_bytes = actual[0].numel() * actual.element_size()
+    k = c["moved"]
+    plans = []
+    for _ in range(args.warmup + args.steps):
+        plans.append(tuple(torch.randperm(n, generator=g)[:k].to(device)
+                           for n in (c["num_actual"], c["num_logical"], c["num_actual"], c["num_logical"])))
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn) -> float:
+        for i in range(args.warmup):
+            fn(plans[i])
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.warmup, args.warmup + args.steps):
+            fn(plans[i])
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / 1e3 / args.steps
+
+    def ours(p):
+        s_out, r_out, s_in, r_in = p
+        ext.copy_blocks(actual, s_out, arena, r_out, check=False)  # spill: device -> host rows
+        ext.copy_blocks(arena, r_in, actual, s_in, check=False)    # fill: host rows -> device
+
+    host_plans = [tuple(t.cpu().tolist() for t in p) for p in plans]
+
+    def per_block(i):
+        s_out, r_out, s_in, r_in = host_plans[i]
+        for s_, r_ in zip(s_out, r_out):
+            arena[r_].copy_(actual[s_], non_blocking=True)
+        for s_, r_ in zip(s_in, r_in):
+            actual[s_].copy_(arena[r_], non_blocking=True)
+
+    def per_block_timed() -> float:
+        for i in range(args.warmup):
+            per_block(i)
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.warmup, args.warmup + args.steps):
+            per_block(i)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / 1e3 / args.steps
+
+    staging_d = torch.empty((k, *c["block"]), dtype=c["dtype"], device=device)
+    staging_h = torch.empty((k, *c["block"]), dtype=c["dtype"], pin_memory=True)
+
+    def contiguous(p):
+        staging_h.copy_(staging_d, non_blocking=True)
+        staging_d.copy_(staging_h, non_blocking=True)
+
+    t_ours = timed(ours)
+    t_ref = per_block_timed()
+    t_peak = timed(contiguous)
+    ext.check_status(device)
+    moved = 2 * k * block_bytes  # bytes crossing the host link per step (one way each)
+    # parity of the timed path: the last step's spilled rows equal the device blocks
+    s_out, r_out, _, _ = plans[-1]
+    ext.copy_blocks(actual, s_out, arena, r_out)
+    torch.cuda.synchronize(device)
+    assert torch.equal(arena.index_select(0, r_out.cpu()), actual.index_select(0, s_out).cpu())
+    if rank != 0:
+        return
+    line = {
+        "metric": "host-tier spill+fill GB/s",
+        "value": round(world * moved / t_ours / 1e9, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_ours * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) blocks, seeded random rows)",
+        "config": {"workload": "host tier: 1,024 x 64 KiB blocks spilled to and 1,024 filled from a 1 GiB "
+                               "pinned arena per step, random rows both sides",
+                   "bytes_per_step": moved},
+        "roofline": {"bound": "host-link", "achieved": round(moved / t_ours / 1e9, 2),
+                     "peak": round(moved / t_peak / 1e9, 2), "unit": "GB/s",
+                     "frac": round(t_peak / t_ours, 4), "traffic": None,
+                     "peak_source": "one contiguous cudaMemcpyAsync per direction of the same bytes, this run"},
+        "per_block_memcpy": {"value": round(moved / t_ref / 1e9, 2), "unit": "GB/s",
+                             "ms_per_step": round(t_ref * 1e3, 4),
+                             "what": "one cudaMemcpyAsync per block and direction (reference CUDA host path)"},
+        "gpu_launches": 2 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, w: dict, world: int, rank: int) -> None:
     if rank != 0:
         return
@@ -678,7 +787,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter"], default="llama70b-shard")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter", "host-tier"],
+                    default="llama70b-shard")
     ap.add_argument("--heads", type=int, default=None, help="KV heads per GPU for the decode mix (default 1)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="override the number of sequences (smaller cases for profiling)")
@@ -711,6 +821,8 @@ def main() -> None:
             run_decode_mix(args, world, rank, device)
         elif args.workload == "adapter":
             run_adapter(args, world, rank, device)
+        elif args.workload == "host-tier":
+            run_host_tier(args, world, rank, device)
         else:
             run_ours(args, w, world, rank, device)
     finally:

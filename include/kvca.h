@@ -58,6 +58,11 @@ typedef struct CUstream_st* kvca_stream_t; /* same type as cudaStream_t */
 
 /* Row-mover flags. */
 #define KVCA_FLAG_SKIP_NEGATIVE 1 /* index < 0 marks a padding row: skip it, no error */
+/* One side of a move lives in pinned host memory that the device reaches at
+ * the same address (cudaHostAlloc under unified addressing; check with
+ * kvca_host_memory_usable): rows move with plain SIMT loads and stores over
+ * the host link, never with bulk copies. */
+#define KVCA_FLAG_HOST_MEMORY 2
 
 /* Upper bound on planes per row-mover call. */
 #define KVCA_MAX_PLANES 256
@@ -285,9 +290,12 @@ int kvca_plan_save(int meta_bits, int order, const int64_t* d_l2p, int64_t num_l
                    int64_t* d_status, kvca_stream_t stream);
 
 /*
- * A block store resident on the same GPU: the in-memory backend
+ * A block store driven from the GPU: the in-memory backend
  * (InMemoryBlockStoreBackend, adapter.py:679-833) with its storage tensor
- * on the device.  Row l of the store holds logical block l at
+ * on the device, or a host tier in pinned host memory (the role of
+ * LMCacheBackend, adapter.py:836-1062; move_flags = KVCA_FLAG_HOST_MEMORY,
+ * present and scratch stay in device memory).  Row l of the store holds
+ * logical block l at
  * storage + l * storage_row_stride; present[l] != 0 once block l was saved.
  * scratch holds one int32 per logical block, zero on entry and left zero.
  */
@@ -296,6 +304,7 @@ typedef struct kvca_device_store {
   int64_t storage_row_stride;
   uint8_t* present;
   int32_t* scratch;
+  int32_t move_flags; /* KVCA_FLAG_HOST_MEMORY when storage is pinned host memory */
 } kvca_device_store;
 
 /*
@@ -335,6 +344,10 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
                            uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
                            uint64_t d_block_data, int64_t* d_work, void* d_work_meta,
                            int64_t* d_counts, int64_t* d_status, kvca_stream_t stream);
+
+/* 1 when [p, p + bytes) is pinned host memory that kernels can reach at the
+ * same address, else 0.  No reference counterpart. */
+int kvca_host_memory_usable(const void* p, int64_t bytes);
 
 /* ------------------------------------------------------------------------ */
 /* Row movers                                                                */

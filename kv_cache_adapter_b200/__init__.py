@@ -8,6 +8,7 @@ updates and KV block/token moves run in the CUDA kernels of
 """
 from .adapter import (
     BlockStoreBackend,
+    HostTierBackend,
     InMemoryBlockStoreBackend,
     KVCacheAdapter,
 )
@@ -16,6 +17,7 @@ from .errors import BlockNotFoundError, InsufficientCapacityError, KVCacheAdapte
 __all__ = [
     "BlockNotFoundError",
     "BlockStoreBackend",
+    "HostTierBackend",
     "InMemoryBlockStoreBackend",
     "InsufficientCapacityError",
     "KVCacheAdapter",

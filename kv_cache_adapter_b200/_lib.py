@@ -26,6 +26,7 @@ KVCA_POP_ORDER_GROUPED = 0
 KVCA_POP_ORDER_PREFIX = 1
 
 KVCA_FLAG_SKIP_NEGATIVE = 1
+KVCA_FLAG_HOST_MEMORY = 2
 KVCA_MAX_PLANES = 256
 
 c_i64 = ctypes.c_int64
@@ -66,6 +67,7 @@ class DeviceStore(ctypes.Structure):
         ("storage_row_stride", c_i64),
         ("present", c_ptr),
         ("scratch", c_ptr),
+        ("move_flags", ctypes.c_int32),
     ]
 
 
@@ -134,6 +136,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.POINTER(DeviceStore), ctypes.c_uint64, c_i64, c_i64, ctypes.c_uint64, c_ptr, c_ptr, c_ptr, c_ptr,
          c_ptr],
     ),
+    "kvca_host_memory_usable": (c_int, [c_ptr, c_i64]),
     "kvca_gather": (
         c_int,
         [ctypes.POINTER(PagedDesc), ctypes.POINTER(ChunkDesc), c_i64, c_i64, c_i64, ctypes.c_int32,

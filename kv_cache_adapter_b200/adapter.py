@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import functools
 import importlib
+import math
 import os
 import time
 from dataclasses import dataclass
@@ -70,6 +71,7 @@ __all__ = [
     "BlockStoreBackend",
     "KVCacheAdapterError",
     "BlockNotFoundError",
+    "HostTierBackend",
     "InsufficientCapacityError",
 ]
 
@@ -549,6 +551,13 @@ class InMemoryBlockStoreBackend:
     fuses the reference's index_select + index_copy_ of load_blocks).  A
     store on the host stays a host store: it uses torch host indexing and
     one host<->device copy per call.
+
+    ``host_tier=True`` keeps the rows in pinned host memory instead and moves
+    them with the GPU (``device``, else the first CUDA tensor it is given):
+    saves scatter device rows straight into the pinned rows and loads copy
+    pinned rows straight into ``actual_blocks``, one kernel each, over the
+    host link; the present mask stays on the GPU.  Host-side reads of the
+    rows (``snapshot``) synchronise with that GPU first.
     """
 
     def __init__(
@@ -561,11 +570,15 @@ class InMemoryBlockStoreBackend:
         load_delay_s: float = 0.0,
         record_device_ops: bool = False,
         ops: Any | None = None,
+        host_tier: bool = False,
+        device: torch.device | str | None = None,
     ) -> None:
         self._storage: torch.Tensor | None = None
         self._present_mask: torch.Tensor | None = None
         self._ops = ops
         self._record_device_ops = record_device_ops
+        self._host_tier = host_tier
+        self._tier_device = torch.device(device) if device is not None else None
         if isinstance(initial_data, torch.Tensor):
             if initial_data.ndim < 1:
                 raise ValueError("initial_data tensor must have a leading block dimension")
@@ -599,6 +612,14 @@ class InMemoryBlockStoreBackend:
                 self._storage.index_copy_(0, ids, payloads)
                 self._present_mask.index_fill_(0, ids, True)
 
+        if host_tier:
+            if self._tier_device is None and self._storage is not None and self._storage.is_cuda:
+                self._tier_device = self._storage.device
+            if self._storage is not None:
+                self._storage = self._storage.cpu().pin_memory()
+            if self._present_mask is not None and self._tier_device is not None:
+                self._present_mask = self._present_mask.to(device=self._tier_device)
+
         self.num_logical_blocks = int(num_logical_blocks)
         self._save_delay_s = save_delay_s
         self._load_delay_s = load_delay_s
@@ -614,18 +635,24 @@ class InMemoryBlockStoreBackend:
     def device_store(self, actual_blocks: torch.Tensor):
         """(storage, present mask, scratch) when loads and saves against this
         store can run on the device without a host round trip: storage on
-        actual_blocks' GPU with its dtype and block shape, the default op set,
-        no recording of device ids and no delays.  None otherwise."""
+        actual_blocks' GPU (or, for a host tier, pinned rows that GPU moves)
+        with its dtype and block shape, the default op set, no recording of
+        device ids and no delays.  None otherwise."""
         st = self._storage
+        dev = actual_blocks.device
         if (self._ops is not None or self._record_device_ops or self._save_delay_s > 0 or self._load_delay_s > 0
-                or st is None or actual_blocks.device.type != "cuda" or st.device != actual_blocks.device
-                or st.dtype != actual_blocks.dtype or st.shape[1:] != actual_blocks.shape[1:]
-                or not st.is_contiguous()):
+                or st is None or dev.type != "cuda" or st.dtype != actual_blocks.dtype
+                or st.shape[1:] != actual_blocks.shape[1:] or not st.is_contiguous()):
             return None
-        self._ensure_present_mask(device=st.device)
+        if self._host_tier:
+            if self._gpu_for(actual_blocks) != dev:
+                return None
+        elif st.device != dev:
+            return None
+        self._ensure_present_mask(device=dev)
         scratch = self._device_scratch
-        if scratch is None or scratch.device != st.device:
-            scratch = self._device_scratch = torch.zeros(st.shape[0], dtype=torch.int32, device=st.device)
+        if scratch is None or scratch.device != dev:
+            scratch = self._device_scratch = torch.zeros(st.shape[0], dtype=torch.int32, device=dev)
         return st, self._present_mask, scratch
 
     def note_device_ops(self, *, saved: bool, loaded: bool) -> None:
@@ -649,6 +676,9 @@ class InMemoryBlockStoreBackend:
         try:
             if self._save_delay_s > 0:
                 time.sleep(self._save_delay_s)
+            if self._host_tier:
+                self._save_host_tier(logical_block_ids, block_data)
+                return
             if self._storage is None:
                 self._storage = block_data.new_zeros((self.num_logical_blocks, *block_data.shape[1:]))
             else:
@@ -680,6 +710,9 @@ class InMemoryBlockStoreBackend:
                 time.sleep(self._load_delay_s)
             if self._storage is None:
                 raise BlockNotFoundError("backend storage is empty")
+            if self._host_tier:
+                self._load_host_tier(logical_block_ids, actual_blocks, physical_slot_ids)
+                return
             self._ensure_present_mask(device=self._storage.device)
             ids = logical_block_ids.to(device=self._storage.device).contiguous()
             hit_mask = self._present_mask.index_select(0, ids)
@@ -701,9 +734,54 @@ class InMemoryBlockStoreBackend:
         finally:
             self._leave_load()
 
+    def _gpu_for(self, t: torch.Tensor) -> torch.device:
+        if self._tier_device is None:
+            if not t.is_cuda:
+                raise ValueError("a host tier moves blocks with a GPU: pass device= or CUDA tensors")
+            self._tier_device = t.device
+        return self._tier_device
+
+    def _save_host_tier(self, logical_block_ids: torch.Tensor, block_data: torch.Tensor) -> None:
+        """save_blocks into pinned rows: one scatter kernel writing host memory."""
+        dev = self._gpu_for(block_data)
+        if self._storage is None:
+            self._storage = torch.zeros((self.num_logical_blocks, *block_data.shape[1:]), dtype=block_data.dtype,
+                                        pin_memory=True)
+        else:
+            _require_trailing_shape(block_data, self._storage, name="block_data")
+            _require_same_dtype(block_data, reference=self._storage, name="block_data")
+        self._ensure_present_mask(device=dev)
+        ids = logical_block_ids.to(device=dev).contiguous()
+        data = block_data.to(device=dev, dtype=self._storage.dtype).contiguous()
+        self._device_ops().scatter_blocks(self._storage, _last_occurrences(ids, self.num_logical_blocks), data,
+                                          skip_negative=True)
+        self._present_mask.index_fill_(0, ids, True)
+        self._record_ids("save", logical_block_ids)
+
+    def _load_host_tier(self, logical_block_ids: torch.Tensor, actual_blocks: torch.Tensor,
+                        physical_slot_ids: torch.Tensor) -> None:
+        """load_blocks from pinned rows: one copy kernel reading host memory."""
+        dev = self._gpu_for(actual_blocks)
+        self._ensure_present_mask(device=dev)
+        ids = logical_block_ids.to(device=dev).contiguous()
+        if not torch.all(self._present_mask.index_select(0, ids)).item():
+            raise BlockNotFoundError("some logical blocks are not in backend")
+        _require_trailing_shape(actual_blocks, self._storage, name="actual_blocks")
+        if actual_blocks.is_cuda and actual_blocks.dtype == self._storage.dtype:
+            slots = physical_slot_ids.to(device=actual_blocks.device).contiguous()
+            self._device_ops().copy_blocks(self._storage, ids, actual_blocks, slots)
+        else:
+            torch.cuda.synchronize(dev)
+            payloads = self._storage.index_select(0, ids.cpu()).to(device=actual_blocks.device,
+                                                                    dtype=actual_blocks.dtype)
+            actual_blocks.index_copy_(0, physical_slot_ids.to(device=actual_blocks.device), payloads)
+        self._record_ids("load", logical_block_ids)
+
     def snapshot(self) -> dict[int, torch.Tensor]:
         if self._storage is None:
             return {}
+        if self._host_tier and self._tier_device is not None:
+            torch.cuda.synchronize(self._tier_device)
         present_ids = torch.nonzero(self._present_mask, as_tuple=False).reshape(-1)
         present_payloads = self._storage.index_select(0, present_ids.to(device=self._storage.device))
         return {
@@ -760,6 +838,89 @@ def _saturating_increment_usage(values: torch.Tensor) -> torch.Tensor:
     """adapter.py:1414-1416."""
     incremented = values.to(dtype=torch.int32) + 1
     return torch.clamp(incremented, max=USAGE_COUNT_MAX).to(dtype=USAGE_DTYPE)
+
+
+class HostTierBackend(InMemoryBlockStoreBackend):
+    """Host tier for evicted blocks: the role of the reference's LMCacheBackend
+    (adapter.py:836-1062), whose CUDA path copies one block per
+    cudaMemcpyAsync into a pinned memory object and back (:1035-1037,
+    :960-966).  Here every block lives in one pinned host arena, row l =
+    logical block l (the key's chunk_hash), and a save or load is one kernel
+    that gathers or scatters all its blocks over the host link; with
+    KVCacheAdapter the whole call is enqueued at once (device-store path).
+
+    The constructor takes LMCacheBackend's arguments.  ``model_name``,
+    ``world_size`` and ``worker_id`` complete the key as in
+    ``CacheEngineKey`` and are kept for the caller; rows are stored in block
+    shape, which for a merged K/V block is byte for byte LMCache's
+    ``KV_2TD`` / ``KV_T2D`` transfer layout (``memory_format``,
+    ``transfer_view``).  Capacity is the logical id space; it must fit in
+    ``max_local_cpu_size_gb``.  Unlike LocalCPUBackend there is no eviction
+    inside the tier.
+    """
+
+    def __init__(self, *, block_shape: tuple[int, ...] | torch.Size, block_dtype: torch.dtype,
+                 num_logical_blocks: int, device: torch.device | str | None = None,
+                 model_name: str = "kv_cache_adapter", world_size: int = 1, worker_id: int = 0,
+                 max_local_cpu_size_gb: float | None = None, record_device_ops: bool = False) -> None:
+        super().__init__(num_logical_blocks=num_logical_blocks, record_device_ops=record_device_ops,
+                         host_tier=True, device=device)
+        self._block_shape = torch.Size(block_shape)
+        self._block_dtype = block_dtype
+        self.model_name, self.world_size, self.worker_id = model_name, world_size, worker_id
+        nbytes = num_logical_blocks * math.prod(self._block_shape) * torch.empty((), dtype=block_dtype).element_size()
+        if max_local_cpu_size_gb is not None and nbytes > max_local_cpu_size_gb * (1 << 30):
+            raise ValueError(f"{nbytes} bytes of host tier exceed max_local_cpu_size_gb={max_local_cpu_size_gb}")
+        self._storage = torch.zeros((num_logical_blocks, *self._block_shape), dtype=block_dtype, pin_memory=True)
+        self.layout = _MergedKVBlockLayout.detect(self._block_shape)
+
+    @property
+    def memory_format(self) -> str:
+        """LMCache's MemoryFormat name of a stored row (adapter.py:1187-1192)."""
+        if self.layout is None:
+            return "UNDEFINED"
+        return "KV_2TD" if self.layout.token_major else "KV_T2D"
+
+    def transfer_view(self, logical_block_id: int) -> torch.Tensor:
+        """Stored row of a block in LMCache's transfer shape (a view, no copy)."""
+        row = self._storage[int(logical_block_id)]
+        return row if self.layout is None else row.reshape(self.layout.transfer_shape)
+
+    def _require_block_layout(self, t: torch.Tensor, *, name: str) -> None:
+        """adapter.py:1126-1130."""
+        if t.dtype != self._block_dtype:
+            raise TypeError(f"{name} must have dtype {self._block_dtype}")
+        if tuple(t.shape[1:]) != tuple(self._block_shape):
+            raise ValueError(f"{name} must have trailing shape {tuple(self._block_shape)}")
+
+    def save_blocks(self, logical_block_ids: torch.Tensor, block_data: torch.Tensor) -> None:
+        """adapter.py:888-907."""
+        _require_id_tensor(logical_block_ids, name="logical_block_ids")
+        _require_block_data_tensor(block_data, expected_blocks=logical_block_ids.shape[0], name="block_data")
+        self._require_block_layout(block_data, name="block_data")
+        if logical_block_ids.numel() == 0:
+            return
+        super().save_blocks(logical_block_ids, block_data)
+
+    def load_blocks(self, logical_block_ids: torch.Tensor, actual_blocks: torch.Tensor,
+                    physical_slot_ids: torch.Tensor) -> None:
+        """adapter.py:909-969; a missing block raises BlockNotFoundError."""
+        _require_id_tensor(logical_block_ids, name="logical_block_ids")
+        _require_id_tensor(physical_slot_ids, name="physical_slot_ids")
+        if logical_block_ids.shape[0] != physical_slot_ids.shape[0]:
+            raise ValueError("physical_slot_ids leading dimension must match logical_block_ids")
+        self._require_block_layout(actual_blocks, name="actual_blocks")
+        if logical_block_ids.numel() == 0:
+            return
+        super().load_blocks(logical_block_ids, actual_blocks, physical_slot_ids)
+
+    def shutdown(self) -> None:
+        """adapter.py:971-976: drop every stored block."""
+        if self._tier_device is not None:
+            torch.cuda.synchronize(self._tier_device)
+        self._storage = None
+        self._present_mask = None
+        self._device_scratch = None
 
 
 def _last_occurrences(ids: torch.Tensor, size: int) -> torch.Tensor:

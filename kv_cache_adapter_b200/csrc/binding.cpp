@@ -309,7 +309,22 @@ static void one_plane(uint64_t base, int64_t rows, int64_t row_stride, const int
 static bool store_ok(const kvca_device_store* store, uint64_t actual, int64_t actual_row_stride,
                      int64_t row_bytes) {
   return store && store->storage && store->present && store->scratch && actual &&
-         row_bytes > 0 && actual_row_stride >= row_bytes && store->storage_row_stride >= row_bytes;
+         row_bytes > 0 && actual_row_stride >= row_bytes && store->storage_row_stride >= row_bytes &&
+         (store->move_flags & ~KVCA_FLAG_HOST_MEMORY) == 0;
+}
+
+int kvca_host_memory_usable(const void* p, int64_t bytes) {
+  if (p == nullptr || bytes <= 0) return 0;
+  const char* last = static_cast<const char*>(p) + (bytes - 1);
+  for (const void* q : {p, static_cast<const void*>(last)}) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, q) != cudaSuccess) {
+      cudaGetLastError();  // clear the sticky-free error of an unknown pointer
+      return 0;
+    }
+    if (attr.type != cudaMemoryTypeHost || attr.devicePointer != q) return 0;
+  }
+  return 1;
 }
 
 int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
@@ -341,11 +356,13 @@ int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   one_plane(store->storage, num_logical, store->storage_row_stride, d_work + 2 * k, &store_missed);
   one_plane(d_actual, num_slots, actual_row_stride, d_work + 6 * k, &actual_filled);
   kvca::MoveArgs spill{kvca::MoveKind::kCopyPaged, &actual_evicted, nullptr, &store_evicted,
-                       nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
+                       nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE | store->move_flags,
+                       d_status};
   rc = status_of(kvca::launch_move(spill, stream));
   if (rc != KVCA_OK) return rc;
   kvca::MoveArgs fill{kvca::MoveKind::kCopyPaged, &store_missed, nullptr, &actual_filled,
-                      nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
+                      nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE | store->move_flags,
+                      d_status};
   return status_of(kvca::launch_move(fill, stream));
 }
 
@@ -378,7 +395,8 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   one_plane(store->storage, num_logical, store->storage_row_stride, d_work + 2 * k, &store_evicted);
   one_plane(d_actual, num_slots, actual_row_stride, d_work + 4 * k, &actual_selected);
   kvca::MoveArgs spill{kvca::MoveKind::kCopyPaged, &actual_evicted, nullptr, &store_evicted,
-                       nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
+                       nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE | store->move_flags,
+                       d_status};
   rc = status_of(kvca::launch_move(spill, stream));
   if (rc != KVCA_OK) return rc;
   kvca::ChunkSide data;

@@ -1533,7 +1533,9 @@ constexpr int64_t kMoverSegmentBytes = 16384;
 // consecutive items share a row: the row's index is loaded and its offset
 // computed once per row, not once per plane or segment.  Each lane keeps
 // kMoverUnroll vectors in flight.
-template <bool kSrcPaged, bool kDstPaged, typename V>
+// kHost: one side is pinned, mapped host memory reached over the host link;
+// rows move with plain loads and stores there (no non-coherent cache path).
+template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost>
 __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_constant__ MoveParams p) {
   const int tpr = 1 << p.tpr_log2;
   const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -1582,12 +1584,17 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
 #pragma unroll
         for (int u = 0; u < kMoverUnroll; ++u) {
           const int64_t i = b + static_cast<int64_t>(u) * tpr;
-          if (i < v_end) buf[u] = ld_stream(src + i);
+          if (i < v_end) buf[u] = kHost ? src[i] : ld_stream(src + i);
         }
 #pragma unroll
         for (int u = 0; u < kMoverUnroll; ++u) {
           const int64_t i = b + static_cast<int64_t>(u) * tpr;
-          if (i < v_end) st_stream(dst + i, buf[u]);
+          if (i < v_end) {
+            if (kHost)
+              dst[i] = buf[u];
+            else
+              st_stream(dst + i, buf[u]);
+          }
         }
       }
     }
@@ -1610,9 +1617,9 @@ int device_sm_count() {
   return sms;
 }
 
-template <bool kSrcPaged, bool kDstPaged, typename V>
+template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost = false>
 cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
-  auto kernel = move_rows_kernel<kSrcPaged, kDstPaged, V>;
+  auto kernel = move_rows_kernel<kSrcPaged, kDstPaged, V, kHost>;
   static int blocks_per_sm = 0;
   if (blocks_per_sm == 0) {
     int b = 0;
@@ -1824,6 +1831,15 @@ cudaError_t launch_move_bulk(const MoveParams& base, cudaStream_t stream) {
 
 template <bool kSrcPaged, bool kDstPaged>
 cudaError_t launch_move_vec(const MoveParams& p, int vec_bytes, cudaStream_t stream) {
+  if (p.flags & KVCA_FLAG_HOST_MEMORY) {  // SIMT only: no bulk copies to or from host memory
+    switch (vec_bytes) {
+      case 16: return launch_move_typed<kSrcPaged, kDstPaged, uint4, true>(p, stream);
+      case 8: return launch_move_typed<kSrcPaged, kDstPaged, uint2, true>(p, stream);
+      case 4: return launch_move_typed<kSrcPaged, kDstPaged, unsigned int, true>(p, stream);
+      case 2: return launch_move_typed<kSrcPaged, kDstPaged, unsigned short, true>(p, stream);
+      default: return launch_move_typed<kSrcPaged, kDstPaged, unsigned char, true>(p, stream);
+    }
+  }
   switch (vec_bytes) {
     case 16:
       if (p.row_vecs * 16 >= kBulkMinRowBytes) return launch_move_bulk<kSrcPaged, kDstPaged>(p, stream);

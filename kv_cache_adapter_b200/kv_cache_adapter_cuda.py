@@ -516,9 +516,17 @@ def _rows_of(t: torch.Tensor, name: str) -> tuple[int, int]:
 
 def _store_desc(storage: torch.Tensor, present: torch.Tensor, scratch: torch.Tensor,
                 actual_blocks: torch.Tensor) -> tuple[_lib.DeviceStore, int, int]:
-    if storage.device != actual_blocks.device or storage.dtype != actual_blocks.dtype \
+    """Descriptor of a store driven from actual_blocks' GPU: storage on that GPU,
+    or in pinned host memory (a host tier; present and scratch stay on the GPU)."""
+    on_host = storage.device.type == "cpu"
+    if (storage.device != actual_blocks.device and not on_host) or storage.dtype != actual_blocks.dtype \
             or storage.shape[1:] != actual_blocks.shape[1:]:
-        raise ValueError("storage and actual_blocks must share device, dtype and block shape")
+        raise ValueError("storage and actual_blocks must share device (or storage be pinned host memory), "
+                         "dtype and block shape")
+    if on_host and not host_memory_usable(storage):
+        raise ValueError("host storage must be pinned (torch pin_memory)")
+    if present.device != actual_blocks.device or scratch.device != actual_blocks.device:
+        raise ValueError("present and scratch must be on actual_blocks' device")
     _require(present, torch.bool, "present")
     _require(scratch, torch.int32, "scratch")
     n_logical = storage.shape[0]
@@ -526,7 +534,9 @@ def _store_desc(storage: torch.Tensor, present: torch.Tensor, scratch: torch.Ten
         raise ValueError("present and scratch need one entry per stored block")
     s_stride, row_bytes = _rows_of(storage, "storage")
     a_stride, _ = _rows_of(actual_blocks, "actual_blocks")
-    return _lib.DeviceStore(storage.data_ptr(), s_stride, present.data_ptr(), scratch.data_ptr()), a_stride, row_bytes
+    flags = _lib.KVCA_FLAG_HOST_MEMORY if on_host else 0
+    return (_lib.DeviceStore(storage.data_ptr(), s_stride, present.data_ptr(), scratch.data_ptr(), flags),
+            a_stride, row_bytes)
 
 
 def load_device_store(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor, slot_meta: torch.Tensor,
@@ -625,8 +635,9 @@ class PlaneTable:
         if len(planes) > _lib.KVCA_MAX_PLANES:
             raise ValueError(f"{name}: at most {_lib.KVCA_MAX_PLANES} planes per call")
         first = planes[0]
-        if not first.is_cuda:
-            raise ValueError(f"{name} must be CUDA tensors")
+        self.host = not first.is_cuda
+        if self.host and not all(host_memory_usable(p) for p in planes):
+            raise ValueError(f"{name} must be CUDA tensors or pinned host memory")
         if first.dim() < row_dim:
             raise ValueError(f"{name} planes must have at least {row_dim} dims")
         for p in planes[1:]:
@@ -658,7 +669,35 @@ class PlaneTable:
 _single_plane_tables: dict[tuple, PlaneTable] = {}
 
 
-def _planes(caches, row_dim: int, name: str) -> PlaneTable:
+def host_memory_usable(t: torch.Tensor) -> bool:
+    """True when every byte of ``t`` is pinned host memory that kernels reach
+    at the same address (torch ``pin_memory`` allocations)."""
+    if t.is_cuda or t.numel() == 0:
+        return False
+    span = (sum((n - 1) * st for n, st in zip(t.shape, t.stride())) + 1) * t.element_size()
+    return bool(_lib_handle.kvca_host_memory_usable(ctypes.c_void_p(t.data_ptr()), span))
+
+
+def _move_device(*sides) -> torch.device:
+    """The GPU a move runs on: the one CUDA side (the other may be host memory)."""
+    devs = {s.device for s in sides if s is not None and s.device.type == "cuda"}
+    if len(devs) != 1:
+        raise ValueError("a move needs its CUDA tensors on one device (the other side may be pinned host memory)")
+    return devs.pop()
+
+
+def _host_flag(*sides) -> int:
+    return _lib.KVCA_FLAG_HOST_MEMORY if any(s is not None and s.device.type != "cuda" for s in sides) else 0
+
+
+def _planes(caches, row_dim: int, name: str, *, allow_host: bool = False) -> PlaneTable:
+    table = _plane_table(caches, row_dim, name)
+    if table.host and not allow_host:
+        raise ValueError(f"{name} must be CUDA tensors")
+    return table
+
+
+def _plane_table(caches, row_dim: int, name: str) -> PlaneTable:
     if isinstance(caches, PlaneTable):
         if caches.row_dim != row_dim:
             raise ValueError(f"{name}: plane table built for row_dim {caches.row_dim}, need {row_dim}")
@@ -704,24 +743,30 @@ def _launch_move(fn_name: str, src, dst, num_planes: int, num_rows: int, row_byt
 
 
 def _chunk_tensor(out: torch.Tensor | None, shape: tuple[int, ...], dtype, device, name: str) -> torch.Tensor:
+    """The contiguous chunk side: ``out`` if it fits (on ``device``, or in
+    pinned host memory when ``device`` is a GPU), else a new tensor on ``device``."""
     if out is None:
         return torch.empty(shape, dtype=dtype, device=device)
-    if tuple(out.shape) != tuple(shape) or out.dtype != dtype or out.device != device:
-        raise ValueError(f"{name} must be {tuple(shape)} {dtype} on {device}")
+    on_host = out.device.type == "cpu" and device.type == "cuda"
+    if tuple(out.shape) != tuple(shape) or out.dtype != dtype or (out.device != device and not on_host):
+        raise ValueError(f"{name} must be {tuple(shape)} {dtype} on {device} or in pinned host memory")
     if not out.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
+    if on_host and not host_memory_usable(out):
+        raise ValueError(f"{name}: host tensors must be pinned (torch pin_memory)")
     return out
 
 
 def gather_blocks(actual_blocks: torch.Tensor, slot_ids: torch.Tensor,
                   out: torch.Tensor | None = None, *, check: bool | None = None) -> torch.Tensor:
     """``actual_blocks.index_select(0, slot_ids)`` (adapter.py:543)."""
-    pl = _planes([actual_blocks], 1, "actual_blocks")
-    _require_index(slot_ids, pl.device, "slot_ids")
+    pl = _planes([actual_blocks], 1, "actual_blocks", allow_host=True)
+    dev = _move_device(pl, slot_ids)
+    _require_index(slot_ids, dev, "slot_ids")
     k = slot_ids.numel()
-    out = _chunk_tensor(out, (k, *pl.row_shape), pl.dtype, pl.device, "out")
+    out = _chunk_tensor(out, (k, *pl.row_shape), pl.dtype, dev, "out")
     _launch_move("kvca_gather", pl.desc(slot_ids), _chunk_desc(out, max(k, 1), 1, pl.row_bytes),
-                 1, k, pl.row_bytes, 0, pl.device, check)
+                 1, k, pl.row_bytes, _host_flag(pl, out), dev, check)
     return out
 
 
@@ -730,29 +775,33 @@ def scatter_blocks(actual_blocks: torch.Tensor, slot_ids: torch.Tensor, block_da
     """``actual_blocks.index_copy_(0, slot_ids, block_data)`` (adapter.py:653-656).
     Slots must be distinct (a repeated slot receives one of its rows); with
     ``skip_negative`` rows whose slot is negative are not written."""
-    pl = _planes([actual_blocks], 1, "actual_blocks")
-    _require_index(slot_ids, pl.device, "slot_ids")
+    pl = _planes([actual_blocks], 1, "actual_blocks", allow_host=True)
+    dev = _move_device(pl, slot_ids)
+    _require_index(slot_ids, dev, "slot_ids")
     k = slot_ids.numel()
-    _chunk_tensor(block_data, (k, *pl.row_shape), pl.dtype, pl.device, "block_data")
+    _chunk_tensor(block_data, (k, *pl.row_shape), pl.dtype, dev, "block_data")
+    flags = (_lib.KVCA_FLAG_SKIP_NEGATIVE if skip_negative else 0) | _host_flag(pl, block_data)
     _launch_move("kvca_scatter", _chunk_desc(block_data, max(k, 1), 1, pl.row_bytes),
-                 pl.desc(slot_ids), 1, k, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE if skip_negative else 0,
-                 pl.device, check)
+                 pl.desc(slot_ids), 1, k, pl.row_bytes, flags, dev, check)
 
 
 def copy_blocks(src_blocks: torch.Tensor, src_ids: torch.Tensor, dst_blocks: torch.Tensor,
                 dst_ids: torch.Tensor, *, check: bool | None = None) -> None:
     """``dst.index_copy_(0, dst_ids, src.index_select(0, src_ids))`` in one pass
     (adapter.py:779-787).  ``src_blocks`` and ``dst_blocks`` must not overlap."""
-    s = _planes([src_blocks], 1, "src_blocks")
-    d = _planes([dst_blocks], 1, "dst_blocks")
-    if s.row_bytes != d.row_bytes or s.dtype != d.dtype or s.device != d.device:
-        raise ValueError("src_blocks and dst_blocks must share block shape, dtype and device")
-    _require_index(src_ids, s.device, "src_ids")
-    _require_index(dst_ids, s.device, "dst_ids")
+    s = _planes([src_blocks], 1, "src_blocks", allow_host=True)
+    d = _planes([dst_blocks], 1, "dst_blocks", allow_host=True)
+    if s.row_bytes != d.row_bytes or s.dtype != d.dtype:
+        raise ValueError("src_blocks and dst_blocks must share block shape and dtype")
+    if s.host and d.host:
+        raise ValueError("at most one of src_blocks / dst_blocks may be host memory")
+    dev = _move_device(s, d, src_ids)
+    _require_index(src_ids, dev, "src_ids")
+    _require_index(dst_ids, dev, "dst_ids")
     if src_ids.numel() != dst_ids.numel():
         raise ValueError("src_ids and dst_ids must have the same length")
     _launch_move("kvca_copy_paged", s.desc(src_ids), d.desc(dst_ids), 1, src_ids.numel(),
-                 s.row_bytes, 0, s.device, check)
+                 s.row_bytes, _host_flag(s, d), dev, check)
 
 
 def _chunks_of(k: int, per_chunk: int | None, what: str) -> tuple[int, int]:
@@ -775,7 +824,7 @@ def gather_layers(caches: Sequence[torch.Tensor], slot_ids: torch.Tensor,
     P = len(pl.planes)
     out = _chunk_tensor(out, (nc, P, cb, *pl.row_shape), pl.dtype, pl.device, "out")
     _launch_move("kvca_gather", pl.desc(slot_ids), _chunk_desc(out, cb, P, pl.row_bytes), P, k,
-                 pl.row_bytes, 0, pl.device, check)
+                 pl.row_bytes, _host_flag(out), pl.device, check)
     return out
 
 
@@ -789,7 +838,7 @@ def scatter_layers(caches: Sequence[torch.Tensor], slot_ids: torch.Tensor, chunk
     P = len(pl.planes)
     _chunk_tensor(chunks, (nc, P, cb, *pl.row_shape), pl.dtype, pl.device, "chunks")
     _launch_move("kvca_scatter", _chunk_desc(chunks, cb, P, pl.row_bytes), pl.desc(slot_ids), P,
-                 k, pl.row_bytes, 0, pl.device, check)
+                 k, pl.row_bytes, _host_flag(chunks), pl.device, check)
 
 
 def gather_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor,
@@ -806,7 +855,7 @@ def gather_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor,
     P = len(pl.planes)
     out = _chunk_tensor(out, (nc, P, tpc, *pl.row_shape), pl.dtype, pl.device, "out")
     _launch_move("kvca_gather", pl.desc(slot_mapping), _chunk_desc(out, tpc, P, pl.row_bytes), P,
-                 t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE, pl.device, check)
+                 t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE | _host_flag(out), pl.device, check)
     return out
 
 
@@ -821,4 +870,4 @@ def scatter_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor, c
     P = len(pl.planes)
     _chunk_tensor(chunks, (nc, P, tpc, *pl.row_shape), pl.dtype, pl.device, "chunks")
     _launch_move("kvca_scatter", _chunk_desc(chunks, tpc, P, pl.row_bytes), pl.desc(slot_mapping),
-                 P, t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE, pl.device, check)
+                 P, t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE | _host_flag(chunks), pl.device, check)

@@ -23,7 +23,7 @@ def _flat(t: torch.Tensor | None):
 
 
 def run_and_compare(case: dict, device: torch.device, *, native_ext=None, backend_ops=None,
-                    planned: bool | None = None, record: bool = True) -> None:
+                    planned: bool | None = None, record: bool = True, host_tier: bool = False) -> None:
     """Replays a recorded reference scenario and compares results, errors and
     the full adapter / backend state after every step.  ``record=False`` runs
     the backend without recording device ids (the operation log is then not
@@ -34,10 +34,12 @@ def run_and_compare(case: dict, device: torch.device, *, native_ext=None, backen
             for k, v in spec["initial"].items()}
     if init:
         backend = InMemoryBlockStoreBackend(init, num_logical_blocks=spec["num_logical"],
-                                            record_device_ops=record, ops=backend_ops)
+                                            record_device_ops=record, ops=backend_ops,
+                                            host_tier=host_tier, device=device if host_tier else None)
     else:
         backend = InMemoryBlockStoreBackend(num_logical_blocks=spec["num_logical"],
-                                            record_device_ops=record, ops=backend_ops)
+                                            record_device_ops=record, ops=backend_ops,
+                                            host_tier=host_tier, device=device if host_tier else None)
     ad = KVCacheAdapter(spec["num_actual"], spec["num_logical"],
                         torch.zeros((spec["num_actual"], *shape), dtype=torch.float32, device=device),
                         backend, native_ext=native_ext)
