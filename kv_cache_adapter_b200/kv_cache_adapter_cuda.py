@@ -47,6 +47,8 @@ __all__ = [
     "scatter_tokens",
     "plan_load",
     "plan_save",
+    "copy_tokens",
+    "batched_fused_single_layer_kv_transfer",
     "load_device_store",
     "save_device_store",
     "check_status",
@@ -871,3 +873,98 @@ def scatter_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor, c
     _chunk_tensor(chunks, (nc, P, tpc, *pl.row_shape), pl.dtype, pl.device, "chunks")
     _launch_move("kvca_scatter", _chunk_desc(chunks, tpc, P, pl.row_bytes), pl.desc(slot_mapping),
                  P, t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE | _host_flag(chunks), pl.device, check)
+
+
+def copy_tokens(src_caches, src_mapping: torch.Tensor, dst_caches, dst_mapping: torch.Tensor, *,
+                check: bool | None = None) -> None:
+    """Token row ``src_mapping[t]`` of every source plane to token row
+    ``dst_mapping[t]`` of the matching destination plane, in one launch; both
+    sides are ``(num_blocks, block_size, *row)`` planes (block sizes may
+    differ), one side may be pinned host memory, negative mappings on either
+    side skip the token."""
+    s = _planes(src_caches, 2, "src_caches", allow_host=True)
+    d = _planes(dst_caches, 2, "dst_caches", allow_host=True)
+    if len(s.planes) != len(d.planes) or s.row_bytes != d.row_bytes or s.dtype != d.dtype:
+        raise ValueError("src and dst planes must match in count, row shape and dtype")
+    if s.host and d.host:
+        raise ValueError("at most one side may be host memory")
+    dev = _move_device(s, d, src_mapping)
+    _require_index(src_mapping, dev, "src_mapping")
+    _require_index(dst_mapping, dev, "dst_mapping")
+    if src_mapping.numel() != dst_mapping.numel():
+        raise ValueError("src_mapping and dst_mapping must have the same length")
+    _launch_move("kvca_copy_paged", s.desc(src_mapping), d.desc(dst_mapping), len(s.planes), src_mapping.numel(),
+                 s.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE | _host_flag(s, d), dev, check)
+
+
+def _pool_rows(memory_objs: Sequence[torch.Tensor], shape: torch.Size, dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    """The buffer the memory objects are rows of, as ``(n_rows, *shape)``, and
+    each object's row index.  Every object must be a contiguous ``shape``
+    view at a whole-row offset of one buffer (a pinned pool, a host tier's
+    arena, or a device tensor)."""
+    first = memory_objs[0]
+    storage = first.untyped_storage()
+    base = storage.data_ptr()
+    row_bytes = math.prod(shape) * first.element_size()
+    rows = []
+    for m in memory_objs:
+        if (m.untyped_storage().data_ptr() != base or m.dtype != dtype or tuple(m.shape) != tuple(shape)
+                or not m.is_contiguous() or (m.data_ptr() - base) % row_bytes):
+            raise ValueError("memory objects must be contiguous rows of one buffer, all of the transfer shape")
+        rows.append((m.data_ptr() - base) // row_bytes)
+    n_rows = storage.nbytes() // row_bytes
+    pool = torch.empty(0, dtype=dtype, device=first.device).set_(storage, 0, (n_rows, *shape))
+    return pool, torch.tensor(rows, dtype=torch.int64)
+
+
+def batched_fused_single_layer_kv_transfer(memory_objs: Sequence[torch.Tensor], staging_cache, kv_blocks: torch.Tensor,
+                                           slot_mapping: torch.Tensor, chunk_offsets: Sequence[int],
+                                           chunk_sizes: Sequence[int], to_memory_objs: bool, num_layers: int = 1,
+                                           token_major: bool = True, reserved: bool = False, *,
+                                           check: bool | None = None) -> None:
+    """Token-granular K/V transfer of one layer between merged paged blocks and
+    per-chunk memory objects, the op the reference calls on its accelerator
+    host path (``lmcache_ascend.c_ops``, adapter.py:1208-1219 to the memory
+    objects, :1231-1242 back), as one copy kernel over both K and V.
+
+    ``kv_blocks`` ``(m, *block)`` with a merged block ``(bs, 2, H, D)``
+    (``token_major``) or ``(2, bs, H, D)``; token slot s is token ``s % bs`` of
+    block ``s // bs``.  Memory object i, of transfer shape ``(T, 2, H*D)`` or
+    ``(2, T, H*D)`` with T = ``chunk_sizes[i]``, holds the tokens
+    ``slot_mapping[chunk_offsets[i] : chunk_offsets[i] + T]`` in order.  The
+    objects must be rows of one buffer (pinned host or device), as a pinned
+    pool hands them out.  ``staging_cache`` is not needed (rows move
+    directly) and ignored; ``num_layers`` must be 1; ``reserved`` is ignored.
+    Negative slots are skipped."""
+    from .adapter import _MergedKVBlockLayout
+
+    if num_layers != 1:
+        raise ValueError("single-layer transfer: num_layers must be 1")
+    layout = _MergedKVBlockLayout.detect(kv_blocks.shape[1:])
+    if layout is None or layout.token_major != bool(token_major):
+        raise ValueError("kv_blocks must be merged K/V blocks of the stated token order")
+    n = len(memory_objs)
+    if n == 0:
+        return
+    if len(chunk_offsets) != n or len(chunk_sizes) != n or len(set(int(c) for c in chunk_sizes)) != 1:
+        raise ValueError("one offset and one (common) size per memory object")
+    T = int(chunk_sizes[0])
+    tshape = torch.Size((T, 2, layout.hidden_dim) if layout.token_major else (2, T, layout.hidden_dim))
+    pool, rows = _pool_rows(memory_objs, tshape, kv_blocks.dtype)
+    dev = kv_blocks.device
+    _require_index(slot_mapping, dev, "slot_mapping")
+    offs = torch.tensor([int(o) for o in chunk_offsets], dtype=torch.int64)
+    if int(offs.min()) < 0 or int(offs.max()) + T > slot_mapping.numel():
+        raise ValueError("chunks must lie inside slot_mapping")
+    t = torch.arange(T, dtype=torch.int64)
+    kv_map = slot_mapping.index_select(0, (offs.view(-1, 1) + t.view(1, -1)).view(-1).to(dev))
+    pool_map = (rows.view(-1, 1) * T + t.view(1, -1)).view(-1).to(dev)
+    kv_planes = layout.token_planes(kv_blocks)
+    if layout.token_major:
+        pool_planes = [pool[:, :, 0], pool[:, :, 1]]
+    else:
+        pool_planes = [pool[:, 0], pool[:, 1]]
+    if to_memory_objs:
+        copy_tokens(kv_planes, kv_map, pool_planes, pool_map, check=check)
+    else:
+        copy_tokens(pool_planes, pool_map, kv_planes, kv_map, check=check)

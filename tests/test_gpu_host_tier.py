@@ -226,3 +226,82 @@ def test_adapter_with_host_tier_matches_oracle_adapter(seed, num_actual, num_log
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda
 
     kv_cache_adapter_cuda.check_status(DEV)
+
+
+def _kv_token(actual: torch.Tensor, layout, s: int, kv: int) -> torch.Tensor:
+    bs = layout.block_size
+    flat = actual.view(actual.shape[0], *layout.transfer_shape)
+    return flat[s // bs, s % bs, kv] if layout.token_major else flat[s // bs, kv, s % bs]
+
+
+def _obj_token(obj: torch.Tensor, layout, t: int, kv: int) -> torch.Tensor:
+    return obj[t, kv] if layout.token_major else obj[kv, t]
+
+
+@pytest.mark.parametrize("token_major", [True, False])
+@pytest.mark.parametrize("where", ["host", "device"])
+def test_fused_single_layer_kv_transfer(ext, token_major, where):
+    """The accelerator host path's fused transfer (adapter.py:1200-1243):
+    block_data -> memory objects with the dense slot mapping, memory objects ->
+    actual_blocks with the physical slot mapping, and an arbitrary token
+    mapping with padding, K and V in one launch."""
+    bs, H, D = 16, 8, 128
+    block = (bs, 2, H, D) if token_major else (2, bs, H, D)
+    layout = adapter_mod._MergedKVBlockLayout.detect(block)
+    k, m = 24, 64
+    g = torch.Generator().manual_seed(31)
+    mk = (lambda shape: torch.zeros(shape, dtype=torch.float16, pin_memory=True)) if where == "host" else \
+        (lambda shape: torch.zeros(shape, dtype=torch.float16, device=DEV))
+    pool = mk((40, *layout.transfer_shape))
+    rows = torch.randperm(40, generator=g)[:k].tolist()
+    objs = [pool[r] for r in rows]
+    block_data = _cache(k, block, torch.float16, 21)
+    ext.batched_fused_single_layer_kv_transfer(objs, None, block_data, layout.dense_slot_mapping(k, device=DEV),
+                                               layout.chunk_offsets(k), layout.chunk_sizes(k), True, 1,
+                                               token_major, False)
+    torch.cuda.synchronize()
+    flat = layout.flatten_block_batch(block_data)
+    for i, r in enumerate(rows):
+        assert torch.equal(pool[r].to(DEV), flat[i]), i
+    actual = torch.zeros((m, *block), dtype=torch.float16, device=DEV)
+    slots = torch.randperm(m, generator=g)[:k].to(DEV)
+    ext.batched_fused_single_layer_kv_transfer(objs, None, actual, layout.physical_slot_mapping(slots),
+                                               layout.chunk_offsets(k), layout.chunk_sizes(k), False, 1,
+                                               token_major, False)
+    torch.cuda.synchronize()
+    for i, s_ in enumerate(slots.tolist()):
+        assert torch.equal(actual[s_], layout.restore_block_tensor(objs[i].to(DEV))), i
+    # arbitrary token mapping: 6 chunks of 8 tokens, offsets out of order, padding slots
+    T, n = 8, 6
+    mapping = torch.randperm(m * bs, generator=g)[: n * T].to(DEV)
+    mapping[5] = -1
+    offsets = [T * j for j in (3, 0, 5, 1, 4, 2)]
+    tshape = (T, 2, layout.hidden_dim) if token_major else (2, T, layout.hidden_dim)
+    pool2 = mk((n, *tshape))
+    objs2 = list(pool2.unbind(0))
+    ext.batched_fused_single_layer_kv_transfer(objs2, None, actual, mapping, offsets, [T] * n, True, 1, token_major)
+    torch.cuda.synchronize()
+    mp = mapping.tolist()
+    for i, off in enumerate(offsets):
+        for t in range(T):
+            sl = mp[off + t]
+            for kv in (0, 1):
+                got = _obj_token(objs2[i], layout, t, kv).to(DEV)
+                want = torch.zeros_like(got) if sl < 0 else _kv_token(actual, layout, sl, kv)
+                assert torch.equal(got, want), (i, t, kv)
+    fresh = torch.zeros_like(actual)
+    ext.batched_fused_single_layer_kv_transfer(objs2, None, fresh, mapping, offsets, [T] * n, False, 1, token_major)
+    torch.cuda.synchronize()
+    for i, off in enumerate(offsets):
+        for t in range(T):
+            sl = mp[off + t]
+            if sl >= 0:
+                for kv in (0, 1):
+                    assert torch.equal(_kv_token(fresh, layout, sl, kv), _obj_token(objs2[i], layout, t, kv).to(DEV))
+    with pytest.raises(ValueError):  # objects that are not rows of one buffer
+        ext.batched_fused_single_layer_kv_transfer([mk(tshape), mk(tshape)], None, actual, mapping[: 2 * T],
+                                                   [0, T], [T, T], True, 1, token_major)
+    with pytest.raises(ValueError):  # wrong token order for the block layout
+        ext.batched_fused_single_layer_kv_transfer(objs2, None, actual, mapping, offsets, [T] * n, True, 1,
+                                                   not token_major)
+    ext.check_status(DEV)
