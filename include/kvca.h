@@ -314,12 +314,15 @@ typedef struct kvca_device_store {
  * adapter.py:735-756; a repeated evicted id keeps its last payload), the
  * store's presence check of the misses (adapter.py:801-806), the fill of the
  * victims from the store (adapter.py:779-787) and the commit (miss usage 1).
+ * Spill and fill of each victim run in one exchange launch, so with a host
+ * store both directions of the host link are busy at once; a miss that the
+ * same call spills is filled by a second launch after every spill.
  * actual_blocks: slot s at d_actual + s * actual_row_stride, row_bytes each.
- * d_work: 7 * count int64, d_work_meta: count slot_meta words.  d_result:
- * the returned slot per request.  d_counts[7] as for kvca_plan_load; a miss
- * absent from the store gives code KVCA_ERR_BLOCK_NOT_FOUND after the spill
- * and before any fill or commit, as the reference's backend raises.  No
- * reference counterpart as one call.
+ * d_work: 9 * count int64, d_work_meta: count slot_meta words.  d_result:
+ * the returned slot per request.  d_counts: 8 words, the first 7 as for
+ * kvca_plan_load; a miss absent from the store gives code
+ * KVCA_ERR_BLOCK_NOT_FOUND after the spill and before any fill or commit, as
+ * the reference's backend raises.  No reference counterpart as one call.
  */
 int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
                            int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
@@ -386,6 +389,21 @@ typedef struct kvca_chunk_desc {
   int64_t row_stride;
   int64_t plane_stride;
 } kvca_chunk_desc;
+
+/*
+ * Spill and fill of the same slots in one pass (one plane): for each row j,
+ * the bytes of slot slots->index[j] go to store row store->index[j] and the
+ * slot is then filled from store row d_fill_rows[j]; a negative store or
+ * fill index skips that part, a negative slot the row.  The adapter's load
+ * with evictions (backend.save_blocks of the victims, adapter.py:735-756,
+ * then the fill, :779-787) as one launch: with the store in pinned host
+ * memory (KVCA_FLAG_HOST_MEMORY) both directions of the host link run at
+ * once.  Spill and fill store rows must be disjoint (a row spilled and
+ * filled in one call has no defined order).  No reference counterpart.
+ */
+int kvca_exchange(const kvca_paged_desc* slots, const kvca_paged_desc* store,
+                  const int64_t* d_fill_rows, int64_t num_rows, int64_t row_bytes, int32_t flags,
+                  int64_t* d_status, kvca_stream_t stream);
 
 /* Paged -> contiguous: per plane, index_select of rows (adapter.py:543). */
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,

@@ -137,6 +137,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_ptr],
     ),
     "kvca_host_memory_usable": (c_int, [c_ptr, c_i64]),
+    "kvca_exchange": (
+        c_int,
+        [ctypes.POINTER(PagedDesc), ctypes.POINTER(PagedDesc), c_ptr, c_i64, c_i64, ctypes.c_int32, c_ptr, c_ptr],
+    ),
     "kvca_gather": (
         c_int,
         [ctypes.POINTER(PagedDesc), ctypes.POINTER(ChunkDesc), c_i64, c_i64, c_i64, ctypes.c_int32,

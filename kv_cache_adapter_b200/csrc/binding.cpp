@@ -350,19 +350,22 @@ int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   vec = min_align(vec, store->storage);
   vec = min_align(vec, static_cast<uint64_t>(store->storage_row_stride));
   const int64_t k = count;
-  kvca::PagedSide actual_evicted, store_evicted, store_missed, actual_filled;
-  one_plane(d_actual, num_slots, actual_row_stride, d_work + 5 * k, &actual_evicted);
-  one_plane(store->storage, num_logical, store->storage_row_stride, d_work + 4 * k, &store_evicted);
-  one_plane(store->storage, num_logical, store->storage_row_stride, d_work + 2 * k, &store_missed);
-  one_plane(d_actual, num_slots, actual_row_stride, d_work + 6 * k, &actual_filled);
-  kvca::MoveArgs spill{kvca::MoveKind::kCopyPaged, &actual_evicted, nullptr, &store_evicted,
-                       nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE | store->move_flags,
-                       d_status};
-  rc = status_of(kvca::launch_move(spill, stream));
+  const int32_t flags = KVCA_FLAG_SKIP_NEGATIVE | store->move_flags;
+  const int64_t* xslot = d_work + 6 * k;
+  const int64_t* spill_to = d_work + 7 * k;
+  const int64_t* fill_from = d_work + 8 * k;
+  const int64_t* gate = d_counts + 7;
+  kvca::PagedSide slots, store_out, store_in, slots_in;
+  one_plane(d_actual, num_slots, actual_row_stride, xslot, &slots);
+  one_plane(store->storage, num_logical, store->storage_row_stride, spill_to, &store_out);
+  kvca::ExchangeArgs x{&slots, &store_out, fill_from, gate, k, row_bytes, vec, flags, d_status};
+  rc = status_of(kvca::launch_exchange(x, stream));
   if (rc != KVCA_OK) return rc;
-  kvca::MoveArgs fill{kvca::MoveKind::kCopyPaged, &store_missed, nullptr, &actual_filled,
-                      nullptr, 1, k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE | store->move_flags,
-                      d_status};
+  // a miss that this call also spills is filled after every spill (gate set)
+  one_plane(store->storage, num_logical, store->storage_row_stride, fill_from, &store_in);
+  one_plane(d_actual, num_slots, actual_row_stride, xslot, &slots_in);
+  kvca::MoveArgs fill{kvca::MoveKind::kCopyPaged, &store_in, nullptr, &slots_in, nullptr, 1, k,
+                      row_bytes, vec, flags, d_status, gate};
   return status_of(kvca::launch_move(fill, stream));
 }
 
@@ -408,6 +411,24 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   kvca::MoveArgs scatter{kvca::MoveKind::kScatter, nullptr, &data, &actual_selected, nullptr, 1,
                          k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
   return status_of(kvca::launch_move(scatter, stream));
+}
+
+int kvca_exchange(const kvca_paged_desc* slots, const kvca_paged_desc* store,
+                  const int64_t* d_fill_rows, int64_t num_rows, int64_t row_bytes, int32_t flags,
+                  int64_t* d_status, kvca_stream_t stream) {
+  if (!common_move_args_ok(1, num_rows, row_bytes)) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_rows == 0) return KVCA_OK;
+  if (slots == nullptr || store == nullptr || slots->index == nullptr || store->index == nullptr ||
+      d_fill_rows == nullptr || slots->block_size != 1 || store->block_size != 1)
+    return KVCA_ERR_BAD_ARGUMENT;
+  int vec = align_of(static_cast<uint64_t>(row_bytes));
+  if (!check_paged(slots, 1, row_bytes, &vec) || !check_paged(store, 1, row_bytes, &vec))
+    return KVCA_ERR_BAD_ARGUMENT;
+  kvca::PagedSide a, st;
+  to_side(slots, 1, &a);
+  to_side(store, 1, &st);
+  kvca::ExchangeArgs x{&a, &st, d_fill_rows, nullptr, num_rows, row_bytes, vec, flags, d_status};
+  return status_of(kvca::launch_exchange(x, stream));
 }
 
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,

@@ -1403,27 +1403,57 @@ __device__ void store_spill_prepare(const int64_t* evict_ids, int64_t* evict_slo
   __syncthreads();
 }
 
-// After plan_load: spill preparation, then the backend's presence check of
-// the misses (adapter.py:801-806); when every miss is present, the slots to
-// fill (load_slots = victims) and the commit.  A missing block sets
-// counts[3..4] = KVCA_ERR_BLOCK_NOT_FOUND, id and leaves load_slots at -1:
-// the evictions stay spilled, nothing is filled or committed, as when the
-// backend raises.  Nothing runs when the plan failed.
+// After plan_load: the per-victim rows of the exchange, the backend's
+// presence check of the misses (adapter.py:801-806) and the commit.
+//   xslot[j]     = victims[j] for every miss j (the slot spilled and filled);
+//   spill_to[j]  = the victim's previous logical id when it is evicted and j
+//                  is the last victim evicting that id (index_copy_ applied in
+//                  order keeps the last payload), else -1;
+//   fill_from[j] = miss_ids[j] when every miss is present in the store.
+// Evicted ids are marked present first, as the backend's save precedes its
+// load.  A miss that is also spilled by this call must be filled after the
+// spill: counts[7] (the gate) is set and the fill moves to a second launch.
+// A missing block sets counts[3..4] = KVCA_ERR_BLOCK_NOT_FOUND, id; the
+// spill still runs, nothing is filled or committed, as when the backend
+// raises.  `scratch` (one int per logical id) is zero on entry and left zero.
+// Nothing runs when the plan failed.
 template <typename MetaT>
 __global__ void __launch_bounds__(1024)
     store_load_finish_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
                              int64_t* counts, const int64_t* hit_slots, const int64_t* hit_pins,
                              const MetaT* hit_usage, const int64_t* miss_ids,
-                             const int64_t* victims, const int64_t* evict_ids,
-                             int64_t* evict_slots, int32_t* scratch, uint8_t* present,
-                             int64_t* load_slots, int64_t* status) {
+                             const int64_t* victims, const int64_t* evict_ids, int32_t* scratch,
+                             uint8_t* present, int64_t* xslot, int64_t* spill_to,
+                             int64_t* fill_from, int64_t* status) {
   __shared__ int bad;
   __shared__ int missing;
+  __shared__ int conflict;
   __shared__ long long missing_id;
   if (counts[3] != 0) return;  // written by the plan launch: uniform
   const int64_t nh = counts[0], nm = counts[1], ne = counts[2];
-  if (threadIdx.x == 0) bad = missing = 0;
-  store_spill_prepare(evict_ids, evict_slots, ne, scratch, present);
+  if (threadIdx.x == 0) bad = missing = conflict = 0;
+  for (int64_t j = threadIdx.x; j < nm; j += blockDim.x) {
+    const int64_t prev = p2l[victims[j]];
+    const bool ev = prev >= 0 && prev != miss_ids[j];
+    spill_to[j] = ev ? prev : -1;
+    xslot[j] = victims[j];
+    if (ev) atomicMax(scratch + prev, static_cast<int32_t>(j + 1));
+  }
+  __syncthreads();
+  for (int64_t j = threadIdx.x; j < nm; j += blockDim.x) {
+    const int64_t sp = spill_to[j];
+    if (sp >= 0 && __ldcg(scratch + sp) != static_cast<int32_t>(j + 1)) spill_to[j] = -1;
+    if (__ldcg(scratch + miss_ids[j]) != 0) conflict = 1;
+  }
+  __syncthreads();
+  for (int64_t j = threadIdx.x; j < nm; j += blockDim.x) {
+    const int64_t prev = p2l[victims[j]];
+    if (prev >= 0 && prev != miss_ids[j]) {
+      scratch[prev] = 0;
+      present[prev] = 1;
+    }
+  }
+  __syncthreads();
   for (int64_t j = threadIdx.x; j < nm; j += blockDim.x)
     if (present[miss_ids[j]] == 0 && atomicCAS(&missing, 0, 1) == 0) missing_id = miss_ids[j];
   __syncthreads();
@@ -1434,7 +1464,8 @@ __global__ void __launch_bounds__(1024)
     }
     return;
   }
-  for (int64_t j = threadIdx.x; j < nm; j += blockDim.x) load_slots[j] = victims[j];
+  for (int64_t j = threadIdx.x; j < nm; j += blockDim.x) fill_from[j] = miss_ids[j];
+  if (threadIdx.x == 0) counts[7] = conflict;
   commit_load_body<MetaT>(l2p, n_logical, p2l, meta, n, evict_ids, ne, miss_ids, victims, nm,
                           hit_slots, hit_pins, hit_usage, nh, nullptr, status, &bad);
 }
@@ -1475,6 +1506,7 @@ struct MoveParams {
   int tpr_log2;  // threads per work item = 1 << tpr_log2 (a power of two <= 32)
   int32_t flags;
   int64_t* status;
+  const int64_t* gate;  // non-null: the launch moves nothing unless *gate != 0
 };
 
 template <typename V>
@@ -1523,6 +1555,11 @@ __device__ __forceinline__ int64_t chunk_row_offset(const ChunkSide& side, int64
 }
 
 constexpr int kMoverThreads = 512;
+// Moves over the host link saturate it with a few CTAs; a full grid only
+// adds contention (B200, random 64 KiB rows: exchange 80 GB/s at 8-16 CTAs,
+// 79 at 32, 73 at 148; one way 52 vs 51 GB/s; 256 B rows device->host 47 at
+// 16 CTAs vs 38 at 148).
+constexpr int kHostMoverCtas = 16;
 constexpr int kMoverUnroll = 8;
 constexpr int64_t kMoverSegmentBytes = 16384;
 
@@ -1537,6 +1574,7 @@ constexpr int64_t kMoverSegmentBytes = 16384;
 // rows move with plain loads and stores there (no non-coherent cache path).
 template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost>
 __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_constant__ MoveParams p) {
+  if (p.gate != nullptr && *p.gate == 0) return;
   const int tpr = 1 << p.tpr_log2;
   const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int lane = static_cast<int>(gtid & (tpr - 1));
@@ -1633,11 +1671,123 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
   int64_t blocks = (threads_needed + kMoverThreads - 1) / kMoverThreads;
   const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
   if (blocks > resident) blocks = resident;
+  if (kHost && blocks > kHostMoverCtas) blocks = kHostMoverCtas;
   if (blocks < 1) blocks = 1;
   kernel<<<static_cast<unsigned>(blocks), kMoverThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// Exchange: spill and fill of the same slots in one pass
+// ---------------------------------------------------------------------------
+//
+// Row j: a.index[j] is a slot of the blocks; its row goes out to store row
+// store.index[j] (spill, when >= 0) and store row fill_from[j] comes in
+// (fill, when >= 0), so that one launch moves both directions and, with the
+// store in host memory, both directions of the host link are busy at once.
+// Each lane loads its vectors of the slot and of the fill row before it
+// stores either, so a spill always reads the slot's old bytes.  All loads are
+// plain: the slot rows are written by this launch.  With *gate != 0 the
+// launch only spills (a fill that must wait for every spill follows it).
+
+struct ExchangeParams {
+  PagedSide a;
+  PagedSide store;
+  const int64_t* fill_from;
+  const int64_t* gate;
+  int64_t num_rows;
+  int64_t row_vecs;
+  int64_t seg_vecs;
+  int64_t segs_per_row;
+  int tpr_log2;
+  int32_t flags;
+  int64_t* status;
+};
+
+template <typename V>
+__global__ void __launch_bounds__(kMoverThreads) exchange_rows_kernel(const __grid_constant__ ExchangeParams p) {
+  const bool fill_open = p.gate == nullptr || *p.gate == 0;
+  const int tpr = 1 << p.tpr_log2;
+  const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int lane = static_cast<int>(gtid & (tpr - 1));
+  const int64_t group = gtid >> p.tpr_log2;
+  const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
+  const int64_t segs = p.segs_per_row;
+  const int64_t items = segs * p.num_rows;
+  const int64_t per = items / num_groups;
+  const int64_t rem = items - per * num_groups;
+  const int64_t begin = group * per + (group < rem ? group : rem);
+  const int64_t end = begin + per + (group < rem ? 1 : 0);
+  const bool lead = lane == 0;
+  int64_t cur_row = -1;
+  int64_t a_row = -1, out_row = -1, in_row = -1;
+  for (int64_t g = begin; g < end; ++g) {
+    const int64_t r = g / segs;
+    const int64_t sg = g - r * segs;
+    if (r != cur_row) {
+      cur_row = r;
+      a_row = paged_row_offset(p.a, r, p.flags, p.status, lead);
+      out_row = paged_row_offset(p.store, r, p.flags, p.status, lead);
+      in_row = -1;
+      if (fill_open) {
+        const int64_t idx = p.fill_from[r];
+        if (idx >= p.store.num_blocks) {
+          if (lead) report(p.status, KVCA_ERR_BAD_INDEX, idx);
+        } else if (idx >= 0) {
+          in_row = idx * p.store.block_stride;
+        }
+      }
+    }
+    if (a_row < 0 || (out_row < 0 && in_row < 0)) continue;
+    V* slot = reinterpret_cast<V*>(p.a.planes[0] + a_row);
+    V* out = reinterpret_cast<V*>(p.store.planes[0] + (out_row >= 0 ? out_row : 0));
+    const V* in = reinterpret_cast<const V*>(p.store.planes[0] + (in_row >= 0 ? in_row : 0));
+    const int64_t v_begin = sg * p.seg_vecs;
+    const int64_t v_end = v_begin + p.seg_vecs < p.row_vecs ? v_begin + p.seg_vecs : p.row_vecs;
+    for (int64_t b = v_begin + lane; b < v_end; b += static_cast<int64_t>(tpr) * kMoverUnroll) {
+      V old_bytes[kMoverUnroll];
+      V new_bytes[kMoverUnroll];
+#pragma unroll
+      for (int u = 0; u < kMoverUnroll; ++u) {
+        const int64_t i = b + static_cast<int64_t>(u) * tpr;
+        if (i < v_end) {
+          if (out_row >= 0) old_bytes[u] = slot[i];
+          if (in_row >= 0) new_bytes[u] = in[i];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kMoverUnroll; ++u) {
+        const int64_t i = b + static_cast<int64_t>(u) * tpr;
+        if (i < v_end) {
+          if (out_row >= 0) out[i] = old_bytes[u];
+          if (in_row >= 0) slot[i] = new_bytes[u];
+        }
+      }
+    }
+  }
+}
+
+template <typename V>
+cudaError_t launch_exchange_typed(const ExchangeParams& p, cudaStream_t stream) {
+  auto kernel = exchange_rows_kernel<V>;
+  static int blocks_per_sm = 0;
+  if (blocks_per_sm == 0) {
+    int b = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kMoverThreads, 0);
+    if (e != cudaSuccess) return e;
+    blocks_per_sm = b > 0 ? b : 1;
+  }
+  const int sms = device_sm_count();
+  const int64_t threads_needed = (p.num_rows * p.segs_per_row) << p.tpr_log2;
+  int64_t blocks = (threads_needed + kMoverThreads - 1) / kMoverThreads;
+  const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
+  if (blocks > resident) blocks = resident;
+  if ((p.flags & KVCA_FLAG_HOST_MEMORY) && blocks > kHostMoverCtas) blocks = kHostMoverCtas;
+  if (blocks < 1) blocks = 1;
+  kernel<<<static_cast<unsigned>(blocks), kMoverThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
 
 // ---------------------------------------------------------------------------
 // Row mover on the TMA bulk-copy engine (16-byte aligned rows of >= 1 KiB)
@@ -1888,10 +2038,58 @@ cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
   while ((int64_t{2} << p.tpr_log2) <= lanes) ++p.tpr_log2;
   p.flags = a.flags;
   p.status = a.status;
+  p.gate = a.gate;
+  if (a.gate != nullptr && a.kind == MoveKind::kCopyPaged) {  // gated moves stay on the SIMT kernel
+    switch (a.vec_bytes) {
+      case 16:
+        return (a.flags & KVCA_FLAG_HOST_MEMORY) ? launch_move_typed<true, true, uint4, true>(p, stream)
+                                                 : launch_move_typed<true, true, uint4>(p, stream);
+      case 8:
+        return (a.flags & KVCA_FLAG_HOST_MEMORY) ? launch_move_typed<true, true, uint2, true>(p, stream)
+                                                 : launch_move_typed<true, true, uint2>(p, stream);
+      case 4:
+        return (a.flags & KVCA_FLAG_HOST_MEMORY) ? launch_move_typed<true, true, unsigned int, true>(p, stream)
+                                                 : launch_move_typed<true, true, unsigned int>(p, stream);
+      case 2:
+        return (a.flags & KVCA_FLAG_HOST_MEMORY) ? launch_move_typed<true, true, unsigned short, true>(p, stream)
+                                                 : launch_move_typed<true, true, unsigned short>(p, stream);
+      default:
+        return (a.flags & KVCA_FLAG_HOST_MEMORY) ? launch_move_typed<true, true, unsigned char, true>(p, stream)
+                                                 : launch_move_typed<true, true, unsigned char>(p, stream);
+    }
+  }
   switch (a.kind) {
     case MoveKind::kGather: return launch_move_vec<true, false>(p, a.vec_bytes, stream);
     case MoveKind::kScatter: return launch_move_vec<false, true>(p, a.vec_bytes, stream);
     default: return launch_move_vec<true, true>(p, a.vec_bytes, stream);
+  }
+}
+
+cudaError_t launch_exchange(const ExchangeArgs& a, cudaStream_t stream) {
+  ExchangeParams p;
+  memset(&p, 0, sizeof(p));
+  p.a = *a.slots;
+  p.store = *a.store;
+  p.fill_from = a.fill_from;
+  p.gate = a.gate;
+  p.num_rows = a.num_rows;
+  p.row_vecs = a.row_bytes / a.vec_bytes;
+  p.seg_vecs = kMoverSegmentBytes / a.vec_bytes;
+  if (p.seg_vecs < 1) p.seg_vecs = 1;
+  if (p.seg_vecs >= p.row_vecs) p.seg_vecs = p.row_vecs;
+  p.segs_per_row = (p.row_vecs + p.seg_vecs - 1) / p.seg_vecs;
+  int64_t lanes = p.seg_vecs / 4;
+  if (lanes > 32) lanes = 32;
+  p.tpr_log2 = 0;
+  while ((int64_t{2} << p.tpr_log2) <= lanes) ++p.tpr_log2;
+  p.flags = a.flags;
+  p.status = a.status;
+  switch (a.vec_bytes) {
+    case 16: return launch_exchange_typed<uint4>(p, stream);
+    case 8: return launch_exchange_typed<uint2>(p, stream);
+    case 4: return launch_exchange_typed<unsigned int>(p, stream);
+    case 2: return launch_exchange_typed<unsigned short>(p, stream);
+    default: return launch_exchange_typed<unsigned char>(p, stream);
   }
 }
 
@@ -2035,10 +2233,14 @@ cudaError_t launch_store_load_meta(int meta_bits, int order, int64_t* l2p, int64
   int64_t* victims = work + 3 * k;
   int64_t* evict_ids = work + 4 * k;
   int64_t* evict_slots = work + 5 * k;
-  int64_t* load_slots = work + 6 * k;
-  // miss_ids, evict_ids, evict_slots and load_slots index the copies: -1
-  // (skipped, no error) wherever the plan or the finish kernel writes nothing
-  cudaError_t e = cudaMemsetAsync(miss_ids, 0xFF, 5 * k * sizeof(int64_t), stream);
+  int64_t* xslot = work + 6 * k;
+  int64_t* spill_to = work + 7 * k;
+  int64_t* fill_from = work + 8 * k;
+  // xslot, spill_to and fill_from index the exchange: -1 (skipped, no error)
+  // wherever the finish kernel writes nothing; the gate starts closed
+  cudaError_t e = cudaMemsetAsync(xslot, 0xFF, 3 * k * sizeof(int64_t), stream);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(counts + 7, 0, sizeof(int64_t), stream);
   if (e != cudaSuccess) return e;
   e = launch_plan_load(meta_bits, order, l2p, num_logical, p2l, meta, num_slots, search_start, ids,
                        count, bitmap, result, hit_slots, hit_pins, work_meta, miss_ids, victims,
@@ -2048,7 +2250,8 @@ cudaError_t launch_store_load_meta(int meta_bits, int order, int64_t* l2p, int64
                                     l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
                                     counts, hit_slots, hit_pins,
                                     static_cast<const MetaT*>(work_meta), miss_ids, victims,
-                                    evict_ids, evict_slots, scratch, present, load_slots, status));
+                                    evict_ids, scratch, present, xslot, spill_to, fill_from,
+                                    status));
   return cudaGetLastError();
 }
 

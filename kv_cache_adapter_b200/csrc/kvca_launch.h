@@ -43,9 +43,28 @@ struct MoveArgs {
   int vec_bytes;  // 16, 8, 4, 2 or 1: widest access every address allows
   int32_t flags;
   int64_t* status;
+  const int64_t* gate = nullptr;  // copy only: move nothing unless *gate != 0 (SIMT kernel)
 };
 
 cudaError_t launch_move(const MoveArgs& args, cudaStream_t stream);
+
+// Spill + fill of the same slots in one launch (one plane): row j sends slot
+// slots->index[j] to store row store->index[j] and fills it from store row
+// fill_from[j]; negative indices skip that part.  With *gate != 0 only the
+// spill runs.
+struct ExchangeArgs {
+  const PagedSide* slots;
+  const PagedSide* store;
+  const int64_t* fill_from;
+  const int64_t* gate;
+  int64_t num_rows;
+  int64_t row_bytes;
+  int vec_bytes;
+  int32_t flags;
+  int64_t* status;
+};
+
+cudaError_t launch_exchange(const ExchangeArgs& args, cudaStream_t stream);
 
 cudaError_t launch_inspect_load(int meta_bits, const int64_t* l2p, int64_t num_logical,
                                 const void* meta, int64_t num_slots, const int64_t* ids,
@@ -113,9 +132,11 @@ cudaError_t launch_plan_save(int meta_bits, int order, const int64_t* l2p, int64
                              int64_t* status, cudaStream_t stream);
 
 // Fused load / save with a device-resident block store: memset, plan, finish
-// (metadata); the caller then enqueues the two row copies.  Work layouts:
+// (metadata); the caller then enqueues the row moves (load: the exchange and
+// the gated fill; save: the spill and the data scatter).  Work layouts:
 // load  int64 [hit_slots, hit_pins, miss_ids, victims, evict_ids, evict_slots,
-//              load_slots] x count, meta [hit_usage] x count;
+//              xslot, spill_to, fill_from] x count, meta [hit_usage] x count,
+//       counts 8 words (counts[7]: the gate of the fill that follows spills);
 // save  int64 [selected, allocated, evict_ids, evict_slots, move_slots] x count,
 //       meta [final_pins, final_usage] x count.
 cudaError_t launch_store_load_meta(int meta_bits, int order, int64_t* l2p, int64_t num_logical,

@@ -48,6 +48,7 @@ __all__ = [
     "plan_load",
     "plan_save",
     "copy_tokens",
+    "exchange_blocks",
     "batched_fused_single_layer_kv_transfer",
     "load_device_store",
     "save_device_store",
@@ -558,10 +559,10 @@ def load_device_store(logical_to_physical: torch.Tensor, physical_to_logical: to
     dev = slot_meta.device
     k = logical_block_ids.numel()
     n = slot_meta.numel()
-    work = torch.empty(7 * k, dtype=torch.int64, device=dev)
+    work = torch.empty(9 * k, dtype=torch.int64, device=dev)
     work_meta = torch.empty(k, dtype=slot_meta.dtype, device=dev)
     result = torch.empty(k, dtype=torch.int64, device=dev)
-    counts = torch.empty(7, dtype=torch.int64, device=dev)
+    counts = torch.empty(8, dtype=torch.int64, device=dev)
     with _on(dev):
         rc = _lib_handle.kvca_load_device_store(
             _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
@@ -804,6 +805,35 @@ def copy_blocks(src_blocks: torch.Tensor, src_ids: torch.Tensor, dst_blocks: tor
         raise ValueError("src_ids and dst_ids must have the same length")
     _launch_move("kvca_copy_paged", s.desc(src_ids), d.desc(dst_ids), 1, src_ids.numel(),
                  s.row_bytes, _host_flag(s, d), dev, check)
+
+
+def exchange_blocks(actual_blocks: torch.Tensor, slot_ids: torch.Tensor, store: torch.Tensor,
+                    spill_ids: torch.Tensor, fill_ids: torch.Tensor, *, check: bool | None = None) -> None:
+    """For each j: ``store[spill_ids[j]] = actual_blocks[slot_ids[j]]`` (old
+    bytes), then ``actual_blocks[slot_ids[j]] = store[fill_ids[j]]``, in one
+    launch; negative spill / fill ids skip that part.  The eviction spill and
+    the miss fill of a load (adapter.py:735-756, :779-787) in one pass: with
+    ``store`` in pinned host memory both directions of the host link are
+    busy at once.  Spilled and filled store rows must be disjoint."""
+    a = _planes([actual_blocks], 1, "actual_blocks")
+    st = _planes([store], 1, "store", allow_host=True)
+    if a.row_bytes != st.row_bytes or a.dtype != st.dtype:
+        raise ValueError("actual_blocks and store must share block shape and dtype")
+    dev = _move_device(a, st, slot_ids)
+    for t, name in ((slot_ids, "slot_ids"), (spill_ids, "spill_ids"), (fill_ids, "fill_ids")):
+        _require_index(t, dev, name)
+    k = slot_ids.numel()
+    if spill_ids.numel() != k or fill_ids.numel() != k:
+        raise ValueError("slot_ids, spill_ids and fill_ids must have the same length")
+    if k == 0:
+        return
+    slots_desc, store_desc = a.desc(slot_ids), st.desc(spill_ids)
+    with _on(dev):
+        rc = _lib_handle.kvca_exchange(ctypes.byref(slots_desc), ctypes.byref(store_desc),
+                                       _ptr(fill_ids), k, a.row_bytes,
+                                       _lib.KVCA_FLAG_SKIP_NEGATIVE | _host_flag(st), _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "exchange_blocks")
+    _maybe_check(dev, check, "exchange_blocks")
 
 
 def _chunks_of(k: int, per_chunk: int | None, what: str) -> tuple[int, int]:

@@ -305,3 +305,36 @@ def test_fused_single_layer_kv_transfer(ext, token_major, where):
         ext.batched_fused_single_layer_kv_transfer(objs2, None, actual, mapping, offsets, [T] * n, True, 1,
                                                    not token_major)
     ext.check_status(DEV)
+
+
+@pytest.mark.parametrize("where", ["host", "device"])
+@pytest.mark.parametrize("row_shape,dtype", [((2, 16, 8, 128), torch.float16), ((3,), torch.float16),
+                                             ((40,), torch.float32)])
+def test_exchange_blocks(ext, where, row_shape, dtype):
+    """Spill the old bytes of each slot to one store row and fill it from
+    another, in one launch; padding entries skip their part."""
+    n, nl, k = 200, 600, 77
+    g = torch.Generator().manual_seed(41)
+    actual = _cache(n, row_shape, dtype, 42)
+    store = _cache(nl, row_shape, dtype, 43, device="cpu")
+    store = store.pin_memory() if where == "host" else store.to(DEV)
+    slots = torch.randperm(n, generator=g)[:k]
+    rows = torch.randperm(nl, generator=g)
+    spill, fill = rows[:k].clone(), rows[k:2 * k].clone()
+    spill[::7] = -1
+    fill[3::9] = -1
+    slots[10] = -1
+    want_actual, want_store = actual.cpu().clone(), store.cpu().clone()
+    for j in range(k):
+        s_ = int(slots[j])
+        if s_ < 0:
+            continue
+        if spill[j] >= 0:
+            want_store[spill[j]] = want_actual[s_]
+        if fill[j] >= 0:
+            want_actual[s_] = store.cpu()[fill[j]]
+    ext.exchange_blocks(actual, slots.to(DEV), store, spill.to(DEV), fill.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(actual.cpu(), want_actual)
+    assert torch.equal(store.cpu(), want_store)
+    ext.check_status(DEV)

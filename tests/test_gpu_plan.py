@@ -323,3 +323,40 @@ def api_gpu():
     import kv_cache_adapter_b200 as m
 
     return m
+
+
+@pytest.mark.parametrize("host_tier", [False, True])
+def test_load_that_spills_and_fills_one_id(host_tier):
+    """A stale reverse entry (two slots saved for one id) makes a later load
+    evict id 1 from one victim while loading id 1 into another: the store
+    must take the spilled payload before the fill reads it (the reference's
+    save_blocks precedes load_blocks)."""
+    prog = [("save", [1, 1]), ("load", [2]), ("release", [2]), ("load", [3]), ("release", [3]),
+            ("load", [0, 1])]
+    nl, na = 8, 3
+    init = {i: torch.full((2,), float(i)) for i in range(nl)}
+    cpu_ops = OracleOps()
+    ref = adapter_mod.KVCacheAdapter(
+        na, nl, torch.zeros((na, 2)),
+        adapter_mod.InMemoryBlockStoreBackend(dict(init), num_logical_blocks=nl, ops=cpu_ops), native_ext=cpu_ops)
+    backend = adapter_mod.InMemoryBlockStoreBackend({k: v.to(DEV) for k, v in init.items()}, num_logical_blocks=nl,
+                                                    host_tier=host_tier, device=DEV)
+    gpu = adapter_mod.KVCacheAdapter(na, nl, torch.zeros((na, 2), device=DEV), backend)
+    assert gpu._device_store() is not None
+    for step, (op, ids) in enumerate(prog):
+        for ad, dev in ((ref, torch.device("cpu")), (gpu, DEV)):
+            t = torch.tensor(ids, device=dev)
+            if op == "load":
+                ad.load(t)
+            elif op == "save":
+                ad.save(t, (torch.arange(2 * len(ids), dtype=torch.float32).reshape(-1, 2) + 100 * step).to(dev))
+            else:
+                ad.release(t)
+        assert torch.equal(gpu.actual_blocks.cpu(), ref.actual_blocks), step
+        assert torch.equal(backend._storage.cpu(), ref.backend._storage), step
+        assert gpu._logical_to_physical.tolist() == ref._logical_to_physical.tolist(), step
+    # the last load filled id 1 with the payload it spilled in the same call
+    assert torch.equal(ref.backend._storage[1], torch.tensor([2.0, 3.0]))
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda
+
+    kv_cache_adapter_cuda.check_status(DEV)
