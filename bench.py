@@ -526,7 +526,8 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         },
         "tokens_per_s": round(world * tokens / (ms / 1e3), 1),
         "evictions_per_s": round(world * blocks / (ms / 1e3), 1),
-        "gpu_launches_per_decode_step": "1 scatter; plus pop, gather, commit, release on steps that evict",
+        "gpu_launches_per_decode_step": "append_step (pop, commit, release, slot_mapping) + scatter_tokens; "
+                                        "plus one gather on steps that evict",
         "issue": "CUDA graph, one replay per 16-step cycle",
         "host_issued": {"value": round(world * moved / (eager_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                         "ms_per_decode_step": round(eager_ms / decode_steps, 5)},

@@ -348,6 +348,29 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
                            uint64_t d_block_data, int64_t* d_work, void* d_work_meta,
                            int64_t* d_counts, int64_t* d_status, kvca_stream_t stream);
 
+/*
+ * One decode step of a paged cache's block bookkeeping, for num_seqs
+ * sequences that each append one token per step.  The num_need sequences
+ * d_need[] (distinct) whose current block is full get new blocks: pop
+ * (kvca_pop_reusable_slots, no blocked slots) -> d_victims[num_need]; each
+ * victim's previous logical id is unmapped; victim j is committed as logical
+ * id *d_next_logical + j, pinned, usage 1 (kvca_commit_save_metadata with
+ * pins and usage 1); the full block (slot of d_cur_logical[q]) is released
+ * (kvca_release_metadata); d_cur_block / d_cur_logical / d_pos of the
+ * sequence are reset and *d_next_logical advances.  Then for every sequence
+ * d_slot_mapping[q] = d_cur_block[q] * block_size + d_pos[q] (the token's
+ * slot, adapter.py:1275-1285) and d_pos[q] += 1.  One launch, no host
+ * synchronisation (capturable in a graph).  Bad ids or too few reusable
+ * slots go to d_status and change nothing.  No reference counterpart as
+ * one call.
+ */
+int kvca_append_step(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                     int64_t* d_search_start, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                     const int64_t* d_need, int64_t num_need, int64_t* d_cur_block,
+                     int64_t* d_cur_logical, int64_t* d_pos, int64_t num_seqs, int64_t block_size,
+                     int64_t* d_next_logical, int64_t* d_victims, int64_t* d_slot_mapping,
+                     uint32_t* d_scratch_bitmap, int64_t* d_status, kvca_stream_t stream);
+
 /* 1 when [p, p + bytes) is pinned host memory that kernels can reach at the
  * same address, else 0.  No reference counterpart. */
 int kvca_host_memory_usable(const void* p, int64_t bytes);

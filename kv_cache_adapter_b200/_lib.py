@@ -137,6 +137,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_ptr],
     ),
     "kvca_host_memory_usable": (c_int, [c_ptr, c_i64]),
+    "kvca_append_step": (
+        c_int,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_i64,
+         c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
     "kvca_exchange": (
         c_int,
         [ctypes.POINTER(PagedDesc), ctypes.POINTER(PagedDesc), c_ptr, c_i64, c_i64, ctypes.c_int32, c_ptr, c_ptr],

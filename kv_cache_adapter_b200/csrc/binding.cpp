@@ -431,6 +431,25 @@ int kvca_exchange(const kvca_paged_desc* slots, const kvca_paged_desc* store,
   return status_of(kvca::launch_exchange(x, stream));
 }
 
+int kvca_append_step(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                     int64_t* d_search_start, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                     const int64_t* d_need, int64_t num_need, int64_t* d_cur_block,
+                     int64_t* d_cur_logical, int64_t* d_pos, int64_t num_seqs, int64_t block_size,
+                     int64_t* d_next_logical, int64_t* d_victims, int64_t* d_slot_mapping,
+                     uint32_t* d_scratch_bitmap, int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) ||
+      (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX) || num_slots <= 0 ||
+      num_logical <= 0 || num_seqs <= 0 || block_size <= 0 || num_need < 0 ||
+      num_need > num_seqs || !d_slot_meta || !d_search_start || !d_l2p || !d_p2l ||
+      !d_cur_block || !d_cur_logical || !d_pos || !d_next_logical || !d_slot_mapping ||
+      !d_scratch_bitmap || (num_need > 0 && (!d_need || !d_victims)))
+    return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_append_step(
+      meta_bits, order, d_slot_meta, num_slots, d_search_start, d_l2p, num_logical, d_p2l, d_need,
+      num_need, d_cur_block, d_cur_logical, d_pos, num_seqs, block_size, d_next_logical,
+      d_scratch_bitmap, d_victims, d_slot_mapping, d_status, stream));
+}
+
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,
                 int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
                 kvca_stream_t stream) {

@@ -1371,6 +1371,92 @@ __global__ void __launch_bounds__(1024)
 }
 
 // ---------------------------------------------------------------------------
+// Decode append: one step of a paged cache's block bookkeeping
+// ---------------------------------------------------------------------------
+//
+// Sequences append one token per step into their current block.  The c
+// sequences need[0..c) whose block is full get a new one in one CTA: pop(c)
+// (victims, in order), each victim's previous logical id unmapped (l2p = -1),
+// the victim committed as logical id next_logical + j, pinned, usage 1 (a
+// fresh save, as commit_save_metadata with pins and usage 1), the full block
+// released (pin - 1), and the sequence's block, logical id and position
+// reset.  Then every sequence's slot_mapping entry for this step is
+// cur_block * block_size + pos and its position advances.  The sequence is
+// the composition pop_reusable_slots -> commit_save_metadata ->
+// release_metadata of those ops (adapter.py:472-525, :647-651, :309-336).
+// Ids are checked before anything changes; too few reusable slots change
+// nothing.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    append_step_kernel(MetaT* meta, int64_t n, int64_t* search_start, int64_t* l2p,
+                       int64_t n_logical, int64_t* p2l, const int64_t* need, int64_t c,
+                       int64_t* cur_block, int64_t* cur_logical, int64_t* pos, int64_t seqs,
+                       int64_t block_size, int64_t* next_logical, uint32_t* bitmap, int order,
+                       bool aligned, int64_t* victims, int64_t* slot_mapping, int64_t* status) {
+  using M = Meta<MetaT>;
+  __shared__ PopShared<MetaT> sh;
+  __shared__ int bad;
+  __shared__ long long bad_value;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  const int64_t base = *next_logical;
+  for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
+    const int64_t q = need[j];
+    int64_t v = q;
+    bool ok = in_range(q, seqs);
+    if (ok) {
+      v = cur_logical[q];
+      ok = in_range(v, n_logical) && in_range(l2p[v], n);
+    }
+    if (!ok && atomicCAS(&bad, 0, 1) == 0) bad_value = v;
+  }
+  if (threadIdx.x == 0 && c > 0 && (base < 0 || base + c > n_logical) && atomicCAS(&bad, 0, 1) == 0)
+    bad_value = base + c;
+  __syncthreads();
+  if (bad) {
+    if (threadIdx.x == 0) report(status, KVCA_ERR_BAD_INDEX, bad_value);
+    return;
+  }
+  if (c > 0) {
+    const int rc = pop_cta<MetaT>(meta, n, search_start, bitmap, c, victims, order, aligned, sh);
+    if (rc != KVCA_OK) {
+      if (threadIdx.x == 0) report(status, rc, c);
+      return;
+    }
+    __syncthreads();
+    for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
+      const int64_t prev = p2l[victims[j]];
+      if (prev >= 0) l2p[prev] = -1;
+    }
+    __syncthreads();
+    for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
+      const int64_t v = victims[j];
+      l2p[base + j] = v;
+      p2l[v] = base + j;
+      meta[v] = M::pack(1, 1);
+    }
+    __syncthreads();
+    // the full blocks are pinned, so none of them was a victim; each sequence
+    // appears once, so each slot is released once
+    for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
+      const int64_t q = need[j];
+      const int64_t full = l2p[cur_logical[q]];
+      const unsigned w = meta[full];
+      meta[full] = M::pack(static_cast<int64_t>(M::pin(w)) - 1, M::usage(w));
+      cur_block[q] = victims[j];
+      cur_logical[q] = base + j;
+      pos[q] = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *next_logical = base + c;
+  }
+  for (int64_t q = threadIdx.x; q < seqs; q += blockDim.x) {
+    slot_mapping[q] = cur_block[q] * block_size + pos[q];
+    pos[q] += 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Device-resident block store: the metadata half of a load / save after the
 // plan, with no host round trip in between
 // ---------------------------------------------------------------------------
@@ -2217,6 +2303,22 @@ cudaError_t launch_plan_save(int meta_bits, int order, const int64_t* l2p, int64
                                     move_slots, static_cast<MetaT*>(final_pins),
                                     static_cast<MetaT*>(final_usage),
                                     allocated, evict_ids, evict_slots, counts, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_append_step(int meta_bits, int order, void* meta, int64_t num_slots,
+                               int64_t* search_start, int64_t* l2p, int64_t num_logical,
+                               int64_t* p2l, const int64_t* need, int64_t num_need,
+                               int64_t* cur_block, int64_t* cur_logical, int64_t* pos,
+                               int64_t num_seqs, int64_t block_size, int64_t* next_logical,
+                               uint32_t* bitmap, int64_t* victims, int64_t* slot_mapping,
+                               int64_t* status, cudaStream_t stream) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  KVCA_META_DISPATCH(meta_bits, append_step_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    static_cast<MetaT*>(meta), num_slots, search_start, l2p,
+                                    num_logical, p2l, need, num_need, cur_block, cur_logical, pos,
+                                    num_seqs, block_size, next_logical, bitmap, order, aligned,
+                                    victims, slot_mapping, status));
   return cudaGetLastError();
 }
 

@@ -153,4 +153,12 @@ cudaError_t launch_store_save_meta(int meta_bits, int order, int64_t* l2p, int64
                                    int64_t* work, void* work_meta, int64_t* counts,
                                    int64_t* status, cudaStream_t stream);
 
+cudaError_t launch_append_step(int meta_bits, int order, void* meta, int64_t num_slots,
+                               int64_t* search_start, int64_t* l2p, int64_t num_logical,
+                               int64_t* p2l, const int64_t* need, int64_t num_need,
+                               int64_t* cur_block, int64_t* cur_logical, int64_t* pos,
+                               int64_t num_seqs, int64_t block_size, int64_t* next_logical,
+                               uint32_t* bitmap, int64_t* victims, int64_t* slot_mapping,
+                               int64_t* status, cudaStream_t stream);
+
 }  // namespace kvca

@@ -47,6 +47,7 @@ __all__ = [
     "scatter_tokens",
     "plan_load",
     "plan_save",
+    "append_step",
     "copy_tokens",
     "exchange_blocks",
     "batched_fused_single_layer_kv_transfer",
@@ -412,6 +413,40 @@ def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps:
     _host_rc(rc, "clock_stream")
     _maybe_check(dev, check, "clock_stream")
     return victims, steps_done
+
+
+def append_step(slot_meta: torch.Tensor, search_start: torch.Tensor, logical_to_physical: torch.Tensor,
+                physical_to_logical: torch.Tensor, need: torch.Tensor, cur_block: torch.Tensor,
+                cur_logical: torch.Tensor, pos: torch.Tensor, block_size: int, next_logical: torch.Tensor,
+                victims: torch.Tensor, slot_mapping: torch.Tensor, *, order: str | None = None,
+                check: bool | None = None) -> None:
+    """One decode step of block bookkeeping in one launch (see
+    kvca_append_step): new blocks for the sequences ``need`` (pop ->
+    commit as fresh pinned saves -> release the full blocks), then this
+    step's ``slot_mapping`` and the positions advanced.  ``victims`` takes
+    ``need.numel()`` slots.  Nothing is read back: capturable in a graph."""
+    for t, name in ((search_start, "search_start"), (logical_to_physical, "logical_to_physical"),
+                    (physical_to_logical, "physical_to_logical"), (need, "need"), (cur_block, "cur_block"),
+                    (cur_logical, "cur_logical"), (pos, "pos"), (next_logical, "next_logical"),
+                    (victims, "victims"), (slot_mapping, "slot_mapping")):
+        _require(t, torch.int64, name)
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    seqs = cur_block.numel()
+    if cur_logical.numel() != seqs or pos.numel() != seqs or slot_mapping.numel() != seqs:
+        raise ValueError("cur_block, cur_logical, pos and slot_mapping need one entry per sequence")
+    c = need.numel()
+    if victims.numel() < c:
+        raise ValueError("victims must hold one slot per sequence in need")
+    dev = slot_meta.device
+    n = slot_meta.numel()
+    with _on(dev):
+        rc = _lib_handle.kvca_append_step(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(slot_meta), n, _ptr(search_start),
+            _ptr(logical_to_physical), logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(need), c,
+            _ptr(cur_block), _ptr(cur_logical), _ptr(pos), seqs, int(block_size), _ptr(next_logical),
+            _ptr(victims), _ptr(slot_mapping), _ptr(_bitmap(dev, n)), _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "append_step")
+    _maybe_check(dev, check, "append_step")
 
 
 class LoadPlan:

@@ -197,7 +197,8 @@ class DecodeMix:
 
     ``ops`` supplies pop_reusable_slots, gather_layers, commit_save_metadata,
     release_metadata and scatter_tokens (the CUDA module, or a CPU stand-in in
-    the tests).  All per-step state lives on the device; the host only keeps
+    the tests); when it also has ``append_step`` the bookkeeping of step 1
+    and the slot_mapping of step 2 run as that one launch.  All per-step state lives on the device; the host only keeps
     the fill positions, which decide which sequences need a block, so steps
     issue no host<->device traffic and a whole cycle of ``block_size`` steps
     can be captured in a CUDA graph (``capture_cycle``).
@@ -245,6 +246,10 @@ class DecodeMix:
         self.spill = torch.empty((seqs, self.num_planes, 1, block_size, heads, head_dim), dtype=dtype,
                                  device=device)
         self.empty_ids = torch.empty(0, dtype=torch.int64, device=device)
+        # one-launch bookkeeping when the op set has it (the CUDA module)
+        self._append = getattr(ops, "append_step", None)
+        self.victims_buf = torch.empty(seqs, dtype=torch.int64, device=device)
+        self.slot_mapping_buf = torch.empty(seqs, dtype=torch.int64, device=device)
         self._need = {}  # need set (bytes) -> (index tensor, ones, arange) on the device
         self.evictions = 0
         self.tokens = 0
@@ -269,6 +274,22 @@ class DecodeMix:
         need = self.need_new_blocks()
         c = int(need.size)
         spill = self.spill[:c]
+        if self._append is not None:
+            need_dev = self._need_tensors(need)[0] if c else self.empty_ids
+            victims = self.victims_buf[:c]
+            self._append(self.slot_meta, self.search_start, self.l2p, self.p2l, need_dev, self.cur_block_dev,
+                         self.cur_logical_dev, self.pos_dev, self.block_size, self.next_logical_dev, victims,
+                         self.slot_mapping_buf, check=check)
+            if c:
+                self.ops.gather_layers(self.block_table, victims, spill, blocks_per_chunk=1, check=check)
+                self.pos[need] = 0
+                self.evictions += c
+                self.gathered_blocks += c
+            self.ops.scatter_tokens(self.token_table, self.slot_mapping_buf, token_rows, tokens_per_chunk=self.seqs,
+                                    check=check)
+            self.pos += 1
+            self.tokens += self.seqs
+            return spill
         if c:
             ops = self.ops
             need_dev, ones, offsets = self._need_tensors(need)

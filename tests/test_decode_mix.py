@@ -58,6 +58,9 @@ def test_decode_mix_matches_oracle_step_by_step():
         assert torch.equal(gpu.slot_meta.cpu(), cpu.slot_meta), step
         assert torch.equal(gpu.l2p.cpu(), cpu.l2p) and torch.equal(gpu.p2l.cpu(), cpu.p2l), step
         assert int(gpu.search_start[0]) == int(cpu.search_start[0]), step
+        for name in ("cur_block_dev", "cur_logical_dev", "pos_dev", "next_logical_dev"):
+            assert torch.equal(getattr(gpu, name).cpu(), getattr(cpu, name)), (step, name)
+    assert gpu._append is not None  # the one-launch bookkeeping ran on the GPU
     assert torch.equal(gpu.kv.cpu().view(torch.int16), cpu.kv.view(torch.int16))
     assert gpu.evictions == cpu.evictions > 100
 
@@ -89,3 +92,28 @@ def test_decode_mix_graph_replay_matches_eager():
     assert torch.equal(eager.search_start, graphed.search_start)
     assert torch.equal(eager.cur_block_dev, graphed.cur_block_dev)
     assert torch.equal(eager.next_logical_dev, graphed.next_logical_dev)
+
+
+@pytest.mark.gpu
+def test_append_step_errors_change_nothing():
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+    from kv_cache_adapter_b200.errors import InsufficientCapacityError
+
+    dev = torch.device("cuda", 0)
+    mix = DecodeMix(ops, dev, **SMALL)
+    state = [t.clone() for t in (mix.slot_meta, mix.l2p, mix.p2l, mix.search_start, mix.cur_block_dev,
+                                 mix.cur_logical_dev, mix.pos_dev, mix.next_logical_dev)]
+    need = torch.tensor([0, 1], dtype=torch.int64, device=dev)
+    victims = torch.empty(2, dtype=torch.int64, device=dev)
+    sm = torch.empty(mix.seqs, dtype=torch.int64, device=dev)
+    args = (mix.slot_meta, mix.search_start, mix.l2p, mix.p2l)
+    tail = (mix.cur_block_dev, mix.cur_logical_dev, mix.pos_dev, mix.block_size, mix.next_logical_dev, victims, sm)
+    with pytest.raises(IndexError):  # a sequence index outside [0, seqs)
+        ops.append_step(*args, torch.tensor([0, mix.seqs], dtype=torch.int64, device=dev), *tail, check=True)
+    pinned = mix.slot_meta | 1  # every slot pinned: no victim
+    with pytest.raises(InsufficientCapacityError):
+        ops.append_step(pinned, *args[1:], need, *tail, check=True)
+    for before, after in zip(state, (mix.slot_meta, mix.l2p, mix.p2l, mix.search_start, mix.cur_block_dev,
+                                     mix.cur_logical_dev, mix.pos_dev, mix.next_logical_dev)):
+        assert torch.equal(before, after)
+    ops.check_status(dev)
