@@ -230,17 +230,21 @@ int kvca_clock_stream(int meta_bits, int order, void* d_slot_meta, int64_t num_s
  * the available usage-0 slots in scan order are the candidates, and a
  * candidate is passed over exactly when its first re-access comes at a step
  * before the one that would take it.  Steps that need aging run one by one.
- * d_scratch: kvca_clock_stream_scratch_bytes(num_slots) = 32 * num_slots
- * bytes, 8-byte aligned, whose bytes from 20 * num_slots on are zero on
- * entry (the call leaves them zero); num_slots and num_steps *
- * alloc_per_step below 2^31.  Calls sharing scratch must be ordered on one stream.
+ * The passes over slots, candidates and events run on a cooperative grid of
+ * `ctas` CTAs (0: one per SM; 1: one CTA), joined by grid barriers whose
+ * waits are bounded (a wait that runs out reports KVCA_ERR_DEVICE_TIMEOUT).
+ * d_scratch: kvca_clock_stream_scratch_bytes(num_slots) = 32 * num_slots +
+ * 16384 bytes, 8-byte aligned, whose bytes from 20 * num_slots to
+ * 32 * num_slots are zero on entry (the call leaves them zero); num_slots and
+ * num_steps * alloc_per_step below 2^31.  Calls sharing scratch must be
+ * ordered on one stream.
  */
 size_t kvca_clock_stream_scratch_bytes(int64_t num_slots);
 int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
                               int64_t* d_search_start, int64_t num_steps, int64_t alloc_per_step,
                               const int64_t* d_reaccess, int64_t reaccess_per_step,
                               int64_t* d_victims, int64_t* d_steps_done, void* d_scratch,
-                              int64_t* d_status, kvca_stream_t stream);
+                              int ctas, int64_t* d_status, kvca_stream_t stream);
 
 /*
  * One-call planning of KVCacheAdapter.load (adapter.py:257-307, the

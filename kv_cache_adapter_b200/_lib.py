@@ -112,7 +112,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvca_clock_stream_scratch_bytes": (ctypes.c_size_t, [c_i64]),
     "kvca_clock_stream_batched": (
         c_int,
-        [c_int, c_int, c_ptr, c_i64, c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_int, c_ptr,
          c_ptr],
     ),
     "kvca_plan_load": (

@@ -224,15 +224,15 @@ int kvca_clock_stream(int meta_bits, int order, void* d_slot_meta, int64_t num_s
 
 size_t kvca_clock_stream_scratch_bytes(int64_t num_slots) {
   if (num_slots <= 0) return 0;
-  return static_cast<size_t>(num_slots) * 32;
+  return static_cast<size_t>(num_slots) * 32 + kvca::kClockStreamGridBytes;
 }
 
 int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
                               int64_t* d_search_start, int64_t num_steps, int64_t alloc_per_step,
                               const int64_t* d_reaccess, int64_t reaccess_per_step,
                               int64_t* d_victims, int64_t* d_steps_done, void* d_scratch,
-                              int64_t* d_status, kvca_stream_t stream) {
-  if (!valid_meta_bits(meta_bits)) return KVCA_ERR_BAD_ARGUMENT;
+                              int ctas, int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) || ctas < 0) return KVCA_ERR_BAD_ARGUMENT;
   if (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX)
     return KVCA_ERR_BAD_ARGUMENT;
   const int64_t limit = INT32_MAX - 2;
@@ -247,7 +247,7 @@ int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64
   return status_of(kvca::launch_clock_stream_batched(
       meta_bits, order, d_slot_meta, num_slots, d_search_start, num_steps, alloc_per_step,
       d_reaccess, reaccess_per_step, d_victims, d_steps_done,
-      reinterpret_cast<unsigned char*>(d_scratch), d_status, stream));
+      reinterpret_cast<unsigned char*>(d_scratch), ctas, d_status, stream));
 }
 
 static bool plan_args_ok(int meta_bits, int order, const int64_t* l2p, int64_t num_logical,

@@ -117,11 +117,12 @@ __device__ __forceinline__ void load_meta_vec(const MetaT* meta, int64_t num_slo
                                               bool aligned, MetaVec<MetaT>& out) {
   constexpr int kSpv = Meta<MetaT>::kSlotsPerVec;
   const int64_t first = v * kSpv;
+  // L2 loads: the batched stream's CTAs read words other CTAs wrote
   if (aligned && first + kSpv <= num_slots) {
-    out.raw = *reinterpret_cast<const uint4*>(meta + first);
+    out.raw = __ldcg(reinterpret_cast<const uint4*>(meta + first));
   } else {
 #pragma unroll
-    for (int j = 0; j < kSpv; ++j) out.s[j] = first + j < num_slots ? meta[first + j] : MetaT(0);
+    for (int j = 0; j < kSpv; ++j) out.s[j] = first + j < num_slots ? __ldcg(meta + first + j) : MetaT(0);
   }
 }
 
@@ -431,7 +432,7 @@ __device__ int stream_step(MetaT* meta, int64_t num_slots, int64_t* search_start
   // gives new saves usage 1; commit at adapter.py:651).
   for (int64_t i = threadIdx.x; i < alloc_per_step; i += blockDim.x) {
     const int64_t v = out[i];
-    meta[v] = M::pack(M::pin(meta[v]), 1);
+    meta[v] = M::pack(M::pin(__ldcg(meta + v)), 1);
   }
   __syncthreads();
   // Usage bump of re-accessed slots: every value is read before any write,
@@ -449,7 +450,7 @@ __device__ int stream_step(MetaT* meta, int64_t num_slots, int64_t* search_start
       if (id < 0 || id >= num_slots) {
         report(status, KVCA_ERR_BAD_INDEX, id);
       } else {
-        const unsigned w = meta[id];
+        const unsigned w = __ldcg(meta + id);
         values[u] = M::pack(M::pin(w), M::sat_inc(M::usage(w)));
         slot_ids[u] = id;
       }
@@ -512,6 +513,8 @@ __global__ void __launch_bounds__(1024)
 // epochs the kernel runs a stretch of exact steps instead.  Results equal the
 // step-by-step stream bit for bit.
 
+constexpr int kStreamThreads = 1024;  // threads per CTA of the batched stream
+constexpr int kStreamMaxCtas = 1024;  // CTAs of its cooperative grid, at most
 constexpr int64_t kEpochMinSteps = 8;
 constexpr int64_t kExactStepsAfterShortEpoch = 64;
 constexpr int kCandPerThread = 16;  // candidates per thread per block-scan tile
@@ -546,56 +549,172 @@ struct EpochScratch {
 
 __device__ __forceinline__ bool slot_ok(int64_t x, int64_t n) { return x >= 0 && x < n; }
 
+// The epoch runs on a cooperative grid (one launch, all CTAs resident): the
+// passes over slots, candidates and re-access events are spread over every
+// CTA, ordered compactions take a per-CTA count, a grid barrier and the
+// prefix of the counts, and the one-warp resolution of the pending
+// candidates and the exact aging steps run on CTA 0 while the others wait.
+// With one CTA the barriers are block barriers.  StreamGrid lives in the
+// scratch buffer after the per-slot arrays and is cleared before each launch.
+struct StreamGrid {
+  unsigned int bar_count;
+  unsigned int bar_gen;
+  int failed;
+  int nu;        // distinct slots re-accessed in the window
+  int tp_total;  // pending candidates taken
+  int rc;        // status of the last exact step
+  long long last_victim;
+  long long cnt[kStreamMaxCtas];  // per-CTA counts of the current compaction
+};
+static_assert(sizeof(StreamGrid) <= kClockStreamGridBytes, "grid words exceed their scratch");
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr uint32_t kGridSpinLimit = 1u << 22;  // about 0.3 s of 64 ns naps
+
+// Grid-wide barrier with a bounded wait.  Every CTA's writes before the
+// barrier are visible to every CTA after it.  A CTA that waits too long (or
+// sees another CTA give up) marks the grid failed, reports
+// KVCA_ERR_DEVICE_TIMEOUT and returns false; callers then return.
+__device__ bool grid_barrier(StreamGrid* g, int64_t* status) {
+  __shared__ int ok_s;
+  __syncthreads();
+  if (gridDim.x == 1) return true;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned gen = ld_acquire_u32(&g->bar_gen);
+    __threadfence();
+    if (atomicAdd(&g->bar_count, 1u) == gridDim.x - 1) {
+      atomicExch(&g->bar_count, 0u);
+      __threadfence();
+      atomicAdd(&g->bar_gen, 1u);
+    } else {
+      uint32_t spins = 0;
+      while (ld_acquire_u32(&g->bar_gen) == gen) {
+        if (++spins > kGridSpinLimit || *reinterpret_cast<volatile int*>(&g->failed) != 0) {
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+    if (!ok) {
+      atomicExch(&g->failed, 1);
+      report(status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
+    }
+    ok_s = ok;
+  }
+  __syncthreads();
+  return ok_s != 0;
+}
+
+// Sum over the CTAs' counts: (sum of the CTAs before this one, total).
+__device__ void grid_prefix(const StreamGrid* g, int64_t* before, int64_t* total, int* scan) {
+  long long b = 0, t = 0;
+  for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += blockDim.x) {
+    const long long c = __ldcg(g->cnt + i);
+    t += c;
+    if (i < static_cast<int>(blockIdx.x)) b += c;
+  }
+  int tot;
+  block_excl_scan(static_cast<int>(b), &tot, scan);
+  *before = tot;
+  block_excl_scan(static_cast<int>(t), &tot, scan);
+  *total = tot;
+}
+
+template <typename MetaT>
+__device__ __forceinline__ unsigned candidate_mask(const MetaT* meta, int64_t n, int64_t p0,
+                                                   int64_t v0b, int64_t V0, int64_t vv,
+                                                   bool aligned, int64_t* v_out) {
+  using M = Meta<MetaT>;
+  constexpr int kSpv = M::kSlotsPerVec;
+  int64_t v, lo, hi;
+  if (vv < V0) {
+    v = v0b + vv;
+    lo = p0;
+    hi = n;
+  } else {
+    v = vv - V0;
+    lo = 0;
+    hi = p0;
+  }
+  *v_out = v;
+  MetaVec<MetaT> mv;
+  load_meta_vec(meta, n, v, aligned, mv);
+  unsigned mask = 0u;
+#pragma unroll
+  for (int j = 0; j < kSpv; ++j) {
+    const int64_t slot = v * kSpv + j;
+    const unsigned wd = mv.s[j];
+    if (slot >= lo && slot < hi && M::pin(wd) == 0u && M::usage(wd) == 0u) mask |= 1u << j;
+  }
+  return mask;
+}
+
+// One epoch from step s0 (see above); returns the first step it did not
+// complete, or s0 with *ok = false when a grid barrier gave up.
 template <typename MetaT>
 __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, int64_t s0,
                                 int64_t steps, int64_t k, const int64_t* reaccess, int64_t m,
-                                int64_t* victims, const EpochScratch& w, bool aligned,
-                                int64_t* status, EpochShared<MetaT>& sh) {
+                                int64_t* victims, const EpochScratch& w, StreamGrid* g,
+                                bool aligned, int64_t* status, EpochShared<MetaT>& sh, bool* ok) {
   using M = Meta<MetaT>;
   constexpr int kSpv = M::kSlotsPerVec;
   constexpr int C = kCandPerThread;
-  if (threadIdx.x == 0) {
-    long long p0 = static_cast<long long>(*search_start % n);
-    if (p0 < 0) p0 += n;
-    sh.start = p0;
-    sh.s_end = s0;
-    sh.last_victim = -1;
-    sh.nu = 0;
+  const int64_t B = gridDim.x;
+  const int64_t b = blockIdx.x;
+  const int64_t T = blockDim.x;
+  const int64_t gt = b * T + threadIdx.x;
+  const int64_t G = B * T;
+#define KVCA_GRID_SYNC()               \
+  if (!grid_barrier(g, status)) {      \
+    *ok = false;                       \
+    return s0;                         \
   }
-  __syncthreads();
-  const int64_t p0 = sh.start;
+  int64_t p0 = __ldcg(reinterpret_cast<const long long*>(search_start)) % n;
+  if (p0 < 0) p0 += n;
+  if (b == 0 && threadIdx.x == 0) g->nu = 0;
 
-  // 1. candidates: available usage-0 slots in scan order from p0
-  int64_t nc = 0;
-  for (int seg = 0; seg < 2; ++seg) {
-    const int64_t lo = seg == 0 ? p0 : 0;
-    const int64_t hi = seg == 0 ? n : p0;
-    if (lo >= hi) continue;
-    const int64_t v_begin = lo / kSpv;
-    const int64_t v_end = (hi + kSpv - 1) / kSpv;
-    for (int64_t tile = v_begin; tile < v_end; tile += blockDim.x) {
-      const int64_t v = tile + threadIdx.x;
-      unsigned mask = 0u;
-      if (v < v_end) {
-        MetaVec<MetaT> mv;
-        load_meta_vec(meta, n, v, aligned, mv);
-#pragma unroll
-        for (int j = 0; j < kSpv; ++j) {
-          const int64_t slot = v * kSpv + j;
-          const unsigned wd = mv.s[j];
-          if (slot >= lo && slot < hi && M::pin(wd) == 0u && M::usage(wd) == 0u) mask |= 1u << j;
-        }
-      }
-      int total;
-      const int base = block_excl_scan(__popc(mask), &total, sh.scan);
-      int64_t rank = nc + base;
-      while (mask != 0u) {
-        const int j = __ffs(mask) - 1;
-        mask &= mask - 1u;
-        w.cand[rank++] = static_cast<int32_t>(v * kSpv + j);
-      }
-      nc += total;
+  // 1. candidates: available usage-0 slots in scan order from p0; CTA b
+  //    takes a contiguous range of the order's vectors (segment [p0, n),
+  //    then [0, p0))
+  const int64_t v0b = p0 / kSpv;
+  const int64_t V0 = (n + kSpv - 1) / kSpv - v0b;
+  const int64_t V = V0 + (p0 + kSpv - 1) / kSpv;
+  const int64_t cb = V * b / B;
+  const int64_t ce = V * (b + 1) / B;
+  {
+    int local = 0;
+    for (int64_t t0 = cb; t0 < ce; t0 += T) {
+      const int64_t vv = t0 + threadIdx.x;
+      int64_t v;
+      if (vv < ce) local += __popc(candidate_mask(meta, n, p0, v0b, V0, vv, aligned, &v));
     }
+    int total;
+    block_excl_scan(local, &total, sh.scan);
+    if (threadIdx.x == 0) g->cnt[b] = total;
+  }
+  KVCA_GRID_SYNC();
+  int64_t nc, run;
+  grid_prefix(g, &run, &nc, sh.scan);
+  for (int64_t t0 = cb; t0 < ce; t0 += T) {
+    const int64_t vv = t0 + threadIdx.x;
+    int64_t v = 0;
+    unsigned mask = vv < ce ? candidate_mask(meta, n, p0, v0b, V0, vv, aligned, &v) : 0u;
+    int total;
+    int64_t rank = run + block_excl_scan(__popc(mask), &total, sh.scan);
+    while (mask != 0u) {
+      const int j = __ffs(mask) - 1;
+      mask &= mask - 1u;
+      w.cand[rank++] = static_cast<int32_t>(v * kSpv + j);
+    }
+    run += total;
   }
   // steps these candidates can serve: at most nc / k, plus the step that fails
   int64_t s_hi = s0 + nc / k + 1;
@@ -604,67 +723,82 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   const int64_t ev_hi = s_hi * m;
 
   // 2. first re-access step in the window, encoded as INT_MAX - step (0 = none)
-  for (int64_t e = ev_lo + threadIdx.x; e < ev_hi; e += blockDim.x) {
+  for (int64_t e = ev_lo + gt; e < ev_hi; e += G) {
     const int64_t x = reaccess[e];
     if (!slot_ok(x, n)) {
       report(status, KVCA_ERR_BAD_INDEX, x);
       continue;
     }
     const int32_t old = atomicMax(w.first_bump + x, static_cast<int32_t>(INT32_MAX - e / m));
-    if (old == 0) w.touched[atomicAdd(&sh.nu, 1)] = static_cast<int32_t>(x);
+    if (old == 0) w.touched[atomicAdd(&g->nu, 1)] = static_cast<int32_t>(x);
   }
-  __syncthreads();
-  const int nu = sh.nu;
-  for (int64_t j = threadIdx.x; j < nc; j += blockDim.x) {
-    const int32_t enc = w.first_bump[w.cand[j]];
+  KVCA_GRID_SYNC();
+  const int nu = __ldcg(&g->nu);
+  for (int64_t j = gt; j < nc; j += G) {
+    const int32_t enc = __ldcg(w.first_bump + __ldcg(w.cand + j));
     w.cand_bump[j] = enc == 0 ? INT32_MAX : INT32_MAX - enc;
   }
-  __syncthreads();
+  KVCA_GRID_SYNC();
 
-  // 3a. list the pending candidates in order: (index << 32) | first re-access step
-  int64_t np = 0;
-  for (int64_t tile = 0; tile < nc; tile += static_cast<int64_t>(blockDim.x) * C) {
-    const int64_t jb = tile + static_cast<int64_t>(threadIdx.x) * C;
-    int32_t b[C];
-    int cnt = 0;
-#pragma unroll
-    for (int u = 0; u < C; ++u) {
-      b[u] = jb + u < nc ? w.cand_bump[jb + u] : INT32_MAX;
-      cnt += b[u] != INT32_MAX;
-    }
+  // 3a. list the pending candidates in order: (index << 32) | first re-access
+  //     step; CTA b takes candidates [jc0, jc1)
+  const int64_t jc0 = nc * b / B;
+  const int64_t jc1 = nc * (b + 1) / B;
+  {
+    int local = 0;
+    for (int64_t j = jc0 + threadIdx.x; j < jc1; j += T) local += __ldcg(w.cand_bump + j) != INT32_MAX;
     int total;
-    int64_t p = np + block_excl_scan(cnt, &total, sh.scan);
-#pragma unroll
-    for (int u = 0; u < C; ++u)
-      if (b[u] != INT32_MAX)
-        w.pending[p++] = (static_cast<int64_t>(jb + u) << 32) | static_cast<uint32_t>(b[u]);
-    np += total;
+    block_excl_scan(local, &total, sh.scan);
+    if (threadIdx.x == 0) g->cnt[b] = total;
   }
-  __syncthreads();
+  KVCA_GRID_SYNC();
+  int64_t pend0, np;
+  grid_prefix(g, &pend0, &np, sh.scan);
+  {
+    int64_t p_run = pend0;
+    for (int64_t tile = jc0; tile < jc1; tile += T * C) {
+      const int64_t jb = tile + static_cast<int64_t>(threadIdx.x) * C;
+      int32_t bb[C];
+      int cnt = 0;
+#pragma unroll
+      for (int u = 0; u < C; ++u) {
+        bb[u] = jb + u < jc1 ? __ldcg(w.cand_bump + jb + u) : INT32_MAX;
+        cnt += bb[u] != INT32_MAX;
+      }
+      int total;
+      int64_t p = p_run + block_excl_scan(cnt, &total, sh.scan);
+#pragma unroll
+      for (int u = 0; u < C; ++u)
+        if (bb[u] != INT32_MAX)
+          w.pending[p++] = (static_cast<int64_t>(jb + u) << 32) | static_cast<uint32_t>(bb[u]);
+      p_run += total;
+    }
+  }
+  KVCA_GRID_SYNC();
 
-  // 3b. one warp resolves the pending candidates; each entry becomes
+  // 3b. one warp of CTA 0 resolves the pending candidates; each entry becomes
   //     (pending candidates taken before it << 1) | taken
   const int32_t kk = static_cast<int32_t>(k);
   const int32_t max_taken = static_cast<int32_t>((steps - s0) * k);
   const int32_t step0 = static_cast<int32_t>(s0);
-  if (threadIdx.x < 32) {
+  if (b == 0 && threadIdx.x < 32) {
     const int lane = threadIdx.x;
     const unsigned below = (1u << lane) - 1u;
     int32_t tp = 0;
     for (int64_t p0w = 0; p0w < np; p0w += 32) {
       const int64_t p = p0w + lane;
       const bool here = p < np;
-      const int64_t pr = here ? w.pending[p] : 0;
+      const int64_t pr = here ? __ldcg(reinterpret_cast<const long long*>(w.pending) + p) : 0;
       const int32_t jj = static_cast<int32_t>(pr >> 32);
-      const int32_t b = static_cast<int32_t>(pr & 0xffffffffll);
+      const int32_t bv = static_cast<int32_t>(pr & 0xffffffffll);
       const int32_t nonpending_before = here ? jj - static_cast<int32_t>(p) : 0;
       const unsigned present = __ballot_sync(0xffffffffu, here);
       unsigned cur = present;
       for (int it = 0; it < 33; ++it) {  // converges in at most 32 rounds
         const int32_t tb = nonpending_before + tp + __popc(cur & below);
         const int32_t st = kk == 1 ? step0 + tb : step0 + tb / kk;
-        const bool ok = here && tb < max_taken && b >= st;
-        const unsigned ok_mask = __ballot_sync(0xffffffffu, ok);
+        const bool take = here && tb < max_taken && bv >= st;
+        const unsigned ok_mask = __ballot_sync(0xffffffffu, take);
         const unsigned diff = (ok_mask ^ cur) & present;
         if (diff == 0u) break;
         const unsigned keep = (1u << (__ffs(diff) - 1)) - 1u;
@@ -675,10 +809,10 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
                        static_cast<int64_t>((cur >> lane) & 1u);
       tp += __popc(cur);
     }
-    if (lane == 0) sh.tp_total = tp;
+    if (lane == 0) g->tp_total = tp;
   }
-  __syncthreads();
-  const int32_t tp_total = sh.tp_total;
+  KVCA_GRID_SYNC();
+  const int32_t tp_total = __ldcg(&g->tp_total);
   int64_t total_taken = (nc - np) + tp_total;
   if (total_taken > max_taken) total_taken = max_taken;
   const int64_t full = total_taken / k;  // complete steps of this epoch
@@ -688,15 +822,15 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   // 3c. place every victim of the complete steps:
   //     taken before j = (j - pending before j) + pending taken before j
   {
-    int64_t np_run = 0;
-    for (int64_t tile = 0; tile < nc; tile += static_cast<int64_t>(blockDim.x) * C) {
+    int64_t np_run = pend0;
+    for (int64_t tile = jc0; tile < jc1; tile += T * C) {
       const int64_t jb = tile + static_cast<int64_t>(threadIdx.x) * C;
-      int32_t b[C];
+      int32_t bb[C];
       int cnt = 0;
 #pragma unroll
       for (int u = 0; u < C; ++u) {
-        b[u] = jb + u < nc ? w.cand_bump[jb + u] : INT32_MAX;
-        cnt += b[u] != INT32_MAX;
+        bb[u] = jb + u < jc1 ? __ldcg(w.cand_bump + jb + u) : INT32_MAX;
+        cnt += bb[u] != INT32_MAX;
       }
       int total;
       int64_t pp = np_run + block_excl_scan(cnt, &total, sh.scan);
@@ -705,30 +839,30 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
 #pragma unroll
       for (int u = 0; u < C; ++u) {
         const int64_t j = jb + u;
-        if (j >= nc) continue;
-        const bool is_pending = b[u] != INT32_MAX;
+        if (j >= jc1) continue;
+        const bool is_pending = bb[u] != INT32_MAX;
         int64_t tpb = tp_total;
         if (pp < np) {
           if (pp != cached_pp) {
-            entry = w.pending[pp];
+            entry = __ldcg(reinterpret_cast<const long long*>(w.pending) + pp);
             cached_pp = pp;
           }
           tpb = entry >> 1;
         }
         const int64_t tb = (j - pp) + tpb;
-        const bool ok = is_pending ? (entry & 1) != 0 : tb < max_taken;
-        if (ok && tb < full_pos) {
-          const int32_t x = w.cand[j];
+        const bool take = is_pending ? (entry & 1) != 0 : tb < max_taken;
+        if (take && tb < full_pos) {
+          const int32_t x = __ldcg(w.cand + j);
           victims[s0 * k + tb] = x;
           w.victim_step[x] = static_cast<int32_t>(s0 + tb / k + 1);
-          if (tb == full_pos - 1) sh.last_victim = x;
+          if (tb == full_pos - 1) g->last_victim = x;
         }
         if (is_pending) ++pp;
       }
       np_run += total;
     }
   }
-  __syncthreads();
+  KVCA_GRID_SYNC();
   const int64_t v_lo = s0 * k;
   const int64_t v_hi = s_end * k;
   const int64_t cnt_hi = s_end * m;
@@ -739,8 +873,8 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   //     scans its step's earlier ids in memory.
   if (m >= kWarpDedupMin && m <= kWarpDedupMax) {
     const int lane = threadIdx.x & 31;
-    const int nwarps = static_cast<int>(blockDim.x >> 5);
-    for (int64_t t = s0 + (threadIdx.x >> 5); t < s_end; t += nwarps) {
+    const int64_t nwarps = G >> 5;
+    for (int64_t t = s0 + (gt >> 5); t < s_end; t += nwarps) {
       int64_t ids[kWarpDedupMax / 32];
       bool dup[kWarpDedupMax / 32];
 #pragma unroll
@@ -764,12 +898,12 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
       for (int q = 0; q < kWarpDedupMax / 32; ++q) {
         const int64_t x = ids[q];
         if (dup[q] || !slot_ok(x, n)) continue;
-        const int32_t vs = w.victim_step[x];
+        const int32_t vs = __ldcg(w.victim_step + x);
         if (vs == 0 || vs - 1 <= t) atomicAdd(w.bump_count + x, 1);
       }
     }
   } else {
-    for (int64_t e = ev_lo + threadIdx.x; e < cnt_hi; e += blockDim.x) {
+    for (int64_t e = ev_lo + gt; e < cnt_hi; e += G) {
       const int64_t x = reaccess[e];
       if (!slot_ok(x, n)) continue;
       const int64_t t = e / m;
@@ -777,34 +911,35 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
 #pragma unroll 8
       for (int64_t i = t * m; i < e; ++i) dup |= reaccess[i] == x;
       if (dup) continue;
-      const int32_t vs = w.victim_step[x];
+      const int32_t vs = __ldcg(w.victim_step + x);
       if (vs == 0 || vs - 1 <= t) atomicAdd(w.bump_count + x, 1);
     }
   }
-  __syncthreads();
+  KVCA_GRID_SYNC();
 
   // 4b. final usage of every touched slot (each listed re-accessed slot once,
   //     plus the victims), computed from the epoch-start words
   const int64_t n_touched = nu + (v_hi - v_lo);
   auto touched_slot = [&](int64_t i) -> int64_t {
-    return i < nu ? static_cast<int64_t>(w.touched[i]) : victims[v_lo + (i - nu)];
+    return i < nu ? static_cast<int64_t>(__ldcg(w.touched + i))
+                  : static_cast<int64_t>(__ldcg(reinterpret_cast<const long long*>(victims) + v_lo + (i - nu)));
   };
   constexpr int kU = 4;
-  for (int64_t i0 = threadIdx.x; i0 < n_touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
+  for (int64_t i0 = gt; i0 < n_touched; i0 += G * kU) {
     int64_t xs[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      const int64_t i = i0 + static_cast<int64_t>(u) * G;
       xs[u] = i < n_touched ? touched_slot(i) : -1;
     }
     unsigned ws[kU];
     int32_t vss[kU], cts[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      const bool ok = slot_ok(xs[u], n);
-      ws[u] = ok ? static_cast<unsigned>(meta[xs[u]]) : 0u;
-      vss[u] = ok ? w.victim_step[xs[u]] : 0;
-      cts[u] = ok ? w.bump_count[xs[u]] : 0;
+      const bool okx = slot_ok(xs[u], n);
+      ws[u] = okx ? static_cast<unsigned>(__ldcg(meta + xs[u])) : 0u;
+      vss[u] = okx ? __ldcg(w.victim_step + xs[u]) : 0;
+      cts[u] = okx ? __ldcg(w.bump_count + xs[u]) : 0;
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -814,42 +949,44 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
       w.first_bump[xs[u]] = static_cast<int32_t>(fin + 1);
     }
   }
-  __syncthreads();
-  for (int64_t i0 = threadIdx.x; i0 < n_touched; i0 += static_cast<int64_t>(blockDim.x) * kU) {
+  KVCA_GRID_SYNC();
+  for (int64_t i0 = gt; i0 < n_touched; i0 += G * kU) {
     int64_t xs[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      const int64_t i = i0 + static_cast<int64_t>(u) * blockDim.x;
+      const int64_t i = i0 + static_cast<int64_t>(u) * G;
       xs[u] = i < n_touched ? touched_slot(i) : -1;
     }
     unsigned ws[kU];
     int32_t fins[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      const bool ok = slot_ok(xs[u], n);
-      ws[u] = ok ? static_cast<unsigned>(meta[xs[u]]) : 0u;
-      fins[u] = ok ? w.first_bump[xs[u]] : 0;
+      const bool okx = slot_ok(xs[u], n);
+      ws[u] = okx ? static_cast<unsigned>(__ldcg(meta + xs[u])) : 0u;
+      fins[u] = okx ? __ldcg(w.first_bump + xs[u]) : 0;
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u)
       if (slot_ok(xs[u], n)) meta[xs[u]] = M::pack(M::pin(ws[u]), fins[u] - 1);
   }
-  __syncthreads();
+  KVCA_GRID_SYNC();
   // 4c. leave the per-slot scratch words zero again
-  for (int64_t i = threadIdx.x; i < n_touched; i += blockDim.x) {
+  for (int64_t i = gt; i < n_touched; i += G) {
     const int64_t x = touched_slot(i);
     if (!slot_ok(x, n)) continue;
     w.first_bump[x] = 0;
     w.victim_step[x] = 0;
     w.bump_count[x] = 0;
   }
-  if (threadIdx.x == 0 && s_end > s0) *search_start = (sh.last_victim + 1) % n;
-  __syncthreads();
+  if (b == 0 && threadIdx.x == 0 && s_end > s0)
+    *search_start = (__ldcg(&g->last_victim) + 1) % n;
+  KVCA_GRID_SYNC();
+#undef KVCA_GRID_SYNC
   return s_end;
 }
 
 template <typename MetaT>
-__global__ void __launch_bounds__(1024)
+__global__ void __launch_bounds__(kStreamThreads)
     clock_stream_batched_kernel(MetaT* meta, int64_t num_slots, int64_t* search_start,
                                 int64_t num_steps, int64_t alloc_per_step, const int64_t* reaccess,
                                 int64_t reaccess_per_step, int64_t* victims, int64_t* steps_done,
@@ -864,26 +1001,35 @@ __global__ void __launch_bounds__(1024)
   w.first_bump = reinterpret_cast<int32_t*>(scratch + 20 * n);
   w.victim_step = reinterpret_cast<int32_t*>(scratch + 24 * n);
   w.bump_count = reinterpret_cast<int32_t*>(scratch + 28 * n);
+  StreamGrid* g = reinterpret_cast<StreamGrid*>(scratch + 32 * n);
   int64_t s = 0;
   int64_t exact_until = 0;
+  bool ok = true;
   while (s < num_steps) {
     if (s >= exact_until) {
       const int64_t s_end = stream_epoch<MetaT>(meta, n, search_start, s, num_steps, alloc_per_step,
-                                                reaccess, reaccess_per_step, victims, w, aligned,
-                                                status, sh);
+                                                reaccess, reaccess_per_step, victims, w, g,
+                                                aligned, status, sh, &ok);
+      if (!ok) return;
       if (s_end - s < kEpochMinSteps) exact_until = s_end + 1 + kExactStepsAfterShortEpoch;
       s = s_end;
       if (s >= num_steps) break;
     }
-    const int rc = stream_step<MetaT>(meta, n, search_start, s, alloc_per_step, reaccess,
-                                      reaccess_per_step, victims, order, aligned, status, sh.pop);
+    // an exact step (one that ages usage) on CTA 0 while the others wait
+    if (blockIdx.x == 0) {
+      const int rc = stream_step<MetaT>(meta, n, search_start, s, alloc_per_step, reaccess,
+                                        reaccess_per_step, victims, order, aligned, status, sh.pop);
+      if (threadIdx.x == 0) g->rc = rc;
+    }
+    if (!grid_barrier(g, status)) return;
+    const int rc = __ldcg(&g->rc);
     if (rc != KVCA_OK) {
-      if (threadIdx.x == 0) report(status, rc, s);
+      if (blockIdx.x == 0 && threadIdx.x == 0) report(status, rc, s);
       break;
     }
     ++s;
   }
-  if (threadIdx.x == 0) *steps_done = s;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *steps_done = s;
 }
 
 // ---------------------------------------------------------------------------
@@ -2418,18 +2564,55 @@ cudaError_t launch_clock_stream(int meta_bits, int order, void* meta, int64_t nu
   return cudaGetLastError();
 }
 
+template <typename MetaT>
+cudaError_t launch_stream_grid(int grid, MetaT* meta, int64_t num_slots, int64_t* search_start,
+                               int64_t num_steps, int64_t alloc_per_step, const int64_t* reaccess,
+                               int64_t reaccess_per_step, int64_t* victims, int64_t* steps_done,
+                               int order, bool aligned, unsigned char* scratch, int64_t* status,
+                               cudaStream_t stream) {
+  if (grid == 1) {
+    clock_stream_batched_kernel<MetaT><<<1, kStreamThreads, 0, stream>>>(
+        meta, num_slots, search_start, num_steps, alloc_per_step, reaccess, reaccess_per_step,
+        victims, steps_done, order, aligned, scratch, status);
+    return cudaGetLastError();
+  }
+  void* args[] = {&meta,     &num_slots,  &search_start, &num_steps, &alloc_per_step,
+                  &reaccess, &reaccess_per_step, &victims, &steps_done, &order,
+                  &aligned,  &scratch,    &status};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(clock_stream_batched_kernel<MetaT>),
+                                     dim3(grid), dim3(kStreamThreads), args, 0, stream);
+}
+
+template <typename MetaT>
+int stream_grid_size(int ctas) {
+  if (ctas > 0) return ctas < kStreamMaxCtas ? ctas : kStreamMaxCtas;
+  // one CTA per SM (a cooperative grid must be resident all at once)
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, clock_stream_batched_kernel<MetaT>,
+                                                    kStreamThreads, 0) != cudaSuccess ||
+      per_sm < 1)
+    return 1;
+  const int sms = device_sm_count();
+  return sms < 1 ? 1 : (sms < kStreamMaxCtas ? sms : kStreamMaxCtas);
+}
+
 cudaError_t launch_clock_stream_batched(int meta_bits, int order, void* meta, int64_t num_slots,
                                         int64_t* search_start, int64_t num_steps,
                                         int64_t alloc_per_step, const int64_t* reaccess,
                                         int64_t reaccess_per_step, int64_t* victims,
-                                        int64_t* steps_done, unsigned char* scratch,
+                                        int64_t* steps_done, unsigned char* scratch, int ctas,
                                         int64_t* status, cudaStream_t stream) {
-  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
-  KVCA_META_DISPATCH(meta_bits, clock_stream_batched_kernel<MetaT><<<1, 1024, 0, stream>>>(
-                                    static_cast<MetaT*>(meta), num_slots, search_start, num_steps,
-                                    alloc_per_step, reaccess, reaccess_per_step, victims,
-                                    steps_done, order, aligned, scratch, status));
-  return cudaGetLastError();
+  bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  cudaError_t e = cudaMemsetAsync(scratch + 32 * num_slots, 0, sizeof(StreamGrid), stream);
+  if (e != cudaSuccess) return e;
+  KVCA_META_DISPATCH(meta_bits,
+                     e = launch_stream_grid<MetaT>(stream_grid_size<MetaT>(ctas),
+                                                   static_cast<MetaT*>(meta), num_slots,
+                                                   search_start, num_steps, alloc_per_step,
+                                                   reaccess, reaccess_per_step, victims,
+                                                   steps_done, order, aligned, scratch, status,
+                                                   stream));
+  return e;
 }
 
 }  // namespace kvca

@@ -108,11 +108,15 @@ cudaError_t launch_clock_stream(int meta_bits, int order, void* meta, int64_t nu
                                 int64_t* victims, int64_t* steps_done, int64_t* status,
                                 cudaStream_t stream);
 
+// Bytes of the batched stream's grid words after its 32 bytes per slot.
+constexpr size_t kClockStreamGridBytes = 16384;
+
+// ctas: CTAs of the cooperative grid (0: one per SM; 1: a single CTA).
 cudaError_t launch_clock_stream_batched(int meta_bits, int order, void* meta, int64_t num_slots,
                                         int64_t* search_start, int64_t num_steps,
                                         int64_t alloc_per_step, const int64_t* reaccess,
                                         int64_t reaccess_per_step, int64_t* victims,
-                                        int64_t* steps_done, unsigned char* scratch,
+                                        int64_t* steps_done, unsigned char* scratch, int ctas,
                                         int64_t* status, cudaStream_t stream);
 
 cudaError_t launch_plan_load(int meta_bits, int order, const int64_t* l2p, int64_t num_logical,

@@ -375,13 +375,14 @@ def _clock_scratch(dev: torch.device, num_slots: int) -> torch.Tensor:
 def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps: int,
                  alloc_per_step: int, reaccess: torch.Tensor, reaccess_per_step: int, *,
                  victims: torch.Tensor | None = None, order: str | None = None,
-                 method: str = "batched", check: bool | None = None):
+                 method: str = "batched", ctas: int = 0, check: bool | None = None):
     """Run ``num_steps`` of (pop ``alloc_per_step`` victims, refill them with
     usage 1, bump the step's ``reaccess_per_step`` re-accessed slots) in one
     launch.  Returns (victims, steps_done tensor).
 
     ``method="batched"`` resolves runs of steps that need no aging at once
-    (same results); ``method="steps"`` runs the steps one after another."""
+    (same results) on a cooperative grid of ``ctas`` CTAs (0: one per SM, 1:
+    one CTA); ``method="steps"`` runs the steps one after another."""
     _require(slot_meta, _META_DTYPES, "slot_meta")
     _require(search_start, torch.int64, "search_start")
     _require(reaccess, torch.int64, "reaccess")
@@ -402,7 +403,7 @@ def clock_stream(slot_meta: torch.Tensor, search_start: torch.Tensor, num_steps:
             rc = _lib_handle.kvca_clock_stream_batched(
                 _meta_bits(slot_meta), order_code, _ptr(slot_meta), slot_meta.numel(), _ptr(search_start),
                 num_steps, alloc_per_step, _ptr(reaccess), reaccess_per_step, _ptr(victims), _ptr(steps_done),
-                _ptr(_clock_scratch(dev, slot_meta.numel())), _ptr(_status(dev)), _stream(dev))
+                _ptr(_clock_scratch(dev, slot_meta.numel())), int(ctas), _ptr(_status(dev)), _stream(dev))
         elif method == "steps":
             rc = _lib_handle.kvca_clock_stream(
                 _meta_bits(slot_meta), order_code, _ptr(slot_meta), slot_meta.numel(), _ptr(search_start),

@@ -29,7 +29,15 @@ def _pack16(pins, usage):
     return ((pins.to(torch.int32) & 255) | ((usage.to(torch.int32) & 255) << 8)).to(torch.uint16)
 
 
-@pytest.mark.parametrize("method", ["batched", "steps"])
+# "batched" runs on a cooperative grid (one CTA per SM), "batched1" on one CTA
+METHODS = ["batched", "batched1", "steps"]
+
+
+def _method(name):
+    return ("batched", 1) if name == "batched1" else (name, 0)
+
+
+@pytest.mark.parametrize("method", METHODS)
 def test_recorded_reference_streams(ops, golden_dir, method):
     for rec in json.loads((golden_dir / "clock_stream.json").read_text()):
         p = rec["params"]
@@ -37,7 +45,7 @@ def test_recorded_reference_streams(ops, golden_dir, method):
         ss = torch.zeros(1, dtype=torch.int64, device=DEV)
         victims, done = ops.clock_stream(meta, ss, p["num_steps"], p["alloc_per_step"],
                                          workloads.zipf_reaccess(p).to(DEV), p["reaccess_per_step"],
-                                         method=method)
+                                         method=_method(method)[0], ctas=_method(method)[1])
         assert int(done) == rec["steps_done"]
         assert victims.tolist() == rec["victims"]
         assert workloads.sha256_of(meta) == rec["final_slot_meta_sha256"]
@@ -53,13 +61,14 @@ def _run_both(ops, p, *, order="grouped", bits=8, method="batched"):
                                            p["reaccess_per_step"], order=order)
     meta_d = workloads.clock_initial_meta(p, pack).to(DEV)
     ss_d = torch.zeros(1, dtype=torch.int64, device=DEV)
+    name, ctas = _method(method)
     got, done_d = ops.clock_stream(meta_d, ss_d, p["num_steps"], p["alloc_per_step"], reacc.to(DEV),
-                                   p["reaccess_per_step"], order=order, method=method, check=False)
+                                   p["reaccess_per_step"], order=order, method=name, ctas=ctas, check=False)
     torch.cuda.synchronize()
     return (want, done_h, rc, meta_h, ss_h), (got, int(done_d), meta_d, ss_d)
 
 
-@pytest.mark.parametrize("method", ["batched", "steps"])
+@pytest.mark.parametrize("method", METHODS)
 @pytest.mark.parametrize("order", ["grouped", "prefix"])
 @pytest.mark.parametrize("bits", [8, 16])
 @pytest.mark.parametrize("k,m,usage_hi", [(1, 1, 3), (256, 256, 3), (5, 40, 15), (64, 8, 1)])
@@ -75,7 +84,7 @@ def test_streams_match_oracle(ops, method, order, bits, k, m, usage_hi):
     ops.check_status(DEV)
 
 
-@pytest.mark.parametrize("method", ["batched", "steps"])
+@pytest.mark.parametrize("method", METHODS)
 @pytest.mark.parametrize("k", [1, 256])
 def test_full_size_clock_stress_matches_oracle(ops, k, method):
     """1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations with one
@@ -98,9 +107,10 @@ def test_full_size_clock_stress_matches_oracle(ops, k, method):
     (1, 0, 777, 5000, 2, 0.5),         # no re-access at all
     (128, 1024, 4096, 300, 7, 0.1),    # heavy re-access with duplicates in each batch
 ])
-def test_batched_stream_with_frequent_aging_matches_oracle(ops, k, m, n, steps, usage_hi, pinned):
+@pytest.mark.parametrize("method", ["batched", "batched1"])
+def test_batched_stream_with_frequent_aging_matches_oracle(ops, k, m, n, steps, usage_hi, pinned, method):
     p = workloads.clock_params(n, steps, k, m, seed=99 + k + m + n, usage_hi=usage_hi, pinned_frac=pinned)
-    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p, method="batched")
+    (want, done_h, rc, meta_h, ss_h), (got, done_d, meta_d, ss_d) = _run_both(ops, p, method=method)
     assert done_d == done_h
     assert torch.equal(got.cpu()[: done_h * k], want[: done_h * k])
     assert np.array_equal(meta_d.cpu().numpy(), meta_h.numpy())
@@ -109,7 +119,7 @@ def test_batched_stream_with_frequent_aging_matches_oracle(ops, k, m, n, steps, 
         ops.check_status(DEV)
 
 
-@pytest.mark.parametrize("method", ["batched", "steps"])
+@pytest.mark.parametrize("method", METHODS)
 def test_stream_stops_on_insufficient_capacity(ops, method):
     from kv_cache_adapter_b200.errors import InsufficientCapacityError
 
@@ -119,9 +129,30 @@ def test_stream_stops_on_insufficient_capacity(ops, method):
     meta = adapter_mod._pack_slot_meta(pins, torch.zeros(10, dtype=torch.int64)).to(DEV)
     ss = torch.zeros(1, dtype=torch.int64, device=DEV)
     reacc = torch.zeros(0, dtype=torch.int64, device=DEV)
-    victims, done = ops.clock_stream(meta, ss, 3, 8, reacc, 0, check=False, method=method)
+    name, ctas = _method(method)
+    victims, done = ops.clock_stream(meta, ss, 3, 8, reacc, 0, check=False, method=name, ctas=ctas)
     assert int(done) == 0
     with pytest.raises(InsufficientCapacityError):
         ops.check_status(DEV)
-    victims, done = ops.clock_stream(meta, ss, 3, 7, reacc, 0, method=method)
+    victims, done = ops.clock_stream(meta, ss, 3, 7, reacc, 0, method=name, ctas=ctas)
     assert int(done) == 3
+
+
+@pytest.mark.parametrize("ctas", [2, 7, 33])
+def test_batched_stream_on_odd_grids(ops, ctas):
+    """Grids that do not divide the slots, candidates or events evenly."""
+    p = workloads.clock_params(100_003, 500, 3, 17, seed=77 + ctas, usage_hi=5, pinned_frac=0.2)
+    meta_h = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta)
+    reacc = workloads.zipf_reaccess(p)
+    ss_h = torch.zeros(1, dtype=torch.int64)
+    want, done_h, rc = oracle.clock_stream(meta_h, ss_h, p["num_steps"], p["alloc_per_step"], reacc,
+                                           p["reaccess_per_step"])
+    meta_d = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta).to(DEV)
+    ss_d = torch.zeros(1, dtype=torch.int64, device=DEV)
+    got, done_d = ops.clock_stream(meta_d, ss_d, p["num_steps"], p["alloc_per_step"], reacc.to(DEV),
+                                   p["reaccess_per_step"], ctas=ctas)
+    assert int(done_d) == done_h
+    assert torch.equal(got.cpu()[: done_h * 3], want[: done_h * 3])
+    assert np.array_equal(meta_d.cpu().numpy(), meta_h.numpy())
+    assert int(ss_d[0]) == int(ss_h[0])
+    ops.check_status(DEV)
