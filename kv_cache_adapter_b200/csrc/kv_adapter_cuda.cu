@@ -498,8 +498,9 @@ __global__ void __launch_bounds__(1024)
 //   2. first re-access step of every slot re-accessed in the window of steps
 //      the candidates can cover (atomicMax on an encoded step; the thread
 //      that sets a slot first lists it, so touched slots are listed once);
-//   3. candidates with a re-access in the window ("pending") are listed in
-//      order; one warp resolves only those, 32 at a time with a ballot fixed
+//   3. candidates whose first re-access can come before the step that takes
+//      them ("pending") are listed in order; one warp resolves only those,
+//      32 at a time with a ballot fixed
 //      point: pending candidate j is taken unless its first re-access step is
 //      below s0 + (taken before j) / k, where taken before j = (candidates
 //      before j that are not pending) + (pending ones taken before it);
@@ -521,9 +522,12 @@ constexpr int kCandPerThread = 16;  // candidates per thread per block-scan tile
 constexpr int kWarpDedupMin = 16;   // re-accesses per step deduplicated in registers
 constexpr int kWarpDedupMax = 256;
 
+constexpr int kPendingTile = 4096;  // pending candidates staged per round of the resolution
+
 template <typename MetaT>
 struct EpochShared {
   PopShared<MetaT> pop;
+  long long tile[kPendingTile];
   int scan[33];
   long long start;
   long long s_end;
@@ -723,20 +727,42 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   const int64_t ev_hi = s_hi * m;
 
   // 2. first re-access step in the window, encoded as INT_MAX - step (0 = none)
-  for (int64_t e = ev_lo + gt; e < ev_hi; e += G) {
-    const int64_t x = reaccess[e];
-    if (!slot_ok(x, n)) {
-      report(status, KVCA_ERR_BAD_INDEX, x);
-      continue;
+  // (the first setter of a slot lists it; one list reservation per warp)
+  for (int64_t e0 = ev_lo + (gt & ~int64_t{31}); e0 < ev_hi; e0 += G) {
+    const int64_t e = e0 + (threadIdx.x & 31);
+    bool first = false;
+    int64_t x = -1;
+    if (e < ev_hi) {
+      x = reaccess[e];
+      if (!slot_ok(x, n)) {
+        report(status, KVCA_ERR_BAD_INDEX, x);
+        x = -1;
+      }
     }
-    const int32_t old = atomicMax(w.first_bump + x, static_cast<int32_t>(INT32_MAX - e / m));
-    if (old == 0) w.touched[atomicAdd(&g->nu, 1)] = static_cast<int32_t>(x);
+    // lanes holding the same slot (a popular one) send one atomic: the
+    // highest lane carries the earliest step, the largest encoding
+    const unsigned peers = __match_any_sync(0xffffffffu, x);
+    if (x >= 0 && (threadIdx.x & 31) == 31 - __clz(peers))
+      first = atomicMax(w.first_bump + x, static_cast<int32_t>(INT32_MAX - (e0 + __ffs(peers) - 1) / m)) == 0;
+    const unsigned firsts = __ballot_sync(0xffffffffu, first);
+    if (firsts != 0u) {
+      const int lane = threadIdx.x & 31;
+      int base = 0;
+      if (lane == __ffs(firsts) - 1) base = atomicAdd(&g->nu, __popc(firsts));
+      base = __shfl_sync(0xffffffffu, base, __ffs(firsts) - 1);
+      if (first) w.touched[base + __popc(firsts & ((1u << lane) - 1u))] = static_cast<int32_t>(x);
+    }
   }
   KVCA_GRID_SYNC();
   const int nu = __ldcg(&g->nu);
+  // A candidate is pending only if its first re-access can come before the
+  // step that takes it.  At most j candidates are taken before candidate j,
+  // so it is taken by step s0 + j / k at the latest: a first re-access at or
+  // after that step never passes it over, and it is treated as not pending.
   for (int64_t j = gt; j < nc; j += G) {
     const int32_t enc = __ldcg(w.first_bump + __ldcg(w.cand + j));
-    w.cand_bump[j] = enc == 0 ? INT32_MAX : INT32_MAX - enc;
+    const int64_t first = enc == 0 ? INT32_MAX : INT32_MAX - enc;
+    w.cand_bump[j] = first >= s0 + j / k ? INT32_MAX : static_cast<int32_t>(first);
   }
   KVCA_GRID_SYNC();
 
@@ -777,39 +803,53 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   KVCA_GRID_SYNC();
 
   // 3b. one warp of CTA 0 resolves the pending candidates; each entry becomes
-  //     (pending candidates taken before it << 1) | taken
+  //     (pending candidates taken before it << 1) | taken.  The whole CTA
+  //     stages them through shared memory a tile at a time, so the warp's
+  //     sequential pass reads shared memory, not global.
   const int32_t kk = static_cast<int32_t>(k);
   const int32_t max_taken = static_cast<int32_t>((steps - s0) * k);
   const int32_t step0 = static_cast<int32_t>(s0);
-  if (b == 0 && threadIdx.x < 32) {
-    const int lane = threadIdx.x;
+  if (b == 0) {
+    const int lane = threadIdx.x & 31;
     const unsigned below = (1u << lane) - 1u;
     int32_t tp = 0;
-    for (int64_t p0w = 0; p0w < np; p0w += 32) {
-      const int64_t p = p0w + lane;
-      const bool here = p < np;
-      const int64_t pr = here ? __ldcg(reinterpret_cast<const long long*>(w.pending) + p) : 0;
-      const int32_t jj = static_cast<int32_t>(pr >> 32);
-      const int32_t bv = static_cast<int32_t>(pr & 0xffffffffll);
-      const int32_t nonpending_before = here ? jj - static_cast<int32_t>(p) : 0;
-      const unsigned present = __ballot_sync(0xffffffffu, here);
-      unsigned cur = present;
-      for (int it = 0; it < 33; ++it) {  // converges in at most 32 rounds
-        const int32_t tb = nonpending_before + tp + __popc(cur & below);
-        const int32_t st = kk == 1 ? step0 + tb : step0 + tb / kk;
-        const bool take = here && tb < max_taken && bv >= st;
-        const unsigned ok_mask = __ballot_sync(0xffffffffu, take);
-        const unsigned diff = (ok_mask ^ cur) & present;
-        if (diff == 0u) break;
-        const unsigned keep = (1u << (__ffs(diff) - 1)) - 1u;
-        cur = (cur & keep) | (ok_mask & ~keep);
+    for (int64_t t0 = 0; t0 < np; t0 += kPendingTile) {
+      const int cnt = static_cast<int>(np - t0 < kPendingTile ? np - t0 : kPendingTile);
+      for (int i = threadIdx.x; i < cnt; i += blockDim.x)
+        sh.tile[i] = __ldcg(reinterpret_cast<const long long*>(w.pending) + t0 + i);
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        for (int q0 = 0; q0 < cnt; q0 += 32) {
+          const int q = q0 + lane;
+          const bool here = q < cnt;
+          const int64_t p = t0 + q;
+          const int64_t pr = here ? sh.tile[q] : 0;
+          const int32_t jj = static_cast<int32_t>(pr >> 32);
+          const int32_t bv = static_cast<int32_t>(pr & 0xffffffffll);
+          const int32_t nonpending_before = here ? jj - static_cast<int32_t>(p) : 0;
+          const unsigned present = __ballot_sync(0xffffffffu, here);
+          unsigned cur = present;
+          for (int it = 0; it < 33; ++it) {  // converges in at most 32 rounds
+            const int32_t tb = nonpending_before + tp + __popc(cur & below);
+            const int32_t st = kk == 1 ? step0 + tb : step0 + tb / kk;
+            const bool take = here && tb < max_taken && bv >= st;
+            const unsigned ok_mask = __ballot_sync(0xffffffffu, take);
+            const unsigned diff = (ok_mask ^ cur) & present;
+            if (diff == 0u) break;
+            const unsigned keep = (1u << (__ffs(diff) - 1)) - 1u;
+            cur = (cur & keep) | (ok_mask & ~keep);
+          }
+          if (here)
+            sh.tile[q] = (static_cast<long long>(tp + __popc(cur & below)) << 1) |
+                         static_cast<long long>((cur >> lane) & 1u);
+          tp += __popc(cur);
+        }
       }
-      if (here)
-        w.pending[p] = (static_cast<int64_t>(tp + __popc(cur & below)) << 1) |
-                       static_cast<int64_t>((cur >> lane) & 1u);
-      tp += __popc(cur);
+      __syncthreads();
+      for (int i = threadIdx.x; i < cnt; i += blockDim.x) w.pending[t0 + i] = sh.tile[i];
+      __syncthreads();
     }
-    if (lane == 0) g->tp_total = tp;
+    if (threadIdx.x == 0) g->tp_total = tp;
   }
   KVCA_GRID_SYNC();
   const int32_t tp_total = __ldcg(&g->tp_total);
@@ -903,16 +943,24 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
       }
     }
   } else {
-    for (int64_t e = ev_lo + gt; e < cnt_hi; e += G) {
-      const int64_t x = reaccess[e];
-      if (!slot_ok(x, n)) continue;
-      const int64_t t = e / m;
-      bool dup = false;
+    for (int64_t e0 = ev_lo + (gt & ~int64_t{31}); e0 < cnt_hi; e0 += G) {
+      const int64_t e = e0 + (threadIdx.x & 31);
+      int64_t key = -1;
+      if (e < cnt_hi) {
+        const int64_t x = reaccess[e];
+        if (slot_ok(x, n)) {
+          const int64_t t = e / m;
+          bool dup = false;
 #pragma unroll 8
-      for (int64_t i = t * m; i < e; ++i) dup |= reaccess[i] == x;
-      if (dup) continue;
-      const int32_t vs = __ldcg(w.victim_step + x);
-      if (vs == 0 || vs - 1 <= t) atomicAdd(w.bump_count + x, 1);
+          for (int64_t i = t * m; i < e; ++i) dup |= reaccess[i] == x;
+          const int32_t vs = dup ? 0 : __ldcg(w.victim_step + x);
+          if (!dup && (vs == 0 || vs - 1 <= t)) key = x;
+        }
+      }
+      // one atomic per slot per warp (popular slots are bumped by many lanes)
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      if (key >= 0 && (threadIdx.x & 31) == __ffs(peers) - 1)
+        atomicAdd(w.bump_count + key, __popc(peers));
     }
   }
   KVCA_GRID_SYNC();
