@@ -915,29 +915,31 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = G >> 5;
     for (int64_t t = s0 + (gt >> 5); t < s_end; t += nwarps) {
-      int64_t ids[kWarpDedupMax / 32];
-      bool dup[kWarpDedupMax / 32];
+      // slot ids fit 31 bits (num_slots < 2^31): 32-bit keys, one shuffle each
+      int32_t ids[kWarpDedupMax / 32];
+      unsigned dup = 0u;  // bit q: ids[q] repeats an earlier id of the step
 #pragma unroll
       for (int q = 0; q < kWarpDedupMax / 32; ++q) {
         const int64_t i = static_cast<int64_t>(q) * 32 + lane;
-        ids[q] = i < m ? reaccess[t * m + i] : -1;
-        dup[q] = false;
+        const int64_t x = i < m ? reaccess[t * m + i] : -1;
+        ids[q] = slot_ok(x, n) ? static_cast<int32_t>(x) : -1 - q * 32 - lane;  // invalid: unique negatives
       }
 #pragma unroll
       for (int u = 0; u < kWarpDedupMax / 32; ++u) {
         if (static_cast<int64_t>(u) * 32 >= m) break;
-#pragma unroll
+#pragma unroll 8
         for (int l = 0; l < 32; ++l) {
-          const int64_t v = __shfl_sync(0xffffffffu, ids[u], l);
+          const int32_t v = __shfl_sync(0xffffffffu, ids[u], l);
           const int i = u * 32 + l;
 #pragma unroll
-          for (int q = 0; q < kWarpDedupMax / 32; ++q) dup[q] |= (q * 32 + lane > i) && ids[q] == v;
+          for (int q = 0; q < kWarpDedupMax / 32; ++q)
+            dup |= static_cast<unsigned>((q * 32 + lane > i) && ids[q] == v) << q;
         }
       }
 #pragma unroll
       for (int q = 0; q < kWarpDedupMax / 32; ++q) {
-        const int64_t x = ids[q];
-        if (dup[q] || !slot_ok(x, n)) continue;
+        const int32_t x = ids[q];
+        if (((dup >> q) & 1u) != 0u || x < 0) continue;
         const int32_t vs = __ldcg(w.victim_step + x);
         if (vs == 0 || vs - 1 <= t) atomicAdd(w.bump_count + x, 1);
       }
