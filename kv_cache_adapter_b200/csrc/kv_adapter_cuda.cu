@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(1024)
 // epochs the kernel runs a stretch of exact steps instead.  Results equal the
 // step-by-step stream bit for bit.
 
-constexpr int kStreamThreads = 1024;  // threads per CTA of the batched stream
+constexpr int kStreamThreads = 512;   // threads per CTA of the batched stream
 constexpr int kStreamMaxCtas = 1024;  // CTAs of its cooperative grid, at most
 constexpr int64_t kEpochMinSteps = 8;
 constexpr int64_t kExactStepsAfterShortEpoch = 64;
@@ -815,24 +815,28 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
     int32_t tp = 0;
     for (int64_t t0 = 0; t0 < np; t0 += kPendingTile) {
       const int cnt = static_cast<int>(np - t0 < kPendingTile ? np - t0 : kPendingTile);
-      for (int i = threadIdx.x; i < cnt; i += blockDim.x)
-        sh.tile[i] = __ldcg(reinterpret_cast<const long long*>(w.pending) + t0 + i);
+      // per entry, the largest count of pending candidates taken before it
+      // that still lets it be taken: with tb = (candidates before it that
+      // are not pending) + that count, it is taken while tb < max_taken and
+      // its first re-access bv >= s0 + tb / k, i.e. tb <= k (bv - s0) + k - 1
+      for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+        const int64_t pr = __ldcg(reinterpret_cast<const long long*>(w.pending) + t0 + i);
+        const int64_t nonpending_before = (pr >> 32) - (t0 + i);
+        const int64_t bv = pr & 0xffffffffll;
+        int64_t c = kk * (bv - step0) + kk - 1 - nonpending_before;
+        if (c > max_taken - 1 - nonpending_before) c = max_taken - 1 - nonpending_before;
+        sh.tile[i] = c;
+      }
       __syncthreads();
       if (threadIdx.x < 32) {
         for (int q0 = 0; q0 < cnt; q0 += 32) {
           const int q = q0 + lane;
           const bool here = q < cnt;
-          const int64_t p = t0 + q;
-          const int64_t pr = here ? sh.tile[q] : 0;
-          const int32_t jj = static_cast<int32_t>(pr >> 32);
-          const int32_t bv = static_cast<int32_t>(pr & 0xffffffffll);
-          const int32_t nonpending_before = here ? jj - static_cast<int32_t>(p) : 0;
+          const int64_t c = here ? sh.tile[q] : -1;
           const unsigned present = __ballot_sync(0xffffffffu, here);
           unsigned cur = present;
           for (int it = 0; it < 33; ++it) {  // converges in at most 32 rounds
-            const int32_t tb = nonpending_before + tp + __popc(cur & below);
-            const int32_t st = kk == 1 ? step0 + tb : step0 + tb / kk;
-            const bool take = here && tb < max_taken && bv >= st;
+            const bool take = here && tp + __popc(cur & below) <= c;
             const unsigned ok_mask = __ballot_sync(0xffffffffu, take);
             const unsigned diff = (ok_mask ^ cur) & present;
             if (diff == 0u) break;
