@@ -445,6 +445,43 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_clock_stress(args, world: int, rank: int, device) -> None:
+    """The clock stress alone: 1,048,576 slots, 200k allocations with one
+    Zipf(1.1) re-access each, batches k = 1 and k = 256, one launch each."""
+    runs = [gpu_clock(device, 1, reps=max(args.steps, 1)), gpu_clock(device, 256, reps=max(args.steps, 1))]
+    if rank != 0:
+        return
+    k1 = runs[0]
+    line = {
+        "metric": "clock evictions/s",
+        "value": round(world * k1["evictions_per_s"], 1),
+        "unit": "evictions/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": k1["ms"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u8",
+        "data": "synthetic (seeded usage, pins and Zipf re-access stream)",
+        "config": {"workload": "clock stress: 1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations, "
+                               "1 Zipf(1.1) re-access per allocation, batch k = 1 (value) and 256, "
+                               "device-resident stream, one cooperative launch per run",
+                   "timing": "CUDA events around each launch, best of the timed runs"},
+        "runs": runs,
+        "roofline": {"bound": "latency", "achieved": k1["evictions_per_s"], "peak": None, "unit": "evictions/s",
+                     "frac": None, "traffic": None,
+                     "note": "a chain of dependent pops: the one-warp pending resolution and grid barriers "
+                             "bound it, not HBM"},
+        "gpu_launches": 2 * (max(args.steps, 1) + 1),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_clock(1)
+        line["cpu_baseline_k256"] = cpu_clock(256)
+    print(json.dumps(line), flush=True)
+
+
 DECODE_STEPS_PER_BENCH_STEP = 50
 
 
@@ -800,7 +837,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter", "host-tier"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter", "host-tier", "clock-stress"],
                     default="llama70b-shard")
     ap.add_argument("--heads", type=int, default=None, help="KV heads per GPU for the decode mix (default 1)")
     ap.add_argument("--seqs", type=int, default=None,
@@ -836,6 +873,8 @@ def main() -> None:
             run_adapter(args, world, rank, device)
         elif args.workload == "host-tier":
             run_host_tier(args, world, rank, device)
+        elif args.workload == "clock-stress":
+            run_clock_stress(args, world, rank, device)
         else:
             run_ours(args, w, world, rank, device)
     finally:
