@@ -1600,15 +1600,28 @@ __global__ void __launch_bounds__(1024)
   if (threadIdx.x == 0) bad = 0;
   __syncthreads();
   const int64_t base = *next_logical;
+  // Thread t keeps what it reads for need entry t (the common case: at most
+  // one entry per thread); entries beyond the block size are read again.
+  int64_t my_q = -1, my_full = -1;
   for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
     const int64_t q = need[j];
     int64_t v = q;
+    int64_t full = -1;
     bool ok = in_range(q, seqs);
     if (ok) {
       v = cur_logical[q];
-      ok = in_range(v, n_logical) && in_range(l2p[v], n);
+      ok = in_range(v, n_logical);
+      if (ok) {
+        full = l2p[v];
+        ok = in_range(full, n);
+        if (!ok) v = full;
+      }
     }
     if (!ok && atomicCAS(&bad, 0, 1) == 0) bad_value = v;
+    if (j == threadIdx.x) {
+      my_q = q;
+      my_full = full;
+    }
   }
   if (threadIdx.x == 0 && c > 0 && (base < 0 || base + c > n_logical) && atomicCAS(&bad, 0, 1) == 0)
     bad_value = base + c;
@@ -1624,35 +1637,39 @@ __global__ void __launch_bounds__(1024)
       return;
     }
     __syncthreads();
+    // Unmap the victims' previous ids, commit the new ones, release the full
+    // blocks.  The writes of different entries never meet: evicted ids are
+    // older than base, the full blocks are pinned (never victims) and each
+    // sequence appears once.
     for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
-      const int64_t prev = p2l[victims[j]];
-      if (prev >= 0) l2p[prev] = -1;
-    }
-    __syncthreads();
-    for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
+      const int64_t q = j == threadIdx.x ? my_q : need[j];
+      const int64_t full = j == threadIdx.x ? my_full : l2p[cur_logical[q]];
       const int64_t v = victims[j];
+      const int64_t prev = p2l[v];
+      if (prev >= 0) l2p[prev] = -1;
       l2p[base + j] = v;
       p2l[v] = base + j;
       meta[v] = M::pack(1, 1);
-    }
-    __syncthreads();
-    // the full blocks are pinned, so none of them was a victim; each sequence
-    // appears once, so each slot is released once
-    for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
-      const int64_t q = need[j];
-      const int64_t full = l2p[cur_logical[q]];
       const unsigned w = meta[full];
       meta[full] = M::pack(static_cast<int64_t>(M::pin(w)) - 1, M::usage(w));
-      cur_block[q] = victims[j];
+      cur_block[q] = v;
       cur_logical[q] = base + j;
-      pos[q] = 0;
     }
-    __syncthreads();
     if (threadIdx.x == 0) *next_logical = base + c;
   }
+  // this step's token slots; the sequences that got a new block are
+  // rewritten below (block v, position 0)
   for (int64_t q = threadIdx.x; q < seqs; q += blockDim.x) {
     slot_mapping[q] = cur_block[q] * block_size + pos[q];
     pos[q] += 1;
+  }
+  if (c > 0) {
+    __syncthreads();
+    for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
+      const int64_t q = j == threadIdx.x ? my_q : need[j];
+      slot_mapping[q] = victims[j] * block_size;
+      pos[q] = 1;
+    }
   }
 }
 
