@@ -527,13 +527,8 @@ constexpr int kPendingTile = 4096;  // pending candidates staged per round of th
 template <typename MetaT>
 struct EpochShared {
   PopShared<MetaT> pop;
-  long long tile[kPendingTile];
+  long long tile[kPendingTile];  // pending candidates staged for the one-warp pass
   int scan[33];
-  long long start;
-  long long s_end;
-  long long last_victim;
-  int tp_total;  // pending candidates taken
-  int nu;        // distinct slots re-accessed in the window
 };
 
 // Scratch of kvca_clock_stream_batched, carved from one buffer (byte
