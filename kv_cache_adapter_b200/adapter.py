@@ -269,15 +269,17 @@ class KVCacheAdapter:
             selected_physical.index_copy_(0, missing_positions, allocated_physical)
 
         # pins and usage are read after the sweep, which may have aged usage
-        final_pin_counts = _slot_meta_pin_counts(self._slot_meta.index_select(0, selected_physical))
+        final_pin_counts = _slot_meta_pin_counts(_take(self._slot_meta, selected_physical))
         final_usage_counts = inspected_usage
         if missing_ids.numel() > 0 and existing_physical.numel() > 0:
-            final_usage_counts = torch.ones_like(logical_block_ids, dtype=USAGE_DTYPE)
+            final_usage_counts = torch.ones_like(logical_block_ids, dtype=torch.int32)
             final_usage_counts.index_copy_(
                 0,
                 existing_positions,
-                _saturating_increment_usage(_slot_meta_usage_counts(self._slot_meta.index_select(0, existing_physical))),
+                _saturating_increment_usage(_slot_meta_usage_counts(_take(self._slot_meta, existing_physical)))
+                .to(dtype=torch.int32),
             )
+            final_usage_counts = final_usage_counts.to(dtype=USAGE_DTYPE)
         eviction_plan = self._build_eviction_plan(logical_block_ids, selected_physical)
         if eviction_plan.logical_block_ids.numel() > 0:
             self.backend.save_blocks(eviction_plan.logical_block_ids, eviction_plan.payloads)
@@ -319,9 +321,9 @@ class KVCacheAdapter:
             self.backend.load_blocks(miss_logical_ids, self.actual_blocks, miss_slot_ids)
 
         if miss_logical_ids.numel() > 0 and hit_slot_ids.numel() > 0:
-            hit_usage = _saturating_increment_usage(_slot_meta_usage_counts(self._slot_meta.index_select(0, hit_slot_ids)))
+            hit_usage = _saturating_increment_usage(_slot_meta_usage_counts(_take(self._slot_meta, hit_slot_ids)))
         else:
-            hit_usage = updated_usage.index_select(0, resident_positions)
+            hit_usage = _take(updated_usage, resident_positions)
         miss_usage = torch.ones((miss_slot_ids.shape[0],), dtype=USAGE_DTYPE, device=self.actual_blocks.device)
         result_physical = current_physical
         if miss_positions.numel() > 0:
@@ -832,6 +834,14 @@ def _load_cuda_extension_module() -> Any | None:
         return importlib.import_module(f"{__package__}.kv_cache_adapter_cuda")
     except ImportError:
         return None
+
+
+def _take(t: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """``t.index_select(0, index)``, also for uint16 words (16-bit slot meta),
+    which torch's index_select does not take."""
+    if t.dtype == torch.uint16:
+        return t.to(dtype=torch.int32).index_select(0, index).to(dtype=torch.uint16)
+    return t.index_select(0, index)
 
 
 def _saturating_increment_usage(values: torch.Tensor) -> torch.Tensor:
