@@ -523,6 +523,7 @@ constexpr int kWarpDedupMin = 16;   // re-accesses per step deduplicated in regi
 constexpr int kWarpDedupMax = 256;
 
 constexpr int kPendingTile = 4096;  // pending candidates staged per round of the resolution
+static_assert(kPendingTile % kStreamThreads == 0, "pending tile split evenly over the CTA");
 
 template <typename MetaT>
 struct EpochShared {
@@ -797,36 +798,55 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   }
   KVCA_GRID_SYNC();
 
-  // 3b. one warp of CTA 0 resolves the pending candidates; each entry becomes
-  //     (pending candidates taken before it << 1) | taken.  The whole CTA
-  //     stages them through shared memory a tile at a time, so the warp's
-  //     sequential pass reads shared memory, not global.
+  // 3b. CTA 0 resolves the pending candidates; each entry becomes
+  //     (pending candidates taken before it << 1) | taken.
+  //     Pending entry p (candidate j, first re-access bv) is taken iff
+  //     tb < max_taken and bv >= s0 + tb / k, where tb = (j - p) + (pending
+  //     taken before it), i.e. iff (pending taken before it) <= c with
+  //     c = min(k (bv - s0) + k - 1, max_taken - 1) - (j - p).  As
+  //     (pending taken before it) >= 0, an entry with c < 0 is surely passed
+  //     over; only the others (few: their first re-access falls in the short
+  //     window of steps the earlier pending ones can shift) go through the
+  //     one-warp sequential pass, compacted in order through shared memory.
+  //     A block-wide scan then gives every entry its count.
   const int32_t kk = static_cast<int32_t>(k);
   const int32_t max_taken = static_cast<int32_t>((steps - s0) * k);
   const int32_t step0 = static_cast<int32_t>(s0);
   if (b == 0) {
+    constexpr int E = kPendingTile / kStreamThreads;
     const int lane = threadIdx.x & 31;
     const unsigned below = (1u << lane) - 1u;
-    int32_t tp = 0;
+    int64_t tp_start = 0;  // pending taken before the tile, same in every thread
     for (int64_t t0 = 0; t0 < np; t0 += kPendingTile) {
       const int cnt = static_cast<int>(np - t0 < kPendingTile ? np - t0 : kPendingTile);
-      // per entry, the largest count of pending candidates taken before it
-      // that still lets it be taken: with tb = (candidates before it that
-      // are not pending) + that count, it is taken while tb < max_taken and
-      // its first re-access bv >= s0 + tb / k, i.e. tb <= k (bv - s0) + k - 1
-      for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
-        const int64_t pr = __ldcg(reinterpret_cast<const long long*>(w.pending) + t0 + i);
-        const int64_t nonpending_before = (pr >> 32) - (t0 + i);
-        const int64_t bv = pr & 0xffffffffll;
-        int64_t c = kk * (bv - step0) + kk - 1 - nonpending_before;
-        if (c > max_taken - 1 - nonpending_before) c = max_taken - 1 - nonpending_before;
-        sh.tile[i] = c;
+      // each thread takes E consecutive entries of the tile
+      int64_t cs[E];
+      int unc = 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int i = static_cast<int>(threadIdx.x) * E + e;
+        cs[e] = -1;
+        if (i < cnt) {
+          const int64_t pr = __ldcg(reinterpret_cast<const long long*>(w.pending) + t0 + i);
+          const int64_t nonpending_before = (pr >> 32) - (t0 + i);
+          const int64_t bv = pr & 0xffffffffll;
+          int64_t c = kk * (bv - step0) + kk - 1;
+          if (c > max_taken - 1) c = max_taken - 1;
+          cs[e] = c - nonpending_before;
+        }
+        unc += cs[e] >= 0;
       }
+      int n_unc;
+      int pos = block_excl_scan(unc, &n_unc, sh.scan);
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (cs[e] >= 0) sh.tile[pos++] = cs[e];
       __syncthreads();
       if (threadIdx.x < 32) {
-        for (int q0 = 0; q0 < cnt; q0 += 32) {
+        int64_t tp = tp_start;
+        for (int q0 = 0; q0 < n_unc; q0 += 32) {
           const int q = q0 + lane;
-          const bool here = q < cnt;
+          const bool here = q < n_unc;
           const int64_t c = here ? sh.tile[q] : -1;
           const unsigned present = __ballot_sync(0xffffffffu, here);
           unsigned cur = present;
@@ -838,17 +858,39 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
             const unsigned keep = (1u << (__ffs(diff) - 1)) - 1u;
             cur = (cur & keep) | (ok_mask & ~keep);
           }
-          if (here)
-            sh.tile[q] = (static_cast<long long>(tp + __popc(cur & below)) << 1) |
-                         static_cast<long long>((cur >> lane) & 1u);
+          if (here) sh.tile[q] = (cur >> lane) & 1u;
           tp += __popc(cur);
         }
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < cnt; i += blockDim.x) w.pending[t0 + i] = sh.tile[i];
-      __syncthreads();
+      // taken flags in entry order, then the count before each entry
+      int taken_local = 0;
+      unsigned flags = 0u;
+      pos -= unc;  // this thread's first compacted slot again
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if (cs[e] >= 0) {
+          if (sh.tile[pos++] != 0) {
+            flags |= 1u << e;
+            ++taken_local;
+          }
+        }
+      }
+      int tile_taken;
+      int64_t before = tp_start + block_excl_scan(taken_local, &tile_taken, sh.scan);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int i = static_cast<int>(threadIdx.x) * E + e;
+        if (i < cnt) {
+          const unsigned t = (flags >> e) & 1u;
+          w.pending[t0 + i] = (before << 1) | t;
+          before += t;
+        }
+      }
+      tp_start += tile_taken;
+      __syncthreads();  // sh.tile is refilled by the next tile
     }
-    if (threadIdx.x == 0) g->tp_total = tp;
+    if (threadIdx.x == 0) g->tp_total = static_cast<int>(tp_start);
   }
   KVCA_GRID_SYNC();
   const int32_t tp_total = __ldcg(&g->tp_total);
