@@ -519,8 +519,8 @@ constexpr int kStreamMaxCtas = 1024;  // CTAs of its cooperative grid, at most
 constexpr int64_t kEpochMinSteps = 8;
 constexpr int64_t kExactStepsAfterShortEpoch = 64;
 constexpr int kCandPerThread = 16;  // candidates per thread per block-scan tile
-constexpr int kWarpDedupMin = 16;   // re-accesses per step deduplicated in registers
-constexpr int kWarpDedupMax = 256;
+constexpr int kHashDedupMin = 16;    // re-accesses per step deduplicated in a shared-memory set
+constexpr int kHashDedupMax = 4096;  // (the set, 2 x m rounded up to a power of two, fits the pending tile)
 
 constexpr int kPendingTile = 4096;  // pending candidates staged per round of the resolution
 static_assert(kPendingTile % kStreamThreads == 0, "pending tile split evenly over the CTA");
@@ -751,24 +751,24 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   }
   KVCA_GRID_SYNC();
   const int nu = __ldcg(&g->nu);
-  // A candidate is pending only if its first re-access can come before the
-  // step that takes it.  At most j candidates are taken before candidate j,
-  // so it is taken by step s0 + j / k at the latest: a first re-access at or
-  // after that step never passes it over, and it is treated as not pending.
-  for (int64_t j = gt; j < nc; j += G) {
-    const int32_t enc = __ldcg(w.first_bump + __ldcg(w.cand + j));
-    const int64_t first = enc == 0 ? INT32_MAX : INT32_MAX - enc;
-    w.cand_bump[j] = first >= s0 + j / k ? INT32_MAX : static_cast<int32_t>(first);
-  }
-  KVCA_GRID_SYNC();
-
   // 3a. list the pending candidates in order: (index << 32) | first re-access
-  //     step; CTA b takes candidates [jc0, jc1)
+  //     step; CTA b takes candidates [jc0, jc1) here and in 3c.
+  //     A candidate is pending only if its first re-access can come before
+  //     the step that takes it.  At most j candidates are taken before
+  //     candidate j, so it is taken by step s0 + j / k at the latest: a first
+  //     re-access at or after that step never passes it over, and it is
+  //     treated as not pending.
   const int64_t jc0 = nc * b / B;
   const int64_t jc1 = nc * (b + 1) / B;
   {
     int local = 0;
-    for (int64_t j = jc0 + threadIdx.x; j < jc1; j += T) local += __ldcg(w.cand_bump + j) != INT32_MAX;
+    for (int64_t j = jc0 + threadIdx.x; j < jc1; j += T) {
+      const int32_t enc = __ldcg(w.first_bump + __ldcg(w.cand + j));
+      const int64_t first = enc == 0 ? INT32_MAX : INT32_MAX - enc;
+      const int32_t cb = first >= s0 + j / k ? INT32_MAX : static_cast<int32_t>(first);
+      w.cand_bump[j] = cb;
+      local += cb != INT32_MAX;
+    }
     int total;
     block_excl_scan(local, &total, sh.scan);
     if (threadIdx.x == 0) g->cnt[b] = total;
@@ -949,41 +949,38 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   const int64_t cnt_hi = s_end * m;
 
   // 4a. distinct bumping steps per slot (only steps >= a victim's own step).
-  //     16 to 256 re-accesses per step: one warp per step compares each id
-  //     with the step's earlier ids through shuffles; otherwise each event
-  //     scans its step's earlier ids in memory.
-  if (m >= kWarpDedupMin && m <= kWarpDedupMax) {
-    const int lane = threadIdx.x & 31;
-    const int64_t nwarps = G >> 5;
-    for (int64_t t = s0 + (gt >> 5); t < s_end; t += nwarps) {
-      // slot ids fit 31 bits (num_slots < 2^31): 32-bit keys, one shuffle each
-      int32_t ids[kWarpDedupMax / 32];
-      unsigned dup = 0u;  // bit q: ids[q] repeats an earlier id of the step
-#pragma unroll
-      for (int q = 0; q < kWarpDedupMax / 32; ++q) {
-        const int64_t i = static_cast<int64_t>(q) * 32 + lane;
-        const int64_t x = i < m ? reaccess[t * m + i] : -1;
-        ids[q] = slot_ok(x, n) ? static_cast<int32_t>(x) : -1 - q * 32 - lane;  // invalid: unique negatives
-      }
-#pragma unroll
-      for (int u = 0; u < kWarpDedupMax / 32; ++u) {
-        if (static_cast<int64_t>(u) * 32 >= m) break;
-#pragma unroll 8
-        for (int l = 0; l < 32; ++l) {
-          const int32_t v = __shfl_sync(0xffffffffu, ids[u], l);
-          const int i = u * 32 + l;
-#pragma unroll
-          for (int q = 0; q < kWarpDedupMax / 32; ++q)
-            dup |= static_cast<unsigned>((q * 32 + lane > i) && ids[q] == v) << q;
+  //     16 to 4,096 re-accesses per step: each CTA takes whole steps and
+  //     inserts a step's ids into an open-addressing set in shared memory;
+  //     the thread that inserts an id counts it.  Otherwise each event scans
+  //     its step's earlier ids in memory.
+  if (m >= kHashDedupMin && m <= kHashDedupMax) {
+    int32_t* set = reinterpret_cast<int32_t*>(sh.tile);
+    int tsz = 1;
+    while (tsz < 2 * m) tsz <<= 1;
+    const uint32_t mask = static_cast<uint32_t>(tsz - 1);
+    for (int64_t t = s0 + b; t < s_end; t += B) {
+      for (int i = threadIdx.x; i < tsz; i += blockDim.x) set[i] = -1;
+      __syncthreads();
+      for (int64_t i = threadIdx.x; i < m; i += T) {
+        const int64_t x = reaccess[t * m + i];
+        if (!slot_ok(x, n)) continue;
+        const int32_t key = static_cast<int32_t>(x);
+        uint32_t h = (static_cast<uint32_t>(key) * 0x9E3779B1u) & mask;
+        bool first = false;
+        for (int probe = 0; probe < tsz; ++probe) {  // at most half full: ends at a free slot
+          const int32_t old = atomicCAS(set + h, -1, key);
+          if (old == -1) {
+            first = true;
+            break;
+          }
+          if (old == key) break;
+          h = (h + 1u) & mask;
         }
-      }
-#pragma unroll
-      for (int q = 0; q < kWarpDedupMax / 32; ++q) {
-        const int32_t x = ids[q];
-        if (((dup >> q) & 1u) != 0u || x < 0) continue;
+        if (!first) continue;
         const int32_t vs = __ldcg(w.victim_step + x);
         if (vs == 0 || vs - 1 <= t) atomicAdd(w.bump_count + x, 1);
       }
+      __syncthreads();
     }
   } else {
     for (int64_t e0 = ev_lo + (gt & ~int64_t{31}); e0 < cnt_hi; e0 += G) {
