@@ -953,7 +953,54 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   //     inserts a step's ids into an open-addressing set in shared memory;
   //     the thread that inserts an id counts it.  Otherwise each event scans
   //     its step's earlier ids in memory.
-  if (m >= kHashDedupMin && m <= kHashDedupMax) {
+  constexpr int kWarpSet = kPendingTile * 2 / (kStreamThreads / 32);  // int32 slots per warp
+  if (m >= kHashDedupMin && 2 * m <= kWarpSet) {
+    // small steps: every warp takes whole steps with a set of its own
+    const int lane = threadIdx.x & 31;
+    int32_t* set = reinterpret_cast<int32_t*>(sh.tile) + (threadIdx.x >> 5) * kWarpSet;
+    int tsz = 1;
+    while (tsz < 2 * m) tsz <<= 1;
+    const uint32_t mask = static_cast<uint32_t>(tsz - 1);
+    // consecutive steps go to different CTAs, so a short epoch still spreads
+    const int64_t warp_id = b + B * (threadIdx.x >> 5);
+    for (int64_t t = s0 + warp_id; t < s_end; t += G >> 5) {
+      for (int i = lane; i < tsz; i += 32) set[i] = -1;
+      // the step's ids (at most kWarpSet / 64 per lane), loaded together
+      constexpr int kPerLane = kWarpSet / 64;
+      int32_t keys[kPerLane];
+#pragma unroll
+      for (int u = 0; u < kPerLane; ++u) {
+        const int64_t i = lane + 32 * u;
+        const int64_t x = i < m ? reaccess[t * m + i] : -1;
+        keys[u] = slot_ok(x, n) ? static_cast<int32_t>(x) : -1;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < kPerLane; ++u) {
+        const int32_t key = keys[u];
+        if (key < 0) continue;
+        uint32_t h = (static_cast<uint32_t>(key) * 0x9E3779B1u) & mask;
+        bool first = false;
+        for (int probe = 0; probe < tsz; ++probe) {  // at most half full: ends at a free slot
+          const int32_t old = atomicCAS(set + h, -1, key);
+          if (old == -1) {
+            first = true;
+            break;
+          }
+          if (old == key) break;
+          h = (h + 1u) & mask;
+        }
+        if (!first) keys[u] = -1;  // a repeat within the step
+      }
+      int32_t vss[kPerLane];
+#pragma unroll
+      for (int u = 0; u < kPerLane; ++u) vss[u] = keys[u] >= 0 ? __ldcg(w.victim_step + keys[u]) : -1;
+#pragma unroll
+      for (int u = 0; u < kPerLane; ++u)
+        if (keys[u] >= 0 && (vss[u] == 0 || vss[u] - 1 <= t)) atomicAdd(w.bump_count + keys[u], 1);
+      __syncwarp();
+    }
+  } else if (m >= kHashDedupMin && m <= kHashDedupMax) {
     int32_t* set = reinterpret_cast<int32_t*>(sh.tile);
     int tsz = 1;
     while (tsz < 2 * m) tsz <<= 1;
