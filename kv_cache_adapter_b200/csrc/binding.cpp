@@ -214,8 +214,11 @@ int kvca_clock_stream(int meta_bits, int order, void* d_slot_meta, int64_t num_s
   if (num_slots <= 0 || num_steps < 0 || alloc_per_step < 1 || reaccess_per_step < 0 ||
       reaccess_per_step > 8192)
     return KVCA_ERR_BAD_ARGUMENT;
-  if (!d_slot_meta || !d_search_start || !d_victims || !d_steps_done) return KVCA_ERR_BAD_ARGUMENT;
-  if (reaccess_per_step > 0 && num_steps > 0 && !d_reaccess) return KVCA_ERR_BAD_ARGUMENT;
+  if (!d_slot_meta || !d_search_start || !d_steps_done) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_steps == 0)  // nothing to run: no victims buffer needed
+    return status_of(cudaMemsetAsync(d_steps_done, 0, sizeof(int64_t), stream));
+  if (!d_victims) return KVCA_ERR_BAD_ARGUMENT;
+  if (reaccess_per_step > 0 && !d_reaccess) return KVCA_ERR_BAD_ARGUMENT;
   return status_of(kvca::launch_clock_stream(meta_bits, order, d_slot_meta, num_slots,
                                              d_search_start, num_steps, alloc_per_step,
                                              d_reaccess, reaccess_per_step, d_victims,
@@ -240,10 +243,12 @@ int kvca_clock_stream_batched(int meta_bits, int order, void* d_slot_meta, int64
       alloc_per_step < 1 || alloc_per_step > limit || reaccess_per_step < 0 ||
       reaccess_per_step > 8192 || num_steps * alloc_per_step > limit)
     return KVCA_ERR_BAD_ARGUMENT;
-  if (!d_slot_meta || !d_search_start || !d_victims || !d_steps_done || !d_scratch)
-    return KVCA_ERR_BAD_ARGUMENT;
+  if (!d_slot_meta || !d_search_start || !d_steps_done || !d_scratch) return KVCA_ERR_BAD_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(d_scratch) & 7u) != 0u) return KVCA_ERR_BAD_ARGUMENT;
-  if (reaccess_per_step > 0 && num_steps > 0 && !d_reaccess) return KVCA_ERR_BAD_ARGUMENT;
+  if (num_steps == 0)  // nothing to run: no victims buffer needed
+    return status_of(cudaMemsetAsync(d_steps_done, 0, sizeof(int64_t), stream));
+  if (!d_victims) return KVCA_ERR_BAD_ARGUMENT;
+  if (reaccess_per_step > 0 && !d_reaccess) return KVCA_ERR_BAD_ARGUMENT;
   return status_of(kvca::launch_clock_stream_batched(
       meta_bits, order, d_slot_meta, num_slots, d_search_start, num_steps, alloc_per_step,
       d_reaccess, reaccess_per_step, d_victims, d_steps_done,
