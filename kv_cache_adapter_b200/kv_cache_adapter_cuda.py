@@ -54,6 +54,8 @@ __all__ = [
     "load_device_store",
     "save_device_store",
     "check_status",
+    "status_word",
+    "raise_status",
     "library_path",
     "PlaneTable",
 ]
@@ -143,6 +145,25 @@ def check_status(device: torch.device | int | None = None, what: str = "kv_cache
     code, value = st.tolist()
     if code != 0:
         st.zero_()
+        _raise_for(int(code), int(value), what)
+
+
+def status_word(device: torch.device | int | None = None) -> torch.Tensor:
+    """The device's status word (code, value), int64, that every launch of
+    this module reports into (first error wins).  A pipelined caller copies it
+    to pinned host memory after each step and reads it a step later, instead
+    of synchronising every step with check_status."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    return _status(device)
+
+
+def raise_status(code: int, value: int, what: str = "kv_cache_adapter_cuda") -> None:
+    """Raise the error a (code, value) pair read from status_word stands for;
+    the caller clears the word (status_word(dev).zero_()) before going on."""
+    if code != 0:
         _raise_for(int(code), int(value), what)
 
 
