@@ -1405,13 +1405,16 @@ __global__ void __launch_bounds__(1024)
 
 constexpr int kPackShift = 16;  // hit/miss tile counts packed in one scan word
 
+constexpr int kPlanThreads = 1024;
+
 template <typename MetaT>
 struct PlanShared {
   PopShared<MetaT> pop;
   int bad;
   int repeated;
   long long bad_value;
-  long long ids[1024];
+  long long rkeys[2 * kPlanThreads];  // slot -> largest position in the tile (repeated saves)
+  int rvals[2 * kPlanThreads];
 };
 
 __device__ __forceinline__ void plan_fail(int64_t* counts, int64_t* status, int code, int64_t value) {
@@ -1577,9 +1580,51 @@ __global__ void __launch_bounds__(1024)
   int rc = KVCA_OK;
   if (nm > 0) rc = pop_cta<MetaT>(meta, n, search_start, bitmap, nm, allocated, order, aligned, sh.pop);
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
-    const int64_t cur = l2p[ids[i]];
-    if (cur >= 0) atomicAnd(bitmap + (cur >> 5), ~(1u << (cur & 31)));
+  const bool repeated = sh.repeated != 0;
+  if (!repeated) {
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+      const int64_t cur = l2p[ids[i]];
+      if (cur >= 0) atomicAnd(bitmap + (cur >> 5), ~(1u << (cur & 31)));
+    }
+  } else {
+    // Rows for the data scatter: an existing slot named more than once takes
+    // the row of its last occurrence (index_copy_ applied in order), the
+    // earlier ones are dropped (-1).  Tiles from the last to the first: in a
+    // tile, a shared-memory map elects each slot's largest position, and that
+    // position is the last occurrence overall if the slot's blocked bit is
+    // still set; clearing the bit tells earlier tiles.  Every bit ends clear.
+    const int tsz = 2 * static_cast<int>(blockDim.x);
+    for (int64_t tile = ((k - 1) / blockDim.x) * blockDim.x; tile >= 0; tile -= blockDim.x) {
+      for (int h = threadIdx.x; h < tsz; h += blockDim.x) {
+        sh.rkeys[h] = -1;
+        sh.rvals[h] = -1;
+      }
+      __syncthreads();
+      const int64_t i = tile + threadIdx.x;
+      const int64_t cur = i < k ? l2p[ids[i]] : -1;
+      int h = -1;
+      if (cur >= 0) {
+        h = static_cast<int>((static_cast<uint64_t>(cur) * 0x9E3779B97F4A7C15ull) >> 40) & (tsz - 1);
+        for (int probe = 0; probe < tsz; ++probe) {  // at most half full
+          const long long old = atomicCAS(reinterpret_cast<unsigned long long*>(sh.rkeys + h),
+                                          static_cast<unsigned long long>(-1ll),
+                                          static_cast<unsigned long long>(cur));
+          if (old == -1ll || old == cur) break;
+          h = (h + 1) & (tsz - 1);
+        }
+        atomicMax(sh.rvals + h, static_cast<int>(threadIdx.x));
+      }
+      __syncthreads();
+      if (cur >= 0) {
+        bool last = false;
+        if (sh.rvals[h] == static_cast<int>(threadIdx.x)) {
+          const unsigned bit = 1u << (cur & 31);
+          last = (atomicAnd(bitmap + (cur >> 5), ~bit) & bit) != 0u;
+        }
+        if (rc == KVCA_OK) move_slots[i] = last ? cur : -1;
+      }
+      __syncthreads();
+    }
   }
   if (rc != KVCA_OK) {
     if (threadIdx.x == 0) plan_fail(counts, status, rc, nm);
@@ -1597,7 +1642,7 @@ __global__ void __launch_bounds__(1024)
       slot = allocated[mi + base];
       selected[i] = slot;
     }
-    if (i < k) move_slots[i] = slot;
+    if (i < k && (miss || !repeated)) move_slots[i] = slot;
     bool ev = false;
     int64_t prev = -1;
     if (i < k) {
@@ -1616,33 +1661,6 @@ __global__ void __launch_bounds__(1024)
       evict_slots[ne + ebase] = slot;
     }
     ne += etotal;
-  }
-  // Rows for the data scatter: an existing slot named more than once takes
-  // the row of its last occurrence (index_copy_ applied in order), so the
-  // earlier ones are dropped (-1).  Only when the first pass saw a repeat:
-  // every existing position compares its id with the later ones, staged
-  // through shared memory one 1024-id chunk at a time.
-  __syncthreads();
-  if (sh.repeated) {
-    for (int64_t tile = 0; tile < k; tile += blockDim.x) {
-      const int64_t i = tile + threadIdx.x;
-      const int64_t id = i < k ? ids[i] : -1;
-      const bool ex = i < k && l2p[id] >= 0;
-      bool later = false;
-      for (int64_t c = tile; c < k; c += blockDim.x) {
-        __syncthreads();
-        if (c + threadIdx.x < k) sh.ids[threadIdx.x] = ids[c + threadIdx.x];
-        __syncthreads();
-        const int64_t m = k - c < blockDim.x ? k - c : blockDim.x;
-        if (ex && !later)
-          for (int64_t j = 0; j < m; ++j)
-            if (c + j > i && sh.ids[j] == id) {
-              later = true;
-              break;
-            }
-      }
-      if (later) move_slots[i] = -1;
-    }
   }
   if (threadIdx.x == 0) {
     counts[0] = nx;
@@ -2579,7 +2597,7 @@ cudaError_t launch_plan_load(int meta_bits, int order, const int64_t* l2p, int64
                              int64_t* evict_ids, int64_t* evict_slots, int64_t* counts,
                              int64_t* status, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
-  KVCA_META_DISPATCH(meta_bits, plan_load_kernel<MetaT><<<1, 1024, 0, stream>>>(
+  KVCA_META_DISPATCH(meta_bits, plan_load_kernel<MetaT><<<1, kPlanThreads, 0, stream>>>(
                                     l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
                                     search_start, ids, count, bitmap, order, aligned, result,
                                     hit_slots, hit_pins, static_cast<MetaT*>(hit_usage), miss_ids,
@@ -2595,7 +2613,7 @@ cudaError_t launch_plan_save(int meta_bits, int order, const int64_t* l2p, int64
                              int64_t* evict_ids, int64_t* evict_slots, int64_t* counts,
                              int64_t* status, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
-  KVCA_META_DISPATCH(meta_bits, plan_save_kernel<MetaT><<<1, 1024, 0, stream>>>(
+  KVCA_META_DISPATCH(meta_bits, plan_save_kernel<MetaT><<<1, kPlanThreads, 0, stream>>>(
                                     l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots,
                                     search_start, ids, count, bitmap, order, aligned, selected,
                                     move_slots, static_cast<MetaT*>(final_pins),

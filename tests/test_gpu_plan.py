@@ -360,3 +360,23 @@ def test_load_that_spills_and_fills_one_id(host_tier):
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda
 
     kv_cache_adapter_cuda.check_status(DEV)
+
+
+def test_plan_save_repeats_across_tiles(ops):
+    """Every id resident and named many times across several 1,024-id tiles:
+    only the last occurrence of each keeps its slot for the data scatter, and
+    the blocked bitmap is left clear."""
+    n = 4096
+    l2p = torch.randperm(n, generator=torch.Generator().manual_seed(8))
+    p2l = torch.empty_like(l2p)
+    p2l[l2p] = torch.arange(n)
+    meta = torch.zeros(n, dtype=torch.uint8)
+    ids = torch.from_numpy(np.random.default_rng(9).choice(30, 5000).astype(np.int64))
+    ss = torch.zeros(1, dtype=torch.int64, device=DEV)
+    plan = ops.plan_save(l2p.to(DEV), p2l.to(DEV), meta.to(DEV), ss, ids.to(DEV))
+    sel = l2p[ids].tolist()
+    want = [s if s not in sel[i + 1:] else -1 for i, s in enumerate(sel)]
+    assert plan.move_slots.tolist() == want
+    assert plan.selected.tolist() == sel
+    assert int(ops._bitmap(DEV, n).count_nonzero()) == 0
+    ops.check_status(DEV)
