@@ -12,6 +12,7 @@ import pytest
 import torch
 
 import scenario_runner
+from kv_cache_adapter_b200 import adapter as adapter_mod
 
 pytestmark = pytest.mark.gpu
 
@@ -191,3 +192,63 @@ def test_program_transcript_on_cuda(api, golden_dir):
     ad.release(_ids([1, 2]))
     assert ad.load(_ids([2, 3])).tolist() == [0, 1]
     assert ad.debug_snapshot()["logical_to_physical"] == {2: 0, 3: 1}
+
+
+@pytest.mark.parametrize("path", ["planned", "stepwise", "device_store"])
+def test_save_materializes_cold_block_by_evicting_unpinned_resident(api, path):
+    """test_adapter.py:165-199 on CUDA, on each path (the operation log is
+    recorded, so compared, on the first two)."""
+    record = path != "device_store"
+    backend = api.InMemoryBlockStoreBackend({k: _payload(v) for k, v in {0: [0, 10], 1: [1, 11], 2: [2, 12]}.items()},
+                                            record_device_ops=record)
+    ad = make_adapter(api, backend=backend)
+    ad._planned = path != "stepwise"
+    updated, inserted = _payload([[100, 101]]), _payload([[200, 201]])
+    ad.load(_ids([0, 1]))
+    ad.save(_ids([0]), updated)
+    ad.release(_ids([0, 1]))
+    ad.save(_ids([2]), inserted)
+    snap = ad.debug_snapshot()
+    l2p = snap["logical_to_physical"]
+    assert 2 in l2p
+    evicted = {0, 1} - set(l2p)
+    assert len(evicted) == 1
+    if record:
+        assert backend.operation_log[-1] == ("save", next(iter(evicted)))
+    assert torch.equal(snap["actual_blocks"][l2p[2]], inserted[0].cpu())
+    if 0 in l2p:
+        assert torch.equal(snap["actual_blocks"][l2p[0]], updated[0].cpu())
+    else:
+        assert torch.equal(backend.snapshot()[0], updated[0].cpu())
+    ad.shutdown()
+
+
+@pytest.mark.parametrize("target_device", ["cuda", "cpu"])
+def test_host_tier_loads_into_target_slots_in_place(api, target_device):
+    """test_adapter.py:346-401 (LMCacheBackend, CPU and CUDA targets) against
+    the pinned host tier."""
+    backend = api.HostTierBackend(block_shape=(2,), block_dtype=torch.float32, num_logical_blocks=8,
+                                  model_name="kv-cache-adapter-test", max_local_cpu_size_gb=0.01, device=DEV)
+    target = torch.full((3, 2), -1.0, dtype=torch.float32, device=target_device)
+    backend.save_blocks(_ids([1, 3]), _payload([[10, 11], [30, 31]]))
+    backend.load_blocks(_ids([3, 1]), target, torch.tensor([0, 2], device=target_device))
+    torch.cuda.synchronize()
+    assert torch.equal(target.cpu(), torch.tensor([[30.0, 31.0], [-1.0, -1.0], [10.0, 11.0]]))
+    backend.shutdown()
+
+
+def test_host_tier_load_restores_flattened_merged_kv_payload(api):
+    """test_adapter.py:452-478: a row stored in LMCache's transfer layout comes
+    back as the merged block."""
+    block_shape = (2, 4, 2, 3)
+    layout = adapter_mod._MergedKVBlockLayout.detect(block_shape)
+    backend = api.HostTierBackend(block_shape=block_shape, block_dtype=torch.float32, num_logical_blocks=8,
+                                  max_local_cpu_size_gb=0.01, device=DEV)
+    payload = torch.arange(1, 1 + 2 * 4 * 2 * 3, dtype=torch.float32).view(block_shape)
+    flattened = layout.flatten_block_batch(payload.unsqueeze(0))[0].contiguous()
+    backend.save_blocks(_ids([7]), payload.unsqueeze(0).to(DEV))
+    assert torch.equal(backend.transfer_view(7), flattened)
+    actual = torch.zeros((1,) + block_shape, dtype=torch.float32, device=DEV)
+    backend.load_blocks(_ids([7]), actual, _ids([0]))
+    assert torch.equal(actual[0].cpu(), payload)
+    backend.shutdown()
