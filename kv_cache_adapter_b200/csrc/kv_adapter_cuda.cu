@@ -2150,13 +2150,17 @@ __global__ void __launch_bounds__(kMoverThreads) exchange_rows_kernel(const __gr
     for (int64_t b = v_begin + lane; b < v_end; b += static_cast<int64_t>(tpr) * kMoverUnroll) {
       V old_bytes[kMoverUnroll];
       V new_bytes[kMoverUnroll];
+      // the incoming row's loads (the long ones, over the host link for a
+      // host store) go out first, then the slot's
 #pragma unroll
       for (int u = 0; u < kMoverUnroll; ++u) {
         const int64_t i = b + static_cast<int64_t>(u) * tpr;
-        if (i < v_end) {
-          if (out_row >= 0) old_bytes[u] = slot[i];
-          if (in_row >= 0) new_bytes[u] = in[i];
-        }
+        if (i < v_end && in_row >= 0) new_bytes[u] = in[i];
+      }
+#pragma unroll
+      for (int u = 0; u < kMoverUnroll; ++u) {
+        const int64_t i = b + static_cast<int64_t>(u) * tpr;
+        if (i < v_end && out_row >= 0) old_bytes[u] = slot[i];
       }
 #pragma unroll
       for (int u = 0; u < kMoverUnroll; ++u) {
