@@ -156,3 +156,39 @@ def test_batched_stream_on_odd_grids(ops, ctas):
     assert np.array_equal(meta_d.cpu().numpy(), meta_h.numpy())
     assert int(ss_d[0]) == int(ss_h[0])
     ops.check_status(DEV)
+
+
+def test_batched_stream_replays_from_a_cuda_graph(ops):
+    """The cooperative launch (and its scratch clearing) can be captured in a
+    CUDA graph: a replay from the same start state gives the same stream."""
+    p = workloads.clock_params(65536, 500, 2, 3, seed=31)
+    meta0 = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta).to(DEV)
+    reacc = workloads.zipf_reaccess(p).to(DEV)
+    meta = meta0.clone()
+    ss = torch.zeros(1, dtype=torch.int64, device=DEV)
+    victims = torch.empty(p["num_steps"] * 2, dtype=torch.int64, device=DEV)
+    want, _ = ops.clock_stream(meta, ss, p["num_steps"], 2, reacc, 3, check=True)
+    want_meta, want_ss = meta.clone(), ss.clone()
+    meta.copy_(meta0)
+    ss.zero_()
+    ops.clock_stream(meta, ss, p["num_steps"], 2, reacc, 3, victims=victims)  # scratch and status exist now
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(DEV)
+    side.wait_stream(torch.cuda.current_stream(DEV))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        ops.clock_stream(meta, ss, p["num_steps"], 2, reacc, 3, victims=victims, check=False)  # warm this stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=side):
+            ops.clock_stream(meta, ss, p["num_steps"], 2, reacc, 3, victims=victims, check=False)
+    torch.cuda.current_stream(DEV).wait_stream(side)
+    for _ in range(2):
+        meta.copy_(meta0)
+        ss.zero_()
+        victims.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(victims, want)
+        assert torch.equal(meta, want_meta) and torch.equal(ss, want_ss)
+    del graph
+    ops.check_status(DEV)
