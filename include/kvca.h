@@ -375,6 +375,13 @@ int kvca_append_step(int meta_bits, int order, void* d_slot_meta, int64_t num_sl
                      int64_t* d_next_logical, int64_t* d_victims, int64_t* d_slot_mapping,
                      uint32_t* d_scratch_bitmap, int64_t* d_status, kvca_stream_t stream);
 
+/* Failure-detection self-test: one thread waits, with the bounded wait of
+ * the batched clock stream's grid barriers, for *d_flag to differ from
+ * `from`.  If it does not within about 0.3 s, d_status gets
+ * KVCA_ERR_DEVICE_TIMEOUT (value -1) and the kernel returns; the context
+ * stays usable.  No reference counterpart. */
+int kvca_wait_selftest(const uint32_t* d_flag, uint32_t from, int64_t* d_status, kvca_stream_t stream);
+
 /* 1 when [p, p + bytes) is pinned host memory that kernels can reach at the
  * same address, else 0.  No reference counterpart. */
 int kvca_host_memory_usable(const void* p, int64_t bytes);

@@ -137,6 +137,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_ptr],
     ),
     "kvca_host_memory_usable": (c_int, [c_ptr, c_i64]),
+    "kvca_wait_selftest": (c_int, [c_ptr, ctypes.c_uint32, c_ptr, c_ptr]),
     "kvca_append_step": (
         c_int,
         [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_i64,

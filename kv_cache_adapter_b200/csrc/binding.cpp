@@ -455,6 +455,11 @@ int kvca_append_step(int meta_bits, int order, void* d_slot_meta, int64_t num_sl
       d_scratch_bitmap, d_victims, d_slot_mapping, d_status, stream));
 }
 
+int kvca_wait_selftest(const uint32_t* d_flag, uint32_t from, int64_t* d_status, kvca_stream_t stream) {
+  if (!d_flag || !d_status) return KVCA_ERR_BAD_ARGUMENT;
+  return status_of(kvca::launch_wait_selftest(d_flag, from, d_status, stream));
+}
+
 int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t num_planes,
                 int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
                 kvca_stream_t stream) {

@@ -576,6 +576,18 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 
 constexpr uint32_t kGridSpinLimit = 1u << 22;  // about 0.3 s of 64 ns naps
 
+// Waits until *word differs from `from` (or *abort != 0); gives up after
+// about kGridSpinLimit naps.  Returns true when the word changed.
+__device__ bool bounded_wait_change(const unsigned* word, unsigned from, const int* abort) {
+  uint32_t spins = 0;
+  while (ld_acquire_u32(word) == from) {
+    if (++spins > kGridSpinLimit || (abort != nullptr && *reinterpret_cast<const volatile int*>(abort) != 0))
+      return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
 // Grid-wide barrier with a bounded wait.  Every CTA's writes before the
 // barrier are visible to every CTA after it.  A CTA that waits too long (or
 // sees another CTA give up) marks the grid failed, reports
@@ -593,14 +605,7 @@ __device__ bool grid_barrier(StreamGrid* g, int64_t* status) {
       __threadfence();
       atomicAdd(&g->bar_gen, 1u);
     } else {
-      uint32_t spins = 0;
-      while (ld_acquire_u32(&g->bar_gen) == gen) {
-        if (++spins > kGridSpinLimit || *reinterpret_cast<volatile int*>(&g->failed) != 0) {
-          ok = 0;
-          break;
-        }
-        __nanosleep(64);
-      }
+      ok = bounded_wait_change(&g->bar_gen, gen, &g->failed) ? 1 : 0;
     }
     __threadfence();
     if (!ok) {
@@ -2738,6 +2743,13 @@ cudaError_t launch_clock_stream(int meta_bits, int order, void* meta, int64_t nu
   return cudaGetLastError();
 }
 
+// The grid barrier's bounded wait on a word nothing may change: reports
+// KVCA_ERR_DEVICE_TIMEOUT (value -1) when *flag stays `from`.
+__global__ void wait_selftest_kernel(const unsigned* flag, unsigned from, int64_t* status) {
+  if (threadIdx.x == 0 && !bounded_wait_change(flag, from, nullptr))
+    report(status, KVCA_ERR_DEVICE_TIMEOUT, -1);
+}
+
 template <typename MetaT>
 cudaError_t launch_stream_grid(int grid, MetaT* meta, int64_t num_slots, int64_t* search_start,
                                int64_t num_steps, int64_t alloc_per_step, const int64_t* reaccess,
@@ -2768,6 +2780,12 @@ int stream_grid_size(int ctas) {
     return 1;
   const int sms = device_sm_count();
   return sms < 1 ? 1 : (sms < kStreamMaxCtas ? sms : kStreamMaxCtas);
+}
+
+cudaError_t launch_wait_selftest(const uint32_t* flag, uint32_t from, int64_t* status,
+                                 cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(flag, from, status);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_clock_stream_batched(int meta_bits, int order, void* meta, int64_t num_slots,

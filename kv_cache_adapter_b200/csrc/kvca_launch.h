@@ -165,4 +165,7 @@ cudaError_t launch_append_step(int meta_bits, int order, void* meta, int64_t num
                                uint32_t* bitmap, int64_t* victims, int64_t* slot_mapping,
                                int64_t* status, cudaStream_t stream);
 
+cudaError_t launch_wait_selftest(const uint32_t* flag, uint32_t from, int64_t* status,
+                                 cudaStream_t stream);
+
 }  // namespace kvca
