@@ -71,3 +71,44 @@ def test_two_rank_harness_logic():
         assert same is True and differs is False
         assert rc == 0 and done == 300
         assert tables_differ
+
+
+def _failing_worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    import bench
+
+    if rank == 1:
+        # this rank fails between steps: it never joins the next collective
+        results[rank] = "left"
+        os._exit(0)
+    t0 = __import__("time").perf_counter()
+    try:
+        bench._max_over_ranks(1.0, world, torch.device("cpu"))
+        results[rank] = "no error"
+    except Exception as exc:  # the surviving rank learns of it instead of hanging
+        results[rank] = (type(exc).__name__, __import__("time").perf_counter() - t0)
+    os._exit(0)
+
+
+@pytest.mark.timeout(300)
+def test_a_rank_that_leaves_surfaces_as_an_error_not_a_hang():
+    """A rank that exits between steps: the other rank's next collective (the
+    bench's max-over-ranks timing) ends with an error within the process
+    group's timeout."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, results)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=240)
+        assert pr.exitcode == 0
+    assert results[1] == "left"
+    name, waited = results[0]
+    assert name != "no error" and waited < 120
