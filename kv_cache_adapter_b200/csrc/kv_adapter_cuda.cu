@@ -1690,8 +1690,13 @@ __global__ void __launch_bounds__(1024)
 // release_metadata of those ops (adapter.py:472-525, :647-651, :309-336).
 // Ids are checked before anything changes; too few reusable slots change
 // nothing.
+// A small CTA: the step is a chain of short dependent phases, and block
+// barriers of 8 warps are cheaper than of 32 (decode mix, B200: 16.1 us per
+// decode step at 256 threads, 16.7 at 512, 18.5 at 1024, 16.3 at 128).
+constexpr int kAppendThreads = 256;
+
 template <typename MetaT>
-__global__ void __launch_bounds__(1024)
+__global__ void __launch_bounds__(kAppendThreads)
     append_step_kernel(MetaT* meta, int64_t n, int64_t* search_start, int64_t* l2p,
                        int64_t n_logical, int64_t* p2l, const int64_t* need, int64_t c,
                        int64_t* cur_block, int64_t* cur_logical, int64_t* pos, int64_t seqs,
@@ -2639,7 +2644,7 @@ cudaError_t launch_append_step(int meta_bits, int order, void* meta, int64_t num
                                uint32_t* bitmap, int64_t* victims, int64_t* slot_mapping,
                                int64_t* status, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
-  KVCA_META_DISPATCH(meta_bits, append_step_kernel<MetaT><<<1, 1024, 0, stream>>>(
+  KVCA_META_DISPATCH(meta_bits, append_step_kernel<MetaT><<<1, kAppendThreads, 0, stream>>>(
                                     static_cast<MetaT*>(meta), num_slots, search_start, l2p,
                                     num_logical, p2l, need, num_need, cur_block, cur_logical, pos,
                                     num_seqs, block_size, next_logical, bitmap, order, aligned,
