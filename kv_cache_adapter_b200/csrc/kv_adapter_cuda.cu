@@ -2059,6 +2059,89 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
   }
 }
 
+// Rows of at most kSmallRowMaxVecs 16-byte vectors (256 bytes): up to 8
+// lanes share a row, one or two vectors each, so that every load or store
+// instruction covers whole 128-byte lines of its rows, and each group of
+// lanes moves kSmallRowItems rows per iteration (all loads, then all stores)
+// to keep enough bytes in flight.  B200, random 256-byte token rows over 64
+// planes: gather / scatter 5.3 / 5.7 TB/s, against 4.9 / 4.5 with four lanes
+// of four vectors and one row at a time, where every instruction touches
+// half-lines of eight rows.  Same work items, row-offset reuse, index checks
+// and gate as move_rows_kernel; rows are never split into segments here.
+constexpr int kSmallRowItems = 4;
+constexpr int64_t kSmallRowMaxVecs = 16;
+
+template <bool kSrcPaged, bool kDstPaged>
+__global__ void __launch_bounds__(kMoverThreads) move_small_rows_kernel(const __grid_constant__ MoveParams p) {
+  if (p.gate != nullptr && *p.gate == 0) return;
+  const int tpr = 1 << p.tpr_log2;
+  const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int lane = static_cast<int>(gtid & (tpr - 1));
+  const int64_t group = gtid >> p.tpr_log2;
+  const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
+  const int64_t planes = p.num_planes;
+  const int64_t items = planes * p.num_rows;
+  const int64_t per = items / num_groups;
+  const int64_t rem = items - per * num_groups;
+  const int64_t begin = group * per + (group < rem ? group : rem);
+  const int64_t end = begin + per + (group < rem ? 1 : 0);
+  if (begin >= end) return;
+
+  int64_t r = begin / planes;
+  int64_t pl = begin - r * planes;
+  int64_t row_at = -1;
+  int64_t src_row = 0;
+  int64_t dst_row = 0;
+  const bool lead = lane == 0;
+  const int row_vecs = static_cast<int>(p.row_vecs);
+
+  for (int64_t g = begin; g < end; g += kSmallRowItems) {
+    const uint4* src[kSmallRowItems];
+    uint4* dst[kSmallRowItems];
+#pragma unroll
+    for (int u = 0; u < kSmallRowItems; ++u) {
+      src[u] = nullptr;
+      dst[u] = nullptr;
+      if (g + u < end) {
+        if (r != row_at) {
+          row_at = r;
+          src_row = kSrcPaged ? paged_row_offset(p.src_paged, r, p.flags, p.status, lead)
+                              : chunk_row_offset(p.src_chunk, r);
+          dst_row = kDstPaged ? paged_row_offset(p.dst_paged, r, p.flags, p.status, lead)
+                              : chunk_row_offset(p.dst_chunk, r);
+        }
+        if (src_row >= 0 && dst_row >= 0) {
+          src[u] = reinterpret_cast<const uint4*>(
+              kSrcPaged ? p.src_paged.planes[pl] + src_row
+                        : p.src_chunk.base + src_row + pl * p.src_chunk.plane_stride);
+          dst[u] = reinterpret_cast<uint4*>(
+              kDstPaged ? p.dst_paged.planes[pl] + dst_row
+                        : p.dst_chunk.base + dst_row + pl * p.dst_chunk.plane_stride);
+        }
+        if (++pl == planes) {
+          pl = 0;
+          ++r;
+        }
+      }
+    }
+    uint4 buf[kSmallRowItems][2];
+#pragma unroll
+    for (int u = 0; u < kSmallRowItems; ++u)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int i = lane + j * tpr;
+        if (src[u] != nullptr && i < row_vecs) buf[u][j] = ld_stream(src[u] + i);
+      }
+#pragma unroll
+    for (int u = 0; u < kSmallRowItems; ++u)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int i = lane + j * tpr;
+        if (dst[u] != nullptr && i < row_vecs) st_stream(dst[u] + i, buf[u][j]);
+      }
+  }
+}
+
 int device_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -2084,6 +2167,33 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
   const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
   if (blocks > resident) blocks = resident;
   if (kHost && blocks > kHostMoverCtas) blocks = kHostMoverCtas;
+  if (blocks < 1) blocks = 1;
+  kernel<<<static_cast<unsigned>(blocks), kMoverThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// Rows of 16-byte vectors, at most kSmallRowMaxVecs of them, in device
+// memory: 2^k lanes per row with 2^k >= the row's vectors, at most 8.
+template <bool kSrcPaged, bool kDstPaged>
+cudaError_t launch_move_small(MoveParams p, cudaStream_t stream) {
+  auto kernel = move_small_rows_kernel<kSrcPaged, kDstPaged>;
+  static int blocks_per_sm = 0;
+  if (blocks_per_sm == 0) {
+    int b = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kMoverThreads, 0);
+    if (e != cudaSuccess) return e;
+    blocks_per_sm = b > 0 ? b : 1;
+  }
+  p.tpr_log2 = 0;
+  while (p.tpr_log2 < 3 && (int64_t{1} << p.tpr_log2) < p.row_vecs) ++p.tpr_log2;
+  p.seg_vecs = p.row_vecs;
+  p.segs_per_row = 1;
+  const int sms = device_sm_count();
+  const int64_t items = p.num_planes * p.num_rows;
+  const int64_t threads_needed = ((items + kSmallRowItems - 1) / kSmallRowItems) << p.tpr_log2;
+  int64_t blocks = (threads_needed + kMoverThreads - 1) / kMoverThreads;
+  const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
+  if (blocks > resident) blocks = resident;
   if (blocks < 1) blocks = 1;
   kernel<<<static_cast<unsigned>(blocks), kMoverThreads, 0, stream>>>(p);
   return cudaGetLastError();
@@ -2409,6 +2519,7 @@ cudaError_t launch_move_vec(const MoveParams& p, int vec_bytes, cudaStream_t str
   switch (vec_bytes) {
     case 16:
       if (p.row_vecs * 16 >= kBulkMinRowBytes) return launch_move_bulk<kSrcPaged, kDstPaged>(p, stream);
+      if (p.row_vecs <= kSmallRowMaxVecs) return launch_move_small<kSrcPaged, kDstPaged>(p, stream);
       return launch_move_typed<kSrcPaged, kDstPaged, uint4>(p, stream);
     case 8: return launch_move_typed<kSrcPaged, kDstPaged, uint2>(p, stream);
     case 4: return launch_move_typed<kSrcPaged, kDstPaged, unsigned int>(p, stream);

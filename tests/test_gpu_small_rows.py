@@ -1,0 +1,148 @@
+"""GPU parity for rows of at most 256 bytes in 16-byte vectors, which take
+the small-row mover (up to 8 lanes per row, four rows per lane group and
+iteration), against the oracle's torch CPU indexing, byte for byte: every
+row width from 16 to 256 bytes, plane counts that make one iteration's rows
+straddle tokens, work ranges that end inside an iteration, padding tokens,
+out-of-range ids, and block-granular moves of small blocks."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moves
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as m
+
+    return m
+
+
+def _same(a: torch.Tensor, b: torch.Tensor) -> bool:
+    a = a.detach().contiguous().cpu().view(torch.uint8).numpy()
+    b = b.detach().contiguous().cpu().view(torch.uint8).numpy()
+    return a.shape == b.shape and np.array_equal(a, b)
+
+
+def _rand_bytes(shape, gen) -> torch.Tensor:
+    return torch.randint(0, 256, shape, generator=gen, dtype=torch.uint8)
+
+
+ROW_BYTES = [16, 32, 48, 64, 112, 128, 144, 240, 256]
+
+
+@pytest.mark.parametrize("row", ROW_BYTES)
+@pytest.mark.parametrize("planes", [1, 3, 7])
+def test_token_gather_scatter_small_rows(ops, row, planes):
+    gen = torch.Generator().manual_seed(row * 31 + planes)
+    nblk, bs = 29, 16
+    caches_h = [_rand_bytes((nblk, bs, row), gen) for _ in range(planes)]
+    caches_d = [c.to(DEV) for c in caches_h]
+    for t in (1, 2, 5, 61, 300):
+        tpc = t if t < 61 else (61 if t == 61 else 100)
+        mapping = torch.randperm(nblk * bs, generator=gen)[:t]
+        if t > 4:
+            mapping[torch.randperm(t, generator=gen)[: t // 5]] = -1
+        out = torch.zeros((t // tpc, planes, tpc, row), dtype=torch.uint8, device=DEV)
+        ops.gather_tokens(caches_d, mapping.to(DEV), out, tokens_per_chunk=tpc)
+        assert _same(out, moves.gather_tokens(caches_h, mapping, tokens_per_chunk=tpc)), t
+        src_h = _rand_bytes((t // tpc, planes, tpc, row), gen)
+        moves.scatter_tokens(caches_h, mapping, src_h, tokens_per_chunk=tpc)
+        ops.scatter_tokens(caches_d, mapping.to(DEV), src_h.to(DEV), tokens_per_chunk=tpc)
+        for a, b in zip(caches_d, caches_h):
+            assert _same(a, b), t
+
+
+@pytest.mark.parametrize("row", [32, 144, 256])
+def test_token_copy_small_rows(ops, row):
+    gen = torch.Generator().manual_seed(row)
+    src_h = [_rand_bytes((13, 8, row), gen) for _ in range(5)]
+    dst_h = [_rand_bytes((21, 4, row), gen) for _ in range(5)]
+    dst_d = [d.to(DEV) for d in dst_h]
+    t = 77
+    src_map = torch.randint(0, 13 * 8, (t,), generator=gen)
+    dst_map = torch.randperm(21 * 4, generator=gen)[:t]
+    src_map[3] = -1
+    dst_map[40] = -1
+    ops.copy_tokens([s.to(DEV) for s in src_h], src_map.to(DEV), dst_d, dst_map.to(DEV))
+    keep = (src_map >= 0) & (dst_map >= 0)
+    rows = moves.gather_tokens(src_h, src_map[keep])
+    moves.scatter_tokens(dst_h, dst_map[keep], rows)
+    for a, b in zip(dst_d, dst_h):
+        assert _same(a, b)
+
+
+@pytest.mark.parametrize("shape,dtype", [((128,), torch.float16), ((4, 16), torch.bfloat16),
+                                         ((3, 16), torch.float32), ((16,), torch.uint8)])
+def test_block_moves_small_rows(ops, shape, dtype):
+    """Whole blocks of 16 to 256 bytes (block-granular gather / scatter /
+    fused copy, the backend's index_select + index_copy_)."""
+    gen = torch.Generator().manual_seed(sum(shape))
+    m = 300
+    cache_h = _rand_bytes((m, *shape[:-1], shape[-1] * torch.empty((), dtype=dtype).element_size()), gen).view(dtype)
+    cache_d = cache_h.to(DEV)
+    for k in (1, 3, 4, 5, 255):
+        ids = torch.randint(0, m, (k,), generator=gen)
+        assert _same(ops.gather_blocks(cache_d, ids.to(DEV)), moves.gather_blocks(cache_h, ids))
+    ids = torch.randperm(m, generator=gen)[:203]
+    data = _rand_bytes((203, *cache_h.shape[1:-1], cache_h.shape[-1] * cache_h.element_size()), gen).view(dtype)
+    moves.scatter_blocks(cache_h, ids, data)
+    ops.scatter_blocks(cache_d, ids.to(DEV), data.to(DEV))
+    assert _same(cache_d, cache_h)
+    store_h = _rand_bytes(tuple(cache_h.shape[:-1]) + (cache_h.shape[-1] * cache_h.element_size(),), gen).view(dtype)
+    src = torch.randint(0, m, (97,), generator=gen)
+    dst = torch.randperm(m, generator=gen)[:97]
+    moves.copy_blocks(store_h, src, cache_h, dst)
+    ops.copy_blocks(store_h.to(DEV), src.to(DEV), cache_d, dst.to(DEV))
+    assert _same(cache_d, cache_h)
+
+
+def test_small_rows_out_of_range_raise_and_skip(ops):
+    cache = torch.arange(64 * 16, dtype=torch.int32, device=DEV).reshape(64, 16)  # 64-byte rows
+    before = cache.clone()
+    with pytest.raises(IndexError):
+        ops.scatter_blocks(cache, torch.tensor([3, 64, 5], device=DEV), torch.ones((3, 16), dtype=torch.int32, device=DEV))
+    want = before.clone()
+    want[3] = 1
+    want[5] = 1
+    assert torch.equal(cache, want)
+    planes = [cache.reshape(16, 4, 16)]
+    with pytest.raises(IndexError):
+        ops.gather_tokens(planes, torch.tensor([0, 1, 2, 3, 64], device=DEV))
+    got = torch.full((1, 1, 5, 16), -7, dtype=torch.int32, device=DEV)
+    ops.gather_tokens(planes, torch.tensor([0, -1, 63, -1, 7], device=DEV), got)
+    assert torch.equal(got[0, 0, 2], planes[0][15, 3]) and torch.equal(got[0, 0, 4], planes[0][1, 3])
+    assert bool((got[0, 0, 1] == -7).all()) and bool((got[0, 0, 3] == -7).all())  # padding untouched
+
+
+def test_small_rows_large_random_round_trip(ops):
+    """256-byte rows over 64 planes, 32,768 tokens (one KV head of a 70B-shaped
+    cache, fp16): gather through a random slot mapping, scatter into zeroed
+    planes, gather again; three planes checked byte for byte against the
+    oracle, all of them by the round trip on the device."""
+    gen = torch.Generator().manual_seed(5)
+    nblk, bs, P = 4096, 16, 64
+    base = torch.randint(-30000, 30000, (P, nblk, bs, 128), generator=gen, dtype=torch.int16).to(DEV)
+    caches = [base[p] for p in range(P)]
+    t = 32768
+    mapping_h = torch.randperm(nblk * bs, generator=gen)[:t]
+    mapping = mapping_h.to(DEV)
+    chunks = ops.gather_tokens(caches, mapping, tokens_per_chunk=256)
+    for p in (0, 17, 63):
+        want = moves.gather_tokens([base[p].cpu()], mapping_h, tokens_per_chunk=256)
+        assert _same(chunks[:, p:p + 1], want)
+    fresh = torch.zeros_like(base)
+    ops.scatter_tokens([fresh[p] for p in range(P)], mapping, chunks, tokens_per_chunk=256)
+    flat = mapping.view(-1)
+    assert torch.equal(fresh.view(P, -1, 128)[:, flat], base.view(P, -1, 128)[:, flat])
+    untouched = torch.ones(nblk * bs, dtype=torch.bool, device=DEV)
+    untouched[flat] = False
+    assert int(fresh.view(P, -1, 128)[:, untouched].abs().sum()) == 0
+    again = ops.gather_tokens([fresh[p] for p in range(P)], mapping, tokens_per_chunk=256)
+    assert torch.equal(again, chunks)
