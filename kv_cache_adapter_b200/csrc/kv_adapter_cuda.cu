@@ -2059,20 +2059,23 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
   }
 }
 
-// Rows of at most kSmallRowMaxVecs 16-byte vectors (256 bytes): up to 8
-// lanes share a row, one or two vectors each, so that every load or store
-// instruction covers whole 128-byte lines of its rows, and each group of
-// lanes moves kSmallRowItems rows per iteration (all loads, then all stores)
-// to keep enough bytes in flight.  B200, random 256-byte token rows over 64
-// planes: gather / scatter 5.3 / 5.7 TB/s, against 4.9 / 4.5 with four lanes
-// of four vectors and one row at a time, where every instruction touches
-// half-lines of eight rows.  Same work items, row-offset reuse, index checks
-// and gate as move_rows_kernel; rows are never split into segments here.
-constexpr int kSmallRowItems = 4;
+// Short rows of 16-byte vectors, several rows per lane group and iteration:
+// 2^k lanes share a row, kVpl vectors each, so that every load or store
+// instruction covers whole 128-byte lines of its rows, and each group moves
+// kRows rows per iteration (all loads, then all stores) to keep enough bytes
+// in flight.  Two shapes:
+//   rows <= 256 B: at most 8 lanes, 2 vectors each, 4 rows per iteration;
+//   rows <= 1.5 KiB: 32 lanes, 3 vectors each, 2 rows per iteration.
+// B200, random token rows: 256 B (64 planes) gather / scatter 5.6 / 5.7 TB/s
+// against 4.9 / 4.7 with four lanes of four vectors and one row at a time,
+// where every instruction touches half-lines of eight rows.  Same work
+// items, row-offset reuse, index checks and gate as move_rows_kernel; rows
+// are never split into segments here.
 constexpr int64_t kSmallRowMaxVecs = 16;
+constexpr int64_t kShortRowMaxVecs = 96;
 
-template <bool kSrcPaged, bool kDstPaged>
-__global__ void __launch_bounds__(kMoverThreads) move_small_rows_kernel(const __grid_constant__ MoveParams p) {
+template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
+__global__ void __launch_bounds__(kMoverThreads) move_short_rows_kernel(const __grid_constant__ MoveParams p) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int tpr = 1 << p.tpr_log2;
   const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -2095,11 +2098,11 @@ __global__ void __launch_bounds__(kMoverThreads) move_small_rows_kernel(const __
   const bool lead = lane == 0;
   const int row_vecs = static_cast<int>(p.row_vecs);
 
-  for (int64_t g = begin; g < end; g += kSmallRowItems) {
-    const uint4* src[kSmallRowItems];
-    uint4* dst[kSmallRowItems];
+  for (int64_t g = begin; g < end; g += kRows) {
+    const uint4* src[kRows];
+    uint4* dst[kRows];
 #pragma unroll
-    for (int u = 0; u < kSmallRowItems; ++u) {
+    for (int u = 0; u < kRows; ++u) {
       src[u] = nullptr;
       dst[u] = nullptr;
       if (g + u < end) {
@@ -2124,18 +2127,18 @@ __global__ void __launch_bounds__(kMoverThreads) move_small_rows_kernel(const __
         }
       }
     }
-    uint4 buf[kSmallRowItems][2];
+    uint4 buf[kRows][kVpl];
 #pragma unroll
-    for (int u = 0; u < kSmallRowItems; ++u)
+    for (int u = 0; u < kRows; ++u)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kVpl; ++j) {
         const int i = lane + j * tpr;
         if (src[u] != nullptr && i < row_vecs) buf[u][j] = ld_stream(src[u] + i);
       }
 #pragma unroll
-    for (int u = 0; u < kSmallRowItems; ++u)
+    for (int u = 0; u < kRows; ++u)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kVpl; ++j) {
         const int i = lane + j * tpr;
         if (dst[u] != nullptr && i < row_vecs) st_stream(dst[u] + i, buf[u][j]);
       }
@@ -2172,11 +2175,11 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-// Rows of 16-byte vectors, at most kSmallRowMaxVecs of them, in device
-// memory: 2^k lanes per row with 2^k >= the row's vectors, at most 8.
-template <bool kSrcPaged, bool kDstPaged>
-cudaError_t launch_move_small(MoveParams p, cudaStream_t stream) {
-  auto kernel = move_small_rows_kernel<kSrcPaged, kDstPaged>;
+// Rows of 16-byte vectors in device memory, at most kShortRowMaxVecs of
+// them: the shape of move_short_rows_kernel for the row length.
+template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
+cudaError_t launch_move_short_typed(MoveParams p, cudaStream_t stream) {
+  auto kernel = move_short_rows_kernel<kSrcPaged, kDstPaged, kVpl, kRows>;
   static int blocks_per_sm = 0;
   if (blocks_per_sm == 0) {
     int b = 0;
@@ -2184,19 +2187,28 @@ cudaError_t launch_move_small(MoveParams p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     blocks_per_sm = b > 0 ? b : 1;
   }
-  p.tpr_log2 = 0;
-  while (p.tpr_log2 < 3 && (int64_t{1} << p.tpr_log2) < p.row_vecs) ++p.tpr_log2;
   p.seg_vecs = p.row_vecs;
   p.segs_per_row = 1;
   const int sms = device_sm_count();
   const int64_t items = p.num_planes * p.num_rows;
-  const int64_t threads_needed = ((items + kSmallRowItems - 1) / kSmallRowItems) << p.tpr_log2;
+  const int64_t threads_needed = ((items + kRows - 1) / kRows) << p.tpr_log2;
   int64_t blocks = (threads_needed + kMoverThreads - 1) / kMoverThreads;
   const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
   if (blocks > resident) blocks = resident;
   if (blocks < 1) blocks = 1;
   kernel<<<static_cast<unsigned>(blocks), kMoverThreads, 0, stream>>>(p);
   return cudaGetLastError();
+}
+
+template <bool kSrcPaged, bool kDstPaged>
+cudaError_t launch_move_short(MoveParams p, cudaStream_t stream) {
+  if (p.row_vecs <= kSmallRowMaxVecs) {  // 2^k >= the row's vectors lanes, at most 8
+    p.tpr_log2 = 0;
+    while (p.tpr_log2 < 3 && (int64_t{1} << p.tpr_log2) < p.row_vecs) ++p.tpr_log2;
+    return launch_move_short_typed<kSrcPaged, kDstPaged, 2, 4>(p, stream);
+  }
+  p.tpr_log2 = 5;
+  return launch_move_short_typed<kSrcPaged, kDstPaged, 3, 2>(p, stream);
 }
 
 
@@ -2519,7 +2531,7 @@ cudaError_t launch_move_vec(const MoveParams& p, int vec_bytes, cudaStream_t str
   switch (vec_bytes) {
     case 16:
       if (p.row_vecs * 16 >= kBulkMinRowBytes) return launch_move_bulk<kSrcPaged, kDstPaged>(p, stream);
-      if (p.row_vecs <= kSmallRowMaxVecs) return launch_move_small<kSrcPaged, kDstPaged>(p, stream);
+      if (p.row_vecs <= kShortRowMaxVecs) return launch_move_short<kSrcPaged, kDstPaged>(p, stream);
       return launch_move_typed<kSrcPaged, kDstPaged, uint4>(p, stream);
     case 8: return launch_move_typed<kSrcPaged, kDstPaged, uint2>(p, stream);
     case 4: return launch_move_typed<kSrcPaged, kDstPaged, unsigned int>(p, stream);

@@ -1,9 +1,10 @@
-"""GPU parity for rows of at most 256 bytes in 16-byte vectors, which take
-the small-row mover (up to 8 lanes per row, four rows per lane group and
-iteration), against the oracle's torch CPU indexing, byte for byte: every
-row width from 16 to 256 bytes, plane counts that make one iteration's rows
+"""GPU parity for rows of at most 1.5 KiB in 16-byte vectors, which take the
+short-row mover (up to 8 lanes and four rows per lane group and iteration
+for rows up to 256 bytes, 32 lanes and two rows above), against the
+oracle's torch CPU indexing, byte for byte: row widths from 16 bytes to
+1.5 KiB and just past it, plane counts that make one iteration's rows
 straddle tokens, work ranges that end inside an iteration, padding tokens,
-out-of-range ids, and block-granular moves of small blocks."""
+out-of-range ids, and block-granular moves of short blocks."""
 from __future__ import annotations
 
 import numpy as np
@@ -34,12 +35,12 @@ def _rand_bytes(shape, gen) -> torch.Tensor:
     return torch.randint(0, 256, shape, generator=gen, dtype=torch.uint8)
 
 
-ROW_BYTES = [16, 32, 48, 64, 112, 128, 144, 240, 256]
+ROW_BYTES = [16, 32, 48, 64, 112, 128, 144, 240, 256, 272, 512, 576, 1040, 1152, 1536, 1552]
 
 
 @pytest.mark.parametrize("row", ROW_BYTES)
 @pytest.mark.parametrize("planes", [1, 3, 7])
-def test_token_gather_scatter_small_rows(ops, row, planes):
+def test_token_gather_scatter_short_rows(ops, row, planes):
     gen = torch.Generator().manual_seed(row * 31 + planes)
     nblk, bs = 29, 16
     caches_h = [_rand_bytes((nblk, bs, row), gen) for _ in range(planes)]
@@ -59,8 +60,8 @@ def test_token_gather_scatter_small_rows(ops, row, planes):
             assert _same(a, b), t
 
 
-@pytest.mark.parametrize("row", [32, 144, 256])
-def test_token_copy_small_rows(ops, row):
+@pytest.mark.parametrize("row", [32, 144, 256, 576, 1536])
+def test_token_copy_short_rows(ops, row):
     gen = torch.Generator().manual_seed(row)
     src_h = [_rand_bytes((13, 8, row), gen) for _ in range(5)]
     dst_h = [_rand_bytes((21, 4, row), gen) for _ in range(5)]
@@ -79,9 +80,11 @@ def test_token_copy_small_rows(ops, row):
 
 
 @pytest.mark.parametrize("shape,dtype", [((128,), torch.float16), ((4, 16), torch.bfloat16),
-                                         ((3, 16), torch.float32), ((16,), torch.uint8)])
-def test_block_moves_small_rows(ops, shape, dtype):
-    """Whole blocks of 16 to 256 bytes (block-granular gather / scatter /
+                                         ((3, 16), torch.float32), ((16,), torch.uint8),
+                                         ((2, 4, 32), torch.float16), ((9, 64), torch.uint8),
+                                         ((16, 24), torch.float32)])
+def test_block_moves_short_rows(ops, shape, dtype):
+    """Whole blocks of 16 bytes to 1.5 KiB (block-granular gather / scatter /
     fused copy, the backend's index_select + index_copy_)."""
     gen = torch.Generator().manual_seed(sum(shape))
     m = 300
@@ -103,7 +106,7 @@ def test_block_moves_small_rows(ops, shape, dtype):
     assert _same(cache_d, cache_h)
 
 
-def test_small_rows_out_of_range_raise_and_skip(ops):
+def test_short_rows_out_of_range_raise_and_skip(ops):
     cache = torch.arange(64 * 16, dtype=torch.int32, device=DEV).reshape(64, 16)  # 64-byte rows
     before = cache.clone()
     with pytest.raises(IndexError):
@@ -121,28 +124,29 @@ def test_small_rows_out_of_range_raise_and_skip(ops):
     assert bool((got[0, 0, 1] == -7).all()) and bool((got[0, 0, 3] == -7).all())  # padding untouched
 
 
-def test_small_rows_large_random_round_trip(ops):
-    """256-byte rows over 64 planes, 32,768 tokens (one KV head of a 70B-shaped
-    cache, fp16): gather through a random slot mapping, scatter into zeroed
-    planes, gather again; three planes checked byte for byte against the
-    oracle, all of them by the round trip on the device."""
-    gen = torch.Generator().manual_seed(5)
-    nblk, bs, P = 4096, 16, 64
-    base = torch.randint(-30000, 30000, (P, nblk, bs, 128), generator=gen, dtype=torch.int16).to(DEV)
+@pytest.mark.parametrize("row,P,nblk,bs", [(128, 64, 4096, 16), (288, 8, 4096, 64)])
+def test_short_rows_large_random_round_trip(ops, row, P, nblk, bs):
+    """256-byte rows over 64 planes (one KV head of a 70B-shaped cache, fp16)
+    and 576-byte rows over 8 planes (an fp8 MLA latent), half of all token
+    slots through a random slot mapping: gather, scatter into zeroed planes,
+    gather again; three planes checked byte for byte against the oracle, all
+    of them by the round trip on the device."""
+    gen = torch.Generator().manual_seed(5 + row)
+    base = torch.randint(-30000, 30000, (P, nblk, bs, row), generator=gen, dtype=torch.int16).to(DEV)
     caches = [base[p] for p in range(P)]
-    t = 32768
+    t = nblk * bs // 2
     mapping_h = torch.randperm(nblk * bs, generator=gen)[:t]
     mapping = mapping_h.to(DEV)
     chunks = ops.gather_tokens(caches, mapping, tokens_per_chunk=256)
-    for p in (0, 17, 63):
+    for p in (0, P // 3, P - 1):
         want = moves.gather_tokens([base[p].cpu()], mapping_h, tokens_per_chunk=256)
         assert _same(chunks[:, p:p + 1], want)
     fresh = torch.zeros_like(base)
     ops.scatter_tokens([fresh[p] for p in range(P)], mapping, chunks, tokens_per_chunk=256)
     flat = mapping.view(-1)
-    assert torch.equal(fresh.view(P, -1, 128)[:, flat], base.view(P, -1, 128)[:, flat])
+    assert torch.equal(fresh.view(P, -1, row)[:, flat], base.view(P, -1, row)[:, flat])
     untouched = torch.ones(nblk * bs, dtype=torch.bool, device=DEV)
     untouched[flat] = False
-    assert int(fresh.view(P, -1, 128)[:, untouched].abs().sum()) == 0
+    assert int(fresh.view(P, -1, row)[:, untouched].abs().sum()) == 0
     again = ops.gather_tokens([fresh[p] for p in range(P)], mapping, tokens_per_chunk=256)
     assert torch.equal(again, chunks)
