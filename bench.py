@@ -48,6 +48,12 @@ WORKLOADS = {
                     seqs=64, seq_tokens=256, chunk_tokens=256,
                     label="Llama-3-8B cache: 32 layers x K/V, 8 KV heads, head_dim 128, block 16, fp16, "
                           "1024 blocks/layer, 64 requests x 256 tokens"),
+    "llama70b-shard-tokens": dict(layers=80, kv=2, heads=1, head_dim=128, block_size=16, dtype=torch.bfloat16,
+                                  seqs=16, seq_tokens=32768, chunk_tokens=256, tokens=True,
+                                  label="Llama-3-70B KV-head shard, token-granular: 80 layers x K/V, 1 KV head/GPU, "
+                                        "head_dim 128, block 16, bf16, 16 x 32k-token sequences (524,288 tokens/GPU), "
+                                        "slot_mapping = block table x 16 + offset, 256-byte token rows, "
+                                        "256-token chunks"),
     "mla-layer-shard": dict(layers=8, kv=1, heads=1, head_dim=576, block_size=64, dtype=torch.bfloat16,
                             seqs=1, seq_tokens=131072, chunk_tokens=256,
                             label="MLA latent cache, one GPU's layer range (8 of 61 layers): one 576-wide "
@@ -212,6 +218,13 @@ def _dtype_name(dt) -> str:
     return {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float8_e4m3fn: "fp8-e4m3 (bytes)"}.get(dt, str(dt))
 
 
+def slot_mapping_of(table: torch.Tensor, block_size: int) -> torch.Tensor:
+    """Token slots of the blocks of ``table`` in order: block * block_size +
+    offset (the slot_mapping of a request whose block table is ``table``)."""
+    offsets = torch.arange(block_size, dtype=torch.int64, device=table.device)
+    return (table.view(-1, 1) * block_size + offsets.view(1, -1)).reshape(-1)
+
+
 def block_bytes(w: dict) -> int:
     return w["block_size"] * w["heads"] * w["head_dim"] * torch.empty(0, dtype=w["dtype"]).element_size()
 
@@ -231,18 +244,27 @@ def cpu_moves(w: dict, steps: int, warmup: int) -> dict:
     _, planes, table, nb = build_cache(w, torch.device("cpu"), 1234, num_blocks=nb)
     planes = [p.view(torch.uint8) if p.dtype == torch.float8_e4m3fn else p for p in planes]
     payload = len(planes) * nb * block_bytes(w)
+    tokens = bool(w.get("tokens"))
+    if tokens:
+        mapping = slot_mapping_of(table, w["block_size"])
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
-        chunks = moves.gather_layers(planes, table, blocks_per_chunk=cb)
-        moves.scatter_layers(planes, table, chunks, blocks_per_chunk=cb)
+        if tokens:
+            chunks = moves.gather_tokens(planes, mapping, tokens_per_chunk=w["chunk_tokens"])
+            moves.scatter_tokens(planes, mapping, chunks, tokens_per_chunk=w["chunk_tokens"])
+        else:
+            chunks = moves.gather_layers(planes, table, blocks_per_chunk=cb)
+            moves.scatter_layers(planes, table, chunks, blocks_per_chunk=cb)
         t1 = time.perf_counter()
         if i >= warmup:
             times.append(t1 - t0)
     gbs = 4 * payload * len(times) / sum(times) / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{len(planes)} planes x {nb} blocks ({payload / 1e9:.2f} GB of the cache) per step, "
-                      f"{len(times)} steps: per-plane index_select + index_copy_ on CPU tensors"}
+                      f"{len(times)} steps: per-plane "
+                      + ("token-row indexing through the slot mapping" if tokens else "index_select + index_copy_")
+                      + " on CPU tensors"}
 
 
 def cpu_clock(k: int) -> dict:
@@ -308,14 +330,36 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     P = len(planes)
     bbytes = block_bytes(w)
     payload = P * nb * bbytes  # bytes of cache moved by one gather (and by one scatter)
-    chunks = torch.empty((nb // cb, P, cb, w["block_size"], w["heads"], w["head_dim"]), dtype=w["dtype"],
-                         device=device)
+    tokens = bool(w.get("tokens"))
+    if tokens:  # token-granular: one row per token and plane (256 bytes here), through a slot mapping
+        tpc = w["chunk_tokens"]
+        index_h = slot_mapping_of(table_h, w["block_size"])
+        chunks = torch.empty((nb * w["block_size"] // tpc, P, tpc, w["heads"], w["head_dim"]), dtype=w["dtype"],
+                             device=device)
+        ptab = ops.PlaneTable(planes, 2)
+
+        def gather(idx):
+            ops.gather_tokens(ptab, idx, chunks, tokens_per_chunk=tpc, check=False)
+
+        def scatter(idx):
+            ops.scatter_tokens(ptab, idx, chunks, tokens_per_chunk=tpc, check=False)
+    else:
+        index_h = table_h
+        chunks = torch.empty((nb // cb, P, cb, w["block_size"], w["heads"], w["head_dim"]), dtype=w["dtype"],
+                             device=device)
+        ptab = ops.PlaneTable(planes, 1)
+
+        def gather(idx):
+            ops.gather_layers(ptab, idx, chunks, blocks_per_chunk=cb, check=False)
+
+        def scatter(idx):
+            ops.scatter_layers(ptab, idx, chunks, blocks_per_chunk=cb, check=False)
     table = table_h.to(device)
-    ptab = ops.PlaneTable(planes, 1)
+    index = index_h.to(device)
 
     def step():
-        ops.gather_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
-        ops.scatter_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
+        gather(index)
+        scatter(index)
 
     for _ in range(args.warmup):
         step()
@@ -325,7 +369,8 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     # correctness guard on the bench data: chunk 0 holds the first cb blocks
     # of the table for plane 0 and the last plane
     for p in (0, P - 1):
-        assert torch.equal(chunks[0, p].view(torch.uint8), planes[p][table[:cb]].view(torch.uint8))
+        assert torch.equal(chunks[0, p].reshape(-1).view(torch.uint8),
+                           planes[p][table[:cb]].reshape(-1).view(torch.uint8))
 
     # ---- device-timed region ------------------------------------------------
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
@@ -338,9 +383,9 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
         start.record()
         for g0, g1, s1 in events:
             g0.record()
-            ops.gather_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
+            gather(index)
             g1.record()
-            ops.scatter_layers(ptab, table, chunks, blocks_per_chunk=cb, check=False)
+            scatter(index)
             s1.record()
         end.record()
         torch.cuda.synchronize(device)
@@ -351,8 +396,8 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     avg_launch_ms = _max_over_ranks(sum(launch_ms) / len(launch_ms), world, device)
 
     # ---- end-to-end through the public API with host buffers ------------------
-    table_pinned = table_h.clone().pin_memory()
-    table_dev = torch.empty_like(table)
+    index_pinned = index_h.clone().pin_memory()
+    index_dev = torch.empty_like(index)
     _barrier(world)
     torch.cuda.synchronize(device)
     # every step copies its inputs host -> device and its status word device ->
@@ -362,9 +407,9 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     word = ops.status_word(device)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        table_dev.copy_(table_pinned, non_blocking=True)
-        ops.gather_layers(ptab, table_dev, chunks, blocks_per_chunk=cb, check=False)
-        ops.scatter_layers(ptab, table_dev, chunks, blocks_per_chunk=cb, check=False)
+        index_dev.copy_(index_pinned, non_blocking=True)
+        gather(index_dev)
+        scatter(index_dev)
         status_host[i % 2].copy_(word, non_blocking=True)
         done[i % 2].record()
         if i > 0:
@@ -410,6 +455,7 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
             "block_bytes_per_plane": bbytes,
             "cache_bytes_per_gpu": payload,
             "chunk_layout": "KV_2LTD per 256-token chunk",
+            "granularity": "token rows through a slot mapping" if tokens else "blocks through a block table",
             "l2": "inputs larger than L2 (cache and chunks are each > 126 MB)",
             "parallelism": f"kv-head shard x{world}, no data-path collective",
         },
@@ -423,16 +469,19 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
             "frac": round(achieved / peak, 4),
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
             "traffic": traffic,
-            "kernel": "move_rows_bulk_kernel (gather and scatter launches; TMA bulk copies)",
+            "kernel": ("move_short_rows_pm_kernel (gather and scatter launches; 8 lanes x 2 vectors per 256-byte "
+                       "row, 4 rows per lane group and iteration, plane-major)" if tokens else
+                       "move_rows_bulk_kernel (gather and scatter launches; TMA bulk copies)"),
             "algorithmic_bytes_per_launch": 2 * payload,
             "avg_launch_ms": round(avg_launch_ms, 4),
         },
         "e2e": {
             "value": round(world * algo_per_step * args.steps / e2e_s / 1e9, 2),
             "unit": "GB/s",
-            "h2d_bytes_per_step": table_h.numel() * 8,
+            "h2d_bytes_per_step": index_h.numel() * 8,
             "d2h_bytes_per_step": 16,
-            "api": "kv_cache_adapter_cuda.gather_layers / scatter_layers (ctypes -> C ABI)",
+            "api": ("kv_cache_adapter_cuda.gather_tokens / scatter_tokens" if tokens else
+                    "kv_cache_adapter_cuda.gather_layers / scatter_layers") + " (ctypes -> C ABI)",
             "pipelining": "each step's status word is copied to pinned host memory and read by the host "
                           "while the next step runs (one step of lag); the last one after the loop",
         },

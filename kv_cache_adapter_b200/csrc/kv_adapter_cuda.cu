@@ -2064,13 +2064,16 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
 // instruction covers whole 128-byte lines of its rows, and each group moves
 // kRows rows per iteration (all loads, then all stores) to keep enough bytes
 // in flight.  Two shapes:
-//   rows <= 256 B: at most 8 lanes, 2 vectors each, 4 rows per iteration;
-//   rows <= 1.5 KiB: 32 lanes, 3 vectors each, 2 rows per iteration.
-// B200, random token rows: 256 B (64 planes) gather / scatter 5.6 / 5.7 TB/s
+//   rows <= 256 B: at most 8 lanes, 2 vectors each, 4 rows per iteration,
+//     in plane-major order (move_short_rows_pm_kernel);
+//   rows <= 1.5 KiB: 32 lanes, 3 vectors each, 2 rows per iteration, in
+//     row-major order (this kernel: one index load and offset per row,
+//     reused across the planes).
+// B200, random token rows: 256 B (64 planes) gather / scatter 5.7 / 5.7 TB/s
 // against 4.9 / 4.7 with four lanes of four vectors and one row at a time,
-// where every instruction touches half-lines of eight rows.  Same work
-// items, row-offset reuse, index checks and gate as move_rows_kernel; rows
-// are never split into segments here.
+// where every instruction touches half-lines of eight rows; 576 B (8 planes)
+// 5.2 / 5.0 against 4.6 / 4.4.  Same work items, row-offset reuse, index
+// checks and gate as move_rows_kernel; rows are never split into segments.
 constexpr int64_t kSmallRowMaxVecs = 16;
 constexpr int64_t kShortRowMaxVecs = 96;
 
@@ -2145,6 +2148,143 @@ __global__ void __launch_bounds__(kMoverThreads) move_short_rows_kernel(const __
   }
 }
 
+// Offset of slot id idx on a paged side (shift = log2 of the block size when
+// that is a power of two, else -1), or -1 when the row is skipped; the same
+// checks and reports as paged_row_offset.
+__device__ __forceinline__ int64_t paged_slot_offset(const PagedSide& side, int64_t idx, int shift,
+                                                     int32_t flags, int64_t* status, bool lead) {
+  if (idx < 0) {
+    if (!(flags & KVCA_FLAG_SKIP_NEGATIVE) && lead) report(status, KVCA_ERR_BAD_INDEX, idx);
+    return -1;
+  }
+  int64_t blk;
+  int64_t off;
+  if (shift >= 0) {
+    blk = idx >> shift;
+    off = idx & ((int64_t{1} << shift) - 1);
+  } else {
+    blk = idx / side.block_size;
+    off = idx - blk * side.block_size;
+  }
+  if (blk >= side.num_blocks) {
+    if (lead) report(status, KVCA_ERR_BAD_INDEX, idx);
+    return -1;
+  }
+  return blk * side.block_stride + off * side.row_stride;
+}
+
+__device__ __forceinline__ int pow2_shift(int64_t v) {
+  return v > 0 && (v & (v - 1)) == 0 ? __ffsll(static_cast<long long>(v)) - 1 : -1;
+}
+
+// Plane-major order of the same work: item g = plane * num_rows + row, so a
+// lane group walks consecutive rows of one plane, which are consecutive
+// rows of a chunk and, for slot mappings made from block tables, runs of
+// consecutive rows of a block.  Every item loads its own index; power-of-two
+// block sizes divide by shifting, and the chunk position advances by
+// counting instead of dividing.  Used for rows of at most 256 bytes, where
+// four lane groups share a warp's instruction stream (B200, 256-byte token
+// rows through a block-table slot mapping, 160 planes: 6.05 TB/s against
+// 5.81 in row-major order).  With one group per warp (32-lane rows) the
+// per-item index arithmetic makes it issue-bound (576-byte rows: 3.7 TB/s
+// against 5.2), so longer rows stay row-major.
+template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
+__global__ void __launch_bounds__(kMoverThreads) move_short_rows_pm_kernel(const __grid_constant__ MoveParams p) {
+  if (p.gate != nullptr && *p.gate == 0) return;
+  const int tpr = 1 << p.tpr_log2;
+  const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int lane = static_cast<int>(gtid & (tpr - 1));
+  const int64_t group = gtid >> p.tpr_log2;
+  const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
+  const int64_t rows = p.num_rows;
+  const int64_t items = p.num_planes * rows;
+  const int64_t per = items / num_groups;
+  const int64_t rem = items - per * num_groups;
+  const int64_t begin = group * per + (group < rem ? group : rem);
+  const int64_t end = begin + per + (group < rem ? 1 : 0);
+  if (begin >= end) return;
+
+  constexpr bool kChunk = !(kSrcPaged && kDstPaged);
+  const ChunkSide& cs = kSrcPaged ? p.dst_chunk : p.src_chunk;  // the chunk side, when there is one
+  int64_t pl = begin / rows;
+  int64_t r = begin - pl * rows;
+  int64_t c = 0;
+  int64_t cr = 0;
+  if (kChunk) {
+    c = r / cs.rows_per_chunk;
+    cr = r - c * cs.rows_per_chunk;
+  }
+  const int s_shift = kSrcPaged ? pow2_shift(p.src_paged.block_size) : 0;
+  const int d_shift = kDstPaged ? pow2_shift(p.dst_paged.block_size) : 0;
+  const bool lead = lane == 0;
+  const int row_vecs = static_cast<int>(p.row_vecs);
+
+  for (int64_t g = begin; g < end; g += kRows) {
+    int64_t row[kRows];
+    int64_t plane[kRows];
+    int64_t coff[kRows];
+#pragma unroll
+    for (int u = 0; u < kRows; ++u) {
+      row[u] = r;
+      plane[u] = pl;
+      coff[u] = kChunk ? c * cs.chunk_stride + cr * cs.row_stride + pl * cs.plane_stride : 0;
+      if (++r == rows) {
+        r = 0;
+        ++pl;
+        c = 0;
+        cr = 0;
+      } else if (kChunk && ++cr == cs.rows_per_chunk) {
+        cr = 0;
+        ++c;
+      }
+    }
+    int64_t sidx[kRows];
+    int64_t didx[kRows];
+#pragma unroll
+    for (int u = 0; u < kRows; ++u) {
+      const bool live = g + u < end;
+      sidx[u] = 0;
+      didx[u] = 0;
+      if (kSrcPaged && live) sidx[u] = p.src_paged.index != nullptr ? p.src_paged.index[row[u]] : row[u];
+      if (kDstPaged && live) didx[u] = p.dst_paged.index != nullptr ? p.dst_paged.index[row[u]] : row[u];
+    }
+    const uint4* src[kRows];
+    uint4* dst[kRows];
+#pragma unroll
+    for (int u = 0; u < kRows; ++u) {
+      src[u] = nullptr;
+      dst[u] = nullptr;
+      if (g + u < end) {
+        const int64_t so = kSrcPaged ? paged_slot_offset(p.src_paged, sidx[u], s_shift, p.flags, p.status, lead)
+                                     : coff[u];
+        const int64_t dso = kDstPaged ? paged_slot_offset(p.dst_paged, didx[u], d_shift, p.flags, p.status, lead)
+                                      : coff[u];
+        if (so >= 0 && dso >= 0) {
+          src[u] = reinterpret_cast<const uint4*>(kSrcPaged ? p.src_paged.planes[plane[u]] + so
+                                                            : p.src_chunk.base + so);
+          dst[u] = reinterpret_cast<uint4*>(kDstPaged ? p.dst_paged.planes[plane[u]] + dso
+                                                      : p.dst_chunk.base + dso);
+        }
+      }
+    }
+    uint4 buf[kRows][kVpl];
+#pragma unroll
+    for (int u = 0; u < kRows; ++u)
+#pragma unroll
+      for (int j = 0; j < kVpl; ++j) {
+        const int i = lane + j * tpr;
+        if (src[u] != nullptr && i < row_vecs) buf[u][j] = ld_stream(src[u] + i);
+      }
+#pragma unroll
+    for (int u = 0; u < kRows; ++u)
+#pragma unroll
+      for (int j = 0; j < kVpl; ++j) {
+        const int i = lane + j * tpr;
+        if (dst[u] != nullptr && i < row_vecs) st_stream(dst[u] + i, buf[u][j]);
+      }
+  }
+}
+
 int device_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -2177,9 +2317,10 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
 
 // Rows of 16-byte vectors in device memory, at most kShortRowMaxVecs of
 // them: the shape of move_short_rows_kernel for the row length.
-template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
+template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows, bool kPlaneMajor>
 cudaError_t launch_move_short_typed(MoveParams p, cudaStream_t stream) {
-  auto kernel = move_short_rows_kernel<kSrcPaged, kDstPaged, kVpl, kRows>;
+  auto kernel = kPlaneMajor ? move_short_rows_pm_kernel<kSrcPaged, kDstPaged, kVpl, kRows>
+                            : move_short_rows_kernel<kSrcPaged, kDstPaged, kVpl, kRows>;
   static int blocks_per_sm = 0;
   if (blocks_per_sm == 0) {
     int b = 0;
@@ -2205,10 +2346,10 @@ cudaError_t launch_move_short(MoveParams p, cudaStream_t stream) {
   if (p.row_vecs <= kSmallRowMaxVecs) {  // 2^k >= the row's vectors lanes, at most 8
     p.tpr_log2 = 0;
     while (p.tpr_log2 < 3 && (int64_t{1} << p.tpr_log2) < p.row_vecs) ++p.tpr_log2;
-    return launch_move_short_typed<kSrcPaged, kDstPaged, 2, 4>(p, stream);
+    return launch_move_short_typed<kSrcPaged, kDstPaged, 2, 4, true>(p, stream);
   }
   p.tpr_log2 = 5;
-  return launch_move_short_typed<kSrcPaged, kDstPaged, 3, 2>(p, stream);
+  return launch_move_short_typed<kSrcPaged, kDstPaged, 3, 2, false>(p, stream);
 }
 
 
