@@ -1,7 +1,8 @@
 """Benchmark of the paged-KV hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload llama70b-shard|llama8b]
+                    [--workload llama70b-shard|llama70b-shard-tokens|llama8b|mla-layer-shard[-fp8]|
+                                decode-mix|adapter|host-tier|clock-stress]
 
 One step = one pass of the hot path over one batch: gather every block of a
 GPU's paged KV cache, for every layer and K/V, through a seeded random block
@@ -14,6 +15,8 @@ KV head): 80 layers x K/V, 1 KV head per GPU, head_dim 128, block 16 tokens,
 bf16, 16 sequences x 32k tokens = 32,768 blocks per GPU, 21.47 GB of cache
 per GPU.  With N GPUs each rank owns its own head shard and block table
 (weak scaling, no collective in the data path; NCCL only aggregates timings).
+llama70b-shard-tokens moves the same cache token by token (256-byte rows)
+through the slot mapping of the same block table.
 
 Also reported: the device-resident clock stream on the clock-stress workload
 (1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations, one Zipf(1.1)
