@@ -472,8 +472,8 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
             "frac": round(achieved / peak, 4),
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
             "traffic": traffic,
-            "kernel": ("move_short_rows_pm_kernel (gather and scatter launches; 8 lanes x 2 vectors per 256-byte "
-                       "row, 4 rows per lane group and iteration, plane-major)" if tokens else
+            "kernel": ("move_rows_stream_kernel (gather and scatter launches; warp-cooperative: 18 rows of 256 bytes per "
+                       "warp and batch, 9 vectors per lane, plane-major)" if tokens else
                        "move_rows_bulk_kernel (gather and scatter launches; TMA bulk copies)"),
             "algorithmic_bytes_per_launch": 2 * payload,
             "avg_launch_ms": round(avg_launch_ms, 4),

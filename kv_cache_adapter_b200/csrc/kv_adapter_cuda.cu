@@ -1919,6 +1919,7 @@ struct MoveParams {
   int32_t flags;
   int64_t* status;
   const int64_t* gate;  // non-null: the launch moves nothing unless *gate != 0
+  int rows_per_batch;   // move_rows_stream_kernel: rows a warp moves per batch
 };
 
 template <typename V>
@@ -2059,94 +2060,8 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
   }
 }
 
-// Short rows of 16-byte vectors, several rows per lane group and iteration:
-// 2^k lanes share a row, kVpl vectors each, so that every load or store
-// instruction covers whole 128-byte lines of its rows, and each group moves
-// kRows rows per iteration (all loads, then all stores) to keep enough bytes
-// in flight.  Two shapes:
-//   rows <= 256 B: at most 8 lanes, 2 vectors each, 4 rows per iteration,
-//     in plane-major order (move_short_rows_pm_kernel);
-//   rows <= 1.5 KiB: 32 lanes, 3 vectors each, 2 rows per iteration, in
-//     row-major order (this kernel: one index load and offset per row,
-//     reused across the planes).
-// B200, random token rows: 256 B (64 planes) gather / scatter 5.7 / 5.7 TB/s
-// against 4.9 / 4.7 with four lanes of four vectors and one row at a time,
-// where every instruction touches half-lines of eight rows; 576 B (8 planes)
-// 5.2 / 5.0 against 4.6 / 4.4.  Same work items, row-offset reuse, index
-// checks and gate as move_rows_kernel; rows are never split into segments.
+// Rows of at most kSmallRowMaxVecs 16-byte vectors (256 bytes).
 constexpr int64_t kSmallRowMaxVecs = 16;
-constexpr int64_t kShortRowMaxVecs = 96;
-
-template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
-__global__ void __launch_bounds__(kMoverThreads) move_short_rows_kernel(const __grid_constant__ MoveParams p) {
-  if (p.gate != nullptr && *p.gate == 0) return;
-  const int tpr = 1 << p.tpr_log2;
-  const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  const int lane = static_cast<int>(gtid & (tpr - 1));
-  const int64_t group = gtid >> p.tpr_log2;
-  const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
-  const int64_t planes = p.num_planes;
-  const int64_t items = planes * p.num_rows;
-  const int64_t per = items / num_groups;
-  const int64_t rem = items - per * num_groups;
-  const int64_t begin = group * per + (group < rem ? group : rem);
-  const int64_t end = begin + per + (group < rem ? 1 : 0);
-  if (begin >= end) return;
-
-  int64_t r = begin / planes;
-  int64_t pl = begin - r * planes;
-  int64_t row_at = -1;
-  int64_t src_row = 0;
-  int64_t dst_row = 0;
-  const bool lead = lane == 0;
-  const int row_vecs = static_cast<int>(p.row_vecs);
-
-  for (int64_t g = begin; g < end; g += kRows) {
-    const uint4* src[kRows];
-    uint4* dst[kRows];
-#pragma unroll
-    for (int u = 0; u < kRows; ++u) {
-      src[u] = nullptr;
-      dst[u] = nullptr;
-      if (g + u < end) {
-        if (r != row_at) {
-          row_at = r;
-          src_row = kSrcPaged ? paged_row_offset(p.src_paged, r, p.flags, p.status, lead)
-                              : chunk_row_offset(p.src_chunk, r);
-          dst_row = kDstPaged ? paged_row_offset(p.dst_paged, r, p.flags, p.status, lead)
-                              : chunk_row_offset(p.dst_chunk, r);
-        }
-        if (src_row >= 0 && dst_row >= 0) {
-          src[u] = reinterpret_cast<const uint4*>(
-              kSrcPaged ? p.src_paged.planes[pl] + src_row
-                        : p.src_chunk.base + src_row + pl * p.src_chunk.plane_stride);
-          dst[u] = reinterpret_cast<uint4*>(
-              kDstPaged ? p.dst_paged.planes[pl] + dst_row
-                        : p.dst_chunk.base + dst_row + pl * p.dst_chunk.plane_stride);
-        }
-        if (++pl == planes) {
-          pl = 0;
-          ++r;
-        }
-      }
-    }
-    uint4 buf[kRows][kVpl];
-#pragma unroll
-    for (int u = 0; u < kRows; ++u)
-#pragma unroll
-      for (int j = 0; j < kVpl; ++j) {
-        const int i = lane + j * tpr;
-        if (src[u] != nullptr && i < row_vecs) buf[u][j] = ld_stream(src[u] + i);
-      }
-#pragma unroll
-    for (int u = 0; u < kRows; ++u)
-#pragma unroll
-      for (int j = 0; j < kVpl; ++j) {
-        const int i = lane + j * tpr;
-        if (dst[u] != nullptr && i < row_vecs) st_stream(dst[u] + i, buf[u][j]);
-      }
-  }
-}
 
 // Offset of slot id idx on a paged side (shift = log2 of the block size when
 // that is a power of two, else -1), or -1 when the row is skipped; the same
@@ -2177,17 +2092,22 @@ __device__ __forceinline__ int pow2_shift(int64_t v) {
   return v > 0 && (v & (v - 1)) == 0 ? __ffsll(static_cast<long long>(v)) - 1 : -1;
 }
 
-// Plane-major order of the same work: item g = plane * num_rows + row, so a
-// lane group walks consecutive rows of one plane, which are consecutive
-// rows of a chunk and, for slot mappings made from block tables, runs of
-// consecutive rows of a block.  Every item loads its own index; power-of-two
-// block sizes divide by shifting, and the chunk position advances by
-// counting instead of dividing.  Used for rows of at most 256 bytes, where
-// four lane groups share a warp's instruction stream (B200, 256-byte token
-// rows through a block-table slot mapping, 160 planes: 6.05 TB/s against
-// 5.81 in row-major order).  With one group per warp (32-lane rows) the
-// per-item index arithmetic makes it issue-bound (576-byte rows: 3.7 TB/s
-// against 5.2), so longer rows stay row-major.
+// Small rows (at most 256 bytes) of 16-byte vectors, several rows per lane
+// group and iteration: 2^k <= 8 lanes share a row, kVpl vectors each, so
+// that every load or store instruction covers whole 128-byte lines of its
+// rows, and each group moves kRows rows per iteration (all loads, then all
+// stores).  Work items in plane-major order, g = plane * num_rows + row: a
+// group walks consecutive rows of one plane, which are consecutive rows of
+// a chunk and, for slot mappings made from block tables, runs of
+// consecutive rows of a block.  Every item loads its own index;
+// power-of-two block sizes divide by shifting, and the chunk position
+// advances by counting instead of dividing.  Same work items, index checks
+// and gate as move_rows_kernel; rows are never split into segments.
+// Used for rows under 128 bytes (the stream mover covers 128 B to 1.5 KiB).
+// B200, random 256-byte token rows over 64 planes: gather / scatter
+// 5.7 / 5.7 TB/s, against 4.9 / 4.7 for the SIMT mover's shape (four lanes
+// of four vectors, one row at a time: every instruction touches half-lines
+// of eight rows).
 template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
 __global__ void __launch_bounds__(kMoverThreads) move_short_rows_pm_kernel(const __grid_constant__ MoveParams p) {
   if (p.gate != nullptr && *p.gate == 0) return;
@@ -2285,6 +2205,133 @@ __global__ void __launch_bounds__(kMoverThreads) move_short_rows_pm_kernel(const
   }
 }
 
+// Warp-cooperative mover for rows of 128 bytes to 1.5 KiB in 16-byte
+// vectors: each warp takes a contiguous range of work items in plane-major
+// order (consecutive rows of one plane) and moves them in batches of
+// rows_per_batch rows.  Lane r computes the source and destination
+// addresses of the batch's row r (one index load per row, coalesced across
+// the warp), and the warp's 32 x kRowStreamSlots vector slots tile the
+// batch's rows back to back: slot k of lane l is vector l + 32k of the
+// batch, and takes its row's address from the lane that computed it by a
+// shuffle.  Nearly every slot does useful work whatever the row length
+// (9 slots per lane: 8 rows of 576 bytes or 4 of 1,152 fill all 288), so
+// each lane keeps 9 vectors in flight and consecutive lanes cover
+// consecutive bytes.  B200, token rows through a product-path gather /
+// scatter: 576-byte rows under a block-table slot mapping 5.8 / 5.8 TB/s
+// (5.3 / 5.4 with 32 lanes of 3 vectors, 2 rows per iteration), 1,152-byte
+// rows 5.9 / 5.9 (5.6 / 5.6), random 128-byte rows 4.7 / 4.8 (3.7 / 3.7 with
+// the small-row shape).  Above 1.5 KiB a batch holds one or two rows and
+// the SIMT mover is as fast or faster (3 KiB rows: 5.6 against 6.0).
+constexpr int kRowStreamThreads = 512;
+constexpr int kRowStreamSlots = 9;
+
+template <bool kSrcPaged, bool kDstPaged>
+__global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(const __grid_constant__ MoveParams p) {
+  if (p.gate != nullptr && *p.gate == 0) return;
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t num_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t rows = p.num_rows;
+  const int64_t items = p.num_planes * rows;
+  const int64_t per = items / num_warps;
+  const int64_t rem = items - per * num_warps;
+  const int64_t begin = warp * per + (warp < rem ? warp : rem);
+  const int64_t end = begin + per + (warp < rem ? 1 : 0);
+  if (begin >= end) return;  // the whole warp
+
+  const int rpb = p.rows_per_batch;
+  const int rv = static_cast<int>(p.row_vecs);
+  constexpr bool kChunk = !(kSrcPaged && kDstPaged);
+  const ChunkSide& cs = kSrcPaged ? p.dst_chunk : p.src_chunk;  // the chunk side, when there is one
+  const int s_shift = kSrcPaged ? pow2_shift(p.src_paged.block_size) : 0;
+  const int d_shift = kDstPaged ? pow2_shift(p.dst_paged.block_size) : 0;
+
+  // This lane's item (begin + lane), advanced by rpb per batch, and its
+  // position in the chunk side; 32-bit (the launcher checks the row count).
+  int pl = static_cast<int>((begin + lane) / rows);
+  int r = static_cast<int>((begin + lane) - static_cast<int64_t>(pl) * rows);
+  const int rows32 = static_cast<int>(rows);
+  const int rpc = kChunk ? static_cast<int>(cs.rows_per_chunk) : 1;
+  int c = r / rpc;
+  int cr = r - c * rpc;
+  const int qc = rpb / rpc;
+  const int mc = rpb - qc * rpc;
+
+  // Slot k of this lane is vector f = lane + 32k of a batch: row f / rv,
+  // vector f % rv; successive slots step by 32 = q32 * rv + m32.
+  const int row0 = lane / rv;
+  const int vec0 = lane - row0 * rv;
+  const int q32 = 32 / rv;
+  const int m32 = 32 - q32 * rv;
+
+  for (int64_t g = begin; g < end; g += rpb) {
+    const int nrows = end - g < rpb ? static_cast<int>(end - g) : rpb;
+    uint64_t my_src = 0;
+    uint64_t my_dst = 0;
+    if (lane < nrows) {
+      const int64_t coff = kChunk ? c * cs.chunk_stride + cr * cs.row_stride + pl * cs.plane_stride : 0;
+      int64_t so = coff;
+      int64_t dso = coff;
+      if (kSrcPaged) {
+        const int64_t idx = p.src_paged.index != nullptr ? p.src_paged.index[r] : r;
+        so = paged_slot_offset(p.src_paged, idx, s_shift, p.flags, p.status, true);
+      }
+      if (kDstPaged) {
+        const int64_t idx = p.dst_paged.index != nullptr ? p.dst_paged.index[r] : r;
+        dso = paged_slot_offset(p.dst_paged, idx, d_shift, p.flags, p.status, true);
+      }
+      if (so >= 0 && dso >= 0) {
+        my_src = kSrcPaged ? p.src_paged.planes[pl] + so : p.src_chunk.base + so;
+        my_dst = kDstPaged ? p.dst_paged.planes[pl] + dso : p.dst_chunk.base + dso;
+      }
+    }
+    r += rpb;
+    cr += mc;
+    c += qc;
+    if (cr >= rpc) {
+      cr -= rpc;
+      ++c;
+    }
+    if (r >= rows32) {
+      do {
+        r -= rows32;
+        ++pl;
+      } while (r >= rows32);
+      c = r / rpc;
+      cr = r - c * rpc;
+    }
+
+    // my_src and my_dst are both set or both zero (a skipped row).
+    uint4 buf[kRowStreamSlots];
+    int row = row0;
+    int vec = vec0;
+#pragma unroll
+    for (int k = 0; k < kRowStreamSlots; ++k) {
+      const uint64_t sb = __shfl_sync(0xffffffffu, my_src, row & 31);
+      if (row < nrows && sb != 0) buf[k] = ld_stream(reinterpret_cast<const uint4*>(sb) + vec);
+      vec += m32;
+      row += q32;
+      if (vec >= rv) {
+        vec -= rv;
+        ++row;
+      }
+    }
+    row = row0;
+    vec = vec0;
+#pragma unroll
+    for (int k = 0; k < kRowStreamSlots; ++k) {
+      const uint64_t db = __shfl_sync(0xffffffffu, my_dst, row & 31);
+      if (row < nrows && db != 0) st_stream(reinterpret_cast<uint4*>(db) + vec, buf[k]);
+      vec += m32;
+      row += q32;
+      if (vec >= rv) {
+        vec -= rv;
+        ++row;
+      }
+    }
+  }
+}
+
 int device_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -2315,12 +2362,12 @@ cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-// Rows of 16-byte vectors in device memory, at most kShortRowMaxVecs of
-// them: the shape of move_short_rows_kernel for the row length.
-template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows, bool kPlaneMajor>
-cudaError_t launch_move_short_typed(MoveParams p, cudaStream_t stream) {
-  auto kernel = kPlaneMajor ? move_short_rows_pm_kernel<kSrcPaged, kDstPaged, kVpl, kRows>
-                            : move_short_rows_kernel<kSrcPaged, kDstPaged, kVpl, kRows>;
+// Rows of at most kSmallRowMaxVecs 16-byte vectors in device memory: 2^k
+// lanes per row with 2^k >= the row's vectors, at most 8, 2 vectors each,
+// 4 rows per iteration.
+template <bool kSrcPaged, bool kDstPaged>
+cudaError_t launch_move_small(MoveParams p, cudaStream_t stream) {
+  auto kernel = move_short_rows_pm_kernel<kSrcPaged, kDstPaged, 2, 4>;
   static int blocks_per_sm = 0;
   if (blocks_per_sm == 0) {
     int b = 0;
@@ -2328,11 +2375,13 @@ cudaError_t launch_move_short_typed(MoveParams p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     blocks_per_sm = b > 0 ? b : 1;
   }
+  p.tpr_log2 = 0;
+  while (p.tpr_log2 < 3 && (int64_t{1} << p.tpr_log2) < p.row_vecs) ++p.tpr_log2;
   p.seg_vecs = p.row_vecs;
   p.segs_per_row = 1;
   const int sms = device_sm_count();
   const int64_t items = p.num_planes * p.num_rows;
-  const int64_t threads_needed = ((items + kRows - 1) / kRows) << p.tpr_log2;
+  const int64_t threads_needed = ((items + 3) / 4) << p.tpr_log2;
   int64_t blocks = (threads_needed + kMoverThreads - 1) / kMoverThreads;
   const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
   if (blocks > resident) blocks = resident;
@@ -2341,16 +2390,39 @@ cudaError_t launch_move_short_typed(MoveParams p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Rows of kRowStreamMinVecs to kRowStreamMaxVecs 16-byte vectors in device
+// memory (and fewer than 2^30 rows: the kernel keeps row positions in 32
+// bits): the warp-cooperative stream mover.
+constexpr int64_t kRowStreamMinVecs = 8;
+constexpr int64_t kRowStreamMaxVecs = 96;
+
 template <bool kSrcPaged, bool kDstPaged>
-cudaError_t launch_move_short(MoveParams p, cudaStream_t stream) {
-  if (p.row_vecs <= kSmallRowMaxVecs) {  // 2^k >= the row's vectors lanes, at most 8
-    p.tpr_log2 = 0;
-    while (p.tpr_log2 < 3 && (int64_t{1} << p.tpr_log2) < p.row_vecs) ++p.tpr_log2;
-    return launch_move_short_typed<kSrcPaged, kDstPaged, 2, 4, true>(p, stream);
+cudaError_t launch_move_stream(MoveParams p, cudaStream_t stream) {
+  auto kernel = move_rows_stream_kernel<kSrcPaged, kDstPaged>;
+  static int blocks_per_sm = 0;
+  if (blocks_per_sm == 0) {
+    int b = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kRowStreamThreads, 0);
+    if (e != cudaSuccess) return e;
+    blocks_per_sm = b > 0 ? b : 1;
   }
-  p.tpr_log2 = 5;
-  return launch_move_short_typed<kSrcPaged, kDstPaged, 3, 2, false>(p, stream);
+  int64_t rpb = (int64_t{32} * kRowStreamSlots) / p.row_vecs;
+  if (rpb > 32) rpb = 32;
+  if (rpb < 1) rpb = 1;
+  p.rows_per_batch = static_cast<int>(rpb);
+  p.seg_vecs = p.row_vecs;
+  p.segs_per_row = 1;
+  const int sms = device_sm_count();
+  const int64_t items = p.num_planes * p.num_rows;
+  const int64_t warps_needed = (items + rpb - 1) / rpb;
+  int64_t blocks = (warps_needed * 32 + kRowStreamThreads - 1) / kRowStreamThreads;
+  const int64_t resident = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
+  if (blocks > resident) blocks = resident;
+  if (blocks < 1) blocks = 1;
+  kernel<<<static_cast<unsigned>(blocks), kRowStreamThreads, 0, stream>>>(p);
+  return cudaGetLastError();
 }
+
 
 
 // ---------------------------------------------------------------------------
@@ -2672,7 +2744,9 @@ cudaError_t launch_move_vec(const MoveParams& p, int vec_bytes, cudaStream_t str
   switch (vec_bytes) {
     case 16:
       if (p.row_vecs * 16 >= kBulkMinRowBytes) return launch_move_bulk<kSrcPaged, kDstPaged>(p, stream);
-      if (p.row_vecs <= kShortRowMaxVecs) return launch_move_short<kSrcPaged, kDstPaged>(p, stream);
+      if (p.row_vecs >= kRowStreamMinVecs && p.row_vecs <= kRowStreamMaxVecs && p.num_rows < (int64_t{1} << 30))
+        return launch_move_stream<kSrcPaged, kDstPaged>(p, stream);
+      if (p.row_vecs <= kSmallRowMaxVecs) return launch_move_small<kSrcPaged, kDstPaged>(p, stream);
       return launch_move_typed<kSrcPaged, kDstPaged, uint4>(p, stream);
     case 8: return launch_move_typed<kSrcPaged, kDstPaged, uint2>(p, stream);
     case 4: return launch_move_typed<kSrcPaged, kDstPaged, unsigned int>(p, stream);

@@ -1,10 +1,12 @@
 """GPU parity for rows of at most 1.5 KiB in 16-byte vectors, which take the
-short-row mover (up to 8 lanes and four rows per lane group and iteration
-for rows up to 256 bytes, 32 lanes and two rows above), against the
+small-row mover (rows under 128 bytes: up to 8 lanes and four rows per lane
+group and iteration) or the warp-cooperative stream mover (128 bytes to
+1.5 KiB: a warp's 32 x 9 vector slots tile a batch of rows), against the
 oracle's torch CPU indexing, byte for byte: row widths from 16 bytes to
 1.5 KiB and just past it, plane counts that make one iteration's rows
-straddle tokens, work ranges that end inside an iteration, padding tokens,
-out-of-range ids, and block-granular moves of short blocks."""
+straddle tokens, work ranges that end inside a batch, chunks shorter than a
+batch, padding tokens, out-of-range ids, and block-granular moves of short
+blocks."""
 from __future__ import annotations
 
 import numpy as np
@@ -60,6 +62,32 @@ def test_token_gather_scatter_short_rows(ops, row, planes):
             assert _same(a, b), t
 
 
+@pytest.mark.parametrize("row", [128, 256, 576, 1152])
+@pytest.mark.parametrize("tpc,t", [(1, 7), (3, 60), (7, 301), (17, 34), (256, 512)])
+def test_token_chunk_sizes_short_rows(ops, row, tpc, t):
+    """Chunk lengths below, at and above the rows one warp moves per batch
+    (18 rows of 256 B, 8 of 576 B, 4 of 1,152 B), so the chunk position
+    carries across chunks inside a batch, and row counts below a batch, so
+    the row position wraps into the next plane more than once."""
+    gen = torch.Generator().manual_seed(row + 7 * tpc + t)
+    planes = 5
+    nblk, bs = 40, 16
+    caches_h = [_rand_bytes((nblk, bs, row), gen) for _ in range(planes)]
+    caches_d = [c.to(DEV) for c in caches_h]
+    table = torch.randperm(nblk, generator=gen)
+    mapping = (table.view(-1, 1) * bs + torch.arange(bs).view(1, -1)).reshape(-1)[:t].clone()
+    if t > 10:
+        mapping[torch.randperm(t, generator=gen)[: t // 9]] = -1
+    out = torch.zeros((t // tpc, planes, tpc, row), dtype=torch.uint8, device=DEV)
+    ops.gather_tokens(caches_d, mapping.to(DEV), out, tokens_per_chunk=tpc)
+    assert _same(out, moves.gather_tokens(caches_h, mapping, tokens_per_chunk=tpc))
+    src_h = _rand_bytes((t // tpc, planes, tpc, row), gen)
+    moves.scatter_tokens(caches_h, mapping, src_h, tokens_per_chunk=tpc)
+    ops.scatter_tokens(caches_d, mapping.to(DEV), src_h.to(DEV), tokens_per_chunk=tpc)
+    for a, b in zip(caches_d, caches_h):
+        assert _same(a, b)
+
+
 @pytest.mark.parametrize("row", [32, 144, 256, 576, 1536])
 def test_token_copy_short_rows(ops, row):
     gen = torch.Generator().manual_seed(row)
@@ -106,22 +134,28 @@ def test_block_moves_short_rows(ops, shape, dtype):
     assert _same(cache_d, cache_h)
 
 
-def test_short_rows_out_of_range_raise_and_skip(ops):
-    cache = torch.arange(64 * 16, dtype=torch.int32, device=DEV).reshape(64, 16)  # 64-byte rows
+@pytest.mark.parametrize("cols", [16, 64, 144])  # int32 rows of 64 B (small mover), 256 B and 576 B (stream)
+def test_short_rows_out_of_range_raise_and_skip(ops, cols):
+    cache = torch.arange(64 * cols, dtype=torch.int32, device=DEV).reshape(64, cols)
     before = cache.clone()
     with pytest.raises(IndexError):
-        ops.scatter_blocks(cache, torch.tensor([3, 64, 5], device=DEV), torch.ones((3, 16), dtype=torch.int32, device=DEV))
+        ops.scatter_blocks(cache, torch.tensor([3, 64, 5], device=DEV), torch.ones((3, cols), dtype=torch.int32, device=DEV))
     want = before.clone()
     want[3] = 1
     want[5] = 1
     assert torch.equal(cache, want)
-    planes = [cache.reshape(16, 4, 16)]
+    planes = [cache.reshape(16, 4, cols), cache.reshape(16, 4, cols)]
     with pytest.raises(IndexError):
         ops.gather_tokens(planes, torch.tensor([0, 1, 2, 3, 64], device=DEV))
-    got = torch.full((1, 1, 5, 16), -7, dtype=torch.int32, device=DEV)
+    with pytest.raises(IndexError):
+        ops.scatter_tokens(planes, torch.tensor([0, 64], device=DEV),
+                           torch.zeros((1, 2, 2, cols), dtype=torch.int32, device=DEV), tokens_per_chunk=2)
+    assert int(cache[0].abs().sum()) == 0  # the valid token was written, the bad one skipped
+    got = torch.full((1, 2, 5, cols), -7, dtype=torch.int32, device=DEV)
     ops.gather_tokens(planes, torch.tensor([0, -1, 63, -1, 7], device=DEV), got)
-    assert torch.equal(got[0, 0, 2], planes[0][15, 3]) and torch.equal(got[0, 0, 4], planes[0][1, 3])
-    assert bool((got[0, 0, 1] == -7).all()) and bool((got[0, 0, 3] == -7).all())  # padding untouched
+    for p in range(2):
+        assert torch.equal(got[0, p, 2], planes[p][15, 3]) and torch.equal(got[0, p, 4], planes[p][1, 3])
+        assert bool((got[0, p, 1] == -7).all()) and bool((got[0, p, 3] == -7).all())  # padding untouched
 
 
 @pytest.mark.parametrize("row,P,nblk,bs", [(128, 64, 4096, 16), (288, 8, 4096, 64)])
