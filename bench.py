@@ -564,7 +564,7 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     cycles = -(-args.steps * per // 16)  # timed decode steps, rounded up to whole 16-step cycles
     mix = DecodeMix(ops, device, layers=32, heads=heads, head_dim=128, block_size=16, num_blocks=65536,
                     seqs=256, dtype=torch.float16, seed=1234 + rank,
-                    max_steps=(args.warmup * per + 17) + 2 * cycles * 16 + 64)
+                    max_steps=(args.warmup * per + 17) + 3 * cycles * 16 + 64)  # warm-up + 3 timed runs
     rows = torch.randn((1, mix.num_planes, mix.seqs, *mix.row_shape), dtype=torch.float16, device=device)
     # warm-up: eager steps (at least one full cycle), aligned to the start of a cycle
     warm = max(args.warmup * per, 17)
@@ -591,8 +591,15 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     tok0, blk0 = mix.tokens, mix.gathered_blocks
     eager_ms = timed(lambda: [mix.step(rows) for _ in range(cycles * 16)])
     eager_tokens, eager_blocks = mix.tokens - tok0, mix.gathered_blocks - blk0
-    # graph-captured: one replay per 16-step cycle
+    # graph-captured: one replay per 16-step cycle, first with every step's
+    # launches in order on one stream, then pipelined (each step's bookkeeping
+    # on a second stream, overlapping the previous step's moves)
     graph, per_cycle = mix.capture_cycle(rows)
+    serial_ms = timed(lambda: [graph.replay() for _ in range(cycles)])
+    del graph
+    mix.pipelined = True
+    graph, per_cycle_p = mix.capture_cycle(rows)
+    assert per_cycle_p == per_cycle
     with ClockSampler(device.index) as clocks:
         ms = timed(lambda: [graph.replay() for _ in range(cycles)])
     tokens, blocks = cycles * 16 * mix.seqs, cycles * per_cycle
@@ -629,9 +636,14 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         "evictions_per_s": round(world * blocks / (ms / 1e3), 1),
         "gpu_launches_per_decode_step": "append_step (pop, commit, release, slot_mapping) + scatter_tokens; "
                                         "plus one gather on steps that evict",
-        "issue": "CUDA graph, one replay per 16-step cycle",
+        "issue": "CUDA graph, one replay per 16-step cycle; each step's bookkeeping on a second stream, one "
+                 "step ahead of the moves (double-buffered victims and slot_mapping)",
+        "serial_graph": {"value": round(world * moved / (serial_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                         "ms_per_decode_step": round(serial_ms / decode_steps, 5),
+                         "issue": "CUDA graph, every step's launches in order on one stream"},
         "host_issued": {"value": round(world * moved / (eager_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                        "ms_per_decode_step": round(eager_ms / decode_steps, 5)},
+                        "ms_per_decode_step": round(eager_ms / decode_steps, 5),
+                        "issue": "one Python call per op, one stream"},
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

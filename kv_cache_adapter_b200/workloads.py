@@ -202,6 +202,18 @@ class DecodeMix:
     the fill positions, which decide which sequences need a block, so steps
     issue no host<->device traffic and a whole cycle of ``block_size`` steps
     can be captured in a CUDA graph (``capture_cycle``).
+
+    ``pipelined`` (CUDA op set with ``append_step``): the bookkeeping runs on
+    a stream of its own, one step ahead of the moves.  Step i + 1's
+    bookkeeping reads and writes only metadata (slot_meta, l2p / p2l,
+    search_start, the sequences' blocks and positions) and its own half of
+    double-buffered victim and slot_mapping arrays, so it overlaps step i's
+    gather and scatter, which touch only cache bytes; step i + 1's moves
+    still wait for its bookkeeping, and the moves stay in order on the
+    caller's stream (a block released at step i and popped at step i + 1 is
+    spilled after step i's scatter wrote its last token).  Step i's
+    bookkeeping waits for the moves of step i - 2, the last readers of the
+    buffer half it rewrites.  Results are the same bytes as unpipelined.
     """
 
     def __init__(self, ops, device, *, layers: int = 32, heads: int = 1, head_dim: int = 128,
@@ -248,12 +260,37 @@ class DecodeMix:
         self.empty_ids = torch.empty(0, dtype=torch.int64, device=device)
         # one-launch bookkeeping when the op set has it (the CUDA module)
         self._append = getattr(ops, "append_step", None)
-        self.victims_buf = torch.empty(seqs, dtype=torch.int64, device=device)
-        self.slot_mapping_buf = torch.empty(seqs, dtype=torch.int64, device=device)
+        self.victims_bufs = [torch.empty(seqs, dtype=torch.int64, device=device) for _ in range(2)]
+        self.slot_mapping_bufs = [torch.empty(seqs, dtype=torch.int64, device=device) for _ in range(2)]
+        self._half = 0  # the buffer half of the next step
+        self._pipelined = False
+        self._book_stream = None
+        self._booked = self._moved = None
         self._need = {}  # need set (bytes) -> (index tensor, ones, arange) on the device
         self.evictions = 0
         self.tokens = 0
         self.gathered_blocks = 0
+
+    @property
+    def slot_mapping_buf(self) -> torch.Tensor:
+        """The slot_mapping of the last step."""
+        return self.slot_mapping_bufs[self._half ^ 1]
+
+    @property
+    def pipelined(self) -> bool:
+        return self._pipelined
+
+    @pipelined.setter
+    def pipelined(self, on: bool) -> None:
+        on = bool(on) and self.device.type == "cuda" and self._append is not None
+        if on and self._book_stream is None:
+            self._book_stream = torch.cuda.Stream(self.device)
+            self._booked = [torch.cuda.Event() for _ in range(2)]
+            self._moved = [torch.cuda.Event() for _ in range(2)]
+        if on != self._pipelined:  # switch between steps with nothing in flight on the side stream
+            torch.cuda.current_stream(self.device).wait_stream(self._book_stream)
+            self._book_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self._pipelined = on
 
     def need_new_blocks(self) -> np.ndarray:
         return np.nonzero(self.pos == self.block_size)[0]
@@ -266,6 +303,8 @@ class DecodeMix:
             got = (torch.tensor(need, device=self.device), torch.ones(c, dtype=torch.uint8, device=self.device),
                    torch.arange(c, dtype=torch.int64, device=self.device))
             self._need[key] = got
+            if self._pipelined:  # made on the caller's stream, read on the bookkeeping stream
+                self._book_stream.wait_stream(torch.cuda.current_stream(self.device))
         return got
 
     def step(self, token_rows: torch.Tensor, *, check: bool = False):
@@ -276,17 +315,34 @@ class DecodeMix:
         spill = self.spill[:c]
         if self._append is not None:
             need_dev = self._need_tensors(need)[0] if c else self.empty_ids
-            victims = self.victims_buf[:c]
-            self._append(self.slot_meta, self.search_start, self.l2p, self.p2l, need_dev, self.cur_block_dev,
-                         self.cur_logical_dev, self.pos_dev, self.block_size, self.next_logical_dev, victims,
-                         self.slot_mapping_buf, check=check)
+            h = self._half
+            self._half ^= 1
+            victims = self.victims_bufs[h][:c]
+            slot_mapping = self.slot_mapping_bufs[h]
+
+            def book():
+                self._append(self.slot_meta, self.search_start, self.l2p, self.p2l, need_dev, self.cur_block_dev,
+                             self.cur_logical_dev, self.pos_dev, self.block_size, self.next_logical_dev, victims,
+                             slot_mapping, check=check)
+
+            if self._pipelined:
+                moves = torch.cuda.current_stream(self.device)
+                self._book_stream.wait_event(self._moved[h])  # step i - 2's moves: the last readers of half h
+                with torch.cuda.stream(self._book_stream):
+                    book()
+                    self._booked[h].record(self._book_stream)
+                moves.wait_event(self._booked[h])
+            else:
+                book()
             if c:
                 self.ops.gather_layers(self.block_table, victims, spill, blocks_per_chunk=1, check=check)
                 self.pos[need] = 0
                 self.evictions += c
                 self.gathered_blocks += c
-            self.ops.scatter_tokens(self.token_table, self.slot_mapping_buf, token_rows, tokens_per_chunk=self.seqs,
+            self.ops.scatter_tokens(self.token_table, slot_mapping, token_rows, tokens_per_chunk=self.seqs,
                                     check=check)
+            if self._pipelined:
+                self._moved[h].record(torch.cuda.current_stream(self.device))
             self.pos += 1
             self.tokens += self.seqs
             return spill
@@ -328,11 +384,22 @@ class DecodeMix:
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
         graph = torch.cuda.CUDAGraph()
+        if self._pipelined:
+            stream.wait_stream(self._book_stream)
         with torch.cuda.stream(stream):
             with torch.cuda.graph(graph, stream=stream):
+                if self._pipelined:  # fork the bookkeeping stream from the capture; no outside events
+                    for ev in self._moved:
+                        ev.record(stream)
+                    self._book_stream.wait_stream(stream)
                 for _ in range(self.block_size):
                     self.step(token_rows, check=False)
         torch.cuda.current_stream(self.device).wait_stream(stream)
+        if self._pipelined:  # later eager steps wait on real records, not on captured ones
+            cur = torch.cuda.current_stream(self.device)
+            self._book_stream.wait_stream(cur)
+            for ev in self._moved + self._booked:
+                ev.record(cur)
         per_replay = self.evictions - counters[0]
         self.evictions, self.tokens, self.gathered_blocks = counters
         assert np.array_equal(self.pos, pos)  # a full cycle: the schedule repeats

@@ -43,11 +43,16 @@ def test_decode_mix_host_logic_on_cpu():
 
 
 @pytest.mark.gpu
-def test_decode_mix_matches_oracle_step_by_step():
+@pytest.mark.parametrize("pipelined", [False, True])
+def test_decode_mix_matches_oracle_step_by_step(pipelined):
+    """Unpipelined, and with each step's bookkeeping on its own stream
+    overlapping the previous step's moves: identical bytes either way."""
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda as cuda_ops
 
     dev = torch.device("cuda", 0)
     gpu = DecodeMix(cuda_ops, dev, **SMALL)
+    gpu.pipelined = pipelined
+    assert gpu.pipelined == pipelined
     cpu = DecodeMix(OracleOps(), torch.device("cpu"), **SMALL)
     cpu.kv.copy_(gpu.kv.cpu())
     for step in range(150):
@@ -66,14 +71,18 @@ def test_decode_mix_matches_oracle_step_by_step():
 
 
 @pytest.mark.gpu
-def test_decode_mix_graph_replay_matches_eager():
+@pytest.mark.parametrize("pipelined", [False, True])
+def test_decode_mix_graph_replay_matches_eager(pipelined):
     """A captured cycle of block_size steps, replayed, leaves exactly the state
-    that running the same steps eagerly leaves."""
+    that running the same steps eagerly (unpipelined) leaves; pipelined, the
+    capture forks the bookkeeping stream inside the graph, and eager steps
+    after the replays still line up."""
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda as cuda_ops
 
     dev = torch.device("cuda", 0)
     eager = DecodeMix(cuda_ops, dev, **SMALL)
     graphed = DecodeMix(cuda_ops, dev, **SMALL)
+    graphed.pipelined = pipelined
     rows = _rows(0, eager).to(dev)
     for _ in range(SMALL["block_size"] + 1):  # one full cycle eagerly, then step 1 of the next
         eager.step(rows)
@@ -84,6 +93,9 @@ def test_decode_mix_graph_replay_matches_eager():
         for _ in range(SMALL["block_size"]):
             eager.step(rows)
         graph.replay()
+    for step in range(7):  # eager steps after the replays
+        eager.step(_rows(step, eager).to(dev))
+        graphed.step(_rows(step, eager).to(dev))
     torch.cuda.synchronize()
     cuda_ops.check_status(dev)
     assert torch.equal(eager.kv.view(torch.int16), graphed.kv.view(torch.int16))
