@@ -557,8 +557,8 @@ __device__ __forceinline__ bool slot_ok(int64_t x, int64_t n) { return x >= 0 &&
 // With one CTA the barriers are block barriers.  StreamGrid lives in the
 // scratch buffer after the per-slot arrays and is cleared before each launch.
 struct StreamGrid {
-  unsigned int bar_count;
-  unsigned int bar_gen;
+  unsigned int bar_count;  // arrivals at grid barriers since the launch began
+  unsigned int unused0;
   int failed;
   int nu;        // distinct slots re-accessed in the window
   int tp_total;  // pending candidates taken
@@ -574,7 +574,7 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   return v;
 }
 
-constexpr uint32_t kGridSpinLimit = 1u << 22;  // about 0.3 s of 64 ns naps
+constexpr uint32_t kGridSpinLimit = 1u << 22;  // polls of a wait: a few seconds at most
 
 // Waits until *word differs from `from` (or *abort != 0); gives up after
 // about kGridSpinLimit naps.  Returns true when the word changed.
@@ -589,25 +589,31 @@ __device__ bool bounded_wait_change(const unsigned* word, unsigned from, const i
 }
 
 // Grid-wide barrier with a bounded wait.  Every CTA's writes before the
-// barrier are visible to every CTA after it.  A CTA that waits too long (or
-// sees another CTA give up) marks the grid failed, reports
+// barrier are visible to every CTA after it: the CTA's threads meet at a
+// block barrier, then one thread arrives with a release add on a counter
+// that only grows (barrier j of the launch completes when it reaches
+// (j + 1) x gridDim.x) and waits with acquire loads until it does; no CTA
+// resets anything, so the last arrival releases the others with its one
+// atomic.  The counter starts at zero with each launch.  A CTA that waits
+// too long (or sees another CTA give up) marks the grid failed, reports
 // KVCA_ERR_DEVICE_TIMEOUT and returns false; callers then return.
 __device__ bool grid_barrier(StreamGrid* g, int64_t* status) {
   __shared__ int ok_s;
   __syncthreads();
   if (gridDim.x == 1) return true;
   if (threadIdx.x == 0) {
+    const unsigned B = gridDim.x;
+    unsigned old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(&g->bar_count) : "memory");
+    const unsigned target = (old / B + 1u) * B;
     int ok = 1;
-    const unsigned gen = ld_acquire_u32(&g->bar_gen);
-    __threadfence();
-    if (atomicAdd(&g->bar_count, 1u) == gridDim.x - 1) {
-      atomicExch(&g->bar_count, 0u);
-      __threadfence();
-      atomicAdd(&g->bar_gen, 1u);
-    } else {
-      ok = bounded_wait_change(&g->bar_gen, gen, &g->failed) ? 1 : 0;
+    uint32_t spins = 0;
+    while (static_cast<int>(ld_acquire_u32(&g->bar_count) - target) < 0) {
+      if (++spins > kGridSpinLimit || *reinterpret_cast<const volatile int*>(&g->failed) != 0) {
+        ok = 0;
+        break;
+      }
     }
-    __threadfence();
     if (!ok) {
       atomicExch(&g->failed, 1);
       report(status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
