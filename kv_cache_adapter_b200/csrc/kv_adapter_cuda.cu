@@ -1064,7 +1064,11 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   KVCA_GRID_SYNC();
 
   // 4b. final usage of every touched slot (each listed re-accessed slot once,
-  //     plus the victims), computed from the epoch-start words
+  //     plus the victims), computed from the epoch-start words and written
+  //     straight back.  A slot listed twice (a victim that was also
+  //     re-accessed) gets the same word from both: a victim's final usage
+  //     does not depend on its old usage, and no pin changes, so whichever
+  //     of the two reads the word first or last, both store the same value.
   const int64_t n_touched = nu + (v_hi - v_lo);
   auto touched_slot = [&](int64_t i) -> int64_t {
     return i < nu ? static_cast<int64_t>(__ldcg(w.touched + i))
@@ -1092,28 +1096,8 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
       if (!slot_ok(xs[u], n)) continue;
       int64_t fin = (vss[u] != 0 ? 1 : static_cast<int64_t>(M::usage(ws[u]))) + cts[u];
       if (fin > M::kUsageMax) fin = M::kUsageMax;
-      w.first_bump[xs[u]] = static_cast<int32_t>(fin + 1);
+      meta[xs[u]] = M::pack(M::pin(ws[u]), fin);
     }
-  }
-  KVCA_GRID_SYNC();
-  for (int64_t i0 = gt; i0 < n_touched; i0 += G * kU) {
-    int64_t xs[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int64_t i = i0 + static_cast<int64_t>(u) * G;
-      xs[u] = i < n_touched ? touched_slot(i) : -1;
-    }
-    unsigned ws[kU];
-    int32_t fins[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const bool okx = slot_ok(xs[u], n);
-      ws[u] = okx ? static_cast<unsigned>(__ldcg(meta + xs[u])) : 0u;
-      fins[u] = okx ? __ldcg(w.first_bump + xs[u]) : 0;
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u)
-      if (slot_ok(xs[u], n)) meta[xs[u]] = M::pack(M::pin(ws[u]), fins[u] - 1);
   }
   KVCA_GRID_SYNC();
   // 4c. leave the per-slot scratch words zero again
@@ -1126,7 +1110,9 @@ __device__ int64_t stream_epoch(MetaT* meta, int64_t n, int64_t* search_start, i
   }
   if (b == 0 && threadIdx.x == 0 && s_end > s0)
     *search_start = (__ldcg(&g->last_victim) + 1) % n;
-  KVCA_GRID_SYNC();
+  // the stream goes on: the next epoch or exact step needs the cleared
+  // scratch and search_start; when it ends here, so does the launch
+  if (s_end < steps) KVCA_GRID_SYNC();
 #undef KVCA_GRID_SYNC
   return s_end;
 }
