@@ -562,9 +562,10 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     per = DECODE_STEPS_PER_BENCH_STEP
     heads = args.heads or 1
     cycles = -(-args.steps * per // 16)  # timed decode steps, rounded up to whole 16-step cycles
-    mix = DecodeMix(ops, device, layers=32, heads=heads, head_dim=128, block_size=16, num_blocks=65536,
+    pool = args.pool_blocks or 65536
+    mix = DecodeMix(ops, device, layers=32, heads=heads, head_dim=128, block_size=16, num_blocks=pool,
                     seqs=256, dtype=torch.float16, seed=1234 + rank,
-                    max_steps=(args.warmup * per + 17) + 3 * cycles * 16 + 64)  # warm-up + 3 timed runs
+                    max_steps=(args.warmup * per + 17) + 4 * cycles * 16 + 256)  # warm-up + 4 timed runs
     rows = torch.randn((1, mix.num_planes, mix.seqs, *mix.row_shape), dtype=torch.float16, device=device)
     # warm-up: eager steps (at least one full cycle), aligned to the start of a cycle
     warm = max(args.warmup * per, 17)
@@ -600,26 +601,41 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     mix.pipelined = True
     graph, per_cycle_p = mix.capture_cycle(rows)
     assert per_cycle_p == per_cycle
-    with ClockSampler(device.index) as clocks:
-        ms = timed(lambda: [graph.replay() for _ in range(cycles)])
+    step_ms = timed(lambda: [graph.replay() for _ in range(cycles)])
     tokens, blocks = cycles * 16 * mix.seqs, cycles * per_cycle
     assert (tokens, blocks) == (eager_tokens, eager_blocks)
     row_bytes = heads * 128 * 2
     moved = 2 * mix.num_planes * (tokens * row_bytes + blocks * row_bytes * mix.block_size)
     del graph
+    # whole-cycle booking: one append_steps launch books the 16 steps of the
+    # next cycle while the current cycle's moves run; a replay = 2 cycles
+    mix.pipelined = False
+    mix.start_cycles()
+    mix.run_cycle(rows)
+    graph, per_two = mix.capture_cycles(rows)
+    assert per_two == 2 * per_cycle
+    replays = -(-cycles // 2)
+    with ClockSampler(device.index) as clocks:
+        ms = timed(lambda: [graph.replay() for _ in range(replays)])
+    del graph
+    mix.stop_cycles(rows)
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    cyc_steps = 2 * replays * 16
+    cyc_moved = 2 * mix.num_planes * (cyc_steps * mix.seqs * row_bytes + replays * per_two * row_bytes * mix.block_size)
     if rank != 0:
         return
     decode_steps = cycles * 16
     line = {
         "metric": "paged-KV decode append + eviction gather GB/s",
-        "value": round(world * moved / (ms / 1e3) / 1e9, 2),
+        "value": round(world * cyc_moved / (ms / 1e3) / 1e9, 2),
         "unit": "GB/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(ms / args.steps, 4),
-        "ms_per_decode_step": round(ms / decode_steps, 5),
-        "decode_steps_timed": decode_steps,
+        "ms_per_step": round(ms / cyc_steps * per, 4),
+        "ms_per_decode_step": round(ms / cyc_steps, 5),
+        "decode_steps_timed": cyc_steps,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -627,17 +643,23 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         "data": "synthetic (seeded N(0,1) cache and token rows, seeded pool state)",
         "config": {
             "workload": f"decode append + gather mix: 32 layers x K/V, {heads} KV head(s)/GPU, head_dim 128, "
-                        f"block 16, fp16, full 65,536-block pool, 256 sequences x 1 token per decode step, "
+                        f"block 16, fp16, {'full 65,536' if pool == 65536 else f'reduced {pool:,}'}-block pool, "
+                        f"256 sequences x 1 token per decode step, "
                         f"{per} decode steps per bench step (timed in whole 16-step cycles), clock eviction + "
                         f"spill gather when a block fills",
             "parallelism": f"kv-head shard x{world}, no data-path collective",
         },
-        "tokens_per_s": round(world * tokens / (ms / 1e3), 1),
-        "evictions_per_s": round(world * blocks / (ms / 1e3), 1),
-        "gpu_launches_per_decode_step": "append_step (pop, commit, release, slot_mapping) + scatter_tokens; "
-                                        "plus one gather on steps that evict",
-        "issue": "CUDA graph, one replay per 16-step cycle; each step's bookkeeping on a second stream, one "
-                 "step ahead of the moves (double-buffered victims and slot_mapping)",
+        "tokens_per_s": round(world * cyc_steps * mix.seqs / (ms / 1e3), 1),
+        "evictions_per_s": round(world * replays * per_two / (ms / 1e3), 1),
+        "gpu_launches_per_decode_step": "scatter_tokens, plus one gather on steps that evict, plus 1/16 of an "
+                                        "append_steps launch (pop, commit, release, slot_mapping of 16 steps)",
+        "issue": "CUDA graph, one replay per two 16-step cycles; the bookkeeping of the next cycle (one "
+                 "append_steps launch) on a second stream, overlapping the current cycle's moves "
+                 "(victims and slot_mappings double-buffered by cycle)",
+        "per_step_pipelined_graph": {"value": round(world * moved / (step_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                                     "ms_per_decode_step": round(step_ms / decode_steps, 5),
+                                     "issue": "CUDA graph per 16-step cycle, each step's append_step on a second "
+                                              "stream, one step ahead of the moves"},
         "serial_graph": {"value": round(world * moved / (serial_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                          "ms_per_decode_step": round(serial_ms / decode_steps, 5),
                          "issue": "CUDA graph, every step's launches in order on one stream"},
@@ -916,6 +938,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter", "host-tier", "clock-stress"],
                     default="llama70b-shard")
     ap.add_argument("--heads", type=int, default=None, help="KV heads per GPU for the decode mix (default 1)")
+    ap.add_argument("--pool-blocks", type=int, default=None,
+                    help="blocks of the decode mix's pool (default 65,536; smaller only for profiler captures)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="override the number of sequences (smaller cases for profiling)")
     ap.add_argument("--no-clock", action="store_true")

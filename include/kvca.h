@@ -375,6 +375,30 @@ int kvca_append_step(int meta_bits, int order, void* d_slot_meta, int64_t num_sl
                      int64_t* d_next_logical, int64_t* d_victims, int64_t* d_slot_mapping,
                      uint32_t* d_scratch_bitmap, int64_t* d_status, kvca_stream_t stream);
 
+/*
+ * num_steps decode steps of kvca_append_step in one launch (one CTA; runs of
+ * more than 256 steps take one launch per 256, in stream order): step s
+ * gives new blocks to the sequences d_need[d_need_offsets[s] ..
+ * d_need_offsets[s + 1]), writes their victims to d_victims from index
+ * d_need_offsets[s] on and its slot_mapping to d_slot_mapping[s * num_seqs ..
+ * (s + 1) * num_seqs).  The results equal num_steps kvca_append_step calls;
+ * a serving loop that knows which sequences fill a block in the next steps
+ * (decode with a fixed batch) books them all at once, ahead of their token
+ * moves.  d_need_offsets (num_steps + 1 entries, device memory) must be
+ * non-decreasing within [0, num_need] with at most num_seqs entries per step,
+ * else KVCA_ERR_BAD_INDEX and nothing changes.  An error at step s (bad ids,
+ * too few reusable slots) leaves steps 0..s-1 done, step s unchanged, and
+ * stops.  No reference counterpart as one call (the composition is
+ * adapter.py:472-525 -> :647-651 -> :309-336 per step).
+ */
+int kvca_append_steps(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                      int64_t* d_search_start, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                      const int64_t* d_need, const int64_t* d_need_offsets, int64_t num_need,
+                      int64_t num_steps, int64_t* d_cur_block, int64_t* d_cur_logical,
+                      int64_t* d_pos, int64_t num_seqs, int64_t block_size,
+                      int64_t* d_next_logical, int64_t* d_victims, int64_t* d_slot_mapping,
+                      int64_t* d_status, kvca_stream_t stream);
+
 /* Failure-detection self-test: one thread waits, with the bounded wait of
  * the batched clock stream's grid barriers, for *d_flag to differ from
  * `from`.  If it does not within about 0.3 s, d_status gets
@@ -448,6 +472,24 @@ int kvca_gather(const kvca_paged_desc* src, const kvca_chunk_desc* dst, int64_t 
 int kvca_scatter(const kvca_chunk_desc* src, const kvca_paged_desc* dst, int64_t num_planes,
                  int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
                  kvca_stream_t stream);
+
+/*
+ * A kvca_scatter and a kvca_gather in one launch (the scatter's arguments
+ * first, then the gather's, then the flags of each): the CTAs are split between the
+ * two by bytes.  Results equal the two calls, provided the moves touch
+ * disjoint bytes (nothing orders one before the other).  For a decode
+ * loop, whose steps move a few MiB each (the token scatter of step i and the
+ * spill gather of the blocks step i + 1 evicts, which step i does not
+ * write), one launch instead of two.  Without 16-byte alignment, with
+ * KVCA_FLAG_HOST_MEMORY, or above 32 MiB moved by the two together (when
+ * each fills the GPU on its own), the two moves take two launches, the
+ * scatter first.  No reference counterpart.
+ */
+int kvca_scatter_gather(const kvca_chunk_desc* s_src, const kvca_paged_desc* s_dst, int64_t s_planes,
+                        int64_t s_rows, int64_t s_row_bytes, const kvca_paged_desc* g_src,
+                        const kvca_chunk_desc* g_dst, int64_t g_planes, int64_t g_rows,
+                        int64_t g_row_bytes, int32_t s_flags, int32_t g_flags, int64_t* d_status,
+                        kvca_stream_t stream);
 
 /* Paged -> paged in one pass: dst[dst.index[r]] = src[src.index[r]]
  * (the index_select + index_copy_ pair of adapter.py:779-787). */

@@ -143,6 +143,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_i64,
          c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
     ),
+    "kvca_append_steps": (
+        c_int,
+        [c_int, c_int, c_ptr, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_ptr, c_ptr, c_ptr,
+         c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
     "kvca_exchange": (
         c_int,
         [ctypes.POINTER(PagedDesc), ctypes.POINTER(PagedDesc), c_ptr, c_i64, c_i64, ctypes.c_int32, c_ptr, c_ptr],
@@ -156,6 +161,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [ctypes.POINTER(ChunkDesc), ctypes.POINTER(PagedDesc), c_i64, c_i64, c_i64, ctypes.c_int32,
          c_ptr, c_ptr],
+    ),
+    "kvca_scatter_gather": (
+        c_int,
+        [ctypes.POINTER(ChunkDesc), ctypes.POINTER(PagedDesc), c_i64, c_i64, c_i64, ctypes.POINTER(PagedDesc),
+         ctypes.POINTER(ChunkDesc), c_i64, c_i64, c_i64, ctypes.c_int32, ctypes.c_int32, c_ptr, c_ptr],
     ),
     "kvca_copy_paged": (
         c_int,

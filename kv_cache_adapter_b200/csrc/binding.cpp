@@ -455,6 +455,27 @@ int kvca_append_step(int meta_bits, int order, void* d_slot_meta, int64_t num_sl
       d_scratch_bitmap, d_victims, d_slot_mapping, d_status, stream));
 }
 
+int kvca_append_steps(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
+                      int64_t* d_search_start, int64_t* d_l2p, int64_t num_logical, int64_t* d_p2l,
+                      const int64_t* d_need, const int64_t* d_need_offsets, int64_t num_need,
+                      int64_t num_steps, int64_t* d_cur_block, int64_t* d_cur_logical,
+                      int64_t* d_pos, int64_t num_seqs, int64_t block_size,
+                      int64_t* d_next_logical, int64_t* d_victims, int64_t* d_slot_mapping,
+                      int64_t* d_status, kvca_stream_t stream) {
+  if (!valid_meta_bits(meta_bits) ||
+      (order != KVCA_POP_ORDER_GROUPED && order != KVCA_POP_ORDER_PREFIX) || num_slots <= 0 ||
+      num_logical <= 0 || num_seqs <= 0 || block_size <= 0 || num_need < 0 || num_steps < 0 ||
+      !d_slot_meta || !d_search_start || !d_l2p || !d_p2l || !d_cur_block || !d_cur_logical ||
+      !d_pos || !d_next_logical || !d_status || (num_steps > 0 && (!d_need_offsets || !d_slot_mapping)) ||
+      (num_need > 0 && (!d_need || !d_victims)))
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (num_steps == 0) return KVCA_OK;
+  return status_of(kvca::launch_append_steps(
+      meta_bits, order, d_slot_meta, num_slots, d_search_start, d_l2p, num_logical, d_p2l, d_need,
+      d_need_offsets, num_need, num_steps, d_cur_block, d_cur_logical, d_pos, num_seqs, block_size,
+      d_next_logical, d_victims, d_slot_mapping, d_status, stream));
+}
+
 int kvca_wait_selftest(const uint32_t* d_flag, uint32_t from, int64_t* d_status, kvca_stream_t stream) {
   if (!d_flag || !d_status) return KVCA_ERR_BAD_ARGUMENT;
   return status_of(kvca::launch_wait_selftest(d_flag, from, d_status, stream));
@@ -492,6 +513,37 @@ int kvca_scatter(const kvca_chunk_desc* src, const kvca_paged_desc* dst, int64_t
   kvca::MoveArgs a{kvca::MoveKind::kScatter, nullptr, &sc, &dp, nullptr, num_planes, num_rows,
                    row_bytes, vec, flags, d_status};
   return status_of(kvca::launch_move(a, stream));
+}
+
+int kvca_scatter_gather(const kvca_chunk_desc* s_src, const kvca_paged_desc* s_dst, int64_t s_planes,
+                        int64_t s_rows, int64_t s_row_bytes, const kvca_paged_desc* g_src,
+                        const kvca_chunk_desc* g_dst, int64_t g_planes, int64_t g_rows,
+                        int64_t g_row_bytes, int32_t s_flags, int32_t g_flags, int64_t* d_status,
+                        kvca_stream_t stream) {
+  if (!common_move_args_ok(s_planes, s_rows, s_row_bytes) || !common_move_args_ok(g_planes, g_rows, g_row_bytes))
+    return KVCA_ERR_BAD_ARGUMENT;
+  kvca::ChunkSide sc{}, gc{};
+  kvca::PagedSide sp{}, gp{};
+  int s_vec = align_of(static_cast<uint64_t>(s_row_bytes));
+  int g_vec = align_of(static_cast<uint64_t>(g_row_bytes));
+  if (s_rows > 0) {
+    if (!check_chunk(s_src, &s_vec) || !check_paged(s_dst, s_planes, s_row_bytes, &s_vec))
+      return KVCA_ERR_BAD_ARGUMENT;
+    to_side(s_src, &sc);
+    to_side(s_dst, s_planes, &sp);
+  }
+  if (g_rows > 0) {
+    if (!check_paged(g_src, g_planes, g_row_bytes, &g_vec) || !check_chunk(g_dst, &g_vec))
+      return KVCA_ERR_BAD_ARGUMENT;
+    to_side(g_src, g_planes, &gp);
+    to_side(g_dst, &gc);
+  }
+  if (s_rows == 0 && g_rows == 0) return KVCA_OK;
+  kvca::MoveArgs s{kvca::MoveKind::kScatter, nullptr, &sc, &sp, nullptr, s_planes, s_rows,
+                   s_row_bytes, s_vec, s_flags, d_status};
+  kvca::MoveArgs g{kvca::MoveKind::kGather, &gp, nullptr, nullptr, &gc, g_planes, g_rows,
+                   g_row_bytes, g_vec, g_flags, d_status};
+  return status_of(kvca::launch_scatter_gather(s, g, stream));
 }
 
 int kvca_copy_paged(const kvca_paged_desc* src, const kvca_paged_desc* dst, int64_t num_planes,

@@ -181,21 +181,33 @@ struct PopShared {
 // histogram fixes T, and pass 2 walks every tile once more, ranking classes
 // 1..T (grouped order) or all usage <= T (prefix order) and writing the aged
 // usage of every slot.
+//
+// start_set: the caller already put the scan start into sh.start and
+// sh.last_slot (pop_start) and passed a barrier since, so the read of
+// *search_start can overlap the caller's own loads.  out_sh (optional, in
+// shared memory): victims 0..out_sh_cap-1 are also written there, so the
+// caller reads them without a global round trip.
+template <typename MetaT>
+__device__ __forceinline__ void pop_start(const int64_t* search_start, int64_t n, PopShared<MetaT>& sh) {
+  long long s = static_cast<long long>(*search_start % n);
+  if (s < 0) s += n;
+  sh.start = s;
+  sh.last_slot = s;
+}
+
 template <typename MetaT>
 __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
                        const uint32_t* bitmap, int64_t count, int64_t* out, int order,
-                       bool aligned, PopShared<MetaT>& sh) {
+                       bool aligned, PopShared<MetaT>& sh, bool start_set = false,
+                       int64_t* out_sh = nullptr, int64_t out_sh_cap = 0) {
   using M = Meta<MetaT>;
   constexpr int kSpv = M::kSlotsPerVec;
   const int64_t n = num_slots;
 
-  if (threadIdx.x == 0) {
-    long long s = static_cast<long long>(*search_start % n);
-    if (s < 0) s += n;
-    sh.start = s;
-    sh.last_slot = s;
+  if (!start_set) {
+    if (threadIdx.x == 0) pop_start(search_start, n, sh);
+    __syncthreads();
   }
-  __syncthreads();
   const int64_t s = sh.start;
 
   // ---- Pass 1: usage-0 candidates with early exit -------------------------
@@ -231,6 +243,7 @@ __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
         mask &= mask - 1u;
         if (rank < count) {
           out[rank] = v * kSpv + j;
+          if (rank < out_sh_cap) out_sh[rank] = v * kSpv + j;
           if (rank == count - 1) sh.last_slot = v * kSpv + j;
         }
         ++rank;
@@ -345,6 +358,7 @@ __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
             mask &= mask - 1u;
             if (rank < limit) {
               out[sh.cls_base[c] + rank] = v * kSpv + j;
+              if (sh.cls_base[c] + rank < out_sh_cap) out_sh[sh.cls_base[c] + rank] = v * kSpv + j;
               if (c == threshold && rank == need - 1) sh.last_slot = v * kSpv + j;
             }
             ++rank;
@@ -367,6 +381,7 @@ __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
           mask &= mask - 1u;
           if (rank < count) {
             out[rank] = v * kSpv + j;
+            if (rank < out_sh_cap) out_sh[rank] = v * kSpv + j;
             if (rank == count - 1) sh.last_slot = v * kSpv + j;
           }
           ++rank;
@@ -1685,25 +1700,49 @@ __global__ void __launch_bounds__(1024)
 // A small CTA: the step is a chain of short dependent phases, and block
 // barriers of 8 warps are cheaper than of 32 (decode mix, B200: 16.1 us per
 // decode step at 256 threads, 16.7 at 512, 18.5 at 1024, 16.3 at 128).
+//
+// The step is latency-bound: its cost is the number of dependent global
+// round trips.  Every read that does not depend on another is issued at
+// the start (the id checks' need -> cur_logical -> l2p chain, the scan
+// start, the sequences' blocks and positions), the pop's scan reads the
+// metadata right after the checks, and the victims stay in shared memory,
+// so the chain is: ids (3 deep) -> metadata tile -> p2l of the victims and
+// the full blocks' words -> stores.  Nothing is written before the checks
+// pass.  The step blocks no slot, so the pop reads no bitmap.
 constexpr int kAppendThreads = 256;
+constexpr int kAppendMaxSteps = 256;  // steps of one append_steps launch (offsets staged in shared memory)
 
 template <typename MetaT>
-__global__ void __launch_bounds__(kAppendThreads)
-    append_step_kernel(MetaT* meta, int64_t n, int64_t* search_start, int64_t* l2p,
-                       int64_t n_logical, int64_t* p2l, const int64_t* need, int64_t c,
-                       int64_t* cur_block, int64_t* cur_logical, int64_t* pos, int64_t seqs,
-                       int64_t block_size, int64_t* next_logical, uint32_t* bitmap, int order,
-                       bool aligned, int64_t* victims, int64_t* slot_mapping, int64_t* status) {
+struct AppendShared {
+  PopShared<MetaT> pop;
+  int64_t victims[kAppendThreads];
+  long long bad_value;
+};
+
+// One step (see above) for need[0..c), victims[0..c) and slot_mapping[0..seqs).
+// Returns KVCA_OK or the reported error code, uniformly across the CTA.  On
+// an error the step has changed nothing.  Every thread's global writes of
+// the step are visible to the CTA after its next block barrier.
+template <typename MetaT>
+__device__ int append_step_body(MetaT* meta, int64_t n, int64_t* search_start, int64_t* l2p,
+                                int64_t n_logical, int64_t* p2l, const int64_t* need, int64_t c,
+                                int64_t* cur_block, int64_t* cur_logical, int64_t* pos,
+                                int64_t seqs, int64_t block_size, int64_t* next_logical, int order,
+                                bool aligned, int64_t* victims, int64_t* slot_mapping,
+                                int64_t* status, AppendShared<MetaT>& sh) {
   using M = Meta<MetaT>;
-  __shared__ PopShared<MetaT> sh;
-  __shared__ int bad;
-  __shared__ long long bad_value;
-  if (threadIdx.x == 0) bad = 0;
-  __syncthreads();
   const int64_t base = *next_logical;
+  if (c > 0 && threadIdx.x == 0) pop_start(search_start, n, sh.pop);
+  // this thread's sequence for the slot_mapping pass
+  int64_t my_block = 0, my_pos = 0;
+  if (threadIdx.x < seqs) {
+    my_block = cur_block[threadIdx.x];
+    my_pos = pos[threadIdx.x];
+  }
   // Thread t keeps what it reads for need entry t (the common case: at most
   // one entry per thread); entries beyond the block size are read again.
   int64_t my_q = -1, my_full = -1;
+  bool bad = false;
   for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
     const int64_t q = need[j];
     int64_t v = q;
@@ -1718,40 +1757,45 @@ __global__ void __launch_bounds__(kAppendThreads)
         if (!ok) v = full;
       }
     }
-    if (!ok && atomicCAS(&bad, 0, 1) == 0) bad_value = v;
+    if (!ok) {
+      bad = true;
+      sh.bad_value = v;  // any one of the bad values
+    }
     if (j == threadIdx.x) {
       my_q = q;
       my_full = full;
     }
   }
-  if (threadIdx.x == 0 && c > 0 && (base < 0 || base + c > n_logical) && atomicCAS(&bad, 0, 1) == 0)
-    bad_value = base + c;
-  __syncthreads();
-  if (bad) {
-    if (threadIdx.x == 0) report(status, KVCA_ERR_BAD_INDEX, bad_value);
-    return;
+  if (threadIdx.x == 0 && c > 0 && (base < 0 || base + c > n_logical)) {
+    bad = true;
+    sh.bad_value = base + c;
+  }
+  if (__syncthreads_or(bad)) {
+    if (threadIdx.x == 0) report(status, KVCA_ERR_BAD_INDEX, sh.bad_value);
+    return KVCA_ERR_BAD_INDEX;
   }
   if (c > 0) {
-    const int rc = pop_cta<MetaT>(meta, n, search_start, bitmap, c, victims, order, aligned, sh);
+    const int rc = pop_cta<MetaT>(meta, n, search_start, nullptr, c, victims, order, aligned, sh.pop,
+                                  true, sh.victims, kAppendThreads);
     if (rc != KVCA_OK) {
       if (threadIdx.x == 0) report(status, rc, c);
-      return;
+      return rc;
     }
-    __syncthreads();
     // Unmap the victims' previous ids, commit the new ones, release the full
     // blocks.  The writes of different entries never meet: evicted ids are
     // older than base, the full blocks are pinned (never victims) and each
-    // sequence appears once.
+    // sequence appears once.  The full blocks' words are read after the pop,
+    // which may have aged them.
     for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
       const int64_t q = j == threadIdx.x ? my_q : need[j];
       const int64_t full = j == threadIdx.x ? my_full : l2p[cur_logical[q]];
-      const int64_t v = victims[j];
+      const int64_t v = j < kAppendThreads ? sh.victims[j] : victims[j];
       const int64_t prev = p2l[v];
+      const unsigned w = meta[full];
       if (prev >= 0) l2p[prev] = -1;
       l2p[base + j] = v;
       p2l[v] = base + j;
       meta[v] = M::pack(1, 1);
-      const unsigned w = meta[full];
       meta[full] = M::pack(static_cast<int64_t>(M::pin(w)) - 1, M::usage(w));
       cur_block[q] = v;
       cur_logical[q] = base + j;
@@ -1761,16 +1805,82 @@ __global__ void __launch_bounds__(kAppendThreads)
   // this step's token slots; the sequences that got a new block are
   // rewritten below (block v, position 0)
   for (int64_t q = threadIdx.x; q < seqs; q += blockDim.x) {
-    slot_mapping[q] = cur_block[q] * block_size + pos[q];
-    pos[q] += 1;
+    const int64_t b = q == threadIdx.x ? my_block : cur_block[q];
+    const int64_t p = q == threadIdx.x ? my_pos : pos[q];
+    slot_mapping[q] = b * block_size + p;
+    pos[q] = p + 1;
   }
   if (c > 0) {
     __syncthreads();
     for (int64_t j = threadIdx.x; j < c; j += blockDim.x) {
       const int64_t q = j == threadIdx.x ? my_q : need[j];
-      slot_mapping[q] = victims[j] * block_size;
+      const int64_t v = j < kAppendThreads ? sh.victims[j] : victims[j];
+      slot_mapping[q] = v * block_size;
       pos[q] = 1;
     }
+  }
+  return KVCA_OK;
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(kAppendThreads)
+    append_step_kernel(MetaT* meta, int64_t n, int64_t* search_start, int64_t* l2p,
+                       int64_t n_logical, int64_t* p2l, const int64_t* need, int64_t c,
+                       int64_t* cur_block, int64_t* cur_logical, int64_t* pos, int64_t seqs,
+                       int64_t block_size, int64_t* next_logical, int order, bool aligned,
+                       int64_t* victims, int64_t* slot_mapping, int64_t* status) {
+  __shared__ AppendShared<MetaT> sh;
+  append_step_body<MetaT>(meta, n, search_start, l2p, n_logical, p2l, need, c, cur_block,
+                          cur_logical, pos, seqs, block_size, next_logical, order, aligned,
+                          victims, slot_mapping, status, sh);
+}
+
+// num_steps steps in a row in one CTA: step s takes need[off[s]..off[s+1]),
+// writes its victims to victims[off[s]..] and its slot_mapping to
+// slot_mapping[s * seqs..], exactly as num_steps append_step launches would.
+// The offsets are checked first (non-decreasing, at most seqs per step,
+// within [0, num_need]); an error at step s leaves steps 0..s-1 done and
+// stops there.  Steps after the first read the state the previous one wrote
+// (same CTA, ordered by a block barrier).
+template <typename MetaT>
+__global__ void __launch_bounds__(kAppendThreads)
+    append_steps_kernel(MetaT* meta, int64_t n, int64_t* search_start, int64_t* l2p,
+                        int64_t n_logical, int64_t* p2l, const int64_t* need,
+                        const int64_t* need_offsets, int64_t num_need, int64_t num_steps,
+                        int64_t* cur_block, int64_t* cur_logical, int64_t* pos, int64_t seqs,
+                        int64_t block_size, int64_t* next_logical, int order, bool aligned,
+                        int64_t* victims, int64_t* slot_mapping, int64_t* status) {
+  __shared__ AppendShared<MetaT> sh;
+  __shared__ int64_t off[kAppendMaxSteps + 1];
+  bool bad = false;
+  for (int64_t s = threadIdx.x; s <= num_steps; s += blockDim.x) {
+    const int64_t o = need_offsets[s];
+    off[s] = o;
+    if (o < 0 || o > num_need) {
+      bad = true;
+      sh.bad_value = o;
+    }
+  }
+  __syncthreads();
+  for (int64_t s = threadIdx.x; s < num_steps; s += blockDim.x) {
+    const int64_t c = off[s + 1] - off[s];
+    if (c < 0 || c > seqs) {
+      bad = true;
+      sh.bad_value = off[s + 1];
+    }
+  }
+  if (__syncthreads_or(bad)) {
+    if (threadIdx.x == 0) report(status, KVCA_ERR_BAD_INDEX, sh.bad_value);
+    return;
+  }
+  for (int64_t s = 0; s < num_steps; ++s) {
+    const int64_t o = off[s];
+    const int rc = append_step_body<MetaT>(meta, n, search_start, l2p, n_logical, p2l, need + o,
+                                           off[s + 1] - o, cur_block, cur_logical, pos, seqs,
+                                           block_size, next_logical, order, aligned, victims + o,
+                                           slot_mapping + s * seqs, status, sh);
+    if (rc != KVCA_OK) return;
+    __syncthreads();
   }
 }
 
@@ -1977,14 +2087,17 @@ constexpr int64_t kMoverSegmentBytes = 16384;
 // kMoverUnroll vectors in flight.
 // kHost: one side is pinned, mapped host memory reached over the host link;
 // rows move with plain loads and stores there (no non-coherent cache path).
+// The movers' bodies take the CTA's index and the CTA count of the work
+// split (blockIdx.x and gridDim.x for a launch of their own), so that one
+// launch can also split its CTAs between two moves (move_pair_kernel).
 template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost>
-__global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_constant__ MoveParams p) {
+__device__ __forceinline__ void move_rows_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int tpr = 1 << p.tpr_log2;
-  const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t gtid = cta * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int lane = static_cast<int>(gtid & (tpr - 1));
   const int64_t group = gtid >> p.tpr_log2;
-  const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
+  const int64_t num_groups = (ctas * blockDim.x) >> p.tpr_log2;
   const int64_t planes = p.num_planes;
   const int64_t segs = p.segs_per_row;
   const int64_t per_row = planes * segs;
@@ -2052,6 +2165,11 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
   }
 }
 
+template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost>
+__global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_constant__ MoveParams p) {
+  move_rows_body<kSrcPaged, kDstPaged, V, kHost>(p, blockIdx.x, gridDim.x);
+}
+
 // Rows of at most kSmallRowMaxVecs 16-byte vectors (256 bytes).
 constexpr int64_t kSmallRowMaxVecs = 16;
 
@@ -2101,13 +2219,13 @@ __device__ __forceinline__ int pow2_shift(int64_t v) {
 // of four vectors, one row at a time: every instruction touches half-lines
 // of eight rows).
 template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
-__global__ void __launch_bounds__(kMoverThreads) move_short_rows_pm_kernel(const __grid_constant__ MoveParams p) {
+__device__ __forceinline__ void move_short_rows_pm_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int tpr = 1 << p.tpr_log2;
-  const int64_t gtid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t gtid = cta * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int lane = static_cast<int>(gtid & (tpr - 1));
   const int64_t group = gtid >> p.tpr_log2;
-  const int64_t num_groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> p.tpr_log2;
+  const int64_t num_groups = (ctas * blockDim.x) >> p.tpr_log2;
   const int64_t rows = p.num_rows;
   const int64_t items = p.num_planes * rows;
   const int64_t per = items / num_groups;
@@ -2197,6 +2315,11 @@ __global__ void __launch_bounds__(kMoverThreads) move_short_rows_pm_kernel(const
   }
 }
 
+template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
+__global__ void __launch_bounds__(kMoverThreads) move_short_rows_pm_kernel(const __grid_constant__ MoveParams p) {
+  move_short_rows_pm_body<kSrcPaged, kDstPaged, kVpl, kRows>(p, blockIdx.x, gridDim.x);
+}
+
 // Warp-cooperative mover for rows of 128 bytes to 1.5 KiB in 16-byte
 // vectors: each warp takes a contiguous range of work items in plane-major
 // order (consecutive rows of one plane) and moves them in batches of
@@ -2218,11 +2341,11 @@ constexpr int kRowStreamThreads = 512;
 constexpr int kRowStreamSlots = 9;
 
 template <bool kSrcPaged, bool kDstPaged>
-__global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(const __grid_constant__ MoveParams p) {
+__device__ __forceinline__ void move_rows_stream_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int lane = static_cast<int>(threadIdx.x & 31);
-  const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  const int64_t num_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t warp = (cta * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t num_warps = (ctas * blockDim.x) >> 5;
   const int64_t rows = p.num_rows;
   const int64_t items = p.num_planes * rows;
   const int64_t per = items / num_warps;
@@ -2322,6 +2445,43 @@ __global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(con
       }
     }
   }
+}
+
+template <bool kSrcPaged, bool kDstPaged>
+__global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(const __grid_constant__ MoveParams p) {
+  move_rows_stream_body<kSrcPaged, kDstPaged>(p, blockIdx.x, gridDim.x);
+}
+
+// Two independent moves in one launch: CTAs [0, split) run move a, the
+// others move b, each with the body its rows take on their own (the bulk
+// mover's rows take the SIMT body: one CTA shape for both).  For moves that
+// are each too small to fill the GPU for long (a decode step's token scatter
+// and the next step's spill gather), one launch instead of two saves a
+// launch's latency, ramp and tail.  The two moves must not touch the same
+// bytes.
+enum class MoverBody : int { kSimt = 0, kStream = 1, kSmall = 2 };
+
+template <MoverBody kBody, bool kSrcPaged, bool kDstPaged>
+__device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta, int64_t ctas) {
+  if constexpr (kBody == MoverBody::kStream)
+    move_rows_stream_body<kSrcPaged, kDstPaged>(p, cta, ctas);
+  else if constexpr (kBody == MoverBody::kSmall)
+    move_short_rows_pm_body<kSrcPaged, kDstPaged, 2, 4>(p, cta, ctas);
+  else
+    move_rows_body<kSrcPaged, kDstPaged, uint4, false>(p, cta, ctas);
+}
+
+static_assert(kMoverThreads == kRowStreamThreads, "the pair kernel runs every body at one CTA size");
+
+// a: a scatter (chunk -> paged), b: a gather (paged -> chunk)
+template <MoverBody kA, MoverBody kB>
+__global__ void __launch_bounds__(kMoverThreads)
+    move_pair_kernel(const __grid_constant__ MoveParams a, const __grid_constant__ MoveParams b, int split) {
+  if (static_cast<int>(blockIdx.x) < split)
+    run_mover_body<kA, false, true>(a, blockIdx.x, split);
+  else
+    run_mover_body<kB, true, false>(b, static_cast<int64_t>(blockIdx.x) - split,
+                                    static_cast<int64_t>(gridDim.x) - split);
 }
 
 int device_sm_count() {
@@ -2762,7 +2922,9 @@ int grid_for(int64_t count, int threads) {
 // Launchers
 // ---------------------------------------------------------------------------
 
-cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
+namespace {
+
+MoveParams make_move_params(const MoveArgs& a) {
   MoveParams p;
   memset(&p, 0, sizeof(p));
   if (a.src_paged) p.src_paged = *a.src_paged;
@@ -2785,6 +2947,58 @@ cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
   p.flags = a.flags;
   p.status = a.status;
   p.gate = a.gate;
+  return p;
+}
+
+// The body a 16-byte-vector move in device memory takes in the pair kernel
+// (the rules of launch_move_vec, with the bulk mover's rows on the SIMT
+// body), its parameters adjusted for that body, and the CTAs it can use.
+MoverBody pair_body(MoveParams* p, int64_t* ctas_wanted) {
+  const int64_t items = p->num_planes * p->num_rows;
+  if (p->row_vecs * 16 < kBulkMinRowBytes && p->row_vecs >= kRowStreamMinVecs &&
+      p->row_vecs <= kRowStreamMaxVecs && p->num_rows < (int64_t{1} << 30)) {
+    int64_t rpb = (int64_t{32} * kRowStreamSlots) / p->row_vecs;
+    if (rpb > 32) rpb = 32;
+    if (rpb < 1) rpb = 1;
+    p->rows_per_batch = static_cast<int>(rpb);
+    p->seg_vecs = p->row_vecs;
+    p->segs_per_row = 1;
+    *ctas_wanted = (((items + rpb - 1) / rpb) * 32 + kMoverThreads - 1) / kMoverThreads;
+    return MoverBody::kStream;
+  }
+  if (p->row_vecs <= kSmallRowMaxVecs) {
+    p->tpr_log2 = 0;
+    while (p->tpr_log2 < 3 && (int64_t{1} << p->tpr_log2) < p->row_vecs) ++p->tpr_log2;
+    p->seg_vecs = p->row_vecs;
+    p->segs_per_row = 1;
+    *ctas_wanted = ((((items + 3) / 4) << p->tpr_log2) + kMoverThreads - 1) / kMoverThreads;
+    return MoverBody::kSmall;
+  }
+  *ctas_wanted = (((items * p->segs_per_row) << p->tpr_log2) + kMoverThreads - 1) / kMoverThreads;
+  return MoverBody::kSimt;
+}
+
+template <MoverBody kA, MoverBody kB>
+cudaError_t launch_pair_typed(const MoveParams& a, const MoveParams& b, int split, int grid,
+                              cudaStream_t stream) {
+  move_pair_kernel<kA, kB><<<static_cast<unsigned>(grid), kMoverThreads, 0, stream>>>(a, b, split);
+  return cudaGetLastError();
+}
+
+template <MoverBody kA>
+cudaError_t launch_pair_b(MoverBody b_body, const MoveParams& a, const MoveParams& b, int split, int grid,
+                          cudaStream_t stream) {
+  switch (b_body) {
+    case MoverBody::kStream: return launch_pair_typed<kA, MoverBody::kStream>(a, b, split, grid, stream);
+    case MoverBody::kSmall: return launch_pair_typed<kA, MoverBody::kSmall>(a, b, split, grid, stream);
+    default: return launch_pair_typed<kA, MoverBody::kSimt>(a, b, split, grid, stream);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
+  MoveParams p = make_move_params(a);
   if (a.gate != nullptr && a.kind == MoveKind::kCopyPaged) {  // gated moves stay on the SIMT kernel
     switch (a.vec_bytes) {
       case 16:
@@ -2808,6 +3022,50 @@ cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
     case MoveKind::kGather: return launch_move_vec<true, false>(p, a.vec_bytes, stream);
     case MoveKind::kScatter: return launch_move_vec<false, true>(p, a.vec_bytes, stream);
     default: return launch_move_vec<true, true>(p, a.vec_bytes, stream);
+  }
+}
+
+// Above this many bytes moved by the two together, each move keeps the GPU
+// busy on its own and two launches, each with all SMs and its own best
+// kernel, are faster than one split launch (B200, a decode step with 8 KV
+// heads, 64 MiB each way: 32.2 us per step paired against 29.4 in two
+// launches; with 1 KV head, 4 MiB each way: 6.0 us paired against 10.4).
+constexpr double kPairMaxBytes = 32.0 * 1024 * 1024;
+
+cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gather, cudaStream_t stream) {
+  const double bytes_a = static_cast<double>(scatter.num_planes) * scatter.num_rows * scatter.row_bytes;
+  const double bytes_b = static_cast<double>(gather.num_planes) * gather.num_rows * gather.row_bytes;
+  const bool pairable = scatter.kind == MoveKind::kScatter && gather.kind == MoveKind::kGather &&
+                        scatter.vec_bytes == 16 && gather.vec_bytes == 16 && scatter.gate == nullptr &&
+                        gather.gate == nullptr && !((scatter.flags | gather.flags) & KVCA_FLAG_HOST_MEMORY) &&
+                        scatter.num_rows > 0 && gather.num_rows > 0 && bytes_a + bytes_b <= kPairMaxBytes;
+  if (!pairable) {  // two launches, in this order
+    if (scatter.num_rows > 0) {
+      const cudaError_t e = launch_move(scatter, stream);
+      if (e != cudaSuccess) return e;
+    }
+    return gather.num_rows > 0 ? launch_move(gather, stream) : cudaSuccess;
+  }
+  MoveParams a = make_move_params(scatter);
+  MoveParams b = make_move_params(gather);
+  int64_t want_a = 1, want_b = 1;
+  const MoverBody body_a = pair_body(&a, &want_a);
+  const MoverBody body_b = pair_body(&b, &want_b);
+  // CTAs split by bytes over the resident grid (one CTA of 512 threads per SM)
+  const int sms = device_sm_count();
+  const int64_t grid_max = sms > 1 ? sms : 2;
+  int64_t ca = static_cast<int64_t>(grid_max * bytes_a / (bytes_a + bytes_b) + 0.5);
+  if (ca < 1) ca = 1;
+  if (ca > grid_max - 1) ca = grid_max - 1;
+  int64_t cb = grid_max - ca;
+  if (ca > want_a) ca = want_a > 0 ? want_a : 1;
+  if (cb > want_b) cb = want_b > 0 ? want_b : 1;
+  const int split = static_cast<int>(ca);
+  const int grid = static_cast<int>(ca + cb);
+  switch (body_a) {
+    case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, split, grid, stream);
+    case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, split, grid, stream);
+    default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, split, grid, stream);
   }
 }
 
@@ -2974,12 +3232,36 @@ cudaError_t launch_append_step(int meta_bits, int order, void* meta, int64_t num
                                uint32_t* bitmap, int64_t* victims, int64_t* slot_mapping,
                                int64_t* status, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  (void)bitmap;  // the step blocks no slot
   KVCA_META_DISPATCH(meta_bits, append_step_kernel<MetaT><<<1, kAppendThreads, 0, stream>>>(
                                     static_cast<MetaT*>(meta), num_slots, search_start, l2p,
                                     num_logical, p2l, need, num_need, cur_block, cur_logical, pos,
-                                    num_seqs, block_size, next_logical, bitmap, order, aligned,
+                                    num_seqs, block_size, next_logical, order, aligned,
                                     victims, slot_mapping, status));
   return cudaGetLastError();
+}
+
+cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t num_slots,
+                                int64_t* search_start, int64_t* l2p, int64_t num_logical,
+                                int64_t* p2l, const int64_t* need, const int64_t* need_offsets,
+                                int64_t num_need, int64_t num_steps, int64_t* cur_block,
+                                int64_t* cur_logical, int64_t* pos, int64_t num_seqs,
+                                int64_t block_size, int64_t* next_logical, int64_t* victims,
+                                int64_t* slot_mapping, int64_t* status, cudaStream_t stream) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  // launches of at most kAppendMaxSteps steps, in stream order
+  for (int64_t s0 = 0; s0 < num_steps; s0 += kAppendMaxSteps) {
+    const int64_t k = num_steps - s0 < kAppendMaxSteps ? num_steps - s0 : kAppendMaxSteps;
+    KVCA_META_DISPATCH(meta_bits, append_steps_kernel<MetaT><<<1, kAppendThreads, 0, stream>>>(
+                                      static_cast<MetaT*>(meta), num_slots, search_start, l2p,
+                                      num_logical, p2l, need, need_offsets + s0, num_need, k,
+                                      cur_block, cur_logical, pos, num_seqs, block_size,
+                                      next_logical, order, aligned, victims,
+                                      slot_mapping + s0 * num_seqs, status));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_store_load_meta(int meta_bits, int order, int64_t* l2p, int64_t num_logical,

@@ -48,6 +48,10 @@ struct MoveArgs {
 
 cudaError_t launch_move(const MoveArgs& args, cudaStream_t stream);
 
+// A scatter and a gather that touch disjoint bytes, in one launch when both
+// move 16-byte vectors in device memory (else two launches, scatter first).
+cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gather, cudaStream_t stream);
+
 // Spill + fill of the same slots in one launch (one plane): row j sends slot
 // slots->index[j] to store row store->index[j] and fills it from store row
 // fill_from[j]; negative indices skip that part.  With *gate != 0 only the
@@ -164,6 +168,14 @@ cudaError_t launch_append_step(int meta_bits, int order, void* meta, int64_t num
                                int64_t num_seqs, int64_t block_size, int64_t* next_logical,
                                uint32_t* bitmap, int64_t* victims, int64_t* slot_mapping,
                                int64_t* status, cudaStream_t stream);
+
+cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t num_slots,
+                                int64_t* search_start, int64_t* l2p, int64_t num_logical,
+                                int64_t* p2l, const int64_t* need, const int64_t* need_offsets,
+                                int64_t num_need, int64_t num_steps, int64_t* cur_block,
+                                int64_t* cur_logical, int64_t* pos, int64_t num_seqs,
+                                int64_t block_size, int64_t* next_logical, int64_t* victims,
+                                int64_t* slot_mapping, int64_t* status, cudaStream_t stream);
 
 cudaError_t launch_wait_selftest(const uint32_t* flag, uint32_t from, int64_t* status,
                                  cudaStream_t stream);

@@ -48,7 +48,9 @@ __all__ = [
     "plan_load",
     "plan_save",
     "append_step",
+    "append_steps",
     "copy_tokens",
+    "scatter_tokens_gather_layers",
     "exchange_blocks",
     "batched_fused_single_layer_kv_transfer",
     "load_device_store",
@@ -469,6 +471,47 @@ def append_step(slot_meta: torch.Tensor, search_start: torch.Tensor, logical_to_
             _ptr(victims), _ptr(slot_mapping), _ptr(_bitmap(dev, n)), _ptr(_status(dev)), _stream(dev))
     _host_rc(rc, "append_step")
     _maybe_check(dev, check, "append_step")
+
+
+def append_steps(slot_meta: torch.Tensor, search_start: torch.Tensor, logical_to_physical: torch.Tensor,
+                 physical_to_logical: torch.Tensor, need: torch.Tensor, need_offsets: torch.Tensor,
+                 cur_block: torch.Tensor, cur_logical: torch.Tensor, pos: torch.Tensor, block_size: int,
+                 next_logical: torch.Tensor, victims: torch.Tensor, slot_mapping: torch.Tensor, *,
+                 order: str | None = None, check: bool | None = None) -> None:
+    """``need_offsets.numel() - 1`` decode steps of ``append_step`` in one
+    launch (see kvca_append_steps): step s serves the sequences
+    ``need[need_offsets[s]:need_offsets[s + 1]]``, its victims go to the same
+    positions of ``victims`` and its slot_mapping to ``slot_mapping[s]``
+    (shape ``(steps, seqs)``).  Equal to that many ``append_step`` calls; an
+    error at step s leaves the earlier steps done.  Nothing is read back:
+    capturable in a graph."""
+    for t, name in ((search_start, "search_start"), (logical_to_physical, "logical_to_physical"),
+                    (physical_to_logical, "physical_to_logical"), (need, "need"), (need_offsets, "need_offsets"),
+                    (cur_block, "cur_block"), (cur_logical, "cur_logical"), (pos, "pos"),
+                    (next_logical, "next_logical"), (victims, "victims"), (slot_mapping.reshape(-1), "slot_mapping")):
+        _require(t, torch.int64, name)
+    _require(slot_meta, _META_DTYPES, "slot_meta")
+    if not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be contiguous")
+    seqs = cur_block.numel()
+    steps = need_offsets.numel() - 1
+    if steps < 0:
+        raise ValueError("need_offsets needs one entry more than there are steps")
+    if cur_logical.numel() != seqs or pos.numel() != seqs or slot_mapping.numel() != steps * seqs:
+        raise ValueError("cur_block, cur_logical and pos need one entry per sequence, slot_mapping one per "
+                         "sequence and step")
+    if victims.numel() < need.numel():
+        raise ValueError("victims must hold one slot per entry of need")
+    dev = slot_meta.device
+    with _on(dev):
+        rc = _lib_handle.kvca_append_steps(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(slot_meta), slot_meta.numel(),
+            _ptr(search_start), _ptr(logical_to_physical), logical_to_physical.numel(), _ptr(physical_to_logical),
+            _ptr(need), _ptr(need_offsets), need.numel(), steps, _ptr(cur_block), _ptr(cur_logical), _ptr(pos),
+            seqs, int(block_size), _ptr(next_logical), _ptr(victims), _ptr(slot_mapping), _ptr(_status(dev)),
+            _stream(dev))
+    _host_rc(rc, "append_steps")
+    _maybe_check(dev, check, "append_steps")
 
 
 class LoadPlan:
@@ -960,6 +1003,42 @@ def scatter_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor, c
     _chunk_tensor(chunks, (nc, P, tpc, *pl.row_shape), pl.dtype, pl.device, "chunks")
     _launch_move("kvca_scatter", _chunk_desc(chunks, tpc, P, pl.row_bytes), pl.desc(slot_mapping),
                  P, t, pl.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE | _host_flag(chunks), pl.device, check)
+
+
+def scatter_tokens_gather_layers(token_caches, slot_mapping: torch.Tensor, chunks: torch.Tensor, block_caches,
+                                 slot_ids: torch.Tensor, out: torch.Tensor, *, tokens_per_chunk: int | None = None,
+                                 blocks_per_chunk: int | None = None, check: bool | None = None) -> None:
+    """``scatter_tokens(token_caches, slot_mapping, chunks)`` and
+    ``gather_layers(block_caches, slot_ids, out)`` in one launch
+    (kvca_scatter_gather).  The two moves must touch disjoint bytes: nothing
+    orders one before the other.  A decode step's token scatter and the spill
+    gather of the blocks the next step evicts (which this step does not
+    write) are such a pair."""
+    tp = _planes(token_caches, 2, "token_caches")
+    bp = _planes(block_caches, 1, "block_caches")
+    dev = tp.device
+    if bp.device != dev:
+        raise ValueError("token_caches and block_caches must be on one device")
+    _require_index(slot_mapping, dev, "slot_mapping")
+    _require_index(slot_ids, dev, "slot_ids")
+    t = slot_mapping.numel()
+    nc, tpc = _chunks_of(t, tokens_per_chunk, "len(slot_mapping)") if t else (0, max(1, tokens_per_chunk or 1))
+    P = len(tp.planes)
+    _chunk_tensor(chunks, (nc, P, tpc, *tp.row_shape), tp.dtype, dev, "chunks")
+    k = slot_ids.numel()
+    gc, cb = _chunks_of(k, blocks_per_chunk, "len(slot_ids)") if k else (0, max(1, blocks_per_chunk or 1))
+    Q = len(bp.planes)
+    _chunk_tensor(out, (gc, Q, cb, *bp.row_shape), bp.dtype, dev, "out")
+    if t == 0 and k == 0:
+        return
+    s_src, s_dst = _chunk_desc(chunks, tpc, P, tp.row_bytes), tp.desc(slot_mapping)
+    g_src, g_dst = bp.desc(slot_ids), _chunk_desc(out, cb, Q, bp.row_bytes)
+    with _on(dev):
+        rc = _lib_handle.kvca_scatter_gather(
+            ctypes.byref(s_src), ctypes.byref(s_dst), P, t, tp.row_bytes, ctypes.byref(g_src), ctypes.byref(g_dst),
+            Q, k, bp.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE, 0, _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "scatter_tokens_gather_layers")
+    _maybe_check(dev, check, "scatter_tokens_gather_layers")
 
 
 def copy_tokens(src_caches, src_mapping: torch.Tensor, dst_caches, dst_mapping: torch.Tensor, *,

@@ -209,11 +209,15 @@ class DecodeMix:
     search_start, the sequences' blocks and positions) and its own half of
     double-buffered victim and slot_mapping arrays, so it overlaps step i's
     gather and scatter, which touch only cache bytes; step i + 1's moves
-    still wait for its bookkeeping, and the moves stay in order on the
-    caller's stream (a block released at step i and popped at step i + 1 is
-    spilled after step i's scatter wrote its last token).  Step i's
-    bookkeeping waits for the moves of step i - 2, the last readers of the
-    buffer half it rewrites.  Results are the same bytes as unpipelined.
+    still wait for its bookkeeping.  Step i's bookkeeping waits for the
+    moves of step i - 2, the last readers of the buffer half it rewrites.
+    The moves stay in order on the caller's stream (a block released at step
+    i and popped at step i + 1 is spilled after step i's scatter wrote its
+    last token).  Results are the same bytes as unpipelined.  (Running the
+    spill gathers on a third stream, so that step i + 1's gather overlaps
+    step i's scatter, is safe, as the pop of a step precedes that step's
+    release, but was slower on B200: 36.9 against 29.3 us per step with 8
+    KV heads.)
     """
 
     def __init__(self, ops, device, *, layers: int = 32, heads: int = 1, head_dim: int = 128,
@@ -260,6 +264,20 @@ class DecodeMix:
         self.empty_ids = torch.empty(0, dtype=torch.int64, device=device)
         # one-launch bookkeeping when the op set has it (the CUDA module)
         self._append = getattr(ops, "append_step", None)
+        # whole-cycle booking (append_steps): a cycle = block_size steps, after
+        # which the fill positions repeat, so every sequence gets exactly one
+        # new block per cycle
+        self._append_many = getattr(ops, "append_steps", None)
+        self.cycle_victims = [torch.empty(seqs, dtype=torch.int64, device=device) for _ in range(2)]
+        self.cycle_slot_mapping = [torch.empty((block_size, seqs), dtype=torch.int64, device=device)
+                                   for _ in range(2)]
+        self._cycles_on = False
+        self._cycle_queue = []  # (buffer half, need offsets) of the cycles booked and not yet moved
+        self._cycle_half = 0
+        self._cycle_booked = self._cycle_moved = None
+        self._pair = getattr(ops, "scatter_tokens_gather_layers", None)
+        self._head_gathered = False  # the first gather of the next cycle to move went with the previous one
+        self._schedules = {}  # fill positions (bytes) -> (need, offsets on the device, offsets on the host)
         self.victims_bufs = [torch.empty(seqs, dtype=torch.int64, device=device) for _ in range(2)]
         self.slot_mapping_bufs = [torch.empty(seqs, dtype=torch.int64, device=device) for _ in range(2)]
         self._half = 0  # the buffer half of the next step
@@ -403,4 +421,167 @@ class DecodeMix:
         per_replay = self.evictions - counters[0]
         self.evictions, self.tokens, self.gathered_blocks = counters
         assert np.array_equal(self.pos, pos)  # a full cycle: the schedule repeats
+        return graph, per_replay
+
+    # ---- whole-cycle booking --------------------------------------------
+    #
+    # The bookkeeping of a step reads and writes only metadata, and which
+    # sequences need a block in the next block_size steps follows from the
+    # fill positions.  So one append_steps launch books a whole cycle (pop,
+    # commit, release and slot_mapping of each of its steps, in order), on
+    # the bookkeeping stream, one cycle ahead of the token moves: while the
+    # moves of cycle c run, cycle c + 1 is booked.  Victims and slot_mapping
+    # are double-buffered by cycle; cycle c + 1's booking waits for the moves
+    # of cycle c - 1, the last readers of its half.  The moves of each step
+    # (the spill gather of its victims, then its token scatter) stay in step
+    # order on the caller's stream, so every byte moved equals step-by-step.
+
+    def _cycle_schedule(self, pos: np.ndarray):
+        """Need lists of the block_size steps from fill positions `pos`, as
+        device tensors (cached: the schedule repeats every cycle)."""
+        key = pos.tobytes()
+        got = self._schedules.get(key)
+        if got is None:
+            pos = pos.copy()
+            ids, offs = [], [0]
+            for _ in range(self.block_size):
+                need = np.nonzero(pos == self.block_size)[0]
+                ids.append(need)
+                offs.append(offs[-1] + int(need.size))
+                pos[need] = 0
+                pos += 1
+            need_all = np.concatenate(ids).astype(np.int64)
+            got = (torch.tensor(need_all, device=self.device),
+                   torch.tensor(np.array(offs, np.int64), device=self.device), offs)
+            self._schedules[key] = got
+            # made on the caller's stream, read on the bookkeeping stream
+            self._book_stream.wait_stream(torch.cuda.current_stream(self.device))
+        return got
+
+    def start_cycles(self) -> None:
+        """Switch to whole-cycle booking and book the next cycle.  Call at a
+        step count that is a multiple of block_size, with the per-step
+        pipeline off."""
+        assert self._append_many is not None and self.device.type == "cuda" and not self._cycles_on
+        assert not self._pipelined
+        assert (self.pos >= 1).all()  # past the first step: the fill positions repeat every cycle
+        if self._book_stream is None:
+            self._book_stream = torch.cuda.Stream(self.device)
+            self._booked = [torch.cuda.Event() for _ in range(2)]
+            self._moved = [torch.cuda.Event() for _ in range(2)]
+        if self._cycle_booked is None:
+            self._cycle_booked = [torch.cuda.Event() for _ in range(2)]
+            self._cycle_moved = [torch.cuda.Event() for _ in range(2)]
+        self._book_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self._cycles_on = True
+        self._head_gathered = False
+        self._book_cycle()
+
+    def _book_cycle(self) -> None:
+        need, offsets, offs = self._cycle_schedule(self.pos)
+        h = self._cycle_half
+        self._cycle_half ^= 1
+        bs = self._book_stream
+        bs.wait_event(self._cycle_moved[h])  # the moves of the cycle two back read half h
+        with torch.cuda.stream(bs):
+            self._append_many(self.slot_meta, self.search_start, self.l2p, self.p2l, need, offsets,
+                              self.cur_block_dev, self.cur_logical_dev, self.pos_dev, self.block_size,
+                              self.next_logical_dev, self.cycle_victims[h][: offs[-1]],
+                              self.cycle_slot_mapping[h], check=False)
+            self._cycle_booked[h].record(bs)
+        self._cycle_queue.append((h, offs))
+
+    def _move_cycle(self, token_rows: torch.Tensor) -> None:
+        """The moves of the oldest booked cycle.  With the pair op, step i's
+        token scatter and step i + 1's spill gather go in one launch: the pop
+        of step i + 1 precedes its release, so its victims were unpinned
+        while step i wrote, and step i writes only its sequences' current,
+        pinned blocks.  The last scatter of the cycle takes the first gather
+        of the next cycle when that one is booked already."""
+        h, offs = self._cycle_queue.pop(0)
+        cur = torch.cuda.current_stream(self.device)
+        cur.wait_event(self._cycle_booked[h])
+        victims, slot_mapping = self.cycle_victims[h], self.cycle_slot_mapping[h]
+        pair = self._pair
+        if pair is None or not self._head_gathered:
+            a, b = offs[0], offs[1]
+            if b > a:
+                self.ops.gather_layers(self.block_table, victims[a:b], self.spill[: b - a], blocks_per_chunk=1,
+                                       check=False)
+        self._head_gathered = False
+        for step in range(self.block_size):
+            if pair is None:
+                if step > 0 and offs[step + 1] > offs[step]:
+                    a, b = offs[step], offs[step + 1]
+                    self.ops.gather_layers(self.block_table, victims[a:b], self.spill[: b - a],
+                                           blocks_per_chunk=1, check=False)
+                self.ops.scatter_tokens(self.token_table, slot_mapping[step], token_rows,
+                                        tokens_per_chunk=self.seqs, check=False)
+                continue
+            if step + 1 < self.block_size:  # with the next step's gather
+                nv = victims[offs[step + 1]:offs[step + 2]]
+            elif self._cycle_queue:  # with the next cycle's first gather
+                nh, noffs = self._cycle_queue[0]
+                cur.wait_event(self._cycle_booked[nh])
+                nv = self.cycle_victims[nh][noffs[0]:noffs[1]]
+                self._head_gathered = True
+            else:
+                nv = self.empty_ids
+            pair(self.token_table, slot_mapping[step], token_rows, self.block_table, nv,
+                 self.spill[: nv.numel()], tokens_per_chunk=self.seqs, blocks_per_chunk=1, check=False)
+        self._cycle_moved[h].record(cur)
+        self.evictions += offs[-1]
+        self.gathered_blocks += offs[-1]
+        self.tokens += self.block_size * self.seqs
+
+    def run_cycle(self, token_rows: torch.Tensor) -> None:
+        """Book the cycle after the next one's moves, then enqueue the next
+        cycle's moves (block_size steps, each with the same token rows)."""
+        assert self._cycles_on
+        self._book_cycle()
+        self._move_cycle(token_rows)
+
+    def stop_cycles(self, token_rows: torch.Tensor) -> None:
+        """Move the cycle booked ahead and leave whole-cycle booking: the
+        state then equals that of the same number of single steps."""
+        assert self._cycles_on
+        self._move_cycle(token_rows)
+        assert not self._cycle_queue
+        torch.cuda.current_stream(self.device).wait_stream(self._book_stream)
+        self._cycles_on = False
+
+    def capture_cycles(self, token_rows: torch.Tensor):
+        """Capture two cycles of ``run_cycle`` (the buffer halves alternate by
+        cycle, so a replay ends on the half it started from) into a CUDA
+        graph: within a replay the booking of each next cycle overlaps the
+        moves of the current one.  The schedule's tensors must exist (run a
+        cycle eagerly first).  Replays must be issued on the caller's stream
+        after anything else on the bookkeeping stream; returns (graph,
+        evictions per replay)."""
+        assert self._cycles_on
+        counters = (self.evictions, self.tokens, self.gathered_blocks)
+        queue, half, head = list(self._cycle_queue), self._cycle_half, self._head_gathered
+        cur = torch.cuda.current_stream(self.device)
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(cur)
+        stream.wait_stream(self._book_stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                # fork the bookkeeping stream; the booked cycle and the moved
+                # ones before the replay are done when it starts
+                for ev in self._cycle_booked + self._cycle_moved:
+                    ev.record(stream)
+                self._book_stream.wait_stream(stream)
+                for _ in range(2):
+                    self.run_cycle(token_rows)
+                stream.wait_stream(self._book_stream)
+        cur.wait_stream(stream)
+        self._book_stream.wait_stream(cur)
+        for ev in self._cycle_booked + self._cycle_moved:  # later eager cycles wait on real records
+            ev.record(cur)
+        per_replay = self.evictions - counters[0]
+        self.evictions, self.tokens, self.gathered_blocks = counters
+        assert self._cycle_half == half and [q[0] for q in self._cycle_queue] == [q[0] for q in queue]
+        assert self._head_gathered == head
         return graph, per_replay

@@ -15,6 +15,8 @@ from kv_cache_adapter_b200.workloads import DecodeMix
 from oracle_ops import OracleOps
 
 SMALL = dict(layers=2, heads=2, head_dim=32, block_size=16, num_blocks=256, seqs=48, max_steps=200)
+# more sequences needing a block in one step than the bookkeeping CTA has threads
+WIDE = dict(layers=1, heads=1, head_dim=16, block_size=4, num_blocks=8192, seqs=1500, max_steps=60)
 
 
 def _rows(step: int, mix: DecodeMix) -> torch.Tensor:
@@ -28,11 +30,18 @@ def test_decode_mix_host_logic_on_cpu():
     pins0 = int(((mix.slot_meta & 15) != 0).sum())
     assert pins0 == SMALL["seqs"]
     total_new = 0
+    written = set()  # blocks the previous step's scatter wrote
     for step in range(120):
-        need = mix.need_new_blocks().size
+        need_set = mix.need_new_blocks()
+        need = need_set.size
         spill = mix.step(_rows(step, mix))
         assert spill.shape[0] == need
         total_new += need
+        # this step's victims were not written by the previous step's scatter
+        # (the pop of a step precedes its release of the full blocks)
+        victims = set(mix.cur_block_dev[torch.from_numpy(need_set)].tolist())
+        assert not victims & written, step
+        written = set(mix.cur_block_dev.tolist())
         # one pinned block per sequence, all of them distinct
         pinned = torch.nonzero((mix.slot_meta & 15) != 0).flatten().sort().values
         assert torch.equal(pinned, mix.cur_block_dev.sort().values)
@@ -43,19 +52,22 @@ def test_decode_mix_host_logic_on_cpu():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("pipelined", [False, True])
-def test_decode_mix_matches_oracle_step_by_step(pipelined):
+@pytest.mark.parametrize("pipelined,cfg", [(False, SMALL), (True, SMALL), (True, WIDE)])
+def test_decode_mix_matches_oracle_step_by_step(pipelined, cfg):
     """Unpipelined, and with each step's bookkeeping on its own stream
     overlapping the previous step's moves: identical bytes either way."""
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda as cuda_ops
 
     dev = torch.device("cuda", 0)
-    gpu = DecodeMix(cuda_ops, dev, **SMALL)
+    gpu = DecodeMix(cuda_ops, dev, **cfg)
     gpu.pipelined = pipelined
     assert gpu.pipelined == pipelined
-    cpu = DecodeMix(OracleOps(), torch.device("cpu"), **SMALL)
+    cpu = DecodeMix(OracleOps(), torch.device("cpu"), **cfg)
     cpu.kv.copy_(gpu.kv.cpu())
-    for step in range(150):
+    steps = min(150, cfg["max_steps"])
+    wide = 0
+    for step in range(steps):
+        wide = max(wide, cpu.need_new_blocks().size)
         rows = _rows(step, cpu)
         spill_g = gpu.step(rows.to(dev), check=True)
         spill_c = cpu.step(rows)
@@ -68,6 +80,8 @@ def test_decode_mix_matches_oracle_step_by_step(pipelined):
     assert gpu._append is not None  # the one-launch bookkeeping ran on the GPU
     assert torch.equal(gpu.kv.cpu().view(torch.int16), cpu.kv.view(torch.int16))
     assert gpu.evictions == cpu.evictions > 100
+    if cfg is WIDE:
+        assert wide > 256
 
 
 @pytest.mark.gpu
@@ -128,4 +142,133 @@ def test_append_step_errors_change_nothing():
     for before, after in zip(state, (mix.slot_meta, mix.l2p, mix.p2l, mix.search_start, mix.cur_block_dev,
                                      mix.cur_logical_dev, mix.pos_dev, mix.next_logical_dev)):
         assert torch.equal(before, after)
+    ops.check_status(dev)
+
+
+def _state(mix: DecodeMix):
+    return [t.clone() for t in (mix.kv, mix.slot_meta, mix.l2p, mix.p2l, mix.search_start, mix.cur_block_dev,
+                                mix.cur_logical_dev, mix.pos_dev, mix.next_logical_dev)]
+
+
+def _assert_same_state(a: DecodeMix, b: DecodeMix):
+    torch.cuda.synchronize()
+    for x, y in zip(_state(a), _state(b)):
+        assert torch.equal(x.view(torch.uint8) if x.dtype != torch.int64 else x,
+                           y.view(torch.uint8) if y.dtype != torch.int64 else y)
+    assert (a.evictions, a.tokens) == (b.evictions, b.tokens)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cfg", [SMALL, WIDE])
+def test_cycle_booking_matches_single_steps(cfg):
+    """Whole-cycle booking (one append_steps launch per cycle, one cycle ahead
+    of the moves), eager and replayed from a graph, leaves the same cache
+    bytes and metadata as the same number of single unpipelined steps."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as cuda_ops
+
+    dev = torch.device("cuda", 0)
+    bs = cfg["block_size"]
+    ref = DecodeMix(cuda_ops, dev, **cfg)
+    cyc = DecodeMix(cuda_ops, dev, **cfg)
+    rows = _rows(0, ref).to(dev)
+    for _ in range(bs + 1):  # past the first step: positions periodic
+        ref.step(rows)
+        cyc.step(rows)
+    cyc.start_cycles()
+    cyc.run_cycle(rows)
+    cyc.run_cycle(rows)
+    cyc.stop_cycles(rows)
+    for _ in range(3 * bs):
+        ref.step(rows)
+    _assert_same_state(ref, cyc)
+    # graph replays of two cycles each, then single steps again
+    cyc.start_cycles()
+    cyc.run_cycle(rows)
+    graph, per_replay = cyc.capture_cycles(rows)
+    assert per_replay == 2 * cfg["seqs"]
+    replays = 2 if cfg is SMALL else 1
+    for _ in range(replays):
+        graph.replay()
+    cyc.stop_cycles(rows)
+    for _ in range(3):
+        cyc.step(rows)
+    for _ in range((2 + 2 * replays) * bs + 3):
+        ref.step(rows)
+    torch.cuda.synchronize()
+    cuda_ops.check_status(dev)
+    cyc.evictions += replays * per_replay  # graph replays are not counted on the host
+    cyc.tokens += replays * 2 * bs * cfg["seqs"]
+    _assert_same_state(ref, cyc)
+
+
+@pytest.mark.gpu
+def test_append_steps_equals_single_steps_across_launches():
+    """300 steps in one append_steps call (two launches of at most 256 steps)
+    against 300 append_step calls: victims, slot mappings and state."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+
+    dev = torch.device("cuda", 0)
+    cfg = dict(layers=1, heads=1, head_dim=8, block_size=4, num_blocks=2048, seqs=100, max_steps=320)
+    a = DecodeMix(ops, dev, **cfg)
+    b = DecodeMix(ops, dev, **cfg)
+    steps = 300
+    pos = a.pos.copy()
+    needs, offs = [], [0]
+    for _ in range(steps):
+        need = np.nonzero(pos == cfg["block_size"])[0]
+        needs.append(need)
+        offs.append(offs[-1] + need.size)
+        pos[need] = 0
+        pos += 1
+    need_all = torch.tensor(np.concatenate(needs), dtype=torch.int64, device=dev)
+    offsets = torch.tensor(offs, dtype=torch.int64, device=dev)
+    victims = torch.full((offs[-1],), -1, dtype=torch.int64, device=dev)
+    sm = torch.full((steps, cfg["seqs"]), -1, dtype=torch.int64, device=dev)
+    ops.append_steps(a.slot_meta, a.search_start, a.l2p, a.p2l, need_all, offsets, a.cur_block_dev,
+                     a.cur_logical_dev, a.pos_dev, a.block_size, a.next_logical_dev, victims, sm, check=True)
+    for s in range(steps):
+        v = torch.empty(offs[s + 1] - offs[s], dtype=torch.int64, device=dev)
+        one = torch.empty(cfg["seqs"], dtype=torch.int64, device=dev)
+        ops.append_step(b.slot_meta, b.search_start, b.l2p, b.p2l, need_all[offs[s]:offs[s + 1]], b.cur_block_dev,
+                        b.cur_logical_dev, b.pos_dev, b.block_size, b.next_logical_dev, v, one, check=True)
+        assert torch.equal(v, victims[offs[s]:offs[s + 1]]), s
+        assert torch.equal(one, sm[s]), s
+    for x, y in zip(_state(a)[1:], _state(b)[1:]):
+        assert torch.equal(x, y)
+    assert offs[-1] > cfg["num_blocks"] // 4  # enough evictions to age the table
+
+
+@pytest.mark.gpu
+def test_append_steps_errors():
+    """Bad offsets change nothing; too few reusable slots at step s leave the
+    earlier steps done and step s unchanged."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+    from kv_cache_adapter_b200.errors import InsufficientCapacityError
+
+    dev = torch.device("cuda", 0)
+    cfg = dict(layers=1, heads=1, head_dim=8, block_size=4, num_blocks=64, seqs=8, max_steps=64)
+    mix = DecodeMix(ops, dev, **cfg)
+    state = _state(mix)
+    need = torch.arange(8, dtype=torch.int64, device=dev)
+    victims = torch.empty(8, dtype=torch.int64, device=dev)
+    sm = torch.empty((2, 8), dtype=torch.int64, device=dev)
+    args = (mix.slot_meta, mix.search_start, mix.l2p, mix.p2l, need)
+    tail = (mix.cur_block_dev, mix.cur_logical_dev, mix.pos_dev, mix.block_size, mix.next_logical_dev, victims, sm)
+    for bad in ([0, 5, 3], [0, 3, 9], [-1, 2, 4]):  # decreasing, past the need list, negative
+        with pytest.raises(IndexError):
+            ops.append_steps(*args, torch.tensor(bad, dtype=torch.int64, device=dev), *tail, check=True)
+    for before, after in zip(state, _state(mix)):
+        assert torch.equal(before, after)
+    # all but 3 unpinned slots pinned: step 0 takes those 3 and releases the
+    # 3 full blocks; step 1 needs 5
+    meta = mix.slot_meta.clone()
+    free = torch.nonzero((meta & 15) == 0).flatten()
+    keep = free[:3]
+    pinned = meta | 1
+    pinned[keep] = meta[keep]
+    mix.slot_meta.copy_(pinned)
+    with pytest.raises(InsufficientCapacityError):
+        ops.append_steps(*args, torch.tensor([0, 3, 8], dtype=torch.int64, device=dev), *tail, check=True)
+    assert set(victims[:3].tolist()) == set(keep.tolist())
+    assert int(mix.next_logical_dev[0]) == int(state[-1][0]) + 3  # step 0 committed, step 1 not
     ops.check_status(dev)
