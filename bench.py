@@ -668,7 +668,38 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
                         "issue": "one Python call per op, one stream"},
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_mix(heads, rows.cpu())
     print(json.dumps(line), flush=True)
+
+
+def cpu_decode_mix(heads: int, rows: torch.Tensor, steps: int = 32) -> dict:
+    """The decode mix's steps through the same driver on CPU tensors with the
+    oracle op set (the reference's strict pop / commit / release restated,
+    torch CPU indexing for the moves), on a smaller pool (the per-step moves
+    are the same; the pool only sets how far the sweep scans)."""
+    sys.path.insert(0, str(REPO / "tests"))
+    from oracle_ops import OracleOps
+    from kv_cache_adapter_b200.workloads import DecodeMix
+
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    pool = 8192 if heads == 1 else 1024
+    mix = DecodeMix(OracleOps(), torch.device("cpu"), layers=32, heads=heads, head_dim=128, block_size=16,
+                    num_blocks=pool, seqs=256, dtype=torch.float16, seed=1234, max_steps=17 + steps + 16)
+    for _ in range(17):
+        mix.step(rows)
+    tok0, blk0 = mix.tokens, mix.gathered_blocks
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        mix.step(rows)
+    dt = time.perf_counter() - t0
+    row_bytes = heads * 128 * 2
+    moved = 2 * mix.num_planes * ((mix.tokens - tok0) * row_bytes + (mix.gathered_blocks - blk0) * row_bytes * 16)
+    return {"value": round(moved / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "ms_per_decode_step": round(dt / steps * 1e3, 3),
+            "sample": f"{steps} decode steps of the same shapes (256 sequences, 32 layers x K/V, {heads} KV head(s)) "
+                      f"on a {pool:,}-block pool, CPU tensors, oracle op set (strict-path restatement) and torch "
+                      f"CPU indexing"}
 
 
 ADAPTER_CONFIG = dict(num_actual=256, num_logical=1024, batch=32, block=128, hit_rates=(0.0, 0.5, 1.0))
