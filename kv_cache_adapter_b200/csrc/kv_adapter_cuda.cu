@@ -2473,10 +2473,16 @@ __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta,
 
 static_assert(kMoverThreads == kRowStreamThreads, "the pair kernel runs every body at one CTA size");
 
-// a: a scatter (chunk -> paged), b: a gather (paged -> chunk)
+// a: a scatter (chunk -> paged), b: a gather (paged -> chunk).  Launched as
+// a programmatic dependent of the kernel before it on the stream: the launch
+// and the CTAs' dispatch may overlap that kernel's last CTAs, and every CTA
+// waits (griddepcontrol.wait: that grid complete, its writes visible)
+// before touching memory, then lets the next pair launch start early.
 template <MoverBody kA, MoverBody kB>
 __global__ void __launch_bounds__(kMoverThreads)
     move_pair_kernel(const __grid_constant__ MoveParams a, const __grid_constant__ MoveParams b, int split) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (static_cast<int>(blockIdx.x) < split)
     run_mover_body<kA, false, true>(a, blockIdx.x, split);
   else
@@ -2981,8 +2987,18 @@ MoverBody pair_body(MoveParams* p, int64_t* ctas_wanted) {
 template <MoverBody kA, MoverBody kB>
 cudaError_t launch_pair_typed(const MoveParams& a, const MoveParams& b, int split, int grid,
                               cudaStream_t stream) {
-  move_pair_kernel<kA, kB><<<static_cast<unsigned>(grid), kMoverThreads, 0, stream>>>(a, b, split);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kMoverThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, move_pair_kernel<kA, kB>, a, b, split);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <MoverBody kA>
