@@ -22,6 +22,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <utility>
+
 #include "kvca_launch.h"
 
 namespace kvca {
@@ -1835,6 +1837,15 @@ __global__ void __launch_bounds__(kAppendThreads)
                           victims, slot_mapping, status, sh);
 }
 
+// Per-sequence state (block, logical id, position) of up to kAppendSmemSeqs
+// sequences, and up to kAppendSmemNeed need entries, live in shared memory
+// for the whole launch: a step's dependent chain is then l2p of the full
+// blocks -> metadata tile -> p2l / full-block words, three global round
+// trips instead of five.
+constexpr int64_t kAppendSmemSeqs = 4096;
+constexpr int64_t kAppendSmemNeed = 4096;
+constexpr size_t kAppendSmemBytes = (3 * kAppendSmemSeqs + kAppendSmemNeed) * sizeof(int64_t);
+
 // num_steps steps in a row in one CTA: step s takes need[off[s]..off[s+1]),
 // writes its victims to victims[off[s]..] and its slot_mapping to
 // slot_mapping[s * seqs..], exactly as num_steps append_step launches would.
@@ -1849,9 +1860,10 @@ __global__ void __launch_bounds__(kAppendThreads)
                         const int64_t* need_offsets, int64_t num_need, int64_t num_steps,
                         int64_t* cur_block, int64_t* cur_logical, int64_t* pos, int64_t seqs,
                         int64_t block_size, int64_t* next_logical, int order, bool aligned,
-                        int64_t* victims, int64_t* slot_mapping, int64_t* status) {
+                        int64_t* victims, int64_t* slot_mapping, int64_t* status, bool staged) {
   __shared__ AppendShared<MetaT> sh;
   __shared__ int64_t off[kAppendMaxSteps + 1];
+  extern __shared__ int64_t dyn[];  // staged: block | logical id | position (seqs each), need entries
   bool bad = false;
   for (int64_t s = threadIdx.x; s <= num_steps; s += blockDim.x) {
     const int64_t o = need_offsets[s];
@@ -1873,14 +1885,44 @@ __global__ void __launch_bounds__(kAppendThreads)
     if (threadIdx.x == 0) report(status, KVCA_ERR_BAD_INDEX, sh.bad_value);
     return;
   }
+  int64_t* cb = cur_block;
+  int64_t* cl = cur_logical;
+  int64_t* ps = pos;
+  const int64_t* nd = need;
+  int64_t nd_base = 0;
+  if (staged) {  // seqs <= kAppendSmemSeqs: the launch sized dyn for it
+    cb = dyn;
+    cl = dyn + seqs;
+    ps = dyn + 2 * seqs;
+    for (int64_t q = threadIdx.x; q < seqs; q += blockDim.x) {
+      cb[q] = cur_block[q];
+      cl[q] = cur_logical[q];
+      ps[q] = pos[q];
+    }
+    const int64_t total = off[num_steps] - off[0];
+    if (total <= kAppendSmemNeed) {
+      int64_t* sn = dyn + 3 * seqs;
+      for (int64_t j = threadIdx.x; j < total; j += blockDim.x) sn[j] = need[off[0] + j];
+      nd = sn;
+      nd_base = off[0];
+    }
+    __syncthreads();
+  }
   for (int64_t s = 0; s < num_steps; ++s) {
     const int64_t o = off[s];
-    const int rc = append_step_body<MetaT>(meta, n, search_start, l2p, n_logical, p2l, need + o,
-                                           off[s + 1] - o, cur_block, cur_logical, pos, seqs,
+    const int rc = append_step_body<MetaT>(meta, n, search_start, l2p, n_logical, p2l,
+                                           nd + (o - nd_base), off[s + 1] - o, cb, cl, ps, seqs,
                                            block_size, next_logical, order, aligned, victims + o,
                                            slot_mapping + s * seqs, status, sh);
-    if (rc != KVCA_OK) return;
     __syncthreads();
+    if (rc != KVCA_OK) break;  // uniform across the CTA
+  }
+  if (staged) {
+    for (int64_t q = threadIdx.x; q < seqs; q += blockDim.x) {
+      cur_block[q] = cb[q];
+      cur_logical[q] = cl[q];
+      pos[q] = ps[q];
+    }
   }
 }
 
@@ -2163,6 +2205,21 @@ __device__ __forceinline__ void move_rows_body(const MoveParams& p, int64_t cta,
       }
     }
   }
+}
+
+// Entry of a kernel launched as a programmatic dependent of the kernel
+// before it on its stream (launch_dependent): its CTAs may be dispatched
+// while that kernel drains, wait for it (griddepcontrol.wait: the grid
+// complete, its writes visible) before touching memory, and then let the
+// next launch start dispatching.  Without a programmatic predecessor the
+// wait returns at once.  Only the pair mover launches this way: its
+// consecutive launches are short and latency-bound (a decode step), while
+// early-resident CTAs of large moves took the SMs that a concurrent kernel
+// on another stream needed (decode mix, 8 KV heads: 39.6 against 29.6 us
+// per step, the cycle booking starved).
+__device__ __forceinline__ void dependent_launch_entry() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost>
@@ -2473,21 +2530,36 @@ __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta,
 
 static_assert(kMoverThreads == kRowStreamThreads, "the pair kernel runs every body at one CTA size");
 
-// a: a scatter (chunk -> paged), b: a gather (paged -> chunk).  Launched as
-// a programmatic dependent of the kernel before it on the stream: the launch
-// and the CTAs' dispatch may overlap that kernel's last CTAs, and every CTA
-// waits (griddepcontrol.wait: that grid complete, its writes visible)
-// before touching memory, then lets the next pair launch start early.
+// a: a scatter (chunk -> paged), b: a gather (paged -> chunk); launched as a
+// programmatic dependent (dependent_launch_entry).
 template <MoverBody kA, MoverBody kB>
 __global__ void __launch_bounds__(kMoverThreads)
     move_pair_kernel(const __grid_constant__ MoveParams a, const __grid_constant__ MoveParams b, int split) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  dependent_launch_entry();
   if (static_cast<int>(blockIdx.x) < split)
     run_mover_body<kA, false, true>(a, blockIdx.x, split);
   else
     run_mover_body<kB, true, false>(b, static_cast<int64_t>(blockIdx.x) - split,
                                     static_cast<int64_t>(gridDim.x) - split);
+}
+
+// Launch as a programmatic dependent of the kernel before it on the stream
+// (the kernel must begin with dependent_launch_entry()).
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(Params...), unsigned grid, unsigned block, size_t smem,
+                             cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 int device_sm_count() {
@@ -2987,18 +3059,8 @@ MoverBody pair_body(MoveParams* p, int64_t* ctas_wanted) {
 template <MoverBody kA, MoverBody kB>
 cudaError_t launch_pair_typed(const MoveParams& a, const MoveParams& b, int split, int grid,
                               cudaStream_t stream) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kMoverThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, move_pair_kernel<kA, kB>, a, b, split);
-  return e != cudaSuccess ? e : cudaGetLastError();
+  return launch_dependent(move_pair_kernel<kA, kB>, static_cast<unsigned>(grid), kMoverThreads, 0, stream, a,
+                          b, split);
 }
 
 template <MoverBody kA>
@@ -3265,15 +3327,28 @@ cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t nu
                                 int64_t block_size, int64_t* next_logical, int64_t* victims,
                                 int64_t* slot_mapping, int64_t* status, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(append_steps_kernel<uint8_t>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kAppendSmemBytes));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(append_steps_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kAppendSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const bool staged = num_seqs <= kAppendSmemSeqs;
+  const size_t smem = staged ? static_cast<size_t>(3 * num_seqs + kAppendSmemNeed) * sizeof(int64_t) : 0;
   // launches of at most kAppendMaxSteps steps, in stream order
   for (int64_t s0 = 0; s0 < num_steps; s0 += kAppendMaxSteps) {
     const int64_t k = num_steps - s0 < kAppendMaxSteps ? num_steps - s0 : kAppendMaxSteps;
-    KVCA_META_DISPATCH(meta_bits, append_steps_kernel<MetaT><<<1, kAppendThreads, 0, stream>>>(
+    KVCA_META_DISPATCH(meta_bits, append_steps_kernel<MetaT><<<1, kAppendThreads, smem, stream>>>(
                                       static_cast<MetaT*>(meta), num_slots, search_start, l2p,
                                       num_logical, p2l, need, need_offsets + s0, num_need, k,
                                       cur_block, cur_logical, pos, num_seqs, block_size,
                                       next_logical, order, aligned, victims,
-                                      slot_mapping + s0 * num_seqs, status));
+                                      slot_mapping + s0 * num_seqs, status, staged));
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

@@ -17,6 +17,8 @@ from oracle_ops import OracleOps
 SMALL = dict(layers=2, heads=2, head_dim=32, block_size=16, num_blocks=256, seqs=48, max_steps=200)
 # more sequences needing a block in one step than the bookkeeping CTA has threads
 WIDE = dict(layers=1, heads=1, head_dim=16, block_size=4, num_blocks=8192, seqs=1500, max_steps=60)
+# more sequences than the multi-step booking keeps in shared memory
+HUGE = dict(layers=1, heads=1, head_dim=8, block_size=4, num_blocks=16384, seqs=5000, max_steps=40)
 
 
 def _rows(step: int, mix: DecodeMix) -> torch.Tensor:
@@ -159,7 +161,7 @@ def _assert_same_state(a: DecodeMix, b: DecodeMix):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("cfg", [SMALL, WIDE])
+@pytest.mark.parametrize("cfg", [SMALL, WIDE, HUGE])
 def test_cycle_booking_matches_single_steps(cfg):
     """Whole-cycle booking (one append_steps launch per cycle, one cycle ahead
     of the moves), eager and replayed from a graph, leaves the same cache
