@@ -63,6 +63,14 @@ typedef struct CUstream_st* kvca_stream_t; /* same type as cudaStream_t */
  * kvca_host_memory_usable): rows move with plain SIMT loads and stores over
  * the host link, never with bulk copies. */
 #define KVCA_FLAG_HOST_MEMORY 2
+/* kvca_scatter_gather only (given in both flag words): no kernel that may
+ * still run when this launch starts writes the scatter's source rows or
+ * either index array; in a chain of kvca_scatter_gather launches on one
+ * stream, none of them writes them (they were produced before the chain, or
+ * on another stream the chain waited for).  The launch then reads them
+ * while the launches before it drain, and only its reads of paged rows and
+ * its stores wait for those. */
+#define KVCA_FLAG_INPUTS_READY 4
 
 /* Upper bound on planes per row-mover call. */
 #define KVCA_MAX_PLANES 256

@@ -27,6 +27,7 @@ KVCA_POP_ORDER_PREFIX = 1
 
 KVCA_FLAG_SKIP_NEGATIVE = 1
 KVCA_FLAG_HOST_MEMORY = 2
+KVCA_FLAG_INPUTS_READY = 4
 KVCA_MAX_PLANES = 256
 
 c_i64 = ctypes.c_int64

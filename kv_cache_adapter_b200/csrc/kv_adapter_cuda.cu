@@ -2132,7 +2132,13 @@ constexpr int64_t kMoverSegmentBytes = 16384;
 // The movers' bodies take the CTA's index and the CTA count of the work
 // split (blockIdx.x and gridDim.x for a launch of their own), so that one
 // launch can also split its CTAs between two moves (move_pair_kernel).
-template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost>
+// kEarly (pair mover, inputs ready): the body itself waits for the launch's
+// programmatic predecessor (grid_dependency_wait) after its index loads and
+// before any load of paged rows or any store; loads of a chunk source may
+// come before it too (stream and small-row bodies).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost, bool kEarly = false>
 __device__ __forceinline__ void move_rows_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int tpr = 1 << p.tpr_log2;
@@ -2168,6 +2174,7 @@ __device__ __forceinline__ void move_rows_body(const MoveParams& p, int64_t cta,
       dst_row = kDstPaged ? paged_row_offset(p.dst_paged, r, p.flags, p.status, lead)
                           : chunk_row_offset(p.dst_chunk, r);
     }
+    if constexpr (kEarly) grid_dependency_wait();
     if (src_row >= 0 && dst_row >= 0) {
       const V* src = reinterpret_cast<const V*>(
           kSrcPaged ? p.src_paged.planes[pl] + src_row
@@ -2275,7 +2282,7 @@ __device__ __forceinline__ int pow2_shift(int64_t v) {
 // 5.7 / 5.7 TB/s, against 4.9 / 4.7 for the SIMT mover's shape (four lanes
 // of four vectors, one row at a time: every instruction touches half-lines
 // of eight rows).
-template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows>
+template <bool kSrcPaged, bool kDstPaged, int kVpl, int kRows, bool kEarly = false>
 __device__ __forceinline__ void move_short_rows_pm_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int tpr = 1 << p.tpr_log2;
@@ -2355,6 +2362,7 @@ __device__ __forceinline__ void move_short_rows_pm_body(const MoveParams& p, int
       }
     }
     uint4 buf[kRows][kVpl];
+    if constexpr (kEarly && kSrcPaged) grid_dependency_wait();
 #pragma unroll
     for (int u = 0; u < kRows; ++u)
 #pragma unroll
@@ -2362,6 +2370,7 @@ __device__ __forceinline__ void move_short_rows_pm_body(const MoveParams& p, int
         const int i = lane + j * tpr;
         if (src[u] != nullptr && i < row_vecs) buf[u][j] = ld_stream(src[u] + i);
       }
+    if constexpr (kEarly && !kSrcPaged) grid_dependency_wait();
 #pragma unroll
     for (int u = 0; u < kRows; ++u)
 #pragma unroll
@@ -2397,7 +2406,7 @@ __global__ void __launch_bounds__(kMoverThreads) move_short_rows_pm_kernel(const
 constexpr int kRowStreamThreads = 512;
 constexpr int kRowStreamSlots = 9;
 
-template <bool kSrcPaged, bool kDstPaged>
+template <bool kSrcPaged, bool kDstPaged, bool kEarly = false>
 __device__ __forceinline__ void move_rows_stream_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int lane = static_cast<int>(threadIdx.x & 31);
@@ -2477,6 +2486,7 @@ __device__ __forceinline__ void move_rows_stream_body(const MoveParams& p, int64
     uint4 buf[kRowStreamSlots];
     int row = row0;
     int vec = vec0;
+    if constexpr (kEarly && kSrcPaged) grid_dependency_wait();
 #pragma unroll
     for (int k = 0; k < kRowStreamSlots; ++k) {
       const uint64_t sb = __shfl_sync(0xffffffffu, my_src, row & 31);
@@ -2488,6 +2498,7 @@ __device__ __forceinline__ void move_rows_stream_body(const MoveParams& p, int64
         ++row;
       }
     }
+    if constexpr (kEarly && !kSrcPaged) grid_dependency_wait();
     row = row0;
     vec = vec0;
 #pragma unroll
@@ -2518,29 +2529,36 @@ __global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(con
 // bytes.
 enum class MoverBody : int { kSimt = 0, kStream = 1, kSmall = 2 };
 
-template <MoverBody kBody, bool kSrcPaged, bool kDstPaged>
+template <MoverBody kBody, bool kSrcPaged, bool kDstPaged, bool kEarly>
 __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if constexpr (kBody == MoverBody::kStream)
-    move_rows_stream_body<kSrcPaged, kDstPaged>(p, cta, ctas);
+    move_rows_stream_body<kSrcPaged, kDstPaged, kEarly>(p, cta, ctas);
   else if constexpr (kBody == MoverBody::kSmall)
-    move_short_rows_pm_body<kSrcPaged, kDstPaged, 2, 4>(p, cta, ctas);
+    move_short_rows_pm_body<kSrcPaged, kDstPaged, 2, 4, kEarly>(p, cta, ctas);
   else
-    move_rows_body<kSrcPaged, kDstPaged, uint4, false>(p, cta, ctas);
+    move_rows_body<kSrcPaged, kDstPaged, uint4, false, kEarly>(p, cta, ctas);
 }
 
 static_assert(kMoverThreads == kRowStreamThreads, "the pair kernel runs every body at one CTA size");
 
 // a: a scatter (chunk -> paged), b: a gather (paged -> chunk); launched as a
-// programmatic dependent (dependent_launch_entry).
-template <MoverBody kA, MoverBody kB>
+// programmatic dependent.  kEarly (KVCA_FLAG_INPUTS_READY: the index arrays
+// and the scatter's source rows were complete before the previous kernel on
+// the stream started): the next launch is let in at once, and the bodies
+// load indices and chunk rows before waiting for the previous grid, so only
+// the paged loads and the stores wait.  Otherwise everything waits.
+template <MoverBody kA, MoverBody kB, bool kEarly>
 __global__ void __launch_bounds__(kMoverThreads)
     move_pair_kernel(const __grid_constant__ MoveParams a, const __grid_constant__ MoveParams b, int split) {
-  dependent_launch_entry();
-  if (static_cast<int>(blockIdx.x) < split)
-    run_mover_body<kA, false, true>(a, blockIdx.x, split);
+  if constexpr (kEarly)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   else
-    run_mover_body<kB, true, false>(b, static_cast<int64_t>(blockIdx.x) - split,
-                                    static_cast<int64_t>(gridDim.x) - split);
+    dependent_launch_entry();
+  if (static_cast<int>(blockIdx.x) < split)
+    run_mover_body<kA, false, true, kEarly>(a, blockIdx.x, split);
+  else
+    run_mover_body<kB, true, false, kEarly>(b, static_cast<int64_t>(blockIdx.x) - split,
+                                            static_cast<int64_t>(gridDim.x) - split);
 }
 
 // Launch as a programmatic dependent of the kernel before it on the stream
@@ -3057,19 +3075,22 @@ MoverBody pair_body(MoveParams* p, int64_t* ctas_wanted) {
 }
 
 template <MoverBody kA, MoverBody kB>
-cudaError_t launch_pair_typed(const MoveParams& a, const MoveParams& b, int split, int grid,
+cudaError_t launch_pair_typed(const MoveParams& a, const MoveParams& b, int split, int grid, bool early,
                               cudaStream_t stream) {
-  return launch_dependent(move_pair_kernel<kA, kB>, static_cast<unsigned>(grid), kMoverThreads, 0, stream, a,
-                          b, split);
+  if (early)
+    return launch_dependent(move_pair_kernel<kA, kB, true>, static_cast<unsigned>(grid), kMoverThreads, 0,
+                            stream, a, b, split);
+  return launch_dependent(move_pair_kernel<kA, kB, false>, static_cast<unsigned>(grid), kMoverThreads, 0,
+                          stream, a, b, split);
 }
 
 template <MoverBody kA>
 cudaError_t launch_pair_b(MoverBody b_body, const MoveParams& a, const MoveParams& b, int split, int grid,
-                          cudaStream_t stream) {
+                          bool early, cudaStream_t stream) {
   switch (b_body) {
-    case MoverBody::kStream: return launch_pair_typed<kA, MoverBody::kStream>(a, b, split, grid, stream);
-    case MoverBody::kSmall: return launch_pair_typed<kA, MoverBody::kSmall>(a, b, split, grid, stream);
-    default: return launch_pair_typed<kA, MoverBody::kSimt>(a, b, split, grid, stream);
+    case MoverBody::kStream: return launch_pair_typed<kA, MoverBody::kStream>(a, b, split, grid, early, stream);
+    case MoverBody::kSmall: return launch_pair_typed<kA, MoverBody::kSmall>(a, b, split, grid, early, stream);
+    default: return launch_pair_typed<kA, MoverBody::kSimt>(a, b, split, grid, early, stream);
   }
 }
 
@@ -3140,10 +3161,11 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   if (cb > want_b) cb = want_b > 0 ? want_b : 1;
   const int split = static_cast<int>(ca);
   const int grid = static_cast<int>(ca + cb);
+  const bool early = ((scatter.flags & gather.flags) & KVCA_FLAG_INPUTS_READY) != 0;
   switch (body_a) {
-    case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, split, grid, stream);
-    case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, split, grid, stream);
-    default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, split, grid, stream);
+    case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, split, grid, early, stream);
+    case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, split, grid, early, stream);
+    default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, split, grid, early, stream);
   }
 }
 

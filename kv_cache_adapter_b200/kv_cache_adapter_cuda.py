@@ -1007,13 +1007,18 @@ def scatter_tokens(caches: Sequence[torch.Tensor], slot_mapping: torch.Tensor, c
 
 def scatter_tokens_gather_layers(token_caches, slot_mapping: torch.Tensor, chunks: torch.Tensor, block_caches,
                                  slot_ids: torch.Tensor, out: torch.Tensor, *, tokens_per_chunk: int | None = None,
-                                 blocks_per_chunk: int | None = None, check: bool | None = None) -> None:
+                                 blocks_per_chunk: int | None = None, inputs_ready: bool = False,
+                                 check: bool | None = None) -> None:
     """``scatter_tokens(token_caches, slot_mapping, chunks)`` and
     ``gather_layers(block_caches, slot_ids, out)`` in one launch
     (kvca_scatter_gather).  The two moves must touch disjoint bytes: nothing
     orders one before the other.  A decode step's token scatter and the spill
     gather of the blocks the next step evicts (which this step does not
-    write) are such a pair."""
+    write) are such a pair.  ``inputs_ready`` (KVCA_FLAG_INPUTS_READY): no
+    kernel that may still run when this launch starts writes ``chunks``,
+    ``slot_mapping`` or ``slot_ids`` (true in a chain of these calls whose
+    inputs were made before it), so the launch reads them while the
+    launches before it drain."""
     tp = _planes(token_caches, 2, "token_caches")
     bp = _planes(block_caches, 1, "block_caches")
     dev = tp.device
@@ -1031,12 +1036,13 @@ def scatter_tokens_gather_layers(token_caches, slot_mapping: torch.Tensor, chunk
     _chunk_tensor(out, (gc, Q, cb, *bp.row_shape), bp.dtype, dev, "out")
     if t == 0 and k == 0:
         return
+    ready = _lib.KVCA_FLAG_INPUTS_READY if inputs_ready else 0
     s_src, s_dst = _chunk_desc(chunks, tpc, P, tp.row_bytes), tp.desc(slot_mapping)
     g_src, g_dst = bp.desc(slot_ids), _chunk_desc(out, cb, Q, bp.row_bytes)
     with _on(dev):
         rc = _lib_handle.kvca_scatter_gather(
             ctypes.byref(s_src), ctypes.byref(s_dst), P, t, tp.row_bytes, ctypes.byref(g_src), ctypes.byref(g_dst),
-            Q, k, bp.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE, 0, _ptr(_status(dev)), _stream(dev))
+            Q, k, bp.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE | ready, ready, _ptr(_status(dev)), _stream(dev))
     _host_rc(rc, "scatter_tokens_gather_layers")
     _maybe_check(dev, check, "scatter_tokens_gather_layers")
 
