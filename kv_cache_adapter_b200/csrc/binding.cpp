@@ -81,6 +81,18 @@ bool common_move_args_ok(int64_t num_planes, int64_t num_rows, int64_t row_bytes
   return num_planes >= 1 && num_planes <= KVCA_MAX_PLANES && num_rows >= 0 && row_bytes >= 1;
 }
 
+// A device-store call whose rows total at most this many bytes runs as one
+// single-CTA launch (plan, finish and row copies): its cost is launches and
+// dependent round trips, not bandwidth.  Over the host link one CTA moves
+// less, so the limit is lower for a pinned store.
+constexpr int64_t kSmallStoreBytes = 256 * 1024;
+constexpr int64_t kSmallHostStoreBytes = 64 * 1024;
+
+bool small_store_call(int64_t count, int64_t row_bytes, int32_t move_flags) {
+  const int64_t limit = (move_flags & KVCA_FLAG_HOST_MEMORY) ? kSmallHostStoreBytes : kSmallStoreBytes;
+  return count <= limit / (row_bytes > 0 ? row_bytes : 1);
+}
+
 }  // namespace
 
 extern "C" {
@@ -344,16 +356,24 @@ int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
       !store_ok(store, d_actual, actual_row_stride, row_bytes) || !d_work || !d_work_meta ||
       !d_result)
     return KVCA_ERR_BAD_ARGUMENT;
-  int rc = status_of(kvca::launch_store_load_meta(
-      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
-      count, d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_result,
-      d_counts, d_status, stream));
-  if (rc != KVCA_OK) return rc;
   int vec = align_of(static_cast<uint64_t>(row_bytes));
   vec = min_align(vec, d_actual);
   vec = min_align(vec, static_cast<uint64_t>(actual_row_stride));
   vec = min_align(vec, store->storage);
   vec = min_align(vec, static_cast<uint64_t>(store->storage_row_stride));
+  if (small_store_call(count, row_bytes, store->move_flags)) {
+    const kvca::StoreRowArgs rows{d_actual, actual_row_stride, store->storage, store->storage_row_stride, 0,
+                                  row_bytes, vec};
+    return status_of(kvca::launch_store_load_small(
+        meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids, count,
+        d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_result, d_counts, d_status,
+        rows, stream));
+  }
+  int rc = status_of(kvca::launch_store_load_meta(
+      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
+      count, d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_result,
+      d_counts, d_status, stream));
+  if (rc != KVCA_OK) return rc;
   const int64_t k = count;
   const int32_t flags = KVCA_FLAG_SKIP_NEGATIVE | store->move_flags;
   const int64_t* xslot = d_work + 6 * k;
@@ -386,17 +406,25 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
       !store_ok(store, d_actual, actual_row_stride, row_bytes) || !d_block_data || !d_work ||
       !d_work_meta)
     return KVCA_ERR_BAD_ARGUMENT;
-  int rc = status_of(kvca::launch_store_save_meta(
-      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
-      count, d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_counts,
-      d_status, stream));
-  if (rc != KVCA_OK) return rc;
   int vec = align_of(static_cast<uint64_t>(row_bytes));
   vec = min_align(vec, d_actual);
   vec = min_align(vec, static_cast<uint64_t>(actual_row_stride));
   vec = min_align(vec, store->storage);
   vec = min_align(vec, static_cast<uint64_t>(store->storage_row_stride));
   vec = min_align(vec, d_block_data);
+  if (small_store_call(count, row_bytes, store->move_flags)) {
+    const kvca::StoreRowArgs rows{d_actual, actual_row_stride, store->storage, store->storage_row_stride,
+                                  d_block_data, row_bytes, vec};
+    return status_of(kvca::launch_store_save_small(
+        meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids, count,
+        d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_counts, d_status, rows,
+        stream));
+  }
+  int rc = status_of(kvca::launch_store_save_meta(
+      meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
+      count, d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_counts,
+      d_status, stream));
+  if (rc != KVCA_OK) return rc;
   const int64_t k = count;
   kvca::PagedSide actual_evicted, store_evicted, actual_selected;
   one_plane(d_actual, num_slots, actual_row_stride, d_work + 3 * k, &actual_evicted);

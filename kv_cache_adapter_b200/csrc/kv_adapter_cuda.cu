@@ -1478,14 +1478,13 @@ __device__ bool plan_validate(const int64_t* l2p, int64_t n_logical, int64_t n, 
 // the popped slots, the hits' usage re-read after the pop's aging, and the
 // returned slots.
 template <typename MetaT>
-__global__ void __launch_bounds__(1024)
-    plan_load_kernel(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
-                     int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
-                     int order, bool aligned, int64_t* result, int64_t* hit_slots, int64_t* hit_pins,
-                     MetaT* hit_usage, int64_t* miss_ids, int64_t* victims, int64_t* evict_ids,
-                     int64_t* evict_slots, int64_t* counts, int64_t* status) {
+__device__ void plan_load_body(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
+                               int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
+                               int order, bool aligned, int64_t* result, int64_t* hit_slots,
+                               int64_t* hit_pins, MetaT* hit_usage, int64_t* miss_ids, int64_t* victims,
+                               int64_t* evict_ids, int64_t* evict_slots, int64_t* counts, int64_t* status,
+                               PlanShared<MetaT>& sh) {
   using M = Meta<MetaT>;
-  __shared__ PlanShared<MetaT> sh;
   if (threadIdx.x == 0) plan_begin(counts, status);
   if (!plan_validate<MetaT>(l2p, n_logical, n, ids, k, counts, status, sh)) return;
   // hits and misses in request order; the hit slots are blocked for the pop
@@ -1556,19 +1555,30 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    plan_load_kernel(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
+                     int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
+                     int order, bool aligned, int64_t* result, int64_t* hit_slots, int64_t* hit_pins,
+                     MetaT* hit_usage, int64_t* miss_ids, int64_t* victims, int64_t* evict_ids,
+                     int64_t* evict_slots, int64_t* counts, int64_t* status) {
+  __shared__ PlanShared<MetaT> sh;
+  plan_load_body<MetaT>(l2p, n_logical, p2l, meta, n, search_start, ids, k, bitmap, order, aligned, result,
+                        hit_slots, hit_pins, hit_usage, miss_ids, victims, evict_ids, evict_slots, counts,
+                        status, sh);
+}
+
 // KVCacheAdapter.save up to the backend call (adapter.py:221-243): existing /
 // missing compaction, pop(#missing) with the existing slots blocked, the
 // selected slots, final pins and usage read after the pop, and the eviction
 // plan over every selected slot in request order.
 template <typename MetaT>
-__global__ void __launch_bounds__(1024)
-    plan_save_kernel(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
-                     int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
-                     int order, bool aligned, int64_t* selected, int64_t* move_slots,
-                     MetaT* final_pins, MetaT* final_usage, int64_t* allocated, int64_t* evict_ids,
-                     int64_t* evict_slots, int64_t* counts, int64_t* status) {
+__device__ void plan_save_body(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
+                               int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
+                               int order, bool aligned, int64_t* selected, int64_t* move_slots,
+                               MetaT* final_pins, MetaT* final_usage, int64_t* allocated, int64_t* evict_ids,
+                               int64_t* evict_slots, int64_t* counts, int64_t* status, PlanShared<MetaT>& sh) {
   using M = Meta<MetaT>;
-  __shared__ PlanShared<MetaT> sh;
   if (threadIdx.x == 0) {
     plan_begin(counts, status);
     sh.repeated = 0;
@@ -1681,6 +1691,19 @@ __global__ void __launch_bounds__(1024)
     counts[1] = nm;
     counts[2] = ne;
   }
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    plan_save_kernel(const int64_t* l2p, int64_t n_logical, const int64_t* p2l, MetaT* meta, int64_t n,
+                     int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap,
+                     int order, bool aligned, int64_t* selected, int64_t* move_slots,
+                     MetaT* final_pins, MetaT* final_usage, int64_t* allocated, int64_t* evict_ids,
+                     int64_t* evict_slots, int64_t* counts, int64_t* status) {
+  __shared__ PlanShared<MetaT> sh;
+  plan_save_body<MetaT>(l2p, n_logical, p2l, meta, n, search_start, ids, k, bitmap, order, aligned, selected,
+                        move_slots, final_pins, final_usage, allocated, evict_ids, evict_slots, counts, status,
+                        sh);
 }
 
 // ---------------------------------------------------------------------------
@@ -1973,19 +1996,25 @@ __device__ void store_spill_prepare(const int64_t* evict_ids, int64_t* evict_slo
 // spill still runs, nothing is filled or committed, as when the backend
 // raises.  `scratch` (one int per logical id) is zero on entry and left zero.
 // Nothing runs when the plan failed.
+struct FinishShared {
+  int bad;
+  int missing;
+  int conflict;
+  long long missing_id;
+};
+
 template <typename MetaT>
-__global__ void __launch_bounds__(1024)
-    store_load_finish_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
-                             int64_t* counts, const int64_t* hit_slots, const int64_t* hit_pins,
-                             const MetaT* hit_usage, const int64_t* miss_ids,
-                             const int64_t* victims, const int64_t* evict_ids, int32_t* scratch,
-                             uint8_t* present, int64_t* xslot, int64_t* spill_to,
-                             int64_t* fill_from, int64_t* status) {
-  __shared__ int bad;
-  __shared__ int missing;
-  __shared__ int conflict;
-  __shared__ long long missing_id;
-  if (counts[3] != 0) return;  // written by the plan launch: uniform
+__device__ void store_load_finish_body(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
+                                       int64_t* counts, const int64_t* hit_slots, const int64_t* hit_pins,
+                                       const MetaT* hit_usage, const int64_t* miss_ids,
+                                       const int64_t* victims, const int64_t* evict_ids, int32_t* scratch,
+                                       uint8_t* present, int64_t* xslot, int64_t* spill_to,
+                                       int64_t* fill_from, int64_t* status, FinishShared& fs) {
+  int& bad = fs.bad;
+  int& missing = fs.missing;
+  int& conflict = fs.conflict;
+  long long& missing_id = fs.missing_id;
+  if (counts[3] != 0) return;  // written by the plan (an earlier launch, or before a barrier): uniform
   const int64_t nh = counts[0], nm = counts[1], ne = counts[2];
   if (threadIdx.x == 0) bad = missing = conflict = 0;
   for (int64_t j = threadIdx.x; j < nm; j += blockDim.x) {
@@ -2026,8 +2055,36 @@ __global__ void __launch_bounds__(1024)
                           hit_slots, hit_pins, hit_usage, nh, nullptr, status, &bad);
 }
 
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    store_load_finish_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
+                             int64_t* counts, const int64_t* hit_slots, const int64_t* hit_pins,
+                             const MetaT* hit_usage, const int64_t* miss_ids,
+                             const int64_t* victims, const int64_t* evict_ids, int32_t* scratch,
+                             uint8_t* present, int64_t* xslot, int64_t* spill_to,
+                             int64_t* fill_from, int64_t* status) {
+  __shared__ FinishShared fs;
+  store_load_finish_body<MetaT>(l2p, n_logical, p2l, meta, n, counts, hit_slots, hit_pins, hit_usage, miss_ids,
+                                victims, evict_ids, scratch, present, xslot, spill_to, fill_from, status, fs);
+}
+
 // After plan_save: spill preparation and the commit.  Nothing runs when the
 // plan failed.
+template <typename MetaT>
+__device__ void store_save_finish_body(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
+                                       int64_t* counts, const int64_t* ids, int64_t k,
+                                       const int64_t* selected, const MetaT* final_pins,
+                                       const MetaT* final_usage, const int64_t* evict_ids,
+                                       int64_t* evict_slots, int32_t* scratch, uint8_t* present,
+                                       int64_t* status, FinishShared& fs) {
+  if (counts[3] != 0) return;
+  const int64_t ne = counts[2];
+  if (threadIdx.x == 0) fs.bad = 0;
+  store_spill_prepare(evict_ids, evict_slots, ne, scratch, present);
+  commit_save_body<MetaT>(l2p, n_logical, p2l, meta, n, evict_ids, ne, ids, selected, final_pins,
+                          final_usage, k, status, &fs.bad);
+}
+
 template <typename MetaT>
 __global__ void __launch_bounds__(1024)
     store_save_finish_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
@@ -2036,13 +2093,135 @@ __global__ void __launch_bounds__(1024)
                              const MetaT* final_usage, const int64_t* evict_ids,
                              int64_t* evict_slots, int32_t* scratch, uint8_t* present,
                              int64_t* status) {
-  __shared__ int bad;
-  if (counts[3] != 0) return;
-  const int64_t ne = counts[2];
-  if (threadIdx.x == 0) bad = 0;
-  store_spill_prepare(evict_ids, evict_slots, ne, scratch, present);
-  commit_save_body<MetaT>(l2p, n_logical, p2l, meta, n, evict_ids, ne, ids, selected, final_pins,
-                          final_usage, k, status, &bad);
+  __shared__ FinishShared fs;
+  store_save_finish_body<MetaT>(l2p, n_logical, p2l, meta, n, counts, ids, k, selected, final_pins, final_usage,
+                                evict_ids, evict_slots, scratch, present, status, fs);
+}
+
+// ---------------------------------------------------------------------------
+// Small device-store calls in one launch
+// ---------------------------------------------------------------------------
+//
+// A load or save whose rows total at most a few hundred KiB (an adapter call
+// of tens of blocks) spends its time in launches, not in moving bytes.  Then
+// one CTA runs the whole call: plan, finish (spill preparation, presence
+// check, commit) and the row copies, each phase behind a block barrier, with
+// the same results as the multi-launch sequence: spill rows are read before
+// any fill or data row is written (the exchange's gate is the barrier).
+
+// Row j: dst[dst_idx[j]] = src[src_idx[j]] (a null index array means row j
+// itself), rows with a negative index skipped; one warp per row, vectors of
+// `vec` bytes (the widest every address and stride allows).  Plain loads and
+// stores, so either side may be pinned host memory.
+template <typename V>
+__device__ void copy_rows_cta_typed(uint64_t dst, int64_t dst_stride, const int64_t* dst_idx, uint64_t src,
+                                    int64_t src_stride, const int64_t* src_idx, int64_t rows, int64_t row_bytes) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nv = row_bytes / static_cast<int64_t>(sizeof(V));
+  for (int64_t j = threadIdx.x >> 5; j < rows; j += blockDim.x >> 5) {
+    const int64_t di = dst_idx != nullptr ? dst_idx[j] : j;
+    const int64_t si = src_idx != nullptr ? src_idx[j] : j;
+    if (di < 0 || si < 0) continue;
+    const V* s = reinterpret_cast<const V*>(src + si * src_stride);
+    V* d = reinterpret_cast<V*>(dst + di * dst_stride);
+    for (int64_t v = lane; v < nv; v += 32) d[v] = s[v];
+  }
+}
+
+__device__ void copy_rows_cta(uint64_t dst, int64_t dst_stride, const int64_t* dst_idx, uint64_t src,
+                              int64_t src_stride, const int64_t* src_idx, int64_t rows, int64_t row_bytes,
+                              int vec) {
+  switch (vec) {
+    case 16: copy_rows_cta_typed<uint4>(dst, dst_stride, dst_idx, src, src_stride, src_idx, rows, row_bytes); break;
+    case 8: copy_rows_cta_typed<uint2>(dst, dst_stride, dst_idx, src, src_stride, src_idx, rows, row_bytes); break;
+    case 4: copy_rows_cta_typed<unsigned>(dst, dst_stride, dst_idx, src, src_stride, src_idx, rows, row_bytes); break;
+    case 2:
+      copy_rows_cta_typed<unsigned short>(dst, dst_stride, dst_idx, src, src_stride, src_idx, rows, row_bytes);
+      break;
+    default:
+      copy_rows_cta_typed<unsigned char>(dst, dst_stride, dst_idx, src, src_stride, src_idx, rows, row_bytes);
+  }
+}
+
+// The slot rows and store rows of a small call.
+struct StoreRows {
+  uint64_t actual;
+  int64_t actual_stride;
+  uint64_t storage;
+  int64_t storage_stride;
+  uint64_t data;  // save: the caller's block_data rows
+  int64_t row_bytes;
+  int vec;
+};
+
+// work as in launch_store_load_meta (9 x k int64): hit_slots, hit_pins,
+// miss_ids, victims, evict_ids, evict_slots, xslot, spill_to, fill_from.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    store_load_small_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
+                            int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap, int order,
+                            bool aligned, int32_t* scratch, uint8_t* present, int64_t* work, MetaT* hit_usage,
+                            int64_t* result, int64_t* counts, int64_t* status, StoreRows rows) {
+  __shared__ PlanShared<MetaT> sh;
+  __shared__ FinishShared fs;
+  int64_t* hit_slots = work;
+  int64_t* hit_pins = work + k;
+  int64_t* miss_ids = work + 2 * k;
+  int64_t* victims = work + 3 * k;
+  int64_t* evict_ids = work + 4 * k;
+  int64_t* evict_slots = work + 5 * k;
+  int64_t* xslot = work + 6 * k;
+  int64_t* spill_to = work + 7 * k;
+  int64_t* fill_from = work + 8 * k;
+  for (int64_t i = threadIdx.x; i < 3 * k; i += blockDim.x) xslot[i] = -1;  // xslot, spill_to, fill_from
+  if (threadIdx.x == 0) counts[7] = 0;
+  __syncthreads();
+  plan_load_body<MetaT>(l2p, n_logical, p2l, meta, n, search_start, ids, k, bitmap, order, aligned, result,
+                        hit_slots, hit_pins, hit_usage, miss_ids, victims, evict_ids, evict_slots, counts, status,
+                        sh);
+  __syncthreads();
+  store_load_finish_body<MetaT>(l2p, n_logical, p2l, meta, n, counts, hit_slots, hit_pins, hit_usage, miss_ids,
+                                victims, evict_ids, scratch, present, xslot, spill_to, fill_from, status, fs);
+  __syncthreads();
+  // spill the victims' old rows, then fill them
+  copy_rows_cta(rows.storage, rows.storage_stride, spill_to, rows.actual, rows.actual_stride, xslot, k,
+                rows.row_bytes, rows.vec);
+  __syncthreads();
+  copy_rows_cta(rows.actual, rows.actual_stride, xslot, rows.storage, rows.storage_stride, fill_from, k,
+                rows.row_bytes, rows.vec);
+}
+
+// work as in launch_store_save_meta (5 x k int64): selected, allocated,
+// evict_ids, evict_slots, move_slots; work_meta: final pins, final usage.
+template <typename MetaT>
+__global__ void __launch_bounds__(1024)
+    store_save_small_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
+                            int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap, int order,
+                            bool aligned, int32_t* scratch, uint8_t* present, int64_t* work, MetaT* work_meta,
+                            int64_t* counts, int64_t* status, StoreRows rows) {
+  __shared__ PlanShared<MetaT> sh;
+  __shared__ FinishShared fs;
+  int64_t* selected = work;
+  int64_t* allocated = work + k;
+  int64_t* evict_ids = work + 2 * k;
+  int64_t* evict_slots = work + 3 * k;
+  int64_t* move_slots = work + 4 * k;
+  MetaT* final_pins = work_meta;
+  MetaT* final_usage = work_meta + k;
+  for (int64_t i = threadIdx.x; i < 3 * k; i += blockDim.x) evict_ids[i] = -1;  // evict_ids, evict_slots, move_slots
+  __syncthreads();
+  plan_save_body<MetaT>(l2p, n_logical, p2l, meta, n, search_start, ids, k, bitmap, order, aligned, selected,
+                        move_slots, final_pins, final_usage, allocated, evict_ids, evict_slots, counts, status, sh);
+  __syncthreads();
+  store_save_finish_body<MetaT>(l2p, n_logical, p2l, meta, n, counts, ids, k, selected, final_pins, final_usage,
+                                evict_ids, evict_slots, scratch, present, status, fs);
+  __syncthreads();
+  // spill the evicted rows, then scatter the data rows
+  copy_rows_cta(rows.storage, rows.storage_stride, evict_ids, rows.actual, rows.actual_stride, evict_slots, k,
+                rows.row_bytes, rows.vec);
+  __syncthreads();
+  copy_rows_cta(rows.actual, rows.actual_stride, move_slots, rows.data, rows.row_bytes, nullptr, k, rows.row_bytes,
+                rows.vec);
 }
 
 // ---------------------------------------------------------------------------
@@ -3440,6 +3619,34 @@ cudaError_t launch_store_save_meta(int meta_bits, int order, int64_t* l2p, int64
                                     static_cast<const MetaT*>(final_pins),
                                     static_cast<const MetaT*>(final_usage), evict_ids,
                                     evict_slots, scratch, present, status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_store_load_small(int meta_bits, int order, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                                    void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
+                                    int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                    int64_t* work, void* work_meta, int64_t* result, int64_t* counts,
+                                    int64_t* status, const StoreRowArgs& r, cudaStream_t stream) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  const StoreRows rows{r.actual, r.actual_stride, r.storage, r.storage_stride, r.data, r.row_bytes, r.vec};
+  KVCA_META_DISPATCH(meta_bits, store_load_small_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots, search_start, ids,
+                                    count, bitmap, order, aligned, scratch, present, work,
+                                    static_cast<MetaT*>(work_meta), result, counts, status, rows));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_store_save_small(int meta_bits, int order, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                                    void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
+                                    int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                    int64_t* work, void* work_meta, int64_t* counts, int64_t* status,
+                                    const StoreRowArgs& r, cudaStream_t stream) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  const StoreRows rows{r.actual, r.actual_stride, r.storage, r.storage_stride, r.data, r.row_bytes, r.vec};
+  KVCA_META_DISPATCH(meta_bits, store_save_small_kernel<MetaT><<<1, 1024, 0, stream>>>(
+                                    l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots, search_start, ids,
+                                    count, bitmap, order, aligned, scratch, present, work,
+                                    static_cast<MetaT*>(work_meta), counts, status, rows));
   return cudaGetLastError();
 }
 

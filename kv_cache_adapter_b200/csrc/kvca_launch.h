@@ -177,6 +177,31 @@ cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t nu
                                 int64_t block_size, int64_t* next_logical, int64_t* victims,
                                 int64_t* slot_mapping, int64_t* status, cudaStream_t stream);
 
+// Rows of a small device-store call moved inside its one launch.
+struct StoreRowArgs {
+  uint64_t actual;
+  int64_t actual_stride;
+  uint64_t storage;
+  int64_t storage_stride;
+  uint64_t data;  // save only
+  int64_t row_bytes;
+  int vec;
+};
+
+// The whole device-store load / save in one single-CTA launch (plan, finish,
+// row copies), for calls whose rows are small; same work layouts and results
+// as launch_store_*_meta followed by the row movers.
+cudaError_t launch_store_load_small(int meta_bits, int order, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                                    void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
+                                    int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                    int64_t* work, void* work_meta, int64_t* result, int64_t* counts,
+                                    int64_t* status, const StoreRowArgs& rows, cudaStream_t stream);
+cudaError_t launch_store_save_small(int meta_bits, int order, int64_t* l2p, int64_t num_logical, int64_t* p2l,
+                                    void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
+                                    int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
+                                    int64_t* work, void* work_meta, int64_t* counts, int64_t* status,
+                                    const StoreRowArgs& rows, cudaStream_t stream);
+
 cudaError_t launch_wait_selftest(const uint32_t* flag, uint32_t from, int64_t* status,
                                  cudaStream_t stream);
 

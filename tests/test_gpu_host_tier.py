@@ -175,12 +175,15 @@ def test_host_tier_backend_api():
     b.shutdown()
 
 
-@pytest.mark.parametrize("seed,num_actual,num_logical,max_batch", [(11, 64, 256, 48), (12, 1000, 4000, 700)])
-def test_adapter_with_host_tier_matches_oracle_adapter(seed, num_actual, num_logical, max_batch):
+@pytest.mark.parametrize("seed,num_actual,num_logical,max_batch,shape", [
+    (11, 64, 256, 48, (2, 3)), (12, 1000, 4000, 700, (2, 3)),
+    # 32 KiB blocks: most calls exceed the one-launch size limit of a pinned store
+    (13, 64, 256, 48, (8, 1024)),
+])
+def test_adapter_with_host_tier_matches_oracle_adapter(seed, num_actual, num_logical, max_batch, shape):
     """Random programs as in the planner tests, the CUDA adapter spilling to
     and filling from the pinned host tier (device-store path)."""
     rng = np.random.default_rng(seed)
-    shape = (2, 3)
     init = {i: torch.full(shape, float(i)) for i in range(num_logical) if i % 13 != 4}
     cpu_ops = OracleOps()
     ref = adapter_mod.KVCacheAdapter(
@@ -207,7 +210,7 @@ def test_adapter_with_host_tier_matches_oracle_adapter(seed, num_actual, num_log
                 if op == "load":
                     outs.append(("ok", ad.load(t).tolist()))
                 elif op == "save":
-                    data = torch.arange(k * 6, dtype=torch.float32).reshape(k, *shape) + 1000 * step
+                    data = torch.arange(k * shape[0] * shape[1], dtype=torch.float32).reshape(k, *shape) + 1000 * step
                     ad.save(t, data.to(dev))
                     outs.append(("ok", None))
                 else:

@@ -230,19 +230,22 @@ def test_save_with_repeated_ids_keeps_last_row(api_gpu):
 
 
 @pytest.mark.parametrize("path", ["device_store", "planned"])
-@pytest.mark.parametrize("seed,num_actual,num_logical,max_batch", [
-    (1, 4, 16, 4),
-    (2, 64, 256, 48),
-    (3, 1000, 4000, 700),
-    (4, 3000, 20000, 2500),
+@pytest.mark.parametrize("seed,num_actual,num_logical,max_batch,shape", [
+    (1, 4, 16, 4, (2, 3)),
+    (2, 64, 256, 48, (2, 3)),
+    (3, 1000, 4000, 700, (2, 3)),
+    (4, 3000, 20000, 2500, (2, 3)),
+    # 128 KiB blocks: calls above the one-launch size limit take the
+    # multi-launch device-store sequence, small ones the single launch
+    (5, 4, 16, 4, (32, 1024)),
+    (6, 64, 256, 48, (32, 1024)),
 ])
-def test_planned_adapter_matches_oracle_adapter(api_gpu, seed, num_actual, num_logical, max_batch, path):
+def test_planned_adapter_matches_oracle_adapter(api_gpu, seed, num_actual, num_logical, max_batch, shape, path):
     """Random load / save / release programs with duplicates, pin pressure,
     capacity errors and blocks missing from the store: the CUDA adapter (store
     driven on the device, or plan + backend calls) and the oracle-backed CPU
     adapter agree on every result, error and the full state after each op."""
     rng = np.random.default_rng(seed)
-    shape = (2, 3)
     # a few logical blocks are in no store: loading them raises BlockNotFoundError
     init = {i: torch.full(shape, float(i)) for i in range(num_logical) if i % 17 != 5}
     cpu_ops = OracleOps()
@@ -272,7 +275,7 @@ def test_planned_adapter_matches_oracle_adapter(api_gpu, seed, num_actual, num_l
                 if op == "load":
                     outs.append(("ok", ad.load(t).tolist()))
                 elif op == "save":
-                    data = torch.arange(k * 6, dtype=torch.float32).reshape(k, *shape) + 1000 * step
+                    data = torch.arange(k * shape[0] * shape[1], dtype=torch.float32).reshape(k, *shape) + 1000 * step
                     ad.save(t, data.to(dev))
                     outs.append(("ok", None))
                 else:
