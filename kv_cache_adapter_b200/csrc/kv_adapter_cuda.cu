@@ -3622,6 +3622,11 @@ cudaError_t launch_store_save_meta(int meta_bits, int order, int64_t* l2p, int64
   return cudaGetLastError();
 }
 
+// Threads of a small store call's CTA: its phases are chains of short
+// dependent steps joined by block barriers, and barriers of 8 warps are
+// cheaper than of 32; larger requests keep 1,024 threads for their scans.
+unsigned small_store_threads(int64_t count) { return count <= 256 ? 256u : 1024u; }
+
 cudaError_t launch_store_load_small(int meta_bits, int order, int64_t* l2p, int64_t num_logical, int64_t* p2l,
                                     void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
                                     int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
@@ -3629,7 +3634,7 @@ cudaError_t launch_store_load_small(int meta_bits, int order, int64_t* l2p, int6
                                     int64_t* status, const StoreRowArgs& r, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
   const StoreRows rows{r.actual, r.actual_stride, r.storage, r.storage_stride, r.data, r.row_bytes, r.vec};
-  KVCA_META_DISPATCH(meta_bits, store_load_small_kernel<MetaT><<<1, 1024, 0, stream>>>(
+  KVCA_META_DISPATCH(meta_bits, store_load_small_kernel<MetaT><<<1, small_store_threads(count), 0, stream>>>(
                                     l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots, search_start, ids,
                                     count, bitmap, order, aligned, scratch, present, work,
                                     static_cast<MetaT*>(work_meta), result, counts, status, rows));
@@ -3643,7 +3648,7 @@ cudaError_t launch_store_save_small(int meta_bits, int order, int64_t* l2p, int6
                                     const StoreRowArgs& r, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
   const StoreRows rows{r.actual, r.actual_stride, r.storage, r.storage_stride, r.data, r.row_bytes, r.vec};
-  KVCA_META_DISPATCH(meta_bits, store_save_small_kernel<MetaT><<<1, 1024, 0, stream>>>(
+  KVCA_META_DISPATCH(meta_bits, store_save_small_kernel<MetaT><<<1, small_store_threads(count), 0, stream>>>(
                                     l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots, search_start, ids,
                                     count, bitmap, order, aligned, scratch, present, work,
                                     static_cast<MetaT*>(work_meta), counts, status, rows));

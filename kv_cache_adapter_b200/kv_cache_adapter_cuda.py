@@ -642,6 +642,80 @@ def _store_desc(storage: torch.Tensor, present: torch.Tensor, scratch: torch.Ten
             a_stride, row_bytes)
 
 
+_store_descs: dict[tuple, tuple] = {}
+
+
+def _store_desc_cached(storage: torch.Tensor, present: torch.Tensor, scratch: torch.Tensor,
+                       actual_blocks: torch.Tensor) -> tuple[_lib.DeviceStore, int, int]:
+    """_store_desc, remembered for the same tensors: the descriptor is a pure
+    function of the key (addresses, shapes, strides, dtypes, devices and,
+    for host storage, pinning), which the adapter passes unchanged on every
+    call."""
+    key = tuple((t.data_ptr(), tuple(t.shape), t.stride(), t.dtype, t.device)
+                for t in (storage, present, scratch, actual_blocks)) + \
+        ((storage.is_pinned(),) if storage.device.type == "cpu" else ())
+    got = _store_descs.get(key)
+    if got is None:
+        got = _store_desc(storage, present, scratch, actual_blocks)
+        if len(_store_descs) >= 64:
+            _store_descs.clear()
+        _store_descs[key] = got
+    return got
+
+
+class _StoreCallBuffers:
+    """Work space of the device-store calls on one (device, stream): device
+    work arrays grown to the largest request so far, the count vector, and a
+    pinned host copy of it.  Each call ends by reading its counts (a stream
+    synchronisation), so the next call on the stream may reuse them."""
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev
+        self.cap = 0
+        self.work = self.work_meta = None
+        self.counts = torch.empty(8, dtype=torch.int64, device=dev)
+        self.counts_host = torch.empty(8, dtype=torch.int64, pin_memory=True)
+
+    def get(self, k: int, meta_dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
+        if k > self.cap or self.work_meta.dtype != meta_dtype:
+            self.cap = max(k, 2 * self.cap, 64)
+            self.work = torch.empty(9 * self.cap, dtype=torch.int64, device=self.dev)
+            self.work_meta = torch.empty(2 * self.cap, dtype=meta_dtype, device=self.dev)
+        return self.work, self.work_meta
+
+    def read_counts(self, n: int) -> list[int]:
+        self.counts_host.copy_(self.counts, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return self.counts_host.tolist()[:n]
+
+
+_store_buffers: dict[tuple[int, int], _StoreCallBuffers] = {}
+
+
+def _store_call_buffers(dev: torch.device) -> _StoreCallBuffers:
+    idx = _index(dev)
+    key = (idx, _stream(dev).value or 0)
+    got = _store_buffers.get(key)
+    if got is None:
+        got = _StoreCallBuffers(torch.device("cuda", idx))
+        _store_buffers[key] = got
+    return got
+
+
+def _store_counts(vals: list[int], what: str, dev: torch.device) -> list[int]:
+    """_plan_counts on counts already read to the host."""
+    if vals[5] != 0 or vals[3] != 0:
+        _status(dev).zero_()
+        if vals[5] != 0:
+            _raise_for(int(vals[5]), int(vals[6]), "an earlier unchecked launch")
+        try:
+            _raise_for(int(vals[3]), int(vals[4]), what)
+        except BlockNotFoundError as exc:
+            exc.counts = vals  # the plan's counts: the spill has run
+            raise
+    return vals
+
+
 def load_device_store(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor, slot_meta: torch.Tensor,
                       search_start: torch.Tensor, logical_block_ids: torch.Tensor, actual_blocks: torch.Tensor,
                       storage: torch.Tensor, present: torch.Tensor, scratch: torch.Tensor, *,
@@ -655,23 +729,23 @@ def load_device_store(logical_to_physical: torch.Tensor, physical_to_logical: to
                     (search_start, "search_start"), (logical_block_ids, "logical_block_ids")):
         _require(t, torch.int64, name)
     _require(slot_meta, _META_DTYPES, "slot_meta")
-    desc, a_stride, row_bytes = _store_desc(storage, present, scratch, actual_blocks)
+    desc, a_stride, row_bytes = _store_desc_cached(storage, present, scratch, actual_blocks)
     dev = slot_meta.device
     k = logical_block_ids.numel()
     n = slot_meta.numel()
-    work = torch.empty(9 * k, dtype=torch.int64, device=dev)
-    work_meta = torch.empty(k, dtype=slot_meta.dtype, device=dev)
+    bufs = _store_call_buffers(dev)
+    work, work_meta = bufs.get(k, slot_meta.dtype)
     result = torch.empty(k, dtype=torch.int64, device=dev)
-    counts = torch.empty(8, dtype=torch.int64, device=dev)
     with _on(dev):
         rc = _lib_handle.kvca_load_device_store(
             _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
             logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
             _ptr(logical_block_ids), k, _ptr(_bitmap(dev, n)), ctypes.byref(desc), actual_blocks.data_ptr(),
-            a_stride, row_bytes, _ptr(work), _ptr(work_meta), _ptr(result), _ptr(counts), _ptr(_status(dev)),
+            a_stride, row_bytes, _ptr(work), _ptr(work_meta), _ptr(result), _ptr(bufs.counts), _ptr(_status(dev)),
             _stream(dev))
-    _host_rc(rc, "load_device_store")
-    return result, _plan_counts(counts, "load_device_store")
+        _host_rc(rc, "load_device_store")
+        vals = bufs.read_counts(8)
+    return result, _store_counts(vals, "load_device_store", dev)
 
 
 def save_device_store(logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor, slot_meta: torch.Tensor,
@@ -685,23 +759,23 @@ def save_device_store(logical_to_physical: torch.Tensor, physical_to_logical: to
                     (search_start, "search_start"), (logical_block_ids, "logical_block_ids")):
         _require(t, torch.int64, name)
     _require(slot_meta, _META_DTYPES, "slot_meta")
-    desc, a_stride, row_bytes = _store_desc(storage, present, scratch, actual_blocks)
+    desc, a_stride, row_bytes = _store_desc_cached(storage, present, scratch, actual_blocks)
     dev = slot_meta.device
     k = logical_block_ids.numel()
     _chunk_tensor(block_data, (k, *actual_blocks.shape[1:]), actual_blocks.dtype, dev, "block_data")
     n = slot_meta.numel()
-    work = torch.empty(5 * k, dtype=torch.int64, device=dev)
-    work_meta = torch.empty(2 * k, dtype=slot_meta.dtype, device=dev)
-    counts = torch.empty(7, dtype=torch.int64, device=dev)
+    bufs = _store_call_buffers(dev)
+    work, work_meta = bufs.get(k, slot_meta.dtype)
     with _on(dev):
         rc = _lib_handle.kvca_save_device_store(
             _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], _ptr(logical_to_physical),
             logical_to_physical.numel(), _ptr(physical_to_logical), _ptr(slot_meta), n, _ptr(search_start),
             _ptr(logical_block_ids), k, _ptr(_bitmap(dev, n)), ctypes.byref(desc), actual_blocks.data_ptr(),
-            a_stride, row_bytes, block_data.data_ptr(), _ptr(work), _ptr(work_meta), _ptr(counts),
+            a_stride, row_bytes, block_data.data_ptr(), _ptr(work), _ptr(work_meta), _ptr(bufs.counts),
             _ptr(_status(dev)), _stream(dev))
-    _host_rc(rc, "save_device_store")
-    return _plan_counts(counts, "save_device_store")
+        _host_rc(rc, "save_device_store")
+        vals = bufs.read_counts(7)
+    return _store_counts(vals, "save_device_store", dev)
 
 
 # ---------------------------------------------------------------------------
