@@ -677,7 +677,7 @@ class _StoreCallBuffers:
         self.counts_host = torch.empty(8, dtype=torch.int64, pin_memory=True)
 
     def get(self, k: int, meta_dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
-        if k > self.cap or self.work_meta.dtype != meta_dtype:
+        if self.work is None or k > self.cap or self.work_meta.dtype != meta_dtype:
             self.cap = max(k, 2 * self.cap, 64)
             self.work = torch.empty(9 * self.cap, dtype=torch.int64, device=self.dev)
             self.work_meta = torch.empty(2 * self.cap, dtype=meta_dtype, device=self.dev)
