@@ -528,10 +528,12 @@ class DecodeMix:
             else:
                 nv = self.empty_ids
             # the indices come from the booking (another stream, waited for) and
-            # the token rows from before the cycle: no pair launch writes them
+            # the token rows from before the cycle, and after the first pair of
+            # the cycle the kernels before a pair are pairs, which write none of
+            # them; the first one waits for whatever the caller ran before
             pair(self.token_table, slot_mapping[step], token_rows, self.block_table, nv,
-                 self.spill[: nv.numel()], tokens_per_chunk=self.seqs, blocks_per_chunk=1, inputs_ready=True,
-                 check=False)
+                 self.spill[: nv.numel()], tokens_per_chunk=self.seqs, blocks_per_chunk=1,
+                 inputs_ready=step > 0, check=False)
         self._cycle_moved[h].record(cur)
         self.evictions += offs[-1]
         self.gathered_blocks += offs[-1]
