@@ -649,6 +649,7 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
                         f"spill gather when a block fills",
             "parallelism": f"kv-head shard x{world}, no data-path collective",
         },
+        "gpu_launches": replays * 2 * (mix.block_size + 1),  # per cycle: one booking, one pair launch per step
         "tokens_per_s": round(world * cyc_steps * mix.seqs / (ms / 1e3), 1),
         "evictions_per_s": round(world * replays * per_two / (ms / 1e3), 1),
         "gpu_launches_per_decode_step": "scatter_tokens, plus one gather on steps that evict, plus 1/16 of an "
