@@ -622,14 +622,9 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     torch.cuda.synchronize(device)
     ops.check_status(device)
     cyc_steps = 2 * replays * 16
-    # launches per cycle: the booking, then per step one pair launch (scatter
-    # + the next step's gather), or two when the pair exceeds 32 MiB
-    offs = mix._cycle_schedule(mix.pos)[2]
-    cycle_launches = 1
-    for st in range(16):
-        nxt = offs[(st + 1) % 16 + 1] - offs[(st + 1) % 16]
-        pair_bytes = mix.num_planes * row_bytes * (mix.seqs + nxt * mix.block_size)
-        cycle_launches += 1 if nxt == 0 or pair_bytes <= 32 * 1024 * 1024 else 2
+    # launches per cycle: the booking, then one per step (the token scatter
+    # with the next step's spill gather)
+    cycle_launches = 1 + 16
     cyc_moved = 2 * mix.num_planes * (cyc_steps * mix.seqs * row_bytes + replays * per_two * row_bytes * mix.block_size)
     if rank != 0:
         return

@@ -488,9 +488,10 @@ int kvca_scatter(const kvca_chunk_desc* src, const kvca_paged_desc* dst, int64_t
  * disjoint bytes (nothing orders one before the other).  For a decode
  * loop, whose steps move a few MiB each (the token scatter of step i and the
  * spill gather of the blocks step i + 1 evicts, which step i does not
- * write), one launch instead of two.  Without 16-byte alignment, with
- * KVCA_FLAG_HOST_MEMORY, or above 32 MiB moved by the two together (when
- * each fills the GPU on its own), the two moves take two launches, the
+ * write), one launch instead of two.  Up to 32 MiB moved by the two
+ * together the CTAs are split between the moves; above it every CTA moves
+ * its share of the scatter, then of the gather.  Without 16-byte alignment,
+ * or with KVCA_FLAG_HOST_MEMORY, the two moves take two launches, the
  * scatter first.  No reference counterpart.
  */
 int kvca_scatter_gather(const kvca_chunk_desc* s_src, const kvca_paged_desc* s_dst, int64_t s_planes,

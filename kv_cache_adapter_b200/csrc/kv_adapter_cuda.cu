@@ -2740,6 +2740,16 @@ __global__ void __launch_bounds__(kMoverThreads)
                                             static_cast<int64_t>(gridDim.x) - split);
 }
 
+// Two large independent moves in one launch: every CTA moves its share of
+// the scatter, then its share of the gather, so the two share one ramp and
+// one tail and every SM carries both.
+template <MoverBody kA, MoverBody kB>
+__global__ void __launch_bounds__(kMoverThreads)
+    move_pair_all_kernel(const __grid_constant__ MoveParams a, const __grid_constant__ MoveParams b) {
+  run_mover_body<kA, false, true, false>(a, blockIdx.x, gridDim.x);
+  run_mover_body<kB, true, false, false>(b, blockIdx.x, gridDim.x);
+}
+
 // Launch as a programmatic dependent of the kernel before it on the stream
 // (the kernel must begin with dependent_launch_entry()).
 template <typename... Params, typename... Args>
@@ -3256,6 +3266,10 @@ MoverBody pair_body(MoveParams* p, int64_t* ctas_wanted) {
 template <MoverBody kA, MoverBody kB>
 cudaError_t launch_pair_typed(const MoveParams& a, const MoveParams& b, int split, int grid, bool early,
                               cudaStream_t stream) {
+  if (split < 0) {  // large: every CTA takes part in both moves
+    move_pair_all_kernel<kA, kB><<<static_cast<unsigned>(grid), kMoverThreads, 0, stream>>>(a, b);
+    return cudaGetLastError();
+  }
   if (early)
     return launch_dependent(move_pair_kernel<kA, kB, true>, static_cast<unsigned>(grid), kMoverThreads, 0,
                             stream, a, b, split);
@@ -3303,11 +3317,12 @@ cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
   }
 }
 
-// Above this many bytes moved by the two together, each move keeps the GPU
-// busy on its own and two launches, each with all SMs and its own best
-// kernel, are faster than one split launch (B200, a decode step with 8 KV
-// heads, 64 MiB each way: 32.2 us per step paired against 29.4 in two
-// launches; with 1 KV head, 4 MiB each way: 6.0 us paired against 10.4).
+// Up to this many bytes moved by the two together, the CTAs are split
+// between the moves (each move's chain of loads runs once, side by side);
+// above it every CTA takes part in both, one after the other (a decode step
+// with 8 KV heads, 64 MiB each way, B200: 32.2 us per step split, 29.3 all
+// CTAs in both, 29.6 as two launches; with 1 KV head, 4 MiB each way: 6.0 us
+// split against 10.4 as two launches).
 constexpr double kPairMaxBytes = 32.0 * 1024 * 1024;
 
 cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gather, cudaStream_t stream) {
@@ -3316,7 +3331,7 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   const bool pairable = scatter.kind == MoveKind::kScatter && gather.kind == MoveKind::kGather &&
                         scatter.vec_bytes == 16 && gather.vec_bytes == 16 && scatter.gate == nullptr &&
                         gather.gate == nullptr && !((scatter.flags | gather.flags) & KVCA_FLAG_HOST_MEMORY) &&
-                        scatter.num_rows > 0 && gather.num_rows > 0 && bytes_a + bytes_b <= kPairMaxBytes;
+                        scatter.num_rows > 0 && gather.num_rows > 0;
   if (!pairable) {  // two launches, in this order
     if (scatter.num_rows > 0) {
       const cudaError_t e = launch_move(scatter, stream);
@@ -3329,6 +3344,15 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   int64_t want_a = 1, want_b = 1;
   const MoverBody body_a = pair_body(&a, &want_a);
   const MoverBody body_b = pair_body(&b, &want_b);
+  if (bytes_a + bytes_b > kPairMaxBytes) {  // every CTA takes part in both
+    const int sms_all = device_sm_count();
+    const int grid_all = sms_all > 0 ? sms_all : 1;
+    switch (body_a) {
+      case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, -1, grid_all, false, stream);
+      case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, -1, grid_all, false, stream);
+      default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, -1, grid_all, false, stream);
+    }
+  }
   // CTAs split by bytes over the resident grid (one CTA of 512 threads per SM)
   const int sms = device_sm_count();
   const int64_t grid_max = sms > 1 ? sms : 2;
