@@ -249,8 +249,7 @@ def inspect_save_requests(logical_to_physical: torch.Tensor, slot_meta: torch.Te
 
 def _bitmap(dev: torch.device, num_slots: int) -> torch.Tensor:
     words = (num_slots + 31) // 32
-    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
-           torch.cuda.current_stream(dev).cuda_stream, words)
+    key = (_index(dev), _stream(dev).value or 0, words)
     bm = _pop_bitmaps.get(key)
     if bm is None:
         bm = torch.zeros(words, dtype=torch.int32, device=dev)
@@ -386,8 +385,7 @@ _stream_scratch: dict[tuple[int, int, int], torch.Tensor] = {}
 
 def _clock_scratch(dev: torch.device, num_slots: int) -> torch.Tensor:
     words = int(_lib_handle.kvca_clock_stream_scratch_bytes(num_slots)) // 4
-    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
-           torch.cuda.current_stream(dev).cuda_stream, words)
+    key = (_index(dev), _stream(dev).value or 0, words)
     buf = _stream_scratch.get(key)
     if buf is None:
         buf = torch.zeros(words, dtype=torch.int32, device=dev)
