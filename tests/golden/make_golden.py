@@ -22,9 +22,16 @@ Fixtures written (JSON, small):
   * layout.json         - _MergedKVBlockLayout shapes and
                           _physical_slot_mapping outputs;
   * program.json        - the reference demo (test_program.py) transcript.
-The reference's 16-bit slot-meta mode (KVCA_SLOT_META_BITS=16) cannot be
-run here: its strict path calls index_select on a uint16 tensor, which torch
-2.11 does not implement on CPU, so no 16-bit fixtures are produced.
+  * kat_metadata_u16.json, pop_u16.json, scenarios_u16.json - the same
+                          with the reference's 16-bit slot meta
+                          (KVCA_SLOT_META_BITS=16: 8-bit pin and usage
+                          fields), made in a child process with that
+                          variable set.
+The reference's 16-bit mode calls index_select, index_put_ and arithmetic
+on uint16 tensors, which torch 2.11 implements for conversions only on CPU;
+the child installs install_uint16_shim (below), which computes those ops
+through the int16 view or int64 values with uint16 results, so the
+reference's own code runs unchanged.
 The Zipf and scenario generators live in kv_cache_adapter_b200/workloads.py
 so that the GPU tests and bench.py regenerate identical inputs.
 """
@@ -34,8 +41,10 @@ import argparse
 import contextlib
 import io
 import json
+import os
 import pathlib
 import shutil
+import subprocess
 import sys
 import tempfile
 
@@ -46,6 +55,71 @@ sys.path.insert(0, str(REPO))
 import torch  # noqa: E402
 
 from kv_cache_adapter_b200 import workloads  # noqa: E402
+
+
+def install_uint16_shim() -> None:
+    """Make the uint16 ops the reference's 16-bit mode needs run on a torch
+    build whose CPU kernels lack them (torch 2.11 implements conversions for
+    uint16 but not index_select, index_put_, arithmetic or comparisons).
+    Each wrapped op computes the same values through a wider or same-width
+    type: indexing and in-place copies on the int16 view (bit moves only),
+    arithmetic on int32 with the result wrapped to 16 bits (what uint16
+    arithmetic does), comparisons on int32 (exact for every uint16 value).
+    Only tensors whose dtype is uint16 take the wrapped path; the reference
+    code itself is unchanged."""
+    u16 = torch.uint16
+
+    def conv(x, fn):
+        if isinstance(x, torch.Tensor) and x.dtype == u16:
+            return fn(x)
+        if isinstance(x, (tuple, list)):
+            return type(x)(conv(y, fn) for y in x)
+        return x
+
+    def has_u16(a, k):
+        flat = list(a) + list(k.values())
+        return any(isinstance(x, torch.Tensor) and x.dtype == u16 or
+                   isinstance(x, (tuple, list)) and has_u16(x, {}) for x in flat)
+
+    i16 = lambda t: t.view(torch.int16)  # noqa: E731  same bits
+    i64 = lambda t: t.to(torch.int64)  # noqa: E731  same values
+
+    def bits(name, inplace):
+        orig = getattr(torch.Tensor, name)
+
+        def f(self, *a, **k):
+            if self.dtype == u16:  # bit moves on the int16 view; other dtypes convert mod 2^16
+                r = orig(i16(self), *conv(a, i16), **{kk: conv(v, i16) for kk, v in k.items()})
+                if inplace:
+                    return self
+                return r.view(u16) if isinstance(r, torch.Tensor) and r.dtype == torch.int16 else r
+            if has_u16(a, k):  # a uint16 operand into another dtype: by value
+                return orig(self, *conv(a, i64), **{kk: conv(v, i64) for kk, v in k.items()})
+            return orig(self, *a, **k)
+        setattr(torch.Tensor, name, f)
+
+    def arith(name, compare):
+        orig = getattr(torch.Tensor, name)
+
+        def f(self, other):
+            if self.dtype != u16 and not (isinstance(other, torch.Tensor) and other.dtype == u16):
+                return orig(self, other)
+            rt = torch.result_type(self, other)
+            r = orig(conv(self, i64), conv(other, i64))
+            if compare:
+                return r
+            return (r & 0xFFFF).to(u16) if rt == u16 else r.to(rt)
+        setattr(torch.Tensor, name, f)
+
+    for name in ("index_select",):
+        bits(name, inplace=False)
+    for name in ("index_put_", "index_fill_", "index_copy_", "copy_"):
+        bits(name, inplace=True)
+    for name in ("__add__", "__radd__", "__sub__", "__rsub__", "__mul__", "__rmul__", "__and__", "__rand__",
+                 "__or__", "__ror__", "__xor__", "__rshift__", "__lshift__"):
+        arith(name, compare=False)
+    for name in ("__eq__", "__ne__", "__lt__", "__le__", "__gt__", "__ge__"):
+        arith(name, compare=True)
 
 
 def _import_reference(scratch: pathlib.Path):
@@ -317,21 +391,35 @@ def program_transcript(scratch: pathlib.Path) -> dict:
     return {"stdout": lines}
 
 
+POP_U16 = dict(count=200, seed=4321)
+SCENARIOS_U16 = dict(count=30, seed=4321)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--meta16", action="store_true", help="(child) the 16-bit fixtures")
     args = ap.parse_args()
     out = pathlib.Path(args.out)
+
+    def dump(name: str, obj) -> None:
+        (out / name).write_text(json.dumps(obj, separators=(",", ":")) + "\n")
 
     with tempfile.TemporaryDirectory() as tmp:
         scratch = pathlib.Path(tmp)
         shutil.copytree(args.reference, scratch / "kv_cache_adapter")
+        if args.meta16:
+            assert os.environ.get("KVCA_SLOT_META_BITS") == "16"
+            install_uint16_shim()
+            ref = _import_reference(scratch)
+            assert ref.SLOT_META_DTYPE == torch.uint16
+            dump("kat_metadata_u16.json", kat_cases(ref))
+            dump("pop_u16.json", pop_cases(ref, **POP_U16))
+            dump("scenarios_u16.json", scenarios(ref, **SCENARIOS_U16))
+            return
         ref = _import_reference(scratch)
         assert ref.SLOT_META_DTYPE == torch.uint8, "run with 8-bit slot meta"
-
-        def dump(name: str, obj) -> None:
-            (out / name).write_text(json.dumps(obj, separators=(",", ":")) + "\n")
 
         dump("kat_metadata.json", kat_cases(ref))
         dump("pop_u8.json", pop_cases(ref, 400, seed=1234))
@@ -339,6 +427,9 @@ def main() -> None:
         dump("clock_stream.json", clock_streams(ref))
         dump("layout.json", layout_cases(ref))
         dump("program.json", program_transcript(scratch))
+    env = dict(os.environ, KVCA_SLOT_META_BITS="16")
+    subprocess.run([sys.executable, __file__, "--reference", args.reference, "--out", str(out), "--meta16"],
+                   env=env, check=True)
 
 
 if __name__ == "__main__":

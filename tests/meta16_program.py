@@ -6,6 +6,8 @@ file in a child process with the variable set:
 
     KVCA_SLOT_META_BITS=16 python tests/meta16_program.py cpu   # oracle op set only
     KVCA_SLOT_META_BITS=16 python tests/meta16_program.py gpu   # CUDA paths vs the oracle
+    KVCA_SLOT_META_BITS=16 python tests/meta16_program.py golden      # reference scenarios, oracle op set
+    KVCA_SLOT_META_BITS=16 python tests/meta16_program.py golden-gpu  # reference scenarios, CUDA paths
 
 Exit status 0 when every check holds.
 """
@@ -106,8 +108,32 @@ def check_gpu() -> None:
         kv_cache_adapter_cuda.check_status(dev)
 
 
+def check_golden() -> None:
+    """The scenarios recorded from the reference in its 16-bit mode, through
+    this repository's adapter driven by the oracle op set."""
+    import scenario_runner
+
+    cases = scenario_runner.load_scenarios("scenarios_u16.json")
+    assert len(cases) == 30
+    for case in cases:
+        ops = OracleOps()
+        scenario_runner.run_and_compare(case, torch.device("cpu"), native_ext=ops, backend_ops=ops)
+
+
+def check_golden_gpu() -> None:
+    """The same scenarios through the CUDA adapter on each of its paths."""
+    import scenario_runner
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda
+
+    dev = torch.device("cuda", 0)
+    for case in scenario_runner.load_scenarios("scenarios_u16.json"):
+        for path in ("device_store", "planned", "stepwise"):
+            scenario_runner.run_and_compare(case, dev, planned=path != "stepwise", record=path != "device_store")
+    kv_cache_adapter_cuda.check_status(dev)
+
+
 if __name__ == "__main__":
     if os.environ.get("KVCA_SLOT_META_BITS") != "16":
         sys.exit("run with KVCA_SLOT_META_BITS=16")
-    {"cpu": check_cpu, "gpu": check_gpu}[sys.argv[1]]()
+    {"cpu": check_cpu, "gpu": check_gpu, "golden": check_golden, "golden-gpu": check_golden_gpu}[sys.argv[1]]()
     print("meta16 ok:", sys.argv[1])

@@ -1,4 +1,4 @@
-"""Replays recorded reference scenarios (tests/golden/scenarios_u8.json) through
+"""Replays recorded reference scenarios (tests/golden/scenarios_u*.json) through
 this repository's KVCacheAdapter and compares the full state after every op."""
 from __future__ import annotations
 
@@ -12,8 +12,11 @@ from kv_cache_adapter_b200 import InMemoryBlockStoreBackend, KVCacheAdapter
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
 
 
-def load_scenarios() -> list[dict]:
-    return json.loads((GOLDEN / "scenarios_u8.json").read_text())
+def load_scenarios(name: str = "scenarios_u8.json") -> list[dict]:
+    """scenarios_u8.json (8-bit slot meta) or scenarios_u16.json (recorded
+    with KVCA_SLOT_META_BITS=16; replay those in a process with the same
+    setting)."""
+    return json.loads((GOLDEN / name).read_text())
 
 
 def _flat(t: torch.Tensor | None):

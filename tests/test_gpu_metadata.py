@@ -51,66 +51,77 @@ def _gold(golden_dir, name):
     return json.loads((golden_dir / name).read_text())
 
 
+# known answers recorded with 8-bit slot meta and with the reference's 16-bit mode
+KAT_FIXTURES = [("kat_metadata.json", torch.uint8), ("kat_metadata_u16.json", torch.uint16)]
+
+
 # ---------------------------------------------------------------------------
 # the reference's known answers (test_adapter_npu_kernels.py:42-194)
 # ---------------------------------------------------------------------------
 
 
-def test_kat_inspect_save(ops, golden_dir):
-    c = _gold(golden_dir, "kat_metadata.json")["inspect_save"]
-    cur, existing, usage = ops.inspect_save_requests(_ids(c["l2p"]), _meta(c["slot_meta"]), _ids(c["ids"]))
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_inspect_save(ops, golden_dir, fixture, dtype):
+    c = _gold(golden_dir, fixture)["inspect_save"]
+    cur, existing, usage = ops.inspect_save_requests(_ids(c["l2p"]), _meta(c["slot_meta"], dtype), _ids(c["ids"]))
     assert cur.tolist() == c["expect"]["cur"]
     assert existing.dtype == torch.bool and existing.int().tolist() == c["expect"]["existing"]
-    assert usage.dtype == torch.uint8 and usage.tolist() == c["expect"]["usage"]
+    assert usage.dtype == dtype and usage.tolist() == c["expect"]["usage"]
 
 
-def test_kat_inspect_load(ops, golden_dir):
-    c = _gold(golden_dir, "kat_metadata.json")["inspect_load"]
-    cur, resident, pins, usage = ops.inspect_load_requests(_ids(c["l2p"]), _meta(c["slot_meta"]), _ids(c["ids"]))
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_inspect_load(ops, golden_dir, fixture, dtype):
+    c = _gold(golden_dir, fixture)["inspect_load"]
+    cur, resident, pins, usage = ops.inspect_load_requests(_ids(c["l2p"]), _meta(c["slot_meta"], dtype), _ids(c["ids"]))
     assert cur.tolist() == c["expect"]["cur"]
     assert resident.int().tolist() == c["expect"]["resident"]
     assert pins.dtype == torch.int64 and pins.tolist() == c["expect"]["pins"]
     assert usage.tolist() == c["expect"]["usage"]
 
 
-def test_kat_pop(ops, golden_dir):
-    c = _gold(golden_dir, "kat_metadata.json")["pop"]
-    meta, ss = _meta(c["slot_meta"]), _ids([c["search_start"]])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_pop(ops, golden_dir, fixture, dtype):
+    c = _gold(golden_dir, fixture)["pop"]
+    meta, ss = _meta(c["slot_meta"], dtype), _ids([c["search_start"]])
     sel = ops.pop_reusable_slots(meta, ss, _ids(c["blocked"]), c["count"])
     assert sel.tolist() == c["expect"]["selected"] == [3, 0]
     assert ss.tolist() == [c["expect"]["search_start"]]
     assert meta.tolist() == c["expect"]["slot_meta"]
 
 
-def test_kat_pop_prefix_order(ops, golden_dir):
-    c = _gold(golden_dir, "kat_metadata.json")["pop"]
-    meta, ss = _meta(c["slot_meta"]), _ids([c["search_start"]])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_pop_prefix_order(ops, golden_dir, fixture, dtype):
+    c = _gold(golden_dir, fixture)["pop"]
+    meta, ss = _meta(c["slot_meta"], dtype), _ids([c["search_start"]])
     sel = ops.pop_reusable_slots(meta, ss, _ids(c["blocked"]), c["count"], order="prefix")
     assert sel.tolist() == [0, 3] and ss.tolist() == [0]
 
 
-def test_kat_commit_save(ops, golden_dir):
-    c = _gold(golden_dir, "kat_metadata.json")["commit_save"]
-    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_commit_save(ops, golden_dir, fixture, dtype):
+    c = _gold(golden_dir, fixture)["commit_save"]
+    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"], dtype)
     ops.commit_save_metadata(l2p, p2l, meta, _ids(c["evicted"]), _ids(c["ids"]), _ids(c["slots"]),
-                             _meta(c["final_pins"]), _meta(c["final_usage"]))
+                             _meta(c["final_pins"], dtype), _meta(c["final_usage"], dtype))
     assert l2p.tolist() == c["expect"]["l2p"] and p2l.tolist() == c["expect"]["p2l"]
     assert meta.tolist() == c["expect"]["slot_meta"]
 
 
-def test_kat_commit_load(ops, golden_dir):
-    c = _gold(golden_dir, "kat_metadata.json")["commit_load"]
-    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_commit_load(ops, golden_dir, fixture, dtype):
+    c = _gold(golden_dir, fixture)["commit_load"]
+    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"], dtype)
     ops.commit_load_metadata(l2p, p2l, meta, _ids(c["evicted"]), _ids(c["miss_ids"]), _ids(c["miss_slots"]),
-                             _ids(c["hit_slots"]), _ids(c["hit_pins"]), _meta(c["hit_usage"]),
-                             _meta(c["miss_usage"]))
+                             _ids(c["hit_slots"]), _ids(c["hit_pins"]), _meta(c["hit_usage"], dtype),
+                             _meta(c["miss_usage"], dtype))
     assert l2p.tolist() == c["expect"]["l2p"] and p2l.tolist() == c["expect"]["p2l"]
     assert meta.tolist() == c["expect"]["slot_meta"]
 
 
-def test_kat_release(ops, golden_dir):
-    c = _gold(golden_dir, "kat_metadata.json")["release"]
-    meta = _meta(c["slot_meta"])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_release(ops, golden_dir, fixture, dtype):
+    c = _gold(golden_dir, fixture)["release"]
+    meta = _meta(c["slot_meta"], dtype)
     ops.release_metadata(_ids(c["l2p"]), meta, _ids(c["ids"]))
     assert meta.tolist() == c["expect"]["slot_meta"]
 
@@ -120,12 +131,14 @@ def test_kat_release(ops, golden_dir):
 # ---------------------------------------------------------------------------
 
 
-def test_pop_reference_cases(ops, golden_dir):
-    """400 cases recorded from the reference's strict path, bit-exact."""
+@pytest.mark.parametrize("fixture,dtype", [("pop_u8.json", torch.uint8), ("pop_u16.json", torch.uint16)])
+def test_pop_reference_cases(ops, golden_dir, fixture, dtype):
+    """Cases recorded from the reference's strict path (400 with 8-bit slot
+    meta, 200 in its 16-bit mode), bit-exact."""
     from kv_cache_adapter_b200.errors import InsufficientCapacityError
 
-    for i, c in enumerate(_gold(golden_dir, "pop_u8.json")):
-        meta, ss = _meta(c["slot_meta"]), _ids([c["search_start"]])
+    for i, c in enumerate(_gold(golden_dir, fixture)):
+        meta, ss = _meta(c["slot_meta"], dtype), _ids([c["search_start"]])
         try:
             sel, err = ops.pop_reusable_slots(meta, ss, _ids(c["blocked"]), c["count"]).tolist(), None
         except InsufficientCapacityError:

@@ -25,3 +25,13 @@ def test_meta16_pins_and_usage_on_cpu():
 @pytest.mark.gpu
 def test_meta16_adapter_paths_match_oracle():
     _run("gpu")
+
+
+def test_meta16_reference_scenarios_on_cpu():
+    """Scenarios recorded from the reference's own 16-bit mode."""
+    _run("golden")
+
+
+@pytest.mark.gpu
+def test_meta16_reference_scenarios_on_gpu():
+    _run("golden-gpu")

@@ -25,8 +25,13 @@ def _ids(v):
     return torch.tensor(v, dtype=torch.int64)
 
 
-def _meta(v):
-    return torch.tensor(v, dtype=torch.uint8)
+def _meta(v, dtype=torch.uint8):
+    return torch.tensor(v, dtype=torch.int64).to(dtype)
+
+
+# the reference's known answers and pop cases with 8-bit slot meta, and with
+# 16-bit slot meta (KVCA_SLOT_META_BITS=16: 8-bit pin and usage fields)
+KAT_FIXTURES = [("kat_metadata.json", torch.uint8), ("kat_metadata_u16.json", torch.uint16)]
 
 
 # ---------------------------------------------------------------------------
@@ -34,56 +39,62 @@ def _meta(v):
 # ---------------------------------------------------------------------------
 
 
-def test_kat_inspect_save(golden_dir):
-    c = _load(golden_dir, "kat_metadata.json")["inspect_save"]
-    cur, existing, usage = oracle.inspect_save_requests(_ids(c["l2p"]), _meta(c["slot_meta"]), _ids(c["ids"]))
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_inspect_save(golden_dir, fixture, dtype):
+    c = _load(golden_dir, fixture)["inspect_save"]
+    cur, existing, usage = oracle.inspect_save_requests(_ids(c["l2p"]), _meta(c["slot_meta"], dtype), _ids(c["ids"]))
     assert cur.tolist() == c["expect"]["cur"]
     assert existing.int().tolist() == c["expect"]["existing"]
     assert usage.tolist() == c["expect"]["usage"]
 
 
-def test_kat_inspect_load(golden_dir):
-    c = _load(golden_dir, "kat_metadata.json")["inspect_load"]
-    cur, resident, pins, usage = oracle.inspect_load_requests(_ids(c["l2p"]), _meta(c["slot_meta"]), _ids(c["ids"]))
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_inspect_load(golden_dir, fixture, dtype):
+    c = _load(golden_dir, fixture)["inspect_load"]
+    cur, resident, pins, usage = oracle.inspect_load_requests(_ids(c["l2p"]), _meta(c["slot_meta"], dtype), _ids(c["ids"]))
     assert cur.tolist() == c["expect"]["cur"]
     assert resident.int().tolist() == c["expect"]["resident"]
     assert pins.tolist() == c["expect"]["pins"]
     assert usage.tolist() == c["expect"]["usage"]
 
 
-def test_kat_pop_threshold_scan_and_age(golden_dir):
-    c = _load(golden_dir, "kat_metadata.json")["pop"]
-    meta, ss = _meta(c["slot_meta"]), _ids([c["search_start"]])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_pop_threshold_scan_and_age(golden_dir, fixture, dtype):
+    c = _load(golden_dir, fixture)["pop"]
+    meta, ss = _meta(c["slot_meta"], dtype), _ids([c["search_start"]])
     sel = oracle.pop_reusable_slots(meta, ss, _ids(c["blocked"]), c["count"])
     assert sel.tolist() == c["expect"]["selected"] == [3, 0]
     assert ss.tolist() == [c["expect"]["search_start"]]
     assert meta.tolist() == c["expect"]["slot_meta"]
 
 
-def test_kat_commit_save(golden_dir):
-    c = _load(golden_dir, "kat_metadata.json")["commit_save"]
-    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_commit_save(golden_dir, fixture, dtype):
+    c = _load(golden_dir, fixture)["commit_save"]
+    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"], dtype)
     oracle.commit_save_metadata(l2p, p2l, meta, _ids(c["evicted"]), _ids(c["ids"]), _ids(c["slots"]),
-                                _meta(c["final_pins"]), _meta(c["final_usage"]))
+                                _meta(c["final_pins"], dtype), _meta(c["final_usage"], dtype))
     assert l2p.tolist() == c["expect"]["l2p"]
     assert p2l.tolist() == c["expect"]["p2l"]
     assert meta.tolist() == c["expect"]["slot_meta"]
 
 
-def test_kat_commit_load(golden_dir):
-    c = _load(golden_dir, "kat_metadata.json")["commit_load"]
-    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_commit_load(golden_dir, fixture, dtype):
+    c = _load(golden_dir, fixture)["commit_load"]
+    l2p, p2l, meta = _ids(c["l2p"]), _ids(c["p2l"]), _meta(c["slot_meta"], dtype)
     oracle.commit_load_metadata(l2p, p2l, meta, _ids(c["evicted"]), _ids(c["miss_ids"]), _ids(c["miss_slots"]),
-                                _ids(c["hit_slots"]), _ids(c["hit_pins"]), _meta(c["hit_usage"]),
-                                _meta(c["miss_usage"]))
+                                _ids(c["hit_slots"]), _ids(c["hit_pins"]), _meta(c["hit_usage"], dtype),
+                                _meta(c["miss_usage"], dtype))
     assert l2p.tolist() == c["expect"]["l2p"]
     assert p2l.tolist() == c["expect"]["p2l"]
     assert meta.tolist() == c["expect"]["slot_meta"]
 
 
-def test_kat_release(golden_dir):
-    c = _load(golden_dir, "kat_metadata.json")["release"]
-    meta = _meta(c["slot_meta"])
+@pytest.mark.parametrize("fixture,dtype", KAT_FIXTURES)
+def test_kat_release(golden_dir, fixture, dtype):
+    c = _load(golden_dir, fixture)["release"]
+    meta = _meta(c["slot_meta"], dtype)
     oracle.release_metadata(_ids(c["l2p"]), meta, _ids(c["ids"]))
     assert meta.tolist() == c["expect"]["slot_meta"]
 
@@ -93,11 +104,13 @@ def test_kat_release(golden_dir):
 # ---------------------------------------------------------------------------
 
 
-def test_pop_cases_match_reference(golden_dir):
-    cases = _load(golden_dir, "pop_u8.json")
-    assert len(cases) == 400
+@pytest.mark.parametrize("fixture,dtype,count", [("pop_u8.json", torch.uint8, 400),
+                                                 ("pop_u16.json", torch.uint16, 200)])
+def test_pop_cases_match_reference(golden_dir, fixture, dtype, count):
+    cases = _load(golden_dir, fixture)
+    assert len(cases) == count
     for i, c in enumerate(cases):
-        meta = _meta(c["slot_meta"])
+        meta = _meta(c["slot_meta"], dtype)
         ss = _ids([c["search_start"]])
         try:
             sel = oracle.pop_reusable_slots(meta, ss, _ids(c["blocked"]), c["count"]).tolist()
@@ -118,6 +131,15 @@ def test_pop_cases_regenerate_identically(golden_dir):
     for c, r in zip(cases, regen):
         assert c["usage"] == r["usage"] and c["pins"] == r["pins"] and c["blocked"] == r["blocked"]
         assert c["count"] == r["count"] and c["search_start"] == r["search_start"]
+
+
+def test_pop_u16_cases_regenerate_identically(golden_dir):
+    cases = _load(golden_dir, "pop_u16.json")
+    regen = list(workloads.pop_case_params(len(cases), 4321, usage_max=255, pin_max=255))
+    for c, r in zip(cases, regen):
+        assert c["usage"] == r["usage"] and c["pins"] == r["pins"] and c["blocked"] == r["blocked"]
+        assert c["count"] == r["count"] and c["search_start"] == r["search_start"]
+    assert max(max(c["usage"]) for c in cases) == 255  # past the 4-bit field
 
 
 def test_pop_prefix_order_differs_on_known_answer():
