@@ -22,7 +22,8 @@ Fixtures written (JSON, small):
   * layout.json         - _MergedKVBlockLayout shapes and
                           _physical_slot_mapping outputs;
   * program.json        - the reference demo (test_program.py) transcript.
-  * kat_metadata_u16.json, pop_u16.json, scenarios_u16.json - the same
+  * kat_metadata_u16.json, pop_u16.json, scenarios_u16.json,
+    clock_stream_u16.json - the same
                           with the reference's 16-bit slot meta
                           (KVCA_SLOT_META_BITS=16: 8-bit pin and usage
                           fields), made in a child process with that
@@ -417,6 +418,7 @@ def main() -> None:
             dump("kat_metadata_u16.json", kat_cases(ref))
             dump("pop_u16.json", pop_cases(ref, **POP_U16))
             dump("scenarios_u16.json", scenarios(ref, **SCENARIOS_U16))
+            dump("clock_stream_u16.json", clock_streams(ref))
             return
         ref = _import_reference(scratch)
         assert ref.SLOT_META_DTYPE == torch.uint8, "run with 8-bit slot meta"

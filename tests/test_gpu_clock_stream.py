@@ -38,10 +38,13 @@ def _method(name):
 
 
 @pytest.mark.parametrize("method", METHODS)
-def test_recorded_reference_streams(ops, golden_dir, method):
-    for rec in json.loads((golden_dir / "clock_stream.json").read_text()):
+@pytest.mark.parametrize("fixture", ["clock_stream.json", "clock_stream_u16.json"])
+def test_recorded_reference_streams(ops, golden_dir, method, fixture):
+    """Streams recorded from the reference (8-bit slot meta, and its 16-bit mode)."""
+    pack = adapter_mod._pack_slot_meta if fixture == "clock_stream.json" else _pack16
+    for rec in json.loads((golden_dir / fixture).read_text()):
         p = rec["params"]
-        meta = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta).to(DEV)
+        meta = workloads.clock_initial_meta(p, pack).to(DEV)
         ss = torch.zeros(1, dtype=torch.int64, device=DEV)
         victims, done = ops.clock_stream(meta, ss, p["num_steps"], p["alloc_per_step"],
                                          workloads.zipf_reaccess(p).to(DEV), p["reaccess_per_step"],

@@ -166,10 +166,17 @@ def test_pop_bad_blocked_index_raises_without_mutation():
 # ---------------------------------------------------------------------------
 
 
-def test_clock_streams_match_reference(golden_dir):
-    for rec in _load(golden_dir, "clock_stream.json"):
+def _pack16(pins, usage):
+    """16-bit slot word: 8-bit pin | 8-bit usage << 8."""
+    return ((pins.to(torch.int64) & 255) | ((usage.to(torch.int64) & 255) << 8)).to(torch.uint16)
+
+
+@pytest.mark.parametrize("fixture,pack", [("clock_stream.json", adapter_mod._pack_slot_meta),
+                                          ("clock_stream_u16.json", _pack16)])
+def test_clock_streams_match_reference(golden_dir, fixture, pack):
+    for rec in _load(golden_dir, fixture):
         p = rec["params"]
-        meta = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta)
+        meta = workloads.clock_initial_meta(p, pack)
         ss = _ids([0])
         victims, done, rc = oracle.clock_stream(meta, ss, p["num_steps"], p["alloc_per_step"],
                                                 workloads.zipf_reaccess(p), p["reaccess_per_step"])
