@@ -121,7 +121,8 @@ def check_golden() -> None:
 
 
 def check_golden_gpu() -> None:
-    """The same scenarios through the CUDA adapter on each of its paths."""
+    """The same scenarios through the CUDA adapter on each of its paths, and
+    against a pinned host store."""
     import scenario_runner
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda
 
@@ -129,6 +130,8 @@ def check_golden_gpu() -> None:
     for case in scenario_runner.load_scenarios("scenarios_u16.json"):
         for path in ("device_store", "planned", "stepwise"):
             scenario_runner.run_and_compare(case, dev, planned=path != "stepwise", record=path != "device_store")
+        # the store in pinned host memory (the host tier's device-store path)
+        scenario_runner.run_and_compare(case, dev, planned=True, record=False, host_tier=True)
     kv_cache_adapter_cuda.check_status(dev)
 
 
