@@ -695,6 +695,8 @@ def _store_call_buffers(dev: torch.device) -> _StoreCallBuffers:
     key = (idx, _stream(dev).value or 0)
     got = _store_buffers.get(key)
     if got is None:
+        if len(_store_buffers) >= 64:  # many short-lived streams: start over
+            _store_buffers.clear()
         got = _StoreCallBuffers(torch.device("cuda", idx))
         _store_buffers[key] = got
     return got
