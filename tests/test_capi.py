@@ -69,3 +69,31 @@ def test_host_side_argument_checks_need_no_device():
     assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), 1, 4, 0, 0, null, null) == bad
     assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), 1, 4, 16, 0, null, null) == bad  # null planes
     assert lib.kvca_gather(ctypes.byref(src), ctypes.byref(dst), 1, 0, 16, 0, null, null) == 0  # nothing to move
+
+
+def test_decode_loop_entry_points_check_arguments_on_the_host():
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    bad = _lib.KVCA_ERR_BAD_ARGUMENT
+    # append_steps: no table, negative step count, missing offsets with steps to run
+    assert lib.kvca_append_steps(8, 0, null, 0, null, null, 4, null, null, null, 0, 1, null, null, null, 2, 16,
+                                 null, null, null, null, null) == bad
+    one = ctypes.c_void_p(16)  # never dereferenced: the call is refused first
+    assert lib.kvca_append_steps(8, 0, one, 8, one, one, 4, one, null, null, 0, -1, one, one, one, 2, 16,
+                                 one, null, one, one, null) == bad
+    assert lib.kvca_append_steps(8, 0, one, 8, one, one, 4, one, null, null, 0, 3, one, one, one, 2, 16,
+                                 one, null, one, one, null) == bad
+    # zero steps is a no-op
+    assert lib.kvca_append_steps(8, 0, one, 8, one, one, 4, one, null, null, 0, 0, one, one, one, 2, 16,
+                                 one, null, null, one, null) == 0
+    # scatter_gather: plane and row limits on either side, missing descriptors
+    c, pdesc = _lib.ChunkDesc(), _lib.PagedDesc()
+    args = (ctypes.byref(c), ctypes.byref(pdesc))
+    assert lib.kvca_scatter_gather(*args, 0, 4, 16, ctypes.byref(pdesc), ctypes.byref(c), 1, 4, 16, 0, 0, null,
+                                   null) == bad
+    assert lib.kvca_scatter_gather(*args, 1, 4, 16, ctypes.byref(pdesc), ctypes.byref(c), 1, 4, 0, 0, 0, null,
+                                   null) == bad
+    assert lib.kvca_scatter_gather(*args, 1, 4, 16, ctypes.byref(pdesc), ctypes.byref(c), 1, 4, 16, 0, 0, null,
+                                   null) == bad  # null plane tables
+    assert lib.kvca_scatter_gather(*args, 1, 0, 16, ctypes.byref(pdesc), ctypes.byref(c), 1, 0, 16, 0, 0, null,
+                                   null) == 0  # nothing to move
