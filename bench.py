@@ -228,6 +228,23 @@ def slot_mapping_of(table: torch.Tensor, block_size: int) -> torch.Tensor:
     return (table.view(-1, 1) * block_size + offsets.view(1, -1)).reshape(-1)
 
 
+def full_byte_check(chunks: torch.Tensor, planes, index: torch.Tensor, tokens: bool) -> int:
+    """Every byte of ``chunks`` against the cache rows that ``index`` names,
+    plane by plane, with torch ``index_select`` on the device (the reference's
+    own gather op, adapter.py:543) as the checker.  Returns the bytes compared;
+    raises on the first differing plane."""
+    n = index.numel()
+    for p, plane in enumerate(planes):
+        rows = plane.shape[0] * plane.shape[1] if tokens else plane.shape[0]
+        src = plane.reshape(rows, -1)
+        src = src.view(torch.uint8) if src.element_size() == 1 else src.view(torch.int16)
+        got = chunks[:, p].reshape(n, -1)
+        got = got.view(torch.uint8) if got.element_size() == 1 else got.view(torch.int16)
+        if not torch.equal(got, src.index_select(0, index)):
+            raise RuntimeError(f"bench data check failed: plane {p} of the chunks differs from the cache")
+    return chunks.numel() * chunks.element_size()
+
+
 def block_bytes(w: dict) -> int:
     return w["block_size"] * w["heads"] * w["head_dim"] * torch.empty(0, dtype=w["dtype"]).element_size()
 
@@ -270,21 +287,74 @@ def cpu_moves(w: dict, steps: int, warmup: int) -> dict:
                       + " on CPU tensors"}
 
 
-def cpu_clock(k: int) -> dict:
-    import oracle
+CLOCK_VARIANTS = {
+    # the clock stress as specified: 25% of the slots start at usage 0, so no pop ages
+    "stress": dict(slots=1 << 20, usage_hi=3, no_zero=False,
+                   label="1,048,576 slots, usage U{0..3}, 5% pinned"),
+    # no usage-0 slot at the start and a pool the size of the decode mix's:
+    # the first pop ages, and aging recurs whenever the zeros it made run out
+    "aging": dict(slots=1 << 16, usage_hi=15, no_zero=True,
+                  label="65,536 slots, usage U{1..15} (no usage-0 slot at the start), 5% pinned"),
+}
+
+
+def clock_inputs(k: int, variant: str = "stress"):
+    """Parameters, initial slot_meta (CPU) and re-access ids (CPU) of a clock
+    stream: 200k allocations in steps of k, one Zipf(1.1) re-access each."""
     from kv_cache_adapter_b200 import adapter as adapter_mod
     from kv_cache_adapter_b200 import workloads
 
+    v = CLOCK_VARIANTS[variant]
     steps = 200_000 // k
-    p = workloads.clock_params(1 << 20, steps, k, k, seed=1234)
+    p = workloads.clock_params(v["slots"], steps, k, k, seed=1234, usage_hi=v["usage_hi"])
     meta = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta)
-    reacc = workloads.zipf_reaccess(p)
+    if v["no_zero"]:
+        usage = (meta >> 4).to(torch.int64)
+        meta = adapter_mod._pack_slot_meta((meta & 15).to(torch.int64), torch.clamp(usage, min=1))
+    return p, meta, workloads.zipf_reaccess(p)
+
+
+def clock_algorithmic_bytes(victims: torch.Tensor, thresholds: torch.Tensor, n: int, k: int) -> int:
+    """Algorithmic bytes of a clock stream from the oracle's trace: per pop,
+    the slot words scanned from search_start to its last victim when it does
+    not age, else a read and a write of every word; the 8-byte victim ids;
+    the refill (read + write of each victim's word); the 8-byte re-access ids
+    and the usage bump (read + write of each re-accessed word)."""
+    import numpy as np
+
+    steps = thresholds.numel()
+    last = victims.view(steps, k)[:, -1].numpy()
+    ss = np.concatenate([[0], (last[:-1] + 1) % n])
+    scanned = np.where(thresholds.numpy() > 0, 2 * n, (last - ss) % n + 1)
+    return int(scanned.sum()) + steps * k * (8 + 2) + steps * k * (8 + 2)
+
+
+def cpu_clock(k: int, variant: str = "stress") -> dict:
+    """The sequential C restatement of the stream on one host core, and the
+    stream's algorithmic bytes and aging steps from its trace."""
+    import oracle
+
+    p, meta, reacc = clock_inputs(k, variant)
+    steps = p["num_steps"]
     ss = torch.zeros(1, dtype=torch.int64)
     t0 = time.perf_counter()
-    _, done, rc = oracle.clock_stream(meta, ss, steps, k, reacc, k)
+    victims, done, rc, thresholds = oracle.clock_stream(meta, ss, steps, k, reacc, k, trace=True)
     dt = time.perf_counter() - t0
+    assert rc == 0 and done == steps
     return {"value": round(done * k / dt, 1), "unit": "evictions/s", "cores": 1, "kind": "port",
-            "sample": f"the full clock stress ({done * k} allocations), sequential C restatement"}
+            "sample": f"the full {variant} stream ({done * k} allocations), sequential C restatement",
+            "alloc_per_step": k, "variant": variant,
+            "algorithmic_bytes": clock_algorithmic_bytes(victims, thresholds, p["num_slots"], k),
+            "aging_steps": int((thresholds > 0).sum())}
+
+
+def clock_roofline(run: dict, trace: dict, peak: float) -> dict:
+    achieved = trace["algorithmic_bytes"] / (run["ms"] / 1e3) / 1e9
+    return {"bound": "latency", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 5), "traffic": None,
+            "algorithmic_bytes": trace["algorithmic_bytes"], "aging_steps": trace["aging_steps"],
+            "note": "a chain of dependent pops over a few MB of slot words: dependent phases and grid "
+                    "barriers bound it, not HBM"}
 
 
 # ---------------------------------------------------------------------------
@@ -292,15 +362,13 @@ def cpu_clock(k: int) -> dict:
 # ---------------------------------------------------------------------------
 
 
-def gpu_clock(device, k: int, reps: int = 3, method: str = "batched") -> dict:
-    from kv_cache_adapter_b200 import adapter as adapter_mod
+def gpu_clock(device, k: int, reps: int = 3, method: str = "batched", variant: str = "stress") -> dict:
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
     from kv_cache_adapter_b200 import workloads
 
-    steps = 200_000 // k
-    p = workloads.clock_params(1 << 20, steps, k, k, seed=1234)
-    meta0 = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta).to(device)
-    reacc = workloads.zipf_reaccess(p).to(device)
+    p, meta0, reacc = clock_inputs(k, variant)
+    steps = p["num_steps"]
+    meta0, reacc = meta0.to(device), reacc.to(device)
     meta = meta0.clone()
     ss = torch.zeros(1, dtype=torch.int64, device=device)
     victims = torch.empty(steps * k, dtype=torch.int64, device=device)
@@ -319,9 +387,177 @@ def gpu_clock(device, k: int, reps: int = 3, method: str = "batched") -> dict:
             ms.append(e0.elapsed_time(e1))
     ops.check_status(device)
     best = min(ms)
-    return {"alloc_per_step": k, "method": method, "steps": steps, "ms": round(best, 3),
+    return {"variant": variant, "alloc_per_step": k, "method": method, "steps": steps, "ms": round(best, 3),
             "evictions_per_s": round(steps * k / (best / 1e3), 1), "launches": 1,
             "victims_sha256": workloads.sha256_of(victims), "slot_meta_sha256": workloads.sha256_of(meta)}
+
+
+# ---------------------------------------------------------------------------
+# Per-call pop at 1,048,576 slots (the clock-stress table)
+# ---------------------------------------------------------------------------
+
+POP_SLOTS = 1 << 20
+POP_CASES = ((1, 0), (256, 0), (1, 64), (256, 64))  # (count, blocked ids)
+
+
+def pop_inputs() -> tuple[dict, torch.Tensor]:
+    """The clock-stress table (usage U{0..3}, 5% pinned, seed 1234) and its
+    aging variant (every usage + 1: no free slot has usage 0, so each pop must
+    age the whole table), plus 64 seeded blocked ids."""
+    import numpy as np
+
+    from kv_cache_adapter_b200 import adapter as adapter_mod
+    from kv_cache_adapter_b200 import workloads
+
+    p = workloads.clock_params(POP_SLOTS, 1, 1, 1, seed=1234)
+    meta = workloads.clock_initial_meta(p, adapter_mod._pack_slot_meta)
+    pins, usage = meta & 15, meta >> 4
+    aging = adapter_mod._pack_slot_meta(pins.to(torch.int64), usage.to(torch.int64) + 1)
+    blocked = torch.from_numpy(np.random.default_rng(99).integers(0, POP_SLOTS, 64).astype(np.int64))
+    return {"no-aging": meta, "aging": aging}, blocked
+
+
+def _pop_bytes(table: str, ss_before: int, last: int, count: int) -> int:
+    """Algorithmic bytes of one pop: the slot words scanned up to the last
+    victim when nothing ages, else a read and a write of every word; plus the
+    8-byte victim ids."""
+    scanned = (last - ss_before) % POP_SLOTS + 1 if table == "no-aging" else 2 * POP_SLOTS
+    return scanned + 8 * count
+
+
+def gpu_pop(device, calls: int = 200) -> dict:
+    """kv_cache_adapter_cuda.pop_reusable_slots per call: wall time of a call
+    that returns with the victims ready and the status read (as the reference's
+    op synchronises at nonzero), and the device time of its launch."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+
+    tables, blocked_h = pop_inputs()
+    peak, _ = _peaks()
+    runs = []
+    for name, base_h in tables.items():
+        base = base_h.to(device)
+        restore = name == "aging"
+        for count, nb in POP_CASES:
+            blocked = blocked_h[:nb].to(device)
+            for order in ("prefix", "grouped"):
+                meta = base.clone()
+                ss = torch.zeros(1, dtype=torch.int64, device=device)
+                for _ in range(5):
+                    if restore:
+                        meta.copy_(base)
+                    ops.pop_reusable_slots(meta, ss, blocked, count, order=order)
+                wall, dev_ms, nbytes = [], [], []
+                for _ in range(calls):
+                    if restore:
+                        meta.copy_(base)
+                    torch.cuda.synchronize(device)
+                    ss0 = int(ss[0])
+                    t0 = time.perf_counter()
+                    out = ops.pop_reusable_slots(meta, ss, blocked, count, order=order)
+                    wall.append(time.perf_counter() - t0)
+                    nbytes.append(_pop_bytes(name, ss0, int(out[-1]), count))
+                for _ in range(calls):
+                    if restore:
+                        meta.copy_(base)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    ops.pop_reusable_slots(meta, ss, blocked, count, order=order, check=False)
+                    e1.record()
+                    dev_ms.append((e0, e1))
+                torch.cuda.synchronize(device)
+                ops.check_status(device)
+                dev = statistics.median(a.elapsed_time(b) for a, b in dev_ms)
+                us = statistics.median(wall) * 1e6
+                alg = statistics.median(nbytes)
+                runs.append({"table": name, "count": count, "blocked": nb, "order": order,
+                             "us_per_call": round(us, 2), "evictions_per_s": round(count / (us / 1e6), 1),
+                             "kernel_us": round(dev * 1e3, 2), "algorithmic_bytes": int(alg),
+                             "kernel_gbs": round(alg / (dev / 1e3) / 1e9, 1),
+                             "hbm_frac": round(alg / (dev / 1e3) / 1e9 / peak, 4)})
+    return {"metric": "per-call pop", "slots": POP_SLOTS, "calls_per_case": calls,
+            "api": "kv_cache_adapter_cuda.pop_reusable_slots (check=True: one status read per call)",
+            "roofline": "no-aging pops scan a few words (latency-bound); aging pops read and write every "
+                        "slot word (HBM-bound; hbm_frac against MEASURED_PEAKS.json hbm_gbs)",
+            "runs": runs}
+
+
+def reference_gpu_pop(device, calls: int = 50) -> dict:
+    """The reference's own CUDA pop (csrc/kv_adapter_cuda.cu:64-237, host
+    :406-450, compiled unchanged into oracle/_ref), per call on the same
+    inputs: unpacked usage (uint8) and reusable mask (pin == 0) as the
+    reference adapter passes them (adapter.py:485-491)."""
+    from oracle import build_ref
+
+    if not build_ref.available():
+        return {"unavailable": "reference CUDA extension not built (python -m oracle.build_ref)"}
+    ref = build_ref.load()
+    tables, blocked_h = pop_inputs()
+    runs = []
+    for name, base_h in tables.items():
+        usage0 = (base_h >> 4).to(torch.uint8).to(device)
+        reusable = ((base_h & 15) == 0).to(device)
+        restore = name == "aging"
+        for count, nb in POP_CASES:
+            blocked = blocked_h[:nb].to(device)
+            usage = usage0.clone()
+            ss = torch.zeros(1, dtype=torch.int64, device=device)
+            for _ in range(3):
+                if restore:
+                    usage.copy_(usage0)
+                ref.pop_reusable_slots(usage, reusable, ss, blocked, count)
+            torch.cuda.synchronize(device)
+            wall, dev_ms = [], []
+            for _ in range(calls):
+                if restore:
+                    usage.copy_(usage0)
+                torch.cuda.synchronize(device)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                t0 = time.perf_counter()
+                e0.record()
+                ref.pop_reusable_slots(usage, reusable, ss, blocked, count)
+                e1.record()
+                torch.cuda.synchronize(device)  # the kernel runs after the op returns
+                wall.append(time.perf_counter() - t0)
+                dev_ms.append(e0.elapsed_time(e1))
+            us = statistics.median(wall) * 1e6
+            runs.append({"table": name, "count": count, "blocked": nb, "order": "prefix (the reference kernel)",
+                         "us_per_call": round(us, 2), "evictions_per_s": round(count / (us / 1e6), 1),
+                         "device_us_per_call": round(statistics.median(dev_ms) * 1e3, 2)})
+    return {"metric": "per-call pop", "slots": POP_SLOTS, "calls_per_case": calls,
+            "api": "reference torch extension pop_reusable_slots (host nonzero sync, then one 1-CTA kernel)",
+            "device_us_per_call": "GPU time from before the op's first kernel to after its pop kernel, "
+                                  "including the gap while the host waits for nonzero",
+            "runs": runs}
+
+
+def cpu_strict_pop(calls: int = 20) -> dict:
+    """The reference's strict-path pop (adapter.py:472-525) as torch CPU ops
+    (oracle/strict_pop.py), per call on the same inputs, grouped order."""
+    from oracle import strict_pop
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    tables, blocked_h = pop_inputs()
+    runs = []
+    for name, base in tables.items():
+        for count, nb in POP_CASES:
+            blocked = blocked_h[:nb]
+            meta = base.clone()
+            ss = torch.zeros(1, dtype=torch.int64)
+            times = []
+            for i in range(calls + 2):
+                if name == "aging":
+                    meta.copy_(base)
+                t0 = time.perf_counter()
+                strict_pop.pop_reusable_slots(meta, ss, blocked, count)
+                if i >= 2:
+                    times.append(time.perf_counter() - t0)
+            us = statistics.median(times) * 1e6
+            runs.append({"table": name, "count": count, "blocked": nb, "order": "grouped",
+                         "us_per_call": round(us, 1), "evictions_per_s": round(count / (us / 1e6), 1)})
+    return {"kind": "port", "cores": torch.get_num_threads(), "slots": POP_SLOTS,
+            "sample": f"{calls} calls per case of the strict path's torch CPU ops (oracle/strict_pop.py)",
+            "runs": runs}
 
 
 def run_ours(args, w: dict, world: int, rank: int, device) -> None:
@@ -357,23 +593,30 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
 
         def scatter(idx):
             ops.scatter_layers(ptab, idx, chunks, blocks_per_chunk=cb, check=False)
-    table = table_h.to(device)
     index = index_h.to(device)
 
     def step():
         gather(index)
         scatter(index)
 
+    # full-size byte check, outside the timed region: a gather through the
+    # bench's table, then a scatter through a second permutation (the cache
+    # becomes a permutation of itself), each compared on every plane
+    table2_h = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 1000))
+    index2 = (slot_mapping_of(table2_h, w["block_size"]) if tokens else table2_h).to(device)
+    gather(index)
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    verified = full_byte_check(chunks, planes, index, tokens)
+    scatter(index2)
+    torch.cuda.synchronize(device)
+    ops.check_status(device)
+    verified += full_byte_check(chunks, planes, index2, tokens)
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(device)
     ops.check_status(device)
-
-    # correctness guard on the bench data: chunk 0 holds the first cb blocks
-    # of the table for plane 0 and the last plane
-    for p in (0, P - 1):
-        assert torch.equal(chunks[0, p].reshape(-1).view(torch.uint8),
-                           planes[p][table[:cb]].reshape(-1).view(torch.uint8))
 
     # ---- device-timed region ------------------------------------------------
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
@@ -394,6 +637,7 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
         torch.cuda.synchronize(device)
     _barrier(world)
     ops.check_status(device)
+    verified += full_byte_check(chunks, planes, index, tokens)  # the timed steps' last gather
     total_ms = _max_over_ranks(start.elapsed_time(end), world, device)
     launch_ms = [g0.elapsed_time(g1) for g0, g1, _ in events] + [g1.elapsed_time(s1) for _, g1, s1 in events]
     avg_launch_ms = _max_over_ranks(sum(launch_ms) / len(launch_ms), world, device)
@@ -424,12 +668,18 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     _barrier(world)
 
     # ---- clock stream (replicated pool per GPU) -------------------------------
-    clock = None if args.no_clock else [gpu_clock(device, 1), gpu_clock(device, 256),
-                                        gpu_clock(device, 1, reps=1, method="steps")]
+    clock = None if args.no_clock else [
+        gpu_clock(device, 1), gpu_clock(device, 256), gpu_clock(device, 1, reps=1, method="steps"),
+        gpu_clock(device, 1, variant="aging"), gpu_clock(device, 256, variant="aging"),
+        gpu_clock(device, 1, reps=1, method="steps", variant="aging")]
     if clock is not None:
         for c in clock:
             c["evictions_per_s"] = _min_over_ranks(c["evictions_per_s"], world, device)  # slowest rank
             c["identical_on_all_ranks"] = _same_on_all_ranks(c["victims_sha256"] + c["slot_meta_sha256"], world)
+    pop = None if args.no_clock else gpu_pop(device)
+    if pop is not None:
+        for r in pop["runs"]:
+            r["us_per_call"] = _max_over_ranks(r["us_per_call"], world, device)  # slowest rank
 
     if rank != 0:
         return
@@ -462,6 +712,10 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
             "l2": "inputs larger than L2 (cache and chunks are each > 126 MB)",
             "parallelism": f"kv-head shard x{world}, no data-path collective",
         },
+        "verified_bytes": verified,
+        "verification": "outside the timed region, every byte of the chunks against torch index_select on the "
+                        "device, plane by plane: after a gather, after a scatter through a second permutation, "
+                        "and after the last timed step",
         "per_gpu_gbs": round(value / world, 2),
         "hbm_frac_per_gpu": round(value / world / peak, 4),
         "roofline": {
@@ -494,28 +748,39 @@ def run_ours(args, w: dict, world: int, rank: int, device) -> None:
     if clock is not None:
         line["clock_eviction"] = {
             "metric": "clock evictions/s",
-            "workload": "1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations, "
-                        "1 Zipf(1.1) re-access per allocation, device-resident stream (1 launch); "
-                        "method batched = runs of steps without aging resolved at once (exact), "
-                        "steps = one step after another",
+            "workload": "200k allocations, 1 Zipf(1.1) re-access per allocation, device-resident stream "
+                        "(1 launch); variants: " + "; ".join(f"{k}: {v['label']}" for k, v in CLOCK_VARIANTS.items())
+                        + "; method batched = runs of steps without aging resolved at once (exact), "
+                          "steps = one step after another",
             "runs": clock,
             "aggregate_evictions_per_s": {str(c["alloc_per_step"]): round(world * c["evictions_per_s"], 1)
-                                          for c in clock if c["method"] == "batched"},
+                                          for c in clock if c["method"] == "batched" and c["variant"] == "stress"},
         }
+    if pop is not None:
+        line["pop"] = pop
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_moves(w, steps=2, warmup=1)
         if clock is not None:
-            line["cpu_baseline_clock"] = [cpu_clock(1), cpu_clock(256)]
+            traces = {(c["variant"], c["alloc_per_step"]): c for c in
+                      (cpu_clock(k, v) for v in CLOCK_VARIANTS for k in (1, 256))}
+            for c in clock:
+                c["roofline"] = clock_roofline(c, traces[(c["variant"], c["alloc_per_step"])], peak)
+            line["cpu_baseline_clock"] = list(traces.values())
+        if pop is not None:
+            line["cpu_baseline_pop"] = cpu_strict_pop()
     print(json.dumps(line), flush=True)
 
 
 def run_clock_stress(args, world: int, rank: int, device) -> None:
     """The clock stress alone: 1,048,576 slots, 200k allocations with one
     Zipf(1.1) re-access each, batches k = 1 and k = 256, one launch each."""
-    runs = [gpu_clock(device, 1, reps=max(args.steps, 1)), gpu_clock(device, 256, reps=max(args.steps, 1))]
+    reps = max(args.steps, 1)
+    runs = [gpu_clock(device, k, reps=reps, variant=v) for v in CLOCK_VARIANTS for k in (1, 256)]
+    runs += [gpu_clock(device, 1, reps=1, method="steps", variant=v) for v in CLOCK_VARIANTS]
     if rank != 0:
         return
     k1 = runs[0]
+    peak, _ = _peaks()
     line = {
         "metric": "clock evictions/s",
         "value": round(world * k1["evictions_per_s"], 1),
@@ -531,18 +796,20 @@ def run_clock_stress(args, world: int, rank: int, device) -> None:
         "data": "synthetic (seeded usage, pins and Zipf re-access stream)",
         "config": {"workload": "clock stress: 1,048,576 slots, usage U{0..3}, 5% pinned, 200k allocations, "
                                "1 Zipf(1.1) re-access per allocation, batch k = 1 (value) and 256, "
-                               "device-resident stream, one cooperative launch per run",
+                               "device-resident stream, one cooperative launch per run; also the aging "
+                               "variant (" + CLOCK_VARIANTS["aging"]["label"] + ")",
                    "timing": "CUDA events around each launch, best of the timed runs"},
         "runs": runs,
-        "roofline": {"bound": "latency", "achieved": k1["evictions_per_s"], "peak": None, "unit": "evictions/s",
-                     "frac": None, "traffic": None,
-                     "note": "a chain of dependent pops: the one-warp pending resolution and grid barriers "
-                             "bound it, not HBM"},
-        "gpu_launches": 2 * (max(args.steps, 1) + 1),
+        "gpu_launches": 4 * (reps + 1) + 2 * 2,
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_clock(1)
-        line["cpu_baseline_k256"] = cpu_clock(256)
+        traces = {(c["variant"], c["alloc_per_step"]): c for c in
+                  (cpu_clock(k, v) for v in CLOCK_VARIANTS for k in (1, 256))}
+        for c in runs:
+            c["roofline"] = clock_roofline(c, traces[(c["variant"], c["alloc_per_step"])], peak)
+        line["roofline"] = runs[0]["roofline"]
+        line["cpu_baseline"] = traces[("stress", 1)]
+        line["cpu_baseline_all"] = list(traces.values())
     print(json.dumps(line), flush=True)
 
 
@@ -961,6 +1228,11 @@ def run_reference(args, w: dict, world: int, rank: int) -> None:
         "cpu_baseline": cpu,
         "e2e": {"value": cpu["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_clock:
+        # the reference's own CUDA pop kernel per call on the GPU, beside its strict CPU path
+        line["pop"] = (reference_gpu_pop(torch.device("cuda", 0)) if torch.cuda.is_available()
+                       else {"unavailable": "no CUDA device"})
+        line["cpu_baseline_pop"] = cpu_strict_pop()
     print(json.dumps(line), flush=True)
 
 

@@ -157,7 +157,16 @@ int kvca_pop_reusable_slots(int meta_bits, int order, void* d_slot_meta, int64_t
  *     before any stream capture.
  *   - All calls on a device share the array: calls that may overlap on the
  *     GPU (different streams without ordering between them) race and must
- *     not be issued.
+ *     not be issued.  Each call clears the words it uses before marking its
+ *     blocked slots, so whatever an earlier call left there has no effect.
+ *   - d_status is required (KVCA_ERR_BAD_ARGUMENT without it when count > 0):
+ *     a blocked id outside [0, num_slots) (KVCA_ERR_BAD_INDEX, value = the
+ *     id) and too few reusable slots (KVCA_ERR_INSUFFICIENT_CAPACITY) are
+ *     found on the device and reported only there; either leaves slot_meta
+ *     and search_start untouched (d_out then holds no defined result).
+ *   - The array's address is looked up once per device and kept for the
+ *     life of the process; after cudaDeviceReset on a device this entry
+ *     point must not be called on that device again.
  *   - Allocates nothing (no cudaMalloc, no cudaFree, no allocating library
  *     routine).
  */

@@ -3803,7 +3803,10 @@ std::mutex g_scratch_mutex;
 uint32_t* g_scratch_address[kMaxDevices] = {};
 
 // Device address of g_pop_scratch_bitmap on the current device, looked up
-// once per device (host code only holds a stand-in for the symbol).
+// once per device (host code only holds a stand-in for the symbol).  The
+// cached address belongs to the context that was current at the lookup; a
+// cudaDeviceReset destroys that context, so a process that resets a device
+// must not call the no-alloc entry point on it again.
 cudaError_t scratch_bitmap_address(uint32_t** address) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -3864,7 +3867,9 @@ extern "C" int kvca_pop_reusable_slots_noalloc(int meta_bits, int order, void* d
   if (num_slots <= 0 || count < 0 || num_blocked < 0) return KVCA_ERR_BAD_ARGUMENT;
   if (num_slots > KVCA_NOALLOC_MAX_SLOTS) return KVCA_ERR_SIZE_LIMIT;
   if (count == 0) return KVCA_OK;
-  if (!d_slot_meta || !d_search_start || !d_out) return KVCA_ERR_BAD_ARGUMENT;
+  // d_status is required: a bad blocked id or too few reusable slots is only
+  // found on the device, and without the status pair it would go unreported.
+  if (!d_slot_meta || !d_search_start || !d_out || !d_status) return KVCA_ERR_BAD_ARGUMENT;
   if (num_blocked > 0 && !d_blocked) return KVCA_ERR_BAD_ARGUMENT;
   uint32_t* bitmap = nullptr;
   if (kvca::scratch_bitmap_address(&bitmap) != cudaSuccess) return KVCA_ERR_CUDA;

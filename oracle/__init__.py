@@ -62,6 +62,7 @@ def _load() -> ctypes.CDLL:
             "oracle_commit_save",
             "oracle_release",
             "oracle_clock_stream",
+            "oracle_clock_stream_traced",
         ):
             getattr(_lib, name).restype = ctypes.c_int
     return _lib
@@ -174,15 +175,20 @@ def release_metadata(l2p, slot_meta, ids):
 
 
 def clock_stream(slot_meta, search_start, num_steps, alloc_per_step, reaccess,
-                 reaccess_per_step, *, order: str = "grouped"):
-    """Returns (victims[num_steps * alloc_per_step], steps_done, status code)."""
+                 reaccess_per_step, *, order: str = "grouped", trace: bool = False):
+    """Returns (victims[num_steps * alloc_per_step], steps_done, status code),
+    plus with ``trace`` each step's usage class T (int8, -1 past steps_done)."""
     assert slot_meta.device.type == "cpu" and slot_meta.is_contiguous()
     assert search_start.device.type == "cpu" and search_start.is_contiguous()
     reaccess = _cpu(reaccess)
     victims = torch.full((int(num_steps) * int(alloc_per_step),), -1, dtype=torch.int64)
+    thresholds = torch.full((int(num_steps),), -1, dtype=torch.int8)
     done = ctypes.c_int64(0)
-    rc = _load().oracle_clock_stream(
+    rc = _load().oracle_clock_stream_traced(
         meta_bits_of(slot_meta), 0 if order == "grouped" else 1, _p(slot_meta),
         _i(slot_meta.numel()), _p(search_start), _i(num_steps), _i(alloc_per_step),
-        _p(reaccess), _i(reaccess_per_step), _p(victims), ctypes.byref(done))
+        _p(reaccess), _i(reaccess_per_step), _p(victims), ctypes.byref(done),
+        _p(thresholds) if trace else ctypes.c_void_p(0))
+    if trace:
+        return victims, int(done.value), rc, thresholds
     return victims, int(done.value), rc

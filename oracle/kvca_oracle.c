@@ -133,9 +133,13 @@ static int is_available(const codec* c, const void* meta, int64_t slot, const in
          bsearch(&slot, blocked_sorted, (size_t)num_blocked, sizeof(int64_t), cmp_i64) == NULL;
 }
 
-int oracle_pop(int meta_bits, int order, void* meta, int64_t num_slots, int64_t* search_start,
-               const int64_t* blocked, int64_t num_blocked, int64_t count, int64_t* out) {
+/* threshold_out (optional): the usage class T of the pop, -1 when nothing
+ * was selected (count 0 or an error). */
+static int pop_impl(int meta_bits, int order, void* meta, int64_t num_slots, int64_t* search_start,
+                    const int64_t* blocked, int64_t num_blocked, int64_t count, int64_t* out,
+                    int64_t* threshold_out) {
   codec c;
+  if (threshold_out) *threshold_out = -1;
   if (make_codec(meta_bits, &c)) return BAD_ARGUMENT;
   if (num_slots <= 0 || count < 0) return BAD_ARGUMENT;
   if (count == 0) return OK; /* adapter.py:473-474 */
@@ -200,7 +204,14 @@ int oracle_pop(int meta_bits, int order, void* meta, int64_t num_slots, int64_t*
     }
   }
   search_start[0] = (out[count - 1] + 1) % num_slots; /* adapter.py:523 */
+  if (threshold_out) *threshold_out = threshold;
   return OK;
+}
+
+int oracle_pop(int meta_bits, int order, void* meta, int64_t num_slots, int64_t* search_start,
+               const int64_t* blocked, int64_t num_blocked, int64_t count, int64_t* out) {
+  return pop_impl(meta_bits, order, meta, num_slots, search_start, blocked, num_blocked, count, out,
+                  NULL);
 }
 
 /* KVCacheAdapter._commit_load_metadata strict branch, adapter.py:595-604 */
@@ -279,10 +290,13 @@ int oracle_release(int meta_bits, const int64_t* l2p, int64_t num_logical, void*
  * (adapter.py:1414-1416 applied through index_put_).  Returns the status of
  * the first failing step; *steps_done counts completed steps.
  */
-int oracle_clock_stream(int meta_bits, int order, void* meta, int64_t num_slots,
-                        int64_t* search_start, int64_t num_steps, int64_t alloc_per_step,
-                        const int64_t* reaccess, int64_t reaccess_per_step, int64_t* victims,
-                        int64_t* steps_done) {
+/* step_threshold (optional, num_steps entries): each completed step's usage
+ * class T (T > 0: that pop aged every slot), for the workload's algorithmic
+ * byte count. */
+int oracle_clock_stream_traced(int meta_bits, int order, void* meta, int64_t num_slots,
+                               int64_t* search_start, int64_t num_steps, int64_t alloc_per_step,
+                               const int64_t* reaccess, int64_t reaccess_per_step,
+                               int64_t* victims, int64_t* steps_done, int8_t* step_threshold) {
   codec c;
   if (make_codec(meta_bits, &c)) return BAD_ARGUMENT;
   uint32_t* next = (uint32_t*)malloc(sizeof(uint32_t) *
@@ -292,8 +306,10 @@ int oracle_clock_stream(int meta_bits, int order, void* meta, int64_t num_slots,
   int64_t step = 0;
   for (; step < num_steps; ++step) {
     int64_t* out = victims + step * alloc_per_step;
-    rc = oracle_pop(meta_bits, order, meta, num_slots, search_start, NULL, 0, alloc_per_step, out);
+    int64_t t = -1;
+    rc = pop_impl(meta_bits, order, meta, num_slots, search_start, NULL, 0, alloc_per_step, out, &t);
     if (rc != OK) break;
+    if (step_threshold) step_threshold[step] = (int8_t)(t > 127 ? 127 : t);
     for (int64_t i = 0; i < alloc_per_step; ++i)
       set_word(&c, meta, out[i], pack(&c, pin_of(&c, get_word(&c, meta, out[i])), 1));
     const int64_t* ids = reaccess + step * reaccess_per_step;
@@ -311,4 +327,13 @@ int oracle_clock_stream(int meta_bits, int order, void* meta, int64_t num_slots,
   free(next);
   *steps_done = step;
   return rc;
+}
+
+int oracle_clock_stream(int meta_bits, int order, void* meta, int64_t num_slots,
+                        int64_t* search_start, int64_t num_steps, int64_t alloc_per_step,
+                        const int64_t* reaccess, int64_t reaccess_per_step, int64_t* victims,
+                        int64_t* steps_done) {
+  return oracle_clock_stream_traced(meta_bits, order, meta, num_slots, search_start, num_steps,
+                                    alloc_per_step, reaccess, reaccess_per_step, victims,
+                                    steps_done, NULL);
 }

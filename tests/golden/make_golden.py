@@ -2,7 +2,9 @@
 
 Usage (in a container where the reference project is mounted):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference project dir>
+
+(or with the directory in the KVCA_REFERENCE_DIR environment variable).
 
 The reference package is copied to a scratch directory under the name
 ``kv_cache_adapter`` and imported from there; nothing of it is copied into
@@ -398,10 +400,13 @@ SCENARIOS_U16 = dict(count=30, seed=4321)
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("KVCA_REFERENCE_DIR"),
+                    help="the reference project's directory (default: $KVCA_REFERENCE_DIR)")
     ap.add_argument("--out", default=str(HERE))
     ap.add_argument("--meta16", action="store_true", help="(child) the 16-bit fixtures")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference project's directory (--reference or KVCA_REFERENCE_DIR)")
     out = pathlib.Path(args.out)
 
     def dump(name: str, obj) -> None:
