@@ -213,27 +213,17 @@ class KVCacheAdapter:
         # eviction-plan part of load / save as one launch with one host sync.
         self._planned = all(callable(getattr(self._native_ext, n, None)) for n in ("plan_load", "plan_save"))
 
-    # -- derived views (adapter.py:185-203) --------------------------------
-
-    @property
-    def _pin_count(self) -> torch.Tensor:
-        return _slot_meta_pin_counts(self._slot_meta)
-
-    @property
-    def _usage_count(self) -> torch.Tensor:
-        return _slot_meta_usage_counts(self._slot_meta)
-
-    @property
-    def _reusable_mask(self) -> torch.Tensor:
-        return self._pin_count == 0
+    # -- views of the packed words (the reference's properties, adapter.py:185-203);
+    # each read builds a new tensor, so writing to one changes nothing
+    _pin_count = property(lambda self: _slot_meta_pin_counts(self._slot_meta))
+    _usage_count = property(lambda self: _slot_meta_usage_counts(self._slot_meta))
+    _reusable_mask = property(lambda self: _slot_meta_pin_counts(self._slot_meta).eq(0))
 
     @property
     def _slot_state(self) -> torch.Tensor:
-        return torch.where(
-            self._physical_to_logical >= 0,
-            torch.full_like(self._physical_to_logical, STATE_RESIDENT),
-            torch.full_like(self._physical_to_logical, STATE_FREE),
-        )
+        """STATE_RESIDENT for slots that hold a logical block, else STATE_FREE."""
+        state = torch.full_like(self._physical_to_logical, STATE_FREE)
+        return state.masked_fill_(self._physical_to_logical.ge(0), STATE_RESIDENT)
 
     # -- public API ---------------------------------------------------------
 
@@ -258,8 +248,8 @@ class KVCacheAdapter:
             return
 
         current_physical, existing_mask, inspected_usage = self._inspect_save_requests(logical_block_ids)
-        existing_positions = _selected_positions(existing_mask)
-        missing_positions = _unselected_positions(existing_mask)
+        existing_positions = _positions(existing_mask)
+        missing_positions = _positions(existing_mask, False)
         existing_physical = current_physical.index_select(0, existing_positions)
         missing_ids = logical_block_ids.index_select(0, missing_positions)
         allocated_physical = self._pop_reusable_slots(missing_ids.shape[0], blocked_slot_ids=existing_physical)
@@ -308,8 +298,8 @@ class KVCacheAdapter:
             return self._load_planned(logical_block_ids)
 
         current_physical, resident_mask, updated_pins, updated_usage = self._inspect_load_requests(logical_block_ids)
-        resident_positions = _selected_positions(resident_mask)
-        miss_positions = _unselected_positions(resident_mask)
+        resident_positions = _positions(resident_mask)
+        miss_positions = _positions(resident_mask, False)
         hit_slot_ids = current_physical.index_select(0, resident_positions)
         miss_logical_ids = logical_block_ids.index_select(0, miss_positions)
         miss_slot_ids = self._pop_reusable_slots(miss_logical_ids.shape[0], blocked_slot_ids=hit_slot_ids)
@@ -355,22 +345,19 @@ class KVCacheAdapter:
         return self.actual_blocks[physical_slot_id]
 
     def debug_snapshot(self) -> dict[str, object]:
-        """adapter.py:342-357."""
-        reusable_slots = self._ordered_reusable_slots()
-        logical_to_physical = self._logical_to_physical.detach().to(device="cpu")
-        slot_state = self._slot_state.detach().to(device="cpu")
-        return {
-            "runtime_path": self.runtime_path,
-            "logical_to_physical": {
-                logical_block_id: int(physical_slot_id)
-                for logical_block_id, physical_slot_id in enumerate(logical_to_physical.tolist())
-                if physical_slot_id >= 0
-            },
-            "lru_unpinned": reusable_slots.detach().to(device="cpu").tolist(),
-            "slot_state": [STATE_NAMES[int(state)] for state in slot_state.tolist()],
-            "pin_count": self._pin_count.detach().cpu().clone(),
-            "actual_blocks": self.actual_blocks.detach().cpu().clone(),
-        }
+        """A host copy of the adapter's state under the keys the reference's
+        snapshot uses (adapter.py:342-357): resident logical id -> slot, the
+        unpinned slots in scan order, each slot's state name, pin counts and
+        the cache rows."""
+        l2p = self._logical_to_physical.detach().cpu()
+        mapped = l2p.ge(0).nonzero().flatten()
+        snap: dict[str, object] = {"runtime_path": self.runtime_path}
+        snap["logical_to_physical"] = dict(zip(mapped.tolist(), l2p[mapped].tolist()))
+        snap["lru_unpinned"] = self._ordered_reusable_slots().detach().cpu().tolist()
+        snap["slot_state"] = list(map(STATE_NAMES.__getitem__, self._slot_state.cpu().tolist()))
+        snap["pin_count"] = self._pin_count.cpu().clone()
+        snap["actual_blocks"] = self.actual_blocks.detach().cpu().clone()
+        return snap
 
     def shutdown(self) -> None:
         backend_shutdown = getattr(self.backend, "shutdown", None)
@@ -499,7 +486,7 @@ class KVCacheAdapter:
             return _EvictionPlan(logical_block_ids[:0], self.actual_blocks[:0])
         previous_logical_ids = self._physical_to_logical.index_select(0, physical_slot_ids)
         eviction_mask = (previous_logical_ids >= 0) & (previous_logical_ids != logical_block_ids)
-        eviction_positions = _selected_positions(eviction_mask)
+        eviction_positions = _positions(eviction_mask)
         eviction_logical_ids = previous_logical_ids.index_select(0, eviction_positions)
         eviction_slot_ids = physical_slot_ids.index_select(0, eviction_positions)
         payloads = self._native_ext.gather_blocks(self.actual_blocks, eviction_slot_ids)
@@ -575,44 +562,12 @@ class InMemoryBlockStoreBackend:
         host_tier: bool = False,
         device: torch.device | str | None = None,
     ) -> None:
-        self._storage: torch.Tensor | None = None
-        self._present_mask: torch.Tensor | None = None
         self._ops = ops
         self._record_device_ops = record_device_ops
         self._host_tier = host_tier
         self._tier_device = torch.device(device) if device is not None else None
-        if isinstance(initial_data, torch.Tensor):
-            if initial_data.ndim < 1:
-                raise ValueError("initial_data tensor must have a leading block dimension")
-            self._storage = initial_data.detach().clone()
-            inferred = int(self._storage.shape[0])
-            if num_logical_blocks is None:
-                num_logical_blocks = inferred
-            elif num_logical_blocks != inferred:
-                raise ValueError("num_logical_blocks must match initial_data.shape[0]")
-            self._present_mask = (
-                present_mask.detach().clone().to(device=self._storage.device)
-                if present_mask is not None
-                else torch.ones((num_logical_blocks,), dtype=torch.bool, device=self._storage.device)
-            )
-        else:
-            if num_logical_blocks is None:
-                if initial_data:
-                    num_logical_blocks = max(initial_data) + 1
-                else:
-                    raise ValueError("num_logical_blocks is required when initial_data is empty")
-            self._present_mask = present_mask.detach().clone() if present_mask is not None else None
-            if initial_data:
-                first = next(iter(initial_data.values()))
-                self._storage = first.new_zeros((num_logical_blocks, *first.shape))
-                if self._present_mask is None:
-                    self._present_mask = torch.zeros((num_logical_blocks,), dtype=torch.bool, device=first.device)
-                else:
-                    self._present_mask = self._present_mask.to(device=first.device)
-                ids = torch.tensor(list(initial_data.keys()), dtype=ID_DTYPE, device=first.device)
-                payloads = torch.stack([initial_data[key] for key in initial_data.keys()], dim=0)
-                self._storage.index_copy_(0, ids, payloads)
-                self._present_mask.index_fill_(0, ids, True)
+        self._storage, self._present_mask, num_logical_blocks = _initial_store(
+            initial_data, num_logical_blocks, present_mask)
 
         if host_tier:
             if self._tier_device is None and self._storage is not None and self._storage.is_cuda:
@@ -629,10 +584,16 @@ class InMemoryBlockStoreBackend:
         self.load_calls: list[int] = []
         self.operation_log: list[tuple[str, int]] = []
         self._device_scratch: torch.Tensor | None = None
-        self.max_concurrent_saves = 0
-        self.max_concurrent_loads = 0
-        self._concurrent_saves = 0
-        self._concurrent_loads = 0
+        self._saving = _InFlight()
+        self._loading = _InFlight()
+
+    @property
+    def max_concurrent_saves(self) -> int:
+        return self._saving.peak
+
+    @property
+    def max_concurrent_loads(self) -> int:
+        return self._loading.peak
 
     def device_store(self, actual_blocks: torch.Tensor):
         """(storage, present mask, scratch) when loads and saves against this
@@ -651,7 +612,7 @@ class InMemoryBlockStoreBackend:
                 return None
         elif st.device != dev:
             return None
-        self._ensure_present_mask(device=dev)
+        self._mask_on(dev)
         scratch = self._device_scratch
         if scratch is None or scratch.device != dev:
             scratch = self._device_scratch = torch.zeros(st.shape[0], dtype=torch.int32, device=dev)
@@ -661,11 +622,11 @@ class InMemoryBlockStoreBackend:
         """Bookkeeping of a save / load that ran on the device (device ids are
         not recorded, as for ``record_device_ops=False``)."""
         if saved:
-            self._enter_save()
-            self._leave_save()
+            with self._saving:
+                pass
         if loaded:
-            self._enter_load()
-            self._leave_load()
+            with self._loading:
+                pass
 
     def _device_ops(self):
         return self._ops if self._ops is not None else _load_cuda_extension_module()
@@ -674,8 +635,7 @@ class InMemoryBlockStoreBackend:
         """adapter.py:735-756."""
         _require_id_tensor(logical_block_ids, name="logical_block_ids")
         _require_block_data_tensor(block_data, expected_blocks=logical_block_ids.shape[0], name="block_data")
-        self._enter_save()
-        try:
+        with self._saving:
             if self._save_delay_s > 0:
                 time.sleep(self._save_delay_s)
             if self._host_tier:
@@ -686,7 +646,7 @@ class InMemoryBlockStoreBackend:
             else:
                 _require_trailing_shape(block_data, self._storage, name="block_data")
                 _require_same_dtype(block_data, reference=self._storage, name="block_data")
-            self._ensure_present_mask(device=self._storage.device)
+            present = self._mask_on(self._storage.device)
             ids = logical_block_ids.to(device=self._storage.device).contiguous()
             data = block_data.to(device=self._storage.device, dtype=self._storage.dtype).contiguous()
             if self._storage.device.type == "cpu" and self._ops is None:
@@ -694,10 +654,8 @@ class InMemoryBlockStoreBackend:
             else:  # a repeated id keeps its last row, as index_copy_ in order does
                 self._device_ops().scatter_blocks(self._storage, _last_occurrences(ids, self.num_logical_blocks),
                                                   data, skip_negative=True)
-            self._present_mask.index_fill_(0, ids, True)
-            self._record_ids("save", logical_block_ids)
-        finally:
-            self._leave_save()
+            present.index_fill_(0, ids, True)
+            self._log("save", logical_block_ids)
 
     def load_blocks(self, logical_block_ids: torch.Tensor, actual_blocks: torch.Tensor,
                     physical_slot_ids: torch.Tensor) -> None:
@@ -706,8 +664,7 @@ class InMemoryBlockStoreBackend:
         _require_id_tensor(physical_slot_ids, name="physical_slot_ids")
         if logical_block_ids.shape[0] != physical_slot_ids.shape[0]:
             raise ValueError("physical_slot_ids leading dimension must match logical_block_ids")
-        self._enter_load()
-        try:
+        with self._loading:
             if self._load_delay_s > 0:
                 time.sleep(self._load_delay_s)
             if self._storage is None:
@@ -715,10 +672,9 @@ class InMemoryBlockStoreBackend:
             if self._host_tier:
                 self._load_host_tier(logical_block_ids, actual_blocks, physical_slot_ids)
                 return
-            self._ensure_present_mask(device=self._storage.device)
+            present = self._mask_on(self._storage.device)
             ids = logical_block_ids.to(device=self._storage.device).contiguous()
-            hit_mask = self._present_mask.index_select(0, ids)
-            if not torch.all(hit_mask).item():
+            if not bool(present.index_select(0, ids).all()):
                 raise BlockNotFoundError("some logical blocks are not in backend")
             _require_trailing_shape(actual_blocks, self._storage, name="actual_blocks")
             slots = physical_slot_ids.to(device=actual_blocks.device).contiguous()
@@ -732,9 +688,7 @@ class InMemoryBlockStoreBackend:
                     actual_blocks.index_copy_(0, slots, payloads)
                 else:
                     self._device_ops().scatter_blocks(actual_blocks, slots, payloads.contiguous())
-            self._record_ids("load", logical_block_ids)
-        finally:
-            self._leave_load()
+            self._log("load", logical_block_ids)
 
     def _gpu_for(self, t: torch.Tensor) -> torch.device:
         if self._tier_device is None:
@@ -752,21 +706,21 @@ class InMemoryBlockStoreBackend:
         else:
             _require_trailing_shape(block_data, self._storage, name="block_data")
             _require_same_dtype(block_data, reference=self._storage, name="block_data")
-        self._ensure_present_mask(device=dev)
+        present = self._mask_on(dev)
         ids = logical_block_ids.to(device=dev).contiguous()
         data = block_data.to(device=dev, dtype=self._storage.dtype).contiguous()
         self._device_ops().scatter_blocks(self._storage, _last_occurrences(ids, self.num_logical_blocks), data,
                                           skip_negative=True)
-        self._present_mask.index_fill_(0, ids, True)
-        self._record_ids("save", logical_block_ids)
+        present.index_fill_(0, ids, True)
+        self._log("save", logical_block_ids)
 
     def _load_host_tier(self, logical_block_ids: torch.Tensor, actual_blocks: torch.Tensor,
                         physical_slot_ids: torch.Tensor) -> None:
         """load_blocks from pinned rows: one copy kernel reading host memory."""
         dev = self._gpu_for(actual_blocks)
-        self._ensure_present_mask(device=dev)
+        present = self._mask_on(dev)
         ids = logical_block_ids.to(device=dev).contiguous()
-        if not torch.all(self._present_mask.index_select(0, ids)).item():
+        if not bool(present.index_select(0, ids).all()):
             raise BlockNotFoundError("some logical blocks are not in backend")
         _require_trailing_shape(actual_blocks, self._storage, name="actual_blocks")
         if actual_blocks.is_cuda and actual_blocks.dtype == self._storage.dtype:
@@ -777,54 +731,93 @@ class InMemoryBlockStoreBackend:
             payloads = self._storage.index_select(0, ids.cpu()).to(device=actual_blocks.device,
                                                                     dtype=actual_blocks.dtype)
             actual_blocks.index_copy_(0, physical_slot_ids.to(device=actual_blocks.device), payloads)
-        self._record_ids("load", logical_block_ids)
+        self._log("load", logical_block_ids)
 
     def snapshot(self) -> dict[int, torch.Tensor]:
-        if self._storage is None:
+        """Each present logical id -> a host copy of its row."""
+        rows = self._storage
+        if rows is None:
             return {}
         if self._host_tier and self._tier_device is not None:
-            torch.cuda.synchronize(self._tier_device)
-        present_ids = torch.nonzero(self._present_mask, as_tuple=False).reshape(-1)
-        present_payloads = self._storage.index_select(0, present_ids.to(device=self._storage.device))
-        return {
-            logical_block_id: payload.detach().clone().cpu()
-            for logical_block_id, payload in zip(present_ids.tolist(), present_payloads.unbind(0))
-        }
-
-    def _enter_save(self) -> None:
-        self._concurrent_saves += 1
-        self.max_concurrent_saves = max(self.max_concurrent_saves, self._concurrent_saves)
-
-    def _leave_save(self) -> None:
-        self._concurrent_saves -= 1
-
-    def _enter_load(self) -> None:
-        self._concurrent_loads += 1
-        self.max_concurrent_loads = max(self.max_concurrent_loads, self._concurrent_loads)
-
-    def _leave_load(self) -> None:
-        self._concurrent_loads -= 1
+            torch.cuda.synchronize(self._tier_device)  # rows the GPU wrote into pinned memory
+        ids = self._present_mask.nonzero().flatten().to(rows.device)
+        copies = rows.index_select(0, ids).detach().cpu()
+        return {i: copies[j].clone() for j, i in enumerate(ids.tolist())}
 
     def shutdown(self) -> None:
         return None
 
-    def _ensure_present_mask(self, *, device: torch.device) -> None:
-        if self._present_mask is None:
-            self._present_mask = torch.zeros((self.num_logical_blocks,), dtype=torch.bool, device=device)
-        elif self._present_mask.device != device:
-            self._present_mask = self._present_mask.to(device=device)
+    def _mask_on(self, device: torch.device) -> torch.Tensor:
+        """The present mask on ``device`` (all absent when there was none)."""
+        mask = self._present_mask
+        if mask is None:
+            mask = torch.zeros((self.num_logical_blocks,), dtype=torch.bool, device=device)
+        elif mask.device != device:
+            mask = mask.to(device=device)
+        self._present_mask = mask
+        return mask
 
-    def _record_ids(self, operation: str, logical_block_ids: torch.Tensor) -> None:
-        """adapter.py:825-833; device ids are recorded only when asked for
-        (``record_device_ops=True``), since reading them synchronises."""
+    def _log(self, operation: str, logical_block_ids: torch.Tensor) -> None:
+        """The reference backend's call log (adapter.py:825-833).  Ids on a
+        device are logged only with ``record_device_ops=True``: reading them
+        synchronises with the device."""
         if logical_block_ids.device.type != "cpu" and not self._record_device_ops:
             return
-        ids = logical_block_ids.detach().tolist()
-        if operation == "save":
-            self.save_calls.extend(ids)
-        else:
-            self.load_calls.extend(ids)
-        self.operation_log.extend((operation, i) for i in ids)
+        ids = logical_block_ids.detach().cpu().tolist()
+        (self.save_calls if operation == "save" else self.load_calls).extend(ids)
+        self.operation_log += [(operation, i) for i in ids]
+
+
+class _InFlight:
+    """Calls of one kind inside a backend right now, and the most seen at once."""
+
+    __slots__ = ("now", "peak")
+
+    def __init__(self) -> None:
+        self.now = 0
+        self.peak = 0
+
+    def __enter__(self) -> "_InFlight":
+        self.now += 1
+        self.peak = max(self.peak, self.now)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.now -= 1
+
+
+def _initial_store(initial, num_logical: int | None, present: torch.Tensor | None):
+    """(rows, present mask, number of logical ids) of a new in-memory store.
+
+    A tensor gives one row per logical id, all present unless ``present``
+    says otherwise.  A dict gives rows for some ids (the others are absent);
+    without ``num_logical`` the largest id sets the size.  No rows yet: the
+    first save allocates them."""
+    mask = None if present is None else present.detach().clone()
+    if isinstance(initial, torch.Tensor):
+        if initial.ndim < 1:
+            raise ValueError("initial_data tensor must have a leading block dimension")
+        rows = initial.detach().clone()
+        if num_logical is not None and num_logical != rows.shape[0]:
+            raise ValueError("num_logical_blocks must match initial_data.shape[0]")
+        if mask is None:
+            mask = torch.ones((rows.shape[0],), dtype=torch.bool, device=rows.device)
+        return rows, mask.to(device=rows.device), int(rows.shape[0])
+    entries = dict(initial) if initial else {}
+    if num_logical is None:
+        if not entries:
+            raise ValueError("num_logical_blocks is required when initial_data is empty")
+        num_logical = max(entries) + 1
+    if not entries:
+        return None, mask, int(num_logical)
+    keys = list(entries)
+    sample = entries[keys[0]]
+    rows = sample.new_zeros((num_logical, *sample.shape))
+    ids = torch.tensor(keys, dtype=ID_DTYPE, device=sample.device)
+    rows.index_copy_(0, ids, torch.stack([entries[k] for k in keys]))
+    mask = (torch.zeros((num_logical,), dtype=torch.bool, device=sample.device) if mask is None
+            else mask.to(device=sample.device))
+    return rows, mask.index_fill_(0, ids, True), int(num_logical)
 
 
 @functools.lru_cache(maxsize=1)
@@ -964,12 +957,11 @@ def _pack_slot_meta(pin_counts: torch.Tensor, usage_counts: torch.Tensor) -> tor
     return packed.to(dtype=SLOT_META_DTYPE)
 
 
-def _selected_positions(mask: torch.Tensor) -> torch.Tensor:
-    return torch.nonzero(mask.to(dtype=torch.int32), as_tuple=False).flatten()
-
-
-def _unselected_positions(mask: torch.Tensor) -> torch.Tensor:
-    return torch.nonzero(mask.to(dtype=torch.int32) == 0, as_tuple=False).flatten()
+def _positions(mask: torch.Tensor, where: bool = True) -> torch.Tensor:
+    """Indices, in order, of the entries of ``mask`` that are true (or, with
+    ``where=False``, false): the split of a request into hits and misses."""
+    picked = mask.bool() if where else mask.logical_not()
+    return picked.nonzero().flatten()
 
 
 def _require_id_tensor(values: torch.Tensor, *, name: str) -> None:
