@@ -425,16 +425,63 @@ def _pop_bytes(table: str, ss_before: int, last: int, count: int) -> int:
     return scanned + 8 * count
 
 
-def gpu_pop(device, calls: int = 200) -> dict:
+def _graph_pop_ms(ops, meta, base, ss, blocked, count: int, order: str, restore: bool, k: int = 50) -> float:
+    """Device time of one pop launch: k pops captured in a CUDA graph and
+    replayed back to back (each after a restore of the table when it ages),
+    less the same graph's restores alone."""
+    device = meta.device
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):  # the op's per-stream scratch exists before the capture
+        ops.pop_reusable_slots(meta, ss, blocked, count, order=order, check=False)
+    torch.cuda.synchronize(device)
+
+    def graph_of(with_pop: bool) -> torch.cuda.CUDAGraph:
+        g = torch.cuda.CUDAGraph()
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+            for _ in range(k):
+                if restore:
+                    meta.copy_(base)
+                if with_pop:
+                    ops.pop_reusable_slots(meta, ss, blocked, count, order=order, check=False)
+        torch.cuda.current_stream(device).wait_stream(s)
+        return g
+
+    def replay_ms(g) -> float:
+        g.replay()
+        torch.cuda.synchronize(device)
+        best = float("inf")
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize(device)
+            best = min(best, e0.elapsed_time(e1))
+        return best
+
+    pops = graph_of(True)
+    ms = replay_ms(pops)
+    if restore:
+        ms -= replay_ms(graph_of(False))
+    ops.check_status(device)
+    return ms / k
+
+
+def gpu_pop(device, calls: int = 200, tables: str | None = None) -> dict:
     """kv_cache_adapter_cuda.pop_reusable_slots per call: wall time of a call
     that returns with the victims ready and the status read (as the reference's
     op synchronises at nonzero), and the device time of its launch."""
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
 
+    chosen = tables
     tables, blocked_h = pop_inputs()
     peak, _ = _peaks()
     runs = []
     for name, base_h in tables.items():
+        if chosen and name != chosen:
+            continue
         base = base_h.to(device)
         restore = name == "aging"
         for count, nb in POP_CASES:
@@ -446,7 +493,7 @@ def gpu_pop(device, calls: int = 200) -> dict:
                     if restore:
                         meta.copy_(base)
                     ops.pop_reusable_slots(meta, ss, blocked, count, order=order)
-                wall, dev_ms, nbytes = [], [], []
+                wall, nbytes = [], []
                 for _ in range(calls):
                     if restore:
                         meta.copy_(base)
@@ -456,17 +503,7 @@ def gpu_pop(device, calls: int = 200) -> dict:
                     out = ops.pop_reusable_slots(meta, ss, blocked, count, order=order)
                     wall.append(time.perf_counter() - t0)
                     nbytes.append(_pop_bytes(name, ss0, int(out[-1]), count))
-                for _ in range(calls):
-                    if restore:
-                        meta.copy_(base)
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    ops.pop_reusable_slots(meta, ss, blocked, count, order=order, check=False)
-                    e1.record()
-                    dev_ms.append((e0, e1))
-                torch.cuda.synchronize(device)
-                ops.check_status(device)
-                dev = statistics.median(a.elapsed_time(b) for a, b in dev_ms)
+                dev = _graph_pop_ms(ops, meta, base, ss, blocked, count, order, restore)
                 us = statistics.median(wall) * 1e6
                 alg = statistics.median(nbytes)
                 runs.append({"table": name, "count": count, "blocked": nb, "order": order,
@@ -476,6 +513,8 @@ def gpu_pop(device, calls: int = 200) -> dict:
                              "hbm_frac": round(alg / (dev / 1e3) / 1e9 / peak, 4)})
     return {"metric": "per-call pop", "slots": POP_SLOTS, "calls_per_case": calls,
             "api": "kv_cache_adapter_cuda.pop_reusable_slots (check=True: one status read per call)",
+            "kernel_us": "device time per pop launch: 50 pops in a CUDA graph replayed back to back (less the "
+                         "table restores of the aging case), no status read",
             "roofline": "no-aging pops scan a few words (latency-bound); aging pops read and write every "
                         "slot word (HBM-bound; hbm_frac against MEASURED_PEAKS.json hbm_gbs)",
             "runs": runs}
@@ -558,6 +597,98 @@ def cpu_strict_pop(calls: int = 20) -> dict:
     return {"kind": "port", "cores": torch.get_num_threads(), "slots": POP_SLOTS,
             "sample": f"{calls} calls per case of the strict path's torch CPU ops (oracle/strict_pop.py)",
             "runs": runs}
+
+
+def run_pop(args, world: int, rank: int, device) -> None:
+    """Per-call pop alone (the default bench line carries the same record)."""
+    pop = gpu_pop(device, calls=max(args.steps, 20), tables=args.pop_table)
+    for r in pop["runs"]:
+        r["us_per_call"] = _max_over_ranks(r["us_per_call"], world, device)
+    if rank != 0:
+        return
+    first = pop["runs"][0]
+    line = {"metric": "per-call pop evictions/s", "value": round(world * first["evictions_per_s"], 1),
+            "unit": "evictions/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (the clock-stress table, seed 1234)",
+            "config": {"workload": f"per-call pop, {POP_SLOTS:,} slots: counts 1 / 256, 0 / 64 blocked ids, "
+                                   "a table that needs no aging and one that ages on every pop"},
+            "pop": pop}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_strict_pop()
+    print(json.dumps(line), flush=True)
+
+
+TOKEN_ROW_WIDTHS = (64, 128, 256, 576, 1152, 2048)
+
+
+def run_token_rows(args, world: int, rank: int, device) -> None:
+    """Random token rows through a slot mapping: per row width, gather half
+    of the token slots of every plane (chosen at random) into 256-token
+    chunks and scatter them back, about --move-mib MiB per move.  Rows of
+    64 B take the small-row mover, 128 B to 1.5 KiB the stream mover, 2 KiB
+    the SIMT mover."""
+    from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
+
+    widths = [args.row_bytes] if args.row_bytes else list(TOKEN_ROW_WIDTHS)
+    peak, _ = _peaks()
+    runs = []
+    for rb in widths:
+        planes_n = 8 if rb in (576, 1152) else 64
+        rows = max(256, (args.move_mib << 20) // (planes_n * rb) // 256 * 256)
+        bs = 16
+        nb = -(-2 * rows // bs)
+        gen = torch.Generator(device=device).manual_seed(1234 + rb)
+        cache = torch.empty((planes_n, nb, bs, rb), dtype=torch.uint8, device=device)
+        cache.random_(0, 256, generator=gen)
+        planes = [cache[p] for p in range(planes_n)]
+        ptab = ops.PlaneTable(planes, 2)
+        mapping = torch.randperm(nb * bs, generator=torch.Generator().manual_seed(rb))[:rows].to(device)
+        chunks = torch.empty((rows // 256, planes_n, 256, rb), dtype=torch.uint8, device=device)
+        ops.gather_tokens(ptab, mapping, chunks, tokens_per_chunk=256, check=True)
+        flat = cache.view(planes_n, nb * bs, rb)
+        for p in range(planes_n):
+            if not torch.equal(chunks[:, p].reshape(rows, rb), flat[p].index_select(0, mapping)):
+                raise RuntimeError(f"token-rows check failed: {rb}-byte rows, plane {p}")
+        for _ in range(args.warmup):
+            ops.gather_tokens(ptab, mapping, chunks, tokens_per_chunk=256, check=False)
+            ops.scatter_tokens(ptab, mapping, chunks, tokens_per_chunk=256, check=False)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        _barrier(world)
+        torch.cuda.synchronize(device)
+        for e0, e1, e2 in ev:
+            e0.record()
+            ops.gather_tokens(ptab, mapping, chunks, tokens_per_chunk=256, check=False)
+            e1.record()
+            ops.scatter_tokens(ptab, mapping, chunks, tokens_per_chunk=256, check=False)
+            e2.record()
+        torch.cuda.synchronize(device)
+        ops.check_status(device)
+        moved = 2 * planes_n * rows * rb
+        g_ms = _max_over_ranks(statistics.median(a.elapsed_time(b) for a, b, _ in ev), world, device)
+        s_ms = _max_over_ranks(statistics.median(b.elapsed_time(c) for _, b, c in ev), world, device)
+        runs.append({"row_bytes": rb, "planes": planes_n, "rows_per_plane": rows, "bytes_per_move": moved,
+                     "gather_gbs": round(moved / (g_ms / 1e3) / 1e9, 1),
+                     "scatter_gbs": round(moved / (s_ms / 1e3) / 1e9, 1),
+                     "gather_frac": round(moved / (g_ms / 1e3) / 1e9 / peak, 4),
+                     "scatter_frac": round(moved / (s_ms / 1e3) / 1e9 / peak, 4),
+                     "gather_ms": round(g_ms, 4), "scatter_ms": round(s_ms, 4)})
+        del cache, chunks, planes, ptab
+        torch.cuda.empty_cache()
+    if rank != 0:
+        return
+    worst = min(min(r["gather_frac"], r["scatter_frac"]) for r in runs)
+    line = {"metric": "random token-row gather / scatter GB/s", "value": runs[0]["gather_gbs"], "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8 (rows moved as bytes)",
+            "data": "synthetic (seeded random bytes, seeded random half of the token slots)",
+            "config": {"workload": "token rows through a random slot mapping, 256-token chunks, row widths "
+                                   + ", ".join(str(r["row_bytes"]) for r in runs) + " B",
+                       "l2": "each move reads and writes about 2 x move_mib MiB, above L2"},
+            "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s", "worst_frac": worst,
+                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"},
+            "runs": runs, "gpu_launches": 2 * args.steps * len(runs)}
+    print(json.dumps(line), flush=True)
 
 
 def run_ours(args, w: dict, world: int, rank: int, device) -> None:
@@ -1242,13 +1373,17 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter", "host-tier", "clock-stress"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode-mix", "adapter", "host-tier", "clock-stress",
+                                                             "pop", "token-rows"],
                     default="llama70b-shard")
     ap.add_argument("--heads", type=int, default=None, help="KV heads per GPU for the decode mix (default 1)")
     ap.add_argument("--pool-blocks", type=int, default=None,
                     help="blocks of the decode mix's pool (default 65,536; smaller only for profiler captures)")
     ap.add_argument("--seqs", type=int, default=None,
                     help="override the number of sequences (smaller cases for profiling)")
+    ap.add_argument("--row-bytes", type=int, default=None, help="token-rows: one row width instead of all")
+    ap.add_argument("--pop-table", choices=["no-aging", "aging"], default=None, help="pop: one table instead of both")
+    ap.add_argument("--move-mib", type=int, default=1024, help="token-rows: MiB per move (smaller for profiling)")
     ap.add_argument("--no-clock", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -1261,6 +1396,12 @@ def main() -> None:
     world, rank, local = _dist()
 
     if args.impl == "reference":
+        if args.workload == "pop":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "metric": "per-call pop evictions/s",
+                                  "pop": reference_gpu_pop(torch.device("cuda", 0)),
+                                  "cpu_baseline": cpu_strict_pop()}), flush=True)
+            return
         run_reference(args, w, world, rank)
         return
 
@@ -1282,6 +1423,10 @@ def main() -> None:
             run_host_tier(args, world, rank, device)
         elif args.workload == "clock-stress":
             run_clock_stress(args, world, rank, device)
+        elif args.workload == "pop":
+            run_pop(args, world, rank, device)
+        elif args.workload == "token-rows":
+            run_token_rows(args, world, rank, device)
         else:
             run_ours(args, w, world, rank, device)
     finally:
