@@ -138,10 +138,7 @@ int kvca_inspect_save_requests(int meta_bits, const int64_t* d_l2p, int64_t num_
                                              d_usage_out, d_status, stream));
 }
 
-size_t kvca_pop_scratch_bytes(int64_t num_slots) {
-  if (num_slots <= 0) return 0;
-  return static_cast<size_t>((num_slots + 31) / 32) * sizeof(uint32_t);
-}
+size_t kvca_pop_scratch_bytes(int64_t num_slots) { return kvca::pop_scratch_bytes(num_slots); }
 
 int kvca_pop_reusable_slots(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,
                             int64_t* d_search_start, const int64_t* d_blocked,

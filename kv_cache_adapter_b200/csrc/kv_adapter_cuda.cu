@@ -605,7 +605,8 @@ __device__ bool bounded_wait_change(const unsigned* word, unsigned from, const i
   return true;
 }
 
-// Grid-wide barrier with a bounded wait.  Every CTA's writes before the
+// Grid-wide barrier with a bounded wait (counter and failure flag given by
+// address; grid_barrier takes the stream's).  Every CTA's writes before the
 // barrier are visible to every CTA after it: the CTA's threads meet at a
 // block barrier, then one thread arrives with a release add on a counter
 // that only grows (barrier j of the launch completes when it reaches
@@ -614,31 +615,35 @@ __device__ bool bounded_wait_change(const unsigned* word, unsigned from, const i
 // atomic.  The counter starts at zero with each launch.  A CTA that waits
 // too long (or sees another CTA give up) marks the grid failed, reports
 // KVCA_ERR_DEVICE_TIMEOUT and returns false; callers then return.
-__device__ bool grid_barrier(StreamGrid* g, int64_t* status) {
+__device__ bool grid_barrier_words(unsigned* bar_count, int* failed, int64_t* status) {
   __shared__ int ok_s;
   __syncthreads();
   if (gridDim.x == 1) return true;
   if (threadIdx.x == 0) {
     const unsigned B = gridDim.x;
     unsigned old;
-    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(&g->bar_count) : "memory");
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(bar_count) : "memory");
     const unsigned target = (old / B + 1u) * B;
     int ok = 1;
     uint32_t spins = 0;
-    while (static_cast<int>(ld_acquire_u32(&g->bar_count) - target) < 0) {
-      if (++spins > kGridSpinLimit || *reinterpret_cast<const volatile int*>(&g->failed) != 0) {
+    while (static_cast<int>(ld_acquire_u32(bar_count) - target) < 0) {
+      if (++spins > kGridSpinLimit || *reinterpret_cast<const volatile int*>(failed) != 0) {
         ok = 0;
         break;
       }
     }
     if (!ok) {
-      atomicExch(&g->failed, 1);
+      atomicExch(failed, 1);
       report(status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
     }
     ok_s = ok;
   }
   __syncthreads();
   return ok_s != 0;
+}
+
+__device__ bool grid_barrier(StreamGrid* g, int64_t* status) {
+  return grid_barrier_words(&g->bar_count, &g->failed, status);
 }
 
 // Sum over the CTAs' counts: (sum of the CTAs before this one, total).
@@ -3436,6 +3441,350 @@ cudaError_t launch_inspect_save(int meta_bits, const int64_t* l2p, int64_t num_l
   return cudaGetLastError();
 }
 
+namespace {
+
+// ---------------------------------------------------------------------------
+// Clock sweep over a large table on the whole GPU
+// ---------------------------------------------------------------------------
+//
+// pop_kernel runs on one CTA, which holds the bandwidth of one SM: fine when
+// the victims are found near the scan start, slow when the pop must rank
+// whole usage classes and age every slot (a 1,048,576-slot table then takes
+// hundreds of microseconds).  pop_grid_kernel splits the scan order (from
+// search_start, wrapping) into one contiguous range per CTA of a cooperative
+// grid:
+//   1. each CTA marks the blocked slots of its range in shared memory (every
+//      CTA reads the whole blocked list), counts its available slots by usage
+//      class and publishes the counts; CTA 0, whose range starts the scan
+//      order, also ranks its usage-0 slots, which are the first victims of
+//      either order;
+//   2. one bounded grid barrier;
+//   3. if CTA 0's range held `count` usage-0 slots, it writes search_start and
+//      every CTA returns; otherwise each CTA derives T, the class bases and
+//      its own offsets from the published counts, writes its victims, ages
+//      its own slots and the CTA holding the last victim writes search_start.
+// The vector that holds the scan start is split between the first range
+// (slots >= start) and the last (slots < start): the first range's owner ages
+// all of it, and the last range's owner classifies its part from a copy
+// taken before the barrier.  Results equal pop_kernel's bit for bit.
+
+constexpr int kGridPopThreads = 512;
+constexpr int kGridPopMaxCtas = 160;
+constexpr int64_t kGridPopMinSlots = 65536;
+constexpr int64_t kGridPopMaxSlots = int64_t{1} << 24;  // blocked bits of a range fit in 16 KiB
+constexpr size_t kGridPopHeader = 256;
+// grid words + per-CTA class counts (sized for 16-bit words: 256 classes)
+constexpr size_t kGridPopAreaBytes = kGridPopHeader + size_t{kGridPopMaxCtas} * 256 * sizeof(int);
+
+struct PopGridWords {
+  unsigned int bar_count;  // grid-barrier arrivals; zeroed before each launch
+  int failed;
+  int done;                // CTA 0 found every victim among its usage-0 slots
+  int unused;
+  long long last_slot;     // the last victim when done
+};
+
+template <typename MetaT>
+struct GridPopShared {
+  int hist[Meta<MetaT>::kUsageMax + 1];
+  long long before[Meta<MetaT>::kUsageMax + 1];  // class members in earlier ranges
+  long long cls_base[Meta<MetaT>::kUsageMax + 1];
+  long long limit[Meta<MetaT>::kUsageMax + 1];
+  long long run[Meta<MetaT>::kUsageMax + 1];
+  int scan[33];
+  long long start;
+  long long need;
+  long long before_le;  // prefix order: slots of usage <= T in earlier ranges
+  long long last0;      // CTA 0: slot of usage-0 rank count - 1
+  long long found0;     // CTA 0: usage-0 slots in its range
+  int threshold;
+  int bad;
+  MetaVec<MetaT> split;  // the split start vector, as read before the barrier
+};
+
+// Vector, segment bounds and word of scan-order piece vv.
+template <typename MetaT>
+__device__ __forceinline__ int64_t piece_vector(int64_t vv, int64_t p0, int64_t n, int64_t v0b,
+                                                int64_t V0, int64_t* lo, int64_t* hi) {
+  if (vv < V0) {
+    *lo = p0;
+    *hi = n;
+    return v0b + vv;
+  }
+  *lo = 0;
+  *hi = p0;
+  return vv - V0;
+}
+
+template <typename MetaT>
+__global__ void __launch_bounds__(kGridPopThreads)
+    pop_grid_kernel(MetaT* meta, int64_t n, int64_t* search_start, const int64_t* blocked,
+                    int64_t num_blocked, int64_t count, int64_t* out, unsigned char* area, int order,
+                    bool aligned, int64_t* status) {
+  using M = Meta<MetaT>;
+  constexpr int kSpv = M::kSlotsPerVec;
+  constexpr int U = M::kUsageMax + 1;
+  extern __shared__ uint32_t blk[];  // blocked bits of this CTA's range, by position in it
+  __shared__ GridPopShared<MetaT> sh;
+  PopGridWords* gw = reinterpret_cast<PopGridWords*>(area);
+  int* ghist = reinterpret_cast<int*>(area + kGridPopHeader);
+  const int64_t G = gridDim.x;
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x;
+
+  if (tid == 0) {
+    long long s = static_cast<long long>(*search_start % n);  // read by every CTA before the barrier
+    if (s < 0) s += n;
+    sh.start = s;
+    sh.bad = 0;
+    sh.found0 = 0;
+    sh.last0 = -1;
+  }
+  __syncthreads();
+  const int64_t p0 = sh.start;
+  const int64_t v0b = p0 / kSpv;
+  const int64_t nvec = (n + kSpv - 1) / kSpv;
+  const int64_t V0 = nvec - v0b;
+  const int64_t V = V0 + (p0 + kSpv - 1) / kSpv;
+  const bool split = (p0 % kSpv) != 0;  // vector v0b is pieces 0 and V - 1
+  const int64_t cb = V * b / G;
+  const int64_t ce = V * (b + 1) / G;
+  const int64_t words = ((ce - cb) * kSpv + 31) / 32;
+
+  // ---- 1. blocked bits of the range, class counts, CTA 0's usage-0 ranks ---
+  for (int64_t i = tid; i < words; i += blockDim.x) blk[i] = 0u;
+  for (int c = tid; c < U; c += blockDim.x) sh.hist[c] = 0;
+  __syncthreads();
+  for (int64_t i = tid; i < num_blocked; i += blockDim.x) {
+    const int64_t x = blocked[i];
+    if (x < 0 || x >= n) {
+      sh.bad = 1;
+      if (b == 0) report(status, KVCA_ERR_BAD_INDEX, x);
+      continue;
+    }
+    const int64_t vv = x >= p0 ? x / kSpv - v0b : V0 + x / kSpv;
+    if (vv >= cb && vv < ce) {
+      const int64_t bit = (vv - cb) * kSpv + x % kSpv;
+      atomicOr(blk + (bit >> 5), 1u << (bit & 31));
+    }
+  }
+  __syncthreads();
+  if (sh.bad) return;  // every CTA saw the same list: none reaches the barrier
+
+  for (int64_t tile = cb; tile < ce; tile += blockDim.x) {
+    const int64_t vv = tile + tid;
+    int64_t v = 0;
+    MetaVec<MetaT> m;
+    unsigned avail = 0u;
+    if (vv < ce) {
+      int64_t lo, hi;
+      v = piece_vector<MetaT>(vv, p0, n, v0b, V0, &lo, &hi);
+      load_meta_vec(meta, n, v, aligned, m);
+      if (split && vv == V - 1) sh.split = m;
+      const int64_t bit0 = (vv - cb) * kSpv;
+#pragma unroll
+      for (int j = 0; j < kSpv; ++j) {
+        const int64_t slot = v * kSpv + j;
+        const int64_t bit = bit0 + j;
+        const bool blocked_here = (blk[bit >> 5] >> (bit & 31)) & 1u;
+        if (slot >= lo && slot < hi && M::pin(m.s[j]) == 0u && !blocked_here) avail |= 1u << j;
+      }
+    }
+    unsigned zero_mask = 0u;
+#pragma unroll
+    for (int j = 0; j < kSpv; ++j) {  // class counts, one shared atomic per class and warp
+      const int key = ((avail >> j) & 1u) ? static_cast<int>(M::usage(m.s[j])) : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      if (key >= 0 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&sh.hist[key], __popc(peers));
+      if (key == 0) zero_mask |= 1u << j;
+    }
+    if (b == 0) {  // uniform per CTA: ranks of usage-0 slots from the scan start
+      int total;
+      const int base = block_excl_scan(__popc(zero_mask), &total, sh.scan);
+      int64_t rank = sh.found0 + base;
+      while (zero_mask != 0u) {
+        const int j = __ffs(zero_mask) - 1;
+        zero_mask &= zero_mask - 1u;
+        if (rank < count) out[rank] = v * kSpv + j;
+        if (rank == count - 1) sh.last0 = v * kSpv + j;
+        ++rank;
+      }
+      __syncthreads();
+      if (tid == 0) sh.found0 += total;
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  for (int c = tid; c < U; c += blockDim.x) __stcg(ghist + b * U + c, sh.hist[c]);
+  if (b == 0 && tid == 0 && sh.found0 >= count) {
+    gw->done = 1;
+    gw->last_slot = sh.last0;
+  }
+  if (!grid_barrier_words(&gw->bar_count, &gw->failed, status)) return;
+
+  // ---- 3a. done by CTA 0 alone --------------------------------------------
+  if (__ldcg(&gw->done) != 0) {
+    if (b == 0 && tid == 0) *search_start = (__ldcg(&gw->last_slot) + 1) % n;
+    return;
+  }
+
+  // ---- 3b. threshold, class bases and this range's offsets ----------------
+  for (int c = tid; c < U; c += blockDim.x) {
+    sh.before[c] = 0;
+    sh.limit[c] = 0;  // the class total for now
+    sh.run[c] = 0;
+  }
+  __syncthreads();
+  for (int64_t i = tid; i < G * U; i += blockDim.x) {  // i = CTA * U + class
+    const int h = __ldcg(ghist + i);
+    if (h != 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&sh.limit[i % U]), static_cast<unsigned long long>(h));
+      if (i / U < b)
+        atomicAdd(reinterpret_cast<unsigned long long*>(&sh.before[i % U]), static_cast<unsigned long long>(h));
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    long long cum = 0, before_le = 0;
+    int t_found = -1;
+    for (int c = 0; c < U; ++c) {
+      sh.cls_base[c] = cum;
+      before_le += sh.before[c];
+      cum += sh.limit[c];
+      if (cum >= count) {
+        t_found = c;
+        break;
+      }
+    }
+    sh.threshold = t_found;
+    if (t_found >= 0) {
+      sh.need = count - sh.cls_base[t_found];
+      sh.limit[t_found] = sh.need;
+      sh.before_le = before_le;
+    }
+  }
+  __syncthreads();
+  const int threshold = sh.threshold;
+  if (threshold < 0) {
+    if (b == 0 && tid == 0) report(status, KVCA_ERR_INSUFFICIENT_CAPACITY, count);
+    return;
+  }
+
+  // ---- 3c. victims and aging of this range --------------------------------
+  int64_t run_prefix = 0;
+  for (int64_t tile = cb; tile < ce; tile += blockDim.x) {
+    const int64_t vv = tile + tid;
+    const bool active = vv < ce;
+    MetaVec<MetaT> m;
+    unsigned avail = 0u;
+    int64_t v = 0;
+    if (active) {
+      int64_t lo, hi;
+      v = piece_vector<MetaT>(vv, p0, n, v0b, V0, &lo, &hi);
+      const bool last_piece = split && vv == V - 1;
+      if (last_piece) m = sh.split;
+      else load_meta_vec(meta, n, v, aligned, m);
+      const int64_t bit0 = (vv - cb) * kSpv;
+      MetaVec<MetaT> aged;
+#pragma unroll
+      for (int j = 0; j < kSpv; ++j) {
+        const int64_t slot = v * kSpv + j;
+        const unsigned w = m.s[j];
+        const int64_t bit = bit0 + j;
+        const bool blocked_here = (blk[bit >> 5] >> (bit & 31)) & 1u;
+        if (slot >= lo && slot < hi && M::pin(w) == 0u && !blocked_here) avail |= 1u << j;
+        const unsigned u = M::usage(w);
+        aged.s[j] = M::pack(M::pin(w), u > static_cast<unsigned>(threshold) ? u - threshold : 0u);
+      }
+      // the first piece's owner ages the whole start vector; the last piece never writes
+      if (threshold > 0 && !last_piece) store_meta_vec(meta, n, v, aligned, aged);
+    }
+    if (order == KVCA_POP_ORDER_GROUPED) {
+      for (int c = 0; c <= threshold; ++c) {
+        if (sh.hist[c] == 0) continue;  // uniform: this range has no member of class c
+        unsigned mask = 0u;
+        if (active) {
+#pragma unroll
+          for (int j = 0; j < kSpv; ++j)
+            if (((avail >> j) & 1u) && M::usage(m.s[j]) == static_cast<unsigned>(c)) mask |= 1u << j;
+        }
+        int total;
+        const int base = block_excl_scan(__popc(mask), &total, sh.scan);
+        int64_t rank = sh.before[c] + sh.run[c] + base;
+        while (mask != 0u) {
+          const int j = __ffs(mask) - 1;
+          mask &= mask - 1u;
+          if (rank < sh.limit[c]) {
+            out[sh.cls_base[c] + rank] = v * kSpv + j;
+            if (c == threshold && rank == sh.need - 1) *search_start = (v * kSpv + j + 1) % n;
+          }
+          ++rank;
+        }
+        __syncthreads();
+        if (tid == 0) sh.run[c] += total;
+        __syncthreads();
+      }
+    } else {
+      unsigned mask = 0u;
+      if (active) {
+#pragma unroll
+        for (int j = 0; j < kSpv; ++j)
+          if (((avail >> j) & 1u) && M::usage(m.s[j]) <= static_cast<unsigned>(threshold)) mask |= 1u << j;
+      }
+      int total;
+      const int base = block_excl_scan(__popc(mask), &total, sh.scan);
+      int64_t rank = sh.before_le + run_prefix + base;
+      while (mask != 0u) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        if (rank < count) {
+          out[rank] = v * kSpv + j;
+          if (rank == count - 1) *search_start = (v * kSpv + j + 1) % n;
+        }
+        ++rank;
+      }
+      run_prefix += total;
+    }
+  }
+}
+
+size_t grid_pop_area_offset(int64_t num_slots) {
+  const size_t bitmap = static_cast<size_t>((num_slots + 31) / 32) * sizeof(uint32_t);
+  return (bitmap + 255) / 256 * 256;
+}
+
+template <typename MetaT>
+cudaError_t launch_pop_grid(MetaT* meta, int64_t n, int64_t* search_start, const int64_t* blocked,
+                            int64_t num_blocked, int64_t count, int64_t* out, unsigned char* area,
+                            int order, bool aligned, int64_t* status, cudaStream_t stream) {
+  constexpr int kSpv = Meta<MetaT>::kSlotsPerVec;
+  const int64_t V = (n + kSpv - 1) / kSpv + 1;
+  int sms = device_sm_count();
+  if (sms < 1) sms = 1;
+  int64_t grid = V / 64;
+  if (grid > sms) grid = sms;
+  if (grid > kGridPopMaxCtas) grid = kGridPopMaxCtas;
+  if (grid < 1) grid = 1;
+  const int64_t per = (V + grid - 1) / grid;
+  const size_t smem = static_cast<size_t>((per * kSpv + 31) / 32) * sizeof(uint32_t);
+  cudaError_t e = cudaMemsetAsync(area, 0, sizeof(PopGridWords), stream);
+  if (e != cudaSuccess) return e;
+  void* args[] = {&meta, &n, &search_start, &blocked, &num_blocked, &count, &out, &area, &order,
+                  &aligned, &status};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(pop_grid_kernel<MetaT>),
+                                     dim3(static_cast<unsigned>(grid)), dim3(kGridPopThreads), args, smem,
+                                     stream);
+}
+
+}  // namespace
+
+size_t pop_scratch_bytes(int64_t num_slots) {
+  if (num_slots <= 0) return 0;
+  const size_t bitmap = static_cast<size_t>((num_slots + 31) / 32) * sizeof(uint32_t);
+  if (num_slots < kGridPopMinSlots || num_slots > kGridPopMaxSlots) return bitmap;
+  return grid_pop_area_offset(num_slots) + kGridPopAreaBytes;
+}
+
 int pop_threads_for(int meta_bits, int64_t num_slots) {
   const int64_t spv = meta_bits == 16 ? 8 : 16;
   const int64_t vecs = (num_slots + spv - 1) / spv;
@@ -3449,8 +3798,16 @@ cudaError_t launch_pop(int meta_bits, int order, void* meta, int64_t num_slots,
                        int64_t* search_start, const int64_t* blocked, int64_t num_blocked,
                        int64_t count, int64_t* out, uint32_t* bitmap, int64_t* status,
                        cudaStream_t stream) {
-  const int threads = pop_threads_for(meta_bits, num_slots);
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
+  if (num_slots >= kGridPopMinSlots && num_slots <= kGridPopMaxSlots) {  // the whole GPU
+    unsigned char* area = reinterpret_cast<unsigned char*>(bitmap) + grid_pop_area_offset(num_slots);
+    cudaError_t e = cudaSuccess;
+    KVCA_META_DISPATCH(meta_bits, e = launch_pop_grid<MetaT>(static_cast<MetaT*>(meta), num_slots, search_start,
+                                                             blocked, num_blocked, count, out, area, order,
+                                                             aligned, status, stream));
+    return e;
+  }
+  const int threads = pop_threads_for(meta_bits, num_slots);
   KVCA_META_DISPATCH(meta_bits, pop_kernel<MetaT><<<1, threads, 0, stream>>>(
                                     static_cast<MetaT*>(meta), num_slots, search_start, blocked,
                                     num_blocked, count, out, bitmap, order, aligned, status));

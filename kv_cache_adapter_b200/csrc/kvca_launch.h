@@ -83,6 +83,10 @@ cudaError_t launch_inspect_save(int meta_bits, const int64_t* l2p, int64_t num_l
 
 int pop_threads_for(int meta_bits, int64_t num_slots);
 
+// Bytes of scratch kvca_pop_reusable_slots takes: the blocked-slot bitmap,
+// then (tables that the whole-GPU pop handles) its grid words and counts.
+size_t pop_scratch_bytes(int64_t num_slots);
+
 cudaError_t launch_pop(int meta_bits, int order, void* meta, int64_t num_slots,
                        int64_t* search_start, const int64_t* blocked, int64_t num_blocked,
                        int64_t count, int64_t* out, uint32_t* bitmap, int64_t* status,

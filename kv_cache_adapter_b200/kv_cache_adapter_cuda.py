@@ -248,11 +248,16 @@ def inspect_save_requests(logical_to_physical: torch.Tensor, slot_meta: torch.Te
 
 
 def _bitmap(dev: torch.device, num_slots: int) -> torch.Tensor:
+    """The pop scratch of this (device, stream, table size), kept for reuse:
+    kvca_pop_scratch_bytes(num_slots) bytes, returned as a view of its first
+    part, the blocked-slot bitmap (zero between calls); the rest is the
+    whole-GPU pop's working area of large tables."""
     words = (num_slots + 31) // 32
     key = (_index(dev), _stream(dev).value or 0, words)
     bm = _pop_bitmaps.get(key)
     if bm is None:
-        bm = torch.zeros(words, dtype=torch.int32, device=dev)
+        total = max(words, int(_lib_handle.kvca_pop_scratch_bytes(num_slots)) // 4)
+        bm = torch.zeros(total, dtype=torch.int32, device=dev)[:words]
         _pop_bitmaps[key] = bm
     return bm
 

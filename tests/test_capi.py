@@ -39,7 +39,10 @@ def test_abi_version_and_scratch_sizes():
     assert lib.kvca_pop_scratch_bytes(1) == 4
     assert lib.kvca_pop_scratch_bytes(32) == 4
     assert lib.kvca_pop_scratch_bytes(33) == 8
-    assert lib.kvca_pop_scratch_bytes(1 << 20) == (1 << 20) // 8
+    # tables of 65,536 to 2^24 slots add the whole-GPU pop's area after the bitmap
+    assert lib.kvca_pop_scratch_bytes(65535) == 65536 // 8
+    assert lib.kvca_pop_scratch_bytes(1 << 20) == (1 << 20) // 8 + 256 + 160 * 256 * 4
+    assert lib.kvca_pop_scratch_bytes((1 << 24) + 1) == ((1 << 24) + 32) // 8
     assert lib.kvca_choose_pop_launch_warps(1) == 1
     assert lib.kvca_choose_pop_launch_warps(1 << 20) == 32
 
