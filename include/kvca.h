@@ -128,10 +128,13 @@ int kvca_inspect_save_requests(int meta_bits, const int64_t* d_l2p, int64_t num_
  * Too few available slots: d_status gets KVCA_ERR_INSUFFICIENT_CAPACITY and
  * neither slot_meta nor search_start changes.
  *
- * d_scratch_bitmap: ceil(num_slots / 32) uint32 words, all zero on entry;
- * the call marks the blocked slots in it and clears them again before it
- * returns, so it is zero on exit.  kvca_pop_scratch_bytes gives its size.
- * Calls sharing one bitmap must be ordered on one stream.
+ * d_scratch_bitmap: kvca_pop_scratch_bytes(num_slots) bytes, all zero on
+ * entry and zero again on exit: ceil(num_slots / 32) uint32 words of
+ * blocked-slot bitmap and, for tables of 65,536 to 2^24 slots, the working
+ * area of the whole-GPU sweep (those tables run on a cooperative grid of one
+ * CTA per SM: each CTA takes a contiguous range of the scan order, and one
+ * bounded grid barrier joins them unless the first range already holds the
+ * victims).  Calls sharing one scratch must be ordered on one stream.
  */
 size_t kvca_pop_scratch_bytes(int64_t num_slots);
 int kvca_pop_reusable_slots(int meta_bits, int order, void* d_slot_meta, int64_t num_slots,

@@ -2497,13 +2497,30 @@ __device__ __forceinline__ void move_short_rows_pm_body(const MoveParams& p, int
   const bool lead = lane == 0;
   const int row_vecs = static_cast<int>(p.row_vecs);
 
+  // Slot indices are loaded one iteration ahead, before the current rows'
+  // loads, so that an iteration waits for its row loads only (the index and
+  // the rows it names no longer form one chain).
+  int64_t sidx[kRows];
+  int64_t didx[kRows];
+  {
+    int64_t rr = r;
+#pragma unroll
+    for (int u = 0; u < kRows; ++u) {
+      sidx[u] = 0;
+      didx[u] = 0;
+      if (begin + u < end) {
+        if (kSrcPaged) sidx[u] = p.src_paged.index != nullptr ? p.src_paged.index[rr] : rr;
+        if (kDstPaged) didx[u] = p.dst_paged.index != nullptr ? p.dst_paged.index[rr] : rr;
+      }
+      if (++rr == rows) rr = 0;
+    }
+  }
+
   for (int64_t g = begin; g < end; g += kRows) {
-    int64_t row[kRows];
     int64_t plane[kRows];
     int64_t coff[kRows];
 #pragma unroll
     for (int u = 0; u < kRows; ++u) {
-      row[u] = r;
       plane[u] = pl;
       coff[u] = kChunk ? c * cs.chunk_stride + cr * cs.row_stride + pl * cs.plane_stride : 0;
       if (++r == rows) {
@@ -2515,16 +2532,6 @@ __device__ __forceinline__ void move_short_rows_pm_body(const MoveParams& p, int
         cr = 0;
         ++c;
       }
-    }
-    int64_t sidx[kRows];
-    int64_t didx[kRows];
-#pragma unroll
-    for (int u = 0; u < kRows; ++u) {
-      const bool live = g + u < end;
-      sidx[u] = 0;
-      didx[u] = 0;
-      if (kSrcPaged && live) sidx[u] = p.src_paged.index != nullptr ? p.src_paged.index[row[u]] : row[u];
-      if (kDstPaged && live) didx[u] = p.dst_paged.index != nullptr ? p.dst_paged.index[row[u]] : row[u];
     }
     const uint4* src[kRows];
     uint4* dst[kRows];
@@ -2543,6 +2550,17 @@ __device__ __forceinline__ void move_short_rows_pm_body(const MoveParams& p, int
           dst[u] = reinterpret_cast<uint4*>(kDstPaged ? p.dst_paged.planes[plane[u]] + dso
                                                       : p.dst_chunk.base + dso);
         }
+      }
+    }
+    {  // the next iteration's indices: rows r, r + 1, ... of the position reached
+      int64_t rr = r;
+#pragma unroll
+      for (int u = 0; u < kRows; ++u) {
+        if (g + kRows + u < end) {
+          if (kSrcPaged) sidx[u] = p.src_paged.index != nullptr ? p.src_paged.index[rr] : rr;
+          if (kDstPaged) didx[u] = p.dst_paged.index != nullptr ? p.dst_paged.index[rr] : rr;
+        }
+        if (++rr == rows) rr = 0;
       }
     }
     uint4 buf[kRows][kVpl];
@@ -2629,6 +2647,16 @@ __device__ __forceinline__ void move_rows_stream_body(const MoveParams& p, int64
   const int q32 = 32 / rv;
   const int m32 = 32 - q32 * rv;
 
+  // The batch's slot indices are loaded one batch ahead, before the previous
+  // batch's row loads, so that a batch waits for its row loads only, not for
+  // an index load and then its row loads (random 128-byte rows: the index
+  // latency took half of each batch).
+  int64_t cur_s = 0;
+  int64_t cur_d = 0;
+  if (lane < (end - begin < rpb ? end - begin : rpb)) {
+    if (kSrcPaged) cur_s = p.src_paged.index != nullptr ? p.src_paged.index[r] : r;
+    if (kDstPaged) cur_d = p.dst_paged.index != nullptr ? p.dst_paged.index[r] : r;
+  }
   for (int64_t g = begin; g < end; g += rpb) {
     const int nrows = end - g < rpb ? static_cast<int>(end - g) : rpb;
     uint64_t my_src = 0;
@@ -2637,14 +2665,8 @@ __device__ __forceinline__ void move_rows_stream_body(const MoveParams& p, int64
       const int64_t coff = kChunk ? c * cs.chunk_stride + cr * cs.row_stride + pl * cs.plane_stride : 0;
       int64_t so = coff;
       int64_t dso = coff;
-      if (kSrcPaged) {
-        const int64_t idx = p.src_paged.index != nullptr ? p.src_paged.index[r] : r;
-        so = paged_slot_offset(p.src_paged, idx, s_shift, p.flags, p.status, true);
-      }
-      if (kDstPaged) {
-        const int64_t idx = p.dst_paged.index != nullptr ? p.dst_paged.index[r] : r;
-        dso = paged_slot_offset(p.dst_paged, idx, d_shift, p.flags, p.status, true);
-      }
+      if (kSrcPaged) so = paged_slot_offset(p.src_paged, cur_s, s_shift, p.flags, p.status, true);
+      if (kDstPaged) dso = paged_slot_offset(p.dst_paged, cur_d, d_shift, p.flags, p.status, true);
       if (so >= 0 && dso >= 0) {
         my_src = kSrcPaged ? p.src_paged.planes[pl] + so : p.src_chunk.base + so;
         my_dst = kDstPaged ? p.dst_paged.planes[pl] + dso : p.dst_chunk.base + dso;
@@ -2664,6 +2686,13 @@ __device__ __forceinline__ void move_rows_stream_body(const MoveParams& p, int64
       } while (r >= rows32);
       c = r / rpc;
       cr = r - c * rpc;
+    }
+    {  // the next batch's indices (its lane's row is now r of plane pl)
+      const int64_t gn = g + rpb;
+      if (gn < end && lane < (end - gn < rpb ? end - gn : rpb)) {
+        if (kSrcPaged) cur_s = p.src_paged.index != nullptr ? p.src_paged.index[r] : r;
+        if (kDstPaged) cur_d = p.dst_paged.index != nullptr ? p.dst_paged.index[r] : r;
+      }
     }
 
     // my_src and my_dst are both set or both zero (a skipped row).
@@ -3452,23 +3481,24 @@ namespace {
 // whole usage classes and age every slot (a 1,048,576-slot table then takes
 // hundreds of microseconds).  pop_grid_kernel splits the scan order (from
 // search_start, wrapping) into one contiguous range per CTA of a cooperative
-// grid:
-//   1. each CTA marks the blocked slots of its range in shared memory (every
-//      CTA reads the whole blocked list), counts its available slots by usage
-//      class and publishes the counts; CTA 0, whose range starts the scan
-//      order, also ranks its usage-0 slots, which are the first victims of
-//      either order;
-//   2. one bounded grid barrier;
-//   3. if CTA 0's range held `count` usage-0 slots, it writes search_start and
-//      every CTA returns; otherwise each CTA derives T, the class bases and
-//      its own offsets from the published counts, writes its victims, ages
-//      its own slots and the CTA holding the last victim writes search_start.
-// The vector that holds the scan start is split between the first range
-// (slots >= start) and the last (slots < start): the first range's owner ages
-// all of it, and the last range's owner classifies its part from a copy
-// taken before the barrier.  Results equal pop_kernel's bit for bit.
+// grid.  Every CTA marks the blocked slots of its range in shared memory
+// (each reads the whole blocked list) and counts its available slots by usage
+// class.  CTA 0, whose range starts the scan order, also ranks its usage-0
+// slots, the first victims of either order: if they are enough it writes
+// them and search_start and tells the grid to stop (no grid barrier at all).
+// Otherwise every CTA publishes its counts, meets the others at one bounded
+// grid barrier, derives T, the class bases and its own offsets, writes its
+// victims and ages its own slots; the CTA holding the last victim writes
+// search_start.  search_start is written only when no CTA will read it
+// again.  The vector that holds the scan start is split between the first
+// range (slots >= start) and the last (slots < start): the first range's
+// owner ages all of it, and the last range's owner classifies its part from
+// a copy taken before the barrier.  The grid words are zero on entry and the
+// last CTA to leave zeroes them again.  Results equal pop_kernel's bit for
+// bit.
 
 constexpr int kGridPopThreads = 512;
+constexpr int kGridPopWarps = kGridPopThreads / 32;
 constexpr int kGridPopMaxCtas = 160;
 constexpr int64_t kGridPopMinSlots = 65536;
 constexpr int64_t kGridPopMaxSlots = int64_t{1} << 24;  // blocked bits of a range fit in 16 KiB
@@ -3476,12 +3506,15 @@ constexpr size_t kGridPopHeader = 256;
 // grid words + per-CTA class counts (sized for 16-bit words: 256 classes)
 constexpr size_t kGridPopAreaBytes = kGridPopHeader + size_t{kGridPopMaxCtas} * 256 * sizeof(int);
 
+constexpr int kGridUndecided = 0;
+constexpr int kGridDone = 1;  // CTA 0 wrote every victim: the others leave
+constexpr int kGridGo = 2;    // the counts of every range decide
+
 struct PopGridWords {
-  unsigned int bar_count;  // grid-barrier arrivals; zeroed before each launch
-  int failed;
-  int done;                // CTA 0 found every victim among its usage-0 slots
-  int unused;
-  long long last_slot;     // the last victim when done
+  unsigned int bar_count;  // grid-barrier arrivals
+  int failed;              // a barrier wait gave up
+  int state;               // kGridUndecided, kGridDone or kGridGo (CTA 0's verdict)
+  unsigned int exits;      // CTAs that have left
 };
 
 template <typename MetaT>
@@ -3499,11 +3532,11 @@ struct GridPopShared {
   long long found0;     // CTA 0: usage-0 slots in its range
   int threshold;
   int bad;
+  int state;
   MetaVec<MetaT> split;  // the split start vector, as read before the barrier
 };
 
-// Vector, segment bounds and word of scan-order piece vv.
-template <typename MetaT>
+// Vector and segment bounds of scan-order piece vv.
 __device__ __forceinline__ int64_t piece_vector(int64_t vv, int64_t p0, int64_t n, int64_t v0b,
                                                 int64_t V0, int64_t* lo, int64_t* hi) {
   if (vv < V0) {
@@ -3514,6 +3547,63 @@ __device__ __forceinline__ int64_t piece_vector(int64_t vv, int64_t p0, int64_t 
   *lo = 0;
   *hi = p0;
   return vv - V0;
+}
+
+// Adds this thread's available slots of one vector to the CTA's class counts.
+// 8-bit words: the 16 class counts of a warp travel as 16-bit fields of four
+// words through one warp sum each; 16-bit words (256 classes): one shared
+// atomic per class and group of equal lanes.
+template <typename MetaT>
+__device__ __forceinline__ void count_classes(const MetaVec<MetaT>& m, unsigned avail, int* hist) {
+  using M = Meta<MetaT>;
+  constexpr int kSpv = M::kSlotsPerVec;
+  if constexpr (sizeof(MetaT) == 1) {
+    unsigned long long f0 = 0ull, f1 = 0ull, f2 = 0ull, f3 = 0ull;  // classes 4q .. 4q + 3
+#pragma unroll
+    for (int j = 0; j < kSpv; ++j) {
+      const unsigned u = M::usage(m.s[j]);
+      const unsigned long long one = ((avail >> j) & 1ull) << (16u * (u & 3u));
+      f0 += (u >> 2) == 0u ? one : 0ull;
+      f1 += (u >> 2) == 1u ? one : 0ull;
+      f2 += (u >> 2) == 2u ? one : 0ull;
+      f3 += (u >> 2) == 3u ? one : 0ull;
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      f0 += __shfl_xor_sync(0xffffffffu, f0, d);
+      f1 += __shfl_xor_sync(0xffffffffu, f1, d);
+      f2 += __shfl_xor_sync(0xffffffffu, f2, d);
+      f3 += __shfl_xor_sync(0xffffffffu, f3, d);
+    }
+    const int c = threadIdx.x & 31;
+    if (c < 16) {
+      const unsigned long long word = c < 4 ? f0 : c < 8 ? f1 : c < 12 ? f2 : f3;
+      const int v = static_cast<int>((word >> (16u * (c & 3))) & 0xffffull);
+      if (v) atomicAdd(hist + c, v);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kSpv; ++j) {
+      const int key = ((avail >> j) & 1u) ? static_cast<int>(M::usage(m.s[j])) : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      if (key >= 0 && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(hist + key, __popc(peers));
+    }
+  }
+}
+
+// The last CTA to leave zeroes the grid words for the next launch.
+__device__ __forceinline__ void grid_pop_leave(PopGridWords* gw) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&gw->exits, 1u) == gridDim.x - 1u) {
+      gw->bar_count = 0u;
+      gw->failed = 0;
+      gw->state = kGridUndecided;
+      __threadfence();
+      gw->exits = 0u;
+    }
+  }
 }
 
 template <typename MetaT>
@@ -3531,9 +3621,13 @@ __global__ void __launch_bounds__(kGridPopThreads)
   const int64_t G = gridDim.x;
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
 
+  // search_start is rewritten only by CTA 0 when it alone finishes (the others
+  // then leave without using what they read) or after the barrier
   if (tid == 0) {
-    long long s = static_cast<long long>(*search_start % n);  // read by every CTA before the barrier
+    long long s = static_cast<long long>(__ldcg(search_start) % n);
     if (s < 0) s += n;
     sh.start = s;
     sh.bad = 0;
@@ -3569,16 +3663,20 @@ __global__ void __launch_bounds__(kGridPopThreads)
     }
   }
   __syncthreads();
-  if (sh.bad) return;  // every CTA saw the same list: none reaches the barrier
+  if (sh.bad) {  // every CTA saw the same list: none goes further
+    grid_pop_leave(gw);
+    return;
+  }
 
   for (int64_t tile = cb; tile < ce; tile += blockDim.x) {
     const int64_t vv = tile + tid;
     int64_t v = 0;
     MetaVec<MetaT> m;
+    m.raw = make_uint4(0u, 0u, 0u, 0u);
     unsigned avail = 0u;
     if (vv < ce) {
       int64_t lo, hi;
-      v = piece_vector<MetaT>(vv, p0, n, v0b, V0, &lo, &hi);
+      v = piece_vector(vv, p0, n, v0b, V0, &lo, &hi);
       load_meta_vec(meta, n, v, aligned, m);
       if (split && vv == V - 1) sh.split = m;
       const int64_t bit0 = (vv - cb) * kSpv;
@@ -3590,15 +3688,12 @@ __global__ void __launch_bounds__(kGridPopThreads)
         if (slot >= lo && slot < hi && M::pin(m.s[j]) == 0u && !blocked_here) avail |= 1u << j;
       }
     }
-    unsigned zero_mask = 0u;
-#pragma unroll
-    for (int j = 0; j < kSpv; ++j) {  // class counts, one shared atomic per class and warp
-      const int key = ((avail >> j) & 1u) ? static_cast<int>(M::usage(m.s[j])) : -1;
-      const unsigned peers = __match_any_sync(0xffffffffu, key);
-      if (key >= 0 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&sh.hist[key], __popc(peers));
-      if (key == 0) zero_mask |= 1u << j;
-    }
+    count_classes<MetaT>(m, avail, sh.hist);
     if (b == 0) {  // uniform per CTA: ranks of usage-0 slots from the scan start
+      unsigned zero_mask = 0u;
+#pragma unroll
+      for (int j = 0; j < kSpv; ++j)
+        if (((avail >> j) & 1u) && M::usage(m.s[j]) == 0u) zero_mask |= 1u << j;
       int total;
       const int base = block_excl_scan(__popc(zero_mask), &total, sh.scan);
       int64_t rank = sh.found0 + base;
@@ -3615,32 +3710,61 @@ __global__ void __launch_bounds__(kGridPopThreads)
     }
   }
   __syncthreads();
-  for (int c = tid; c < U; c += blockDim.x) __stcg(ghist + b * U + c, sh.hist[c]);
-  if (b == 0 && tid == 0 && sh.found0 >= count) {
-    gw->done = 1;
-    gw->last_slot = sh.last0;
-  }
-  if (!grid_barrier_words(&gw->bar_count, &gw->failed, status)) return;
 
-  // ---- 3a. done by CTA 0 alone --------------------------------------------
-  if (__ldcg(&gw->done) != 0) {
-    if (b == 0 && tid == 0) *search_start = (__ldcg(&gw->last_slot) + 1) % n;
+  // ---- 2. CTA 0's verdict -------------------------------------------------
+  if (b == 0) {
+    const bool done = sh.found0 >= count;
+    if (!done)
+      for (int c = tid; c < U; c += blockDim.x) __stcg(ghist + c, sh.hist[c]);
+    __syncthreads();
+    if (tid == 0) {
+      if (done) *search_start = (sh.last0 + 1) % n;
+      __threadfence();
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&gw->state), "r"(done ? kGridDone : kGridGo)
+                   : "memory");
+    }
+    if (done) {
+      grid_pop_leave(gw);
+      return;
+    }
+  } else {
+    for (int c = tid; c < U; c += blockDim.x) __stcg(ghist + b * U + c, sh.hist[c]);
+    if (tid == 0) {
+      int state = kGridUndecided;
+      if (bounded_wait_change(reinterpret_cast<const unsigned*>(&gw->state), kGridUndecided, &gw->failed))
+        state = static_cast<int>(ld_acquire_u32(reinterpret_cast<const unsigned*>(&gw->state)));
+      else
+        report(status, KVCA_ERR_DEVICE_TIMEOUT, b);
+      sh.state = state;
+    }
+    __syncthreads();
+    if (sh.state != kGridGo) {
+      grid_pop_leave(gw);
+      return;
+    }
+  }
+  if (!grid_barrier_words(&gw->bar_count, &gw->failed, status)) {
+    grid_pop_leave(gw);
     return;
   }
 
-  // ---- 3b. threshold, class bases and this range's offsets ----------------
-  for (int c = tid; c < U; c += blockDim.x) {
-    sh.before[c] = 0;
-    sh.limit[c] = 0;  // the class total for now
-    sh.run[c] = 0;
-  }
-  __syncthreads();
-  for (int64_t i = tid; i < G * U; i += blockDim.x) {  // i = CTA * U + class
-    const int h = __ldcg(ghist + i);
-    if (h != 0) {
-      atomicAdd(reinterpret_cast<unsigned long long*>(&sh.limit[i % U]), static_cast<unsigned long long>(h));
-      if (i / U < b)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&sh.before[i % U]), static_cast<unsigned long long>(h));
+  // ---- 3. threshold, class bases and this range's offsets -----------------
+  for (int c = warp; c < U; c += kGridPopWarps) {  // one warp per class
+    long long tot = 0, bef = 0;
+    for (int64_t g = lane; g < G; g += 32) {
+      const int h = __ldcg(ghist + g * U + c);
+      tot += h;
+      if (g < b) bef += h;
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      tot += __shfl_xor_sync(0xffffffffu, tot, d);
+      bef += __shfl_xor_sync(0xffffffffu, bef, d);
+    }
+    if (lane == 0) {
+      sh.before[c] = bef;
+      sh.limit[c] = tot;  // the class total for now
+      sh.run[c] = 0;
     }
   }
   __syncthreads();
@@ -3667,10 +3791,11 @@ __global__ void __launch_bounds__(kGridPopThreads)
   const int threshold = sh.threshold;
   if (threshold < 0) {
     if (b == 0 && tid == 0) report(status, KVCA_ERR_INSUFFICIENT_CAPACITY, count);
+    grid_pop_leave(gw);
     return;
   }
 
-  // ---- 3c. victims and aging of this range --------------------------------
+  // ---- 4. victims and aging of this range ---------------------------------
   int64_t run_prefix = 0;
   for (int64_t tile = cb; tile < ce; tile += blockDim.x) {
     const int64_t vv = tile + tid;
@@ -3680,7 +3805,7 @@ __global__ void __launch_bounds__(kGridPopThreads)
     int64_t v = 0;
     if (active) {
       int64_t lo, hi;
-      v = piece_vector<MetaT>(vv, p0, n, v0b, V0, &lo, &hi);
+      v = piece_vector(vv, p0, n, v0b, V0, &lo, &hi);
       const bool last_piece = split && vv == V - 1;
       if (last_piece) m = sh.split;
       else load_meta_vec(meta, n, v, aligned, m);
@@ -3746,6 +3871,7 @@ __global__ void __launch_bounds__(kGridPopThreads)
       run_prefix += total;
     }
   }
+  grid_pop_leave(gw);
 }
 
 size_t grid_pop_area_offset(int64_t num_slots) {
@@ -3767,8 +3893,6 @@ cudaError_t launch_pop_grid(MetaT* meta, int64_t n, int64_t* search_start, const
   if (grid < 1) grid = 1;
   const int64_t per = (V + grid - 1) / grid;
   const size_t smem = static_cast<size_t>((per * kSpv + 31) / 32) * sizeof(uint32_t);
-  cudaError_t e = cudaMemsetAsync(area, 0, sizeof(PopGridWords), stream);
-  if (e != cudaSuccess) return e;
   void* args[] = {&meta, &n, &search_start, &blocked, &num_blocked, &count, &out, &area, &order,
                   &aligned, &status};
   return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(pop_grid_kernel<MetaT>),
