@@ -373,6 +373,51 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
                            int64_t* d_counts, int64_t* d_status, kvca_stream_t stream);
 
 /*
+ * A KVCacheAdapter over a device-resident store, described once: the
+ * arguments of kvca_load_device_store / kvca_save_device_store that stay
+ * the same from call to call (tables, store, cache rows, work arrays for up
+ * to work_ids ids per call, the 8-word count vector on the device and a
+ * pinned host copy of it, the status pair, the stream).  The session calls
+ * below enqueue the same sequence as those entry points, copy the counts to
+ * counts_host and wait for the stream, so a caller pays one call per
+ * load / save and reads the result from host memory.  No reference
+ * counterpart as one call (the reference's load / save,
+ * adapter.py:205-307, synchronise the host several times per call).
+ */
+typedef struct kvca_adapter_session {
+  int32_t meta_bits;
+  int32_t order;
+  int64_t* l2p;
+  int64_t num_logical;
+  int64_t* p2l;
+  void* slot_meta;
+  int64_t num_slots;
+  int64_t* search_start;
+  uint32_t* scratch_bitmap;    /* kvca_pop_scratch_bytes(num_slots), zero */
+  kvca_device_store store;
+  uint64_t actual;
+  int64_t actual_row_stride;
+  int64_t row_bytes;
+  int64_t* work;               /* 9 x work_ids int64 */
+  void* work_meta;             /* 2 x work_ids slot_meta words */
+  int64_t work_ids;
+  int64_t* counts;             /* device, 8 int64 */
+  int64_t* counts_host;        /* host (pinned), 8 int64: the last call's counts */
+  int64_t* status;             /* device status pair */
+  kvca_stream_t stream;
+} kvca_adapter_session;
+
+/* KVCacheAdapter.load of count ids (count <= work_ids): d_result gets the
+ * slot of each id; counts_host the counts of kvca_load_device_store (error
+ * codes included) when it returns.  Returns a host-side status. */
+int kvca_session_load(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count, int64_t* d_result);
+
+/* KVCacheAdapter.save of count ids and their rows (count <= work_ids);
+ * counts_host gets the counts of kvca_save_device_store. */
+int kvca_session_save(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count,
+                      uint64_t d_block_data);
+
+/*
  * One decode step of a paged cache's block bookkeeping, for num_seqs
  * sequences that each append one token per step.  The num_need sequences
  * d_need[] (distinct) whose current block is full get new blocks: pop

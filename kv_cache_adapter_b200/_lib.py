@@ -72,6 +72,33 @@ class DeviceStore(ctypes.Structure):
     ]
 
 
+class AdapterSession(ctypes.Structure):
+    """kvca_adapter_session."""
+
+    _fields_ = [
+        ("meta_bits", ctypes.c_int32),
+        ("order", ctypes.c_int32),
+        ("l2p", c_ptr),
+        ("num_logical", c_i64),
+        ("p2l", c_ptr),
+        ("slot_meta", c_ptr),
+        ("num_slots", c_i64),
+        ("search_start", c_ptr),
+        ("scratch_bitmap", c_ptr),
+        ("store", DeviceStore),
+        ("actual", ctypes.c_uint64),
+        ("actual_row_stride", c_i64),
+        ("row_bytes", c_i64),
+        ("work", c_ptr),
+        ("work_meta", c_ptr),
+        ("work_ids", c_i64),
+        ("counts", c_ptr),
+        ("counts_host", c_ptr),
+        ("status", c_ptr),
+        ("stream", c_ptr),
+    ]
+
+
 # name -> (restype, argtypes); one entry per declaration in include/kvca.h
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvca_abi_version": (c_int, []),
@@ -137,6 +164,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.POINTER(DeviceStore), ctypes.c_uint64, c_i64, c_i64, ctypes.c_uint64, c_ptr, c_ptr, c_ptr, c_ptr,
          c_ptr],
     ),
+    "kvca_session_load": (c_int, [ctypes.POINTER(AdapterSession), c_ptr, c_i64, c_ptr]),
+    "kvca_session_save": (c_int, [ctypes.POINTER(AdapterSession), c_ptr, c_i64, ctypes.c_uint64]),
     "kvca_host_memory_usable": (c_int, [c_ptr, c_i64]),
     "kvca_wait_selftest": (c_int, [c_ptr, ctypes.c_uint32, c_ptr, c_ptr]),
     "kvca_append_step": (

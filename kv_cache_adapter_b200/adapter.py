@@ -212,6 +212,8 @@ class KVCacheAdapter:
         # An op set with plan_load / plan_save runs the inspect -> split -> pop ->
         # eviction-plan part of load / save as one launch with one host sync.
         self._planned = all(callable(getattr(self._native_ext, n, None)) for n in ("plan_load", "plan_save"))
+        self._session = None  # DeviceStoreSession over the backend's device store (see _store_session)
+        self._session_key = None
 
     # -- views of the packed words (the reference's properties, adapter.py:185-203);
     # each read builds a new tensor, so writing to one changes nothing
@@ -403,14 +405,32 @@ class KVCacheAdapter:
             return None
         return offer(self.actual_blocks)
 
+    def _store_session(self, store):
+        """The op set's session over (these tables, this store), kept while the
+        backend offers the same store tensors; None without sessions."""
+        key = tuple(id(t) for t in store)
+        if self._session is not None and self._session_key == key:
+            return self._session
+        make = getattr(self._native_ext, "DeviceStoreSession", None)
+        if make is None:
+            return None
+        self._session = make(self._logical_to_physical, self._physical_to_logical, self._slot_meta,
+                             self._search_start, self.actual_blocks, *store, order=self.pop_order)
+        self._session_key = key
+        return self._session
+
     def _load_device_store(self, ids: torch.Tensor, store) -> torch.Tensor:
         """load (adapter.py:257-307) with the backend's spill and fill on the
         device: one enqueued sequence and one host read."""
         storage, present, scratch = store
+        session = self._store_session(store)
         try:
-            result, counts = self._native_ext.load_device_store(
-                self._logical_to_physical, self._physical_to_logical, self._slot_meta, self._search_start, ids,
-                self.actual_blocks, storage, present, scratch, order=self.pop_order)
+            if session is not None:
+                result, counts = session.load(ids)
+            else:
+                result, counts = self._native_ext.load_device_store(
+                    self._logical_to_physical, self._physical_to_logical, self._slot_meta, self._search_start, ids,
+                    self.actual_blocks, storage, present, scratch, order=self.pop_order)
         except IndexError as exc:
             raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
         except BlockNotFoundError as exc:
@@ -422,10 +442,14 @@ class KVCacheAdapter:
     def _save_device_store(self, ids: torch.Tensor, block_data: torch.Tensor, store) -> None:
         """save (adapter.py:205-255) with the backend's spill on the device."""
         storage, present, scratch = store
+        session = self._store_session(store)
         try:
-            counts = self._native_ext.save_device_store(
-                self._logical_to_physical, self._physical_to_logical, self._slot_meta, self._search_start, ids,
-                block_data.contiguous(), self.actual_blocks, storage, present, scratch, order=self.pop_order)
+            if session is not None:
+                counts = session.save(ids, block_data.contiguous())
+            else:
+                counts = self._native_ext.save_device_store(
+                    self._logical_to_physical, self._physical_to_logical, self._slot_meta, self._search_start, ids,
+                    block_data.contiguous(), self.actual_blocks, storage, present, scratch, order=self.pop_order)
         except IndexError as exc:
             raise ValueError(f"logical block ids must be inside [0, {self.num_logical_blocks})") from exc
         self.backend.note_device_ops(saved=counts[2] > 0, loaded=False)

@@ -391,6 +391,37 @@ int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   return status_of(kvca::launch_move(fill, stream));
 }
 
+// Copies the counts to the host and waits for the stream: the session
+// calls return with the whole call done.
+static int session_finish(const kvca_adapter_session* s, int rc) {
+  if (rc != KVCA_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(s->stream);
+  if (cudaMemcpyAsync(s->counts_host, s->counts, 8 * sizeof(int64_t), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return KVCA_ERR_CUDA;
+  return KVCA_OK;
+}
+
+int kvca_session_load(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count, int64_t* d_result) {
+  if (!s || !s->counts_host || count < 0 || count > s->work_ids) return KVCA_ERR_BAD_ARGUMENT;
+  return session_finish(
+      s, kvca_load_device_store(s->meta_bits, s->order, s->l2p, s->num_logical, s->p2l, s->slot_meta, s->num_slots,
+                                s->search_start, d_ids, count, s->scratch_bitmap, &s->store, s->actual,
+                                s->actual_row_stride, s->row_bytes, s->work, s->work_meta, d_result, s->counts,
+                                s->status, s->stream));
+}
+
+int kvca_session_save(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count,
+                      uint64_t d_block_data) {
+  if (!s || !s->counts_host || count < 0 || count > s->work_ids) return KVCA_ERR_BAD_ARGUMENT;
+  return session_finish(
+      s, kvca_save_device_store(s->meta_bits, s->order, s->l2p, s->num_logical, s->p2l, s->slot_meta, s->num_slots,
+                                s->search_start, d_ids, count, s->scratch_bitmap, &s->store, s->actual,
+                                s->actual_row_stride, s->row_bytes, d_block_data, s->work, s->work_meta,
+                                s->counts, s->status, s->stream));
+}
+
 int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
                            int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
                            int64_t* d_search_start, const int64_t* d_ids, int64_t count,

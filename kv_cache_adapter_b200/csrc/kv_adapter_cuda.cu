@@ -3202,34 +3202,28 @@ cudaError_t launch_move_bulk(const MoveParams& base, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------------------
-// Staged token-row mover: shared-memory tiles between random rows and chunks
+// Staged token-row gather: shared-memory tiles between random rows and chunks
 // ---------------------------------------------------------------------------
 //
-// For rows of 128 bytes to 1.5 KiB whose chunk side is dense (rows back to
-// back), a (chunk, plane) run of rows is one contiguous range of the chunk,
-// cut into tiles of at most kStagedTileBytes.  A CTA owns a contiguous range
-// of tiles and a ring of kStagedStages tiles in shared memory:
-//   gather: every thread copies its 16-byte vectors of a tile's random source
-//     rows into the tile with cp.async (no register holds the bytes while
-//     they travel), and once the tile has landed one thread writes it to the
-//     chunk with one bulk store; kStagedLookahead tiles are in flight behind
-//     the one being stored;
-//   scatter: one thread bulk-loads the tiles from the chunk (mbarrier
-//     completion), and the threads store each landed tile's vectors to their
-//     random destination rows.
-// The register-bound movers keep at most 9 vectors per lane in flight; here
-// a CTA keeps up to kStagedLookahead x kStagedTileBytes, and several CTAs
-// share an SM.  A gathered row whose index is skipped (negative with
-// KVCA_FLAG_SKIP_NEGATIVE, or reported as bad) is copied from its own chunk
-// row, so the tile store writes its bytes back unchanged.  Waits on the
-// mbarriers are bounded (KVCA_ERR_DEVICE_TIMEOUT).
+// For a gather of rows of 128 to 576 bytes into a dense chunk side (rows
+// back to back), a (chunk, plane) run of rows is one contiguous range of the
+// chunk, cut into tiles of at most kStagedTileBytes.  A CTA owns a
+// contiguous range of tiles and a ring of kStagedStages tiles in shared
+// memory: every thread copies its 16-byte vectors of a tile's random source
+// rows into the tile with cp.async (no register holds the bytes while they
+// travel), and once the tile has landed one thread writes it to the chunk
+// with one bulk store; kStagedLookahead tiles are in flight behind the one
+// being stored, and two CTAs share an SM.  The register-bound stream mover
+// keeps at most 9 vectors per lane in flight.  A row whose index is skipped
+// (negative with KVCA_FLAG_SKIP_NEGATIVE, or reported as bad) is copied
+// from its own chunk row, so the tile store writes its bytes back unchanged.
 
 constexpr int kStagedThreads = 256;
 constexpr int kStagedStages = 5;
 constexpr int kStagedLookahead = kStagedStages - 2;  // one tile stored, one being refilled
 constexpr int64_t kStagedTileBytes = 16384;
 constexpr int64_t kStagedMinVecs = 8;   // 128 bytes
-constexpr int64_t kStagedMaxVecs = 96;  // 1.5 KiB
+constexpr int64_t kStagedMaxVecs = 36;  // 576 bytes
 constexpr int kStagedVecsPerThread = static_cast<int>(kStagedTileBytes / 16 / kStagedThreads);
 static_assert(kStagedVecsPerThread * kStagedThreads * 16 == kStagedTileBytes, "a tile is whole vectors per thread");
 
@@ -3239,20 +3233,35 @@ struct StagedGeom {
   int64_t units;  // chunks x planes
 };
 
-// Tile t of the launch: chunk c, plane pl, rows [r0, r0 + n) of the call.
-__device__ __forceinline__ void staged_tile(const MoveParams& p, const ChunkSide& cs, const StagedGeom& g,
-                                            int64_t t, int64_t* c, int64_t* pl, int64_t* r0, int64_t* n) {
-  const int64_t unit = t / g.tiles_per_unit;
-  const int64_t k = t - unit * g.tiles_per_unit;
-  *c = unit / p.num_planes;
-  *pl = unit - *c * p.num_planes;
-  const int64_t chunk_row0 = *c * cs.rows_per_chunk;
-  const int64_t unit_rows =
-      p.num_rows - chunk_row0 < cs.rows_per_chunk ? p.num_rows - chunk_row0 : cs.rows_per_chunk;
-  *r0 = chunk_row0 + k * g.rows_per_tile;
-  const int64_t left = chunk_row0 + unit_rows - *r0;
-  *n = left < g.rows_per_tile ? left : g.rows_per_tile;
-}
+// Tile position advanced one tile at a time (no divisions per tile).
+struct TileCursor {
+  int64_t c, pl, k;
+  __device__ __forceinline__ void init(const MoveParams& p, const StagedGeom& g, int64_t t) {
+    const int64_t unit = t / g.tiles_per_unit;
+    k = t - unit * g.tiles_per_unit;
+    c = unit / p.num_planes;
+    pl = unit - c * p.num_planes;
+  }
+  __device__ __forceinline__ void next(const MoveParams& p, const StagedGeom& g) {
+    if (++k == g.tiles_per_unit) {
+      k = 0;
+      if (++pl == p.num_planes) {
+        pl = 0;
+        ++c;
+      }
+    }
+  }
+  // first row of the tile and its row count (<= 0 past a short last chunk)
+  __device__ __forceinline__ void rows(const MoveParams& p, const ChunkSide& cs, const StagedGeom& g, int64_t* r0,
+                                       int64_t* n) const {
+    const int64_t chunk_row0 = c * cs.rows_per_chunk;
+    const int64_t unit_rows =
+        p.num_rows - chunk_row0 < cs.rows_per_chunk ? p.num_rows - chunk_row0 : cs.rows_per_chunk;
+    *r0 = chunk_row0 + k * g.rows_per_tile;
+    const int64_t left = chunk_row0 + unit_rows - *r0;
+    *n = left < g.rows_per_tile ? left : g.rows_per_tile;
+  }
+};
 
 __device__ __forceinline__ uint64_t staged_chunk_addr(const ChunkSide& cs, int64_t c, int64_t pl, int64_t r) {
   return cs.base + c * cs.chunk_stride + pl * cs.plane_stride + (r - c * cs.rows_per_chunk) * cs.row_stride;
@@ -3267,7 +3276,7 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__global__ void __launch_bounds__(kStagedThreads) move_rows_staged_gather_kernel(const __grid_constant__ MoveParams p,
+__global__ void __launch_bounds__(kStagedThreads, 1) move_rows_staged_gather_kernel(const __grid_constant__ MoveParams p,
                                                                                  StagedGeom g) {
   extern __shared__ __align__(128) unsigned char tiles[];
   const ChunkSide& cs = p.dst_chunk;
@@ -3281,14 +3290,31 @@ __global__ void __launch_bounds__(kStagedThreads) move_rows_staged_gather_kernel
   const int64_t row_bytes = p.row_vecs * 16;
   const int shift = pow2_shift(ps.block_size);
   const uint32_t base = smem_u32(tiles);
+  // vector v = threadIdx.x + u * kStagedThreads of every tile is row v / rv,
+  // vector v % rv of that row: the same for every tile, so computed once
+  int rr[kStagedVecsPerThread];
+  int64_t voff[kStagedVecsPerThread];
+#pragma unroll
+  for (int u = 0; u < kStagedVecsPerThread; ++u) {
+    const int v = threadIdx.x + u * kStagedThreads;
+    rr[u] = v / rv;
+    voff[u] = static_cast<int64_t>(v - rr[u] * rv) * 16;
+  }
+  TileCursor ld, st;  // the tile loaded next and the tile stored next
+  ld.init(p, g, tb);
+  st = ld;
+  int stage_ld = 0, stage_st = 0;
   for (int64_t k = 0; k < n_tiles + kStagedLookahead; ++k) {
     if (k < n_tiles) {
-      const int stage = static_cast<int>(k % kStagedStages);
+      const int stage = stage_ld;
+      stage_ld = stage_ld + 1 == kStagedStages ? 0 : stage_ld + 1;
       // the store that last read this stage was issued two iterations ago
       if (k >= kStagedStages && threadIdx.x == 0) bulk_wait_read(1);
       __syncthreads();
-      int64_t c, pl, r0, n;
-      staged_tile(p, cs, g, tb + k, &c, &pl, &r0, &n);
+      int64_t r0, n;
+      ld.rows(p, cs, g, &r0, &n);
+      const int64_t c = ld.c, pl = ld.pl;
+      ld.next(p, g);
       const uint64_t plane = ps.planes[pl];
       const uint64_t chunk0 = staged_chunk_addr(cs, c, pl, r0);
       const uint32_t sbase = base + static_cast<uint32_t>(stage * kStagedTileBytes);
@@ -3297,151 +3323,63 @@ __global__ void __launch_bounds__(kStagedThreads) move_rows_staged_gather_kernel
 #pragma unroll
       for (int u = 0; u < kStagedVecsPerThread; ++u) {
         const int v = threadIdx.x + u * kStagedThreads;
-        const int64_t r = r0 + v / rv;
+        const int64_t r = r0 + rr[u];
         idx[u] = v < vecs ? (ps.index != nullptr ? __ldg(ps.index + r) : r) : 0;
       }
 #pragma unroll
       for (int u = 0; u < kStagedVecsPerThread; ++u) {
         const int v = threadIdx.x + u * kStagedThreads;
         if (v < vecs) {
-          const int rr = v / rv;
-          const int vec = v - rr * rv;
-          const int64_t off = paged_slot_offset(ps, idx[u], shift, p.flags, p.status, vec == 0);
-          const uint64_t src = off >= 0 ? plane + off + vec * 16 : chunk0 + rr * row_bytes + vec * 16;
+          const int64_t off = paged_slot_offset(ps, idx[u], shift, p.flags, p.status, voff[u] == 0);
+          const uint64_t src = off >= 0 ? plane + off + voff[u] : chunk0 + rr[u] * row_bytes + voff[u];
           cp_async16(sbase + static_cast<uint32_t>(v) * 16u, src);
         }
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    if (k >= kStagedLookahead) {
-      const int64_t j = k - kStagedLookahead;  // the tile to store
-      cp_async_wait<kStagedLookahead>();       // this thread's copies of tile j have landed
+    if (k >= kStagedLookahead) {              // store tile k - kStagedLookahead
+      cp_async_wait<kStagedLookahead>();       // this thread's copies of that tile have landed
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncthreads();
-      int64_t c, pl, r0, n;
-      staged_tile(p, cs, g, tb + j, &c, &pl, &r0, &n);
+      int64_t r0, n;
+      st.rows(p, cs, g, &r0, &n);
       if (threadIdx.x == 0 && n > 0) {
-        const uint32_t src = base + static_cast<uint32_t>((j % kStagedStages) * kStagedTileBytes);
-        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(staged_chunk_addr(cs, c, pl, r0)),
+        const uint32_t src = base + static_cast<uint32_t>(stage_st * kStagedTileBytes);
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                         staged_chunk_addr(cs, st.c, st.pl, r0)),
                      "r"(src), "r"(static_cast<uint32_t>(n * row_bytes))
                      : "memory");
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       }
+      st.next(p, g);
+      stage_st = stage_st + 1 == kStagedStages ? 0 : stage_st + 1;
     }
   }
   if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(kStagedThreads) move_rows_staged_scatter_kernel(const __grid_constant__ MoveParams p,
-                                                                                  StagedGeom g) {
-  extern __shared__ __align__(128) unsigned char tiles[];
-  __shared__ __align__(8) uint64_t full[kStagedStages];
-  __shared__ int failed;
-  const ChunkSide& cs = p.src_chunk;
-  const PagedSide& ps = p.dst_paged;
-  const int64_t total = g.units * g.tiles_per_unit;
-  const int64_t tb = total * blockIdx.x / gridDim.x;
-  const int64_t te = total * (blockIdx.x + 1) / gridDim.x;
-  const int64_t n_tiles = te - tb;
-  if (n_tiles <= 0) return;
-  const int rv = static_cast<int>(p.row_vecs);
-  const int64_t row_bytes = p.row_vecs * 16;
-  const int shift = pow2_shift(ps.block_size);
-  auto issue = [&](int64_t k) {  // thread 0: bulk load of tile k into its stage
-    const int stage = static_cast<int>(k % kStagedStages);
-    int64_t c, pl, r0, n;
-    staged_tile(p, cs, g, tb + k, &c, &pl, &r0, &n);
-    if (n <= 0) {  // an empty tile (past a short last chunk): complete the phase with no bytes
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&full[stage])) : "memory");
-      return;
-    }
-    const uint32_t bytes = static_cast<uint32_t>(n * row_bytes);
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full[stage])), "r"(bytes)
-                 : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(tiles + stage * kStagedTileBytes)),
-                 "l"(staged_chunk_addr(cs, c, pl, r0)), "r"(bytes), "r"(smem_u32(&full[stage]))
-                 : "memory");
-  };
-  if (threadIdx.x == 0) {
-    failed = 0;
-    for (int s = 0; s < kStagedStages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int64_t k = 0; k < n_tiles && k < kStagedStages; ++k) issue(k);
-  }
-  __syncthreads();
-  int64_t issued = n_tiles < kStagedStages ? n_tiles : kStagedStages;
-  for (int64_t k = 0; k < n_tiles; ++k) {
-    const int stage = static_cast<int>(k % kStagedStages);
-    int64_t c, pl, r0, n;
-    staged_tile(p, cs, g, tb + k, &c, &pl, &r0, &n);
-    const uint64_t plane = ps.planes[pl];
-    const int vecs = static_cast<int>(n) * rv;
-    // this thread's destinations, read before the tile lands
-    int64_t dst_off[kStagedVecsPerThread];
-#pragma unroll
-    for (int u = 0; u < kStagedVecsPerThread; ++u) {
-      const int v = threadIdx.x + u * kStagedThreads;
-      const int64_t r = r0 + v / rv;
-      dst_off[u] = v < vecs ? (ps.index != nullptr ? __ldg(ps.index + r) : r) : 0;
-    }
-#pragma unroll
-    for (int u = 0; u < kStagedVecsPerThread; ++u) {
-      const int v = threadIdx.x + u * kStagedThreads;
-      if (v < vecs) {
-        const int rr = v / rv;
-        const int vec = v - rr * rv;
-        const int64_t off = paged_slot_offset(ps, dst_off[u], shift, p.flags, p.status, vec == 0);
-        dst_off[u] = off >= 0 ? off + vec * 16 : -1;
-      } else {
-        dst_off[u] = -1;
-      }
-    }
-    if (!mbar_wait(&full[stage], static_cast<uint32_t>((k / kStagedStages) & 1))) atomicExch(&failed, 1);
-    __syncthreads();
-    if (failed) break;
-    const unsigned char* tile = tiles + stage * kStagedTileBytes;
-#pragma unroll
-    for (int u = 0; u < kStagedVecsPerThread; ++u) {
-      const int v = threadIdx.x + u * kStagedThreads;
-      if (dst_off[u] >= 0)
-        st_stream(reinterpret_cast<uint4*>(plane + dst_off[u]), *reinterpret_cast<const uint4*>(tile + v * 16));
-    }
-    __syncthreads();  // every thread has read the stage
-    if (threadIdx.x == 0 && issued < n_tiles) {
-      issue(issued);
-      ++issued;
-    }
-  }
-  if (failed && threadIdx.x == 0) {
-    report(p.status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
-    // let the loads still in flight land before shared memory is released
-    for (int64_t k = 0; k < issued; ++k) mbar_wait(&full[k % kStagedStages], static_cast<uint32_t>((k / kStagedStages) & 1));
-  }
-}
-
-// The staged mover takes gathers and scatters of 16-byte-aligned rows of
-// 128 B to 1.5 KiB in device memory whose chunk side is dense.
-bool staged_applies(const MoveParams& p, bool gather) {
-  const ChunkSide& cs = gather ? p.dst_chunk : p.src_chunk;
+// The staged mover takes gathers of 16-byte-aligned rows of 128 to 576
+// bytes in device memory whose chunk side is dense.  B200, random token rows,
+// 1 GiB per move: 128 B 5.25 TB/s (the stream mover 4.87), 576 B 5.60 (5.48),
+// 256 B 5.76 (5.79); 1,152 B 5.64 (5.78) and every scatter width were
+// slower staged (bulk-loaded chunk tiles stored row by row: 128 B 5.01
+// against 5.06, 576 B 4.69 against 5.05), so those stay on the stream mover.
+bool staged_applies(const MoveParams& p) {
   return p.gate == nullptr && !(p.flags & KVCA_FLAG_HOST_MEMORY) && p.row_vecs >= kStagedMinVecs &&
-         p.row_vecs <= kStagedMaxVecs && cs.row_stride == p.row_vecs * 16 && cs.rows_per_chunk > 0 &&
-         p.num_rows > 0;
+         p.row_vecs <= kStagedMaxVecs && p.dst_chunk.row_stride == p.row_vecs * 16 &&
+         p.dst_chunk.rows_per_chunk > 0 && p.num_rows > 0;
 }
 
-template <bool kGather>
 cudaError_t launch_move_staged(const MoveParams& p, cudaStream_t stream) {
   const int64_t row_bytes = p.row_vecs * 16;
-  const ChunkSide& cs = kGather ? p.dst_chunk : p.src_chunk;
+  const ChunkSide& cs = p.dst_chunk;
   StagedGeom g;
   g.rows_per_tile = kStagedTileBytes / row_bytes;
   const int64_t unit_rows = cs.rows_per_chunk < p.num_rows ? cs.rows_per_chunk : p.num_rows;
   if (g.rows_per_tile > unit_rows) g.rows_per_tile = unit_rows;
   g.tiles_per_unit = (unit_rows + g.rows_per_tile - 1) / g.rows_per_tile;
   g.units = (p.num_rows + cs.rows_per_chunk - 1) / cs.rows_per_chunk * p.num_planes;
-  const void* kernel = kGather ? reinterpret_cast<const void*>(move_rows_staged_gather_kernel)
-                               : reinterpret_cast<const void*>(move_rows_staged_scatter_kernel);
+  const void* kernel = reinterpret_cast<const void*>(move_rows_staged_gather_kernel);
   const size_t smem = static_cast<size_t>(kStagedStages) * kStagedTileBytes;
   static int blocks_per_sm = 0;
   if (blocks_per_sm == 0) {
@@ -3456,10 +3394,7 @@ cudaError_t launch_move_staged(const MoveParams& p, cudaStream_t stream) {
   int64_t blocks = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
   const int64_t tiles = g.units * g.tiles_per_unit;
   if (blocks > tiles) blocks = tiles;
-  if (kGather)
-    move_rows_staged_gather_kernel<<<static_cast<unsigned>(blocks), kStagedThreads, smem, stream>>>(p, g);
-  else
-    move_rows_staged_scatter_kernel<<<static_cast<unsigned>(blocks), kStagedThreads, smem, stream>>>(p, g);
+  move_rows_staged_gather_kernel<<<static_cast<unsigned>(blocks), kStagedThreads, smem, stream>>>(p, g);
   return cudaGetLastError();
 }
 
@@ -3477,8 +3412,8 @@ cudaError_t launch_move_vec(const MoveParams& p, int vec_bytes, cudaStream_t str
   switch (vec_bytes) {
     case 16:
       if (p.row_vecs * 16 >= kBulkMinRowBytes) return launch_move_bulk<kSrcPaged, kDstPaged>(p, stream);
-      if constexpr (kSrcPaged != kDstPaged) {
-        if (staged_applies(p, kSrcPaged)) return launch_move_staged<kSrcPaged>(p, stream);
+      if constexpr (kSrcPaged && !kDstPaged) {
+        if (staged_applies(p)) return launch_move_staged(p, stream);
       }
       if (p.row_vecs >= kRowStreamMinVecs && p.row_vecs <= kRowStreamMaxVecs && p.num_rows < (int64_t{1} << 30))
         return launch_move_stream<kSrcPaged, kDstPaged>(p, stream);

@@ -55,6 +55,7 @@ __all__ = [
     "batched_fused_single_layer_kv_transfer",
     "load_device_store",
     "save_device_store",
+    "DeviceStoreSession",
     "check_status",
     "status_word",
     "raise_status",
@@ -781,6 +782,81 @@ def save_device_store(logical_to_physical: torch.Tensor, physical_to_logical: to
         _host_rc(rc, "save_device_store")
         vals = bufs.read_counts(7)
     return _store_counts(vals, "save_device_store", dev)
+
+
+class DeviceStoreSession:
+    """load_device_store / save_device_store for one adapter and store, with
+    the arguments that do not change between calls described once
+    (kvca_adapter_session): a call is one C call that enqueues the whole load
+    or save, copies the counts to pinned host memory and waits for the
+    stream.  The tensors must keep their storage for the session's life (the
+    adapter's tables and cache and the store's rows, present mask and
+    scratch); the work arrays grow with the largest request; the session
+    follows the current stream of the device."""
+
+    def __init__(self, logical_to_physical: torch.Tensor, physical_to_logical: torch.Tensor,
+                 slot_meta: torch.Tensor, search_start: torch.Tensor, actual_blocks: torch.Tensor,
+                 storage: torch.Tensor, present: torch.Tensor, scratch: torch.Tensor, *, order: str | None = None):
+        for t, name in ((logical_to_physical, "logical_to_physical"), (physical_to_logical, "physical_to_logical"),
+                        (search_start, "search_start")):
+            _require(t, torch.int64, name)
+        _require(slot_meta, _META_DTYPES, "slot_meta")
+        desc, a_stride, row_bytes = _store_desc(storage, present, scratch, actual_blocks)
+        self.device = slot_meta.device
+        self.index = _index(self.device)
+        self.row_shape = tuple(actual_blocks.shape[1:])
+        self.dtype = actual_blocks.dtype
+        self.tensors = (logical_to_physical, physical_to_logical, slot_meta, search_start, actual_blocks, storage,
+                        present, scratch)
+        self.meta_dtype = slot_meta.dtype
+        self.counts = torch.zeros(8, dtype=torch.int64, device=self.device)
+        self.counts_host = torch.zeros(8, dtype=torch.int64, pin_memory=True)
+        self.counts_view = (ctypes.c_int64 * 8).from_address(self.counts_host.data_ptr())
+        n = slot_meta.numel()
+        self.s = _lib.AdapterSession(
+            _meta_bits(slot_meta), POP_ORDERS[order or _DEFAULT_POP_ORDER], logical_to_physical.data_ptr(),
+            logical_to_physical.numel(), physical_to_logical.data_ptr(), slot_meta.data_ptr(), n,
+            search_start.data_ptr(), _bitmap(self.device, n).data_ptr(), desc, actual_blocks.data_ptr(), a_stride,
+            row_bytes, None, None, 0, self.counts.data_ptr(), self.counts_host.data_ptr(),
+            _status(self.device).data_ptr(), _stream(self.device).value)
+        self.ref = ctypes.byref(self.s)
+        self.work = self.work_meta = None
+        self._grow(64)
+
+    def _grow(self, k: int) -> None:
+        cap = max(k, 2 * int(self.s.work_ids), 64)
+        self.work = torch.empty(9 * cap, dtype=torch.int64, device=self.device)
+        self.work_meta = torch.empty(2 * cap, dtype=self.meta_dtype, device=self.device)
+        self.s.work = self.work.data_ptr()
+        self.s.work_meta = self.work_meta.data_ptr()
+        self.s.work_ids = cap
+
+    def _prepare(self, k: int) -> None:
+        if k > self.s.work_ids:
+            self._grow(k)
+        stream = _raw_stream(self.index) if _raw_stream is not None else _stream(self.device).value
+        if stream != self.s.stream:
+            self.s.stream = stream
+
+    def load(self, logical_block_ids: torch.Tensor) -> tuple[torch.Tensor, list[int]]:
+        """As load_device_store: (slots, counts)."""
+        k = logical_block_ids.numel()
+        self._prepare(k)
+        result = torch.empty(k, dtype=torch.int64, device=self.device)
+        _host_rc(_lib_handle.kvca_session_load(self.ref, logical_block_ids.data_ptr(), k, result.data_ptr()),
+                 "load_device_store")
+        return result, _store_counts(self.counts_view[:], "load_device_store", self.device)
+
+    def save(self, logical_block_ids: torch.Tensor, block_data: torch.Tensor) -> list[int]:
+        """As save_device_store: counts."""
+        k = logical_block_ids.numel()
+        if block_data.dtype != self.dtype or tuple(block_data.shape) != (k, *self.row_shape) \
+                or not block_data.is_contiguous() or block_data.device != self.device:
+            _chunk_tensor(block_data, (k, *self.row_shape), self.dtype, self.device, "block_data")
+        self._prepare(k)
+        _host_rc(_lib_handle.kvca_session_save(self.ref, logical_block_ids.data_ptr(), k, block_data.data_ptr()),
+                 "save_device_store")
+        return _store_counts(self.counts_view[:7], "save_device_store", self.device)
 
 
 # ---------------------------------------------------------------------------

@@ -1,11 +1,11 @@
-"""GPU parity for the staged token-row mover (rows of 128 B to 1.5 KiB with a
-dense chunk side: shared-memory tiles filled by cp.async and written by one
-bulk store for gathers, bulk-loaded and stored row by row for scatters)
-through the C ABI, where the calls the Python API never makes are possible:
-a last chunk shorter than the others, chunks shorter than a tile and longer
-than several tiles, padding and out-of-range ids in the same call, against
-the oracle's torch CPU indexing, byte for byte.  A padded or refused row of a
-gather leaves its chunk row as it was; of a scatter, its cache row."""
+"""GPU parity for token-row moves through the C ABI, where the calls the
+Python API never makes are possible: a last chunk shorter than the others,
+chunks shorter than a tile and longer than several tiles, padding and
+out-of-range ids in the same call, against the oracle's torch CPU indexing,
+byte for byte.  Gathers of rows of 128 to 576 bytes take the staged mover
+(shared-memory tiles filled by cp.async and written by one bulk store), the
+others the stream mover.  A padded or refused row of a gather leaves its
+chunk row as it was; of a scatter, its cache row."""
 from __future__ import annotations
 
 import ctypes
