@@ -380,7 +380,8 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
  * pinned host copy of it, the status pair, the stream).  The session calls
  * below enqueue the same sequence as those entry points, copy the counts to
  * counts_host and wait for the stream, so a caller pays one call per
- * load / save and reads the result from host memory.  No reference
+ * load / save and reads the result from host memory.  Calls on one session
+ * must not overlap (one host thread).  No reference
  * counterpart as one call (the reference's load / save,
  * adapter.py:205-307, synchronise the host several times per call).
  */
@@ -402,20 +403,25 @@ typedef struct kvca_adapter_session {
   void* work_meta;             /* 2 x work_ids slot_meta words */
   int64_t work_ids;
   int64_t* counts;             /* device, 8 int64 */
-  int64_t* counts_host;        /* host (pinned), 8 int64: the last call's counts */
+  int64_t* counts_host;        /* pinned host memory the device reaches at the same address, 9 int64:
+                                  the last call's 8 counts, then its sequence number */
   int64_t* status;             /* device status pair */
   kvca_stream_t stream;
+  int64_t sequence;            /* calls made so far (the session calls advance it) */
 } kvca_adapter_session;
 
 /* KVCacheAdapter.load of count ids (count <= work_ids): d_result gets the
  * slot of each id; counts_host the counts of kvca_load_device_store (error
- * codes included) when it returns.  Returns a host-side status. */
-int kvca_session_load(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count, int64_t* d_result);
+ * codes included) when it returns.  When the call is one launch, that launch
+ * writes the counts and the sequence number into counts_host as its last
+ * action and the host waits for them there (no copy, no stream
+ * synchronisation); otherwise the counts are copied and the stream waited
+ * for.  Returns a host-side status. */
+int kvca_session_load(kvca_adapter_session* s, const int64_t* d_ids, int64_t count, int64_t* d_result);
 
 /* KVCacheAdapter.save of count ids and their rows (count <= work_ids);
- * counts_host gets the counts of kvca_save_device_store. */
-int kvca_session_save(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count,
-                      uint64_t d_block_data);
+ * counts_host gets the counts of kvca_save_device_store, as for the load. */
+int kvca_session_save(kvca_adapter_session* s, const int64_t* d_ids, int64_t count, uint64_t d_block_data);
 
 /*
  * One decode step of a paged cache's block bookkeeping, for num_seqs

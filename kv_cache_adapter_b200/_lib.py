@@ -96,6 +96,7 @@ class AdapterSession(ctypes.Structure):
         ("counts_host", c_ptr),
         ("status", c_ptr),
         ("stream", c_ptr),
+        ("sequence", c_i64),
     ]
 
 

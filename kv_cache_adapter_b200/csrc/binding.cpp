@@ -5,6 +5,8 @@
 // and stride allows, and hands off to the sm_100a launchers.  It allocates
 // nothing and never synchronises the stream.
 
+#include <chrono>
+
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -341,13 +343,16 @@ int kvca_host_memory_usable(const void* p, int64_t bytes) {
   return 1;
 }
 
-int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
-                           int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
-                           int64_t* d_search_start, const int64_t* d_ids, int64_t count,
-                           uint32_t* d_scratch_bitmap, const kvca_device_store* store,
-                           uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
-                           int64_t* d_work, void* d_work_meta, int64_t* d_result,
-                           int64_t* d_counts, int64_t* d_status, kvca_stream_t stream) {
+// host_counts (session calls): when the call is one launch, that launch
+// ends by writing the counts and seq to host_counts (*signalled = true).
+static int load_device_store_impl(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+                                  int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                                  int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                                  uint32_t* d_scratch_bitmap, const kvca_device_store* store,
+                                  uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
+                                  int64_t* d_work, void* d_work_meta, int64_t* d_result,
+                                  int64_t* d_counts, int64_t* d_status, kvca_stream_t stream,
+                                  int64_t* host_counts, int64_t seq, bool* signalled) {
   if (!plan_args_ok(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
                     d_search_start, d_ids, count, d_scratch_bitmap, d_counts) ||
       !store_ok(store, d_actual, actual_row_stride, row_bytes) || !d_work || !d_work_meta ||
@@ -361,10 +366,11 @@ int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   if (small_store_call(count, row_bytes, store->move_flags)) {
     const kvca::StoreRowArgs rows{d_actual, actual_row_stride, store->storage, store->storage_row_stride, 0,
                                   row_bytes, vec};
+    *signalled = host_counts != nullptr;
     return status_of(kvca::launch_store_load_small(
         meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids, count,
         d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_result, d_counts, d_status,
-        rows, stream));
+        rows, stream, host_counts, seq));
   }
   int rc = status_of(kvca::launch_store_load_meta(
       meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
@@ -391,44 +397,28 @@ int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   return status_of(kvca::launch_move(fill, stream));
 }
 
-// Copies the counts to the host and waits for the stream: the session
-// calls return with the whole call done.
-static int session_finish(const kvca_adapter_session* s, int rc) {
-  if (rc != KVCA_OK) return rc;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(s->stream);
-  if (cudaMemcpyAsync(s->counts_host, s->counts, 8 * sizeof(int64_t), cudaMemcpyDeviceToHost, st) !=
-          cudaSuccess ||
-      cudaStreamSynchronize(st) != cudaSuccess)
-    return KVCA_ERR_CUDA;
-  return KVCA_OK;
-}
-
-int kvca_session_load(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count, int64_t* d_result) {
-  if (!s || !s->counts_host || count < 0 || count > s->work_ids) return KVCA_ERR_BAD_ARGUMENT;
-  return session_finish(
-      s, kvca_load_device_store(s->meta_bits, s->order, s->l2p, s->num_logical, s->p2l, s->slot_meta, s->num_slots,
-                                s->search_start, d_ids, count, s->scratch_bitmap, &s->store, s->actual,
-                                s->actual_row_stride, s->row_bytes, s->work, s->work_meta, d_result, s->counts,
-                                s->status, s->stream));
-}
-
-int kvca_session_save(const kvca_adapter_session* s, const int64_t* d_ids, int64_t count,
-                      uint64_t d_block_data) {
-  if (!s || !s->counts_host || count < 0 || count > s->work_ids) return KVCA_ERR_BAD_ARGUMENT;
-  return session_finish(
-      s, kvca_save_device_store(s->meta_bits, s->order, s->l2p, s->num_logical, s->p2l, s->slot_meta, s->num_slots,
-                                s->search_start, d_ids, count, s->scratch_bitmap, &s->store, s->actual,
-                                s->actual_row_stride, s->row_bytes, d_block_data, s->work, s->work_meta,
-                                s->counts, s->status, s->stream));
-}
-
-int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+int kvca_load_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
                            int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
                            int64_t* d_search_start, const int64_t* d_ids, int64_t count,
                            uint32_t* d_scratch_bitmap, const kvca_device_store* store,
                            uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
-                           uint64_t d_block_data, int64_t* d_work, void* d_work_meta,
+                           int64_t* d_work, void* d_work_meta, int64_t* d_result,
                            int64_t* d_counts, int64_t* d_status, kvca_stream_t stream) {
+  bool signalled = false;
+  return load_device_store_impl(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
+                                d_search_start, d_ids, count, d_scratch_bitmap, store, d_actual,
+                                actual_row_stride, row_bytes, d_work, d_work_meta, d_result, d_counts, d_status,
+                                stream, nullptr, 0, &signalled);
+}
+
+static int save_device_store_impl(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+                                  int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                                  int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                                  uint32_t* d_scratch_bitmap, const kvca_device_store* store,
+                                  uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
+                                  uint64_t d_block_data, int64_t* d_work, void* d_work_meta,
+                                  int64_t* d_counts, int64_t* d_status, kvca_stream_t stream,
+                                  int64_t* host_counts, int64_t seq, bool* signalled) {
   if (!plan_args_ok(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
                     d_search_start, d_ids, count, d_scratch_bitmap, d_counts) ||
       !store_ok(store, d_actual, actual_row_stride, row_bytes) || !d_block_data || !d_work ||
@@ -443,10 +433,11 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   if (small_store_call(count, row_bytes, store->move_flags)) {
     const kvca::StoreRowArgs rows{d_actual, actual_row_stride, store->storage, store->storage_row_stride,
                                   d_block_data, row_bytes, vec};
+    *signalled = host_counts != nullptr;
     return status_of(kvca::launch_store_save_small(
         meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids, count,
         d_scratch_bitmap, store->scratch, store->present, d_work, d_work_meta, d_counts, d_status, rows,
-        stream));
+        stream, host_counts, seq));
   }
   int rc = status_of(kvca::launch_store_save_meta(
       meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots, d_search_start, d_ids,
@@ -472,6 +463,66 @@ int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num
   kvca::MoveArgs scatter{kvca::MoveKind::kScatter, nullptr, &data, &actual_selected, nullptr, 1,
                          k, row_bytes, vec, KVCA_FLAG_SKIP_NEGATIVE, d_status};
   return status_of(kvca::launch_move(scatter, stream));
+}
+
+int kvca_save_device_store(int meta_bits, int order, int64_t* d_l2p, int64_t num_logical,
+                           int64_t* d_p2l, void* d_slot_meta, int64_t num_slots,
+                           int64_t* d_search_start, const int64_t* d_ids, int64_t count,
+                           uint32_t* d_scratch_bitmap, const kvca_device_store* store,
+                           uint64_t d_actual, int64_t actual_row_stride, int64_t row_bytes,
+                           uint64_t d_block_data, int64_t* d_work, void* d_work_meta,
+                           int64_t* d_counts, int64_t* d_status, kvca_stream_t stream) {
+  bool signalled = false;
+  return save_device_store_impl(meta_bits, order, d_l2p, num_logical, d_p2l, d_slot_meta, num_slots,
+                                d_search_start, d_ids, count, d_scratch_bitmap, store, d_actual,
+                                actual_row_stride, row_bytes, d_block_data, d_work, d_work_meta, d_counts,
+                                d_status, stream, nullptr, 0, &signalled);
+}
+
+// Ends a session call: when its one launch signals the host, waits for the
+// sequence number in host memory (bounded; after about a second the stream's
+// own synchronisation decides); otherwise copies the counts to the host and
+// waits for the stream.  Either way the call returns with its work done.
+static int session_finish(kvca_adapter_session* s, int rc, bool signalled) {
+  if (rc != KVCA_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(s->stream);
+  if (signalled) {
+    volatile int64_t* done = s->counts_host + 8;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t spins = 0;; ++spins) {
+      if (*done == s->sequence) return KVCA_OK;
+      if ((spins & 4095u) == 4095u && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(1)) break;
+    }
+    if (cudaStreamSynchronize(st) != cudaSuccess) return KVCA_ERR_CUDA;
+    return *done == s->sequence ? KVCA_OK : KVCA_ERR_CUDA;
+  }
+  if (cudaMemcpyAsync(s->counts_host, s->counts, 8 * sizeof(int64_t), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return KVCA_ERR_CUDA;
+  return KVCA_OK;
+}
+
+int kvca_session_load(kvca_adapter_session* s, const int64_t* d_ids, int64_t count, int64_t* d_result) {
+  if (!s || !s->counts_host || count < 0 || count > s->work_ids) return KVCA_ERR_BAD_ARGUMENT;
+  bool signalled = false;
+  ++s->sequence;
+  const int rc = load_device_store_impl(
+      s->meta_bits, s->order, s->l2p, s->num_logical, s->p2l, s->slot_meta, s->num_slots, s->search_start, d_ids,
+      count, s->scratch_bitmap, &s->store, s->actual, s->actual_row_stride, s->row_bytes, s->work, s->work_meta,
+      d_result, s->counts, s->status, s->stream, s->counts_host, s->sequence, &signalled);
+  return session_finish(s, rc, signalled);
+}
+
+int kvca_session_save(kvca_adapter_session* s, const int64_t* d_ids, int64_t count, uint64_t d_block_data) {
+  if (!s || !s->counts_host || count < 0 || count > s->work_ids) return KVCA_ERR_BAD_ARGUMENT;
+  bool signalled = false;
+  ++s->sequence;
+  const int rc = save_device_store_impl(
+      s->meta_bits, s->order, s->l2p, s->num_logical, s->p2l, s->slot_meta, s->num_slots, s->search_start, d_ids,
+      count, s->scratch_bitmap, &s->store, s->actual, s->actual_row_stride, s->row_bytes, d_block_data, s->work,
+      s->work_meta, s->counts, s->status, s->stream, s->counts_host, s->sequence, &signalled);
+  return session_finish(s, rc, signalled);
 }
 
 int kvca_exchange(const kvca_paged_desc* slots, const kvca_paged_desc* store,

@@ -2161,12 +2161,30 @@ struct StoreRows {
 
 // work as in launch_store_load_meta (9 x k int64): hit_slots, hit_pins,
 // miss_ids, victims, evict_ids, evict_slots, xslot, spill_to, fill_from.
+// The last action of a one-launch store call made for a session: the
+// call's 8 counts and then its sequence number go to pinned host memory, so
+// the host learns that the call is done (and its outcome) by reading host
+// memory instead of copying the counts and synchronising the stream.  The
+// block barrier orders every thread's writes of the call before thread 0's
+// system-scope fence and the sequence store.
+__device__ __forceinline__ void signal_host(const int64_t* counts, int64_t* host_counts, int64_t seq) {
+  if (host_counts == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) host_counts[i] = counts[i];
+    __threadfence_system();
+    *reinterpret_cast<volatile int64_t*>(host_counts + 8) = seq;
+  }
+}
+
 template <typename MetaT>
 __global__ void __launch_bounds__(1024)
     store_load_small_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
                             int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap, int order,
                             bool aligned, int32_t* scratch, uint8_t* present, int64_t* work, MetaT* hit_usage,
-                            int64_t* result, int64_t* counts, int64_t* status, StoreRows rows) {
+                            int64_t* result, int64_t* counts, int64_t* status, StoreRows rows,
+                            int64_t* host_counts, int64_t seq) {
   __shared__ PlanShared<MetaT> sh;
   __shared__ FinishShared fs;
   int64_t* hit_slots = work;
@@ -2194,6 +2212,7 @@ __global__ void __launch_bounds__(1024)
   __syncthreads();
   copy_rows_cta(rows.actual, rows.actual_stride, xslot, rows.storage, rows.storage_stride, fill_from, k,
                 rows.row_bytes, rows.vec);
+  signal_host(counts, host_counts, seq);
 }
 
 // work as in launch_store_save_meta (5 x k int64): selected, allocated,
@@ -2203,7 +2222,7 @@ __global__ void __launch_bounds__(1024)
     store_save_small_kernel(int64_t* l2p, int64_t n_logical, int64_t* p2l, MetaT* meta, int64_t n,
                             int64_t* search_start, const int64_t* ids, int64_t k, uint32_t* bitmap, int order,
                             bool aligned, int32_t* scratch, uint8_t* present, int64_t* work, MetaT* work_meta,
-                            int64_t* counts, int64_t* status, StoreRows rows) {
+                            int64_t* counts, int64_t* status, StoreRows rows, int64_t* host_counts, int64_t seq) {
   __shared__ PlanShared<MetaT> sh;
   __shared__ FinishShared fs;
   int64_t* selected = work;
@@ -2227,6 +2246,7 @@ __global__ void __launch_bounds__(1024)
   __syncthreads();
   copy_rows_cta(rows.actual, rows.actual_stride, move_slots, rows.data, rows.row_bytes, nullptr, k, rows.row_bytes,
                 rows.vec);
+  signal_host(counts, host_counts, seq);
 }
 
 // ---------------------------------------------------------------------------
@@ -4336,13 +4356,15 @@ cudaError_t launch_store_load_small(int meta_bits, int order, int64_t* l2p, int6
                                     void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
                                     int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
                                     int64_t* work, void* work_meta, int64_t* result, int64_t* counts,
-                                    int64_t* status, const StoreRowArgs& r, cudaStream_t stream) {
+                                    int64_t* status, const StoreRowArgs& r, cudaStream_t stream,
+                                    int64_t* host_counts, int64_t seq) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
   const StoreRows rows{r.actual, r.actual_stride, r.storage, r.storage_stride, r.data, r.row_bytes, r.vec};
   KVCA_META_DISPATCH(meta_bits, store_load_small_kernel<MetaT><<<1, small_store_threads(count), 0, stream>>>(
                                     l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots, search_start, ids,
                                     count, bitmap, order, aligned, scratch, present, work,
-                                    static_cast<MetaT*>(work_meta), result, counts, status, rows));
+                                    static_cast<MetaT*>(work_meta), result, counts, status, rows, host_counts,
+                                    seq));
   return cudaGetLastError();
 }
 
@@ -4350,13 +4372,14 @@ cudaError_t launch_store_save_small(int meta_bits, int order, int64_t* l2p, int6
                                     void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
                                     int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
                                     int64_t* work, void* work_meta, int64_t* counts, int64_t* status,
-                                    const StoreRowArgs& r, cudaStream_t stream) {
+                                    const StoreRowArgs& r, cudaStream_t stream, int64_t* host_counts,
+                                    int64_t seq) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
   const StoreRows rows{r.actual, r.actual_stride, r.storage, r.storage_stride, r.data, r.row_bytes, r.vec};
   KVCA_META_DISPATCH(meta_bits, store_save_small_kernel<MetaT><<<1, small_store_threads(count), 0, stream>>>(
                                     l2p, num_logical, p2l, static_cast<MetaT*>(meta), num_slots, search_start, ids,
                                     count, bitmap, order, aligned, scratch, present, work,
-                                    static_cast<MetaT*>(work_meta), counts, status, rows));
+                                    static_cast<MetaT*>(work_meta), counts, status, rows, host_counts, seq));
   return cudaGetLastError();
 }
 

@@ -199,12 +199,14 @@ cudaError_t launch_store_load_small(int meta_bits, int order, int64_t* l2p, int6
                                     void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
                                     int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
                                     int64_t* work, void* work_meta, int64_t* result, int64_t* counts,
-                                    int64_t* status, const StoreRowArgs& rows, cudaStream_t stream);
+                                    int64_t* status, const StoreRowArgs& rows, cudaStream_t stream, int64_t* host_counts = nullptr,
+                                    int64_t seq = 0);
 cudaError_t launch_store_save_small(int meta_bits, int order, int64_t* l2p, int64_t num_logical, int64_t* p2l,
                                     void* meta, int64_t num_slots, int64_t* search_start, const int64_t* ids,
                                     int64_t count, uint32_t* bitmap, int32_t* scratch, uint8_t* present,
                                     int64_t* work, void* work_meta, int64_t* counts, int64_t* status,
-                                    const StoreRowArgs& rows, cudaStream_t stream);
+                                    const StoreRowArgs& rows, cudaStream_t stream, int64_t* host_counts = nullptr,
+                                    int64_t seq = 0);
 
 cudaError_t launch_wait_selftest(const uint32_t* flag, uint32_t from, int64_t* status,
                                  cudaStream_t stream);

@@ -810,7 +810,7 @@ class DeviceStoreSession:
                         present, scratch)
         self.meta_dtype = slot_meta.dtype
         self.counts = torch.zeros(8, dtype=torch.int64, device=self.device)
-        self.counts_host = torch.zeros(8, dtype=torch.int64, pin_memory=True)
+        self.counts_host = torch.zeros(16, dtype=torch.int64, pin_memory=True)  # counts, then the sequence
         self.counts_view = (ctypes.c_int64 * 8).from_address(self.counts_host.data_ptr())
         n = slot_meta.numel()
         self.s = _lib.AdapterSession(
@@ -818,7 +818,7 @@ class DeviceStoreSession:
             logical_to_physical.numel(), physical_to_logical.data_ptr(), slot_meta.data_ptr(), n,
             search_start.data_ptr(), _bitmap(self.device, n).data_ptr(), desc, actual_blocks.data_ptr(), a_stride,
             row_bytes, None, None, 0, self.counts.data_ptr(), self.counts_host.data_ptr(),
-            _status(self.device).data_ptr(), _stream(self.device).value)
+            _status(self.device).data_ptr(), _stream(self.device).value, 0)
         self.ref = ctypes.byref(self.s)
         self.work = self.work_meta = None
         self._grow(64)
