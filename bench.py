@@ -963,8 +963,12 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     pool = args.pool_blocks or 65536
     mix = DecodeMix(ops, device, layers=32, heads=heads, head_dim=128, block_size=16, num_blocks=pool,
                     seqs=256, dtype=torch.float16, seed=1234 + rank,
-                    max_steps=(args.warmup * per + 17) + 4 * cycles * 16 + 256)  # warm-up + 4 timed runs
+                    max_steps=(args.warmup * per + 17) + 5 * (cycles + 4) * 16 + 256)  # warm-up + 5 timed runs
     rows = torch.randn((1, mix.num_planes, mix.seqs, *mix.row_shape), dtype=torch.float16, device=device)
+    # the whole-cycle runs take a new token row per sequence, plane and step
+    # (16 steps' rows, 512 MiB with 8 KV heads), so no step re-reads the last
+    # one's rows from L2
+    cycle_rows = torch.randn((16, mix.num_planes, mix.seqs, *mix.row_shape), dtype=torch.float16, device=device)
     # warm-up: eager steps (at least one full cycle), aligned to the start of a cycle
     warm = max(args.warmup * per, 17)
     warm += (1 - warm) % 16
@@ -1006,27 +1010,34 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     moved = 2 * mix.num_planes * (tokens * row_bytes + blocks * row_bytes * mix.block_size)
     del graph
     # whole-cycle booking: one append_steps launch books the 16 steps of the
-    # next cycle while the current cycle's moves run; a replay = 2 cycles
+    # next cycle while the current cycle's moves run; a replay = 2 cycles.
+    # First each step's scatter paired with the next step's gather (one launch
+    # per decode step), then each cycle's moves as one move_cycle launch.
     mix.pipelined = False
-    mix.start_cycles()
-    mix.run_cycle(rows)
-    graph, per_two = mix.capture_cycles(rows)
-    assert per_two == 2 * per_cycle
     replays = -(-cycles // 2)
-    with ClockSampler(device.index) as clocks:
-        ms = timed(lambda: [graph.replay() for _ in range(replays)])
-    del graph
-    mix.stop_cycles(rows)
-    torch.cuda.synchronize(device)
-    ops.check_status(device)
     cyc_steps = 2 * replays * 16
-    # launches per cycle: the booking, then one per step (the token scatter
-    # with the next step's spill gather)
-    cycle_launches = 1 + 16
+    results = {}
+    for one_launch in (False, True):
+        mix.start_cycles(one_launch=one_launch)
+        mix.run_cycle(cycle_rows)
+        graph, per_two = mix.capture_cycles(cycle_rows)
+        assert per_two == 2 * per_cycle
+        with ClockSampler(device.index) as clk:
+            results[one_launch] = (timed(lambda: [graph.replay() for _ in range(replays)]), clk)
+        del graph
+        mix.stop_cycles(cycle_rows)
+        torch.cuda.synchronize(device)
+        ops.check_status(device)
+    ms, clocks = results[True]
+    pair_ms = results[False][0]
+    # launches per cycle: the booking, then the cycle's moves (one launch, or
+    # one per step: the token scatter with the next step's spill gather)
+    cycle_launches = 1 + 1
     cyc_moved = 2 * mix.num_planes * (cyc_steps * mix.seqs * row_bytes + replays * per_two * row_bytes * mix.block_size)
     if rank != 0:
         return
     decode_steps = cycles * 16
+    peak, peak_kind = _peaks()
     line = {
         "metric": "paged-KV decode append + eviction gather GB/s",
         "value": round(world * cyc_moved / (ms / 1e3) / 1e9, 2),
@@ -1053,11 +1064,33 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         "gpu_launches": replays * 2 * cycle_launches,
         "tokens_per_s": round(world * cyc_steps * mix.seqs / (ms / 1e3), 1),
         "evictions_per_s": round(world * replays * per_two / (ms / 1e3), 1),
-        "gpu_launches_per_decode_step": "scatter_tokens, plus one gather on steps that evict, plus 1/16 of an "
-                                        "append_steps launch (pop, commit, release, slot_mapping of 16 steps)",
+        "gpu_launches_per_decode_step": "1/16 of a move_cycle launch (the cycle's 16 spill gathers and 16 token "
+                                        "scatters) plus 1/16 of an append_steps launch (pop, commit, release, "
+                                        "slot_mapping of 16 steps)",
         "issue": "CUDA graph, one replay per two 16-step cycles; the bookkeeping of the next cycle (one "
-                 "append_steps launch) on a second stream, overlapping the current cycle's moves "
-                 "(victims and slot_mappings double-buffered by cycle)",
+                 "append_steps launch) on a second stream, overlapping the current cycle's moves, which are one "
+                 "move_cycle launch (victims and slot_mappings double-buffered by cycle); needs every step's token "
+                 "rows when the cycle's launch starts (an engine that produces one token per forward pass moves "
+                 "each step as it comes: paired_steps_graph)",
+        "token_rows": "a new row per sequence, plane and step (16 steps' rows in HBM)",
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(cyc_moved / (ms / 1e3) / 1e9, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(cyc_moved / (ms / 1e3) / 1e9 / peak, 4),
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+            "traffic": None,
+            "kernel": "move_cycle_kernel (one launch per 16-step cycle; the cycle's booking runs beside it on "
+                      "another stream), timed over whole graph replays",
+            "algorithmic_bytes_per_decode_step": 2 * mix.num_planes * (mix.seqs * row_bytes +
+                                                                       per_cycle // 16 * row_bytes * mix.block_size),
+        },
+        "paired_steps_graph": {"value": round(world * cyc_moved / (pair_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                               "ms_per_decode_step": round(pair_ms / cyc_steps, 5),
+                               "gpu_launches_per_decode_step": 1 + 1 / 16,
+                               "issue": "same booking; each step's token scatter paired with the next step's "
+                                        "spill gather in one launch (one launch per decode step)"},
         "per_step_pipelined_graph": {"value": round(world * moved / (step_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                                      "ms_per_decode_step": round(step_ms / decode_steps, 5),
                                      "issue": "CUDA graph per 16-step cycle, each step's append_step on a second "

@@ -563,6 +563,42 @@ int kvca_scatter_gather(const kvca_chunk_desc* s_src, const kvca_paged_desc* s_d
                         int64_t g_row_bytes, int32_t s_flags, int32_t g_flags, int64_t* d_status,
                         kvca_stream_t stream);
 
+/*
+ * The moves of a booked decode cycle in one launch (the victims and the
+ * num_steps x num_seqs slot mapping that kvca_append_steps writes).  For
+ * each step q in order, with the result of running them one after the other:
+ *   1. the spill gather of victims[offsets[q] .. offsets[q + 1]): block rows
+ *      (block_row_bytes each, block_src->block_size 1, index = victims) of
+ *      every plane to spill rows offsets[q] .. (the gather of adapter.py:543);
+ *   2. the token scatter of token rows q * num_seqs + s (tokens, chunk
+ *      layout; chunk_stride 0 with rows_per_chunk = num_seqs moves the same
+ *      rows every step) to slots token_dst->index[q * num_seqs + s]
+ *      (reshape-and-cache, adapter.py:1275-1285).
+ * One cooperative launch of one CTA per SM streams every step's rows; items
+ * wait for earlier steps only where a step's rows depend on them (a token
+ * row landing in a block that this or an earlier step evicts waits for that
+ * gather; a gather of a block that an earlier step wrote waits for that
+ * scatter).  token_dst and block_src describe the same cache (same planes,
+ * num_blocks and block_stride).  Slots must be distinct across the call (a
+ * slot given twice ends with either row); negative slots and victims with
+ * KVCA_FLAG_SKIP_NEGATIVE skip their rows, other ids outside the cache give
+ * KVCA_ERR_BAD_INDEX (their rows skipped), offsets that do not start at 0,
+ * decrease or pass num_victims (the entries of block_src->index) or
+ * spill_rows give KVCA_ERR_BAD_ARGUMENT and move nothing.  1 <= num_steps
+ * <= 32; rows, strides and addresses 16-byte aligned; a block's token rows
+ * and its block row lie within block_stride.
+ * d_scratch: kvca_move_cycle_scratch_bytes(num_blocks) bytes, zeroed once
+ * and kept for the cache's life (launches that use one scratch must not
+ * overlap); after KVCA_ERR_DEVICE_TIMEOUT zero it again.  No reference
+ * counterpart.
+ */
+int64_t kvca_move_cycle_scratch_bytes(int64_t num_blocks);
+int kvca_move_cycle(const kvca_chunk_desc* tokens, const kvca_paged_desc* token_dst, int64_t token_row_bytes,
+                    const kvca_paged_desc* block_src, int64_t num_victims, const kvca_chunk_desc* spill,
+                    int64_t block_row_bytes, int64_t num_planes, const int64_t* d_offsets, int64_t num_steps,
+                    int64_t num_seqs, int64_t spill_rows, int32_t flags, void* d_scratch, int64_t* d_status,
+                    kvca_stream_t stream);
+
 /* Paged -> paged in one pass: dst[dst.index[r]] = src[src.index[r]]
  * (the index_select + index_copy_ pair of adapter.py:779-787). */
 int kvca_copy_paged(const kvca_paged_desc* src, const kvca_paged_desc* dst, int64_t num_planes,

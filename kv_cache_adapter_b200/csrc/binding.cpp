@@ -653,6 +653,55 @@ int kvca_scatter_gather(const kvca_chunk_desc* s_src, const kvca_paged_desc* s_d
   return status_of(kvca::launch_scatter_gather(s, g, stream));
 }
 
+int64_t kvca_move_cycle_scratch_bytes(int64_t num_blocks) {
+  if (num_blocks < 0) return -1;
+  return static_cast<int64_t>(kvca::move_cycle_scratch_bytes(num_blocks));
+}
+
+int kvca_move_cycle(const kvca_chunk_desc* tokens, const kvca_paged_desc* token_dst, int64_t token_row_bytes,
+                    const kvca_paged_desc* block_src, int64_t num_victims, const kvca_chunk_desc* spill,
+                    int64_t block_row_bytes, int64_t num_planes, const int64_t* d_offsets, int64_t num_steps,
+                    int64_t num_seqs, int64_t spill_rows, int32_t flags, void* d_scratch, int64_t* d_status,
+                    kvca_stream_t stream) {
+  if (!common_move_args_ok(num_planes, num_seqs, token_row_bytes) || block_row_bytes < 1 || num_seqs < 1 ||
+      num_steps < 1 || num_steps > kvca::kMoveCycleMaxSteps || spill_rows < 0 || num_victims < 0 ||
+      d_offsets == nullptr || d_scratch == nullptr || d_status == nullptr)
+    return KVCA_ERR_BAD_ARGUMENT;
+  int vec = 16;
+  vec = min_align(vec, static_cast<uint64_t>(token_row_bytes));
+  vec = min_align(vec, static_cast<uint64_t>(block_row_bytes));
+  if (!check_chunk(tokens, &vec) || !check_chunk(spill, &vec) ||
+      !check_paged(token_dst, num_planes, token_row_bytes, &vec) ||
+      !check_paged(block_src, num_planes, block_row_bytes, &vec) || vec != 16)
+    return KVCA_ERR_BAD_ARGUMENT;
+  if (token_dst->index == nullptr || (num_victims > 0 && block_src->index == nullptr) ||
+      block_src->block_size != 1 || token_dst->num_blocks != block_src->num_blocks ||
+      token_dst->block_stride != block_src->block_stride || block_row_bytes > block_src->block_stride ||
+      (token_dst->block_size - 1) * token_dst->row_stride + token_row_bytes > token_dst->block_stride)
+    return KVCA_ERR_BAD_ARGUMENT;
+  for (int64_t p = 0; p < num_planes; ++p)
+    if (token_dst->plane_ptrs[p] != block_src->plane_ptrs[p]) return KVCA_ERR_BAD_ARGUMENT;
+  // item numbers and per-item vector counts stay below 2^31
+  const int64_t s_group = kvca::move_cycle_group(token_row_bytes, num_planes);
+  const int64_t g_group = kvca::move_cycle_group(block_row_bytes, num_planes);
+  const int64_t items = num_steps * num_seqs * ((num_planes + s_group - 1) / s_group) *
+                            kvca::move_cycle_segments(token_row_bytes) +
+                        spill_rows * ((num_planes + g_group - 1) / g_group) * kvca::move_cycle_segments(block_row_bytes);
+  if (num_seqs > (int64_t{1} << 26) || spill_rows > (int64_t{1} << 26) || num_victims > (int64_t{1} << 40) ||
+      items >= (int64_t{1} << 31) ||
+      s_group * (token_row_bytes / 16) >= (int64_t{1} << 31) || g_group * (block_row_bytes / 16) >= (int64_t{1} << 31))
+    return KVCA_ERR_SIZE_LIMIT;
+  kvca::PagedSide cache;
+  kvca::ChunkSide src, dst;
+  to_side(token_dst, num_planes, &cache);
+  to_side(tokens, &src);
+  to_side(spill, &dst);
+  kvca::CycleArgs a{&cache, block_src->index, num_victims, d_offsets, &src, &dst, num_planes, num_steps,
+                    num_seqs, spill_rows, token_row_bytes, block_row_bytes, flags,
+                    static_cast<unsigned char*>(d_scratch), d_status};
+  return status_of(kvca::launch_move_cycle(a, stream));
+}
+
 int kvca_copy_paged(const kvca_paged_desc* src, const kvca_paged_desc* dst, int64_t num_planes,
                     int64_t num_rows, int64_t row_bytes, int32_t flags, int64_t* d_status,
                     kvca_stream_t stream) {

@@ -3626,6 +3626,410 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   }
 }
 
+namespace {
+
+// ---------------------------------------------------------------------------
+// The moves of a booked decode cycle in one launch
+// ---------------------------------------------------------------------------
+//
+// Step q of the cycle (q < num_steps <= 32) is the spill gather of its victims
+// (block rows of the cache to spill rows offsets[q] .. offsets[q + 1]) and
+// then the token scatter of its slot-mapping row (num_seqs token rows); the
+// result equals running the steps one after the other.  The work is cut into
+// warp items of at most kMoveCycleItemBytes (a victim's block rows of a few
+// planes, or a sequence's token rows of a few planes; rows longer than that
+// in pieces), numbered step by step with a step's gathers before its
+// scatters, and warps take item numbers from one counter: every SM streams
+// until the cycle's last item, with no launch, ramp or barrier between steps.
+// A warp moves an item through its own shared-memory buffer: each lane issues
+// 16-byte cp.async loads for its share of the item (all of them in flight at
+// once, no registers held), waits, and stores from the buffer.
+//
+// Items wait only where steps depend on each other.  Before the moves, every
+// CTA marks in two per-block words which steps evict the block (victims) and
+// which steps write a token row into it (slot mapping); one grid barrier
+// later those marks say, for each item, which earlier items it needs:
+//   - a token row whose block is a victim of this step or an earlier one
+//     waits until all gathers of that step are done (the spill reads the old
+//     bytes before the first token of the new owner lands);
+//   - a gather of a block that an earlier step's scatter wrote waits until
+//     all scatters of that step are done.
+// In a decode cycle that is the first token of every new block and, rarely, a
+// block released and evicted again within the cycle.  Each wait is for items
+// with smaller numbers, and item numbers are taken in order by resident CTAs
+// (cooperative launch), so the smallest number in flight never waits on
+// anything unfinished.  Token rows written twice in one call (the same slot at
+// two steps) end with either row: the slots of a decode cycle are distinct.
+//
+// The per-block words carry a launch generation in their high half, so words
+// of earlier launches read as empty and nothing has to clear them; the last
+// CTA to leave resets the counters and advances the generation.
+
+constexpr int kCycleWarps = 10;
+constexpr int kCycleThreads = kCycleWarps * 32;
+constexpr int kCycleMaxSteps = static_cast<int>(kMoveCycleMaxSteps);
+constexpr uint32_t kCycleBufVecs = static_cast<uint32_t>(kMoveCycleItemBytes / 16);
+constexpr size_t kCycleSmemBytes = static_cast<size_t>(kCycleWarps) * kMoveCycleItemBytes;
+
+struct CycleWords {
+  unsigned int bar_count;  // grid-barrier arrivals
+  int failed;              // a wait gave up
+  unsigned int ticket;     // next item number
+  unsigned int exits;      // CTAs that have left
+  unsigned int gen;        // launch generation of the per-block words
+  unsigned int pad[3];
+  unsigned int g_done[kCycleMaxSteps];  // finished gather items per step
+  unsigned int s_done[kCycleMaxSteps];  // finished scatter items per step
+};
+static_assert(sizeof(CycleWords) <= kCycleHeaderBytes, "cycle words exceed their header");
+
+// n / d for 0 <= n < 2^31 and 1 <= d < 2^31 by a multiply-high, an add and a
+// shift (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", 1994): with 2^s >= d > 2^(s-1) and
+// m = floor(2^32 (2^s - d) / d) + 1, n / d = (mulhi(n, m) + n) >> s.
+struct FastDiv {
+  uint32_t mul;
+  uint32_t shift;
+};
+
+FastDiv make_fast_div(uint32_t d) {
+  uint32_t s = 0;
+  while ((uint64_t{1} << s) < d) ++s;
+  const uint64_t m = ((uint64_t{1} << 32) * ((uint64_t{1} << s) - d)) / d + 1;
+  return FastDiv{static_cast<uint32_t>(m), s};
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) { return (__umulhi(n, f.mul) + n) >> f.shift; }
+
+// How one kind of row (token rows, block rows) is cut into items: `group`
+// planes of a unit (a sequence, a victim) per item, rows longer than an item
+// in `segs` pieces of kCycleBufVecs vectors (then group = 1).
+struct CycleKind {
+  uint32_t vecs;      // 16-byte vectors per row
+  FastDiv div;        // division by vecs
+  int group;
+  int segs;
+  unsigned per_unit;  // items per unit: ceil(planes / group) * segs
+};
+
+struct CycleParams {
+  uint64_t planes[KVCA_MAX_PLANES];  // the cache's planes (layer x K/V)
+  int64_t num_blocks;
+  int64_t block_stride;      // bytes between blocks of a plane
+  int64_t tokens_per_block;  // token rows of a block
+  int64_t token_stride;      // bytes between token rows of a block
+  const int64_t* slot_mapping;  // num_steps x num_seqs token slots
+  const int64_t* victims;       // offsets[num_steps] block ids
+  const int64_t* offsets;       // num_steps + 1: victims of step q
+  ChunkSide src;                // token rows: row q * num_seqs + s
+  ChunkSide spill;              // victim entry e's block rows: row e
+  int64_t num_seqs;
+  int64_t spill_rows;  // offsets[num_steps] may not pass this
+  int num_planes;
+  int num_steps;
+  CycleKind tok;
+  CycleKind blk;
+  int32_t flags;
+  CycleWords* words;
+  unsigned long long* wmask;  // per block: (generation << 32) | steps whose scatter writes it
+  unsigned long long* pmask;  // per block: (generation << 32) | steps that evict it
+  int64_t* status;
+};
+
+// ORs `bit` into a per-block word of generation `gen` (a word of another
+// generation counts as empty).  A word changes at most 33 times per
+// generation (its generation once, then one bit at a time), so the loop ends
+// within 34 tries.
+__device__ void cycle_mark(unsigned long long* word, unsigned gen, unsigned bit) {
+  unsigned long long old = __ldcg(word);
+  for (int tries = 0; tries < 40; ++tries) {
+    const unsigned long long want = static_cast<unsigned>(old >> 32) == gen
+                                        ? (old | bit)
+                                        : ((static_cast<unsigned long long>(gen) << 32) | bit);
+    if (want == old) return;
+    const unsigned long long seen = atomicCAS(word, old, want);
+    if (seen == old) return;
+    old = seen;
+  }
+}
+
+__device__ __forceinline__ unsigned cycle_bits(const unsigned long long* word, unsigned gen) {
+  const unsigned long long v = __ldcg(word);
+  return static_cast<unsigned>(v >> 32) == gen ? static_cast<unsigned>(v) : 0u;
+}
+
+// Waits until *counter reaches target (bounded; false when it gave up or the
+// grid failed).
+__device__ bool cycle_wait_count(const unsigned* counter, unsigned target, const int* failed) {
+  uint32_t spins = 0;
+  while (ld_acquire_u32(counter) < target) {
+    if (++spins > kGridSpinLimit || *reinterpret_cast<const volatile int*>(failed) != 0) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// Vectors [c0, c0 + nvec) of nrows rows.  The cache side of row r is
+// planes_s[pl0 + r] + tab_off, the other side aff + r * aff_stride (token
+// rows or spill rows).  kGather: cache -> spill, else token rows -> cache.
+// The loads go through L2 (cp.async.cg), so a gather sees the scatters of
+// this launch that it waited for.
+template <bool kGather>
+__device__ __forceinline__ void cycle_copy(uint4* buf, const uint64_t* planes_s, int pl0, int nrows,
+                                           int64_t tab_off, uint64_t aff, int64_t aff_stride, uint32_t vecs,
+                                           FastDiv div, uint32_t c0, uint32_t nvec, int lane) {
+  const uint32_t total = static_cast<uint32_t>(nrows) * nvec;  // <= kCycleBufVecs
+  const uint32_t sbuf = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
+  for (uint32_t e = static_cast<uint32_t>(lane); e < total; e += 32u) {
+    const uint32_t r = nrows == 1 ? 0u : fast_div(e, div);
+    const uint32_t c = c0 + e - r * vecs;
+    const uint64_t row = kGather ? planes_s[pl0 + r] + static_cast<uint64_t>(tab_off)
+                                 : aff + static_cast<uint64_t>(r) * static_cast<uint64_t>(aff_stride);
+    cp_async16(sbuf + e * 16u, row + static_cast<uint64_t>(c) * 16u);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  cp_async_wait<0>();
+  __syncwarp();
+  for (uint32_t e = static_cast<uint32_t>(lane); e < total; e += 32u) {
+    const uint32_t r = nrows == 1 ? 0u : fast_div(e, div);
+    const uint32_t c = c0 + e - r * vecs;
+    const uint64_t row = kGather ? aff + static_cast<uint64_t>(r) * static_cast<uint64_t>(aff_stride)
+                                 : planes_s[pl0 + r] + static_cast<uint64_t>(tab_off);
+    st_stream(reinterpret_cast<uint4*>(row) + c, buf[e]);
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void cycle_leave(CycleWords* w) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&w->exits, 1u) == gridDim.x - 1u) {
+      w->bar_count = 0u;
+      w->failed = 0;
+      w->ticket = 0u;
+      for (int q = 0; q < kCycleMaxSteps; ++q) {
+        w->g_done[q] = 0u;
+        w->s_done[q] = 0u;
+      }
+      w->gen = w->gen + 1u;
+      __threadfence();
+      w->exits = 0u;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kCycleThreads, 2) move_cycle_kernel(const __grid_constant__ CycleParams p) {
+  extern __shared__ __align__(128) uint4 cycle_buf[];
+  __shared__ uint64_t planes_s[KVCA_MAX_PLANES];
+  __shared__ int64_t offs_s[kCycleMaxSteps + 1];
+  __shared__ unsigned first_s[kCycleMaxSteps + 1];  // first item of step q; [num_steps] = all items
+  __shared__ unsigned gitems_s[kCycleMaxSteps];     // gather items of step q
+  __shared__ unsigned gen_s;
+  __shared__ int bad_s;
+  CycleWords* w = p.words;
+  const int tid = static_cast<int>(threadIdx.x);
+  const int S = p.num_steps;
+  const int P = p.num_planes;
+  const int64_t N = p.num_seqs;
+  for (int i = tid; i < P; i += blockDim.x) planes_s[i] = p.planes[i];
+  if (tid <= S) offs_s[tid] = p.offsets[tid];
+  if (tid == 0) gen_s = __ldcg(&w->gen);
+  __syncthreads();
+  const unsigned s_items = static_cast<unsigned>(N) * p.tok.per_unit;
+  if (tid == 0) {
+    int bad = offs_s[0] != 0 || offs_s[S] > p.spill_rows;
+    unsigned first = 0;
+    for (int q = 0; q < S; ++q) {
+      const int64_t nv = offs_s[q + 1] - offs_s[q];
+      if (nv < 0) bad = 1;
+      first_s[q] = first;
+      gitems_s[q] = bad ? 0u : static_cast<unsigned>(nv) * p.blk.per_unit;
+      first += gitems_s[q] + s_items;
+    }
+    first_s[S] = first;
+    bad_s = bad;
+    if (bad && blockIdx.x == 0) report(p.status, KVCA_ERR_BAD_ARGUMENT, offs_s[S]);
+  }
+  __syncthreads();
+  const unsigned gen = gen_s;
+  const bool skip_neg = (p.flags & KVCA_FLAG_SKIP_NEGATIVE) != 0;
+  if (!bad_s) {  // mark which steps evict and which write each block
+    const int64_t gthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid;
+    for (int64_t e = gt; e < S * N; e += gthreads) {
+      const int64_t slot = p.slot_mapping[e];
+      if (slot < 0) {
+        if (!skip_neg) report(p.status, KVCA_ERR_BAD_INDEX, slot);
+        continue;
+      }
+      const int64_t blk = slot / p.tokens_per_block;
+      if (blk >= p.num_blocks) {
+        report(p.status, KVCA_ERR_BAD_INDEX, slot);
+        continue;
+      }
+      cycle_mark(&p.wmask[blk], gen, 1u << static_cast<unsigned>(e / N));
+    }
+    for (int64_t e = gt; e < offs_s[S]; e += gthreads) {
+      const int64_t v = p.victims[e];
+      if (v < 0 || v >= p.num_blocks) {
+        if (v >= 0 || !skip_neg) report(p.status, KVCA_ERR_BAD_INDEX, v);
+        continue;
+      }
+      int q = 0;
+      while (offs_s[q + 1] <= e) ++q;
+      cycle_mark(&p.pmask[v], gen, 1u << q);
+    }
+  }
+  if (!grid_barrier_words(&w->bar_count, &w->failed, p.status)) {
+    cycle_leave(w);
+    return;
+  }
+  if (!bad_s) {
+    const int lane = tid & 31;
+    uint4* buf = cycle_buf + static_cast<size_t>(tid >> 5) * kCycleBufVecs;
+    const unsigned total = first_s[S];
+    unsigned t = 0;
+    if (lane == 0) t = atomicAdd(&w->ticket, 1u);
+    t = __shfl_sync(0xffffffffu, t, 0);
+    while (t < total) {
+      unsigned next = 0;
+      if (lane == 0) next = atomicAdd(&w->ticket, 1u);  // taken now, used after this item
+      int q = 0;
+      while (t >= first_s[q + 1]) ++q;
+      const unsigned local = t - first_s[q];
+      const bool gather = local < gitems_s[q];
+      const CycleKind& kind = gather ? p.blk : p.tok;
+      const unsigned lu = gather ? local : local - gitems_s[q];
+      const unsigned unit = lu / kind.per_unit;
+      const unsigned rem = lu - unit * kind.per_unit;
+      const unsigned grp = rem / static_cast<unsigned>(kind.segs);
+      const unsigned seg = rem - grp * static_cast<unsigned>(kind.segs);
+      const int pl0 = static_cast<int>(grp) * kind.group;
+      const int nrows = min(kind.group, P - pl0);
+      const uint32_t c0 = seg * kCycleBufVecs;
+      const uint32_t nvec = kind.segs > 1 ? min(kCycleBufVecs, kind.vecs - c0) : kind.vecs;
+      const int64_t row = gather ? offs_s[q] + unit : static_cast<int64_t>(q) * N + unit;
+      int64_t blk = -1, pos = 0;
+      unsigned dep = 0;
+      if (lane == 0) {
+        if (gather) {
+          const int64_t v = p.victims[row];
+          if (v >= 0 && v < p.num_blocks) {
+            blk = v;
+            dep = cycle_bits(&p.wmask[v], gen) & ((1u << q) - 1u);
+          }
+        } else {
+          const int64_t slot = p.slot_mapping[row];
+          if (slot >= 0 && slot / p.tokens_per_block < p.num_blocks) {
+            blk = slot / p.tokens_per_block;
+            pos = slot - blk * p.tokens_per_block;
+            dep = cycle_bits(&p.pmask[blk], gen) & ((2u << q) - 1u);
+          }
+        }
+      }
+      int ok = 1;
+      if (lane == 0) {
+        while (dep != 0u && ok) {
+          const int j = 31 - __clz(dep);  // latest step first
+          dep &= ~(1u << j);
+          ok = gather ? cycle_wait_count(&w->s_done[j], s_items, &w->failed)
+                      : cycle_wait_count(&w->g_done[j], gitems_s[j], &w->failed);
+        }
+        if (!ok && atomicExch(&w->failed, 1) == 0) report(p.status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      blk = __shfl_sync(0xffffffffu, blk, 0);
+      pos = __shfl_sync(0xffffffffu, pos, 0);
+      if (blk >= 0) {
+        if (gather) {
+          const uint64_t aff = p.spill.base + static_cast<uint64_t>(chunk_row_offset(p.spill, row)) +
+                               static_cast<uint64_t>(pl0) * p.spill.plane_stride;
+          cycle_copy<true>(buf, planes_s, pl0, nrows, blk * p.block_stride, aff, p.spill.plane_stride, kind.vecs,
+                           kind.div, c0, nvec, lane);
+        } else {
+          const uint64_t aff = p.src.base + static_cast<uint64_t>(chunk_row_offset(p.src, row)) +
+                               static_cast<uint64_t>(pl0) * p.src.plane_stride;
+          cycle_copy<false>(buf, planes_s, pl0, nrows, blk * p.block_stride + pos * p.token_stride, aff,
+                            p.src.plane_stride, kind.vecs, kind.div, c0, nvec, lane);
+        }
+      }
+      int stop = 0;
+      if (lane == 0) {
+        __threadfence();
+        atomicAdd(gather ? &w->g_done[q] : &w->s_done[q], 1u);
+        stop = *reinterpret_cast<const volatile int*>(&w->failed);
+      }
+      stop = __shfl_sync(0xffffffffu, stop, 0);
+      if (stop) break;
+      t = __shfl_sync(0xffffffffu, next, 0);
+    }
+  }
+  cycle_leave(w);
+}
+
+CycleKind make_cycle_kind(int64_t row_bytes, int64_t planes) {
+  CycleKind k;
+  k.vecs = static_cast<uint32_t>(row_bytes / 16);
+  k.div = make_fast_div(k.vecs);
+  k.group = static_cast<int>(move_cycle_group(row_bytes, planes));
+  k.segs = static_cast<int>(move_cycle_segments(row_bytes));
+  k.per_unit = static_cast<unsigned>(((planes + k.group - 1) / k.group) * k.segs);
+  return k;
+}
+
+}  // namespace
+
+size_t move_cycle_scratch_bytes(int64_t num_blocks) {
+  return kCycleHeaderBytes + 2 * static_cast<size_t>(num_blocks) * sizeof(unsigned long long);
+}
+
+cudaError_t launch_move_cycle(const CycleArgs& a, cudaStream_t stream) {
+  CycleParams p;
+  memset(&p, 0, sizeof(p));
+  for (int64_t i = 0; i < a.num_planes; ++i) p.planes[i] = a.cache->planes[i];
+  p.num_blocks = a.cache->num_blocks;
+  p.block_stride = a.cache->block_stride;
+  p.tokens_per_block = a.cache->block_size;
+  p.token_stride = a.cache->row_stride;
+  p.slot_mapping = a.cache->index;
+  p.victims = a.victims;
+  p.offsets = a.offsets;
+  p.src = *a.src;
+  p.spill = *a.spill;
+  p.num_seqs = a.num_seqs;
+  p.spill_rows = a.spill_rows < a.num_victims ? a.spill_rows : a.num_victims;
+  p.num_planes = static_cast<int>(a.num_planes);
+  p.num_steps = static_cast<int>(a.num_steps);
+  p.tok = make_cycle_kind(a.token_row_bytes, a.num_planes);
+  p.blk = make_cycle_kind(a.block_row_bytes, a.num_planes);
+  p.flags = a.flags;
+  p.words = reinterpret_cast<CycleWords*>(a.scratch);
+  p.wmask = reinterpret_cast<unsigned long long*>(a.scratch + kCycleHeaderBytes);
+  p.pmask = p.wmask + a.cache->num_blocks;
+  p.status = a.status;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(move_cycle_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kCycleSmemBytes));
+    if (e != cudaSuccess) return e;
+    int b = 0;
+    const cudaError_t e2 =
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, move_cycle_kernel, kCycleThreads, kCycleSmemBytes);
+    if (e2 != cudaSuccess) return e2;
+    if (b < 1) return cudaErrorInvalidConfiguration;
+    configured = true;
+  }
+  int sms = device_sm_count();
+  if (sms < 1) sms = 1;
+  void* args[] = {&p};
+  // one CTA per SM, leaving registers and shared memory beside it for a
+  // bookkeeping kernel on another stream
+  return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(move_cycle_kernel), dim3(static_cast<unsigned>(sms)),
+                                     dim3(kCycleThreads), args, kCycleSmemBytes, stream);
+}
+
 cudaError_t launch_exchange(const ExchangeArgs& a, cudaStream_t stream) {
   ExchangeParams p;
   memset(&p, 0, sizeof(p));

@@ -52,6 +52,49 @@ cudaError_t launch_move(const MoveArgs& args, cudaStream_t stream);
 // move 16-byte vectors in device memory (else two launches, scatter first).
 cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gather, cudaStream_t stream);
 
+// The moves of a booked decode cycle in one launch (kvca_move_cycle): per
+// step q, the gather of victims[offsets[q] .. offsets[q + 1]) to those spill
+// rows, then the scatter of token rows q * num_seqs + s through
+// cache->index (the num_steps x num_seqs slot mapping).  16-byte rows only.
+struct CycleArgs {
+  const PagedSide* cache;  // token view: block_size tokens per block, row_stride between tokens
+  const int64_t* victims;
+  int64_t num_victims;     // entries of victims
+  const int64_t* offsets;  // num_steps + 1, on the device
+  const ChunkSide* src;    // token rows
+  const ChunkSide* spill;  // one row per victim entry
+  int64_t num_planes;
+  int64_t num_steps;  // 1 .. kMoveCycleMaxSteps
+  int64_t num_seqs;
+  int64_t spill_rows;
+  int64_t token_row_bytes;
+  int64_t block_row_bytes;
+  int32_t flags;
+  unsigned char* scratch;  // move_cycle_scratch_bytes(cache->num_blocks), zeroed once
+  int64_t* status;
+};
+
+constexpr int64_t kMoveCycleMaxSteps = 32;
+constexpr size_t kCycleHeaderBytes = 512;
+// Bytes of one warp's share of work (an item, staged in the warp's buffer):
+// whole rows of at most this many bytes together, longer rows in pieces.
+constexpr int64_t kMoveCycleItemBytes = 16384;
+
+// Planes per item for rows of row_bytes.
+inline int64_t move_cycle_group(int64_t row_bytes, int64_t num_planes) {
+  int64_t g = kMoveCycleItemBytes / (row_bytes > 0 ? row_bytes : 1);
+  if (g < 1) g = 1;
+  return g < num_planes ? g : num_planes;
+}
+
+// Pieces per row (1 unless a row is longer than an item).
+inline int64_t move_cycle_segments(int64_t row_bytes) {
+  return row_bytes <= kMoveCycleItemBytes ? 1 : (row_bytes + kMoveCycleItemBytes - 1) / kMoveCycleItemBytes;
+}
+
+size_t move_cycle_scratch_bytes(int64_t num_blocks);
+cudaError_t launch_move_cycle(const CycleArgs& args, cudaStream_t stream);
+
 // Spill + fill of the same slots in one launch (one plane): row j sends slot
 // slots->index[j] to store row store->index[j] and fills it from store row
 // fill_from[j]; negative indices skip that part.  With *gate != 0 only the

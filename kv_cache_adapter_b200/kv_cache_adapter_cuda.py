@@ -51,6 +51,7 @@ __all__ = [
     "append_steps",
     "copy_tokens",
     "scatter_tokens_gather_layers",
+    "move_cycle",
     "exchange_blocks",
     "batched_fused_single_layer_kv_transfer",
     "load_device_store",
@@ -1200,6 +1201,75 @@ def scatter_tokens_gather_layers(token_caches, slot_mapping: torch.Tensor, chunk
             Q, k, bp.row_bytes, _lib.KVCA_FLAG_SKIP_NEGATIVE | ready, ready, _ptr(_status(dev)), _stream(dev))
     _host_rc(rc, "scatter_tokens_gather_layers")
     _maybe_check(dev, check, "scatter_tokens_gather_layers")
+
+
+_cycle_scratches: dict[tuple, torch.Tensor] = {}
+
+
+def _cycle_scratch(dev: torch.device, num_blocks: int) -> torch.Tensor:
+    """kvca_move_cycle's scratch for this (device, stream, cache size): zeroed
+    once, kept for reuse (the launches keep it consistent)."""
+    words = int(_lib_handle.kvca_move_cycle_scratch_bytes(num_blocks)) // 8
+    key = (_index(dev), _stream(dev).value or 0, words)
+    buf = _cycle_scratches.get(key)
+    if buf is None:
+        buf = torch.zeros(words, dtype=torch.int64, device=dev)
+        _cycle_scratches[key] = buf
+    return buf
+
+
+def move_cycle(token_caches, slot_mapping: torch.Tensor, token_rows: torch.Tensor, block_caches,
+               victims: torch.Tensor, offsets: torch.Tensor, spill: torch.Tensor, *, blocks_per_chunk: int = 1,
+               check: bool | None = None) -> None:
+    """The moves of a booked decode cycle in one launch (kvca_move_cycle).
+    For each step q of ``slot_mapping`` (``(num_steps, num_seqs)``, as
+    ``append_steps`` writes it), in order: the spill gather of
+    ``victims[offsets[q]:offsets[q + 1]]`` into rows ``offsets[q]`` .. of
+    ``spill`` (``gather_layers``' chunk layout, ``blocks_per_chunk`` rows per
+    chunk), then the scatter of step q's token rows (``token_rows`` in
+    ``scatter_tokens``' chunk layout with ``num_seqs`` tokens per chunk:
+    ``(num_steps, P, num_seqs, *row)``, or ``(1, P, num_seqs, *row)`` to
+    scatter the same rows every step) through ``slot_mapping[q]``.
+    ``offsets``: int64 on the device, ``num_steps + 1`` entries from 0.  Rows
+    wait for earlier steps only where they depend on them; slots must be
+    distinct across the call, negative slots and victims are skipped."""
+    tp = _planes(token_caches, 2, "token_caches")
+    bp = _planes(block_caches, 1, "block_caches")
+    dev = tp.device
+    if bp.device != dev:
+        raise ValueError("token_caches and block_caches must be on one device")
+    _require_index(slot_mapping, dev, "slot_mapping")
+    _require_index(victims, dev, "victims")
+    _require_index(offsets, dev, "offsets")
+    if slot_mapping.dim() != 2 or not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be a contiguous (num_steps, num_seqs) tensor")
+    steps, seqs = slot_mapping.shape
+    if offsets.numel() != steps + 1:
+        raise ValueError("offsets must have num_steps + 1 entries")
+    P = len(tp.planes)
+    if len(bp.planes) != P:
+        raise ValueError("token_caches and block_caches must have the same planes")
+    if token_rows.dim() < 1 or token_rows.shape[0] not in (1, steps):
+        raise ValueError("token_rows must be (num_steps or 1, P, num_seqs, *row)")
+    _chunk_tensor(token_rows, (token_rows.shape[0], P, seqs, *tp.row_shape), tp.dtype, dev, "token_rows")
+    cb = int(blocks_per_chunk)
+    if cb < 1 or spill.dim() < 3 or spill.shape[2] != cb:
+        raise ValueError("spill must be (chunks, P, blocks_per_chunk, *block_row)")
+    _chunk_tensor(spill, (spill.shape[0], P, cb, *bp.row_shape), bp.dtype, dev, "spill")
+    if steps == 0 or seqs == 0:
+        return
+    rb = tp.row_bytes
+    tokens = _lib.ChunkDesc(token_rows.data_ptr(), seqs, 0 if token_rows.shape[0] == 1 else P * seqs * rb, rb,
+                            seqs * rb)
+    with _on(dev):
+        rc = _lib_handle.kvca_move_cycle(
+            ctypes.byref(tokens), ctypes.byref(tp.desc(slot_mapping)), rb, ctypes.byref(bp.desc(victims)),
+            victims.numel(), ctypes.byref(_chunk_desc(spill, cb, P, bp.row_bytes)), bp.row_bytes, P, _ptr(offsets),
+            steps, seqs,
+            spill.shape[0] * cb, _lib.KVCA_FLAG_SKIP_NEGATIVE, _ptr(_cycle_scratch(dev, tp.num_blocks)),
+            _ptr(_status(dev)), _stream(dev))
+    _host_rc(rc, "move_cycle")
+    _maybe_check(dev, check, "move_cycle")
 
 
 def copy_tokens(src_caches, src_mapping: torch.Tensor, dst_caches, dst_mapping: torch.Tensor, *,

@@ -277,6 +277,9 @@ class DecodeMix:
         self._cycle_booked = self._cycle_moved = None
         self._pair = getattr(ops, "scatter_tokens_gather_layers", None)
         self._head_gathered = False  # the first gather of the next cycle to move went with the previous one
+        # a whole cycle's moves in one launch (move_cycle) when the op set has it
+        self._cycle_op = getattr(ops, "move_cycle", None)
+        self._one_launch = False
         self._schedules = {}  # fill positions (bytes) -> (need, offsets on the device, offsets on the host)
         self.victims_bufs = [torch.empty(seqs, dtype=torch.int64, device=device) for _ in range(2)]
         self.slot_mapping_bufs = [torch.empty(seqs, dtype=torch.int64, device=device) for _ in range(2)]
@@ -438,7 +441,8 @@ class DecodeMix:
 
     def _cycle_schedule(self, pos: np.ndarray):
         """Need lists of the block_size steps from fill positions `pos`, as
-        device tensors (cached: the schedule repeats every cycle)."""
+        device tensors (need ids, CSR offsets) and the offsets on the host
+        (cached: the schedule repeats every cycle)."""
         key = pos.tobytes()
         got = self._schedules.get(key)
         if got is None:
@@ -458,12 +462,18 @@ class DecodeMix:
             self._book_stream.wait_stream(torch.cuda.current_stream(self.device))
         return got
 
-    def start_cycles(self) -> None:
+    def start_cycles(self, one_launch: bool | None = None) -> None:
         """Switch to whole-cycle booking and book the next cycle.  Call at a
         step count that is a multiple of block_size, with the per-step
-        pipeline off."""
+        pipeline off.  ``one_launch`` (default: when the op set has
+        move_cycle): each cycle's moves are one move_cycle launch, whose
+        spill holds the whole cycle's victims (row offsets[q] + i: victim i
+        of step q); otherwise each step's scatter is paired with the next
+        step's gather, and the spill holds the last step's victims."""
         assert self._append_many is not None and self.device.type == "cuda" and not self._cycles_on
         assert not self._pipelined
+        self._one_launch = self._cycle_op is not None if one_launch is None else bool(one_launch)
+        assert not self._one_launch or self._cycle_op is not None
         assert (self.pos >= 1).all()  # past the first step: the fill positions repeat every cycle
         if self._book_stream is None:
             self._book_stream = torch.cuda.Stream(self.device)
@@ -489,19 +499,33 @@ class DecodeMix:
                               self.next_logical_dev, self.cycle_victims[h][: offs[-1]],
                               self.cycle_slot_mapping[h], check=False)
             self._cycle_booked[h].record(bs)
-        self._cycle_queue.append((h, offs))
+        self._cycle_queue.append((h, offs, offsets))
 
     def _move_cycle(self, token_rows: torch.Tensor) -> None:
-        """The moves of the oldest booked cycle.  With the pair op, step i's
-        token scatter and step i + 1's spill gather go in one launch: the pop
-        of step i + 1 precedes its release, so its victims were unpinned
-        while step i wrote, and step i writes only its sequences' current,
-        pinned blocks.  The last scatter of the cycle takes the first gather
-        of the next cycle when that one is booked already."""
-        h, offs = self._cycle_queue.pop(0)
+        """The moves of the oldest booked cycle.  ``token_rows``: one step's
+        rows ``(1, P, seqs, *row)`` for every step, or ``(block_size, P, seqs,
+        *row)`` with step i's rows at index i.  In one-launch mode the
+        cycle's gathers and scatters are one move_cycle launch.  Otherwise,
+        with the pair op, step i's token scatter and step i + 1's spill
+        gather go in one launch: the pop of step i + 1 precedes its release,
+        so its victims were unpinned while step i wrote, and step i writes
+        only its sequences' current, pinned blocks.  The last scatter of the
+        cycle takes the first gather of the next cycle when that one is
+        booked already."""
+        h, offs, offsets = self._cycle_queue.pop(0)
         cur = torch.cuda.current_stream(self.device)
         cur.wait_event(self._cycle_booked[h])
         victims, slot_mapping = self.cycle_victims[h], self.cycle_slot_mapping[h]
+        per_step = token_rows.shape[0] > 1
+        assert token_rows.shape[0] in (1, self.block_size)
+        if self._one_launch:
+            self._cycle_op(self.token_table, slot_mapping, token_rows, self.block_table, victims[: offs[-1]],
+                           offsets, self.spill[: offs[-1]], check=False)
+            self._cycle_moved[h].record(cur)
+            self.evictions += offs[-1]
+            self.gathered_blocks += offs[-1]
+            self.tokens += self.block_size * self.seqs
+            return
         pair = self._pair
         if pair is None or not self._head_gathered:
             a, b = offs[0], offs[1]
@@ -515,13 +539,14 @@ class DecodeMix:
                     a, b = offs[step], offs[step + 1]
                     self.ops.gather_layers(self.block_table, victims[a:b], self.spill[: b - a],
                                            blocks_per_chunk=1, check=False)
-                self.ops.scatter_tokens(self.token_table, slot_mapping[step], token_rows,
+                self.ops.scatter_tokens(self.token_table, slot_mapping[step],
+                                        token_rows[step:step + 1] if per_step else token_rows,
                                         tokens_per_chunk=self.seqs, check=False)
                 continue
             if step + 1 < self.block_size:  # with the next step's gather
                 nv = victims[offs[step + 1]:offs[step + 2]]
             elif self._cycle_queue:  # with the next cycle's first gather
-                nh, noffs = self._cycle_queue[0]
+                nh, noffs, _ = self._cycle_queue[0]
                 cur.wait_event(self._cycle_booked[nh])
                 nv = self.cycle_victims[nh][noffs[0]:noffs[1]]
                 self._head_gathered = True
@@ -531,7 +556,8 @@ class DecodeMix:
             # the token rows from before the cycle, and after the first pair of
             # the cycle the kernels before a pair are pairs, which write none of
             # them; the first one waits for whatever the caller ran before
-            pair(self.token_table, slot_mapping[step], token_rows, self.block_table, nv,
+            pair(self.token_table, slot_mapping[step], token_rows[step:step + 1] if per_step else token_rows,
+                 self.block_table, nv,
                  self.spill[: nv.numel()], tokens_per_chunk=self.seqs, blocks_per_chunk=1,
                  inputs_ready=step > 0, check=False)
         self._cycle_moved[h].record(cur)

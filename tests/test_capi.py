@@ -100,3 +100,40 @@ def test_decode_loop_entry_points_check_arguments_on_the_host():
                                    null) == bad  # null plane tables
     assert lib.kvca_scatter_gather(*args, 1, 0, 16, ctypes.byref(pdesc), ctypes.byref(c), 1, 0, 16, 0, 0, null,
                                    null) == 0  # nothing to move
+
+
+def test_move_cycle_checks_arguments_on_the_host():
+    lib = _lib.load()
+    assert lib.kvca_move_cycle_scratch_bytes(0) == 512
+    assert lib.kvca_move_cycle_scratch_bytes(65536) == 512 + 16 * 65536
+    assert lib.kvca_move_cycle_scratch_bytes(-1) == -1
+    bad = _lib.KVCA_ERR_BAD_ARGUMENT
+    one = ctypes.c_void_p(4096)  # never dereferenced: every call below is refused first
+    planes = (ctypes.c_uint64 * 2)(1 << 20, 1 << 21)
+    others = (ctypes.c_uint64 * 2)(1 << 20, 1 << 22)
+    ptr = ctypes.cast(planes, ctypes.POINTER(ctypes.c_uint64))
+
+    def paged(table=ptr, block_size=16, row_stride=256, index=one):
+        return _lib.PagedDesc(table, 64, block_size, 4096, row_stride, index)
+
+    tokens = _lib.ChunkDesc(1 << 23, 8, 0, 256, 8 * 256)
+    spill = _lib.ChunkDesc(1 << 24, 1, 2 * 4096, 4096, 4096)
+
+    def call(tok=None, blk=None, row=256, block_row=4096, steps=4, seqs=8, offsets=one, scratch=one):
+        return lib.kvca_move_cycle(ctypes.byref(tokens), ctypes.byref(tok or paged()), row,
+                                   ctypes.byref(blk or paged(block_size=1, row_stride=4096)), 16,
+                                   ctypes.byref(spill), block_row, 2, offsets, steps, seqs, 16, 1, scratch, one,
+                                   None)
+
+    assert call(steps=0) == bad
+    assert call(steps=33) == bad
+    assert call(offsets=None) == bad
+    assert call(scratch=None) == bad
+    assert call(row=264) == bad  # rows of 16-byte vectors only
+    assert call(blk=paged(block_size=16, row_stride=4096)) == bad  # block side must be block-granular
+    assert call(blk=paged(table=ctypes.cast(others, ctypes.POINTER(ctypes.c_uint64)), block_size=1,
+                          row_stride=4096)) == bad  # another cache
+    assert call(tok=paged(index=None)) == bad  # no slot mapping
+    assert call(block_row=8192) == bad  # a block row past its block
+    assert call(tok=paged(row_stride=512)) == bad  # token rows past their block
+    assert call(seqs=1 << 27) == _lib.KVCA_ERR_SIZE_LIMIT

@@ -161,11 +161,15 @@ def _assert_same_state(a: DecodeMix, b: DecodeMix):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("one_launch", [False, True])
 @pytest.mark.parametrize("cfg", [SMALL, WIDE, HUGE])
-def test_cycle_booking_matches_single_steps(cfg):
+def test_cycle_booking_matches_single_steps(cfg, one_launch):
     """Whole-cycle booking (one append_steps launch per cycle, one cycle ahead
     of the moves), eager and replayed from a graph, leaves the same cache
-    bytes and metadata as the same number of single unpipelined steps."""
+    bytes and metadata as the same number of single unpipelined steps; the
+    moves of a cycle are paired launches or one move_cycle launch, whose
+    spill then holds every victim of the cycle (checked against the single
+    steps' spills)."""
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda as cuda_ops
 
     dev = torch.device("cuda", 0)
@@ -176,15 +180,21 @@ def test_cycle_booking_matches_single_steps(cfg):
     for _ in range(bs + 1):  # past the first step: positions periodic
         ref.step(rows)
         cyc.step(rows)
-    cyc.start_cycles()
+    cyc.start_cycles(one_launch=one_launch)
     cyc.run_cycle(rows)
     cyc.run_cycle(rows)
     cyc.stop_cycles(rows)
-    for _ in range(3 * bs):
-        ref.step(rows)
+    spills = []
+    for i in range(3 * bs):
+        spill = ref.step(rows)
+        if i >= 2 * bs:  # the last cycle's victims, step by step
+            spills.append(spill.clone())
     _assert_same_state(ref, cyc)
+    if one_launch:
+        last = torch.cat(spills)
+        assert torch.equal(cyc.spill[: last.shape[0]].view(torch.uint8), last.view(torch.uint8))
     # graph replays of two cycles each, then single steps again
-    cyc.start_cycles()
+    cyc.start_cycles(one_launch=one_launch)
     cyc.run_cycle(rows)
     graph, per_replay = cyc.capture_cycles(rows)
     assert per_replay == 2 * cfg["seqs"]

@@ -138,10 +138,12 @@ def test_mla_layer_range_full_gather_scatter(ops, dtype):
     assert int(flat_b[:, untouched].count_nonzero()) == 0
 
 
-def test_decode_mix_eight_heads_cycles_match_oracle(ops):
+@pytest.mark.parametrize("one_launch", [False, True])
+def test_decode_mix_eight_heads_cycles_match_oracle(ops, one_launch):
     """32 layers x K/V, 8 KV heads, head_dim 128, fp16, 256 sequences: 17 eager
-    steps, then whole-cycle bookings with paired moves (three cycles), against
-    the oracle composition on CPU (a 1,024-block pool, 4.3 GB)."""
+    steps, then whole-cycle bookings with paired moves or one move_cycle launch
+    per cycle (three cycles, a new token rows tensor per step), against the
+    oracle composition on CPU (a 1,024-block pool, 4.3 GB)."""
     from oracle_ops import OracleOps
     from kv_cache_adapter_b200.workloads import DecodeMix
 
@@ -157,12 +159,19 @@ def test_decode_mix_eight_heads_cycles_match_oracle(ops):
         spill_g = gpu.step(rows_d, check=True)
         spill_c = cpu.step(rows)
         assert torch.equal(spill_g.cpu().view(torch.int16), spill_c.view(torch.int16)), step
-    gpu.start_cycles()
-    gpu.run_cycle(rows_d)
-    gpu.run_cycle(rows_d)
-    gpu.stop_cycles(rows_d)
-    for _ in range(48):  # the three booked cycles
-        cpu.step(rows)
+    cycle_rows = [torch.randn((16, gpu.num_planes, gpu.seqs, *gpu.row_shape), generator=gen).to(torch.float16)
+                  for _ in range(3)]
+    gpu.start_cycles(one_launch=one_launch)
+    gpu.run_cycle(cycle_rows[0].to(DEV))
+    gpu.run_cycle(cycle_rows[1].to(DEV))
+    gpu.stop_cycles(cycle_rows[2].to(DEV))
+    spills = []
+    for c in range(3):  # the three booked cycles
+        for i in range(16):
+            spills.append(cpu.step(cycle_rows[c][i:i + 1]).clone())
+    if one_launch:  # the last cycle's victims, in step order
+        last = torch.cat(spills[32:])
+        assert torch.equal(gpu.spill[: last.shape[0]].cpu().view(torch.int16), last.view(torch.int16))
     torch.cuda.synchronize(DEV)
     ops.check_status(DEV)
     assert gpu.tokens == cpu.tokens and gpu.evictions == cpu.evictions > 0
