@@ -3665,11 +3665,20 @@ namespace {
 // of earlier launches read as empty and nothing has to clear them; the last
 // CTA to leave resets the counters and advances the generation.
 
-constexpr int kCycleWarps = 10;
+#ifndef KVCA_CYCLE_WARPS
+#define KVCA_CYCLE_WARPS 10
+#endif
+constexpr int kCycleWarps = KVCA_CYCLE_WARPS;
 constexpr int kCycleThreads = kCycleWarps * 32;
 constexpr int kCycleMaxSteps = static_cast<int>(kMoveCycleMaxSteps);
-constexpr uint32_t kCycleBufVecs = static_cast<uint32_t>(kMoveCycleItemBytes / 16);
-constexpr size_t kCycleSmemBytes = static_cast<size_t>(kCycleWarps) * kMoveCycleItemBytes;
+constexpr uint32_t kCycleItemVecs = static_cast<uint32_t>(kMoveCycleItemBytes / 16);
+// Rows of at least this many bytes move as bulk copies (one lane issues a
+// copy per row into the item's buffer, and one per row out of it); shorter
+// rows move as 16-byte cp.async loads and stores by all lanes.
+constexpr int64_t kCycleBulkMinRowBytes = 1024;
+constexpr unsigned kCycleItemsPerTicket = 8;
+// two items per warp: one landing while the other is stored
+constexpr size_t kCycleSmemBytes = static_cast<size_t>(kCycleWarps) * 2 * kMoveCycleItemBytes;
 
 struct CycleWords {
   unsigned int bar_count;  // grid-barrier arrivals
@@ -3703,13 +3712,14 @@ __device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) { return (__
 
 // How one kind of row (token rows, block rows) is cut into items: `group`
 // planes of a unit (a sequence, a victim) per item, rows longer than an item
-// in `segs` pieces of kCycleBufVecs vectors (then group = 1).
+// in `segs` pieces of kCycleItemVecs vectors (then group = 1).
 struct CycleKind {
   uint32_t vecs;      // 16-byte vectors per row
   FastDiv div;        // division by vecs
   int group;
   int segs;
   unsigned per_unit;  // items per unit: ceil(planes / group) * segs
+  bool bulk;          // rows of kCycleBulkMinRowBytes or more: one bulk copy per row and item
 };
 
 struct CycleParams {
@@ -3769,35 +3779,199 @@ __device__ bool cycle_wait_count(const unsigned* counter, unsigned target, const
   return true;
 }
 
-// Vectors [c0, c0 + nvec) of nrows rows.  The cache side of row r is
-// planes_s[pl0 + r] + tab_off, the other side aff + r * aff_stride (token
-// rows or spill rows).  kGather: cache -> spill, else token rows -> cache.
-// The loads go through L2 (cp.async.cg), so a gather sees the scatters of
-// this launch that it waited for.
-template <bool kGather>
-__device__ __forceinline__ void cycle_copy(uint4* buf, const uint64_t* planes_s, int pl0, int nrows,
-                                           int64_t tab_off, uint64_t aff, int64_t aff_stride, uint32_t vecs,
-                                           FastDiv div, uint32_t c0, uint32_t nvec, int lane) {
-  const uint32_t total = static_cast<uint32_t>(nrows) * nvec;  // <= kCycleBufVecs
-  const uint32_t sbuf = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
-  for (uint32_t e = static_cast<uint32_t>(lane); e < total; e += 32u) {
-    const uint32_t r = nrows == 1 ? 0u : fast_div(e, div);
-    const uint32_t c = c0 + e - r * vecs;
-    const uint64_t row = kGather ? planes_s[pl0 + r] + static_cast<uint64_t>(tab_off)
-                                 : aff + static_cast<uint64_t>(r) * static_cast<uint64_t>(aff_stride);
-    cp_async16(sbuf + e * 16u, row + static_cast<uint64_t>(c) * 16u);
+// One warp item, decoded (the same on every lane of the warp).
+struct CycleItem {
+  int64_t row;      // victim entry (gather: its spill row) or token row q * num_seqs + s (scatter)
+  int64_t tab_off;  // cache side of the item's rows: block * block_stride (+ position * token_stride)
+  uint64_t aff;     // spill or token side of the item's first row
+  int64_t aff_stride;
+  uint32_t vecs;    // vectors per row of this kind
+  FastDiv div;
+  uint32_t c0;      // first vector of each row
+  uint32_t nvec;    // vectors per row in this item
+  int pl0;
+  int nrows;
+  int q;
+  bool gather;
+  bool bulk;        // moved by bulk copies (see CycleKind)
+  bool live;        // the item's block id is inside the cache
+  bool fence;       // scatter: a later step gathers the block, so its rows must be visible before the signal
+  unsigned dep;     // steps whose counters this item waits for
+  int64_t blk;      // block id (-1: outside the cache)
+  int64_t pos;      // scatter: token position in the block
+};
+
+// Decodes item `t` of step layout first_s / gitems_s; lane 0 reads the item's
+// block id and that block's marks, and every lane gets them by shuffle.  An
+// item of the same sequence or victim as `prev` (the warp's previous item:
+// consecutive items mostly are) takes them from `prev` instead, which saves
+// two dependent reads.
+__device__ __forceinline__ CycleItem cycle_decode(const CycleParams& p, unsigned t, const unsigned* first_s,
+                                                  const unsigned* gitems_s, const int64_t* offs_s, unsigned gen,
+                                                  const CycleItem* prev, int lane) {
+  CycleItem it;
+  int q = 0;
+  while (t >= first_s[q + 1]) ++q;
+  const unsigned local = t - first_s[q];
+  it.q = q;
+  it.gather = local < gitems_s[q];
+  const CycleKind& kind = it.gather ? p.blk : p.tok;
+  const unsigned lu = it.gather ? local : local - gitems_s[q];
+  const unsigned unit = lu / kind.per_unit;
+  const unsigned rem = lu - unit * kind.per_unit;
+  const unsigned grp = rem / static_cast<unsigned>(kind.segs);
+  const unsigned seg = rem - grp * static_cast<unsigned>(kind.segs);
+  it.pl0 = static_cast<int>(grp) * kind.group;
+  it.nrows = min(kind.group, p.num_planes - it.pl0);
+  it.vecs = kind.vecs;
+  it.div = kind.div;
+  it.bulk = kind.bulk;
+  it.c0 = seg * kCycleItemVecs;
+  it.nvec = kind.segs > 1 ? min(kCycleItemVecs, kind.vecs - it.c0) : kind.vecs;
+  it.row = it.gather ? offs_s[q] + unit : static_cast<int64_t>(q) * p.num_seqs + unit;
+  int64_t blk = -1, pos = 0;
+  unsigned dep = 0, fence = 0;
+  if (prev != nullptr && prev->gather == it.gather && prev->row == it.row) {
+    blk = prev->live ? prev->blk : -1;
+    pos = prev->pos;
+    dep = prev->dep;
+    fence = prev->fence ? 1u : 0u;
+  } else if (lane == 0) {
+    if (it.gather) {
+      const int64_t v = p.victims[it.row];
+      if (v >= 0 && v < p.num_blocks) {
+        blk = v;
+        dep = cycle_bits(&p.wmask[v], gen) & ((1u << q) - 1u);
+      }
+    } else {
+      const int64_t slot = p.slot_mapping[it.row];
+      if (slot >= 0 && slot / p.tokens_per_block < p.num_blocks) {
+        blk = slot / p.tokens_per_block;
+        pos = slot - blk * p.tokens_per_block;
+        const unsigned bits = cycle_bits(&p.pmask[blk], gen);
+        dep = bits & ((2u << q) - 1u);
+        fence = q < 31 ? bits >> (q + 1) : 0u;
+      }
+    }
+  }
+  blk = __shfl_sync(0xffffffffu, blk, 0);
+  pos = __shfl_sync(0xffffffffu, pos, 0);
+  it.dep = __shfl_sync(0xffffffffu, dep, 0);
+  it.fence = __shfl_sync(0xffffffffu, fence, 0) != 0u;
+  it.live = blk >= 0;
+  it.blk = blk;
+  it.pos = pos;
+  if (it.gather) {
+    it.tab_off = blk * p.block_stride;
+    it.aff = p.spill.base + static_cast<uint64_t>(chunk_row_offset(p.spill, it.row)) +
+             static_cast<uint64_t>(it.pl0) * p.spill.plane_stride;
+    it.aff_stride = p.spill.plane_stride;
+  } else {
+    it.tab_off = blk * p.block_stride + pos * p.token_stride;
+    it.aff = p.src.base + static_cast<uint64_t>(chunk_row_offset(p.src, it.row)) +
+             static_cast<uint64_t>(it.pl0) * p.src.plane_stride;
+    it.aff_stride = p.src.plane_stride;
+  }
+  return it;
+}
+
+// Row r of an item: its cache side and its spill / token side.
+__device__ __forceinline__ uint64_t cycle_cache_row(const CycleItem& it, const uint64_t* planes_s, uint32_t r) {
+  return planes_s[it.pl0 + static_cast<int>(r)] + static_cast<uint64_t>(it.tab_off);
+}
+__device__ __forceinline__ uint64_t cycle_other_row(const CycleItem& it, uint32_t r) {
+  return it.aff + static_cast<uint64_t>(r) * static_cast<uint64_t>(it.aff_stride);
+}
+
+// Loads the item into `buf`.  Bulk items: lane 0 waits until the bulk
+// stores that last read this buffer are done reading it (`reads_left` of its
+// newer store groups may still be reading), arms the buffer's mbarrier with
+// the item's bytes and issues one bulk copy per row.  Other items: every lane
+// issues 16-byte cp.async loads for its vectors (through L2, so a gather sees
+// the scatters it waited for).  Every lane then commits a cp.async group
+// (empty for bulk items and for an item whose block is outside the cache),
+// so that waiting for "all but the newest group" means the same either way.
+__device__ __forceinline__ void cycle_issue(const CycleItem& it, const uint64_t* planes_s, uint4* buf,
+                                            uint64_t* bar, int reads_left, int lane) {
+  if (it.live && it.bulk) {
+    if (lane == 0) {
+      bulk_wait_read(reads_left);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      const uint32_t row_bytes = it.nvec * 16u;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                   "r"(row_bytes * static_cast<uint32_t>(it.nrows))
+                   : "memory");
+      for (int r = 0; r < it.nrows; ++r) {
+        const uint64_t row = it.gather ? cycle_cache_row(it, planes_s, r) : cycle_other_row(it, r);
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(buf) + static_cast<uint32_t>(r) * row_bytes),
+            "l"(row + static_cast<uint64_t>(it.c0) * 16u), "r"(row_bytes), "r"(smem_u32(bar))
+            : "memory");
+      }
+    }
+  } else if (it.live) {
+    if (lane == 0) bulk_wait_read(reads_left);
+    __syncwarp();
+    const uint32_t total = static_cast<uint32_t>(it.nrows) * it.nvec;  // <= kCycleItemVecs
+    const uint32_t sbuf = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
+    for (uint32_t e = static_cast<uint32_t>(lane); e < total; e += 32u) {
+      const uint32_t r = it.nrows == 1 ? 0u : fast_div(e, it.div);
+      const uint32_t c = it.c0 + e - r * it.vecs;
+      const uint64_t row = it.gather ? cycle_cache_row(it, planes_s, r) : cycle_other_row(it, r);
+      cp_async16(sbuf + e * 16u, row + static_cast<uint64_t>(c) * 16u);
+    }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
-  cp_async_wait<0>();
-  __syncwarp();
+}
+
+// Stores the item's vectors from `buf` (its loads have landed): bulk items
+// by lane 0, one bulk copy per row committed as one bulk group; the others by
+// every lane.
+__device__ __forceinline__ void cycle_store(const CycleItem& it, const uint64_t* planes_s, const uint4* buf,
+                                            int lane) {
+  if (!it.live) return;
+  if (it.bulk) {
+    if (lane == 0) {
+      const uint32_t row_bytes = it.nvec * 16u;
+      for (int r = 0; r < it.nrows; ++r) {
+        const uint64_t row = it.gather ? cycle_other_row(it, r) : cycle_cache_row(it, planes_s, r);
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                         row + static_cast<uint64_t>(it.c0) * 16u),
+                     "r"(smem_u32(buf) + static_cast<uint32_t>(r) * row_bytes), "r"(row_bytes)
+                     : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    return;
+  }
+  const uint32_t total = static_cast<uint32_t>(it.nrows) * it.nvec;
   for (uint32_t e = static_cast<uint32_t>(lane); e < total; e += 32u) {
-    const uint32_t r = nrows == 1 ? 0u : fast_div(e, div);
-    const uint32_t c = c0 + e - r * vecs;
-    const uint64_t row = kGather ? aff + static_cast<uint64_t>(r) * static_cast<uint64_t>(aff_stride)
-                                 : planes_s[pl0 + r] + static_cast<uint64_t>(tab_off);
+    const uint32_t r = it.nrows == 1 ? 0u : fast_div(e, it.div);
+    const uint32_t c = it.c0 + e - r * it.vecs;
+    const uint64_t row = it.gather ? cycle_other_row(it, r) : cycle_cache_row(it, planes_s, r);
     st_stream(reinterpret_cast<uint4*>(row) + c, buf[e]);
   }
-  __syncwarp();
+}
+
+// Lane 0 waits for the step counters an item depends on; false (grid marked
+// failed, timeout reported) when a wait gave up.  Uniform across the warp.
+__device__ __forceinline__ bool cycle_wait_deps(const CycleItem& it, CycleWords* w, unsigned s_items,
+                                                const unsigned* gitems_s, int64_t* status, int lane) {
+  int ok = 1;
+  if (lane == 0 && it.dep != 0u) {
+    unsigned dep = it.dep;
+    while (dep != 0u && ok) {
+      const int j = 31 - __clz(dep);  // latest step first
+      dep &= ~(1u << j);
+      ok = it.gather ? cycle_wait_count(&w->s_done[j], s_items, &w->failed)
+                     : cycle_wait_count(&w->g_done[j], gitems_s[j], &w->failed);
+    }
+    if (!ok && atomicExch(&w->failed, 1) == 0) report(status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
+    // the rows it waited for may have been written by bulk copies
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
 __device__ __forceinline__ void cycle_leave(CycleWords* w) {
@@ -3819,6 +3993,30 @@ __device__ __forceinline__ void cycle_leave(CycleWords* w) {
   }
 }
 
+// Item numbers a warp works through: kCycleItemsPerTicket consecutive items
+// per ticket, the next ticket taken one ticket ahead.
+struct CycleTickets {
+  unsigned item;
+  unsigned end;
+  unsigned next_ticket;  // lane 0's prefetched ticket
+};
+
+__device__ __forceinline__ unsigned cycle_next_item(CycleTickets& tk, CycleWords* w, unsigned total, int lane) {
+  if (tk.item < tk.end) return tk.item++;
+  const unsigned t = __shfl_sync(0xffffffffu, tk.next_ticket, 0);
+  int stop = 0;
+  if (lane == 0) {
+    tk.next_ticket = atomicAdd(&w->ticket, 1u);
+    stop = *reinterpret_cast<const volatile int*>(&w->failed);
+  }
+  if (__shfl_sync(0xffffffffu, stop, 0) != 0) return total;
+  const unsigned first = t * kCycleItemsPerTicket;
+  if (first >= total) return total;
+  tk.item = first + 1u;
+  tk.end = min(first + kCycleItemsPerTicket, total);
+  return first;
+}
+
 __global__ void __launch_bounds__(kCycleThreads, 2) move_cycle_kernel(const __grid_constant__ CycleParams p) {
   extern __shared__ __align__(128) uint4 cycle_buf[];
   __shared__ uint64_t planes_s[KVCA_MAX_PLANES];
@@ -3827,6 +4025,7 @@ __global__ void __launch_bounds__(kCycleThreads, 2) move_cycle_kernel(const __gr
   __shared__ unsigned gitems_s[kCycleMaxSteps];     // gather items of step q
   __shared__ unsigned gen_s;
   __shared__ int bad_s;
+  __shared__ __align__(8) uint64_t cycle_bars[2 * kCycleWarps];  // one mbarrier per buffer half
   CycleWords* w = p.words;
   const int tid = static_cast<int>(threadIdx.x);
   const int S = p.num_steps;
@@ -3835,6 +4034,8 @@ __global__ void __launch_bounds__(kCycleThreads, 2) move_cycle_kernel(const __gr
   for (int i = tid; i < P; i += blockDim.x) planes_s[i] = p.planes[i];
   if (tid <= S) offs_s[tid] = p.offsets[tid];
   if (tid == 0) gen_s = __ldcg(&w->gen);
+  if (tid < 2 * kCycleWarps) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&cycle_bars[tid])));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   __syncthreads();
   const unsigned s_items = static_cast<unsigned>(N) * p.tok.per_unit;
   if (tid == 0) {
@@ -3886,85 +4087,96 @@ __global__ void __launch_bounds__(kCycleThreads, 2) move_cycle_kernel(const __gr
     return;
   }
   if (!bad_s) {
+    // Two items in flight per warp, one in each half of the warp's buffer:
+    // the next item's loads are issued before the current item is stored
+    // when the next item waits for nothing.  An item is signalled before the
+    // warp waits for anything else, so the smallest unsignalled item number
+    // never waits for an unsignalled one.
     const int lane = tid & 31;
-    uint4* buf = cycle_buf + static_cast<size_t>(tid >> 5) * kCycleBufVecs;
+    const int warp = tid >> 5;
+    uint4* bufs = cycle_buf + static_cast<size_t>(warp) * 2 * kCycleItemVecs;
+    uint64_t* bars = cycle_bars + 2 * warp;
+    uint32_t parity = 0u;  // bit h: phase of half h's mbarrier to wait for next
+    uint32_t armed = 0u;   // bit h: bulk loads issued into half h and not yet waited for
     const unsigned total = first_s[S];
-    unsigned t = 0;
-    if (lane == 0) t = atomicAdd(&w->ticket, 1u);
-    t = __shfl_sync(0xffffffffu, t, 0);
-    while (t < total) {
-      unsigned next = 0;
-      if (lane == 0) next = atomicAdd(&w->ticket, 1u);  // taken now, used after this item
-      int q = 0;
-      while (t >= first_s[q + 1]) ++q;
-      const unsigned local = t - first_s[q];
-      const bool gather = local < gitems_s[q];
-      const CycleKind& kind = gather ? p.blk : p.tok;
-      const unsigned lu = gather ? local : local - gitems_s[q];
-      const unsigned unit = lu / kind.per_unit;
-      const unsigned rem = lu - unit * kind.per_unit;
-      const unsigned grp = rem / static_cast<unsigned>(kind.segs);
-      const unsigned seg = rem - grp * static_cast<unsigned>(kind.segs);
-      const int pl0 = static_cast<int>(grp) * kind.group;
-      const int nrows = min(kind.group, P - pl0);
-      const uint32_t c0 = seg * kCycleBufVecs;
-      const uint32_t nvec = kind.segs > 1 ? min(kCycleBufVecs, kind.vecs - c0) : kind.vecs;
-      const int64_t row = gather ? offs_s[q] + unit : static_cast<int64_t>(q) * N + unit;
-      int64_t blk = -1, pos = 0;
-      unsigned dep = 0;
-      if (lane == 0) {
-        if (gather) {
-          const int64_t v = p.victims[row];
-          if (v >= 0 && v < p.num_blocks) {
-            blk = v;
-            dep = cycle_bits(&p.wmask[v], gen) & ((1u << q) - 1u);
-          }
-        } else {
-          const int64_t slot = p.slot_mapping[row];
-          if (slot >= 0 && slot / p.tokens_per_block < p.num_blocks) {
-            blk = slot / p.tokens_per_block;
-            pos = slot - blk * p.tokens_per_block;
-            dep = cycle_bits(&p.pmask[blk], gen) & ((2u << q) - 1u);
-          }
-        }
+    CycleTickets tk;
+    tk.item = tk.end = 0u;
+    tk.next_ticket = lane == 0 ? atomicAdd(&w->ticket, 1u) : 0u;
+    unsigned i0 = cycle_next_item(tk, w, total, lane);
+    CycleItem cur;
+    bool have = false;
+    int half = 0;
+    if (i0 < total) {
+      cur = cycle_decode(p, i0, first_s, gitems_s, offs_s, gen, nullptr, lane);
+      have = cycle_wait_deps(cur, w, s_items, gitems_s, p.status, lane);
+      if (have) {
+        cycle_issue(cur, planes_s, bufs, &bars[0], 0, lane);
+        if (cur.live && cur.bulk) armed |= 1u;
       }
-      int ok = 1;
-      if (lane == 0) {
-        while (dep != 0u && ok) {
-          const int j = 31 - __clz(dep);  // latest step first
-          dep &= ~(1u << j);
-          ok = gather ? cycle_wait_count(&w->s_done[j], s_items, &w->failed)
-                      : cycle_wait_count(&w->g_done[j], gitems_s[j], &w->failed);
-        }
-        if (!ok && atomicExch(&w->failed, 1) == 0) report(p.status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      blk = __shfl_sync(0xffffffffu, blk, 0);
-      pos = __shfl_sync(0xffffffffu, pos, 0);
-      if (blk >= 0) {
-        if (gather) {
-          const uint64_t aff = p.spill.base + static_cast<uint64_t>(chunk_row_offset(p.spill, row)) +
-                               static_cast<uint64_t>(pl0) * p.spill.plane_stride;
-          cycle_copy<true>(buf, planes_s, pl0, nrows, blk * p.block_stride, aff, p.spill.plane_stride, kind.vecs,
-                           kind.div, c0, nvec, lane);
-        } else {
-          const uint64_t aff = p.src.base + static_cast<uint64_t>(chunk_row_offset(p.src, row)) +
-                               static_cast<uint64_t>(pl0) * p.src.plane_stride;
-          cycle_copy<false>(buf, planes_s, pl0, nrows, blk * p.block_stride + pos * p.token_stride, aff,
-                            p.src.plane_stride, kind.vecs, kind.div, c0, nvec, lane);
-        }
-      }
-      int stop = 0;
-      if (lane == 0) {
-        __threadfence();
-        atomicAdd(gather ? &w->g_done[q] : &w->s_done[q], 1u);
-        stop = *reinterpret_cast<const volatile int*>(&w->failed);
-      }
-      stop = __shfl_sync(0xffffffffu, stop, 0);
-      if (stop) break;
-      t = __shfl_sync(0xffffffffu, next, 0);
     }
+    while (have) {
+      const unsigned i1 = cycle_next_item(tk, w, total, lane);
+      const bool have_next = i1 < total;
+      CycleItem nx;
+      bool early = false;
+      if (have_next) {
+        nx = cycle_decode(p, i1, first_s, gitems_s, offs_s, gen, &cur, lane);
+        early = nx.dep == 0u;
+        if (early) {
+          // the other half was last read by the newest bulk store group
+          cycle_issue(nx, planes_s, bufs + (half ^ 1) * kCycleItemVecs, &bars[half ^ 1], 0, lane);
+          if (nx.live && nx.bulk) armed |= 1u << (half ^ 1);
+        }
+      }
+      // the current item's loads
+      int ok = 1;
+      if (cur.live && cur.bulk) {
+        if (lane == 0) {
+          ok = mbar_wait(&bars[half], (parity >> half) & 1u) ? 1 : 0;
+          if (!ok && atomicExch(&w->failed, 1) == 0) report(p.status, KVCA_ERR_DEVICE_TIMEOUT, blockIdx.x);
+        }
+        parity ^= 1u << half;
+        armed &= ~(1u << half);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      } else if (early) {
+        cp_async_wait<1>();  // all but the next item's group
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncwarp();
+      if (!ok) break;  // the loads still in flight are waited for below
+      if (cur.gather && lane == 0)  // its reads are done: the block may be overwritten
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&w->g_done[cur.q]) : "memory");
+      cycle_store(cur, planes_s, bufs + half * kCycleItemVecs, lane);
+      __syncwarp();
+      if (!cur.gather && lane == 0) {
+        if (cur.fence) {  // a later gather of this block reads these rows
+          if (cur.bulk) {
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+          }
+          __threadfence();
+        }
+        atomicAdd(&w->s_done[cur.q], 1u);
+      }
+      if (!have_next) break;
+      if (!early) {
+        if (!cycle_wait_deps(nx, w, s_items, gitems_s, p.status, lane)) break;
+        // the other half was last read by the store group before the newest
+        cycle_issue(nx, planes_s, bufs + (half ^ 1) * kCycleItemVecs, &bars[half ^ 1], 1, lane);
+        if (nx.live && nx.bulk) armed |= 1u << (half ^ 1);
+      }
+      cur = nx;
+      half ^= 1;
+    }
+    cp_async_wait<0>();
+    if (lane == 0) {
+      // bulk loads still in flight land before shared memory is released
+      for (int h = 0; h < 2; ++h)
+        if (armed & (1u << h)) mbar_wait(&bars[h], (parity >> h) & 1u);
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
   }
   cycle_leave(w);
 }
@@ -3976,6 +4188,7 @@ CycleKind make_cycle_kind(int64_t row_bytes, int64_t planes) {
   k.group = static_cast<int>(move_cycle_group(row_bytes, planes));
   k.segs = static_cast<int>(move_cycle_segments(row_bytes));
   k.per_unit = static_cast<unsigned>(((planes + k.group - 1) / k.group) * k.segs);
+  k.bulk = row_bytes >= kCycleBulkMinRowBytes;
   return k;
 }
 
@@ -4011,8 +4224,12 @@ cudaError_t launch_move_cycle(const CycleArgs& a, cudaStream_t stream) {
   p.status = a.status;
   static bool configured = false;
   if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(move_cycle_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kCycleSmemBytes));
+    cudaError_t e = cudaFuncSetAttribute(move_cycle_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kCycleSmemBytes));
+    if (e != cudaSuccess) return e;
+    // the largest shared-memory carve-out, so that an SM running this CTA
+    // still has room for the bookkeeping kernel's CTA
+    e = cudaFuncSetAttribute(move_cycle_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     int b = 0;
     const cudaError_t e2 =

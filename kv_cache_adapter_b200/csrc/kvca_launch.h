@@ -76,9 +76,13 @@ struct CycleArgs {
 
 constexpr int64_t kMoveCycleMaxSteps = 32;
 constexpr size_t kCycleHeaderBytes = 512;
-// Bytes of one warp's share of work (an item, staged in the warp's buffer):
-// whole rows of at most this many bytes together, longer rows in pieces.
-constexpr int64_t kMoveCycleItemBytes = 16384;
+// Bytes of one warp's share of work (an item, staged in half of the warp's
+// buffer): whole rows of at most this many bytes together, longer rows in
+// pieces.
+#ifndef KVCA_CYCLE_ITEM_BYTES
+#define KVCA_CYCLE_ITEM_BYTES 8192
+#endif
+constexpr int64_t kMoveCycleItemBytes = KVCA_CYCLE_ITEM_BYTES;
 
 // Planes per item for rows of row_bytes.
 inline int64_t move_cycle_group(int64_t row_bytes, int64_t num_planes) {

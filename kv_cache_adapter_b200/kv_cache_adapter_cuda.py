@@ -1238,12 +1238,12 @@ def move_cycle(token_caches, slot_mapping: torch.Tensor, token_rows: torch.Tenso
     dev = tp.device
     if bp.device != dev:
         raise ValueError("token_caches and block_caches must be on one device")
-    _require_index(slot_mapping, dev, "slot_mapping")
+    if slot_mapping.dim() != 2:
+        raise ValueError("slot_mapping must be a (num_steps, num_seqs) tensor")
+    steps, seqs = slot_mapping.shape
+    _require_index(slot_mapping.view(-1) if slot_mapping.is_contiguous() else slot_mapping, dev, "slot_mapping")
     _require_index(victims, dev, "victims")
     _require_index(offsets, dev, "offsets")
-    if slot_mapping.dim() != 2 or not slot_mapping.is_contiguous():
-        raise ValueError("slot_mapping must be a contiguous (num_steps, num_seqs) tensor")
-    steps, seqs = slot_mapping.shape
     if offsets.numel() != steps + 1:
         raise ValueError("offsets must have num_steps + 1 entries")
     P = len(tp.planes)
@@ -1256,6 +1256,8 @@ def move_cycle(token_caches, slot_mapping: torch.Tensor, token_rows: torch.Tenso
     if cb < 1 or spill.dim() < 3 or spill.shape[2] != cb:
         raise ValueError("spill must be (chunks, P, blocks_per_chunk, *block_row)")
     _chunk_tensor(spill, (spill.shape[0], P, cb, *bp.row_shape), bp.dtype, dev, "spill")
+    if token_rows.device != dev or spill.device != dev:
+        raise ValueError("token_rows and spill must be on the cache's device")
     if steps == 0 or seqs == 0:
         return
     rb = tp.row_bytes

@@ -65,7 +65,8 @@ def _decode_schedule(rng, nb: int, bs: int, steps: int, seqs: int):
 def _random_schedule(rng, nb: int, bs: int, steps: int, seqs: int):
     slots = rng.permutation(nb * bs)[: steps * seqs].reshape(steps, seqs).astype(np.int64)
     counts = rng.integers(0, 7, steps)
-    counts[1] = 0  # a step without victims
+    if steps > 1:
+        counts[1] = 0  # a step without victims
     offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
     victims = rng.integers(0, nb, int(offs[-1])).astype(np.int64)
     # blocks written at the previous step, and blocks the next step writes
