@@ -1028,11 +1028,11 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         mix.stop_cycles(cycle_rows)
         torch.cuda.synchronize(device)
         ops.check_status(device)
-    ms, clocks = results[True]
-    pair_ms = results[False][0]
-    # launches per cycle: the booking, then the cycle's moves (one launch, or
-    # one per step: the token scatter with the next step's spill gather)
-    cycle_launches = 1 + 1
+    ms, clocks = results[False]
+    one_ms = results[True][0]
+    # launches per cycle: the booking, then one per step (the token scatter
+    # with the next step's spill gather)
+    cycle_launches = 1 + 16
     cyc_moved = 2 * mix.num_planes * (cyc_steps * mix.seqs * row_bytes + replays * per_two * row_bytes * mix.block_size)
     if rank != 0:
         return
@@ -1064,14 +1064,12 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         "gpu_launches": replays * 2 * cycle_launches,
         "tokens_per_s": round(world * cyc_steps * mix.seqs / (ms / 1e3), 1),
         "evictions_per_s": round(world * replays * per_two / (ms / 1e3), 1),
-        "gpu_launches_per_decode_step": "1/16 of a move_cycle launch (the cycle's 16 spill gathers and 16 token "
-                                        "scatters) plus 1/16 of an append_steps launch (pop, commit, release, "
-                                        "slot_mapping of 16 steps)",
+        "gpu_launches_per_decode_step": "one scatter_tokens_gather_layers launch (this step's token scatter with the "
+                                        "next step's spill gather) plus 1/16 of an append_steps launch (pop, commit, "
+                                        "release, slot_mapping of 16 steps)",
         "issue": "CUDA graph, one replay per two 16-step cycles; the bookkeeping of the next cycle (one "
-                 "append_steps launch) on a second stream, overlapping the current cycle's moves, which are one "
-                 "move_cycle launch (victims and slot_mappings double-buffered by cycle); needs every step's token "
-                 "rows when the cycle's launch starts (an engine that produces one token per forward pass moves "
-                 "each step as it comes: paired_steps_graph)",
+                 "append_steps launch) on a second stream, overlapping the current cycle's moves (victims and "
+                 "slot_mappings double-buffered by cycle); each step's moves are one launch, issued as the step comes",
         "token_rows": "a new row per sequence, plane and step (16 steps' rows in HBM)",
         "roofline": {
             "bound": "hbm",
@@ -1081,16 +1079,17 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
             "frac": round(cyc_moved / (ms / 1e3) / 1e9 / peak, 4),
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
             "traffic": None,
-            "kernel": "move_cycle_kernel (one launch per 16-step cycle; the cycle's booking runs beside it on "
-                      "another stream), timed over whole graph replays",
+            "kernel": "move_pair_all_kernel (one launch per decode step; the cycle's booking runs beside the "
+                      "cycle's launches on another stream), timed over whole graph replays",
             "algorithmic_bytes_per_decode_step": 2 * mix.num_planes * (mix.seqs * row_bytes +
                                                                        per_cycle // 16 * row_bytes * mix.block_size),
         },
-        "paired_steps_graph": {"value": round(world * cyc_moved / (pair_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                               "ms_per_decode_step": round(pair_ms / cyc_steps, 5),
-                               "gpu_launches_per_decode_step": 1 + 1 / 16,
-                               "issue": "same booking; each step's token scatter paired with the next step's "
-                                        "spill gather in one launch (one launch per decode step)"},
+        "one_launch_cycles_graph": {"value": round(world * cyc_moved / (one_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                                    "ms_per_decode_step": round(one_ms / cyc_steps, 5),
+                                    "gpu_launches_per_decode_step": 2 / 16,
+                                    "issue": "same booking; each cycle's 16 spill gathers and 16 token scatters in "
+                                             "one move_cycle launch (needs every step's token rows when the launch "
+                                             "starts)"},
         "per_step_pipelined_graph": {"value": round(world * moved / (step_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                                      "ms_per_decode_step": round(step_ms / decode_steps, 5),
                                      "issue": "CUDA graph per 16-step cycle, each step's append_step on a second "

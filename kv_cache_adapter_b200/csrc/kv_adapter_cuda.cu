@@ -3666,7 +3666,7 @@ namespace {
 // CTA to leave resets the counters and advances the generation.
 
 #ifndef KVCA_CYCLE_WARPS
-#define KVCA_CYCLE_WARPS 10
+#define KVCA_CYCLE_WARPS 5
 #endif
 constexpr int kCycleWarps = KVCA_CYCLE_WARPS;
 constexpr int kCycleThreads = kCycleWarps * 32;
@@ -3676,7 +3676,7 @@ constexpr uint32_t kCycleItemVecs = static_cast<uint32_t>(kMoveCycleItemBytes / 
 // copy per row into the item's buffer, and one per row out of it); shorter
 // rows move as 16-byte cp.async loads and stores by all lanes.
 constexpr int64_t kCycleBulkMinRowBytes = 1024;
-constexpr unsigned kCycleItemsPerTicket = 8;
+constexpr unsigned kCycleItemsPerTicket = 2;
 // two items per warp: one landing while the other is stored
 constexpr size_t kCycleSmemBytes = static_cast<size_t>(kCycleWarps) * 2 * kMoveCycleItemBytes;
 

@@ -80,7 +80,7 @@ constexpr size_t kCycleHeaderBytes = 512;
 // buffer): whole rows of at most this many bytes together, longer rows in
 // pieces.
 #ifndef KVCA_CYCLE_ITEM_BYTES
-#define KVCA_CYCLE_ITEM_BYTES 8192
+#define KVCA_CYCLE_ITEM_BYTES 16384
 #endif
 constexpr int64_t kMoveCycleItemBytes = KVCA_CYCLE_ITEM_BYTES;
 

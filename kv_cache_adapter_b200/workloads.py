@@ -462,17 +462,17 @@ class DecodeMix:
             self._book_stream.wait_stream(torch.cuda.current_stream(self.device))
         return got
 
-    def start_cycles(self, one_launch: bool | None = None) -> None:
+    def start_cycles(self, one_launch: bool = False) -> None:
         """Switch to whole-cycle booking and book the next cycle.  Call at a
         step count that is a multiple of block_size, with the per-step
-        pipeline off.  ``one_launch`` (default: when the op set has
-        move_cycle): each cycle's moves are one move_cycle launch, whose
-        spill holds the whole cycle's victims (row offsets[q] + i: victim i
-        of step q); otherwise each step's scatter is paired with the next
-        step's gather, and the spill holds the last step's victims."""
+        pipeline off.  Each step's scatter is paired with the next step's
+        gather in one launch, and the spill holds the last step's victims;
+        ``one_launch`` (op sets with move_cycle): each cycle's moves are one
+        move_cycle launch instead, whose spill holds the whole cycle's
+        victims (row offsets[q] + i: victim i of step q)."""
         assert self._append_many is not None and self.device.type == "cuda" and not self._cycles_on
         assert not self._pipelined
-        self._one_launch = self._cycle_op is not None if one_launch is None else bool(one_launch)
+        self._one_launch = bool(one_launch)
         assert not self._one_launch or self._cycle_op is not None
         assert (self.pos >= 1).all()  # past the first step: the fill positions repeat every cycle
         if self._book_stream is None:
