@@ -2440,6 +2440,19 @@ __global__ void __launch_bounds__(kMoverThreads) move_rows_kernel(const __grid_c
 
 // Rows of at most kSmallRowMaxVecs 16-byte vectors (256 bytes).
 constexpr int64_t kSmallRowMaxVecs = 16;
+// In the pair kernel, rows of 97 to 128 vectors (1.5 to 2 KiB) take the
+// short-row body with a whole warp per row, 4 vectors per lane and
+// kMediumRows rows per warp and iteration: a decode step's token scatter
+// with 8 KV heads (2 KiB rows) keeps 8 vectors per lane in flight over every
+// row of its short launch (B200, a step's scatter with the next step's spill
+// gather, 134 MB: 24.4 us per step against 28.2 on the SIMT body; 4 rows per
+// iteration: 25.8 us).  Moves of their own keep the SIMT body for these rows
+// (random 2 KiB token rows, 1 GiB: 5.75 / 5.88 TB/s gather / scatter
+// against 5.65 / 5.63 on this body).
+constexpr int kMediumRows = 2;
+constexpr int64_t kMediumRowMinVecs = 96;
+constexpr int64_t kMediumRowMaxVecs = 128;
+
 
 // Offset of slot id idx on a paged side (shift = log2 of the block size when
 // that is a power of two, else -1), or -1 when the row is skipped; the same
@@ -2760,7 +2773,7 @@ __global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(con
 // and the next step's spill gather), one launch instead of two saves a
 // launch's latency, ramp and tail.  The two moves must not touch the same
 // bytes.
-enum class MoverBody : int { kSimt = 0, kStream = 1, kSmall = 2 };
+enum class MoverBody : int { kSimt = 0, kStream = 1, kSmall = 2, kMedium = 3 };
 
 template <MoverBody kBody, bool kSrcPaged, bool kDstPaged, bool kEarly>
 __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta, int64_t ctas) {
@@ -2768,6 +2781,8 @@ __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta,
     move_rows_stream_body<kSrcPaged, kDstPaged, kEarly>(p, cta, ctas);
   else if constexpr (kBody == MoverBody::kSmall)
     move_short_rows_pm_body<kSrcPaged, kDstPaged, 2, 4, kEarly>(p, cta, ctas);
+  else if constexpr (kBody == MoverBody::kMedium)  // a warp per row of at most 128 vectors
+    move_short_rows_pm_body<kSrcPaged, kDstPaged, 4, kMediumRows, kEarly>(p, cta, ctas);
   else
     move_rows_body<kSrcPaged, kDstPaged, uint4, false, kEarly>(p, cta, ctas);
 }
@@ -3513,6 +3528,13 @@ MoverBody pair_body(MoveParams* p, int64_t* ctas_wanted) {
     *ctas_wanted = ((((items + 3) / 4) << p->tpr_log2) + kMoverThreads - 1) / kMoverThreads;
     return MoverBody::kSmall;
   }
+  if (p->row_vecs > kMediumRowMinVecs && p->row_vecs <= kMediumRowMaxVecs) {
+    p->tpr_log2 = 5;
+    p->seg_vecs = p->row_vecs;
+    p->segs_per_row = 1;
+    *ctas_wanted = ((((items + kMediumRows - 1) / kMediumRows) << 5) + kMoverThreads - 1) / kMoverThreads;
+    return MoverBody::kMedium;
+  }
   *ctas_wanted = (((items * p->segs_per_row) << p->tpr_log2) + kMoverThreads - 1) / kMoverThreads;
   return MoverBody::kSimt;
 }
@@ -3537,6 +3559,7 @@ cudaError_t launch_pair_b(MoverBody b_body, const MoveParams& a, const MoveParam
   switch (b_body) {
     case MoverBody::kStream: return launch_pair_typed<kA, MoverBody::kStream>(a, b, split, grid, early, stream);
     case MoverBody::kSmall: return launch_pair_typed<kA, MoverBody::kSmall>(a, b, split, grid, early, stream);
+    case MoverBody::kMedium: return launch_pair_typed<kA, MoverBody::kMedium>(a, b, split, grid, early, stream);
     default: return launch_pair_typed<kA, MoverBody::kSimt>(a, b, split, grid, early, stream);
   }
 }
@@ -3604,6 +3627,7 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
     switch (body_a) {
       case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, -1, grid_all, false, stream);
       case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, -1, grid_all, false, stream);
+      case MoverBody::kMedium: return launch_pair_b<MoverBody::kMedium>(body_b, a, b, -1, grid_all, false, stream);
       default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, -1, grid_all, false, stream);
     }
   }
@@ -3622,6 +3646,7 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   switch (body_a) {
     case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, split, grid, early, stream);
     case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, split, grid, early, stream);
+    case MoverBody::kMedium: return launch_pair_b<MoverBody::kMedium>(body_b, a, b, split, grid, early, stream);
     default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, split, grid, early, stream);
   }
 }

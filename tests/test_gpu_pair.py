@@ -66,7 +66,8 @@ def _run(ops, kv, slots, ids, rows, bs, row, blocks_per_chunk):
     return kv_d, out, ref, want
 
 
-@pytest.mark.parametrize("row,bs", [(64, 16), (256, 16), (576, 4), (2048, 16), (1024, 1), (100, 8), (48, 2)])
+@pytest.mark.parametrize("row,bs", [(64, 16), (256, 16), (576, 4), (1552, 4), (2048, 16), (2064, 2), (1024, 1),
+                                    (100, 8), (48, 2)])
 def test_pair_matches_oracle(ops, row, bs):
     planes, nb = 6, 96
     kv, slots, ids, rows = _case(planes, nb, bs, row, tokens=200 if bs > 1 else 40, gathered=24, seed=row * 31 + bs)

@@ -1,12 +1,12 @@
-"""GPU parity for rows of at most 1.5 KiB in 16-byte vectors, which take the
+"""GPU parity for rows under 4 KiB in 16-byte vectors, which take the
 small-row mover (rows under 128 bytes: up to 8 lanes and four rows per lane
-group and iteration) or the warp-cooperative stream mover (128 bytes to
-1.5 KiB: a warp's 32 x 9 vector slots tile a batch of rows), against the
-oracle's torch CPU indexing, byte for byte: row widths from 16 bytes to
-1.5 KiB and just past it, plane counts that make one iteration's rows
-straddle tokens, work ranges that end inside a batch, chunks shorter than a
-batch, padding tokens, out-of-range ids, and block-granular moves of short
-blocks."""
+group and iteration), the warp-cooperative stream mover (128 bytes to
+1.5 KiB: a warp's 32 x 9 vector slots tile a batch of rows) or the SIMT
+mover (past 1.5 KiB), against the oracle's torch CPU indexing, byte for
+byte: row widths from 16 bytes to just under 4 KiB, plane counts that make
+one iteration's rows straddle tokens, work ranges that end inside a batch,
+chunks shorter than a batch, padding tokens, out-of-range ids, and
+block-granular moves of short blocks."""
 from __future__ import annotations
 
 import numpy as np
@@ -37,7 +37,7 @@ def _rand_bytes(shape, gen) -> torch.Tensor:
     return torch.randint(0, 256, shape, generator=gen, dtype=torch.uint8)
 
 
-ROW_BYTES = [16, 32, 48, 64, 112, 128, 144, 240, 256, 272, 512, 576, 1040, 1152, 1536, 1552]
+ROW_BYTES = [16, 32, 48, 64, 112, 128, 144, 240, 256, 272, 512, 576, 1040, 1152, 1536, 1552, 2048, 2064, 3072, 4080]
 
 
 @pytest.mark.parametrize("row", ROW_BYTES)
