@@ -29,6 +29,7 @@ bounded sample of the workload with all host cores, on rank 0 only.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import pathlib
@@ -667,12 +668,15 @@ def run_token_rows(args, world: int, rank: int, device) -> None:
         moved = 2 * planes_n * rows * rb
         g_ms = _max_over_ranks(statistics.median(a.elapsed_time(b) for a, b, _ in ev), world, device)
         s_ms = _max_over_ranks(statistics.median(b.elapsed_time(c) for _, b, c in ev), world, device)
+        ceil_g, ceil_s = _row_ceiling(ops, device, rb, planes_n * rows, args.steps, world)
+        g_gbs, s_gbs = moved / (g_ms / 1e3) / 1e9, moved / (s_ms / 1e3) / 1e9
         runs.append({"row_bytes": rb, "planes": planes_n, "rows_per_plane": rows, "bytes_per_move": moved,
-                     "gather_gbs": round(moved / (g_ms / 1e3) / 1e9, 1),
-                     "scatter_gbs": round(moved / (s_ms / 1e3) / 1e9, 1),
-                     "gather_frac": round(moved / (g_ms / 1e3) / 1e9 / peak, 4),
-                     "scatter_frac": round(moved / (s_ms / 1e3) / 1e9 / peak, 4),
-                     "gather_ms": round(g_ms, 4), "scatter_ms": round(s_ms, 4)})
+                     "gather_gbs": round(g_gbs, 1), "scatter_gbs": round(s_gbs, 1),
+                     "gather_frac": round(g_gbs / peak, 4), "scatter_frac": round(s_gbs / peak, 4),
+                     "gather_ms": round(g_ms, 4), "scatter_ms": round(s_ms, 4),
+                     "random_row_ceiling_gbs": {"gather": round(ceil_g, 1), "scatter": round(ceil_s, 1)},
+                     "frac_of_random_row_ceiling": {"gather": round(g_gbs / ceil_g, 4),
+                                                    "scatter": round(s_gbs / ceil_s, 4)}})
         del cache, chunks, planes, ptab
         torch.cuda.empty_cache()
     if rank != 0:
@@ -686,9 +690,48 @@ def run_token_rows(args, world: int, rank: int, device) -> None:
                                    + ", ".join(str(r["row_bytes"]) for r in runs) + " B",
                        "l2": "each move reads and writes about 2 x move_mib MiB, above L2"},
             "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s", "worst_frac": worst,
-                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"},
-            "runs": runs, "gpu_launches": 2 * args.steps * len(runs)}
+                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
+                         "random_row_ceiling": "kvca_row_ceiling on the same box and the same bytes: one dense "
+                                               "plane, rows through a uint32 permutation, no slot or chunk "
+                                               "arithmetic (the DRAM limit of random rows of that width)"},
+            "runs": runs, "gpu_launches": 4 * args.steps * len(runs)}
     print(json.dumps(line), flush=True)
+
+
+def _row_ceiling(ops, device, row_bytes: int, rows: int, steps: int, world: int) -> tuple[float, float]:
+    """GB/s of kvca_row_ceiling gathering and scattering `rows` rows of
+    row_bytes between two dense buffers through a random permutation (median
+    of `steps` launches each, 8 CTAs of 256 threads per SM)."""
+    src = torch.empty(rows * row_bytes, dtype=torch.uint8, device=device)
+    src.random_(0, 256)
+    dst = torch.empty_like(src)
+    perm = torch.randperm(rows, generator=torch.Generator().manual_seed(row_bytes)).to(torch.int32).to(device)
+    lib = ops._lib_handle
+    ctas = 8 * torch.cuda.get_device_properties(device).multi_processor_count
+    out = []
+    for scatter in (0, 1):
+        def launch():
+            rc = lib.kvca_row_ceiling(ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()),
+                                      ctypes.c_void_p(perm.data_ptr()), rows, row_bytes, scatter, ctas,
+                                      ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+            if rc != 0:
+                raise RuntimeError(f"kvca_row_ceiling failed ({rc})")
+        for _ in range(3):
+            launch()
+        ts = []
+        for _ in range(max(steps, 3)):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            launch()
+            b.record()
+            torch.cuda.synchronize(device)
+            ts.append(a.elapsed_time(b))
+        out.append(2 * rows * row_bytes / (_max_over_ranks(statistics.median(ts), world, device) / 1e3) / 1e9)
+    if not torch.equal(dst.view(rows, row_bytes)[perm.long()], src.view(rows, row_bytes)):
+        raise RuntimeError(f"row ceiling check failed: {row_bytes}-byte rows")
+    del src, dst, perm
+    torch.cuda.empty_cache()
+    return out[0], out[1]
 
 
 def run_ours(args, w: dict, world: int, rank: int, device) -> None:

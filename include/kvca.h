@@ -599,6 +599,18 @@ int kvca_move_cycle(const kvca_chunk_desc* tokens, const kvca_paged_desc* token_
                     int64_t num_seqs, int64_t spill_rows, int32_t flags, void* d_scratch, int64_t* d_status,
                     kvca_stream_t stream);
 
+/*
+ * Measurement aid, not an adapter path: moves `rows` rows of row_bytes (64,
+ * 128, 256, 576, 1152 or 2048) between two dense buffers through a uint32
+ * permutation, scatter (dst row d_perm[r] = src row r) or gather (dst row r
+ * = src row d_perm[r]), on `ctas` CTAs of 256 threads, with no other index
+ * work.  The rate it reaches is the ceiling that random-row moves of that
+ * width are measured against (the copy bandwidth is the ceiling of
+ * sequential moves only).  No reference counterpart.
+ */
+int kvca_row_ceiling(const void* d_src, void* d_dst, const uint32_t* d_perm, int64_t rows, int64_t row_bytes,
+                     int scatter, int ctas, kvca_stream_t stream);
+
 /* Paged -> paged in one pass: dst[dst.index[r]] = src[src.index[r]]
  * (the index_select + index_copy_ pair of adapter.py:779-787). */
 int kvca_copy_paged(const kvca_paged_desc* src, const kvca_paged_desc* dst, int64_t num_planes,

@@ -193,6 +193,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [ctypes.POINTER(ChunkDesc), ctypes.POINTER(PagedDesc), c_i64, c_i64, c_i64, ctypes.c_int32,
          c_ptr, c_ptr],
     ),
+    "kvca_row_ceiling": (c_int, [c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_int, c_int, c_ptr]),
     "kvca_move_cycle_scratch_bytes": (c_i64, [c_i64]),
     "kvca_move_cycle": (
         c_int,

@@ -2,8 +2,9 @@
 
     python -m kv_cache_adapter_b200.build [--force] [--ptxas-verbose]
 
-Compiles csrc/kv_adapter_cuda.cu (kernels) and csrc/binding.cpp (the C ABI
-of include/kvca.h) with nvcc into a shared library next to this file, with
+Compiles csrc/kv_adapter_cuda.cu (kernels), csrc/row_ceiling.cu (the
+random-row roofline reference) and csrc/binding.cpp (the C ABI of
+include/kvca.h) with nvcc into a shared library next to this file, with
 the CUDA runtime linked statically so the library has no runtime dependency
 beyond the driver.
 """
@@ -20,7 +21,7 @@ PKG = pathlib.Path(__file__).resolve().parent
 REPO = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = REPO / "include"
-SOURCES = [CSRC / "kv_adapter_cuda.cu", CSRC / "binding.cpp"]
+SOURCES = [CSRC / "kv_adapter_cuda.cu", CSRC / "row_ceiling.cu", CSRC / "binding.cpp"]
 HEADERS = [CSRC / "kvca_launch.h", INCLUDE / "kvca.h"]
 TARGET = PKG / "libkvca_b200.so"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

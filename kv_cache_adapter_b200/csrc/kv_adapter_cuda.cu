@@ -2342,7 +2342,7 @@ constexpr int64_t kMoverSegmentBytes = 16384;
 // come before it too (stream and small-row bodies).
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost, bool kEarly = false>
+template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost, bool kEarly = false, int kUnroll = kMoverUnroll>
 __device__ __forceinline__ void move_rows_body(const MoveParams& p, int64_t cta, int64_t ctas) {
   if (p.gate != nullptr && *p.gate == 0) return;
   const int tpr = 1 << p.tpr_log2;
@@ -2388,15 +2388,15 @@ __device__ __forceinline__ void move_rows_body(const MoveParams& p, int64_t cta,
                                         : p.dst_chunk.base + dst_row + pl * p.dst_chunk.plane_stride);
       const int64_t v_begin = sg * seg_vecs;
       const int64_t v_end = v_begin + seg_vecs < row_vecs ? v_begin + seg_vecs : row_vecs;
-      for (int64_t b = v_begin + lane; b < v_end; b += static_cast<int64_t>(tpr) * kMoverUnroll) {
-        V buf[kMoverUnroll];
+      for (int64_t b = v_begin + lane; b < v_end; b += static_cast<int64_t>(tpr) * kUnroll) {
+        V buf[kUnroll];
 #pragma unroll
-        for (int u = 0; u < kMoverUnroll; ++u) {
+        for (int u = 0; u < kUnroll; ++u) {
           const int64_t i = b + static_cast<int64_t>(u) * tpr;
           if (i < v_end) buf[u] = kHost ? src[i] : ld_stream(src + i);
         }
 #pragma unroll
-        for (int u = 0; u < kMoverUnroll; ++u) {
+        for (int u = 0; u < kUnroll; ++u) {
           const int64_t i = b + static_cast<int64_t>(u) * tpr;
           if (i < v_end) {
             if (kHost)
@@ -2773,6 +2773,11 @@ __global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(con
 // and the next step's spill gather), one launch instead of two saves a
 // launch's latency, ramp and tail.  The two moves must not touch the same
 // bytes.
+#ifndef KVCA_PAIR_SIMT_UNROLL
+#define KVCA_PAIR_SIMT_UNROLL 8
+#endif
+constexpr int kPairSimtUnroll = KVCA_PAIR_SIMT_UNROLL;
+
 enum class MoverBody : int { kSimt = 0, kStream = 1, kSmall = 2, kMedium = 3 };
 
 template <MoverBody kBody, bool kSrcPaged, bool kDstPaged, bool kEarly>
@@ -2784,7 +2789,7 @@ __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta,
   else if constexpr (kBody == MoverBody::kMedium)  // a warp per row of at most 128 vectors
     move_short_rows_pm_body<kSrcPaged, kDstPaged, 4, kMediumRows, kEarly>(p, cta, ctas);
   else
-    move_rows_body<kSrcPaged, kDstPaged, uint4, false, kEarly>(p, cta, ctas);
+    move_rows_body<kSrcPaged, kDstPaged, uint4, false, kEarly, kPairSimtUnroll>(p, cta, ctas);
 }
 
 static_assert(kMoverThreads == kRowStreamThreads, "the pair kernel runs every body at one CTA size");

@@ -137,3 +137,15 @@ def test_move_cycle_checks_arguments_on_the_host():
     assert call(block_row=8192) == bad  # a block row past its block
     assert call(tok=paged(row_stride=512)) == bad  # token rows past their block
     assert call(seqs=1 << 27) == _lib.KVCA_ERR_SIZE_LIMIT
+
+
+def test_row_ceiling_checks_arguments_on_the_host():
+    lib = _lib.load()
+    bad = _lib.KVCA_ERR_BAD_ARGUMENT
+    p = ctypes.c_void_p(1 << 20)  # never dereferenced: every call below is refused first
+    assert lib.kvca_row_ceiling(p, p, p, 100, 100, 1, 4, None) == bad  # unsupported width
+    assert lib.kvca_row_ceiling(p, p, p, 0, 128, 1, 4, None) == bad
+    assert lib.kvca_row_ceiling(p, p, p, 1 << 31, 128, 1, 4, None) == bad
+    assert lib.kvca_row_ceiling(p, p, p, 100, 128, 1, 0, None) == bad
+    assert lib.kvca_row_ceiling(ctypes.c_void_p(8), p, p, 100, 128, 1, 4, None) == bad  # misaligned
+    assert lib.kvca_row_ceiling(None, p, p, 100, 128, 1, 4, None) == bad
