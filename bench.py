@@ -1256,7 +1256,7 @@ def run_adapter(args, world: int, rank: int, device) -> None:
     """KVCacheAdapter.load / save per call on the configuration of the
     reference's runtime-path benchmark (256 physical / 1,024 logical blocks,
     batch 32, 128-float blocks, in-memory backend on the device)."""
-    steps = max(args.steps, 20)
+    steps = max(args.steps, 100)  # calls per hit rate and path: enough to average out single slow calls
     cuda_ad = _adapter_case(device)
     cuda_ad.load(torch.arange(ADAPTER_CONFIG["num_actual"], dtype=torch.int64, device=device))  # opens the session
     assert cuda_ad._session is not None

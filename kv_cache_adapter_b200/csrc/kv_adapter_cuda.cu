@@ -1881,8 +1881,16 @@ constexpr size_t kAppendSmemBytes = (3 * kAppendSmemSeqs + kAppendSmemNeed) * si
 // within [0, num_need]); an error at step s leaves steps 0..s-1 done and
 // stops there.  Steps after the first read the state the previous one wrote
 // (same CTA, ordered by a block barrier).
+// Minimum resident CTAs per SM the booking kernel is compiled for (a build
+// knob for sweeps).  At 4 (64 registers) its CTA fits beside a pair-kernel
+// CTA on one SM; B200, decode mix with the full pool: 8 KV heads 24.46
+// against 24.65 us per step (one-launch cycles 24.64 against 27.03), but one
+// KV head 5.11 against 4.62, where the slower booking shows; 1 is kept.
+#ifndef KVCA_APPEND_MIN_CTAS
+#define KVCA_APPEND_MIN_CTAS 1
+#endif
 template <typename MetaT>
-__global__ void __launch_bounds__(kAppendThreads)
+__global__ void __launch_bounds__(kAppendThreads, KVCA_APPEND_MIN_CTAS)
     append_steps_kernel(MetaT* meta, int64_t n, int64_t* search_start, int64_t* l2p,
                         int64_t n_logical, int64_t* p2l, const int64_t* need,
                         const int64_t* need_offsets, int64_t num_need, int64_t num_steps,
@@ -2773,6 +2781,9 @@ __global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(con
 // and the next step's spill gather), one launch instead of two saves a
 // launch's latency, ramp and tail.  The two moves must not touch the same
 // bytes.
+// Vectors per lane and iteration of the pair kernel's SIMT body (a build
+// knob for sweeps; B200, decode step pairs: 16 was slower than 8, 25.3 against
+// 24.4 us per step with 8 KV heads and 7.8 against 4.7 with one).
 #ifndef KVCA_PAIR_SIMT_UNROLL
 #define KVCA_PAIR_SIMT_UNROLL 8
 #endif
@@ -3695,6 +3706,10 @@ namespace {
 // of earlier launches read as empty and nothing has to clear them; the last
 // CTA to leave resets the counters and advances the generation.
 
+// Warps per CTA (a build knob for sweeps, as is KVCA_CYCLE_ITEM_BYTES; B200,
+// a booked 8-KV-head cycle measured alone with 8 items per ticket: 5 warps of
+// 16 KiB items 542 us, 3, 5 or 10 warps of 8 KiB items 704-739 us; with 2
+// items per ticket, 5 warps of 16 KiB: 368 us under the profiler).
 #ifndef KVCA_CYCLE_WARPS
 #define KVCA_CYCLE_WARPS 5
 #endif
