@@ -1492,7 +1492,7 @@ __device__ void plan_load_body(const int64_t* l2p, int64_t n_logical, const int6
   using M = Meta<MetaT>;
   if (threadIdx.x == 0) plan_begin(counts, status);
   if (!plan_validate<MetaT>(l2p, n_logical, n, ids, k, counts, status, sh)) return;
-  // hits and misses in request order; the hit slots are blocked for the pop
+  // hits and misses in request order
   int64_t nh = 0, nm = 0;
   for (int64_t tile = 0; tile < k; tile += blockDim.x) {
     const int64_t i = tile + threadIdx.x;
@@ -1507,16 +1507,28 @@ __device__ void plan_load_body(const int64_t* l2p, int64_t n_logical, const int6
       hit_slots[r] = cur;
       hit_pins[r] = static_cast<int64_t>(M::pin(w)) + 1;
       hit_usage[r] = static_cast<MetaT>(M::sat_inc(M::usage(w)));
-      atomicOr(bitmap + (cur >> 5), 1u << (cur & 31));
       result[i] = cur;
     }
     if (miss) miss_ids[nm + (base >> kPackShift)] = ids[i];
     nh += total & ((1 << kPackShift) - 1);
     nm += total >> kPackShift;
   }
+  if (nm == 0) {  // every request hit: no pop, no eviction plan (nm is uniform across the CTA)
+    if (threadIdx.x == 0) {
+      counts[0] = nh;
+      counts[1] = 0;
+      counts[2] = 0;
+    }
+    return;
+  }
+  __syncthreads();  // this thread's hit slots were written by others
+  // the hit slots are blocked for the pop
+  for (int64_t j = threadIdx.x; j < nh; j += blockDim.x) {
+    const int64_t b = hit_slots[j];
+    atomicOr(bitmap + (b >> 5), 1u << (b & 31));
+  }
   __syncthreads();
-  int rc = KVCA_OK;
-  if (nm > 0) rc = pop_cta<MetaT>(meta, n, search_start, bitmap, nm, victims, order, aligned, sh.pop);
+  const int rc = pop_cta<MetaT>(meta, n, search_start, bitmap, nm, victims, order, aligned, sh.pop);
   __syncthreads();
   for (int64_t j = threadIdx.x; j < nh; j += blockDim.x) {
     const int64_t b = hit_slots[j];
@@ -1549,10 +1561,9 @@ __device__ void plan_load_body(const int64_t* l2p, int64_t n_logical, const int6
     }
     ne += total;
   }
-  // with misses the pop may have aged usage: hits take usage + 1 of what is left
-  if (nm > 0)
-    for (int64_t j = threadIdx.x; j < nh; j += blockDim.x)
-      hit_usage[j] = static_cast<MetaT>(M::sat_inc(M::usage(meta[hit_slots[j]])));
+  // the pop may have aged usage: hits take usage + 1 of what is left
+  for (int64_t j = threadIdx.x; j < nh; j += blockDim.x)
+    hit_usage[j] = static_cast<MetaT>(M::sat_inc(M::usage(meta[hit_slots[j]])));
   if (threadIdx.x == 0) {
     counts[0] = nh;
     counts[1] = nm;
@@ -2204,12 +2215,23 @@ __global__ void __launch_bounds__(1024)
   int64_t* xslot = work + 6 * k;
   int64_t* spill_to = work + 7 * k;
   int64_t* fill_from = work + 8 * k;
-  for (int64_t i = threadIdx.x; i < 3 * k; i += blockDim.x) xslot[i] = -1;  // xslot, spill_to, fill_from
-  if (threadIdx.x == 0) counts[7] = 0;
-  __syncthreads();
+  if (threadIdx.x == 0) {
+    counts[7] = 0;
+    fs.bad = 0;
+  }
   plan_load_body<MetaT>(l2p, n_logical, p2l, meta, n, search_start, ids, k, bitmap, order, aligned, result,
                         hit_slots, hit_pins, hit_usage, miss_ids, victims, evict_ids, evict_slots, counts, status,
                         sh);
+  __syncthreads();
+  if (counts[1] == 0 && counts[3] == 0) {  // every request hit: commit the hits' pins and usage, no rows move
+    const int64_t nh = counts[0];
+    if (all_in_range(hit_slots, nh, n, status, &fs.bad))
+      for (int64_t i = threadIdx.x; i < nh; i += blockDim.x)
+        meta[hit_slots[i]] = Meta<MetaT>::pack(hit_pins[i], hit_usage[i]);
+    signal_host(counts, host_counts, seq);
+    return;
+  }
+  for (int64_t i = threadIdx.x; i < 3 * k; i += blockDim.x) xslot[i] = -1;  // xslot, spill_to, fill_from
   __syncthreads();
   store_load_finish_body<MetaT>(l2p, n_logical, p2l, meta, n, counts, hit_slots, hit_pins, hit_usage, miss_ids,
                                 victims, evict_ids, scratch, present, xslot, spill_to, fill_from, status, fs);
