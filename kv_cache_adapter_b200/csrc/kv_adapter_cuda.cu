@@ -2806,12 +2806,100 @@ __global__ void __launch_bounds__(kRowStreamThreads) move_rows_stream_kernel(con
 // Vectors per lane and iteration of the pair kernel's SIMT body (a build
 // knob for sweeps; B200, decode step pairs: 16 was slower than 8, 25.3 against
 // 24.4 us per step with 8 KV heads and 7.8 against 4.7 with one).
+// Rows of a multiple of kSplitVecs 16-byte vectors (the bulk mover's rows, in
+// the pair kernel) as sub-rows of kSplitVecs vectors: a warp per sub-row, 4
+// vectors per lane, two sub-rows per warp and iteration, so each lane keeps
+// 8 vectors in flight as on the short-row body.  Work items g = (row *
+// planes + plane) * sub-rows + sub-row: a warp walks the sub-rows of one
+// row's plane (32 KiB of a decode step's victim block) before the next, and
+// loads each row's index once.  A skipped or refused row leaves its
+// destination as it was.
+constexpr int64_t kSplitVecs = 128;
+
+template <bool kSrcPaged, bool kDstPaged, bool kEarly>
+__device__ __forceinline__ void move_split_rows_body(const MoveParams& p, int64_t cta, int64_t ctas) {
+  if (p.gate != nullptr && *p.gate == 0) return;
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const int64_t warp = (cta * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t warps = (ctas * static_cast<int64_t>(blockDim.x)) >> 5;
+  const int64_t subs = p.row_vecs / kSplitVecs;
+  const int64_t planes = p.num_planes;
+  const int64_t per_row = planes * subs;
+  const int64_t items = per_row * p.num_rows;
+  const int64_t per = items / warps;
+  const int64_t rem = items - per * warps;
+  const int64_t begin = warp * per + (warp < rem ? warp : rem);
+  const int64_t end = begin + per + (warp < rem ? 1 : 0);
+  if (begin >= end) return;
+  int64_t r = begin / per_row;
+  int64_t pl = (begin - r * per_row) / subs;
+  int64_t j = begin - r * per_row - pl * subs;
+  int64_t row_r = -1;
+  int64_t src_row = 0;
+  int64_t dst_row = 0;
+  const bool lead = lane == 0;
+  if constexpr (kEarly) grid_dependency_wait();
+  for (int64_t g = begin; g < end; g += 2) {
+    const uint4* src[2];
+    uint4* dst[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      src[u] = nullptr;
+      dst[u] = nullptr;
+      if (g + u < end) {
+        if (r != row_r) {
+          row_r = r;
+          src_row = kSrcPaged ? paged_row_offset(p.src_paged, r, p.flags, p.status, lead)
+                              : chunk_row_offset(p.src_chunk, r);
+          dst_row = kDstPaged ? paged_row_offset(p.dst_paged, r, p.flags, p.status, lead)
+                              : chunk_row_offset(p.dst_chunk, r);
+        }
+        if (src_row >= 0 && dst_row >= 0) {
+          const uint64_t sub = static_cast<uint64_t>(j) * kSplitVecs * 16;
+          src[u] = reinterpret_cast<const uint4*>(
+              (kSrcPaged ? p.src_paged.planes[pl] + src_row
+                         : p.src_chunk.base + src_row + pl * p.src_chunk.plane_stride) + sub);
+          dst[u] = reinterpret_cast<uint4*>(
+              (kDstPaged ? p.dst_paged.planes[pl] + dst_row
+                         : p.dst_chunk.base + dst_row + pl * p.dst_chunk.plane_stride) + sub);
+        }
+        if (++j == subs) {
+          j = 0;
+          if (++pl == planes) {
+            pl = 0;
+            ++r;
+          }
+        }
+      }
+    }
+    uint4 buf[2][4];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        if (src[u] != nullptr) buf[u][v] = ld_stream(src[u] + lane + 32 * v);
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        if (dst[u] != nullptr) st_stream(dst[u] + lane + 32 * v, buf[u][v]);
+  }
+}
+
 #ifndef KVCA_PAIR_SIMT_UNROLL
 #define KVCA_PAIR_SIMT_UNROLL 8
 #endif
 constexpr int kPairSimtUnroll = KVCA_PAIR_SIMT_UNROLL;
+// The pair kernel moves the bulk mover's rows as 2 KiB sub-rows (a build
+// knob for sweeps; 0 keeps them on the SIMT body).  B200, decode step pairs
+// replayed alone: 8 KV heads (32 KiB victim rows) 23.7 against 24.6 us per
+// step; one KV head (4 KiB rows) 4.71 against 4.72.
+#ifndef KVCA_PAIR_SPLIT_ROWS
+#define KVCA_PAIR_SPLIT_ROWS 1
+#endif
+constexpr bool kPairSplitRows = KVCA_PAIR_SPLIT_ROWS != 0;
 
-enum class MoverBody : int { kSimt = 0, kStream = 1, kSmall = 2, kMedium = 3 };
+enum class MoverBody : int { kSimt = 0, kStream = 1, kSmall = 2, kMedium = 3, kSplit = 4 };
 
 template <MoverBody kBody, bool kSrcPaged, bool kDstPaged, bool kEarly>
 __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta, int64_t ctas) {
@@ -2821,6 +2909,8 @@ __device__ __forceinline__ void run_mover_body(const MoveParams& p, int64_t cta,
     move_short_rows_pm_body<kSrcPaged, kDstPaged, 2, 4, kEarly>(p, cta, ctas);
   else if constexpr (kBody == MoverBody::kMedium)  // a warp per row of at most 128 vectors
     move_short_rows_pm_body<kSrcPaged, kDstPaged, 4, kMediumRows, kEarly>(p, cta, ctas);
+  else if constexpr (kBody == MoverBody::kSplit)  // a warp per 2 KiB sub-row of longer rows
+    move_split_rows_body<kSrcPaged, kDstPaged, kEarly>(p, cta, ctas);
   else
     move_rows_body<kSrcPaged, kDstPaged, uint4, false, kEarly, kPairSimtUnroll>(p, cta, ctas);
 }
@@ -3566,6 +3656,11 @@ MoverBody pair_body(MoveParams* p, int64_t* ctas_wanted) {
     *ctas_wanted = ((((items + 3) / 4) << p->tpr_log2) + kMoverThreads - 1) / kMoverThreads;
     return MoverBody::kSmall;
   }
+  if (kPairSplitRows && p->row_vecs * 16 >= kBulkMinRowBytes && p->row_vecs % kSplitVecs == 0) {
+    const int64_t subs = items * (p->row_vecs / kSplitVecs);
+    *ctas_wanted = (((subs + 1) / 2) * 32 + kMoverThreads - 1) / kMoverThreads;
+    return MoverBody::kSplit;
+  }
   if (p->row_vecs > kMediumRowMinVecs && p->row_vecs <= kMediumRowMaxVecs) {
     p->tpr_log2 = 5;
     p->seg_vecs = p->row_vecs;
@@ -3598,6 +3693,7 @@ cudaError_t launch_pair_b(MoverBody b_body, const MoveParams& a, const MoveParam
     case MoverBody::kStream: return launch_pair_typed<kA, MoverBody::kStream>(a, b, split, grid, early, stream);
     case MoverBody::kSmall: return launch_pair_typed<kA, MoverBody::kSmall>(a, b, split, grid, early, stream);
     case MoverBody::kMedium: return launch_pair_typed<kA, MoverBody::kMedium>(a, b, split, grid, early, stream);
+    case MoverBody::kSplit: return launch_pair_typed<kA, MoverBody::kSplit>(a, b, split, grid, early, stream);
     default: return launch_pair_typed<kA, MoverBody::kSimt>(a, b, split, grid, early, stream);
   }
 }
@@ -3666,6 +3762,7 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
       case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, -1, grid_all, false, stream);
       case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, -1, grid_all, false, stream);
       case MoverBody::kMedium: return launch_pair_b<MoverBody::kMedium>(body_b, a, b, -1, grid_all, false, stream);
+      case MoverBody::kSplit: return launch_pair_b<MoverBody::kSplit>(body_b, a, b, -1, grid_all, false, stream);
       default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, -1, grid_all, false, stream);
     }
   }
@@ -3685,6 +3782,7 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
     case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, split, grid, early, stream);
     case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, split, grid, early, stream);
     case MoverBody::kMedium: return launch_pair_b<MoverBody::kMedium>(body_b, a, b, split, grid, early, stream);
+    case MoverBody::kSplit: return launch_pair_b<MoverBody::kSplit>(body_b, a, b, split, grid, early, stream);
     default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, split, grid, early, stream);
   }
 }
