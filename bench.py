@@ -1121,9 +1121,10 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
             "unit": "GB/s",
             "frac": round(cyc_moved / (ms / 1e3) / 1e9 / peak, 4),
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-            "traffic": None,
-            "kernel": "move_pair_all_kernel (one launch per decode step; the cycle's booking runs beside the "
-                      "cycle's launches on another stream), timed over whole graph replays",
+            "traffic": _traffic_per_launch("decode-mix-8heads") if heads == 8 else None,
+            "kernel": f"{'move_pair_all_kernel' if heads == 8 else 'move_pair_kernel'} (one launch per decode step; "
+                      "the cycle's booking runs beside the cycle's launches on another stream), timed over whole "
+                      "graph replays",
             "algorithmic_bytes_per_decode_step": 2 * mix.num_planes * (mix.seqs * row_bytes +
                                                                        per_cycle // 16 * row_bytes * mix.block_size),
         },

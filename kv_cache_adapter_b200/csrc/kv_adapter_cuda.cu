@@ -2937,14 +2937,44 @@ __global__ void __launch_bounds__(kMoverThreads)
                                             static_cast<int64_t>(gridDim.x) - split);
 }
 
+// Build knobs of the all-CTA pair kernel (sweeps): KVCA_PAIR_ALL_PDL=1
+// launches it as a programmatic dependent (with KVCA_FLAG_INPUTS_READY the
+// next launch is let in at once and only paged loads and stores wait);
+// KVCA_PAIR_ALL_MIN_CTAS=2 bounds its registers so that two 512-thread CTAs
+// (or one beside another kernel's CTA of up to 32K registers) fit on an SM;
+// KVCA_PAIR_ALL_GRID_PER_SM sets the CTAs launched per SM.  B200, decode
+// step with 8 KV heads (64 MiB each way), live decode mix / the cycle's 16
+// pair launches replayed alone: plain launch 24.7 / 23.4 us per step,
+// programmatic dependent 23.2 / 21.6 us; 64 registers (spills) 25.9 / 25.4
+// with one CTA per SM, 26.7 / 25.9 with two, 24.8 / 23.8 with two and the
+// programmatic launch.
+#ifndef KVCA_PAIR_ALL_PDL
+#define KVCA_PAIR_ALL_PDL 1
+#endif
+#ifndef KVCA_PAIR_ALL_MIN_CTAS
+#define KVCA_PAIR_ALL_MIN_CTAS 1
+#endif
+#ifndef KVCA_PAIR_ALL_GRID_PER_SM
+#define KVCA_PAIR_ALL_GRID_PER_SM 1
+#endif
+constexpr bool kPairAllPdl = KVCA_PAIR_ALL_PDL != 0;
+constexpr int kPairAllGridPerSm = KVCA_PAIR_ALL_GRID_PER_SM;
+
 // Two large independent moves in one launch: every CTA moves its share of
 // the scatter, then its share of the gather, so the two share one ramp and
-// one tail and every SM carries both.
-template <MoverBody kA, MoverBody kB>
-__global__ void __launch_bounds__(kMoverThreads)
+// one tail and every SM carries both.  kEarly as in move_pair_kernel (only
+// when launched as a programmatic dependent).
+template <MoverBody kA, MoverBody kB, bool kEarly>
+__global__ void __launch_bounds__(kMoverThreads, KVCA_PAIR_ALL_MIN_CTAS)
     move_pair_all_kernel(const __grid_constant__ MoveParams a, const __grid_constant__ MoveParams b) {
-  run_mover_body<kA, false, true, false>(a, blockIdx.x, gridDim.x);
-  run_mover_body<kB, true, false, false>(b, blockIdx.x, gridDim.x);
+  if constexpr (kPairAllPdl) {
+    if constexpr (kEarly)
+      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    else
+      dependent_launch_entry();
+  }
+  run_mover_body<kA, false, true, kEarly>(a, blockIdx.x, gridDim.x);
+  run_mover_body<kB, true, false, kEarly>(b, blockIdx.x, gridDim.x);
 }
 
 // Launch as a programmatic dependent of the kernel before it on the stream
@@ -3676,7 +3706,14 @@ template <MoverBody kA, MoverBody kB>
 cudaError_t launch_pair_typed(const MoveParams& a, const MoveParams& b, int split, int grid, bool early,
                               cudaStream_t stream) {
   if (split < 0) {  // large: every CTA takes part in both moves
-    move_pair_all_kernel<kA, kB><<<static_cast<unsigned>(grid), kMoverThreads, 0, stream>>>(a, b);
+    if constexpr (kPairAllPdl) {
+      if (early)
+        return launch_dependent(move_pair_all_kernel<kA, kB, true>, static_cast<unsigned>(grid), kMoverThreads,
+                                0, stream, a, b);
+      return launch_dependent(move_pair_all_kernel<kA, kB, false>, static_cast<unsigned>(grid), kMoverThreads, 0,
+                              stream, a, b);
+    }
+    move_pair_all_kernel<kA, kB, false><<<static_cast<unsigned>(grid), kMoverThreads, 0, stream>>>(a, b);
     return cudaGetLastError();
   }
   if (early)
@@ -3731,10 +3768,14 @@ cudaError_t launch_move(const MoveArgs& a, cudaStream_t stream) {
 // Up to this many bytes moved by the two together, the CTAs are split
 // between the moves (each move's chain of loads runs once, side by side);
 // above it every CTA takes part in both, one after the other (a decode step
-// with 8 KV heads, 64 MiB each way, B200: 32.2 us per step split, 29.3 all
-// CTAs in both, 29.6 as two launches; with 1 KV head, 4 MiB each way: 6.0 us
-// split against 10.4 as two launches).
-constexpr double kPairMaxBytes = 32.0 * 1024 * 1024;
+// with 8 KV heads, 64 MiB each way, B200, both on the SIMT body and as
+// plain launches: 32.2 us per step split, 29.3 all CTAs in both, 29.6 as
+// two launches; with 1 KV head, 4 MiB each way: 6.0 us split against 10.4
+// as two launches).  KVCA_PAIR_MAX_MIB sets it for sweeps.
+#ifndef KVCA_PAIR_MAX_MIB
+#define KVCA_PAIR_MAX_MIB 32
+#endif
+constexpr double kPairMaxBytes = static_cast<double>(KVCA_PAIR_MAX_MIB) * 1024 * 1024;
 
 cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gather, cudaStream_t stream) {
   const double bytes_a = static_cast<double>(scatter.num_planes) * scatter.num_rows * scatter.row_bytes;
@@ -3755,15 +3796,16 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   int64_t want_a = 1, want_b = 1;
   const MoverBody body_a = pair_body(&a, &want_a);
   const MoverBody body_b = pair_body(&b, &want_b);
+  const bool early = ((scatter.flags & gather.flags) & KVCA_FLAG_INPUTS_READY) != 0;
   if (bytes_a + bytes_b > kPairMaxBytes) {  // every CTA takes part in both
     const int sms_all = device_sm_count();
-    const int grid_all = sms_all > 0 ? sms_all : 1;
+    const int grid_all = sms_all > 0 ? sms_all * kPairAllGridPerSm : 1;
     switch (body_a) {
-      case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, -1, grid_all, false, stream);
-      case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, -1, grid_all, false, stream);
-      case MoverBody::kMedium: return launch_pair_b<MoverBody::kMedium>(body_b, a, b, -1, grid_all, false, stream);
-      case MoverBody::kSplit: return launch_pair_b<MoverBody::kSplit>(body_b, a, b, -1, grid_all, false, stream);
-      default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, -1, grid_all, false, stream);
+      case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, -1, grid_all, early, stream);
+      case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, -1, grid_all, early, stream);
+      case MoverBody::kMedium: return launch_pair_b<MoverBody::kMedium>(body_b, a, b, -1, grid_all, early, stream);
+      case MoverBody::kSplit: return launch_pair_b<MoverBody::kSplit>(body_b, a, b, -1, grid_all, early, stream);
+      default: return launch_pair_b<MoverBody::kSimt>(body_b, a, b, -1, grid_all, early, stream);
     }
   }
   // CTAs split by bytes over the resident grid (one CTA of 512 threads per SM)
@@ -3777,7 +3819,6 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   if (cb > want_b) cb = want_b > 0 ? want_b : 1;
   const int split = static_cast<int>(ca);
   const int grid = static_cast<int>(ca + cb);
-  const bool early = ((scatter.flags & gather.flags) & KVCA_FLAG_INPUTS_READY) != 0;
   switch (body_a) {
     case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, split, grid, early, stream);
     case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, split, grid, early, stream);

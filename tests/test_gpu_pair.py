@@ -108,18 +108,20 @@ def test_pair_bad_gather_id_raises(ops):
     ops.check_status(DEV)  # the error was consumed by the raise
 
 
-@pytest.mark.parametrize("row", [256, 64, 2048])
-def test_pair_chain_with_inputs_ready(ops, row):
+@pytest.mark.parametrize("row,planes,per", [(256, 8, 4), (64, 8, 4), (2048, 8, 4), (2048, 64, 16)])
+def test_pair_chain_with_inputs_ready(ops, row, planes, per):
     """A chain of paired launches with inputs_ready (each reads its indices and
     token rows while the previous one drains): launch k + 1's gather reads the
     blocks launch k's scatter just wrote, so its paged reads must wait; the
-    bytes must equal the oracle's moves applied in order."""
+    bytes must equal the oracle's moves applied in order.  Groups of `per`
+    blocks; 64 planes x 16 blocks of 2 KiB rows moves 64 MiB per launch
+    (every CTA in both moves, the decode step with 8 KV heads)."""
     gen = torch.Generator().manual_seed(row)
-    planes, nb, bs, launches = 8, 64, 16, 8
+    nb, bs, launches = 16 * per, 16, 8
     kv = torch.randint(0, 256, (planes, nb, bs, row), generator=gen, dtype=torch.uint8)
-    groups = torch.randperm(nb, generator=gen)[: 4 * (launches + 1)].reshape(launches + 1, 4)
+    groups = torch.randperm(nb, generator=gen)[: per * (launches + 1)].reshape(launches + 1, per)
     slots = [(g.reshape(-1, 1) * bs + torch.arange(bs).reshape(1, -1)).reshape(-1) for g in groups]
-    rows = [torch.randint(0, 256, (1, planes, 4 * bs, row), generator=gen, dtype=torch.uint8)
+    rows = [torch.randint(0, 256, (1, planes, per * bs, row), generator=gen, dtype=torch.uint8)
             for _ in range(launches)]
     kv_d = kv.to(DEV)
     token_planes = [kv_d[p] for p in range(planes)]
@@ -127,18 +129,18 @@ def test_pair_chain_with_inputs_ready(ops, row):
     slots_d = [s.to(DEV) for s in slots]
     ids_d = [g.to(DEV) for g in groups]
     rows_d = [r.to(DEV) for r in rows]
-    outs = [torch.empty((4, planes, 1, bs * row), dtype=torch.uint8, device=DEV) for _ in range(launches)]
+    outs = [torch.empty((per, planes, 1, bs * row), dtype=torch.uint8, device=DEV) for _ in range(launches)]
     torch.cuda.synchronize()
     for k in range(launches):  # scatter into group k, gather group k (written by launch k - 1's scatter)
         ops.scatter_tokens_gather_layers(token_planes, slots_d[k], rows_d[k],
                                          block_planes, ids_d[k - 1] if k else ids_d[launches], outs[k],
-                                         tokens_per_chunk=4 * bs, blocks_per_chunk=1, inputs_ready=True)
+                                         tokens_per_chunk=per * bs, blocks_per_chunk=1, inputs_ready=True)
     torch.cuda.synchronize()
     ops.check_status(DEV)
     ref = kv.clone()
     for k in range(launches):
         gid = groups[k - 1] if k else groups[launches]
         want = moves.gather_layers([ref[p].reshape(nb, bs * row) for p in range(planes)], gid, blocks_per_chunk=1)
-        moves.scatter_tokens([ref[p] for p in range(planes)], slots[k], rows[k], tokens_per_chunk=4 * bs)
+        moves.scatter_tokens([ref[p] for p in range(planes)], slots[k], rows[k], tokens_per_chunk=per * bs)
         assert _same(outs[k], want), k
     assert _same(kv_d, ref)
