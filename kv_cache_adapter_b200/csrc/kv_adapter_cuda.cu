@@ -2957,6 +2957,17 @@ __global__ void __launch_bounds__(kMoverThreads)
 #ifndef KVCA_PAIR_ALL_GRID_PER_SM
 #define KVCA_PAIR_ALL_GRID_PER_SM 1
 #endif
+// The pair kernel's grid leaves KVCA_PAIR_SPARE_SMS SMs out.  Its CTAs
+// split the work statically and fill every SM with one 512-thread CTA, so a
+// kernel holding one SM meanwhile (a decode loop's one-CTA booking launch on
+// another stream) would leave one CTA waiting for a whole share: the step
+// then takes up to twice as long.  B200, decode mix with 8 KV heads, booking
+// beside the moves: 23.2 us per step with every SM, 21.8 with one spare, 21.7
+// with two; the pair launches alone 21.6 / 21.7 / 21.7 us; one KV head 5.3 us
+// live and 4.6 alone either way.
+#ifndef KVCA_PAIR_SPARE_SMS
+#define KVCA_PAIR_SPARE_SMS 1
+#endif
 constexpr bool kPairAllPdl = KVCA_PAIR_ALL_PDL != 0;
 constexpr int kPairAllGridPerSm = KVCA_PAIR_ALL_GRID_PER_SM;
 
@@ -3799,7 +3810,8 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   const bool early = ((scatter.flags & gather.flags) & KVCA_FLAG_INPUTS_READY) != 0;
   if (bytes_a + bytes_b > kPairMaxBytes) {  // every CTA takes part in both
     const int sms_all = device_sm_count();
-    const int grid_all = sms_all > 0 ? sms_all * kPairAllGridPerSm : 1;
+    const int grid_all =
+        sms_all > KVCA_PAIR_SPARE_SMS ? (sms_all - KVCA_PAIR_SPARE_SMS) * kPairAllGridPerSm : 1;
     switch (body_a) {
       case MoverBody::kStream: return launch_pair_b<MoverBody::kStream>(body_b, a, b, -1, grid_all, early, stream);
       case MoverBody::kSmall: return launch_pair_b<MoverBody::kSmall>(body_b, a, b, -1, grid_all, early, stream);
@@ -3810,7 +3822,7 @@ cudaError_t launch_scatter_gather(const MoveArgs& scatter, const MoveArgs& gathe
   }
   // CTAs split by bytes over the resident grid (one CTA of 512 threads per SM)
   const int sms = device_sm_count();
-  const int64_t grid_max = sms > 1 ? sms : 2;
+  const int64_t grid_max = sms - KVCA_PAIR_SPARE_SMS > 1 ? sms - KVCA_PAIR_SPARE_SMS : 2;
   int64_t ca = static_cast<int64_t>(grid_max * bytes_a / (bytes_a + bytes_b) + 0.5);
   if (ca < 1) ca = 1;
   if (ca > grid_max - 1) ca = grid_max - 1;
