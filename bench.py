@@ -1052,19 +1052,21 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     row_bytes = heads * 128 * 2
     moved = 2 * mix.num_planes * (tokens * row_bytes + blocks * row_bytes * mix.block_size)
     del graph
-    # whole-cycle booking: one append_steps launch books the 16 steps of the
-    # next cycle while the current cycle's moves run; a replay = 2 cycles.
-    # First each step's scatter paired with the next step's gather (one launch
-    # per decode step), then each cycle's moves as one move_cycle launch.
+    # whole-cycle booking: one append_steps launch books the 16 steps of a
+    # later cycle while the current cycle's moves run; a replay =
+    # DecodeMix.CYCLE_BUFFERS cycles.  First each step's scatter paired with
+    # the next step's gather (one launch per decode step), then each cycle's
+    # moves as one move_cycle launch.
     mix.pipelined = False
-    replays = -(-cycles // 2)
-    cyc_steps = 2 * replays * 16
+    cpr = mix.CYCLE_BUFFERS
+    replays = -(-cycles // cpr)
+    cyc_steps = cpr * replays * 16
     results = {}
     for one_launch in (False, True):
         mix.start_cycles(one_launch=one_launch)
         mix.run_cycle(cycle_rows)
-        graph, per_two = mix.capture_cycles(cycle_rows)
-        assert per_two == 2 * per_cycle
+        graph, per_replay = mix.capture_cycles(cycle_rows)
+        assert per_replay == cpr * per_cycle
         with ClockSampler(device.index) as clk:
             results[one_launch] = (timed(lambda: [graph.replay() for _ in range(replays)]), clk)
         del graph
@@ -1076,7 +1078,7 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     # launches per cycle: the booking, then one per step (the token scatter
     # with the next step's spill gather)
     cycle_launches = 1 + 16
-    cyc_moved = 2 * mix.num_planes * (cyc_steps * mix.seqs * row_bytes + replays * per_two * row_bytes * mix.block_size)
+    cyc_moved = 2 * mix.num_planes * (cyc_steps * mix.seqs * row_bytes + replays * per_replay * row_bytes * mix.block_size)
     if rank != 0:
         return
     decode_steps = cycles * 16
@@ -1104,15 +1106,16 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
                         f"spill gather when a block fills",
             "parallelism": f"kv-head shard x{world}, no data-path collective",
         },
-        "gpu_launches": replays * 2 * cycle_launches,
+        "gpu_launches": replays * cpr * cycle_launches,
         "tokens_per_s": round(world * cyc_steps * mix.seqs / (ms / 1e3), 1),
-        "evictions_per_s": round(world * replays * per_two / (ms / 1e3), 1),
+        "evictions_per_s": round(world * replays * per_replay / (ms / 1e3), 1),
         "gpu_launches_per_decode_step": "one scatter_tokens_gather_layers launch (this step's token scatter with the "
                                         "next step's spill gather) plus 1/16 of an append_steps launch (pop, commit, "
                                         "release, slot_mapping of 16 steps)",
-        "issue": "CUDA graph, one replay per two 16-step cycles; the bookkeeping of the next cycle (one "
-                 "append_steps launch) on a second stream, overlapping the current cycle's moves (victims and "
-                 "slot_mappings double-buffered by cycle); each step's moves are one launch, issued as the step comes",
+        "issue": f"CUDA graph, one replay per {cpr} 16-step cycles; the bookkeeping of each later cycle (one "
+                 "append_steps launch) on a second stream, overlapping the current cycle's moves and up to two "
+                 f"cycles ahead of them (victims and slot_mappings in {cpr} buffers by cycle); each step's moves "
+                 "are one launch, issued as the step comes",
         "token_rows": "a new row per sequence, plane and step (16 steps' rows in HBM)",
         "roofline": {
             "bound": "hbm",

@@ -142,6 +142,17 @@ __device__ __forceinline__ void store_meta_vec(MetaT* meta, int64_t num_slots, i
   }
 }
 
+// Vector v of a shared-memory copy of the table (padded to whole vectors).
+template <typename MetaT>
+__device__ __forceinline__ void load_mirror_vec(const MetaT* mirror, int64_t v, MetaVec<MetaT>& out) {
+  out.raw = *reinterpret_cast<const uint4*>(mirror + v * Meta<MetaT>::kSlotsPerVec);
+}
+
+template <typename MetaT>
+__device__ __forceinline__ void store_mirror_vec(MetaT* mirror, int64_t v, const MetaVec<MetaT>& in) {
+  *reinterpret_cast<uint4*>(mirror + v * Meta<MetaT>::kSlotsPerVec) = in.raw;
+}
+
 // Blocked-slot bits for the kSlotsPerVec slots starting at `first` (a
 // multiple of kSlotsPerVec, so they share one 32-bit bitmap word).  The
 // bitmap is written with atomics earlier in the same CTA; read it through L2.
@@ -188,7 +199,10 @@ struct PopShared {
 // sh.last_slot (pop_start) and passed a barrier since, so the read of
 // *search_start can overlap the caller's own loads.  out_sh (optional, in
 // shared memory): victims 0..out_sh_cap-1 are also written there, so the
-// caller reads them without a global round trip.
+// caller reads them without a global round trip.  mirror (optional, in
+// shared memory): a copy of the whole table padded to whole vectors, equal
+// to it on entry; the scans read it instead of global memory and the aging
+// writes go to both.
 template <typename MetaT>
 __device__ __forceinline__ void pop_start(const int64_t* search_start, int64_t n, PopShared<MetaT>& sh) {
   long long s = static_cast<long long>(*search_start % n);
@@ -201,7 +215,7 @@ template <typename MetaT>
 __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
                        const uint32_t* bitmap, int64_t count, int64_t* out, int order,
                        bool aligned, PopShared<MetaT>& sh, bool start_set = false,
-                       int64_t* out_sh = nullptr, int64_t out_sh_cap = 0) {
+                       int64_t* out_sh = nullptr, int64_t out_sh_cap = 0, MetaT* mirror = nullptr) {
   using M = Meta<MetaT>;
   constexpr int kSpv = M::kSlotsPerVec;
   const int64_t n = num_slots;
@@ -226,7 +240,10 @@ __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
       unsigned mask = 0u;
       if (v < v_end) {
         MetaVec<MetaT> m;
-        load_meta_vec(meta, n, v, aligned, m);
+        if (mirror != nullptr)
+          load_mirror_vec(mirror, v, m);
+        else
+          load_meta_vec(meta, n, v, aligned, m);
         const unsigned blk = blocked_bits<MetaT>(bitmap, v * kSpv);
 #pragma unroll
         for (int j = 0; j < kSpv; ++j) {
@@ -275,7 +292,10 @@ __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
       MetaVec<MetaT> m;
       unsigned blk = 0u;
       if (v < nvec) {
-        load_meta_vec(meta, n, v, aligned, m);
+        if (mirror != nullptr)
+          load_mirror_vec(mirror, v, m);
+        else
+          load_meta_vec(meta, n, v, aligned, m);
         blk = blocked_bits<MetaT>(bitmap, v * kSpv);
       }
 #pragma unroll
@@ -325,7 +345,10 @@ __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
       MetaVec<MetaT> m;
       unsigned avail_mask = 0u;  // in segment, unpinned, not blocked
       if (active) {
-        load_meta_vec(meta, n, v, aligned, m);
+        if (mirror != nullptr)
+          load_mirror_vec(mirror, v, m);
+        else
+          load_meta_vec(meta, n, v, aligned, m);
         const unsigned blk = blocked_bits<MetaT>(bitmap, v * kSpv);
         MetaVec<MetaT> aged;
 #pragma unroll
@@ -339,6 +362,7 @@ __device__ int pop_cta(MetaT* meta, int64_t num_slots, int64_t* search_start,
           aged.s[j] = in_seg ? M::pack(M::pin(w), u_aged) : m.s[j];
         }
         store_meta_vec(meta, n, v, aligned, aged);
+        if (mirror != nullptr) store_mirror_vec(mirror, v, aged);
       }
       if (order == KVCA_POP_ORDER_GROUPED) {
         for (int c = 1; c <= threshold; ++c) {
@@ -1770,7 +1794,7 @@ __device__ int append_step_body(MetaT* meta, int64_t n, int64_t* search_start, i
                                 int64_t* cur_block, int64_t* cur_logical, int64_t* pos,
                                 int64_t seqs, int64_t block_size, int64_t* next_logical, int order,
                                 bool aligned, int64_t* victims, int64_t* slot_mapping,
-                                int64_t* status, AppendShared<MetaT>& sh) {
+                                int64_t* status, AppendShared<MetaT>& sh, MetaT* mirror = nullptr) {
   using M = Meta<MetaT>;
   const int64_t base = *next_logical;
   if (c > 0 && threadIdx.x == 0) pop_start(search_start, n, sh.pop);
@@ -1817,7 +1841,7 @@ __device__ int append_step_body(MetaT* meta, int64_t n, int64_t* search_start, i
   }
   if (c > 0) {
     const int rc = pop_cta<MetaT>(meta, n, search_start, nullptr, c, victims, order, aligned, sh.pop,
-                                  true, sh.victims, kAppendThreads);
+                                  true, sh.victims, kAppendThreads, mirror);
     if (rc != KVCA_OK) {
       if (threadIdx.x == 0) report(status, rc, c);
       return rc;
@@ -1832,12 +1856,18 @@ __device__ int append_step_body(MetaT* meta, int64_t n, int64_t* search_start, i
       const int64_t full = j == threadIdx.x ? my_full : l2p[cur_logical[q]];
       const int64_t v = j < kAppendThreads ? sh.victims[j] : victims[j];
       const int64_t prev = p2l[v];
-      const unsigned w = meta[full];
+      const unsigned w = mirror != nullptr ? mirror[full] : meta[full];
       if (prev >= 0) l2p[prev] = -1;
       l2p[base + j] = v;
       p2l[v] = base + j;
-      meta[v] = M::pack(1, 1);
-      meta[full] = M::pack(static_cast<int64_t>(M::pin(w)) - 1, M::usage(w));
+      const MetaT fresh = M::pack(1, 1);
+      const MetaT released = M::pack(static_cast<int64_t>(M::pin(w)) - 1, M::usage(w));
+      meta[v] = fresh;
+      meta[full] = released;
+      if (mirror != nullptr) {
+        mirror[v] = fresh;
+        mirror[full] = released;
+      }
       cur_block[q] = v;
       cur_logical[q] = base + j;
     }
@@ -1884,6 +1914,17 @@ __global__ void __launch_bounds__(kAppendThreads)
 constexpr int64_t kAppendSmemSeqs = 4096;
 constexpr int64_t kAppendSmemNeed = 4096;
 constexpr size_t kAppendSmemBytes = (3 * kAppendSmemSeqs + kAppendSmemNeed) * sizeof(int64_t);
+// The slot table itself is mirrored in shared memory after that state when
+// both fit in kAppendDynMax bytes (a 65,536-slot 8-bit table is 64 KiB): it
+// is read once per launch, every pop scans the copy, and every metadata
+// write goes to both, so a step's chain loses the round trip of the pop's
+// table reads (B200, decode mix with one KV head and a 65,536-block pool:
+// the 16-step booking launch takes 84 us without the copy).
+constexpr size_t kAppendDynMax = 200 * 1024;
+#ifndef KVCA_APPEND_MIRROR
+#define KVCA_APPEND_MIRROR 1
+#endif
+constexpr bool kAppendMirror = KVCA_APPEND_MIRROR != 0;
 
 // num_steps steps in a row in one CTA: step s takes need[off[s]..off[s+1]),
 // writes its victims to victims[off[s]..] and its slot_mapping to
@@ -1907,10 +1948,31 @@ __global__ void __launch_bounds__(kAppendThreads, KVCA_APPEND_MIN_CTAS)
                         const int64_t* need_offsets, int64_t num_need, int64_t num_steps,
                         int64_t* cur_block, int64_t* cur_logical, int64_t* pos, int64_t seqs,
                         int64_t block_size, int64_t* next_logical, int order, bool aligned,
-                        int64_t* victims, int64_t* slot_mapping, int64_t* status, bool staged) {
+                        int64_t* victims, int64_t* slot_mapping, int64_t* status, bool staged,
+                        int64_t mirror_off) {
   __shared__ AppendShared<MetaT> sh;
   __shared__ int64_t off[kAppendMaxSteps + 1];
-  extern __shared__ int64_t dyn[];  // staged: block | logical id | position (seqs each), need entries
+  // staged: block | logical id | position (seqs each), need entries; then,
+  // from byte mirror_off (16-byte aligned; -1: none), the table's copy
+  extern __shared__ __align__(16) int64_t dyn[];
+  MetaT* mirror = mirror_off >= 0 ? reinterpret_cast<MetaT*>(reinterpret_cast<char*>(dyn) + mirror_off) : nullptr;
+  if (mirror != nullptr) {  // issued first: its loads overlap the offset checks
+    const int64_t nvec = (n + Meta<MetaT>::kSlotsPerVec - 1) / Meta<MetaT>::kSlotsPerVec;
+    constexpr int kBatch = 8;  // vectors in flight per thread
+    for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += kBatch * static_cast<int64_t>(blockDim.x)) {
+      MetaVec<MetaT> m[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t v = v0 + u * static_cast<int64_t>(blockDim.x);
+        if (v < nvec) load_meta_vec(meta, n, v, aligned, m[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int64_t v = v0 + u * static_cast<int64_t>(blockDim.x);
+        if (v < nvec) store_mirror_vec(mirror, v, m[u]);
+      }
+    }
+  }
   bool bad = false;
   for (int64_t s = threadIdx.x; s <= num_steps; s += blockDim.x) {
     const int64_t o = need_offsets[s];
@@ -1960,7 +2022,7 @@ __global__ void __launch_bounds__(kAppendThreads, KVCA_APPEND_MIN_CTAS)
     const int rc = append_step_body<MetaT>(meta, n, search_start, l2p, n_logical, p2l,
                                            nd + (o - nd_base), off[s + 1] - o, cb, cl, ps, seqs,
                                            block_size, next_logical, order, aligned, victims + o,
-                                           slot_mapping + s * seqs, status, sh);
+                                           slot_mapping + s * seqs, status, sh, mirror);
     __syncthreads();
     if (rc != KVCA_OK) break;  // uniform across the CTA
   }
@@ -5096,15 +5158,22 @@ cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t nu
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(append_steps_kernel<uint8_t>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kAppendSmemBytes));
+                                         static_cast<int>(kAppendDynMax));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(append_steps_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kAppendSmemBytes));
+                               static_cast<int>(kAppendDynMax));
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  static_assert(kAppendSmemBytes <= kAppendDynMax, "the staged state always fits");
   const bool staged = num_seqs <= kAppendSmemSeqs;
-  const size_t smem = staged ? static_cast<size_t>(3 * num_seqs + kAppendSmemNeed) * sizeof(int64_t) : 0;
+  const size_t staged_bytes = staged ? static_cast<size_t>(3 * num_seqs + kAppendSmemNeed) * sizeof(int64_t) : 0;
+  const size_t mirror_at = (staged_bytes + 15) / 16 * 16;
+  const size_t meta_bytes = meta_bits == 16 ? sizeof(uint16_t) : sizeof(uint8_t);
+  const size_t mirror_bytes = (static_cast<size_t>(num_slots) * meta_bytes + 15) / 16 * 16;
+  const bool mirrored = kAppendMirror && num_slots > 0 && mirror_at + mirror_bytes <= kAppendDynMax;
+  const size_t smem = mirrored ? mirror_at + mirror_bytes : staged_bytes;
+  const int64_t mirror_off = mirrored ? static_cast<int64_t>(mirror_at) : -1;
   // launches of at most kAppendMaxSteps steps, in stream order
   for (int64_t s0 = 0; s0 < num_steps; s0 += kAppendMaxSteps) {
     const int64_t k = num_steps - s0 < kAppendMaxSteps ? num_steps - s0 : kAppendMaxSteps;
@@ -5113,7 +5182,7 @@ cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t nu
                                       num_logical, p2l, need, need_offsets + s0, num_need, k,
                                       cur_block, cur_logical, pos, num_seqs, block_size,
                                       next_logical, order, aligned, victims,
-                                      slot_mapping + s0 * num_seqs, status, staged));
+                                      slot_mapping + s0 * num_seqs, status, staged, mirror_off));
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

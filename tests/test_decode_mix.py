@@ -197,32 +197,41 @@ def test_cycle_booking_matches_single_steps(cfg, one_launch):
     cyc.start_cycles(one_launch=one_launch)
     cyc.run_cycle(rows)
     graph, per_replay = cyc.capture_cycles(rows)
-    assert per_replay == 2 * cfg["seqs"]
+    cpr = cyc.CYCLE_BUFFERS
+    assert per_replay == cpr * cfg["seqs"]
     replays = 2 if cfg is SMALL else 1
     for _ in range(replays):
         graph.replay()
     cyc.stop_cycles(rows)
     for _ in range(3):
         cyc.step(rows)
-    for _ in range((2 + 2 * replays) * bs + 3):
+    for _ in range((2 + cpr * replays) * bs + 3):
         ref.step(rows)
     torch.cuda.synchronize()
     cuda_ops.check_status(dev)
     cyc.evictions += replays * per_replay  # graph replays are not counted on the host
-    cyc.tokens += replays * 2 * bs * cfg["seqs"]
+    cyc.tokens += replays * cpr * bs * cfg["seqs"]
     _assert_same_state(ref, cyc)
 
 
 @pytest.mark.gpu
-def test_append_steps_equals_single_steps_across_launches():
-    """300 steps in one append_steps call (two launches of at most 256 steps)
-    against 300 append_step calls: victims, slot mappings and state."""
+@pytest.mark.parametrize("bits", [8, 16])
+def test_append_steps_equals_single_steps_across_launches(bits):
+    """300 steps in one append_steps call (two launches of at most 256 steps,
+    the slot table copied into shared memory) against 300 append_step calls
+    (table in global memory): victims, slot mappings and state, with 8- and
+    16-bit slot words."""
     from kv_cache_adapter_b200 import kv_cache_adapter_cuda as ops
 
     dev = torch.device("cuda", 0)
     cfg = dict(layers=1, heads=1, head_dim=8, block_size=4, num_blocks=2048, seqs=100, max_steps=320)
     a = DecodeMix(ops, dev, **cfg)
     b = DecodeMix(ops, dev, **cfg)
+    if bits == 16:  # the same pins and usage counts in 16-bit words (8-bit fields)
+        w = a.slot_meta.cpu().numpy().astype(np.uint16)
+        w16 = torch.from_numpy((w & 15) | ((w >> 4) << 8))
+        a.slot_meta = w16.to(dev)
+        b.slot_meta = w16.to(dev)
     steps = 300
     pos = a.pos.copy()
     needs, offs = [], [0]
