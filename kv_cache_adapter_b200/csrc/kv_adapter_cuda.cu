@@ -22,6 +22,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
 #include <utility>
 
 #include "kvca_launch.h"
@@ -3077,6 +3078,23 @@ int device_sm_count() {
   return sms;
 }
 
+// Function attributes (the dynamic shared-memory limit, the carve-out)
+// belong to the current device's context, so a launcher sets them once per
+// device: `done` records the ordinals done (devices past the table are set
+// up on every call).
+constexpr int kTrackedDevices = 64;
+using DeviceFlags = std::atomic<bool>[kTrackedDevices];
+
+bool needs_setup(const DeviceFlags& done, int* dev) {
+  *dev = -1;
+  if (cudaGetDevice(dev) != cudaSuccess) return true;
+  return *dev < 0 || *dev >= kTrackedDevices || !done[*dev].load(std::memory_order_acquire);
+}
+
+void mark_setup(DeviceFlags& done, int dev) {
+  if (dev >= 0 && dev < kTrackedDevices) done[dev].store(true, std::memory_order_release);
+}
+
 template <bool kSrcPaged, bool kDstPaged, typename V, bool kHost = false>
 cudaError_t launch_move_typed(const MoveParams& p, cudaStream_t stream) {
   auto kernel = move_rows_kernel<kSrcPaged, kDstPaged, V, kHost>;
@@ -3451,12 +3469,13 @@ cudaError_t launch_move_bulk(const MoveParams& base, cudaStream_t stream) {
   if (stages < 2) stages = 2;
   const int smem = static_cast<int>(stages * seg_bytes);
   auto kernel = move_rows_bulk_kernel<kSrcPaged, kDstPaged>;
-  static bool configured = false;
-  if (!configured) {
+  static DeviceFlags configured;
+  int dev = -1;
+  if (needs_setup(configured, &dev)) {
     const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(kBulkMaxStages * kBulkSegmentBytes));
     if (e != cudaSuccess) return e;
-    configured = true;
+    mark_setup(configured, dev);
   }
   const int sms = device_sm_count();
   const int64_t items = p.num_planes * p.num_rows * p.segs_per_row;
@@ -3648,13 +3667,16 @@ cudaError_t launch_move_staged(const MoveParams& p, cudaStream_t stream) {
   const void* kernel = reinterpret_cast<const void*>(move_rows_staged_gather_kernel);
   const size_t smem = static_cast<size_t>(kStagedStages) * kStagedTileBytes;
   static int blocks_per_sm = 0;
-  if (blocks_per_sm == 0) {
+  static DeviceFlags configured;
+  int dev = -1;
+  if (needs_setup(configured, &dev)) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     int b = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kStagedThreads, smem);
     if (e != cudaSuccess) return e;
     blocks_per_sm = b > 0 ? b : 1;
+    mark_setup(configured, dev);
   }
   const int sms = device_sm_count();
   int64_t blocks = static_cast<int64_t>(sms > 0 ? sms : 1) * blocks_per_sm;
@@ -4502,8 +4524,9 @@ cudaError_t launch_move_cycle(const CycleArgs& a, cudaStream_t stream) {
   p.wmask = reinterpret_cast<unsigned long long*>(a.scratch + kCycleHeaderBytes);
   p.pmask = p.wmask + a.cache->num_blocks;
   p.status = a.status;
-  static bool configured = false;
-  if (!configured) {
+  static DeviceFlags configured;
+  int dev = -1;
+  if (needs_setup(configured, &dev)) {
     cudaError_t e = cudaFuncSetAttribute(move_cycle_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kCycleSmemBytes));
     if (e != cudaSuccess) return e;
@@ -4516,7 +4539,7 @@ cudaError_t launch_move_cycle(const CycleArgs& a, cudaStream_t stream) {
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, move_cycle_kernel, kCycleThreads, kCycleSmemBytes);
     if (e2 != cudaSuccess) return e2;
     if (b < 1) return cudaErrorInvalidConfiguration;
-    configured = true;
+    mark_setup(configured, dev);
   }
   int sms = device_sm_count();
   if (sms < 1) sms = 1;
@@ -5154,8 +5177,9 @@ cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t nu
                                 int64_t block_size, int64_t* next_logical, int64_t* victims,
                                 int64_t* slot_mapping, int64_t* status, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(meta) & 15u) == 0u;
-  static bool configured = false;
-  if (!configured) {
+  static DeviceFlags configured;
+  int dev = -1;
+  if (needs_setup(configured, &dev)) {
     cudaError_t e = cudaFuncSetAttribute(append_steps_kernel<uint8_t>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kAppendDynMax));
@@ -5163,7 +5187,7 @@ cudaError_t launch_append_steps(int meta_bits, int order, void* meta, int64_t nu
       e = cudaFuncSetAttribute(append_steps_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kAppendDynMax));
     if (e != cudaSuccess) return e;
-    configured = true;
+    mark_setup(configured, dev);
   }
   static_assert(kAppendSmemBytes <= kAppendDynMax, "the staged state always fits");
   const bool staged = num_seqs <= kAppendSmemSeqs;
