@@ -1006,7 +1006,7 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     pool = args.pool_blocks or 65536
     mix = DecodeMix(ops, device, layers=32, heads=heads, head_dim=128, block_size=16, num_blocks=pool,
                     seqs=256, dtype=torch.float16, seed=1234 + rank,
-                    max_steps=(args.warmup * per + 17) + 5 * (cycles + 4) * 16 + 256)  # warm-up + 5 timed runs
+                    max_steps=(args.warmup * per + 17) + 5 * (cycles + 8) * 16 + 256)  # warm-up + 5 timed runs
     rows = torch.randn((1, mix.num_planes, mix.seqs, *mix.row_shape), dtype=torch.float16, device=device)
     # the whole-cycle runs take a new token row per sequence, plane and step
     # (16 steps' rows, 512 MiB with 8 KV heads), so no step re-reads the last
@@ -1041,11 +1041,13 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
     # launches in order on one stream, then pipelined (each step's bookkeeping
     # on a second stream, overlapping the previous step's moves)
     graph, per_cycle = mix.capture_cycle(rows)
+    graph.replay()  # uploads the graph; untimed warm-up
     serial_ms = timed(lambda: [graph.replay() for _ in range(cycles)])
     del graph
     mix.pipelined = True
     graph, per_cycle_p = mix.capture_cycle(rows)
     assert per_cycle_p == per_cycle
+    graph.replay()  # untimed warm-up
     step_ms = timed(lambda: [graph.replay() for _ in range(cycles)])
     tokens, blocks = cycles * 16 * mix.seqs, cycles * per_cycle
     assert (tokens, blocks) == (eager_tokens, eager_blocks)
@@ -1067,6 +1069,7 @@ def run_decode_mix(args, world: int, rank: int, device) -> None:
         mix.run_cycle(cycle_rows)
         graph, per_replay = mix.capture_cycles(cycle_rows)
         assert per_replay == cpr * per_cycle
+        graph.replay()  # uploads the graph; untimed warm-up
         with ClockSampler(device.index) as clk:
             results[one_launch] = (timed(lambda: [graph.replay() for _ in range(replays)]), clk)
         del graph
