@@ -441,10 +441,11 @@ class DecodeMix:
     # sequences need a block in the next block_size steps follows from the
     # fill positions.  So one append_steps launch books a whole cycle (pop,
     # commit, release and slot_mapping of each of its steps, in order), on
-    # the bookkeeping stream, one cycle ahead of the token moves: while the
-    # moves of cycle c run, cycle c + 1 is booked.  Victims and slot_mapping
-    # are double-buffered by cycle; cycle c + 1's booking waits for the moves
-    # of cycle c - 1, the last readers of its half.  The moves of each step
+    # the bookkeeping stream, ahead of the token moves: while the moves of
+    # cycle c run, cycle c + 1 is booked.  Victims and slot_mapping rotate
+    # through CYCLE_BUFFERS buffers by cycle; cycle c + 1's booking waits
+    # for the moves of cycle c + 1 - CYCLE_BUFFERS, the last readers of its
+    # buffer, so the booking stream may run ahead.  The moves of each step
     # (the spill gather of its victims, then its token scatter) stay in step
     # order on the caller's stream, so every byte moved equals step-by-step.
 
